@@ -1,0 +1,397 @@
+"""Benchmark of the SSM-scan hot path on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--op scan|ssd|decode] [--config 1|2]
+
+Default workload (the BASELINE metric): the Mamba-1 selective scan forward +
+backward of BASELINE config 2 -- batch 16, d_inner 5120, seqlen 4096,
+d_state 16, one group, bf16 u/delta/z/B/C, fp32 A/D/delta_bias,
+delta_softplus=True, dy ~ N(0,1) -- sharded by batch over the N ranks
+(global batch 16, 16/N rows per rank), followed by the NCCL all-reduce of the
+shared-parameter gradients (dA, dD, d delta_bias) as one flat fp32 bucket.
+
+One step = forward + backward of the whole batch shard (+ the all-reduce when
+N > 1).  The timed region is bracketed by a barrier and a device synchronise
+on both sides and timed with CUDA events on the launching stream; the reported
+time is the max over ranks.  Inputs are generated on the host from the config's
+seeded distributions (synthetic data), then moved to HBM; every input tensor is
+larger than the 126 MB L2, so no flush is needed between steps.
+
+Rank 0 prints one JSON line (see the keys below).  ``--impl reference`` times
+the reference's CPU implementation of the same op (the oracle restatement of
+``cv/path_scan.py:579-605`` + the ``scan.py:311-320`` epilogue, fp32, autograd
+forward + backward) on the host cores, on a bounded sample of the same
+workload, and prints the same line with ``"impl": "reference"``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    1: dict(batch=8, dim=1536, length=2048, dstate=16, groups=1, seed=1001),
+    2: dict(batch=16, dim=5120, length=4096, dstate=16, groups=1, seed=1002),
+}
+SSD_CONFIG = dict(batch=8, length=8192, nheads=80, headdim=64, dstate=128, ngroups=8, chunk=256,
+                  seed=1003)
+DECODE_CONFIG = dict(batch=256, nheads=80, headdim=64, dstate=128, ngroups=8, seed=1004)
+
+
+def _peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class Clocks:
+    """nvidia-smi sampling (every 200 ms) during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- scan op --
+
+def _scan_inputs(cfg, batch_lo, batch_hi, device):
+    from oracle.ssm_oracle import selective_scan_inputs
+    # generate the full config on the host (seeded), keep this rank's rows
+    full = selective_scan_inputs(cfg["batch"], cfg["dim"], cfg["length"], cfg["dstate"],
+                                 cfg["groups"], seed=cfg["seed"], act_dtype=torch.bfloat16) \
+        if cfg["batch"] * cfg["dim"] * cfg["length"] <= 50_000_000 else None
+    if full is None:
+        full = _scan_inputs_rows(cfg, batch_lo, batch_hi)
+    else:
+        full = {k: (v[batch_lo:batch_hi] if k in ("u", "delta", "z", "dout", "B", "C") else v)
+                for k, v in full.items()}
+    return full
+
+
+def _scan_inputs_rows(cfg, lo, hi):
+    """Large configs: generate per batch row with a row-derived seed so every
+    rank sees the same global tensor without materialising it whole."""
+    from oracle.ssm_oracle import selective_scan_inputs
+    rows = [selective_scan_inputs(1, cfg["dim"], cfg["length"], cfg["dstate"], cfg["groups"],
+                                  seed=cfg["seed"] * 1000 + b, act_dtype=torch.bfloat16)
+            for b in range(lo, hi)]
+    out = {k: torch.cat([r[k] for r in rows]) for k in ("u", "delta", "z", "dout", "B", "C")}
+    base = selective_scan_inputs(1, cfg["dim"], 1, cfg["dstate"], cfg["groups"], seed=cfg["seed"])
+    for k in ("A", "D", "delta_bias"):
+        out[k] = base[k]
+    return out
+
+
+def _scan_alg_bytes(b, d, l, n, g, s_a=2):
+    fwd = 4 * s_a * b * d * l + 2 * s_a * b * g * n * l
+    bwd = 7 * s_a * b * d * l + 4 * s_a * b * g * n * l
+    return fwd, bwd
+
+
+def run_scan(args, world, rank, device):
+    import torch.distributed as dist
+    import metal_kernelops_b200 as mk  # noqa: F401  (registers the ops)
+
+    cfg = CONFIGS[args.config]
+    per = cfg["batch"] // world
+    lo, hi = rank * per, (rank + 1) * per
+    host = _scan_inputs(cfg, lo, hi, device)
+    dev = {k: v.to(device) for k, v in host.items()}
+    u, delta, A, B, C, D, z, bias, dout = (dev[k] for k in
+                                           ("u", "delta", "A", "B", "C", "D", "z", "delta_bias", "dout"))
+    ops = torch.ops.b200ssm
+    bucket = torch.empty(A.numel() + 2 * A.shape[0], dtype=torch.float32, device=device)
+    n_a = A.numel()
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+
+    def step(i=None):
+        e = ev[i] if i is not None else None
+        if e:
+            e[0].record()
+        y, ck = ops.selective_scan_fwd(u, delta, A, B, C, D, z, bias, True, True)
+        if e:
+            e[1].record()
+        du, dd, dA, dB, dC, dD, dz, db = ops.selective_scan_bwd(dout, u, delta, A, B, C, D, z, bias,
+                                                                ck, True)
+        if e:
+            e[2].record()
+        if world > 1:
+            bucket[:n_a].copy_(dA.view(-1))
+            bucket[n_a:n_a + A.shape[0]].copy_(dD)
+            bucket[n_a + A.shape[0]:].copy_(db)
+            dist.all_reduce(bucket)
+        if e:
+            e[3].record()
+        return y
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(torch.cuda.current_device()) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(args.steps):
+        step(i)
+    t1.record()
+    torch.cuda.synchronize()
+    ck_info = clocks.stop() if clocks else None
+    ms = t0.elapsed_time(t1)
+    fwd_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
+    bwd_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
+    ar_ms = sum(e[2].elapsed_time(e[3]) for e in ev) / args.steps
+    if world > 1:
+        t = torch.tensor([ms, fwd_ms, bwd_ms, ar_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, fwd_ms, bwd_ms, ar_ms = t.tolist()
+        dist.barrier()
+
+    # end to end through the public API: pinned host inputs -> H2D, fwd+bwd via
+    # autograd, D2H of the parameter gradients, every step.
+    pinned = {k: v.pin_memory() for k, v in host.items()}
+    e2e_steps = max(1, min(args.steps, 5))
+    names = ("u", "delta", "A", "B", "C", "D", "z", "delta_bias")
+
+    def e2e_step():
+        d = {k: pinned[k].to(device, non_blocking=True) for k in pinned}
+        leaves = [d[k].requires_grad_(True) for k in names]
+        y = mk.selective_scan(*leaves[:5], D=leaves[5], z=leaves[6], delta_bias=leaves[7],
+                              delta_softplus=True)
+        gr = torch.autograd.grad(y, leaves, d["dout"])
+        flat = torch.cat([gr[2].reshape(-1), gr[5], gr[7]])
+        if world > 1:
+            dist.all_reduce(flat)
+        return flat.to("cpu")
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s0 = torch.cuda.Event(enable_timing=True)
+    s1 = torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    s1.record()
+    torch.cuda.synchronize()
+    e2e_ms = s0.elapsed_time(s1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = t.item()
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = (A.numel() + 2 * A.shape[0]) * 4
+
+    if rank != 0:
+        return None
+    b, d, l, n, g = per, cfg["dim"], cfg["length"], cfg["dstate"], cfg["groups"]
+    units = cfg["batch"] * d * l if world > 1 else b * d * l
+    ms_step = ms / args.steps
+    value = units / (ms_step / 1e3)
+    peaks, peak_kind = _peaks()
+    fwd_b, bwd_b = _scan_alg_bytes(b, d, l, n, g)
+    bwd_gbs = bwd_b / (bwd_ms / 1e3) / 1e9
+    fwd_gbs = fwd_b / (fwd_ms / 1e3) / 1e9
+    step_gbs = (fwd_b + bwd_b) / ((fwd_ms + bwd_ms) / 1e3) / 1e9
+    return {
+        "metric": "selective-scan fwd+bwd B*L*D elems/s",
+        "value": value,
+        "unit": "elem/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16 storage, fp32 compute",
+        "data": "synthetic (seeded, BASELINE config distributions)",
+        "config": {"workload": f"mamba1 selective scan fwd+bwd, BASELINE config {args.config}",
+                   "global_batch": cfg["batch"], "batch_per_gpu": b, "dim": d, "seq_len": l,
+                   "dstate": n, "groups": g, "parallelism": f"dp{world} (batch shard)",
+                   "l2": "inputs > L2 (126 MB), no flush"},
+        "breakdown_ms": {"fwd": fwd_ms, "bwd": bwd_ms, "allreduce": ar_ms},
+        "roofline": {"bound": "hbm", "kernel": "selective_scan bwd (bwd_kernel + reduce)",
+                     "achieved": bwd_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": bwd_gbs / peaks["hbm_gbs"], "peak_source": peak_kind,
+                     "traffic": _traffic("selective_scan_bwd"),
+                     "alg_bytes_per_launch": bwd_b,
+                     "fwd": {"achieved": fwd_gbs, "frac": fwd_gbs / peaks["hbm_gbs"]},
+                     "fwd_bwd": {"achieved": step_gbs, "frac": step_gbs / peaks["hbm_gbs"]}},
+        "e2e": {"value": units / (e2e_ms / 1e3), "unit": "elem/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "metal_kernelops_b200.selective_scan + autograd, pinned host buffers"},
+        "gpu_launches": 3 * args.steps,
+        "clocks": ck_info,
+    }
+
+
+def _traffic(kernel):
+    """Per-launch DRAM bytes of the kernel from the committed ncu summary, if any."""
+    f = ROOT / "profiles" / "traffic.txt"
+    try:
+        for line in f.read_text().splitlines():
+            k, _, v = line.partition(":")
+            if k.strip() == kernel:
+                return float(v.split()[0])
+    except Exception:
+        pass
+    return None
+
+
+def cpu_baseline_scan(cfg, threads, budget_s=15.0):
+    """The oracle (reference CPU code restated) on a bounded sample: one batch
+    row, a slice of channels, the full sequence; fwd + bwd with autograd."""
+    from oracle.ssm_oracle import selective_scan_inputs, selective_scan_ref
+    torch.set_num_threads(threads)
+    channels = 64
+    inp = selective_scan_inputs(1, channels, cfg["length"], cfg["dstate"], cfg["groups"],
+                                seed=cfg["seed"], act_dtype=torch.float32)
+    names = ("u", "delta", "A", "B", "C", "D", "z", "delta_bias")
+    done, units, t_start = 0, 0, time.perf_counter()
+    while True:
+        leaves = [inp[k].clone().requires_grad_(True) for k in names]
+        y = selective_scan_ref(*leaves[:5], D=leaves[5], z=leaves[6], delta_bias=leaves[7],
+                               delta_softplus=True)
+        torch.autograd.grad(y, leaves, inp["dout"])
+        done += 1
+        units += channels * cfg["length"]
+        if time.perf_counter() - t_start > budget_s or done >= 3:
+            break
+    el = time.perf_counter() - t_start
+    return {"value": units / el, "unit": "elem/s", "cores": threads, "kind": "port",
+            "sample": f"1 batch row x {channels} channels x {cfg['length']} steps "
+                      f"(dstate {cfg['dstate']}), fp32 fwd+bwd via autograd, {done} pass(es), "
+                      f"{el:.1f} s"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--op", default="scan", choices=["scan", "ssd", "decode"])
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = _dist()
+    threads = len(os.sched_getaffinity(0))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cfg = CONFIGS[args.config]
+        vals = []
+        for _ in range(args.warmup + args.steps):
+            vals.append(cpu_baseline_scan(cfg, threads, budget_s=5.0))
+        timed = vals[args.warmup:]
+        v = statistics.median(x["value"] for x in timed)
+        units = cfg["batch"] * cfg["dim"] * cfg["length"]
+        line = {
+            "impl": "reference", "metric": "selective-scan fwd+bwd B*L*D elems/s", "value": v,
+            "unit": "elem/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": units / v * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": f"mamba1 selective scan fwd+bwd, BASELINE config {args.config}",
+                       "global_batch": cfg["batch"], "dim": cfg["dim"], "seq_len": cfg["length"],
+                       "dstate": cfg["dstate"], "parallelism": "host CPU"},
+            "cpu_baseline": {**timed[0], "value": v},
+            "e2e": {"value": v, "unit": "elem/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+        return
+
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    device = torch.device("cuda", torch.cuda.current_device())
+
+    if args.op == "scan":
+        line = run_scan(args, world, rank, device)
+    else:
+        raise SystemExit(f"--op {args.op}: not available yet")
+    if rank == 0 and line is not None:
+        if world == 1 and not args.no_cpu_baseline and args.op == "scan":
+            line["cpu_baseline"] = cpu_baseline_scan(CONFIGS[args.config], threads)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,231 @@
+/*
+ * ssm_b200.h -- C ABI of the B200 (sm_100a) SSM-scan kernels.
+ *
+ * Plain pointers, sizes and a stream handle; no torch types.  Every entry point
+ * returns an ssm_status (0 = success) and never throws across the boundary.
+ * All pointers are device pointers unless stated otherwise; all tensors are
+ * dense row-major (the Python layer makes them contiguous).  Kernels are
+ * enqueued on `stream` (a cudaStream_t, or NULL for the legacy default stream)
+ * and the call returns without synchronising.
+ *
+ * The reference (dbydd/metal-kernelops 0.3.0) has no native FFI: its hot path
+ * is three Python functions that launch Metal shaders through torch.mps.  Each
+ * entry point below replaces the device work behind one of them; the file:line
+ * citations are paths inside that project.
+ */
+#ifndef SSM_B200_H
+#define SSM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum ssm_status {
+    SSM_OK = 0,
+    SSM_ERR_INVALID = 1,      /* shape / argument violates the op's contract   */
+    SSM_ERR_UNSUPPORTED = 2,  /* dtype or size outside what the kernels handle */
+    SSM_ERR_CUDA = 3,         /* a CUDA runtime call failed (see message)      */
+    SSM_ERR_WORKSPACE = 4     /* workspace missing or smaller than required    */
+} ssm_status;
+
+typedef enum ssm_dtype {
+    SSM_F32 = 0,
+    SSM_BF16 = 1,
+    SSM_F16 = 2
+} ssm_dtype;
+
+/* option bits shared by the three op groups */
+#define SSM_HAS_D        0x01u  /* skip connection D                            */
+#define SSM_HAS_Z        0x02u  /* gate: y *= silu(z)                            */
+#define SSM_HAS_BIAS     0x04u  /* delta/dt bias added before the softplus      */
+#define SSM_SOFTPLUS     0x08u  /* delta/dt = softplus(delta/dt + bias)          */
+#define SSM_D_PER_HEAD   0x10u  /* Mamba-2: D is (nheads, headdim), not (nheads) */
+#define SSM_DT_PER_ROW   0x20u  /* decode: dt is (batch, nheads, headdim)       */
+#define SSM_HAS_INIT     0x40u  /* SSD: initial_states given                    */
+#define SSM_HAS_DY       0x80u  /* backward: gradient of y given                */
+#define SSM_HAS_DSTATE   0x100u /* backward: gradient of the state output given */
+
+/* Human-readable text for a status code, and the message of the last failure
+ * on the calling thread (empty if none). */
+const char* ssm_status_string(int status);
+const char* ssm_last_error(void);
+
+/* ------------------------------------------------------------------------- *
+ * Mamba-1 selective scan.
+ *
+ * Replaces the device work of `metal_kernelops.selective_scan`
+ * (src/metal_kernelops/scan.py:295-320): the bias add and softplus
+ * (:311-314), `_Scan.forward` with its three kernels summarize / boundaries /
+ * outputs (:237-255, MSL :60-127), the skip `+ u*D` (:316-317) and the gate
+ * `* silu(z)` (:318-319) -- all fused into ssm_selective_scan_fwd -- and the
+ * backward `_Scan.backward` (:257-280, MSL :129-232) plus the autograd of the
+ * fused epilogue -- ssm_selective_scan_bwd.
+ *
+ *   u, delta, z, y, dout, du, ddelta, dz : (batch, dim, length), act_dtype
+ *   A                                     : (dim, dstate) fp32
+ *   B, C                                  : (batch, groups, dstate, length), bc_dtype
+ *   D, delta_bias                         : (dim,) fp32
+ *   dA (dim, dstate), dD (dim), ddelta_bias (dim): fp32, summed over the batch
+ *   dB, dC                                : (batch, groups, dstate, length) fp32
+ * ------------------------------------------------------------------------- */
+typedef struct ssm_selective_scan_params {
+    int64_t batch, dim, length, groups, dstate;
+    int32_t act_dtype;          /* ssm_dtype of u, delta, z, y and their grads */
+    int32_t bc_dtype;           /* ssm_dtype of B and C                        */
+    uint32_t flags;             /* SSM_HAS_D | SSM_HAS_Z | SSM_HAS_BIAS | SSM_SOFTPLUS */
+    /* forward inputs */
+    const void* u;
+    const void* delta;
+    const float* A;
+    const void* B;
+    const void* C;
+    const float* D;             /* may be NULL without SSM_HAS_D    */
+    const void* z;              /* may be NULL without SSM_HAS_Z    */
+    const float* delta_bias;    /* may be NULL without SSM_HAS_BIAS */
+    /* forward output */
+    void* y;
+    /* chunk-entering states, fp32, written by the forward and read by the
+     * backward (NULL in the forward = inference, nothing saved) */
+    float* checkpoints;
+    /* backward */
+    const void* dout;
+    void* du;
+    void* ddelta;
+    void* dz;                   /* may be NULL without SSM_HAS_Z */
+    float* dA;
+    float* dB;
+    float* dC;
+    float* dD;                  /* may be NULL without SSM_HAS_D    */
+    float* ddelta_bias;         /* may be NULL without SSM_HAS_BIAS */
+    /* scratch for the backward's deterministic partial sums */
+    void* workspace;
+    size_t workspace_bytes;
+} ssm_selective_scan_params;
+
+/* Sizes of the forward's checkpoint buffer and of the backward's workspace. */
+int ssm_selective_scan_sizes(const ssm_selective_scan_params* p,
+                             size_t* checkpoint_bytes, size_t* workspace_bytes);
+int ssm_selective_scan_fwd(const ssm_selective_scan_params* p, void* stream);
+int ssm_selective_scan_bwd(const ssm_selective_scan_params* p, void* stream);
+
+/* ------------------------------------------------------------------------- *
+ * Mamba-2 decode state update.
+ *
+ * Replaces `metal_kernelops.cv.mamba2_state_update`
+ * (src/metal_kernelops/cv/mamba2_state.py:759-819): the fused forward kernel
+ * `state_update_$S` (:184-267, launched by `_launch` :601-637) and the
+ * two-kernel deterministic backward `state_update_backward` +
+ * `state_update_reduce` (:269-536, driven by `_StateUpdate.backward` :653-756).
+ *
+ *   state, new_state, grad_state, dnew   : (batch, nheads, headdim, dstate), state_dtype
+ *   x, z, y, dy, dx, dz                  : (batch, nheads, headdim), state_dtype (fp32 grads)
+ *   dt                                   : (batch, nheads) or (batch, nheads, headdim)
+ *   A, dt_bias                           : (nheads,) fp32
+ *   B, C                                 : (batch, ngroups, dstate)
+ *   D                                    : (nheads,) or (nheads, headdim) fp32
+ * new_state may alias state (in-place update, `out_state` of the reference).
+ * The backward computes in fp32: its inputs other than A/D/dt_bias are fp32
+ * (the wrapper widens them, as the reference's `_wide` does, :554-558) and
+ * all its outputs are fp32.
+ * ------------------------------------------------------------------------- */
+typedef struct ssm_state_update_params {
+    int64_t batch, nheads, headdim, dstate, ngroups;
+    int32_t dtype;              /* ssm_dtype of state, x, dt, B, C, z, y (forward) */
+    uint32_t flags;             /* SSM_HAS_D | SSM_D_PER_HEAD | SSM_HAS_Z | SSM_HAS_BIAS |
+                                   SSM_SOFTPLUS | SSM_DT_PER_ROW | SSM_HAS_DY | SSM_HAS_DSTATE */
+    const void* state;
+    const void* x;
+    const void* dt;
+    const float* A;
+    const void* B;
+    const void* C;
+    const float* D;
+    const void* z;
+    const float* dt_bias;
+    void* new_state;            /* forward output; may equal `state` */
+    void* y;                    /* forward output */
+    /* backward (all fp32) */
+    const float* dy;            /* may be NULL without SSM_HAS_DY     */
+    const float* dnew;          /* may be NULL without SSM_HAS_DSTATE */
+    float* grad_state;          /* gradient of the entering state */
+    float* dx;
+    float* ddt;                 /* shaped like dt */
+    float* dA;
+    float* dB;
+    float* dC;
+    float* dD;
+    float* dz;
+    float* ddt_bias;
+    void* workspace;
+    size_t workspace_bytes;
+} ssm_state_update_params;
+
+int ssm_state_update_sizes(const ssm_state_update_params* p, size_t* workspace_bytes);
+int ssm_state_update_fwd(const ssm_state_update_params* p, void* stream);
+int ssm_state_update_bwd(const ssm_state_update_params* p, void* stream);
+
+/* ------------------------------------------------------------------------- *
+ * Mamba-2 SSD chunk scan.
+ *
+ * Replaces `metal_kernelops.cv.mamba2_chunk_scan`
+ * (src/metal_kernelops/cv/mamba2_chunk.py:617-678): `_discretize` (:447-462),
+ * `_chunk_states` (:465-484), `_state_passing` (:487-505), `_chunk_outputs`
+ * (:508-533) and the fused Metal output stage `mamba2_cb` / `mamba2_scan`
+ * (:182-347); the backward replaces the autograd of that composition.
+ *
+ *   x, z, y, dy, dx, dz                  : (batch, length, nheads, headdim), dtype
+ *   dt, ddt                              : (batch, length, nheads), dt_dtype / fp32
+ *   A, dA, dt_bias, ddt_bias             : (nheads,) fp32
+ *   B, C                                 : (batch, length, ngroups, dstate), dtype
+ *   dB, dC                               : (batch, length, ngroups, dstate) fp32
+ *   D, dD                                : (nheads,) or (nheads, headdim) fp32
+ *   initial_states, final_state          : (batch, nheads, headdim, dstate) fp32
+ * ------------------------------------------------------------------------- */
+typedef struct ssm_chunk_scan_params {
+    int64_t batch, length, nheads, headdim, ngroups, dstate, chunk_size;
+    int32_t dtype;              /* ssm_dtype of x, B, C, z, y */
+    int32_t dt_dtype;           /* ssm_dtype of dt            */
+    uint32_t flags;             /* SSM_HAS_D | SSM_D_PER_HEAD | SSM_HAS_Z | SSM_HAS_BIAS |
+                                   SSM_SOFTPLUS | SSM_HAS_INIT | SSM_HAS_DY | SSM_HAS_DSTATE */
+    const void* x;
+    const void* dt;
+    const float* A;
+    const void* B;
+    const void* C;
+    const float* D;
+    const void* z;
+    const float* dt_bias;
+    const float* initial_states;
+    void* y;
+    float* final_state;
+    /* backward */
+    const void* dy;             /* dtype of x */
+    const float* dfinal;        /* may be NULL without SSM_HAS_DSTATE */
+    void* dx;                   /* dtype of x */
+    float* ddt;
+    float* dA;
+    float* dB;
+    float* dC;
+    float* dD;
+    void* dz;                   /* dtype of x */
+    float* ddt_bias;
+    float* dinitial;
+    /* forward: chunk states saved for the backward (may be NULL) */
+    float* saved;
+    void* workspace;
+    size_t workspace_bytes;
+} ssm_chunk_scan_params;
+
+int ssm_chunk_scan_sizes(const ssm_chunk_scan_params* p, size_t* saved_bytes,
+                         size_t* workspace_bytes);
+int ssm_chunk_scan_fwd(const ssm_chunk_scan_params* p, void* stream);
+int ssm_chunk_scan_bwd(const ssm_chunk_scan_params* p, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SSM_B200_H */

@@ -1,0 +1,151 @@
+"""ctypes binding of the in-tree C-ABI library ``libssm_b200.so``.
+
+The structs mirror ``include/ssm_b200.h`` field for field.  There is no
+fallback: if the library is missing or a CUDA tensor reaches an op without it,
+the op raises.  The library itself loads without a GPU (it links only the CUDA
+runtime), so the CPU test suite can check its exported symbols.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import threading
+
+import torch
+
+LIB_PATH = pathlib.Path(__file__).resolve().parent / "libssm_b200.so"
+
+SSM_OK, SSM_ERR_INVALID, SSM_ERR_UNSUPPORTED, SSM_ERR_CUDA, SSM_ERR_WORKSPACE = range(5)
+SSM_F32, SSM_BF16, SSM_F16 = 0, 1, 2
+
+HAS_D = 0x01
+HAS_Z = 0x02
+HAS_BIAS = 0x04
+SOFTPLUS = 0x08
+D_PER_HEAD = 0x10
+DT_PER_ROW = 0x20
+HAS_INIT = 0x40
+HAS_DY = 0x80
+HAS_DSTATE = 0x100
+
+EXPORTS = (
+    "ssm_status_string", "ssm_last_error",
+    "ssm_selective_scan_sizes", "ssm_selective_scan_fwd", "ssm_selective_scan_bwd",
+    "ssm_state_update_sizes", "ssm_state_update_fwd", "ssm_state_update_bwd",
+    "ssm_chunk_scan_sizes", "ssm_chunk_scan_fwd", "ssm_chunk_scan_bwd",
+)
+
+_I64, _I32, _U32, _P, _SZ = ctypes.c_int64, ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t
+
+
+class SelectiveScanParams(ctypes.Structure):
+    _fields_ = [
+        ("batch", _I64), ("dim", _I64), ("length", _I64), ("groups", _I64), ("dstate", _I64),
+        ("act_dtype", _I32), ("bc_dtype", _I32), ("flags", _U32),
+        ("u", _P), ("delta", _P), ("A", _P), ("B", _P), ("C", _P),
+        ("D", _P), ("z", _P), ("delta_bias", _P),
+        ("y", _P), ("checkpoints", _P),
+        ("dout", _P), ("du", _P), ("ddelta", _P), ("dz", _P),
+        ("dA", _P), ("dB", _P), ("dC", _P), ("dD", _P), ("ddelta_bias", _P),
+        ("workspace", _P), ("workspace_bytes", _SZ),
+    ]
+
+
+class StateUpdateParams(ctypes.Structure):
+    _fields_ = [
+        ("batch", _I64), ("nheads", _I64), ("headdim", _I64), ("dstate", _I64), ("ngroups", _I64),
+        ("dtype", _I32), ("flags", _U32),
+        ("state", _P), ("x", _P), ("dt", _P), ("A", _P), ("B", _P), ("C", _P),
+        ("D", _P), ("z", _P), ("dt_bias", _P),
+        ("new_state", _P), ("y", _P),
+        ("dy", _P), ("dnew", _P),
+        ("grad_state", _P), ("dx", _P), ("ddt", _P), ("dA", _P), ("dB", _P), ("dC", _P),
+        ("dD", _P), ("dz", _P), ("ddt_bias", _P),
+        ("workspace", _P), ("workspace_bytes", _SZ),
+    ]
+
+
+class ChunkScanParams(ctypes.Structure):
+    _fields_ = [
+        ("batch", _I64), ("length", _I64), ("nheads", _I64), ("headdim", _I64),
+        ("ngroups", _I64), ("dstate", _I64), ("chunk_size", _I64),
+        ("dtype", _I32), ("dt_dtype", _I32), ("flags", _U32),
+        ("x", _P), ("dt", _P), ("A", _P), ("B", _P), ("C", _P), ("D", _P), ("z", _P),
+        ("dt_bias", _P), ("initial_states", _P),
+        ("y", _P), ("final_state", _P),
+        ("dy", _P), ("dfinal", _P),
+        ("dx", _P), ("ddt", _P), ("dA", _P), ("dB", _P), ("dC", _P), ("dD", _P), ("dz", _P),
+        ("ddt_bias", _P), ("dinitial", _P),
+        ("saved", _P), ("workspace", _P), ("workspace_bytes", _SZ),
+    ]
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib():
+    """The loaded library; raises if it was not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"{LIB_PATH.name} is not built; run `python -m metal_kernelops_b200.build` "
+                    "(there is no CPU fallback)")
+            handle = ctypes.CDLL(str(LIB_PATH))
+            handle.ssm_status_string.restype = ctypes.c_char_p
+            handle.ssm_status_string.argtypes = [ctypes.c_int]
+            handle.ssm_last_error.restype = ctypes.c_char_p
+            handle.ssm_last_error.argtypes = []
+            for name, struct in (("selective_scan", SelectiveScanParams),
+                                 ("state_update", StateUpdateParams),
+                                 ("chunk_scan", ChunkScanParams)):
+                for suffix in ("fwd", "bwd"):
+                    fn = getattr(handle, f"ssm_{name}_{suffix}")
+                    fn.restype = ctypes.c_int
+                    fn.argtypes = [ctypes.POINTER(struct), ctypes.c_void_p]
+            handle.ssm_selective_scan_sizes.argtypes = [
+                ctypes.POINTER(SelectiveScanParams), ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]
+            handle.ssm_state_update_sizes.argtypes = [
+                ctypes.POINTER(StateUpdateParams), ctypes.POINTER(_SZ)]
+            handle.ssm_chunk_scan_sizes.argtypes = [
+                ctypes.POINTER(ChunkScanParams), ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]
+            for name in ("ssm_selective_scan_sizes", "ssm_state_update_sizes", "ssm_chunk_scan_sizes"):
+                getattr(handle, name).restype = ctypes.c_int
+            _lib = handle
+    return _lib
+
+
+class NativeError(RuntimeError):
+    pass
+
+
+def check(status: int, what: str) -> None:
+    """Map a C-ABI status to the reference's error convention: contract
+    violations are ``ValueError``, everything else ``RuntimeError``."""
+    if status == SSM_OK:
+        return
+    L = lib()
+    msg = L.ssm_last_error().decode() or L.ssm_status_string(status).decode()
+    if status in (SSM_ERR_INVALID, SSM_ERR_UNSUPPORTED):
+        raise ValueError(f"{what}: {msg}")
+    raise NativeError(f"{what}: {msg} (status {status})")
+
+
+_DTYPES = {torch.float32: SSM_F32, torch.bfloat16: SSM_BF16, torch.float16: SSM_F16}
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    return _DTYPES[dtype]
+
+
+def ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)

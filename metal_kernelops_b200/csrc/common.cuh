@@ -1,0 +1,84 @@
+// Shared device/host helpers for the sm_100a SSM-scan kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "ssm_b200.h"
+
+namespace ssm {
+
+// ---------------------------------------------------------------- errors ----
+void set_error(const std::string& msg);
+int fail(int status, const std::string& msg);
+int check_launch(const char* what);
+
+// ------------------------------------------------------------ dtype I/O ----
+template <typename T> struct Io;
+template <> struct Io<float> {
+    static __device__ __forceinline__ float ld(const float* p) { return *p; }
+    static __device__ __forceinline__ void st(float* p, float v) { *p = v; }
+};
+template <> struct Io<__nv_bfloat16> {
+    static __device__ __forceinline__ float ld(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+    static __device__ __forceinline__ void st(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+};
+template <> struct Io<__half> {
+    static __device__ __forceinline__ float ld(const __half* p) { return __half2float(*p); }
+    static __device__ __forceinline__ void st(__half* p, float v) { *p = __float2half_rn(v); }
+};
+
+template <typename T> __device__ __forceinline__ float ldf(const T* p) { return Io<T>::ld(p); }
+template <typename T> __device__ __forceinline__ void stf(T* p, float v) { Io<T>::st(p, v); }
+
+// Runtime-typed scalar load, for the small or cold operands (B/C staging).
+__device__ __forceinline__ float ld_any(const void* base, int64_t i, int dtype) {
+    if (dtype == SSM_F32) return reinterpret_cast<const float*>(base)[i];
+    if (dtype == SSM_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[i]);
+    return __half2float(reinterpret_cast<const __half*>(base)[i]);
+}
+__device__ __forceinline__ void st_any(void* base, int64_t i, int dtype, float v) {
+    if (dtype == SSM_F32) reinterpret_cast<float*>(base)[i] = v;
+    else if (dtype == SSM_BF16) reinterpret_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16_rn(v);
+    else reinterpret_cast<__half*>(base)[i] = __float2half_rn(v);
+}
+
+// ----------------------------------------------------------------- math ----
+// 2^x on the MUFU pipe (PTX ex2.approx: ~2 ulp in fp32, flushes subnormals).
+__device__ __forceinline__ float exp2_mufu(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// torch.nn.functional.softplus with its default threshold: x > 20 -> x.
+__device__ __forceinline__ float softplus_f(float x) {
+    return x > 20.0f ? x : log1pf(expf(x));
+}
+// d softplus / dx, matching torch's backward (1 above the threshold).
+__device__ __forceinline__ float softplus_grad_f(float x) {
+    return x > 20.0f ? 1.0f : 1.0f / (1.0f + expf(-x));
+}
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// ---------------------------------------------------------- warp reduce ----
+template <int WIDTH>
+__device__ __forceinline__ float sum_low_lanes(float v) {
+    // Sum over the WIDTH consecutive lanes sharing lane / WIDTH (WIDTH a power of two).
+#pragma unroll
+    for (int o = WIDTH / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+__host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace ssm

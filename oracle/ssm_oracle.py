@@ -1,0 +1,415 @@
+"""CPU restatement of the reference's SSM-scan definitions (TEST INFRASTRUCTURE).
+
+This module is the parity oracle and the CPU baseline.  It is never imported by
+``metal_kernelops_b200``.  Every function restates one definition of
+dbydd/metal-kernelops 0.3.0 (paths relative to that project) in plain torch
+so that it evaluates in float64 on the CPU and carries autograd where the
+reference's does:
+
+* ``selective_scan_stepwise``  <- ``src/metal_kernelops/reference.py:5-49``
+  (the triple-loop recurrence; forward only, like the original)
+* ``scan_functional``          <- ``src/metal_kernelops/cv/path_scan.py:579-605``
+  (``_scan_reference``: the same recurrence, rebuilt per step so autograd works)
+* ``selective_scan_ref``       <- ``src/metal_kernelops/scan.py:295-320``
+  (bias, softplus, scan, ``+ u*D``, ``* silu(z)``) over ``scan_functional``
+* ``mamba2_chunk_scan_ref``    <- ``src/metal_kernelops/cv/mamba2_chunk.py:681-723``
+* ``mamba2_chunk_scan_composition`` <- ``cv/mamba2_chunk.py:447-533`` and
+  ``:652-678`` (the chunked torch composition the reference runs off-MPS; it is
+  the reference's CPU path and therefore the timed CPU baseline for SSD)
+* ``mamba2_state_update_ref``  <- ``src/metal_kernelops/cv/mamba2_state.py:822-849``
+* ``ssd_minimal_discrete``     <- ``benchmarks/verify_mamba2_chunk.py:185-216``
+  (the published ``ssd_minimal_discrete`` listing of state-spaces/mamba, used
+  by the reference as a known-answer cross-check)
+
+Input generators follow the seeds and value distributions of the hot-path
+configurations and of the reference's verifiers.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+__all__ = [
+    "selective_scan_stepwise",
+    "scan_functional",
+    "selective_scan_ref",
+    "mamba2_chunk_scan_ref",
+    "mamba2_chunk_scan_composition",
+    "mamba2_state_update_ref",
+    "ssd_minimal_discrete",
+    "max_rel",
+    "norm_rel",
+    "selective_scan_inputs",
+    "ssd_inputs",
+    "decode_inputs",
+]
+
+
+# ---------------------------------------------------------------------------
+# error metrics used by the reference's verifiers
+# ---------------------------------------------------------------------------
+
+def max_rel(got, want):
+    """max|got - want| / max|want| (``benchmarks/verify_mamba2_chunk.py:67-73``)."""
+    got = got.detach().double().cpu()
+    want = want.detach().double().cpu()
+    if want.numel() == 0:
+        return 0.0
+    scale = want.abs().max().item()
+    return (got - want).abs().max().item() / max(scale, 1e-30)
+
+
+def norm_rel(got, want):
+    """||got - want|| / ||want||, 0 when both are zero
+    (``benchmarks/verify_path_scan.py:61-66``)."""
+    got = got.detach().double().cpu()
+    want = want.detach().double().cpu()
+    denom = float(want.norm())
+    if denom == 0.0:
+        return 0.0 if float(got.norm()) == 0.0 else float("inf")
+    return float((got - want).norm()) / denom
+
+
+# ---------------------------------------------------------------------------
+# Mamba-1 selective scan
+# ---------------------------------------------------------------------------
+
+def selective_scan_stepwise(u, dt, A, B, C):
+    """Per-(t, b, channel) loop, forward only (``reference.py:5-49``).
+
+    x_t = exp(dt_t * A) * x_{t-1} + dt_t * B_t * u_t ;  y_t = <x_t, C_t>
+    u, dt: (batch, dim, length); A: (dim, dstate); B, C: (batch, groups, dstate, length).
+    """
+    batch, dim, length = u.shape
+    groups, dstate = B.shape[1], A.shape[1]
+    if dim % groups:
+        raise ValueError("dim must be divisible by groups")
+    width = dim // groups
+    y = torch.zeros_like(u)
+    state = torch.zeros(batch, dim, dstate, dtype=u.dtype)
+    for t in range(length):
+        for b in range(batch):
+            for ch in range(dim):
+                g = ch // width
+                decay = torch.exp(A[ch] * dt[b, ch, t])
+                state[b, ch] = decay * state[b, ch] + dt[b, ch, t] * u[b, ch, t] * B[b, g, :, t]
+                y[b, ch, t] = torch.dot(state[b, ch], C[b, g, :, t])
+    return y
+
+
+def scan_functional(u, dt, A, B, C):
+    """Differentiable stepwise scan (``cv/path_scan.py:579-605``).
+
+    The state is rebuilt every step instead of written in place, so autograd
+    can differentiate it.  Vectorised over (batch, channel, state).
+    """
+    batch, dim, length = u.shape
+    dstate = A.shape[1]
+    groups = B.shape[1]
+    width = dim // groups if groups else 0
+    if length == 0 or dim == 0 or batch == 0:
+        return u.new_zeros(batch, dim, length) + 0.0 * (u.sum() + dt.sum() + A.sum() + B.sum() + C.sum())
+    Bx = B.repeat_interleave(width, dim=1)        # (batch, dim, dstate, length)
+    Cx = C.repeat_interleave(width, dim=1)
+    state = u.new_zeros(batch, dim, dstate)
+    out = []
+    for t in range(length):
+        d_t = dt[:, :, t]
+        state = torch.exp(d_t.unsqueeze(-1) * A) * state + (d_t * u[:, :, t]).unsqueeze(-1) * Bx[..., t]
+        out.append((state * Cx[..., t]).sum(-1))
+    return torch.stack(out, dim=-1)
+
+
+def selective_scan_ref(u, dt, A, B, C, D=None, z=None, delta_bias=None,
+                       delta_softplus=False):
+    """The full Mamba-1 op of ``scan.py:295-320`` over ``scan_functional``.
+
+    bias add, softplus (torch's threshold-20 rule), scan, ``+ u*D``, ``* silu(z)``.
+    """
+    if delta_bias is not None:
+        dt = dt + delta_bias[..., None]
+    if delta_softplus:
+        dt = F.softplus(dt)
+    out = scan_functional(u, dt, A, B, C)
+    if D is not None:
+        out = out + u * D[..., None]
+    if z is not None:
+        out = out * F.silu(z)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Mamba-2 SSD chunk scan
+# ---------------------------------------------------------------------------
+
+def _initial_canonical(initial, batch, nheads, headdim, dstate):
+    """Accepted ``initial_states`` spellings (``cv/mamba2_chunk.py:426-438``)."""
+    if initial is None:
+        return None
+    if initial.dim() == 5 and initial.shape[1] == 1:
+        initial = initial[:, 0]
+    if tuple(initial.shape) != (batch, nheads, headdim, dstate):
+        if tuple(initial.shape) == (batch, nheads, dstate, headdim) and headdim != dstate:
+            initial = initial.transpose(-1, -2)
+        else:
+            raise ValueError("initial_states has the wrong shape")
+    return initial
+
+
+def mamba2_chunk_scan_ref(x, dt, A, B, C, chunk_size=64, D=None, z=None,
+                          dt_bias=None, dt_softplus=False, initial_states=None,
+                          dtype=torch.float64):
+    """Token-by-token SSD recurrence (``cv/mamba2_chunk.py:681-723``).
+
+    ``chunk_size`` is accepted and ignored.  Returns ``(y, final_state)`` cast
+    back to ``x.dtype``.
+    """
+    out_dtype = x.dtype
+    x, dt, A, B, C = (t.to(dtype) for t in (x, dt, A, B, C))
+    batch, length, nheads, headdim = x.shape
+    ngroups, dstate = B.shape[2], B.shape[3]
+    rep = nheads // ngroups
+    Bh = B.repeat_interleave(rep, dim=2)
+    Ch = C.repeat_interleave(rep, dim=2)
+    if dt_bias is not None:
+        dt = dt + dt_bias.to(dtype).view(1, 1, nheads)
+    if dt_softplus:
+        dt = F.softplus(dt)
+    state = x.new_zeros(batch, nheads, headdim, dstate)
+    init = _initial_canonical(initial_states, batch, nheads, headdim, dstate)
+    if init is not None:
+        state = init.to(dtype).clone()
+    ys = []
+    for t in range(length):
+        d_t = dt[:, t]                                              # (b, h)
+        state = state * torch.exp(d_t * A)[..., None, None] + \
+            (d_t[..., None] * x[:, t])[..., :, None] * Bh[:, t][:, :, None, :]
+        ys.append((state * Ch[:, t][:, :, None, :]).sum(-1))
+    y = torch.stack(ys, dim=1) if length else x.new_zeros(batch, 0, nheads, headdim)
+    if D is not None:
+        Dd = D.to(dtype)
+        y = y + x * (Dd.view(1, 1, nheads, 1) if Dd.dim() == 1 else Dd.view(1, 1, nheads, headdim))
+    if z is not None:
+        y = y * F.silu(z.to(dtype))
+    return y.to(out_dtype), state.to(out_dtype)
+
+
+def mamba2_chunk_scan_composition(x, dt, A, B, C, chunk_size=64, D=None, z=None,
+                                  dt_bias=None, dt_softplus=False, initial_states=None):
+    """The reference's chunked torch composition (``cv/mamba2_chunk.py:447-533``,
+    ``:652-678``): fp32 discretisation, chunk states by matmul, a causal
+    chunk-to-chunk decay matrix, intra- and inter-chunk outputs per group.
+    Differentiable through autograd; this is the reference's CPU code path."""
+    batch, length, nheads, headdim = x.shape
+    ngroups, dstate = B.shape[2], B.shape[3]
+    init = _initial_canonical(initial_states, batch, nheads, headdim, dstate)
+    rep = nheads // ngroups
+    q = min(chunk_size, length)
+    nc = -(-length // q)
+    padded = nc * q
+    # discretisation, float32 (:447-462)
+    d = dt.transpose(1, 2).to(torch.float32)
+    if dt_bias is not None:
+        d = d + dt_bias.to(torch.float32).view(1, nheads, 1)
+    if dt_softplus:
+        d = F.softplus(d)
+    if padded > length:
+        d = F.pad(d, (0, padded - length))
+    d = d.reshape(batch, nheads, nc, q)
+    dcs = torch.cumsum(d * A.to(torch.float32).view(1, nheads, 1, 1), dim=-1)
+    if padded > length:
+        pad = (0, 0, 0, 0, 0, padded - length)
+        xp, Bp, Cp = F.pad(x, pad), F.pad(B, pad), F.pad(C, pad)
+    else:
+        xp, Bp, Cp = x, B, C
+    # chunk states (:465-484): (b, h, c, n, p)
+    w = (d * torch.exp(dcs[..., -1:] - dcs)).permute(0, 2, 3, 1).unsqueeze(-1)
+    xw = xp.view(batch, nc, q, nheads, headdim) * w.to(x.dtype)
+    xg = xw.view(batch, nc, q, ngroups, rep, headdim).permute(0, 3, 4, 1, 2, 5)
+    Bg = Bp.view(batch, nc, q, ngroups, dstate).permute(0, 3, 1, 2, 4)
+    states = torch.matmul(Bg.transpose(-1, -2).unsqueeze(2), xg)
+    states = states.float().reshape(batch, nheads, nc, dstate, headdim)
+    # chunk-to-chunk transfer (:487-505)
+    total = dcs[..., -1]
+    before = torch.cumsum(F.pad(total, (1, 0)), dim=-1)
+    diff = before[..., :-1, None] - before[..., None, 1:]
+    mask = torch.ones(nc, nc, dtype=torch.bool).tril(-1)
+    decay = torch.exp(diff.masked_fill(~mask, float("-inf")))
+    entering = torch.matmul(decay, states.reshape(batch, nheads, nc, dstate * headdim))
+    if init is not None:
+        carry = torch.exp(before[..., :-1]).unsqueeze(-1)
+        entering = entering + carry * init.transpose(-1, -2).reshape(
+            batch, nheads, headdim * dstate).unsqueeze(2)
+    entering = entering.reshape(batch, nheads, nc, dstate, headdim)
+    final = states[:, :, -1] + torch.exp(total[:, :, -1])[..., None, None] * entering[:, :, -1]
+    final = final.transpose(-1, -2).contiguous()
+    # outputs (:508-533)
+    lower = torch.ones(q, q, dtype=torch.bool).tril()
+    intra = torch.exp((dcs[..., :, None] - dcs[..., None, :]).masked_fill(~lower, float("-inf")))
+    out_decay = torch.exp(dcs)
+    parts = []
+    for g in range(ngroups):
+        hs = slice(g * rep, (g + 1) * rep)
+        Cg = Cp[:, :, g].reshape(batch, nc, q, dstate).contiguous()
+        Bgg = Bp[:, :, g].reshape(batch, nc, q, dstate).contiguous()
+        cb = torch.matmul(Cg, Bgg.transpose(-1, -2)).float()
+        scores = (intra[:, hs] * cb[:, None] * d[:, hs][..., None, :]).to(x.dtype)
+        xh = xp[:, :, hs].view(batch, nc, q, rep, headdim).permute(0, 3, 1, 2, 4)
+        out = torch.matmul(scores, xh)
+        prev = torch.matmul(Cg[:, None].to(x.dtype), entering[:, hs].to(x.dtype))
+        prev = prev * out_decay[:, hs][..., None].to(x.dtype)
+        parts.append((out + prev).permute(0, 2, 3, 1, 4))
+    y = parts[0] if ngroups == 1 else torch.cat(parts, dim=3)
+    y = y.reshape(batch, padded, nheads, headdim)
+    if D is not None:
+        skip = D.to(x.dtype).view(1, 1, nheads, 1) if D.dim() == 1 else D.to(x.dtype).view(1, 1, nheads, headdim)
+        y = y + xp * skip
+    if z is not None:
+        zp = F.pad(z, (0, 0, 0, 0, 0, padded - length)) if padded > length else z
+        y = y * F.silu(zp)
+    if padded > length:
+        y = y[:, :length].contiguous()
+    return y, final.to(x.dtype)
+
+
+def _segsum(v):
+    """Stable segment sum of the ``ssd_minimal`` listing: out[..., i, j] =
+    sum_{j<k<=i} v[..., k] for j <= i, -inf above the diagonal."""
+    size = v.size(-1)
+    tri_strict = torch.ones(size, size, dtype=torch.bool).tril(-1)
+    tri = torch.ones(size, size, dtype=torch.bool).tril()
+    rep = v.unsqueeze(-1).expand(*v.shape, size).masked_fill(~tri_strict, 0)
+    acc = torch.cumsum(rep, dim=-2)
+    return acc.masked_fill(~tri, float("-inf"))
+
+
+def ssd_minimal_discrete(X, A, B, C, block_len, initial_states=None):
+    """``ssd_minimal_discrete`` as listed in ``verify_mamba2_chunk.py:185-216``.
+
+    X: (b, l, h, p) already multiplied by dt; A: (b, l, h) = A*dt; B, C: (b, l, g, n)
+    with g == h or g == 1.  Returns (y, final_state (b, h, p, n)).
+    """
+    batch, length, nheads, headdim = X.shape
+    nc = length // block_len
+    X = X.reshape(batch, nc, block_len, nheads, headdim)
+    A = A.reshape(batch, nc, block_len, nheads).permute(0, 3, 1, 2)
+    B = B.reshape(batch, nc, block_len, B.shape[2], B.shape[3])
+    C = C.reshape(batch, nc, block_len, C.shape[2], C.shape[3])
+    if B.shape[3] != nheads:
+        B = B.expand(-1, -1, -1, nheads, -1)
+        C = C.expand(-1, -1, -1, nheads, -1)
+    A_cs = torch.cumsum(A, dim=-1)
+    L = torch.exp(_segsum(A))
+    Y_diag = torch.einsum("bclhn,bcshn,bhcls,bcshp->bclhp", C, B, L, X)
+    decay_states = torch.exp(A_cs[:, :, :, -1:] - A_cs)
+    states = torch.einsum("bclhn,bhcl,bclhp->bchpn", B, decay_states, X)
+    if initial_states is None:
+        initial_states = torch.zeros_like(states[:, :1])
+    states = torch.cat([initial_states, states], dim=1)
+    decay_chunk = torch.exp(_segsum(F.pad(A_cs[:, :, :, -1], (1, 0))))
+    new_states = torch.einsum("bhzc,bchpn->bzhpn", decay_chunk, states)
+    states, final_state = new_states[:, :-1], new_states[:, -1]
+    Y_off = torch.einsum("bclhn,bchpn,bhcl->bclhp", C, states, torch.exp(A_cs))
+    return (Y_diag + Y_off).reshape(batch, length, nheads, headdim), final_state
+
+
+# ---------------------------------------------------------------------------
+# Mamba-2 decode state update
+# ---------------------------------------------------------------------------
+
+def mamba2_state_update_ref(state, x, dt, A, B, C, D=None, z=None, dt_bias=None,
+                            dt_softplus=False):
+    """One decode step in closed form (``cv/mamba2_state.py:822-849``).
+
+    Leaves ``state`` untouched; returns ``(y, new_state)``.
+    """
+    if dt.dim() == 2:
+        dt = dt.unsqueeze(-1)
+    if D is not None and D.dim() == 1:
+        D = D.unsqueeze(-1)
+    if dt_bias is not None:
+        dt = dt + dt_bias[None, :, None]
+    if dt_softplus:
+        dt = F.softplus(dt)
+    nheads, ngroups = state.shape[1], B.shape[1]
+    rep = nheads // ngroups
+    Bh = B.repeat_interleave(rep, dim=1)
+    Ch = C.repeat_interleave(rep, dim=1)
+    decay = torch.exp(A[None, :, None, None] * dt[..., None])
+    new_state = decay * state + (dt * x)[..., None] * Bh[:, :, None, :]
+    y = (new_state * Ch[:, :, None, :]).sum(-1)
+    if D is not None:
+        y = y + x * D
+    if z is not None:
+        y = y * F.silu(z)
+    return y, new_state
+
+
+# ---------------------------------------------------------------------------
+# seeded inputs for the hot-path configurations
+# ---------------------------------------------------------------------------
+
+def _softplus_inv(v):
+    return math.log(math.expm1(v))
+
+
+def selective_scan_inputs(batch, dim, length, dstate, groups=1, seed=1000,
+                          act_dtype=torch.float32, delta_std=0.5):
+    """Config 0/1/2 distributions: u, z, B, C ~ N(0,1); delta ~ N(0, delta_std^2);
+    delta_bias ~ U(log(e^0.001-1), log(e^0.1-1)); A[d, n] = -(n+1); D ~ N(0,1);
+    dout ~ N(0,1).  Generated in fp32 on the CPU, then cast (activations and
+    B/C to ``act_dtype``; A, D, delta_bias stay fp32)."""
+    g = torch.Generator().manual_seed(seed)
+    u = torch.randn(batch, dim, length, generator=g)
+    delta = torch.randn(batch, dim, length, generator=g) * delta_std
+    lo, hi = _softplus_inv(0.001), _softplus_inv(0.1)
+    delta_bias = torch.rand(dim, generator=g) * (hi - lo) + lo
+    A = -torch.arange(1, dstate + 1, dtype=torch.float32).repeat(dim, 1)
+    B = torch.randn(batch, groups, dstate, length, generator=g)
+    C = torch.randn(batch, groups, dstate, length, generator=g)
+    D = torch.randn(dim, generator=g)
+    z = torch.randn(batch, dim, length, generator=g)
+    dout = torch.randn(batch, dim, length, generator=g)
+    cast = lambda t: t.to(act_dtype)  # noqa: E731
+    return dict(u=cast(u), delta=cast(delta), A=A, B=cast(B), C=cast(C), D=D,
+                z=cast(z), delta_bias=delta_bias, dout=cast(dout))
+
+
+def ssd_inputs(batch, length, nheads, headdim, dstate, ngroups, seed=1003,
+               dtype=torch.bfloat16):
+    """Config 3 distributions: x, B, C ~ N(0,1) in ``dtype``; raw dt fp32 ~ N(0,1)
+    with dt_bias[h] = softplus^-1(u_h), u_h log-uniform on [0.001, 0.1] and
+    dt_softplus=True; A = -U(1, 16) fp32; D ~ N(0,1) per head; dy ~ N(0,1)."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(batch, length, nheads, headdim, generator=g)
+    dt = torch.randn(batch, length, nheads, generator=g)
+    lu = torch.rand(nheads, generator=g) * (math.log(0.1) - math.log(0.001)) + math.log(0.001)
+    dt_bias = torch.log(torch.expm1(torch.exp(lu)))
+    A = -(torch.rand(nheads, generator=g) * 15 + 1)
+    B = torch.randn(batch, length, ngroups, dstate, generator=g)
+    C = torch.randn(batch, length, ngroups, dstate, generator=g)
+    D = torch.randn(nheads, generator=g)
+    dy = torch.randn(batch, length, nheads, headdim, generator=g)
+    return dict(x=x.to(dtype), dt=dt, A=A, B=B.to(dtype), C=C.to(dtype), D=D,
+                dt_bias=dt_bias, dy=dy.to(dtype))
+
+
+def decode_inputs(batch, nheads, headdim, dstate, ngroups, seed=1004,
+                  dtype=torch.bfloat16):
+    """Config 4 distributions: fp32 state ~ N(0,1); x, B, C ~ N(0,1) in ``dtype``;
+    dt and A as in config 3 (dt per head, dt_softplus=True); D ~ N(0,1)."""
+    g = torch.Generator().manual_seed(seed)
+    state = torch.randn(batch, nheads, headdim, dstate, generator=g)
+    x = torch.randn(batch, nheads, headdim, generator=g)
+    dt = torch.randn(batch, nheads, generator=g)
+    lu = torch.rand(nheads, generator=g) * (math.log(0.1) - math.log(0.001)) + math.log(0.001)
+    dt_bias = torch.log(torch.expm1(torch.exp(lu)))
+    A = -(torch.rand(nheads, generator=g) * 15 + 1)
+    B = torch.randn(batch, ngroups, dstate, generator=g)
+    C = torch.randn(batch, ngroups, dstate, generator=g)
+    D = torch.randn(nheads, generator=g)
+    return dict(state=state, x=x.to(dtype), dt=dt, A=A, B=B.to(dtype), C=C.to(dtype),
+                D=D, dt_bias=dt_bias)

@@ -1,0 +1,192 @@
+"""Generate the golden fixtures from the reference's own functions.
+
+Run once in a container that holds the reference source tree:
+
+    REFERENCE_SRC=<path to metal-kernelops>/src python tests/golden/make_golden.py
+
+It imports dbydd/metal-kernelops 0.3.0 and evaluates, on seeded CPU inputs,
+the functions the hot path is defined by:
+
+* ``metal_kernelops.reference.selective_scan``      (reference.py:5-49)
+* ``metal_kernelops.cv.path_scan._scan_reference``  (cv/path_scan.py:579-605),
+  wrapped in the epilogue of ``scan.selective_scan`` (scan.py:311-320), with
+  autograd for the gradients
+* ``metal_kernelops.cv.mamba2_chunk_scan_reference`` (cv/mamba2_chunk.py:681-723)
+* ``metal_kernelops.cv.mamba2_chunk_scan``  (the CPU composition, :617-678)
+* ``metal_kernelops.cv.mamba2_state_update_reference`` (cv/mamba2_state.py:822-849)
+
+The outputs go to ``tests/golden/*.pt``.  The test suite never imports the
+reference; it only reads these files.
+"""
+
+import os
+import pathlib
+import sys
+
+import torch
+import torch.nn.functional as F
+
+HERE = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, os.environ.get("REFERENCE_SRC", "/root/reference/src"))
+
+from metal_kernelops import reference as stepwise  # noqa: E402
+from metal_kernelops.cv import mamba2_chunk_scan, mamba2_chunk_scan_reference  # noqa: E402
+from metal_kernelops.cv import mamba2_state_update_reference  # noqa: E402
+from metal_kernelops.cv.path_scan import _scan_reference  # noqa: E402
+
+sys.path.insert(0, str(HERE.parent.parent))
+from oracle.ssm_oracle import selective_scan_inputs  # noqa: E402
+
+torch.set_num_threads(8)
+
+
+def _leaf(t):
+    return None if t is None else t.detach().clone().requires_grad_(True)
+
+
+def selective_scan_cases():
+    """Mamba-1: config 0 plus grouped / odd-size variants, fp64."""
+    cases = {}
+    shapes = {
+        "config0": (2, 8, 64, 16, 1),
+        "grouped": (2, 8, 24, 5, 2),
+        "per_channel_groups": (1, 4, 9, 3, 4),
+        "thirty_two_states": (1, 4, 11, 32, 2),
+    }
+    for idx, (name, (b, d, l, n, g)) in enumerate(shapes.items()):
+        inp = selective_scan_inputs(b, d, l, n, g, seed=1000 + idx, act_dtype=torch.float64)
+        inp = {k: v.double() for k, v in inp.items()}
+        # stepwise reference (forward only, as in the original)
+        dt_eff = F.softplus(inp["delta"] + inp["delta_bias"][..., None])
+        y_step = stepwise.selective_scan(inp["u"], dt_eff, inp["A"], inp["B"], inp["C"])
+        # differentiable reference with the selective_scan epilogue
+        names = ("u", "delta", "A", "B", "C", "D", "z", "delta_bias")
+        leaves = {k: _leaf(inp[k]) for k in names}
+        dt = leaves["delta"] + leaves["delta_bias"][..., None]
+        dt = F.softplus(dt)
+        out = _scan_reference(leaves["u"], dt, leaves["A"], leaves["B"], leaves["C"])
+        out = out + leaves["u"] * leaves["D"][..., None]
+        out = out * F.silu(leaves["z"])
+        grads = torch.autograd.grad(out, [leaves[k] for k in names], inp["dout"])
+        cases[name] = {
+            "inputs": inp,
+            "y_stepwise_scan": y_step,
+            "y": out.detach(),
+            "grads": dict(zip(names, grads)),
+        }
+    # cumsum known answer (verify_path_scan.py:125-159): A=0, dt=1, B=C=1
+    g = torch.Generator().manual_seed(77)
+    u = torch.randn(1, 1, 12, generator=g, dtype=torch.float64)
+    y = _scan_reference(u, torch.ones_like(u), torch.zeros(1, 1, dtype=torch.float64),
+                        torch.ones(1, 1, 1, 12, dtype=torch.float64),
+                        torch.ones(1, 1, 1, 12, dtype=torch.float64))
+    cases["cumsum_kat"] = {"u": u, "y": y}
+    return cases
+
+
+def _ssd_problem(batch, length, nheads, headdim, ngroups, dstate, seed):
+    # same draw order as benchmarks/verify_mamba2_chunk.py:_problem/_options
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(batch, length, nheads, headdim, generator=gen)
+    dt = torch.randn(batch, length, nheads, generator=gen)
+    A = -torch.exp(torch.rand(nheads, generator=gen))
+    B = torch.randn(batch, length, ngroups, dstate, generator=gen)
+    C = torch.randn(batch, length, ngroups, dstate, generator=gen)
+    gen = torch.Generator().manual_seed(seed + 10)
+    opts = dict(
+        D=torch.randn(nheads, generator=gen),
+        z=torch.randn(batch, length, nheads, headdim, generator=gen),
+        dt_bias=torch.randn(nheads, generator=gen) * 0.1,
+        initial_states=torch.randn(batch, nheads, headdim, dstate, generator=gen) * 0.1,
+    )
+    return dict(x=x, dt=dt, A=A, B=B, C=C), opts
+
+
+def ssd_cases():
+    cases = {}
+    shapes = {
+        "ragged": (2, 13, 4, 6, 2, 5),
+        "gqa1": (1, 16, 4, 4, 1, 4),
+        "mha": (2, 9, 4, 3, 4, 3),
+        "short": (1, 5, 2, 2, 1, 3),
+    }
+    names = ("x", "dt", "A", "B", "C", "D", "z", "dt_bias", "initial_states")
+    for seed, (name, shape) in enumerate(shapes.items()):
+        base, opts = _ssd_problem(*shape, seed=seed)
+        inp = {k: v.double() for k, v in {**base, **opts}.items()}
+        leaves = {k: _leaf(inp[k]) for k in names}
+        y, s = mamba2_chunk_scan_reference(
+            leaves["x"], leaves["dt"], leaves["A"], leaves["B"], leaves["C"],
+            D=leaves["D"], z=leaves["z"], dt_bias=leaves["dt_bias"], dt_softplus=True,
+            initial_states=leaves["initial_states"])
+        gen = torch.Generator().manual_seed(seed + 50)
+        wy = torch.randn(y.shape, generator=gen, dtype=torch.float64)
+        ws = torch.randn(s.shape, generator=gen, dtype=torch.float64)
+        grads = torch.autograd.grad((y * wy).sum() + (s * ws).sum(), [leaves[k] for k in names])
+        # the reference's own CPU composition, fp32, chunk 4
+        f32 = {k: v.float() for k, v in inp.items()}
+        yc, sc = mamba2_chunk_scan(f32["x"], f32["dt"], f32["A"], f32["B"], f32["C"], 4,
+                                   D=f32["D"], z=f32["z"], dt_bias=f32["dt_bias"],
+                                   dt_softplus=True, initial_states=f32["initial_states"])
+        cases[name] = {"inputs": inp, "y": y.detach(), "final_state": s.detach(),
+                       "wy": wy, "ws": ws, "grads": dict(zip(names, grads)),
+                       "y_composition_f32": yc, "final_composition_f32": sc}
+    # defaults (no options), verify_mamba2_chunk.py:150-157
+    base, _ = _ssd_problem(2, 9, 4, 6, 2, 5, seed=7)
+    inp = {k: v.double() for k, v in base.items()}
+    y, s = mamba2_chunk_scan_reference(inp["x"], inp["dt"], inp["A"], inp["B"], inp["C"])
+    cases["defaults"] = {"inputs": inp, "y": y, "final_state": s}
+    return cases
+
+
+def decode_cases():
+    cases = {}
+    specs = {
+        # name: batch, nheads, dim, dstate, groups, dt_per_row, d_kind, z, bias, softplus
+        "decode": (1, 16, 8, 32, 1, False, "head", True, True, True),
+        "batched": (4, 8, 4, 16, 2, False, "head", True, True, False),
+        "dt_per_element": (2, 4, 6, 8, 2, True, "head", True, True, False),
+        "head_dim_D": (2, 4, 6, 8, 2, False, "head_dim", True, True, False),
+        "no_options": (2, 6, 4, 16, 6, False, "none", False, False, False),
+        "dstate_1": (2, 4, 8, 1, 1, False, "head", True, True, True),
+    }
+    names = ("state", "x", "dt", "A", "B", "C", "D", "z", "dt_bias")
+    for idx, (name, spec) in enumerate(specs.items()):
+        b, h, p, n, g, per_row, d_kind, use_z, use_bias, softplus = spec
+        gen = torch.Generator().manual_seed(7 + idx)
+        inp = {
+            "state": torch.randn(b, h, p, n, generator=gen),
+            "x": torch.randn(b, h, p, generator=gen),
+            "dt": (torch.rand(b, h, p, generator=gen) if per_row else
+                   torch.rand(b, h, generator=gen)) * 0.2,
+            "A": -torch.rand(h, generator=gen) - 0.05,
+            "B": torch.randn(b, g, n, generator=gen),
+            "C": torch.randn(b, g, n, generator=gen),
+            "D": {"none": None, "head": torch.randn(h, generator=gen),
+                  "head_dim": torch.randn(h, p, generator=gen)}[d_kind],
+            "z": torch.randn(b, h, p, generator=gen) if use_z else None,
+            "dt_bias": torch.randn(h, generator=gen) * 0.1 if use_bias else None,
+        }
+        inp = {k: (None if v is None else v.double()) for k, v in inp.items()}
+        leaves = {k: _leaf(inp[k]) for k in names}
+        y, s = mamba2_state_update_reference(*[leaves[k] for k in names], dt_softplus=softplus)
+        wy = torch.randn(y.shape, generator=gen, dtype=torch.float64)
+        ws = torch.randn(s.shape, generator=gen, dtype=torch.float64)
+        present = [k for k in names if leaves[k] is not None]
+        grads = torch.autograd.grad((y * wy).sum() + (s * ws).sum(), [leaves[k] for k in present])
+        cases[name] = {"inputs": {k: v for k, v in inp.items() if v is not None},
+                       "softplus": softplus, "y": y.detach(), "new_state": s.detach(),
+                       "wy": wy, "ws": ws, "grads": dict(zip(present, grads))}
+    return cases
+
+
+def main():
+    torch.save(selective_scan_cases(), HERE / "selective_scan.pt")
+    torch.save(ssd_cases(), HERE / "mamba2_chunk.pt")
+    torch.save(decode_cases(), HERE / "mamba2_state.pt")
+    for f in sorted(HERE.glob("*.pt")):
+        print(f.name, f.stat().st_size)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,112 @@
+"""Host-side checks that need no GPU: the C-ABI library loads and exports every
+symbol ``include/ssm_b200.h`` declares, the ctypes structs match the header's
+layout, and the Python layer enforces the reference's argument contract
+(``ValueError`` for bad shapes and for tensors off the GPU -- there is no CPU
+fallback)."""
+
+import ctypes
+import pathlib
+import re
+
+import pytest
+import torch
+
+ROOT = pathlib.Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "ssm_b200.h"
+
+
+def _declared():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(ssm_\w+)\s*\(", text, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    from metal_kernelops_b200 import _native as nat
+    lib = nat.lib()
+    names = _declared()
+    assert len(names) >= 11
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(names) <= set(nat.EXPORTS) | {"ssm_status_string", "ssm_last_error"}
+    assert lib.ssm_status_string(0) == b"ok"
+
+
+def test_struct_layouts_match_header():
+    """Field order and count of the ctypes mirrors equal the C structs."""
+    from metal_kernelops_b200 import _native as nat
+    text = HEADER.read_text()
+    for cname, struct in (("ssm_selective_scan_params", nat.SelectiveScanParams),
+                          ("ssm_state_update_params", nat.StateUpdateParams),
+                          ("ssm_chunk_scan_params", nat.ChunkScanParams)):
+        body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), text, re.S).group(1)
+        body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+        fields = []
+        for decl in body.split(";"):
+            decl = decl.strip()
+            if not decl:
+                continue
+            names = decl.split(None, 1)[1] if not decl.startswith("const") else decl.split(None, 2)[2]
+            for n in names.split(","):
+                fields.append(n.strip().lstrip("*").strip())
+        assert [f for f, _ in struct._fields_] == fields, cname
+
+
+def test_invalid_arguments_rejected_by_abi():
+    """The C ABI returns a status (no exception, no crash) for bad sizes."""
+    from metal_kernelops_b200 import _native as nat
+    lib = nat.lib()
+    p = nat.SelectiveScanParams()
+    p.batch, p.dim, p.length, p.groups, p.dstate = 1, 6, 4, 4, 16   # groups does not divide dim
+    assert lib.ssm_selective_scan_fwd(p, None) == nat.SSM_ERR_INVALID
+    assert b"divisible" in lib.ssm_last_error()
+    p.groups, p.dstate = 1, 300
+    assert lib.ssm_selective_scan_fwd(p, None) == nat.SSM_ERR_UNSUPPORTED
+    q = nat.StateUpdateParams()
+    q.batch, q.nheads, q.headdim, q.dstate, q.ngroups = 1, 6, 4, 8, 4
+    assert lib.ssm_state_update_fwd(q, None) == nat.SSM_ERR_INVALID
+
+
+def test_selective_scan_contract_on_cpu():
+    import metal_kernelops_b200 as mk
+    u = torch.zeros(1, 4, 8)
+    A = torch.zeros(4, 3)
+    B = torch.zeros(1, 1, 3, 8)
+    with pytest.raises(ValueError, match="runs CUDA kernels"):
+        mk.selective_scan(u, u, A, B, B)
+    with pytest.raises(ValueError):
+        mk.selective_scan(u, u[..., :7], A, B, B)
+    with pytest.raises(ValueError):
+        mk.selective_scan(u, u, A, B.repeat(1, 3, 1, 1), B.repeat(1, 3, 1, 1))
+    with pytest.raises(ValueError):
+        mk.selective_scan(u, u, A, B, B, D=torch.zeros(5))
+
+
+def test_state_update_contract_on_cpu():
+    from metal_kernelops_b200.cv import mamba2_state_update
+    state = torch.zeros(2, 4, 6, 16)
+    x = torch.zeros(2, 4, 6)
+    dt = torch.zeros(2, 4)
+    A = torch.zeros(4)
+    B = torch.zeros(2, 2, 16)
+    with pytest.raises(ValueError, match="runs CUDA kernels"):
+        mamba2_state_update(state, x, dt, A, B, B)
+    with pytest.raises(ValueError):
+        mamba2_state_update(state, x, dt, A, torch.zeros(2, 3, 16), torch.zeros(2, 3, 16))
+    with pytest.raises(ValueError):
+        mamba2_state_update(state, x, dt, A, B, B, out_state=torch.zeros(2, 4, 6))
+
+
+def test_chunk_scan_contract_on_cpu():
+    from metal_kernelops_b200.cv import mamba2_chunk_scan
+    x = torch.zeros(2, 13, 4, 6)
+    dt = torch.zeros(2, 13, 4)
+    A = torch.zeros(4)
+    B = torch.zeros(2, 13, 2, 5)
+    with pytest.raises(ValueError, match="runs CUDA kernels"):
+        mamba2_chunk_scan(x, dt, A, B, B, 5)
+    with pytest.raises(ValueError):
+        mamba2_chunk_scan(x, dt, A, B, B, 5, initial_states=torch.zeros(2, 4, 5, 5))
+    with pytest.raises(ValueError):
+        mamba2_chunk_scan(x, dt, A, B, B, 0)
+    with pytest.raises(ValueError):
+        mamba2_chunk_scan(x, dt, A, torch.zeros(2, 13, 3, 5), torch.zeros(2, 13, 3, 5))

@@ -1,0 +1,207 @@
+"""Mamba-1 selective scan: CUDA kernels vs the fp64 oracle (GPU).
+
+Oracle: ``oracle.selective_scan_ref`` (the reference's ``_scan_reference`` of
+cv/path_scan.py:579-605 wrapped in the epilogue of scan.py:311-320), evaluated
+in float64 on the same rounded inputs, with autograd for the gradients.
+Metrics follow the reference's verifiers: forward max|err|/max|ref|,
+gradients norm-relative.  Tolerances: fp32 forward
+1e-5, fp32 gradients 1e-4, bf16/fp16 inputs 2e-2.
+"""
+
+import pytest
+import torch
+
+from oracle import ssm_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+FWD_TOL = {torch.float32: 1e-5, torch.bfloat16: 2e-2, torch.float16: 2e-2}
+GRAD_TOL = {torch.float32: 1e-4, torch.bfloat16: 2e-2, torch.float16: 2e-2}
+NAMES = ("u", "delta", "A", "B", "C", "D", "z", "delta_bias")
+
+
+def _mk():
+    import metal_kernelops_b200 as mk
+    return mk
+
+
+def _run_pair(inp, dtype, opts=("D", "z", "delta_bias"), softplus=True, grads=True):
+    """Run the CUDA op and the fp64 oracle on the same rounded inputs."""
+    mk = _mk()
+    use = {k: inp[k] for k in NAMES if k in ("u", "delta", "A", "B", "C") or k in opts}
+    dev = {k: v.cuda().requires_grad_(grads) for k, v in use.items()}
+    ref = {k: v.double().requires_grad_(grads) for k, v in use.items()}
+    y = mk.selective_scan(dev["u"], dev["delta"], dev["A"], dev["B"], dev["C"], D=dev.get("D"),
+                          z=dev.get("z"), delta_bias=dev.get("delta_bias"),
+                          delta_softplus=softplus)
+    yr = orc.selective_scan_ref(ref["u"], ref["delta"], ref["A"], ref["B"], ref["C"],
+                                D=ref.get("D"), z=ref.get("z"), delta_bias=ref.get("delta_bias"),
+                                delta_softplus=softplus)
+    assert y.dtype == inp["u"].dtype and y.shape == inp["u"].shape
+    assert torch.isfinite(y).all()
+    err = orc.max_rel(y.float().cpu(), yr)
+    assert err <= FWD_TOL[dtype], f"forward rel {err:.3e}"
+    if not grads:
+        return
+    dout = inp["dout"]
+    keys = list(use)
+    g = torch.autograd.grad(y, [dev[k] for k in keys], dout.cuda())
+    gr = torch.autograd.grad(yr, [ref[k] for k in keys], dout.double())
+    for k, a, b in zip(keys, g, gr):
+        assert a.dtype == dev[k].dtype, k
+        e = orc.norm_rel(a.float().cpu(), b)
+        assert e <= GRAD_TOL[dtype], f"d{k} rel {e:.3e}"
+
+
+@pytest.mark.parametrize("shape", [
+    (2, 8, 64, 16, 1),      # config 0
+    (2, 8, 24, 5, 2),       # grouped, odd dstate
+    (1, 4, 9, 3, 4),        # one channel per group
+    (1, 4, 11, 32, 2),      # 32 states
+    (1, 6, 37, 64, 3),      # 64 states
+    (3, 16, 63, 8, 4),      # L not a multiple of the chunk
+    (1, 1, 1, 16, 1),       # single step, single channel
+    (2, 130, 100, 16, 1),   # several channel tiles, ragged last tile
+    (1, 64, 300, 4, 2),     # dstate 4, many chunks
+])
+def test_fp32_parity(shape):
+    b, d, l, n, g = shape
+    inp = orc.selective_scan_inputs(b, d, l, n, g, seed=11 + l)
+    _run_pair(inp, torch.float32)
+
+
+@pytest.mark.parametrize("opts,softplus", [
+    ((), False), (("D",), False), (("z",), True), (("delta_bias",), False),
+    (("delta_bias",), True), (("D", "z"), False),
+])
+def test_option_matrix(opts, softplus):
+    inp = orc.selective_scan_inputs(2, 12, 45, 16, 2, seed=5)
+    _run_pair(inp, torch.float32, opts=opts, softplus=softplus)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_half_parity(dtype):
+    inp = orc.selective_scan_inputs(2, 40, 150, 16, 1, seed=21, act_dtype=dtype)
+    _run_pair(inp, dtype)
+
+
+@pytest.mark.parametrize("case", ["config0", "grouped", "per_channel_groups", "thirty_two_states"])
+def test_golden_fixture(golden, case):
+    """The reference's own outputs (tests/golden) reproduced from fp32 inputs."""
+    mk = _mk()
+    c = golden("selective_scan")[case]
+    inp = {k: v.float() for k, v in c["inputs"].items()}
+    dev = {k: inp[k].cuda().requires_grad_(True) for k in NAMES}
+    y = mk.selective_scan(dev["u"], dev["delta"], dev["A"], dev["B"], dev["C"], D=dev["D"],
+                          z=dev["z"], delta_bias=dev["delta_bias"], delta_softplus=True)
+    assert orc.max_rel(y.cpu(), c["y"]) <= 1e-5
+    g = torch.autograd.grad(y, [dev[k] for k in NAMES], inp["dout"].cuda())
+    for k, a in zip(NAMES, g):
+        assert orc.norm_rel(a.cpu(), c["grads"][k]) <= 1e-4, k
+
+
+def test_cumsum_kat(golden):
+    mk = _mk()
+    c = golden("selective_scan")["cumsum_kat"]
+    u = c["u"].float().cuda()
+    L = u.shape[-1]
+    y = mk.scan_cuda(u, torch.ones_like(u), torch.zeros(1, 1, device="cuda"),
+                     torch.ones(1, 1, 1, L, device="cuda"), torch.ones(1, 1, 1, L, device="cuda"))
+    assert orc.max_rel(y.cpu(), c["y"]) <= 1e-6
+
+
+def test_degenerate_shapes():
+    mk = _mk()
+    for b, d, l, n, g in [(0, 4, 5, 3, 1), (1, 4, 0, 3, 1), (2, 0, 5, 3, 1)]:
+        inp = orc.selective_scan_inputs(max(b, 1), max(d, 1), max(l, 1), n, 1, seed=3)
+        u = torch.zeros(b, d, l, device="cuda", requires_grad=True)
+        dt = torch.zeros(b, d, l, device="cuda", requires_grad=True)
+        A = torch.zeros(d, n, device="cuda", requires_grad=True)
+        B = torch.zeros(b, g if d else 1, n, l, device="cuda", requires_grad=True)
+        C = torch.zeros_like(B, requires_grad=True)
+        y = mk.selective_scan(u, dt, A, B, C)
+        assert y.shape == (b, d, l)
+        grads = torch.autograd.grad(y.sum(), [u, dt, A, B, C], allow_unused=True)
+        assert all(gr is None or (gr == 0).all() for gr in grads)
+        del inp
+
+
+def test_deterministic_backward():
+    mk = _mk()
+    inp = orc.selective_scan_inputs(2, 256, 200, 16, 1, seed=9)
+    dev = {k: inp[k].cuda().requires_grad_(True) for k in NAMES}
+    runs = []
+    for _ in range(3):
+        y = mk.selective_scan(dev["u"], dev["delta"], dev["A"], dev["B"], dev["C"], D=dev["D"],
+                              z=dev["z"], delta_bias=dev["delta_bias"], delta_softplus=True)
+        runs.append(torch.autograd.grad(y, [dev[k] for k in NAMES], inp["dout"].cuda()))
+    for k, *vals in zip(NAMES, *runs):
+        assert all(torch.equal(vals[0], v) for v in vals[1:]), k
+
+
+def test_inference_saves_nothing():
+    mk = _mk()
+    inp = orc.selective_scan_inputs(1, 8, 40, 16, 1, seed=4)
+    with torch.no_grad():
+        y = mk.selective_scan(*(inp[k].cuda() for k in ("u", "delta", "A", "B", "C")),
+                              D=inp["D"].cuda(), delta_softplus=True)
+    assert y.shape == (1, 8, 40)
+
+
+def test_config1_full_size_slices():
+    """Config 1 at full size (B8 D1536 L2048 N16, bf16).  The oracle checks a
+    slice of channels (channels are independent given B, C), and dB/dC are
+    checked by linearity: the sum over channel slices of their dB equals the
+    full dB."""
+    mk = _mk()
+    inp = orc.selective_scan_inputs(8, 1536, 2048, 16, 1, seed=1001, act_dtype=torch.bfloat16)
+    dev = {k: inp[k].cuda().requires_grad_(True) for k in NAMES}
+    y = mk.selective_scan(dev["u"], dev["delta"], dev["A"], dev["B"], dev["C"], D=dev["D"],
+                          z=dev["z"], delta_bias=dev["delta_bias"], delta_softplus=True)
+    assert torch.isfinite(y).all()
+    g = torch.autograd.grad(y, [dev[k] for k in NAMES], inp["dout"].cuda())
+    grads = dict(zip(NAMES, g))
+    for k, v in grads.items():
+        assert torch.isfinite(v.float()).all(), k
+    # oracle on batch row 3, channels 100..131
+    b, ch = 3, slice(100, 132)
+    sl = {"u": inp["u"][b:b + 1, ch], "delta": inp["delta"][b:b + 1, ch], "A": inp["A"][ch],
+          "B": inp["B"][b:b + 1], "C": inp["C"][b:b + 1], "D": inp["D"][ch],
+          "z": inp["z"][b:b + 1, ch], "delta_bias": inp["delta_bias"][ch]}
+    ref = {k: v.double().requires_grad_(True) for k, v in sl.items()}
+    yr = orc.selective_scan_ref(ref["u"], ref["delta"], ref["A"], ref["B"], ref["C"], D=ref["D"],
+                                z=ref["z"], delta_bias=ref["delta_bias"], delta_softplus=True)
+    assert orc.max_rel(y[b:b + 1, ch].float().cpu(), yr) <= 2e-2
+    gr = torch.autograd.grad(yr, [ref["u"], ref["delta"], ref["z"]],
+                             inp["dout"][b:b + 1, ch].double())
+    for k, want in zip(("u", "delta", "z"), gr):
+        assert orc.norm_rel(grads[k][b:b + 1, ch].float().cpu(), want) <= 2e-2, k
+    # linearity of dB/dC over channel slices
+    parts_B = torch.zeros_like(grads["B"], dtype=torch.float32)
+    parts_C = torch.zeros_like(grads["C"], dtype=torch.float32)
+    for lo in range(0, 1536, 512):
+        s = slice(lo, lo + 512)
+        sub = {k: (dev[k][:, s] if k in ("u", "delta", "z") else dev[k][s] if k in
+                   ("A", "D", "delta_bias") else dev[k]).detach().requires_grad_(True) for k in NAMES}
+        ys = mk.selective_scan(sub["u"], sub["delta"], sub["A"], sub["B"], sub["C"], D=sub["D"],
+                               z=sub["z"], delta_bias=sub["delta_bias"], delta_softplus=True)
+        gb, gc = torch.autograd.grad(ys, [sub["B"], sub["C"]], inp["dout"][:, s].cuda())
+        parts_B += gb.float()
+        parts_C += gc.float()
+    assert orc.norm_rel(parts_B.cpu(), grads["B"].float().cpu()) <= 2e-2
+    assert orc.norm_rel(parts_C.cpu(), grads["C"].float().cpu()) <= 2e-2
+
+
+def test_errors():
+    mk = _mk()
+    inp = orc.selective_scan_inputs(1, 4, 8, 3, 1, seed=2)
+    cu = {k: v.cuda() for k, v in inp.items()}
+    with pytest.raises(ValueError):   # groups must divide dim
+        mk.selective_scan(cu["u"], cu["delta"], cu["A"], cu["B"].repeat(1, 3, 1, 1),
+                          cu["C"].repeat(1, 3, 1, 1))
+    with pytest.raises(ValueError):   # float64 is not a kernel dtype
+        mk.selective_scan(cu["u"].double(), cu["delta"], cu["A"], cu["B"], cu["C"])
+    big = torch.zeros(1, 4, 8, device="cuda")
+    with pytest.raises(ValueError):   # dstate above the supported maximum
+        mk.selective_scan(big, big, torch.zeros(4, 65, device="cuda"),
+                          torch.zeros(1, 1, 65, 8, device="cuda"), torch.zeros(1, 1, 65, 8, device="cuda"))
