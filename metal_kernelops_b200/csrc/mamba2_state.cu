@@ -377,7 +377,9 @@ __global__ void reduce_kernel(const Args a, float* dB, float* dC, float* dA, flo
 // Per-head d dt (dt given per head) when dt is per row: nothing to do; the
 // per-row ddt is written by bwd_kernel.
 
-static int validate(const ssm_state_update_params* p, bool bwd) {
+// mode: 0 = size query (inputs only), 1 = forward, 2 = backward
+static int validate(const ssm_state_update_params* p, int mode) {
+    const bool bwd = mode == 2;
     if (!p) return fail(SSM_ERR_INVALID, "null params");
     if (p->batch < 0 || p->nheads < 1 || p->headdim < 0 || p->dstate < 1 || p->ngroups < 1)
         return fail(SSM_ERR_INVALID, "state_update: bad sizes");
@@ -390,7 +392,7 @@ static int validate(const ssm_state_update_params* p, bool bwd) {
         return fail(SSM_ERR_INVALID, "state_update: null input");
     if (bwd && !empty && (!p->grad_state || !p->dx || !p->ddt || !p->dA || !p->dB || !p->dC))
         return fail(SSM_ERR_INVALID, "state_update bwd: null gradient pointer");
-    if (!bwd && !empty && (!p->new_state || !p->y)) return fail(SSM_ERR_INVALID, "state_update: null output");
+    if (mode == 1 && !empty && (!p->new_state || !p->y)) return fail(SSM_ERR_INVALID, "state_update: null output");
     return SSM_OK;
 }
 
@@ -431,13 +433,13 @@ using namespace ssm;
 using namespace ssm::supd;
 
 extern "C" int ssm_state_update_sizes(const ssm_state_update_params* p, size_t* workspace_bytes) {
-    if (int s = validate(p, false)) return s;
+    if (int s = validate(p, 0)) return s;
     if (workspace_bytes) *workspace_bytes = ws_layout(p).total;
     return SSM_OK;
 }
 
 extern "C" int ssm_state_update_fwd(const ssm_state_update_params* p, void* stream) {
-    if (int s = validate(p, false)) return s;
+    if (int s = validate(p, 1)) return s;
     if (p->batch == 0 || p->headdim == 0) return SSM_OK;
     Args a;
     make_args(p, a);
@@ -455,7 +457,7 @@ extern "C" int ssm_state_update_fwd(const ssm_state_update_params* p, void* stre
 }
 
 extern "C" int ssm_state_update_bwd(const ssm_state_update_params* p, void* stream) {
-    if (int s = validate(p, true)) return s;
+    if (int s = validate(p, 2)) return s;
     if (p->dtype != SSM_F32) return fail(SSM_ERR_UNSUPPORTED, "state_update bwd: inputs must be widened to fp32");
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const bool has_d = p->flags & SSM_HAS_D, d_per_head = p->flags & SSM_D_PER_HEAD;

@@ -540,7 +540,9 @@ static size_t bwd_smem(const Cfg& c) {
     return s + 32;
 }
 
-static int validate(const ssm_selective_scan_params* p, bool bwd) {
+// mode: 0 = size query (inputs only), 1 = forward, 2 = backward
+static int validate(const ssm_selective_scan_params* p, int mode) {
+    const bool bwd = mode == 2;
     if (!p) return fail(SSM_ERR_INVALID, "null params");
     if (p->batch < 0 || p->dim < 0 || p->length < 0 || p->groups < 1 || p->dstate < 1)
         return fail(SSM_ERR_INVALID, "selective_scan: negative size, groups < 1 or dstate < 1");
@@ -561,10 +563,10 @@ static int validate(const ssm_selective_scan_params* p, bool bwd) {
             return fail(SSM_ERR_INVALID, "selective_scan: delta_bias is null");
     }
     if (bwd) {
-        if (!p->dA || (!empty && (!p->dout || !p->du || !p->ddelta || !p->dB || !p->dC || !p->checkpoints)))
+        if ((p->dim * p->dstate > 0 && !p->dA) || (!empty && (!p->dout || !p->du || !p->ddelta || !p->dB || !p->dC || !p->checkpoints)))
             return fail(SSM_ERR_INVALID, "selective_scan bwd: null gradient pointer");
         if ((p->flags & SSM_HAS_Z) && !empty && !p->dz) return fail(SSM_ERR_INVALID, "selective_scan bwd: dz is null");
-    } else if (!empty && !p->y) {
+    } else if (mode == 1 && !empty && !p->y) {
         return fail(SSM_ERR_INVALID, "selective_scan: y is null");
     }
     return SSM_OK;
@@ -642,7 +644,7 @@ using namespace ssm::sscan;
 
 extern "C" int ssm_selective_scan_sizes(const ssm_selective_scan_params* p,
                                         size_t* checkpoint_bytes, size_t* workspace_bytes) {
-    if (int s = validate(p, false)) return s;
+    if (int s = validate(p, 0)) return s;
     Cfg cb;
     bwd_cfg(p->dstate, cb);
     const int64_t nct = ceil_div(p->dim / p->groups, 32 / cb.lpc * kWarps);
@@ -653,7 +655,7 @@ extern "C" int ssm_selective_scan_sizes(const ssm_selective_scan_params* p,
 }
 
 extern "C" int ssm_selective_scan_fwd(const ssm_selective_scan_params* p, void* stream) {
-    if (int s = validate(p, false)) return s;
+    if (int s = validate(p, 1)) return s;
     if (p->batch == 0 || p->dim == 0 || p->length == 0) return SSM_OK;
     Cfg c;
     fwd_cfg(p->dstate, c);
@@ -668,12 +670,12 @@ extern "C" int ssm_selective_scan_fwd(const ssm_selective_scan_params* p, void* 
 }
 
 extern "C" int ssm_selective_scan_bwd(const ssm_selective_scan_params* p, void* stream) {
-    if (int s = validate(p, true)) return s;
+    if (int s = validate(p, 2)) return s;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const bool empty = p->batch == 0 || p->dim == 0 || p->length == 0;
     if (empty) {
         // No steps: every parameter gradient is zero.
-        if (p->dim && p->dstate && cudaMemsetAsync(p->dA, 0, (size_t)(p->dim * p->dstate) * 4, st) != cudaSuccess)
+        if (p->dim && p->dstate && p->dA && cudaMemsetAsync(p->dA, 0, (size_t)(p->dim * p->dstate) * 4, st) != cudaSuccess)
             return check_launch("selective_scan bwd: memset");
         if (p->dD && p->dim) cudaMemsetAsync(p->dD, 0, (size_t)p->dim * 4, st);
         if (p->ddelta_bias && p->dim) cudaMemsetAsync(p->ddelta_bias, 0, (size_t)p->dim * 4, st);

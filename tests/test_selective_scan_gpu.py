@@ -76,6 +76,11 @@ def test_fp32_parity(shape):
 ])
 def test_option_matrix(opts, softplus):
     inp = orc.selective_scan_inputs(2, 12, 45, 16, 2, seed=5)
+    if not softplus:
+        # without the softplus, delta must itself be a positive step size, as in
+        # the reference's verifier inputs (dt = 0.05 + 0.2 * U, verify_path_scan.py:72)
+        inp["delta"] = inp["delta"].abs() * 0.4 + 0.05
+        inp["delta_bias"] = inp["delta_bias"].abs() * 0.01
     _run_pair(inp, torch.float32, opts=opts, softplus=softplus)
 
 
