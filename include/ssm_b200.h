@@ -167,6 +167,21 @@ int ssm_state_update_sizes(const ssm_state_update_params* p, size_t* workspace_b
 int ssm_state_update_fwd(const ssm_state_update_params* p, void* stream);
 int ssm_state_update_bwd(const ssm_state_update_params* p, void* stream);
 
+/* The decode backward for callers that cannot allocate device memory (a
+ * runtime whose device memory is pre-planned and owned elsewhere, or code that
+ * must not touch the allocator where the backward runs).  No counterpart in the
+ * reference.  Same params and results as ssm_state_update_bwd, but
+ * `workspace`/`workspace_bytes` are ignored: the scratch is one fixed device
+ * array inside the library, SSM_STATE_UPDATE_STATIC_SCRATCH_BYTES large and
+ * held by every GPU that loads the library until the process exits.  Problems
+ * whose scratch (ssm_state_update_sizes) exceeds it return SSM_ERR_UNSUPPORTED.
+ * Allocates nothing.  The first call on each device looks up the array's
+ * device address (cudaGetSymbolAddress, with that device current) and caches
+ * it, so make that first call before any stream capture.  All calls share the
+ * array: calls whose kernels overlap on the GPU race and must be serialised. */
+#define SSM_STATE_UPDATE_STATIC_SCRATCH_BYTES ((size_t)8 << 20)
+int ssm_state_update_bwd_noalloc(const ssm_state_update_params* p, void* stream);
+
 /* ------------------------------------------------------------------------- *
  * Mamba-2 SSD chunk scan.
  *

@@ -33,6 +33,7 @@ EXPORTS = (
     "ssm_status_string", "ssm_last_error",
     "ssm_selective_scan_sizes", "ssm_selective_scan_fwd", "ssm_selective_scan_bwd",
     "ssm_state_update_sizes", "ssm_state_update_fwd", "ssm_state_update_bwd",
+    "ssm_state_update_bwd_noalloc",
     "ssm_chunk_scan_sizes", "ssm_chunk_scan_fwd", "ssm_chunk_scan_bwd",
 )
 
@@ -114,6 +115,9 @@ def lib():
                 ctypes.POINTER(StateUpdateParams), ctypes.POINTER(_SZ)]
             handle.ssm_chunk_scan_sizes.argtypes = [
                 ctypes.POINTER(ChunkScanParams), ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]
+            handle.ssm_state_update_bwd_noalloc.restype = ctypes.c_int
+            handle.ssm_state_update_bwd_noalloc.argtypes = [ctypes.POINTER(StateUpdateParams),
+                                                            ctypes.c_void_p]
             for name in ("ssm_selective_scan_sizes", "ssm_state_update_sizes", "ssm_chunk_scan_sizes"):
                 getattr(handle, name).restype = ctypes.c_int
             _lib = handle

@@ -18,6 +18,9 @@
 // deterministic: per-(batch, head) partials of dB, dC, dA, d dt and dD are
 // folded in registers and shared memory inside the CTA, then a second kernel
 // adds them over heads / batch in a fixed order.  No atomics.
+#include <mutex>
+#include <string>
+
 #include "common.cuh"
 
 namespace ssm {
@@ -504,4 +507,73 @@ extern "C" int ssm_state_update_bwd(const ssm_state_update_params* p, void* stre
                                          (p->flags & SSM_HAS_BIAS) ? p->ddt_bias : nullptr,
                                          has_d ? p->dD : nullptr);
     return check_launch("state_update bwd: reduce");
+}
+
+// ----------------------------------------------------------------------------
+// Backward without any allocation.
+//
+// For callers that cannot call cudaMalloc (or any allocating routine) on the
+// path where they run the decode backward -- for example a runtime whose memory
+// is fully pre-planned and owned by someone else, or code that must not touch
+// the device allocator at that point -- this entry point takes its scratch from
+// one fixed array compiled into the library instead of from a caller-supplied
+// workspace.  The array is a file-scope __device__ object: every GPU that loads
+// the library holds its kStaticScratchBytes until the process exits.
+//
+// Only host code needs the array's device address.  In host code the symbol
+// `g_static_scratch` names a host-side stand-in, not device memory, so its
+// address is looked up with cudaGetSymbolAddress once per device (with that
+// device current) on the first call made on that device, and cached.  That
+// first call should therefore happen before any stream capture.
+//
+// All calls on a device share the one array, and it keeps whatever the last
+// call left in it.  The backward writes every scratch element it later reads
+// within the same call, so nothing needs clearing between calls.  Calls whose
+// kernels overlap on the GPU (different streams, or concurrent host threads)
+// race on the array: serialise them.
+namespace ssm {
+namespace supd {
+
+constexpr size_t kStaticScratchBytes = SSM_STATE_UPDATE_STATIC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+static std::mutex g_static_mu;
+static void* g_static_addr[256];   // device address of g_static_scratch, per device ordinal
+
+static int static_scratch(void** out) {
+    int dev = -1;
+    const cudaError_t ge = cudaGetDevice(&dev);
+    if (ge != cudaSuccess)
+        return fail(SSM_ERR_CUDA, std::string("state_update bwd_noalloc: cudaGetDevice: ") + cudaGetErrorString(ge));
+    if (dev < 0 || dev >= 256) return fail(SSM_ERR_UNSUPPORTED, "state_update bwd_noalloc: device ordinal above 255");
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (g_static_addr[dev] == nullptr) {
+        void* addr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&addr, g_static_scratch);
+        if (e != cudaSuccess || addr == nullptr)
+            return fail(SSM_ERR_CUDA, std::string("state_update bwd_noalloc: cudaGetSymbolAddress: ") +
+                                          cudaGetErrorString(e));
+        g_static_addr[dev] = addr;
+    }
+    *out = g_static_addr[dev];
+    return SSM_OK;
+}
+
+}  // namespace supd
+}  // namespace ssm
+
+extern "C" int ssm_state_update_bwd_noalloc(const ssm_state_update_params* p, void* stream) {
+    if (int s = validate(p, 2)) return s;
+    const size_t need = ws_layout(p).total;
+    if (need > kStaticScratchBytes)
+        return fail(SSM_ERR_UNSUPPORTED,
+                    "state_update bwd_noalloc: this problem needs " + std::to_string(need) +
+                        " bytes of scratch but the fixed array holds " + std::to_string(kStaticScratchBytes) +
+                        "; call ssm_state_update_bwd with a workspace instead");
+    void* scratch = nullptr;
+    if (int s = static_scratch(&scratch)) return s;
+    ssm_state_update_params q = *p;
+    q.workspace = scratch;
+    q.workspace_bytes = kStaticScratchBytes;
+    return ssm_state_update_bwd(&q, stream);
 }
