@@ -56,6 +56,8 @@ def _params(x, dt, A, B, C, D, z, dt_bias, init, chunk_size, softplus):
                | (nat.D_PER_HEAD if D is not None and D.dim() == 2 else 0)
                | (nat.HAS_Z if z is not None else 0) | (nat.HAS_BIAS if dt_bias is not None else 0)
                | (nat.SOFTPLUS if softplus else 0) | (nat.HAS_INIT if init is not None else 0))
+    if x.device.type == "meta":
+        return p
     p.x, p.dt, p.A, p.B, p.C = (t.data_ptr() for t in (x, dt, A, B, C))
     p.D = D.data_ptr() if D is not None else None
     p.z = z.data_ptr() if z is not None else None
@@ -81,9 +83,7 @@ def _fwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Tensor, C:
     y = torch.empty_like(x)
     final = torch.empty(batch, nheads, headdim, B.shape[3], dtype=torch.float32, device=x.device)
     saved = torch.empty(saved_bytes // 4, dtype=torch.float32, device=x.device)
-    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
     p.y, p.final_state, p.saved = y.data_ptr(), final.data_ptr(), saved.data_ptr()
-    p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
     nat.check(nat.lib().ssm_chunk_scan_fwd(p, nat.stream_of(x)), "mamba2_chunk_scan")
     return y, final, saved
 
@@ -91,11 +91,9 @@ def _fwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Tensor, C:
 @_fwd.register_fake
 def _(x, dt, A, B, C, D, z, dt_bias, init, chunk_size, softplus, save):
     batch, length, nheads, headdim = x.shape
-    dstate = B.shape[3]
-    q = min(chunk_size, max(length, 1))
-    nc = -(-length // q)
-    return (torch.empty_like(x), x.new_empty(batch, nheads, headdim, dstate, dtype=torch.float32),
-            x.new_empty(batch * nheads * nc * headdim * dstate, dtype=torch.float32))
+    saved_bytes, _ = _sizes(_params(x, dt, A, B, C, D, z, dt_bias, init, chunk_size, softplus))
+    return (torch.empty_like(x), x.new_empty(batch, nheads, headdim, B.shape[3], dtype=torch.float32),
+            x.new_empty(saved_bytes // 4, dtype=torch.float32))
 
 
 @torch.library.custom_op("b200ssm::chunk_scan_bwd", mutates_args=(), device_types="cuda")
@@ -107,16 +105,16 @@ def _bwd(dy: torch.Tensor, dfinal: Optional[torch.Tensor], x: torch.Tensor, dt: 
     _, ws_bytes = _sizes(p)
     dev = x.device
     f32 = dict(dtype=torch.float32, device=dev)
-    e = torch.empty(0, **f32)
     dx = torch.empty_like(x)
     ddt = torch.empty(dt.shape, **f32)
     dA = torch.empty(A.shape, **f32)
     dB = torch.empty(B.shape, **f32)
     dC = torch.empty(C.shape, **f32)
-    dD = torch.empty(D.shape, **f32) if D is not None else e
+    # absent gradients: distinct empty tensors (custom-op returns may not alias)
+    dD = torch.empty(D.shape if D is not None else (0,), **f32)
     dz = torch.empty_like(x) if z is not None else x.new_empty(0)
-    dbias = torch.empty(A.shape, **f32) if dt_bias is not None else e
-    dinit = torch.empty(init.shape, **f32) if init is not None else e
+    dbias = torch.empty(A.shape if dt_bias is not None else (0,), **f32)
+    dinit = torch.empty(init.shape if init is not None else (0,), **f32)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
     p.flags |= nat.HAS_DY
     p.dy = dy.data_ptr()
@@ -137,10 +135,10 @@ def _bwd(dy: torch.Tensor, dfinal: Optional[torch.Tensor], x: torch.Tensor, dt: 
 @_bwd.register_fake
 def _(dy, dfinal, x, dt, A, B, C, D, z, dt_bias, init, saved, chunk_size, softplus):
     f = lambda t: t.new_empty(t.shape, dtype=torch.float32)  # noqa: E731
-    e = x.new_empty(0, dtype=torch.float32)
-    return [torch.empty_like(x), f(dt), f(A), f(B), f(C), f(D) if D is not None else e,
+    e = lambda: x.new_empty(0, dtype=torch.float32)  # noqa: E731
+    return [torch.empty_like(x), f(dt), f(A), f(B), f(C), f(D) if D is not None else e(),
             torch.empty_like(x) if z is not None else x.new_empty(0),
-            f(A) if dt_bias is not None else e, f(init) if init is not None else e]
+            f(A) if dt_bias is not None else e(), f(init) if init is not None else e()]
 
 
 def _setup(ctx, inputs, output):
