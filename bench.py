@@ -142,6 +142,13 @@ def _scan_inputs_rows(cfg, lo, hi):
     return out
 
 
+def _config(args):
+    cfg = dict(CONFIGS[args.config])
+    if args.shape:
+        cfg["batch"], cfg["dim"], cfg["length"] = (int(v) for v in args.shape.split(","))
+    return cfg
+
+
 def _scan_alg_bytes(b, d, l, n, g, s_a=2):
     fwd = 4 * s_a * b * d * l + 2 * s_a * b * g * n * l
     bwd = 7 * s_a * b * d * l + 4 * s_a * b * g * n * l
@@ -152,7 +159,7 @@ def run_scan(args, world, rank, device):
     import torch.distributed as dist
     import metal_kernelops_b200 as mk  # noqa: F401  (registers the ops)
 
-    cfg = CONFIGS[args.config]
+    cfg = _config(args)
     per = cfg["batch"] // world
     lo, hi = rank * per, (rank + 1) * per
     host = _scan_inputs(cfg, lo, hi, device)
@@ -340,6 +347,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--op", default="scan", choices=["scan", "ssd", "decode"])
     ap.add_argument("--config", type=int, default=2, choices=[1, 2])
+    ap.add_argument("--shape", default=None,
+                    help="batch,dim,seqlen override of the config (profiling runs on small cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     world, rank, local = _dist()

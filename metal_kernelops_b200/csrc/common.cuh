@@ -67,6 +67,70 @@ __device__ __forceinline__ float softplus_grad_f(float x) {
 }
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
 
+// 1/x on the MUFU pipe (PTX rcp.approx: max error 2^-23 on [1, 2]).
+__device__ __forceinline__ float rcp_mufu(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// sigmoid(x) = 1 / (1 + 2^(-x log2 e)): two MUFU ops, ~3e-7 relative error.
+__device__ __forceinline__ float sigmoid_fast(float x) {
+    return rcp_mufu(1.0f + exp2_mufu(-x * kLog2e));
+}
+
+// log1p(s) for s in [0, 1] from the area-hyperbolic-tangent series
+//   log(1 + s) = 2 artanh(w) = 2 (w + w^3/3 + w^5/5 + ...),  w = s / (2 + s) <= 1/3,
+// truncated after the w^15 term (relative truncation error < 2e-9), so it keeps
+// full relative accuracy for tiny s where log(1 + s) would lose it.
+__device__ __forceinline__ float log1p_unit(float s) {
+    const float w = s * rcp_mufu(2.0f + s);
+    const float w2 = w * w;
+    float p = 1.0f / 15.0f;
+    p = fmaf(p, w2, 1.0f / 13.0f);
+    p = fmaf(p, w2, 1.0f / 11.0f);
+    p = fmaf(p, w2, 1.0f / 9.0f);
+    p = fmaf(p, w2, 1.0f / 7.0f);
+    p = fmaf(p, w2, 1.0f / 5.0f);
+    p = fmaf(p, w2, 1.0f / 3.0f);
+    p = fmaf(p, w2, 1.0f);
+    return 2.0f * w * p;
+}
+
+// softplus(x) = max(x, 0) + log1p(exp(-|x|)), with torch's threshold rule
+// (x > 20 returns x).  Two MUFU ops and ~15 FMA-pipe instructions.
+__device__ __forceinline__ float softplus_fast(float x) {
+    if (x > 20.0f) return x;
+    return fmaxf(x, 0.0f) + log1p_unit(exp2_mufu(-fabsf(x) * kLog2e));
+}
+// d softplus / dx (torch's backward: 1 above the threshold).
+__device__ __forceinline__ float softplus_grad_fast(float x) {
+    return x > 20.0f ? 1.0f : sigmoid_fast(x);
+}
+
+// paired loads/stores of two consecutive elements as float2
+template <typename T> struct Io2;
+template <> struct Io2<float> {
+    static __device__ __forceinline__ float2 ld(const float* p) { return *reinterpret_cast<const float2*>(p); }
+    static __device__ __forceinline__ void st(float* p, float2 v) { *reinterpret_cast<float2*>(p) = v; }
+};
+template <> struct Io2<__nv_bfloat16> {
+    static __device__ __forceinline__ float2 ld(const __nv_bfloat16* p) {
+        return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+    }
+    static __device__ __forceinline__ void st(__nv_bfloat16* p, float2 v) {
+        *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(v.x, v.y);
+    }
+};
+template <> struct Io2<__half> {
+    static __device__ __forceinline__ float2 ld(const __half* p) {
+        return __half22float2(*reinterpret_cast<const __half2*>(p));
+    }
+    static __device__ __forceinline__ void st(__half* p, float2 v) {
+        *reinterpret_cast<__half2*>(p) = __floats2half2_rn(v.x, v.y);
+    }
+};
+
 // ---------------------------------------------------------- warp reduce ----
 template <int WIDTH>
 __device__ __forceinline__ float sum_low_lanes(float v) {

@@ -7,25 +7,29 @@
 // softplus, D skip and silu(z) gate as separate torch ops.  This file is a
 // different design built for the B200:
 //
-//  * One thread owns one channel and NPT of its states (LPC lanes per channel);
-//    time is walked sequentially, so every exp(delta*A) is evaluated exactly
-//    once in the forward and the per-step output <x, C> is a register sum
-//    (plus a log2(LPC) shuffle).  B and C of the channel's group are staged in
-//    shared memory as fp32 [t][n] and read as broadcasts.
-//  * Bias, softplus, the D skip and the silu(z) gate are fused into the same
-//    kernel; y is written once.
-//  * The forward stores the state entering every kTile-step chunk
-//    (fp32, "checkpoints"); the backward walks the chunks in reverse, recomputes
-//    the chunk from its checkpoint (pass A, which also produces dz, dC and the
-//    output gradient seen by the scan), then replays each TS-step sub-block from
-//    a shared-memory sub-checkpoint with the states and decays kept in
-//    registers, and runs the adjoint recurrence backwards over it (pass B:
-//    du, ddelta, dA, dB).
-//  * The cross-channel sums dB/dC are reduced inside the warp with a butterfly
-//    reduce-scatter, then across the CTA's warps in shared memory, and written
-//    as one deterministic partial per CTA; a small kernel adds the partials and
-//    the per-batch dA/dD/d_bias partials.  No float atomics (the reference uses
-//    them, scan.py:226-227), so the backward is bit-reproducible.
+//  * One thread owns one channel and NPT of its states (LPC lanes per
+//    channel); time is walked sequentially, so every exp(delta*A) is evaluated
+//    once in the forward, on the MUFU pipe, and the per-step output <x, C> is a
+//    register sum (plus log2(LPC) shuffles).
+//  * Every per-step quantity that does not depend on the state -- the bias and
+//    softplus of delta, delta*u, the silu(z) gate and its derivative, the D
+//    skip -- is computed in vectorised phases over the whole staged tile, by
+//    all threads at once, so the sequential loops carry only the recurrence.
+//  * Tiles of u/delta/z(/dout) and of B/C are staged in shared memory with
+//    cp.async (16-byte asynchronous copies, double-buffered in the forward).
+//    B and C are converted to fp32 [t][n] and read as broadcasts.
+//  * The forward stores the state entering every kChunk-step chunk
+//    (fp32 "checkpoints", 1 byte per element per direction at N=16).  The
+//    backward walks chunks in reverse: pass A recomputes the chunk from its
+//    checkpoint (y for dz, dC, sub-checkpoints every kTS steps); pass B replays
+//    each sub-block from its sub-checkpoint with states and decays kept in
+//    registers and runs the adjoint recurrence backwards (du, ddelta, dA, dB).
+//    Two exps per element-state in the backward, one in the forward.
+//  * dB/dC are reduced over the warp's channels with a butterfly
+//    reduce-scatter, over the CTA's warps in shared memory, and written as one
+//    partial per CTA; a small kernel adds the partials and the per-batch
+//    dA/dD/d_bias partials in a fixed order.  No float atomics (the reference
+//    uses them, scan.py:226-227), so the backward is bit-reproducible.
 #include "common.cuh"
 
 namespace ssm {
@@ -33,14 +37,17 @@ namespace sscan {
 
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
-constexpr int kTile = 32;  // time steps per staged tile == checkpoint interval
+constexpr int kChunk = 16;  // checkpoint interval == backward chunk
+constexpr int kFT = 16;     // forward tile
+constexpr int kTS = 4;      // backward sub-block
 
 struct Args {
     int64_t batch, dim, length, groups, dstate, per_group;
-    int64_t ntiles;       // ceil(length / kTile)
+    int64_t nchunks;      // ceil(length / kChunk)
     int64_t nct;          // channel tiles per group
     uint32_t flags;
     int bc_dtype;
+    bool fast;            // 16-byte aligned rows: asynchronous copies allowed
     const void* u; const void* delta; const float* A; const void* B; const void* C;
     const float* D; const void* z; const float* delta_bias;
     void* y; float* ckpt;
@@ -50,215 +57,109 @@ struct Args {
     float* dD_part; float* db_part;   // (batch, dim)
 };
 
-template <typename T> struct Pad { static constexpr int v = 4 / sizeof(T); };  // odd word stride
+// ---------------------------------------------------------- async copies ----
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
-// Stage a [rows][kTile] tile of a (batch, dim, length) tensor into shared memory
-// (row stride kTile + pad), zero-filling rows past `rows_valid` and steps past
-// `len`.  Consecutive threads read consecutive steps of a row.
-template <typename T, int ROWS>
-__device__ __forceinline__ void load_act_tile(T* s, const T* g, int64_t row0, int rows_valid,
-                                              int64_t L, int64_t t0, int len) {
-    constexpr int RS = kTile + Pad<T>::v;
-    for (int i = threadIdx.x; i < ROWS * kTile; i += kThreads) {
-        const int r = i / kTile, t = i % kTile;
-        T v;
-        if (r < rows_valid && t < len) v = g[(row0 + r) * L + t0 + t];
-        else v = T(0.0f);
-        s[r * RS + t] = v;
+// Stage a dense [ROWS][TT] tile of a (batch*dim, length) tensor: rows past
+// `rows` and steps past `len` are zero.  Full tiles of aligned rows go through
+// cp.async; the ragged tail tile and unaligned shapes use plain loads.
+template <typename T, int ROWS, int TT>
+__device__ __forceinline__ void stage_act(T* dst, const T* g, int64_t row0, int rows, int64_t L,
+                                          int64_t t0, int len, bool fast) {
+    constexpr int VT = 16 / sizeof(T);
+    constexpr int CPR = TT / VT;
+    if (fast && len == TT) {
+        for (int i = threadIdx.x; i < ROWS * CPR; i += kThreads) {
+            const int r = i / CPR, q = i % CPR;
+            T* d = dst + r * TT + q * VT;
+            if (r < rows) cp_async16(d, g + (row0 + r) * L + t0 + q * VT);
+            else *reinterpret_cast<uint4*>(d) = make_uint4(0u, 0u, 0u, 0u);
+        }
+    } else {
+        for (int i = threadIdx.x; i < ROWS * TT; i += kThreads) {
+            const int r = i / TT, t = i % TT;
+            dst[i] = (r < rows && t < len) ? g[(row0 + r) * L + t0 + t] : T(0.0f);
+        }
     }
 }
 
-template <typename T, int ROWS>
-__device__ __forceinline__ void store_act_tile(const T* s, T* g, int64_t row0, int rows_valid,
-                                               int64_t L, int64_t t0, int len) {
-    constexpr int RS = kTile + Pad<T>::v;
-    for (int i = threadIdx.x; i < ROWS * kTile; i += kThreads) {
-        const int r = i / kTile, t = i % kTile;
-        if (r < rows_valid && t < len) g[(row0 + r) * L + t0 + t] = s[r * RS + t];
+// Stage B or C of one (batch, group) as raw bytes [NP][bc_pitch(TT)] (the row
+// pitch is TT*4 + 16 bytes whatever the element size: room for fp32 rows, plus
+// 16 bytes so that reading one step of consecutive rows spreads over banks).
+template <int NP, int TT>
+__device__ __forceinline__ void stage_bc(unsigned char* dst, const void* g, int dtype, int64_t bg,
+                                         int64_t N, int64_t L, int64_t t0, int len, bool fast) {
+    const int esz = dtype == SSM_F32 ? 4 : 2;
+    const int cpr = TT * esz / 16;
+    const unsigned char* gb = reinterpret_cast<const unsigned char*>(g);
+    constexpr int pitch = TT * 4 + 16;
+    if (fast && len == TT) {
+        for (int i = threadIdx.x; i < NP * cpr; i += kThreads) {
+            const int n = i / cpr, q = i % cpr;
+            unsigned char* d = dst + n * pitch + q * 16;
+            if (n < N) cp_async16(d, gb + ((bg * N + n) * L + t0) * esz + q * 16);
+            else *reinterpret_cast<uint4*>(d) = make_uint4(0u, 0u, 0u, 0u);
+        }
+    } else {
+        for (int i = threadIdx.x; i < NP * TT; i += kThreads) {
+            const int n = i / TT, t = i % TT;
+            unsigned char* d = dst + n * pitch + t * esz;
+            const float v = (n < N && t < len) ? ld_any(g, (bg * N + n) * L + t0 + t, dtype) : 0.0f;
+            if (esz == 4) *reinterpret_cast<float*>(d) = v;
+            else if (dtype == SSM_BF16) *reinterpret_cast<__nv_bfloat16*>(d) = __float2bfloat16_rn(v);
+            else *reinterpret_cast<__half*>(d) = __float2half_rn(v);
+        }
     }
 }
 
-// B or C of one (batch, group) as fp32 [kTile][NP] (NP >= dstate, zero padded).
-template <int NP>
-__device__ __forceinline__ void load_bc_tile(float* s, const void* g, int dtype, int64_t bg,
-                                             int64_t N, int64_t L, int64_t t0, int len) {
-    for (int i = threadIdx.x; i < NP * kTile; i += kThreads) {
-        const int n = i / kTile, t = i % kTile;
-        float v = 0.0f;
-        if (n < N && t < len) v = ld_any(g, (bg * N + n) * L + t0 + t, dtype);
-        s[t * NP + n] = v;
-    }
+__device__ __forceinline__ float raw_bc(const unsigned char* base, int n, int t, int TT, int dtype) {
+    const unsigned char* p = base + n * (TT * 4 + 16);
+    if (dtype == SSM_F32) return reinterpret_cast<const float*>(p)[t];
+    if (dtype == SSM_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[t]);
+    return __half2float(reinterpret_cast<const __half*>(p)[t]);
 }
 
 // ------------------------------------------------------------------ forward --
+template <typename T, int CPC, int NP>
+struct FwdLayout {
+    static constexpr int TT = kFT;
+    static constexpr size_t o_raw = 0;                                        // [3][CPC][TT] T
+    static constexpr size_t o_rbc = o_raw + 3 * CPC * TT * sizeof(T);         // [2][NP][TT*4+16] B
+    static constexpr size_t o_dvu = o_rbc + 2 * NP * (TT * 4 + 16);           // [CPC][TT+1] float2
+    static constexpr size_t o_bc = o_dvu + (size_t)CPC * (TT + 1) * 8;        // [2][TT][NP] float
+    static constexpr size_t o_ch = o_bc + 2 * TT * NP * 4;                    // [2][CPC] float
+    static constexpr size_t bytes = o_ch + 2 * CPC * 4;
+};
+
 template <typename T, int NPT, int LPC>
 __global__ void __launch_bounds__(kThreads)
 fwd_kernel(const Args a) {
     constexpr int CPW = 32 / LPC;
     constexpr int CPC = CPW * kWarps;
     constexpr int NP = NPT * LPC;
-    constexpr int RS = kTile + Pad<T>::v;
+    constexpr int NH = NPT / 2;
+    constexpr int TT = kFT;
+    constexpr int FS = TT + 1;
+    using Lay = FwdLayout<T, CPC, NP>;
+    static_assert(NPT % 4 == 0, "NPT must be a multiple of 4");
 
     extern __shared__ __align__(16) unsigned char smem[];
-    T* us = reinterpret_cast<T*>(smem);
-    T* ds = us + CPC * RS;
-    T* zs = ds + CPC * RS;
-    T* ys = zs + CPC * RS;
-    float* Bs = reinterpret_cast<float*>(ys + CPC * RS);
-    Bs = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(Bs) + 15) & ~uintptr_t(15));
-    float* Cs = Bs + kTile * NP;
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int cw = lane / LPC, sub = lane % LPC;
-    const int c = warp * CPW + cw;
-    const int64_t ct = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
-    const int64_t dl0 = ct * CPC;                       // first channel of the tile, within group
-    const int rows = (int)min64(CPC, a.per_group - dl0);
-    const int64_t d0 = g * a.per_group + dl0;           // first global channel
-    const int64_t row0 = b * a.dim + d0;                // first (batch, channel) row
-    const bool cvalid = c < rows;
-    const int64_t d = d0 + c;
-    const int64_t N = a.dstate, L = a.length;
-    const bool has_d = a.flags & SSM_HAS_D, has_z = a.flags & SSM_HAS_Z;
-    const bool has_bias = a.flags & SSM_HAS_BIAS, softplus = a.flags & SSM_SOFTPLUS;
-
-    float An[NPT];
-#pragma unroll
-    for (int j = 0; j < NPT; ++j) {
-        const int n = sub * NPT + j;
-        An[j] = (cvalid && n < N) ? a.A[d * N + n] : 0.0f;
-    }
-    const float Dd = (has_d && cvalid) ? a.D[d] : 0.0f;
-    const float bias = (has_bias && cvalid) ? a.delta_bias[d] : 0.0f;
-    float x[NPT];
-#pragma unroll
-    for (int j = 0; j < NPT; ++j) x[j] = 0.0f;
-
-    const T* ug = reinterpret_cast<const T*>(a.u);
-    const T* dg = reinterpret_cast<const T*>(a.delta);
-    const T* zg = reinterpret_cast<const T*>(a.z);
-    T* yg = reinterpret_cast<T*>(a.y);
-    const int64_t bg = b * a.groups + g;
-
-    for (int64_t tile = 0; tile < a.ntiles; ++tile) {
-        const int64_t t0 = tile * kTile;
-        const int len = (int)min64(kTile, L - t0);
-        __syncthreads();
-        load_act_tile<T, CPC>(us, ug, row0, rows, L, t0, len);
-        load_act_tile<T, CPC>(ds, dg, row0, rows, L, t0, len);
-        if (has_z) load_act_tile<T, CPC>(zs, zg, row0, rows, L, t0, len);
-        load_bc_tile<NP>(Bs, a.B, a.bc_dtype, bg, N, L, t0, len);
-        load_bc_tile<NP>(Cs, a.C, a.bc_dtype, bg, N, L, t0, len);
-        __syncthreads();
-
-        if (a.ckpt != nullptr && cvalid) {
-            float* cp = a.ckpt + ((b * a.ntiles + tile) * a.dim + d) * N;
-#pragma unroll
-            for (int j = 0; j < NPT; ++j) {
-                const int n = sub * NPT + j;
-                if (n < N) cp[n] = x[j];
-            }
-        }
-
-        for (int t = 0; t < len; ++t) {
-            float dv = ldf(&ds[c * RS + t]) + bias;
-            if (softplus) dv = softplus_f(dv);
-            const float uv = ldf(&us[c * RS + t]);
-            const float du = dv * uv;
-            const float dl = dv * kLog2e;
-            const float* Bt = Bs + t * NP + sub * NPT;
-            const float* Ct = Cs + t * NP + sub * NPT;
-            float acc = 0.0f;
-#pragma unroll
-            for (int j = 0; j < NPT; ++j) {
-                const float da = exp2_mufu(dl * An[j]);
-                x[j] = fmaf(da, x[j], du * Bt[j]);
-                acc = fmaf(x[j], Ct[j], acc);
-            }
-            acc = sum_low_lanes<LPC>(acc);
-            if (sub == 0) {
-                float out = fmaf(uv, Dd, acc);
-                if (has_z) {
-                    const float zv = ldf(&zs[c * RS + t]);
-                    out *= zv * sigmoid_f(zv);
-                }
-                stf(&ys[c * RS + t], out);
-            }
-        }
-        __syncthreads();
-        store_act_tile<T, CPC>(ys, yg, row0, rows, L, t0, len);
-    }
-}
-
-// ----------------------------------------------------------------- backward --
-// Butterfly reduce-scatter of v[V] over the lanes that differ in lane bits
-// [LO, 5).  Returns the first state index (within the thread's NPT) of the
-// `V >> min(V_levels)` sums it ends up holding; `owner` is false on lanes whose
-// sums duplicate another lane's (levels past log2(V) are plain all-reduces).
-template <int V, int LO>
-__device__ __forceinline__ int reduce_scatter(float (&v)[V], int lane, bool& owner) {
-    int base = 0;
-    owner = true;
-    int cur = V;
-#pragma unroll
-    for (int bit = 4; bit >= LO; --bit) {
-        const int o = 1 << bit;
-        const bool hi = (lane >> bit) & 1;
-        if (cur > 1) {
-            const int half = cur / 2;
-#pragma unroll
-            for (int i = 0; i < V / 2; ++i) {
-                if (i < half) {
-                    const float send = hi ? v[i] : v[half + i];
-                    const float keep = hi ? v[half + i] : v[i];
-                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-                }
-            }
-            if (hi) base += half;
-            cur = half;
-        } else {
-            v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
-            if (hi) owner = false;
-        }
-    }
-    return base;
-}
-
-template <int V, int LO>
-constexpr int scatter_kept() {
-    int cur = V;
-    for (int bit = 4; bit >= LO; --bit) if (cur > 1) cur /= 2;
-    return cur;
-}
-
-template <typename T, int NPT, int LPC, int TS>
-__global__ void __launch_bounds__(kThreads)
-bwd_kernel(const Args a) {
-    constexpr int CPW = 32 / LPC;
-    constexpr int CPC = CPW * kWarps;
-    constexpr int NP = NPT * LPC;
-    constexpr int NPW = NP + 1;
-    constexpr int RS = kTile + Pad<T>::v;
-    constexpr int FS = kTile + 1;
-    constexpr int LO = (LPC == 1) ? 0 : (LPC == 2) ? 1 : (LPC == 4) ? 2 : (LPC == 8) ? 3 : 4;
-    constexpr int KEPT = scatter_kept<NPT, LO>();
-    constexpr int NSB = kTile / TS;
-
-    extern __shared__ __align__(16) unsigned char smem[];
-    T* us = reinterpret_cast<T*>(smem);
-    T* ds = us + CPC * RS;          // raw delta, overwritten by ddelta
-    T* zs = ds + CPC * RS;          // z, overwritten by dz
-    T* gs = zs + CPC * RS;          // dout, overwritten by du
-    float* fbase = reinterpret_cast<float*>(
-        (reinterpret_cast<uintptr_t>(gs + CPC * RS) + 15) & ~uintptr_t(15));
-    float* dps = fbase;                     // delta after bias/softplus  [CPC][FS]
-    float* gps = dps + CPC * FS;            // gradient seen by the scan  [CPC][FS]
-    float* Bs = gps + CPC * FS;             // [kTile][NP]
-    Bs = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(Bs) + 15) & ~uintptr_t(15));
-    float* Cs = Bs + kTile * NP;
-    float* dBw = Cs + kTile * NP;           // [kWarps][kTile][NPW]
-    float* dCw = dBw + kWarps * kTile * NPW;
-    float* sck = dCw + kWarps * kTile * NPW;  // [NSB][NPT][kThreads]
+    T* raw = reinterpret_cast<T*>(smem + Lay::o_raw);
+    T* ru = raw;
+    T* rd = raw + CPC * TT;
+    T* rz = raw + 2 * CPC * TT;
+    unsigned char* rbc = smem + Lay::o_rbc;
+    float2* dvu = reinterpret_cast<float2*>(smem + Lay::o_dvu);   // (delta' log2e, delta' u) -> y in .x
+    float* Bs = reinterpret_cast<float*>(smem + Lay::o_bc);
+    float* Cs = Bs + TT * NP;
+    float* Dch = reinterpret_cast<float*>(smem + Lay::o_ch);
+    float* bch = Dch + CPC;
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -274,116 +175,419 @@ bwd_kernel(const Args a) {
     const int64_t N = a.dstate, L = a.length;
     const bool has_d = a.flags & SSM_HAS_D, has_z = a.flags & SSM_HAS_Z;
     const bool has_bias = a.flags & SSM_HAS_BIAS, softplus = a.flags & SSM_SOFTPLUS;
+    const int64_t bg = b * a.groups + g;
+    const T* ug = reinterpret_cast<const T*>(a.u);
+    const T* dg = reinterpret_cast<const T*>(a.delta);
+    const T* zg = reinterpret_cast<const T*>(a.z);
+    T* yg = reinterpret_cast<T*>(a.y);
 
-    float An[NPT], q[NPT], dA[NPT];
-#pragma unroll
-    for (int j = 0; j < NPT; ++j) {
-        const int n = sub * NPT + j;
-        An[j] = (cvalid && n < N) ? a.A[d * N + n] : 0.0f;
-        q[j] = 0.0f;
-        dA[j] = 0.0f;
+    for (int i = tid; i < CPC; i += kThreads) {
+        Dch[i] = (has_d && i < rows) ? a.D[d0 + i] : 0.0f;
+        bch[i] = (has_bias && i < rows) ? a.delta_bias[d0 + i] : 0.0f;
     }
-    const float Dd = (has_d && cvalid) ? a.D[d] : 0.0f;
-    const float bias = (has_bias && cvalid) ? a.delta_bias[d] : 0.0f;
-    float dDacc = 0.0f, dbacc = 0.0f;
+    float2 An2[NH], x2[NH];
+#pragma unroll
+    for (int j = 0; j < NH; ++j) {
+        const int n = sub * NPT + 2 * j;
+        An2[j] = make_float2((cvalid && n < N) ? a.A[d * N + n] : 0.0f,
+                             (cvalid && n + 1 < N) ? a.A[d * N + n + 1] : 0.0f);
+        x2[j] = make_float2(0.0f, 0.0f);
+    }
+
+    const int64_t ntiles = (L + TT - 1) / TT;
+    for (int64_t tile = 0; tile < ntiles; ++tile) {
+        const int64_t t0 = tile * TT;
+        const int len = (int)min64(TT, L - t0);
+        __syncthreads();                       // previous tile's readers are done
+        stage_act<T, CPC, TT>(ru, ug, row0, rows, L, t0, len, a.fast);
+        stage_act<T, CPC, TT>(rd, dg, row0, rows, L, t0, len, a.fast);
+        if (has_z) stage_act<T, CPC, TT>(rz, zg, row0, rows, L, t0, len, a.fast);
+        stage_bc<NP, TT>(rbc, a.B, a.bc_dtype, bg, N, L, t0, len, a.fast);
+        stage_bc<NP, TT>(rbc + NP * (TT * 4 + 16), a.C, a.bc_dtype, bg, N, L, t0, len, a.fast);
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+
+        // phase 0: per-step scalars (two steps per iteration) and B/C
+        for (int i = tid; i < CPC * (TT / 2); i += kThreads) {
+            const int cc = i / (TT / 2), t = 2 * (i % (TT / 2));
+            const float2 dr = Io2<T>::ld(&rd[cc * TT + t]);
+            const float2 ur = Io2<T>::ld(&ru[cc * TT + t]);
+            float d0v = dr.x + bch[cc], d1v = dr.y + bch[cc];
+            if (softplus) {
+                d0v = softplus_fast(d0v);
+                d1v = softplus_fast(d1v);
+            }
+            dvu[cc * FS + t] = make_float2(d0v * kLog2e, d0v * ur.x);
+            dvu[cc * FS + t + 1] = make_float2(d1v * kLog2e, d1v * ur.y);
+        }
+        for (int i = tid; i < NP * TT; i += kThreads) {
+            const int t = i / NP, n = i % NP;
+            Bs[t * NP + n] = raw_bc(rbc, n, t, TT, a.bc_dtype);
+            Cs[t * NP + n] = raw_bc(rbc + NP * (TT * 4 + 16), n, t, TT, a.bc_dtype);
+        }
+        __syncthreads();
+
+        if (a.ckpt != nullptr && (t0 % kChunk) == 0 && cvalid) {
+            float* cp = a.ckpt + ((b * a.nchunks + t0 / kChunk) * a.dim + d) * N;
+#pragma unroll
+            for (int j = 0; j < NH; ++j) {
+                const int n = sub * NPT + 2 * j;
+                if (n < N) cp[n] = x2[j].x;
+                if (n + 1 < N) cp[n + 1] = x2[j].y;
+            }
+        }
+
+        // phase 1: the recurrence, two states per packed instruction
+        float2* vr = dvu + c * FS;
+#pragma unroll 4
+        for (int t = 0; t < len; ++t) {
+            const float2 v = vr[t];
+            const float2 dl2 = make_float2(v.x, v.x), du2 = make_float2(v.y, v.y);
+            const float4* B4 = reinterpret_cast<const float4*>(Bs + t * NP + sub * NPT);
+            const float4* C4 = reinterpret_cast<const float4*>(Cs + t * NP + sub * NPT);
+            float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int q = 0; q < NPT / 4; ++q) {
+                const float4 bq = B4[q], cq = C4[q];
+                const float2 a0 = __fmul2_rn(dl2, An2[2 * q]);
+                const float2 a1 = __fmul2_rn(dl2, An2[2 * q + 1]);
+                const float2 e0 = make_float2(exp2_mufu(a0.x), exp2_mufu(a0.y));
+                const float2 e1 = make_float2(exp2_mufu(a1.x), exp2_mufu(a1.y));
+                x2[2 * q] = __ffma2_rn(e0, x2[2 * q], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
+                x2[2 * q + 1] = __ffma2_rn(e1, x2[2 * q + 1], __fmul2_rn(du2, make_float2(bq.z, bq.w)));
+                acc0 = __ffma2_rn(x2[2 * q], make_float2(cq.x, cq.y), acc0);
+                acc1 = __ffma2_rn(x2[2 * q + 1], make_float2(cq.z, cq.w), acc1);
+            }
+            float yv = (acc0.x + acc0.y) + (acc1.x + acc1.y);
+            yv = sum_low_lanes<LPC>(yv);
+            if (sub == 0) vr[t].x = yv;        // every lane of the channel has read vr[t]
+        }
+        __syncthreads();
+
+        // phase 2: skip, gate, store (two steps per iteration, coalesced along t)
+        for (int i = tid; i < CPC * (TT / 2); i += kThreads) {
+            const int cc = i / (TT / 2), t = 2 * (i % (TT / 2));
+            if (cc >= rows || t >= len) continue;
+            const float2 ur = Io2<T>::ld(&ru[cc * TT + t]);
+            float o0 = fmaf(ur.x, Dch[cc], dvu[cc * FS + t].x);
+            float o1 = fmaf(ur.y, Dch[cc], dvu[cc * FS + t + 1].x);
+            if (has_z) {
+                const float2 zr = Io2<T>::ld(&rz[cc * TT + t]);
+                o0 *= zr.x * sigmoid_fast(zr.x);
+                o1 *= zr.y * sigmoid_fast(zr.y);
+            }
+            T* dst = &yg[(row0 + cc) * L + t0 + t];
+            if (a.fast || t + 1 >= len) {      // fast: even L, aligned pair
+                if (t + 1 < len) Io2<T>::st(dst, make_float2(o0, o1));
+                else stf(dst, o0);
+            } else {
+                stf(dst, o0);
+                stf(dst + 1, o1);
+            }
+        }
+    }
+}
+
+// ----------------------------------------------------------------- backward --
+// The cross-channel sums dB[t][n] and dC[t][n] are butterfly reduce-scatters
+// over the lanes that hold the same states of different channels (lane bits
+// [LO, 5)).  Each lane stores its NPT states in a lane-dependent order -- slot
+// i holds state (i XOR mask) -- chosen so that at every level both partners
+// keep the LOWER half of their slots and send the upper half: a level is then
+// one shuffle and one add per value, with no selects.  After the scatter
+// levels slot i < kept holds the full sum for state (i + mask); the remaining
+// levels (past log2(NPT)) are plain all-reduces, and `owner` marks the one
+// lane of each duplicate set that writes.
+template <int V, int LO>
+struct Scatter {
+    static constexpr int kept() {
+        int cur = V;
+        for (int bit = 4; bit >= LO; --bit)
+            if (cur > 1) cur /= 2;
+        return cur;
+    }
+    static __device__ __forceinline__ int mask(int lane) {
+        int m = 0, cur = V;
+#pragma unroll
+        for (int bit = 4; bit >= LO; --bit) {
+            if (cur > 1) {
+                cur /= 2;
+                if ((lane >> bit) & 1) m |= cur;
+            }
+        }
+        return m;
+    }
+    static __device__ __forceinline__ bool owner(int lane) {
+        int cur = V;
+        bool own = true;
+#pragma unroll
+        for (int bit = 4; bit >= LO; --bit) {
+            if (cur > 1) cur /= 2;
+            else if ((lane >> bit) & 1) own = false;
+        }
+        return own;
+    }
+    static __device__ __forceinline__ void reduce(float (&v)[V]) {
+        int cur = V;
+#pragma unroll
+        for (int bit = 4; bit >= LO; --bit) {
+            const int o = 1 << bit;
+            if (cur > 1) {
+                const int h = cur / 2;
+#pragma unroll
+                for (int i = 0; i < V / 2; ++i)
+                    if (i < h) v[i] += __shfl_xor_sync(0xffffffffu, v[h + i], o);
+                cur = h;
+            } else {
+                v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+            }
+        }
+    }
+};
+
+template <typename T, int CPC, int NP, int NPT>
+struct BwdLayout {
+    static constexpr int K = kChunk;
+    static constexpr int FS = K + 1;
+    static constexpr size_t o_raw = 0;                                        // [4][CPC][K] T
+    static constexpr size_t o_rbc = o_raw + 4 * CPC * K * sizeof(T);          // [2][NP][K*4+16] B
+    static constexpr size_t o_dvu = o_rbc + 2 * NP * (K * 4 + 16);            // [CPC][FS] float2
+    static constexpr size_t o_f = o_dvu + (size_t)CPC * FS * 8;               // [4][CPC][FS] float
+    // four permuted copies of B (then C), copy stride = K*NP + 16 floats so the
+    // copies start 64 bytes apart modulo 128 and a warp's reads spread over banks
+    static constexpr int CS = K * NP + 16;
+    static constexpr size_t o_bc = (o_f + 4 * (size_t)CPC * FS * 4 + 15) / 16 * 16;  // [2][4][CS]
+    static constexpr size_t o_w = o_bc + 2 * 4 * CS * 4;                      // [2][kWarps][K][NP+1]
+    static constexpr size_t o_sck = o_w + 2 * (size_t)kWarps * K * (NP + 1) * 4;  // [K/TS][NPT/2][thr] f2
+    static constexpr size_t o_ch = o_sck + (size_t)(K / kTS) * NPT * kThreads * 4;  // [4][CPC]
+    static constexpr size_t bytes = o_ch + 4 * CPC * 4;
+};
+
+template <typename T, int NPT, int LPC>
+__global__ void __launch_bounds__(kThreads, 3)
+bwd_kernel(const Args a) {
+    constexpr int CPW = 32 / LPC;
+    constexpr int CPC = CPW * kWarps;
+    constexpr int NP = NPT * LPC;
+    constexpr int NH = NPT / 2;
+    constexpr int NPW = NP + 1;
+    constexpr int K = kChunk;
+    constexpr int FS = K + 1;
+    constexpr int TS = kTS;
+    constexpr int LO = (LPC == 1) ? 0 : (LPC == 2) ? 1 : (LPC == 4) ? 2 : (LPC == 8) ? 3 : 4;
+    using Sc = Scatter<NPT, LO>;
+    constexpr int KEPT = Sc::kept();
+    constexpr int HALF = K / 2;          // lanes per channel row in phase C
+    using Lay = BwdLayout<T, CPC, NP, NPT>;
+    static_assert(NPT % 4 == 0, "NPT must be a multiple of 4");
+    static_assert(K % TS == 0 && HALF <= 32 && (32 % HALF) == 0, "chunk shape");
+
+    extern __shared__ __align__(16) unsigned char smem[];
+    T* raw = reinterpret_cast<T*>(smem + Lay::o_raw);
+    T* ru = raw;                  // u
+    T* rd = raw + CPC * K;        // delta
+    T* rz = raw + 2 * CPC * K;    // z
+    T* rg = raw + 3 * CPC * K;    // dout
+    unsigned char* rbc = smem + Lay::o_rbc;
+    float2* dvu = reinterpret_cast<float2*>(smem + Lay::o_dvu);   // (delta', delta'*u)
+    float* gs = reinterpret_cast<float*>(smem + Lay::o_f);        // gradient seen by the scan
+    float* yv = gs + CPC * FS;                                    // scan output (pass A)
+    float* dua = yv + CPC * FS;                                   // sum_n dh*B (pass B)
+    float* dda = dua + CPC * FS;                                  // sum_n dh*a*x_prev*A (pass B)
+    constexpr int CS = Lay::CS;
+    float* Bs = reinterpret_cast<float*>(smem + Lay::o_bc);       // [4 perms][CS]: [K][NP] + pad
+    float* Cs = Bs + 4 * CS;
+    float* dBw = reinterpret_cast<float*>(smem + Lay::o_w);
+    float* dCw = dBw + kWarps * K * NPW;
+    float2* sck = reinterpret_cast<float2*>(smem + Lay::o_sck);
+    float* Dch = reinterpret_cast<float*>(smem + Lay::o_ch);
+    float* bch = Dch + CPC;
+    float* accD = bch + CPC;      // running sum of dD per channel
+    float* accb = accD + CPC;     // running sum of d bias per channel
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int cw = lane / LPC, sub = lane % LPC;
+    const int c = warp * CPW + cw;
+    const int64_t ct = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int64_t dl0 = ct * CPC;
+    const int rows = (int)min64(CPC, a.per_group - dl0);
+    const int64_t d0 = g * a.per_group + dl0;
+    const int64_t row0 = b * a.dim + d0;
+    const bool cvalid = c < rows;
+    const int64_t d = d0 + c;
+    const int64_t N = a.dstate, L = a.length;
+    const bool has_d = a.flags & SSM_HAS_D, has_z = a.flags & SSM_HAS_Z;
+    const bool has_bias = a.flags & SSM_HAS_BIAS, softplus = a.flags & SSM_SOFTPLUS;
+    const int64_t bg = b * a.groups + g;
+    // this lane's state order: slot i holds state sub*NPT + (i ^ pm)
+    const int pm = Sc::mask(lane);
+    const bool own = Sc::owner(lane);
+    const float* Bp = Bs + (pm & 3) * CS + sub * NPT;       // permuted copy, this lane's states
+    const float* Cp = Cs + (pm & 3) * CS + sub * NPT;
+    const int qx = pm >> 2;                                  // float4 index permutation
+
+    for (int i = tid; i < CPC; i += kThreads) {
+        Dch[i] = (has_d && i < rows) ? a.D[d0 + i] : 0.0f;
+        bch[i] = (has_bias && i < rows) ? a.delta_bias[d0 + i] : 0.0f;
+        accD[i] = 0.0f;
+        accb[i] = 0.0f;
+    }
+    float2 An2[NH], q2[NH], dA2[NH];
+#pragma unroll
+    for (int j = 0; j < NH; ++j) {
+        const int n0 = sub * NPT + ((2 * j) ^ pm), n1 = sub * NPT + ((2 * j + 1) ^ pm);
+        An2[j] = make_float2((cvalid && n0 < N) ? a.A[d * N + n0] : 0.0f,
+                             (cvalid && n1 < N) ? a.A[d * N + n1] : 0.0f);
+        q2[j] = make_float2(0.0f, 0.0f);
+        dA2[j] = make_float2(0.0f, 0.0f);
+    }
 
     const T* ug = reinterpret_cast<const T*>(a.u);
     const T* dg = reinterpret_cast<const T*>(a.delta);
     const T* zg = reinterpret_cast<const T*>(a.z);
     const T* gg = reinterpret_cast<const T*>(a.dout);
-    const int64_t bg = b * a.groups + g;
+    T* dug = reinterpret_cast<T*>(a.du);
+    T* ddg = reinterpret_cast<T*>(a.ddelta);
+    T* dzg = reinterpret_cast<T*>(a.dz);
     float* dBp = a.dB_part + (bg * a.nct + ct) * N * L;
     float* dCp = a.dC_part + (bg * a.nct + ct) * N * L;
 
-    for (int64_t tile = a.ntiles - 1; tile >= 0; --tile) {
-        const int64_t t0 = tile * kTile;
-        const int len = (int)min64(kTile, L - t0);
+    for (int64_t tile = a.nchunks - 1; tile >= 0; --tile) {
+        const int64_t t0 = tile * K;
+        const int len = (int)min64(K, L - t0);
         __syncthreads();
-        load_act_tile<T, CPC>(us, ug, row0, rows, L, t0, len);
-        load_act_tile<T, CPC>(ds, dg, row0, rows, L, t0, len);
-        if (has_z) load_act_tile<T, CPC>(zs, zg, row0, rows, L, t0, len);
-        load_act_tile<T, CPC>(gs, gg, row0, rows, L, t0, len);
-        load_bc_tile<NP>(Bs, a.B, a.bc_dtype, bg, N, L, t0, len);
-        load_bc_tile<NP>(Cs, a.C, a.bc_dtype, bg, N, L, t0, len);
+        stage_act<T, CPC, K>(ru, ug, row0, rows, L, t0, len, a.fast);
+        stage_act<T, CPC, K>(rd, dg, row0, rows, L, t0, len, a.fast);
+        if (has_z) stage_act<T, CPC, K>(rz, zg, row0, rows, L, t0, len, a.fast);
+        stage_act<T, CPC, K>(rg, gg, row0, rows, L, t0, len, a.fast);
+        stage_bc<NP, K>(rbc, a.B, a.bc_dtype, bg, N, L, t0, len, a.fast);
+        stage_bc<NP, K>(rbc + NP * (K * 4 + 16), a.C, a.bc_dtype, bg, N, L, t0, len, a.fast);
+        cp_async_commit();
+        cp_async_wait<0>();
         __syncthreads();
 
-        // ---- pass A: forward recompute from the checkpoint ------------------
-        float x[NPT];
-        {
-            const float* cp = a.ckpt + ((b * a.ntiles + tile) * a.dim + d) * N;
-#pragma unroll
-            for (int j = 0; j < NPT; ++j) {
-                const int n = sub * NPT + j;
-                x[j] = (cvalid && n < N) ? cp[n] : 0.0f;
+        // phase 0: per-step scalars (two steps per iteration) and B/C
+        for (int i = tid; i < CPC * HALF; i += kThreads) {
+            const int cc = i / HALF, t = 2 * (i % HALF);
+            const float2 dr = Io2<T>::ld(&rd[cc * K + t]);
+            const float2 ur = Io2<T>::ld(&ru[cc * K + t]);
+            float2 go = Io2<T>::ld(&rg[cc * K + t]);
+            float d0v = dr.x + bch[cc], d1v = dr.y + bch[cc];
+            if (softplus) {
+                d0v = softplus_fast(d0v);
+                d1v = softplus_fast(d1v);
             }
-        }
-        for (int t = 0; t < len; ++t) {
-            if (t % TS == 0) {
-#pragma unroll
-                for (int j = 0; j < NPT; ++j) sck[((t / TS) * NPT + j) * kThreads + tid] = x[j];
-            }
-            const float raw = ldf(&ds[c * RS + t]) + bias;
-            const float dv = softplus ? softplus_f(raw) : raw;
-            const float uv = ldf(&us[c * RS + t]);
-            const float du = dv * uv;
-            const float dl = dv * kLog2e;
-            const float* Bt = Bs + t * NP + sub * NPT;
-            const float* Ct = Cs + t * NP + sub * NPT;
-            float acc = 0.0f;
-#pragma unroll
-            for (int j = 0; j < NPT; ++j) {
-                const float da = exp2_mufu(dl * An[j]);
-                x[j] = fmaf(da, x[j], du * Bt[j]);
-                acc = fmaf(x[j], Ct[j], acc);
-            }
-            const float yv = sum_low_lanes<LPC>(acc);
-            const float gv = ldf(&gs[c * RS + t]);
-            float gpre = gv, dzv = 0.0f;
+            dvu[cc * FS + t] = make_float2(d0v, d0v * ur.x);
+            dvu[cc * FS + t + 1] = make_float2(d1v, d1v * ur.y);
             if (has_z) {
-                const float zv = ldf(&zs[c * RS + t]);
-                const float sg = sigmoid_f(zv);
-                gpre = gv * zv * sg;
-                dzv = gv * fmaf(uv, Dd, yv) * sg * fmaf(zv, 1.0f - sg, 1.0f);
+                const float2 zr = Io2<T>::ld(&rz[cc * K + t]);
+                go.x *= zr.x * sigmoid_fast(zr.x);
+                go.y *= zr.y * sigmoid_fast(zr.y);
             }
-            float v[NPT];
+            gs[cc * FS + t] = go.x;
+            gs[cc * FS + t + 1] = go.y;
+        }
+        // B/C as fp32 [t][n], in the four within-float4 orders (n & 3) ^ p
+        for (int i = tid; i < NP * K; i += kThreads) {
+            const int t = i / NP, n = i % NP;
+            const float bv = raw_bc(rbc, n, t, K, a.bc_dtype);
+            const float cv = raw_bc(rbc + NP * (K * 4 + 16), n, t, K, a.bc_dtype);
 #pragma unroll
-            for (int j = 0; j < NPT; ++j) v[j] = gpre * x[j];
-            bool owner;
-            const int base = reduce_scatter<NPT, LO>(v, lane, owner);
-            if (owner) {
-#pragma unroll
-                for (int i = 0; i < KEPT; ++i) dCw[(warp * kTile + t) * NPW + sub * NPT + base + i] = v[i];
-            }
-            if (sub == 0) {
-                dps[c * FS + t] = dv;
-                gps[c * FS + t] = gpre;
-                if (has_z) stf(&zs[c * RS + t], dzv);
-                dDacc = fmaf(gpre, uv, dDacc);
+            for (int p = 0; p < 4; ++p) {
+                const int slot = (n & ~3) | ((n & 3) ^ p);
+                Bs[p * CS + t * NP + slot] = bv;
+                Cs[p * CS + t * NP + slot] = cv;
             }
         }
-        __syncwarp();
+        __syncthreads();
 
-        // ---- pass B: reverse over sub-blocks --------------------------------
+        // ---- pass A: forward recompute from the checkpoint -----------------
+        float2 x2[NH];
+        {
+            const float* cp = a.ckpt + ((b * a.nchunks + tile) * a.dim + d) * N;
+#pragma unroll
+            for (int j = 0; j < NH; ++j) {
+                const int n0 = sub * NPT + ((2 * j) ^ pm), n1 = sub * NPT + ((2 * j + 1) ^ pm);
+                x2[j] = make_float2((cvalid && n0 < N) ? cp[n0] : 0.0f,
+                                    (cvalid && n1 < N) ? cp[n1] : 0.0f);
+            }
+        }
+        const float2* vr = dvu + c * FS;
+        const float* gr = gs + c * FS;
+        for (int tb = 0; tb < len; tb += TS) {
+#pragma unroll
+            for (int j = 0; j < NH; ++j) sck[((tb / TS) * NH + j) * kThreads + tid] = x2[j];
+#pragma unroll
+            for (int jj = 0; jj < TS; ++jj) {
+                const int t = tb + jj;
+                if (t >= len) break;
+                const float2 v = vr[t];
+                const float dl = v.x * kLog2e;
+                const float2 dl2 = make_float2(dl, dl), du2 = make_float2(v.y, v.y);
+                const float gv = gr[t];
+                const float2 g2 = make_float2(gv, gv);
+                const float4* B4 = reinterpret_cast<const float4*>(Bp + t * NP);
+                const float4* C4 = reinterpret_cast<const float4*>(Cp + t * NP);
+                float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
+                float w[NPT];
+#pragma unroll
+                for (int qq = 0; qq < NPT / 4; ++qq) {
+                    const float4 bq = B4[qq ^ qx], cq = C4[qq ^ qx];
+                    const float2 a0 = __fmul2_rn(dl2, An2[2 * qq]);
+                    const float2 a1 = __fmul2_rn(dl2, An2[2 * qq + 1]);
+                    const float2 e0 = make_float2(exp2_mufu(a0.x), exp2_mufu(a0.y));
+                    const float2 e1 = make_float2(exp2_mufu(a1.x), exp2_mufu(a1.y));
+                    x2[2 * qq] = __ffma2_rn(e0, x2[2 * qq], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
+                    x2[2 * qq + 1] = __ffma2_rn(e1, x2[2 * qq + 1], __fmul2_rn(du2, make_float2(bq.z, bq.w)));
+                    acc0 = __ffma2_rn(x2[2 * qq], make_float2(cq.x, cq.y), acc0);
+                    acc1 = __ffma2_rn(x2[2 * qq + 1], make_float2(cq.z, cq.w), acc1);
+                    const float2 w0 = __fmul2_rn(g2, x2[2 * qq]);
+                    const float2 w1 = __fmul2_rn(g2, x2[2 * qq + 1]);
+                    w[4 * qq + 0] = w0.x;
+                    w[4 * qq + 1] = w0.y;
+                    w[4 * qq + 2] = w1.x;
+                    w[4 * qq + 3] = w1.y;
+                }
+                float ysum = (acc0.x + acc0.y) + (acc1.x + acc1.y);
+                ysum = sum_low_lanes<LPC>(ysum);
+                Sc::reduce(w);
+                if (own) {
+#pragma unroll
+                    for (int i = 0; i < KEPT; ++i) dCw[(warp * K + t) * NPW + sub * NPT + pm + i] = w[i];
+                }
+                if (sub == 0) yv[c * FS + t] = ysum;
+            }
+        }
+
+        // ---- pass B: reverse over sub-blocks ---------------------------------
         for (int sb = (len - 1) / TS; sb >= 0; --sb) {
             const int tb = sb * TS;
             const int nb = min(TS, len - tb);
-            float xh[TS][NPT], ah[TS][NPT];
+            float2 xh[TS][NH], ah[TS][NH];
 #pragma unroll
-            for (int j = 0; j < NPT; ++j) x[j] = sck[(sb * NPT + j) * kThreads + tid];
+            for (int j = 0; j < NH; ++j) x2[j] = sck[(sb * NH + j) * kThreads + tid];
 #pragma unroll
             for (int jj = 0; jj < TS; ++jj) {
                 if (jj < nb) {
-                    const int t = tb + jj;
-                    const float dv = dps[c * FS + t];
-                    const float du = dv * ldf(&us[c * RS + t]);
-                    const float dl = dv * kLog2e;
-                    const float* Bt = Bs + t * NP + sub * NPT;
+                    const float2 v = vr[tb + jj];
+                    const float dl = v.x * kLog2e;
+                    const float2 dl2 = make_float2(dl, dl), du2 = make_float2(v.y, v.y);
+                    const float4* B4 = reinterpret_cast<const float4*>(Bp + (tb + jj) * NP);
 #pragma unroll
-                    for (int j = 0; j < NPT; ++j) {
-                        const float da = exp2_mufu(dl * An[j]);
-                        ah[jj][j] = da;
-                        xh[jj][j] = x[j];
-                        x[j] = fmaf(da, x[j], du * Bt[j]);
+                    for (int qq = 0; qq < NPT / 4; ++qq) {
+                        const float4 bq = B4[qq ^ qx];
+                        const float2 a0 = __fmul2_rn(dl2, An2[2 * qq]);
+                        const float2 a1 = __fmul2_rn(dl2, An2[2 * qq + 1]);
+                        const float2 e0 = make_float2(exp2_mufu(a0.x), exp2_mufu(a0.y));
+                        const float2 e1 = make_float2(exp2_mufu(a1.x), exp2_mufu(a1.y));
+                        ah[jj][2 * qq] = e0;
+                        ah[jj][2 * qq + 1] = e1;
+                        xh[jj][2 * qq] = x2[2 * qq];
+                        xh[jj][2 * qq + 1] = x2[2 * qq + 1];
+                        x2[2 * qq] = __ffma2_rn(e0, x2[2 * qq], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
+                        x2[2 * qq + 1] = __ffma2_rn(e1, x2[2 * qq + 1], __fmul2_rn(du2, make_float2(bq.z, bq.w)));
                     }
                 }
             }
@@ -391,74 +595,138 @@ bwd_kernel(const Args a) {
             for (int jj = TS - 1; jj >= 0; --jj) {
                 if (jj < nb) {
                     const int t = tb + jj;
-                    const float dv = dps[c * FS + t];
-                    const float gpre = gps[c * FS + t];
-                    const float uv = ldf(&us[c * RS + t]);
-                    const float du = dv * uv;
-                    const float* Bt = Bs + t * NP + sub * NPT;
-                    const float* Ct = Cs + t * NP + sub * NPT;
-                    float duacc = 0.0f, ddacc = 0.0f;
-                    float v[NPT];
+                    const float2 v = vr[t];
+                    const float gv = gr[t];
+                    const float2 g2 = make_float2(gv, gv), dv2 = make_float2(v.x, v.x);
+                    const float2 du2 = make_float2(v.y, v.y);
+                    const float4* B4 = reinterpret_cast<const float4*>(Bp + t * NP);
+                    const float4* C4 = reinterpret_cast<const float4*>(Cp + t * NP);
+                    float2 dua2 = make_float2(0.0f, 0.0f), dda2 = make_float2(0.0f, 0.0f);
+                    float w[NPT];
 #pragma unroll
-                    for (int j = 0; j < NPT; ++j) {
-                        const float dh = fmaf(gpre, Ct[j], q[j]);
-                        const float tmp = dh * (ah[jj][j] * xh[jj][j]);
-                        ddacc = fmaf(tmp, An[j], ddacc);
-                        dA[j] = fmaf(tmp, dv, dA[j]);
-                        duacc = fmaf(dh, Bt[j], duacc);
-                        v[j] = dh * du;
-                        q[j] = dh * ah[jj][j];
+                    for (int qq = 0; qq < NPT / 4; ++qq) {
+                        const float4 bq = B4[qq ^ qx], cq = C4[qq ^ qx];
+                        const float2 bb[2] = {make_float2(bq.x, bq.y), make_float2(bq.z, bq.w)};
+                        const float2 cc2[2] = {make_float2(cq.x, cq.y), make_float2(cq.z, cq.w)};
+#pragma unroll
+                        for (int r = 0; r < 2; ++r) {
+                            const int j = 2 * qq + r;
+                            const float2 dh = __ffma2_rn(g2, cc2[r], q2[j]);
+                            const float2 tmp = __fmul2_rn(dh, __fmul2_rn(ah[jj][j], xh[jj][j]));
+                            dda2 = __ffma2_rn(tmp, An2[j], dda2);
+                            dA2[j] = __ffma2_rn(tmp, dv2, dA2[j]);
+                            dua2 = __ffma2_rn(dh, bb[r], dua2);
+                            const float2 wv = __fmul2_rn(dh, du2);
+                            w[2 * j] = wv.x;
+                            w[2 * j + 1] = wv.y;
+                            q2[j] = __fmul2_rn(dh, ah[jj][j]);
+                        }
                     }
-                    duacc = sum_low_lanes<LPC>(duacc);
-                    ddacc = sum_low_lanes<LPC>(ddacc);
-                    bool owner;
-                    const int base = reduce_scatter<NPT, LO>(v, lane, owner);
-                    if (owner) {
+                    const float duacc = sum_low_lanes<LPC>(dua2.x + dua2.y);
+                    const float ddacc = sum_low_lanes<LPC>(dda2.x + dda2.y);
+                    Sc::reduce(w);
+                    if (own) {
 #pragma unroll
-                        for (int i = 0; i < KEPT; ++i) dBw[(warp * kTile + t) * NPW + sub * NPT + base + i] = v[i];
+                        for (int i = 0; i < KEPT; ++i) dBw[(warp * K + t) * NPW + sub * NPT + pm + i] = w[i];
                     }
                     if (sub == 0) {
-                        const float dut = fmaf(dv, duacc, gpre * Dd);
-                        const float ddp = fmaf(uv, duacc, ddacc);
-                        float ddt = ddp;
-                        if (softplus) ddt = ddp * softplus_grad_f(ldf(&ds[c * RS + t]) + bias);
-                        dbacc += ddt;
-                        stf(&gs[c * RS + t], dut);
-                        stf(&ds[c * RS + t], ddt);
+                        dua[c * FS + t] = duacc;
+                        dda[c * FS + t] = ddacc;
                     }
                 }
             }
         }
         __syncthreads();
 
-        // ---- write the chunk's gradients ------------------------------------
-        store_act_tile<T, CPC>(ds, reinterpret_cast<T*>(a.ddelta), row0, rows, L, t0, len);
-        store_act_tile<T, CPC>(gs, reinterpret_cast<T*>(a.du), row0, rows, L, t0, len);
-        if (has_z) store_act_tile<T, CPC>(zs, reinterpret_cast<T*>(a.dz), row0, rows, L, t0, len);
+        // ---- phase C: element-wise gradients, coalesced stores ---------------
+        // i -> (channel, step pair): HALF lanes cover one channel row of the
+        // chunk, so the per-channel sums are reductions over HALF lanes.
+        for (int i = tid; i < CPC * HALF; i += kThreads) {
+            const int cc = i / HALF, t = 2 * (i % HALF);
+            float pD = 0.0f, pb = 0.0f;
+            if (cc < rows && t < len) {
+                const float2 ur = Io2<T>::ld(&ru[cc * K + t]);
+                const float Dv = Dch[cc];
+                float o_du[2], o_dd[2], o_dz[2] = {0.0f, 0.0f};
+                const float uu[2] = {ur.x, ur.y};
+                float2 dr = make_float2(0.0f, 0.0f), zr = make_float2(0.0f, 0.0f), gor = make_float2(0.0f, 0.0f);
+                if (softplus) dr = Io2<T>::ld(&rd[cc * K + t]);
+                if (has_z) {
+                    zr = Io2<T>::ld(&rz[cc * K + t]);
+                    gor = Io2<T>::ld(&rg[cc * K + t]);
+                }
+                const float draw[2] = {dr.x, dr.y}, zz[2] = {zr.x, zr.y}, gg2[2] = {gor.x, gor.y};
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    const int tt = t + k;
+                    const float2 v = dvu[cc * FS + tt];
+                    const float gv = gs[cc * FS + tt];
+                    const float duacc = dua[cc * FS + tt];
+                    o_du[k] = fmaf(v.x, duacc, gv * Dv);
+                    float ddt = fmaf(uu[k], duacc, dda[cc * FS + tt]);
+                    if (softplus) ddt *= softplus_grad_fast(draw[k] + bch[cc]);
+                    o_dd[k] = ddt;
+                    if (has_z) {
+                        const float sg = sigmoid_fast(zz[k]);
+                        o_dz[k] = gg2[k] * fmaf(uu[k], Dv, yv[cc * FS + tt]) * sg * fmaf(zz[k], 1.0f - sg, 1.0f);
+                    }
+                    if (tt < len) {
+                        pD = fmaf(gv, uu[k], pD);
+                        pb += ddt;
+                    }
+                }
+                const int64_t o = (row0 + cc) * L + t0 + t;
+                if (a.fast && t + 1 < len) {
+                    Io2<T>::st(&dug[o], make_float2(o_du[0], o_du[1]));
+                    Io2<T>::st(&ddg[o], make_float2(o_dd[0], o_dd[1]));
+                    if (has_z) Io2<T>::st(&dzg[o], make_float2(o_dz[0], o_dz[1]));
+                } else {
+                    stf(&dug[o], o_du[0]);
+                    stf(&ddg[o], o_dd[0]);
+                    if (has_z) stf(&dzg[o], o_dz[0]);
+                    if (t + 1 < len) {
+                        stf(&dug[o + 1], o_du[1]);
+                        stf(&ddg[o + 1], o_dd[1]);
+                        if (has_z) stf(&dzg[o + 1], o_dz[1]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int o = HALF / 2; o > 0; o >>= 1) {
+                pD += __shfl_xor_sync(0xffffffffu, pD, o);
+                pb += __shfl_xor_sync(0xffffffffu, pb, o);
+            }
+            if ((lane % HALF) == 0) {
+                accD[cc] += pD;
+                accb[cc] += pb;
+            }
+        }
         for (int i = tid; i < N * len; i += kThreads) {
             const int n = i / len, t = i % len;
             float sb_ = 0.0f, sc_ = 0.0f;
 #pragma unroll
             for (int w = 0; w < kWarps; ++w) {
-                sb_ += dBw[(w * kTile + t) * NPW + n];
-                sc_ += dCw[(w * kTile + t) * NPW + n];
+                sb_ += dBw[(w * K + t) * NPW + n];
+                sc_ += dCw[(w * K + t) * NPW + n];
             }
             dBp[n * L + t0 + t] = sb_;
             dCp[n * L + t0 + t] = sc_;
         }
     }
+    __syncthreads();
 
     if (cvalid) {
         float* dap = a.dA_part + (b * a.dim + d) * N;
 #pragma unroll
-        for (int j = 0; j < NPT; ++j) {
-            const int n = sub * NPT + j;
-            if (n < N) dap[n] = dA[j];
+        for (int j = 0; j < NH; ++j) {
+            const int n0 = sub * NPT + ((2 * j) ^ pm), n1 = sub * NPT + ((2 * j + 1) ^ pm);
+            if (n0 < N) dap[n0] = dA2[j].x;
+            if (n1 < N) dap[n1] = dA2[j].y;
         }
-        if (sub == 0) {
-            a.dD_part[b * a.dim + d] = dDacc;
-            a.db_part[b * a.dim + d] = dbacc;
-        }
+    }
+    for (int i = tid; i < rows; i += kThreads) {
+        a.dD_part[b * a.dim + d0 + i] = accD[i];
+        a.db_part[b * a.dim + d0 + i] = accb[i];
     }
 }
 
@@ -471,10 +739,10 @@ __global__ void reduce_kernel(const Args a, float* dB, float* dC, float* dA, flo
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
         if (i < nbc) {
-            const int64_t t = i % L, n = (i / L) % N, bg = i / (L * N);
+            const int64_t t = i % L, n = (i / L) % N, bgi = i / (L * N);
             float sb = 0.0f, sc = 0.0f;
             for (int64_t k = 0; k < a.nct; ++k) {
-                const int64_t off = ((bg * a.nct + k) * N + n) * L + t;
+                const int64_t off = ((bgi * a.nct + k) * N + n) * L + t;
                 sb += a.dB_part[off];
                 sc += a.dC_part[off];
             }
@@ -501,46 +769,29 @@ __global__ void reduce_kernel(const Args a, float* dB, float* dC, float* dA, flo
 // ------------------------------------------------------------------- host ----
 struct Cfg { int npt, lpc; };
 
-static bool fwd_cfg(int64_t N, Cfg& c) {
+// States per thread and lanes per channel.  Fewer lanes per channel mean fewer
+// shuffles per step; more lanes mean more threads, which small batch*dim
+// problems need to fill 148 SMs.
+static bool fwd_cfg(int64_t N, int64_t rows, Cfg& c) {
     if (N <= 4) c = {4, 1};
-    else if (N <= 8) c = {8, 1};
-    else if (N <= 16) c = {16, 1};
-    else if (N <= 32) c = {16, 2};
+    else if (N <= 8) c = rows >= 49152 ? Cfg{8, 1} : Cfg{4, 2};
+    else if (N <= 16) c = rows >= 49152 ? Cfg{16, 1} : rows >= 24576 ? Cfg{8, 2} : Cfg{4, 4};
+    else if (N <= 32) c = rows >= 24576 ? Cfg{16, 2} : Cfg{8, 4};
     else if (N <= 64) c = {16, 4};
     else return false;
     return true;
 }
-static bool bwd_cfg(int64_t N, Cfg& c) {
+static bool bwd_cfg(int64_t N, int64_t rows, Cfg& c) {
     if (N <= 4) c = {4, 1};
     else if (N <= 8) c = {8, 1};
-    else if (N <= 16) c = {8, 2};
+    else if (N <= 16) c = rows >= 24576 ? Cfg{8, 2} : Cfg{4, 4};
     else if (N <= 32) c = {8, 4};
     else if (N <= 64) c = {8, 8};
     else return false;
     return true;
 }
-constexpr int kTS = 8;
 
-template <typename T>
-static size_t fwd_smem(const Cfg& c) {
-    const int cpc = 32 / c.lpc * kWarps, np = c.npt * c.lpc;
-    const int rs = kTile + Pad<T>::v;
-    return align_up(4 * (size_t)cpc * rs * sizeof(T), 16) + 2 * (size_t)kTile * np * 4 + 16;
-}
-template <typename T>
-static size_t bwd_smem(const Cfg& c) {
-    const int cpc = 32 / c.lpc * kWarps, np = c.npt * c.lpc;
-    const int rs = kTile + Pad<T>::v;
-    size_t s = align_up(4 * (size_t)cpc * rs * sizeof(T), 16);
-    s += 2 * (size_t)cpc * (kTile + 1) * 4;
-    s = align_up(s, 16);
-    s += 2 * (size_t)kTile * np * 4;
-    s += 2 * (size_t)kWarps * kTile * (np + 1) * 4;
-    s += (size_t)(kTile / kTS) * c.npt * kThreads * 4;
-    return s + 32;
-}
-
-// mode: 0 = size query (inputs only), 1 = forward, 2 = backward
+// mode: 0 = size query (shapes only), 1 = forward, 2 = backward
 static int validate(const ssm_selective_scan_params* p, int mode) {
     const bool bwd = mode == 2;
     if (!p) return fail(SSM_ERR_INVALID, "null params");
@@ -550,11 +801,12 @@ static int validate(const ssm_selective_scan_params* p, int mode) {
         return fail(SSM_ERR_INVALID, "selective_scan: dim must be divisible by groups");
     if (p->act_dtype < 0 || p->act_dtype > 2 || p->bc_dtype < 0 || p->bc_dtype > 2)
         return fail(SSM_ERR_UNSUPPORTED, "selective_scan: unknown dtype");
-    Cfg c;
-    if (!fwd_cfg(p->dstate, c))
+    if (p->dstate > 64)
         return fail(SSM_ERR_UNSUPPORTED, "selective_scan: dstate above 64 is not supported");
+    if (p->batch > 65535 || p->groups > 65535)
+        return fail(SSM_ERR_UNSUPPORTED, "selective_scan: batch or groups above 65535");
     const bool empty = p->batch == 0 || p->dim == 0 || p->length == 0;
-    if (!empty) {
+    if (mode >= 1 && !empty) {
         if (!p->u || !p->delta || !p->A || !p->B || !p->C)
             return fail(SSM_ERR_INVALID, "selective_scan: null input pointer");
         if ((p->flags & SSM_HAS_D) && !p->D) return fail(SSM_ERR_INVALID, "selective_scan: D is null");
@@ -563,21 +815,29 @@ static int validate(const ssm_selective_scan_params* p, int mode) {
             return fail(SSM_ERR_INVALID, "selective_scan: delta_bias is null");
     }
     if (bwd) {
-        if ((p->dim * p->dstate > 0 && !p->dA) || (!empty && (!p->dout || !p->du || !p->ddelta || !p->dB || !p->dC || !p->checkpoints)))
+        if ((p->dim * p->dstate > 0 && !p->dA) ||
+            (!empty && (!p->dout || !p->du || !p->ddelta || !p->dB || !p->dC || !p->checkpoints)))
             return fail(SSM_ERR_INVALID, "selective_scan bwd: null gradient pointer");
-        if ((p->flags & SSM_HAS_Z) && !empty && !p->dz) return fail(SSM_ERR_INVALID, "selective_scan bwd: dz is null");
+        if ((p->flags & SSM_HAS_Z) && !empty && !p->dz)
+            return fail(SSM_ERR_INVALID, "selective_scan bwd: dz is null");
     } else if (mode == 1 && !empty && !p->y) {
         return fail(SSM_ERR_INVALID, "selective_scan: y is null");
     }
     return SSM_OK;
 }
 
+static bool aligned16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; }
+
 static void make_args(const ssm_selective_scan_params* p, int cpc, Args& a) {
     a.batch = p->batch; a.dim = p->dim; a.length = p->length; a.groups = p->groups;
     a.dstate = p->dstate; a.per_group = p->dim / p->groups;
-    a.ntiles = ceil_div(p->length, kTile);
+    a.nchunks = ceil_div(p->length, kChunk);
     a.nct = ceil_div(a.per_group, cpc);
     a.flags = p->flags; a.bc_dtype = p->bc_dtype;
+    const int64_t ae = p->act_dtype == SSM_F32 ? 4 : 2, be = p->bc_dtype == SSM_F32 ? 4 : 2;
+    a.fast = (p->length * ae) % 16 == 0 && (p->length * be) % 16 == 0 && aligned16(p->u) &&
+             aligned16(p->delta) && aligned16(p->B) && aligned16(p->C) &&
+             (!(p->flags & SSM_HAS_Z) || aligned16(p->z)) && (p->dout == nullptr || aligned16(p->dout));
     a.u = p->u; a.delta = p->delta; a.A = p->A; a.B = p->B; a.C = p->C;
     a.D = p->D; a.z = p->z; a.delta_bias = p->delta_bias;
     a.y = p->y; a.ckpt = p->checkpoints;
@@ -597,8 +857,8 @@ static WsLayout ws_layout(const ssm_selective_scan_params* p, int64_t nct) {
 
 template <typename T, int NPT, int LPC>
 static int launch_fwd(const Args& a, cudaStream_t st) {
-    const Cfg c{NPT, LPC};
-    const size_t sm = fwd_smem<T>(c);
+    constexpr int CPC = 32 / LPC * kWarps;
+    const size_t sm = FwdLayout<T, CPC, NPT * LPC>::bytes;
     auto k = fwd_kernel<T, NPT, LPC>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
         return check_launch("selective_scan fwd: smem attribute");
@@ -609,9 +869,9 @@ static int launch_fwd(const Args& a, cudaStream_t st) {
 
 template <typename T, int NPT, int LPC>
 static int launch_bwd(const Args& a, cudaStream_t st) {
-    const Cfg c{NPT, LPC};
-    const size_t sm = bwd_smem<T>(c);
-    auto k = bwd_kernel<T, NPT, LPC, kTS>;
+    constexpr int CPC = 32 / LPC * kWarps;
+    const size_t sm = BwdLayout<T, CPC, NPT * LPC, NPT>::bytes;
+    auto k = bwd_kernel<T, NPT, LPC>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
         return check_launch("selective_scan bwd: smem attribute");
     dim3 grid((unsigned)a.nct, (unsigned)a.groups, (unsigned)a.batch);
@@ -621,19 +881,29 @@ static int launch_bwd(const Args& a, cudaStream_t st) {
 
 template <typename T>
 static int dispatch_fwd(const Cfg& c, const Args& a, cudaStream_t st) {
-    if (c.npt == 4) return launch_fwd<T, 4, 1>(a, st);
-    if (c.npt == 8) return launch_fwd<T, 8, 1>(a, st);
-    if (c.lpc == 1) return launch_fwd<T, 16, 1>(a, st);
-    if (c.lpc == 2) return launch_fwd<T, 16, 2>(a, st);
-    return launch_fwd<T, 16, 4>(a, st);
+    switch (c.npt * 100 + c.lpc) {
+        case 401: return launch_fwd<T, 4, 1>(a, st);
+        case 402: return launch_fwd<T, 4, 2>(a, st);
+        case 404: return launch_fwd<T, 4, 4>(a, st);
+        case 801: return launch_fwd<T, 8, 1>(a, st);
+        case 802: return launch_fwd<T, 8, 2>(a, st);
+        case 804: return launch_fwd<T, 8, 4>(a, st);
+        case 1601: return launch_fwd<T, 16, 1>(a, st);
+        case 1602: return launch_fwd<T, 16, 2>(a, st);
+        default: return launch_fwd<T, 16, 4>(a, st);
+    }
 }
+
 template <typename T>
 static int dispatch_bwd(const Cfg& c, const Args& a, cudaStream_t st) {
-    if (c.npt == 4) return launch_bwd<T, 4, 1>(a, st);
-    if (c.lpc == 1) return launch_bwd<T, 8, 1>(a, st);
-    if (c.lpc == 2) return launch_bwd<T, 8, 2>(a, st);
-    if (c.lpc == 4) return launch_bwd<T, 8, 4>(a, st);
-    return launch_bwd<T, 8, 8>(a, st);
+    switch (c.npt * 100 + c.lpc) {
+        case 401: return launch_bwd<T, 4, 1>(a, st);
+        case 404: return launch_bwd<T, 4, 4>(a, st);
+        case 801: return launch_bwd<T, 8, 1>(a, st);
+        case 802: return launch_bwd<T, 8, 2>(a, st);
+        case 804: return launch_bwd<T, 8, 4>(a, st);
+        default: return launch_bwd<T, 8, 8>(a, st);
+    }
 }
 
 }  // namespace sscan
@@ -646,10 +916,10 @@ extern "C" int ssm_selective_scan_sizes(const ssm_selective_scan_params* p,
                                         size_t* checkpoint_bytes, size_t* workspace_bytes) {
     if (int s = validate(p, 0)) return s;
     Cfg cb;
-    bwd_cfg(p->dstate, cb);
+    bwd_cfg(p->dstate, p->batch * p->dim, cb);
     const int64_t nct = ceil_div(p->dim / p->groups, 32 / cb.lpc * kWarps);
     if (checkpoint_bytes)
-        *checkpoint_bytes = (size_t)(p->batch * ceil_div(p->length, kTile) * p->dim * p->dstate) * 4;
+        *checkpoint_bytes = (size_t)(p->batch * ceil_div(p->length, kChunk) * p->dim * p->dstate) * 4;
     if (workspace_bytes) *workspace_bytes = ws_layout(p, nct).total;
     return SSM_OK;
 }
@@ -658,7 +928,7 @@ extern "C" int ssm_selective_scan_fwd(const ssm_selective_scan_params* p, void* 
     if (int s = validate(p, 1)) return s;
     if (p->batch == 0 || p->dim == 0 || p->length == 0) return SSM_OK;
     Cfg c;
-    fwd_cfg(p->dstate, c);
+    fwd_cfg(p->dstate, p->batch * p->dim, c);
     Args a;
     make_args(p, 32 / c.lpc * kWarps, a);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -675,16 +945,15 @@ extern "C" int ssm_selective_scan_bwd(const ssm_selective_scan_params* p, void* 
     const bool empty = p->batch == 0 || p->dim == 0 || p->length == 0;
     if (empty) {
         // No steps: every parameter gradient is zero.
-        if (p->dim && p->dstate && p->dA && cudaMemsetAsync(p->dA, 0, (size_t)(p->dim * p->dstate) * 4, st) != cudaSuccess)
-            return check_launch("selective_scan bwd: memset");
+        if (p->dim && p->dstate && p->dA) cudaMemsetAsync(p->dA, 0, (size_t)(p->dim * p->dstate) * 4, st);
         if (p->dD && p->dim) cudaMemsetAsync(p->dD, 0, (size_t)p->dim * 4, st);
         if (p->ddelta_bias && p->dim) cudaMemsetAsync(p->ddelta_bias, 0, (size_t)p->dim * 4, st);
-        size_t nbc = (size_t)(p->batch * p->groups * p->dstate * p->length) * 4;
+        const size_t nbc = (size_t)(p->batch * p->groups * p->dstate * p->length) * 4;
         if (nbc) { cudaMemsetAsync(p->dB, 0, nbc, st); cudaMemsetAsync(p->dC, 0, nbc, st); }
         return check_launch("selective_scan bwd: memset");
     }
     Cfg c;
-    bwd_cfg(p->dstate, c);
+    bwd_cfg(p->dstate, p->batch * p->dim, c);
     Args a;
     make_args(p, 32 / c.lpc * kWarps, a);
     const WsLayout w = ws_layout(p, a.nct);

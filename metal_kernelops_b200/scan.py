@@ -33,7 +33,7 @@ import torch
 
 from . import _native as nat
 
-CHUNK = 32
+CHUNK = 16
 """Steps between the states the forward saves for the backward."""
 
 __all__ = ["CHUNK", "selective_scan", "selective_scan_fn", "scan_cuda"]
