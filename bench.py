@@ -159,16 +159,17 @@ def run_scan(args, world, rank, device):
     import torch.distributed as dist
     import metal_kernelops_b200 as mk  # noqa: F401  (registers the ops)
 
+    from metal_kernelops_b200.parallel import ParamGradBucket, batch_slice
     cfg = _config(args)
-    per = cfg["batch"] // world
-    lo, hi = rank * per, (rank + 1) * per
+    rows = batch_slice(cfg["batch"], rank, world)
+    lo, hi = rows.start, rows.stop
+    per = hi - lo
     host = _scan_inputs(cfg, lo, hi, device)
     dev = {k: v.to(device) for k, v in host.items()}
     u, delta, A, B, C, D, z, bias, dout = (dev[k] for k in
                                            ("u", "delta", "A", "B", "C", "D", "z", "delta_bias", "dout"))
     ops = torch.ops.b200ssm
-    bucket = torch.empty(A.numel() + 2 * A.shape[0], dtype=torch.float32, device=device)
-    n_a = A.numel()
+    bucket = ParamGradBucket([A.shape, D.shape, bias.shape], device)
 
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
 
@@ -184,10 +185,7 @@ def run_scan(args, world, rank, device):
         if e:
             e[2].record()
         if world > 1:
-            bucket[:n_a].copy_(dA.view(-1))
-            bucket[n_a:n_a + A.shape[0]].copy_(dD)
-            bucket[n_a + A.shape[0]:].copy_(db)
-            dist.all_reduce(bucket)
+            bucket.reduce([dA, dD, db])
         if e:
             e[3].record()
         return y
@@ -195,13 +193,15 @@ def run_scan(args, world, rank, device):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
+    # start the clock sampler before the barrier, so that no rank enters the
+    # timed region while another is still setting it up
     clocks = Clocks(torch.cuda.current_device()) if rank == 0 else None
     if clocks:
         clocks.start()
         time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
@@ -232,10 +232,8 @@ def run_scan(args, world, rank, device):
         y = mk.selective_scan(*leaves[:5], D=leaves[5], z=leaves[6], delta_bias=leaves[7],
                               delta_softplus=True)
         gr = torch.autograd.grad(y, leaves, d["dout"])
-        flat = torch.cat([gr[2].reshape(-1), gr[5], gr[7]])
-        if world > 1:
-            dist.all_reduce(flat)
-        return flat.to("cpu")
+        reduced = bucket.reduce([gr[2], gr[5], gr[7]])
+        return [r.to("cpu") for r in reduced]
 
     e2e_step()
     torch.cuda.synchronize()
@@ -253,8 +251,9 @@ def run_scan(args, world, rank, device):
         t = torch.tensor([e2e_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = t.item()
-    h2d = sum(v.numel() * v.element_size() for v in host.values())
-    d2h = (A.numel() + 2 * A.shape[0]) * 4
+    # whole-job bytes per step (every rank copies its own shard)
+    h2d = world * sum(v.numel() * v.element_size() for v in host.values())
+    d2h = world * (A.numel() + 2 * A.shape[0]) * 4
 
     if rank != 0:
         return None
@@ -311,6 +310,126 @@ def _traffic(kernel):
     except Exception:
         pass
     return None
+
+
+# ------------------------------------------------------------ SSD / decode --
+
+def _timed(fn, steps, warmup, world, dist):
+    """Run fn warmup + steps times; CUDA-event device time per step (max over ranks)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        fn()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    return ms
+
+
+def run_ssd(args, world, rank, device):
+    """Mamba-2 SSD chunk scan fwd+bwd, B8 L8192 H80 P64 N128
+    G8 chunk 256, bf16 x/B/C, fp32 dt/A/D, dt_softplus; batch sharded."""
+    import torch.distributed as dist
+    import metal_kernelops_b200  # noqa: F401
+    from metal_kernelops_b200.parallel import batch_slice
+    from oracle.ssm_oracle import ssd_inputs
+    cfg = dict(SSD_CONFIG)
+    if args.shape:
+        cfg["batch"], cfg["length"] = (int(v) for v in args.shape.split(",")[:2])
+    rows = batch_slice(cfg["batch"], rank, world)
+    host = ssd_inputs(cfg["batch"], cfg["length"], cfg["nheads"], cfg["headdim"], cfg["dstate"],
+                      cfg["ngroups"], seed=cfg["seed"])
+    for k in ("x", "dt", "B", "C", "dy"):
+        host[k] = host[k][rows].contiguous()
+    dev = {k: v.to(device) for k, v in host.items()}
+    ops = torch.ops.b200ssm
+
+    def step():
+        y, fin, saved = ops.chunk_scan_fwd(dev["x"], dev["dt"], dev["A"], dev["B"], dev["C"], dev["D"],
+                                           None, dev["dt_bias"], None, cfg["chunk"], True, True)
+        ops.chunk_scan_bwd(dev["dy"], None, dev["x"], dev["dt"], dev["A"], dev["B"], dev["C"], dev["D"],
+                           None, dev["dt_bias"], None, saved, cfg["chunk"], True)
+
+    ms = _timed(step, args.steps, args.warmup, world, dist)
+    if rank != 0:
+        return None
+    units = cfg["batch"] * cfg["length"] * cfg["nheads"] * cfg["headdim"]
+    b = rows.stop - rows.start
+    L, H, P, N, G, Q = (cfg[k] for k in ("length", "nheads", "headdim", "dstate", "ngroups", "chunk"))
+    nc = L // Q
+    # causal-minimal algorithmic flops, forward + backward (SURVEY 8d)
+    flops = b * nc * (3 * G * Q * Q * N + H * (3 * Q * Q * P + 12 * Q * N * P))
+    alg_bytes = b * L * (H * P * 2 * 4 + 2 * G * N * 2 * 2 + H * 4 * 2) + b * H * P * N * 4
+    peaks, kind = _peaks()
+    tflops = flops / (ms / 1e3) / 1e12
+    return {
+        "metric": "mamba2 SSD chunk scan fwd+bwd B*L*H*P elems/s", "value": units / (ms / 1e3),
+        "unit": "elem/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16 storage, fp32 compute", "data": "synthetic (seeded, BASELINE config 3)",
+        "config": {"workload": "mamba2 SSD chunk scan fwd+bwd, BASELINE config 3", **cfg,
+                   "parallelism": f"dp{world} (batch shard)"},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops"], "peak_source": kind,
+                     "alg_flops_per_step": flops,
+                     "hbm_frac": alg_bytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], "traffic": None},
+        "gpu_launches": 8 * args.steps,
+    }
+
+
+def run_decode(args, world, rank, device):
+    """Mamba-2 decode update, B256 H80 P64 N128 G8, fp32 state,
+    bf16 x/B/C, in place (out_state=state), no grad; one step = one token."""
+    import torch.distributed as dist
+    from metal_kernelops_b200.cv import mamba2_state_update
+    from metal_kernelops_b200.parallel import batch_slice
+    from oracle.ssm_oracle import decode_inputs
+    cfg = dict(DECODE_CONFIG)
+    rows = batch_slice(cfg["batch"], rank, world)
+    host = decode_inputs(cfg["batch"], cfg["nheads"], cfg["headdim"], cfg["dstate"], cfg["ngroups"],
+                         seed=cfg["seed"])
+    for k in ("state", "x", "dt", "B", "C"):
+        host[k] = host[k][rows].contiguous()
+    dev = {k: v.to(device) for k, v in host.items()}
+    state = dev["state"]
+
+    def step():
+        with torch.no_grad():
+            mamba2_state_update(state, dev["x"], dev["dt"], dev["A"], dev["B"], dev["C"], D=dev["D"],
+                                dt_bias=dev["dt_bias"], dt_softplus=True, out_state=state)
+
+    ms = _timed(step, args.steps, args.warmup, world, dist)
+    if rank != 0:
+        return None
+    b = rows.stop - rows.start
+    H, P, N, G = cfg["nheads"], cfg["headdim"], cfg["dstate"], cfg["ngroups"]
+    units = cfg["batch"] * H * P * N
+    alg_bytes = b * H * P * N * 8 + b * H * P * (2 + 4) + b * G * N * 2 * 2 + b * H * 4
+    gbs = alg_bytes / (ms / 1e3) / 1e9
+    peaks, kind = _peaks()
+    return {
+        "metric": "mamba2 decode state update state elems/s", "value": units / (ms / 1e3),
+        "unit": "elem/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp32 state, bf16 x/B/C", "data": "synthetic (seeded, BASELINE config 4)",
+        "config": {"workload": "mamba2 decode update, BASELINE config 4 (in place)", **cfg,
+                   "parallelism": f"dp{world} (batch shard)", "l2": "state 671 MB > L2"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"], "peak_source": kind,
+                     "alg_bytes_per_launch": alg_bytes, "traffic": None},
+        "gpu_launches": args.steps,
+    }
 
 
 def cpu_baseline_scan(cfg, threads, budget_s=15.0):
@@ -379,11 +498,9 @@ def main():
         return
 
     if world > 1:
-        import datetime
-        import torch.distributed as dist
+        from metal_kernelops_b200.parallel import init_process_group
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+        init_process_group("nccl", timeout_s=300, device_id=torch.device("cuda", local))
     else:
         torch.cuda.set_device(0)
     device = torch.device("cuda", torch.cuda.current_device())
@@ -391,7 +508,7 @@ def main():
     if args.op == "scan":
         line = run_scan(args, world, rank, device)
     else:
-        raise SystemExit(f"--op {args.op}: not available yet")
+        line = (run_ssd if args.op == "ssd" else run_decode)(args, world, rank, device)
     if rank == 0 and line is not None:
         if world == 1 and not args.no_cpu_baseline and args.op == "scan":
             line["cpu_baseline"] = cpu_baseline_scan(CONFIGS[args.config], threads)
