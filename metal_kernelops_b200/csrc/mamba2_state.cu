@@ -28,7 +28,6 @@ namespace supd {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kRows = 4;  // rows in flight per warp
 
 struct Args {
     int64_t batch, nheads, headdim, dstate, ngroups;
@@ -99,85 +98,90 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 // ------------------------------------------------------------------ forward --
+// Phase 0: the first P threads compute each row's decay a = exp(A d) and input
+// coefficient d x into shared memory (d per row or per head).  Phase 1: warp w
+// owns rows w*kFwdRows ... and issues all of its state loads for one dstate
+// slice before any arithmetic, so every thread keeps kFwdRows 16-byte loads in
+// flight; the register cap (80) keeps three CTAs resident per SM, which puts
+// about 96 KB of state reads in flight per SM.
+constexpr int kFwdRows = 8;
+
 template <typename T, int VEC>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 3)
 fwd_kernel(const Args a) {
+    extern __shared__ float s_rows[];   // [2][headdim]: decay, d*x
     const int64_t bh = blockIdx.x;
     const int64_t b = bh / a.nheads, h = bh % a.nheads;
     const int64_t g = h / (a.nheads / a.ngroups);
-    const int64_t P = a.headdim, N = a.dstate;
+    const int P = (int)a.headdim, N = (int)a.dstate;   // one CTA's P*N fits in int
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool per_row = a.flags & SSM_DT_PER_ROW, has_bias = a.flags & SSM_HAS_BIAS;
     const bool softplus = a.flags & SSM_SOFTPLUS, has_d = a.flags & SSM_HAS_D;
     const bool d_per_head = a.flags & SSM_D_PER_HEAD, has_z = a.flags & SSM_HAS_Z;
-    const T* st = reinterpret_cast<const T*>(a.state);
-    T* ns = reinterpret_cast<T*>(a.new_state);
+    const T* st = reinterpret_cast<const T*>(a.state) + bh * (int64_t)P * N;
+    T* ns = reinterpret_cast<T*>(a.new_state) + bh * (int64_t)P * N;
     const T* Bg = reinterpret_cast<const T*>(a.B) + (b * a.ngroups + g) * N;
     const T* Cg = reinterpret_cast<const T*>(a.C) + (b * a.ngroups + g) * N;
-    const T* xg = reinterpret_cast<const T*>(a.x);
+    const T* xg = reinterpret_cast<const T*>(a.x) + bh * (int64_t)P;
     const T* dtg = reinterpret_cast<const T*>(a.dt);
-    const T* zg = reinterpret_cast<const T*>(a.z);
-    T* yg = reinterpret_cast<T*>(a.y);
+    const T* zg = reinterpret_cast<const T*>(a.z) + bh * (int64_t)P;
+    T* yg = reinterpret_cast<T*>(a.y) + bh * (int64_t)P;
     const float Ah = a.A[h];
     const float bias = has_bias ? a.dt_bias[h] : 0.0f;
-    float dh_head = 0.0f;
-    if (!per_row) {
-        const float raw = ldf(dtg + bh) + bias;
-        dh_head = softplus ? softplus_f(raw) : raw;
-    }
+    float* s_decay = s_rows;
+    float* s_dx = s_rows + P;
 
-    for (int64_t p0 = (int64_t)warp * kRows; p0 < P; p0 += (int64_t)kWarps * kRows) {
-        float dv[kRows], av[kRows], xv[kRows], acc[kRows];
+    for (int p = threadIdx.x; p < P; p += kThreads) {
+        const float raw = ldf(per_row ? dtg + bh * (int64_t)P + p : dtg + bh) + bias;
+        const float d = softplus ? softplus_f(raw) : raw;
+        s_decay[p] = expf(Ah * d);
+        s_dx[p] = d * ldf(xg + p);
+    }
+    __syncthreads();
+
+    for (int p0 = warp * kFwdRows; p0 < P; p0 += kWarps * kFwdRows) {
+        const int nr = min(kFwdRows, P - p0);
+        float acc[kFwdRows];
 #pragma unroll
-        for (int r = 0; r < kRows; ++r) {
-            const int64_t p = p0 + r;
-            const int64_t row = bh * P + p;
-            float d = dh_head;
-            if (per_row && p < P) {
-                const float raw = ldf(dtg + row) + bias;
-                d = softplus ? softplus_f(raw) : raw;
-            }
-            dv[r] = d;
-            av[r] = expf(Ah * d);
-            xv[r] = p < P ? ldf(xg + row) : 0.0f;
-            acc[r] = 0.0f;
-        }
-        for (int64_t n = (int64_t)lane * VEC; n < N; n += 32 * VEC) {
+        for (int r = 0; r < kFwdRows; ++r) acc[r] = 0.0f;
+        for (int n = lane * VEC; n < N; n += 32 * VEC) {
+            float sv[kFwdRows][VEC];
+#pragma unroll
+            for (int r = 0; r < kFwdRows; ++r)
+                if (r < nr) Vec<T, VEC>::ld(st + (p0 + r) * N + n, sv[r]);
             float bv[VEC], cv[VEC];
             Vec<T, VEC>::ld(Bg + n, bv);
             Vec<T, VEC>::ld(Cg + n, cv);
-            float sv[kRows][VEC];
 #pragma unroll
-            for (int r = 0; r < kRows; ++r)
-                if (p0 + r < P) Vec<T, VEC>::ld(st + (bh * P + p0 + r) * N + n, sv[r]);
-#pragma unroll
-            for (int r = 0; r < kRows; ++r) {
-                if (p0 + r < P) {
-                    const float dx = dv[r] * xv[r];
+            for (int r = 0; r < kFwdRows; ++r) {
+                if (r < nr) {
+                    const float dc = s_decay[p0 + r], dx = s_dx[p0 + r];
                     float out[VEC];
 #pragma unroll
                     for (int k = 0; k < VEC; ++k) {
-                        out[k] = fmaf(av[r], sv[r][k], dx * bv[k]);
+                        out[k] = fmaf(dc, sv[r][k], dx * bv[k]);
                         acc[r] = fmaf(out[k], cv[k], acc[r]);
                     }
-                    Vec<T, VEC>::st(ns + (bh * P + p0 + r) * N + n, out);
+                    Vec<T, VEC>::st(ns + (p0 + r) * N + n, out);
                 }
             }
         }
 #pragma unroll
-        for (int r = 0; r < kRows; ++r) {
-            const float tot = warp_sum(acc[r]);
-            const int64_t p = p0 + r;
-            if (lane == 0 && p < P) {
-                const int64_t row = bh * P + p;
-                float out = tot;
-                if (has_d) out = fmaf(xv[r], d_per_head ? a.D[h * P + p] : a.D[h], out);
-                if (has_z) {
-                    const float zv = ldf(zg + row);
-                    out *= zv * sigmoid_f(zv);
-                }
-                stf(yg + row, out);
+        for (int r = 0; r < kFwdRows; ++r) acc[r] = warp_sum(acc[r]);
+        // lane r finishes row p0 + r
+        float tot = acc[0];
+#pragma unroll
+        for (int r = 1; r < kFwdRows; ++r)
+            if (lane == r) tot = acc[r];
+        if (lane < nr) {
+            const int p = p0 + lane;
+            float out = tot;
+            if (has_d) out = fmaf(ldf(xg + p), d_per_head ? a.D[h * (int64_t)P + p] : a.D[h], out);
+            if (has_z) {
+                const float zv = ldf(zg + p);
+                out *= zv * sigmoid_f(zv);
             }
+            stf(yg + p, out);
         }
     }
 }
@@ -424,8 +428,14 @@ static bool aligned16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 
 template <typename T>
 static int launch_fwd(const Args& a, bool vec, cudaStream_t s) {
     const unsigned grid = (unsigned)(a.batch * a.nheads);
-    if (vec) fwd_kernel<T, 4><<<grid, kThreads, 0, s>>>(a);
-    else fwd_kernel<T, 1><<<grid, kThreads, 0, s>>>(a);
+    const size_t smem = 2 * (size_t)a.headdim * sizeof(float);
+    if (vec) {
+        if (smem > 48 * 1024) cudaFuncSetAttribute(fwd_kernel<T, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        fwd_kernel<T, 4><<<grid, kThreads, smem, s>>>(a);
+    } else {
+        if (smem > 48 * 1024) cudaFuncSetAttribute(fwd_kernel<T, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        fwd_kernel<T, 1><<<grid, kThreads, smem, s>>>(a);
+    }
     return check_launch("state_update fwd");
 }
 
