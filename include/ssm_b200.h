@@ -47,6 +47,8 @@ typedef enum ssm_dtype {
 #define SSM_HAS_INIT     0x40u  /* SSD: initial_states given                    */
 #define SSM_HAS_DY       0x80u  /* backward: gradient of y given                */
 #define SSM_HAS_DSTATE   0x100u /* backward: gradient of the state output given */
+#define SSM_CUDA_CORES   0x200u /* SSD: run the CUDA-core kernels even where the tensor-core
+                                   path applies (bf16/f16, headdim 64, dstate 128)          */
 
 /* Human-readable text for a status code, and the message of the last failure
  * on the calling thread (empty if none). */
@@ -238,6 +240,12 @@ int ssm_chunk_scan_sizes(const ssm_chunk_scan_params* p, size_t* saved_bytes,
                          size_t* workspace_bytes);
 int ssm_chunk_scan_fwd(const ssm_chunk_scan_params* p, void* stream);
 int ssm_chunk_scan_bwd(const ssm_chunk_scan_params* p, void* stream);
+
+/* Kernels that wait on an mbarrier give up after a bounded number of polls,
+ * record a non-zero code in a per-device flag and return.  This reads the flag
+ * of the current device (synchronising with it) and clears it; 0 means no
+ * kernel gave up.  Reference: none (the Metal kernels have no such waits). */
+int ssm_take_kernel_error(void);
 
 #ifdef __cplusplus
 }

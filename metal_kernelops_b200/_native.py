@@ -28,6 +28,7 @@ DT_PER_ROW = 0x20
 HAS_INIT = 0x40
 HAS_DY = 0x80
 HAS_DSTATE = 0x100
+CUDA_CORES = 0x200
 
 EXPORTS = (
     "ssm_status_string", "ssm_last_error",
@@ -35,6 +36,7 @@ EXPORTS = (
     "ssm_state_update_sizes", "ssm_state_update_fwd", "ssm_state_update_bwd",
     "ssm_state_update_bwd_noalloc",
     "ssm_chunk_scan_sizes", "ssm_chunk_scan_fwd", "ssm_chunk_scan_bwd",
+    "ssm_take_kernel_error",
 )
 
 _I64, _I32, _U32, _P, _SZ = ctypes.c_int64, ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t
@@ -120,6 +122,8 @@ def lib():
                                                             ctypes.c_void_p]
             for name in ("ssm_selective_scan_sizes", "ssm_state_update_sizes", "ssm_chunk_scan_sizes"):
                 getattr(handle, name).restype = ctypes.c_int
+            handle.ssm_take_kernel_error.restype = ctypes.c_int
+            handle.ssm_take_kernel_error.argtypes = []
             _lib = handle
     return _lib
 

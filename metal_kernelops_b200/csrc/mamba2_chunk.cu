@@ -24,10 +24,13 @@
 // state_bwd (chunk-state gradients), dt_bwd (cumsum / softplus chain), reduce.
 // Everything accumulates in fp32; every reduction has a fixed order, so the
 // backward is deterministic.  This is the CUDA-core path that serves every
-// dtype and shape; it is exact to fp32 rounding.
+// dtype and shape; it is exact to fp32 rounding.  bf16/f16 inputs with headdim
+// 64 and dstate 128 go to the tensor-core kernels of mamba2_chunk_tc.cu instead
+// (unless the caller sets SSM_CUDA_CORES).
 #include <string>
 
 #include "common.cuh"
+#include "ssd_tc.h"
 
 namespace ssm {
 namespace ssd {
@@ -669,6 +672,10 @@ using namespace ssm::ssd;
 extern "C" int ssm_chunk_scan_sizes(const ssm_chunk_scan_params* p, size_t* saved_bytes,
                                     size_t* workspace_bytes) {
     if (int s = validate(p, 0)) return s;
+    if (ssdtc::eligible(p)) {
+        ssdtc::sizes(p, saved_bytes, workspace_bytes);
+        return SSM_OK;
+    }
     const int64_t Q = pick_q(p->length, p->headdim, p->dstate);
     const int64_t nc = ceil_div(p->length, Q);
     const int64_t BH = p->batch * p->nheads;
@@ -691,6 +698,7 @@ extern "C" int ssm_chunk_scan_fwd(const ssm_chunk_scan_params* p, void* stream) 
             cudaMemsetAsync(p->final_state, 0, bytes, st);
         return check_launch("chunk_scan fwd: empty");
     }
+    if (ssdtc::eligible(p)) return ssdtc::fwd(p, st);
     Args a;
     make_args(p, a);
     const int64_t Q = a.Q, P = p->headdim, N = p->dstate;
@@ -725,6 +733,7 @@ extern "C" int ssm_chunk_scan_bwd(const ssm_chunk_scan_params* p, void* stream) 
         }
         return check_launch("chunk_scan bwd: empty");
     }
+    if (ssdtc::eligible(p)) return ssdtc::bwd(p, st);
     Args a;
     make_args(p, a);
     const int64_t Q = a.Q;

@@ -1,0 +1,1195 @@
+// Mamba-2 SSD chunk scan on the sm_100a tensor cores (tcgen05 + TMEM).
+//
+// Reference behaviour: src/metal_kernelops/cv/mamba2_chunk.py:617-723 (the
+// public op) and its chunk factorisation :15-31 / :447-533.  This path serves
+// bf16 and f16 inputs with headdim 64 and dstate 128 (the Mamba-2 layer shape);
+// every other case runs the CUDA-core kernels of mamba2_chunk.cu.  The internal
+// chunk is Q = 128 positions whatever chunk_size the caller asks for (the
+// result does not depend on it).
+//
+// Per (batch b, head h, chunk c), with d_s the (softplus'd) step, cd_s its
+// running sum inside the chunk, cs_s = A_h cd_s, T = cs_{Q-1}, G = C B^T:
+//
+//   Mh[l][s] = G[l][s] exp(cs_l - cs_s) d_s            (s <= l, else 0)
+//   y_l      = (Mh X)_l + exp(cs_l) (C H_c^T)_l + D x_l          [* silu(z_l)]
+//   H_{c+1}  = exp(T) H_c + sum_s exp(T - cs_s) d_s x_s B_s^T    (P x N)
+//
+// Kernels.  Forward: `states` (one CTA per (b, h), sequential over chunks)
+// accumulates H^T (dstate x headdim) in TMEM -- the chunk GEMM
+// H^T += B^T (w o X) runs on the tensor core, the exp(T) rescale between
+// chunks on the CUDA cores -- and writes every entering state H_c as a 16 KB
+// operand image (bf16/f16, the shared-memory tile layout of tc.cuh), so that
+// the consumers copy it linearly.  `outputs` (one CTA per (b, group, chunk))
+// computes G once, then for each head of the group the decay-masked Mh into
+// shared memory and the two output GEMMs Mh X and C H_c^T.
+//
+// Backward: `dstates` (one CTA per (b, h), reverse over chunks) carries dH^T in
+// TMEM: dH_c = exp(T) dH_{c+1} + sum_l exp(cs_l) dy_l C_l^T, written as operand
+// images; it also produces exp(T_c) <dH_{c+1}, H_c> and the per-position
+// derivative of the inter-chunk output with respect to cs.  The derivative with
+// respect to the chunk's total decay T_c is <dH_{c+1}, H_{c+1}> =
+// exp(T_c) <dH_{c+1}, H_c> + sum_s d_s v_s (v_s = exp(T - cs_s) <x_s, dH_{c+1} B_s>);
+// `grads` adds the second sum from the same v_s it subtracts at each position,
+// so the two cancel exactly instead of leaving the rounding of two differently
+// rounded state products (which dominated dA and d dt_bias in bf16).  `grads` (one CTA
+// per (b, group, chunk)) runs eight GEMMs per head -- dY X^T, Mh^T dY,
+// B dH^T, dG B, dYs H, dG^T C, (w o X) dH -- accumulating dB and dC for the
+// whole group in TMEM, and finishes dx, d dt and the parameter partials.  Every
+// reduction has a fixed order: the backward is deterministic.
+//
+// Operands are rounded to the input dtype before each GEMM (fp32 accumulate),
+// so the result carries the input dtype's rounding, as the reference's own
+// bf16/f16 runs do.
+#include <string>
+
+#include "common.cuh"
+#include "ssd_tc.h"
+#include "tc.cuh"
+
+namespace ssm {
+namespace ssdtc {
+
+constexpr int Q = 128;        // chunk
+constexpr int P = 64;         // headdim
+constexpr int N = 128;        // dstate
+constexpr int kThreads = 128;
+constexpr int WX = P / 8;     // 16-byte chunks per row of an X-like tile (Q x P)
+constexpr int WB = N / 8;     // per row of a B/C-like tile (Q x N)
+constexpr int WH = P / 8;     // per row of an H^T tile (N x P)
+constexpr uint32_t kTileX = Q * P * 2;
+constexpr uint32_t kTileB = Q * N * 2;
+constexpr uint32_t kTileH = N * P * 2;
+
+__device__ int g_kernel_error;
+
+struct Args {
+    int64_t batch, length, nheads, ngroups, nc, hpg;
+    uint32_t flags;
+    int dt_dtype;
+    const void* x; const void* dt; const float* A; const void* B; const void* C;
+    const float* D; const void* z; const float* dt_bias; const float* init;
+    void* y; float* final_state;
+    unsigned char* Ht;     // (b, h, c) H_c^T tiles, the state entering chunk c
+    void* ypre;            // (b, l, h, p) pre-gate output, saved when z is given
+    const void* dy; const float* dfinal;
+    void* dx; float* ddt; float* dB; float* dC; void* dz; float* dinit;
+    unsigned char* dHt;    // (b, h, c) dH_{c+1}^T tiles
+    float* dcs_inter;      // (b, h, nc * Q)
+    float* dT;             // (b, h, nc)
+    float* dA_part; float* db_part; float* dD_part;   // (b, h, nc) [x headdim]
+};
+
+// ----------------------------------------------------------- element types --
+template <typename T> struct Pk;
+template <> struct Pk<__nv_bfloat16> {
+    static constexpr uint32_t kFmt = 1;
+    static __device__ __forceinline__ void unpack(const uint4& q, float* f) {
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            f[2 * i] = __uint_as_float(w[i] << 16);
+            f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        }
+    }
+    static __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+        __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
+};
+template <> struct Pk<__half> {
+    static constexpr uint32_t kFmt = 0;
+    static __device__ __forceinline__ void unpack(const uint4& q, float* f) {
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+            f[2 * i] = v.x;
+            f[2 * i + 1] = v.y;
+        }
+    }
+    static __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+        __half2 v = __floats2half2_rn(lo, hi);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
+};
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float* f) {
+    return make_uint4(Pk<T>::pack2(f[0], f[1]), Pk<T>::pack2(f[2], f[3]), Pk<T>::pack2(f[4], f[5]),
+                      Pk<T>::pack2(f[6], f[7]));
+}
+
+__device__ __forceinline__ float ld_dt(const Args& a, int64_t i) {
+    switch (a.dt_dtype) {
+        case SSM_F32: return reinterpret_cast<const float*>(a.dt)[i];
+        case SSM_BF16: return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.dt)[i]);
+        default: return __half2float(reinterpret_cast<const __half*>(a.dt)[i]);
+    }
+}
+
+__device__ __forceinline__ void report(int code) { atomicCAS(&g_kernel_error, 0, code); }
+
+// ------------------------------------------------------------ block helpers --
+__device__ __forceinline__ float block_incl_scan(float v, float* sh) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+    }
+    if (lane == 31) sh[w] = v;
+    __syncthreads();
+    float off = 0.0f;
+    for (int i = 0; i < w; ++i) off += sh[i];
+    __syncthreads();
+    return v + off;
+}
+__device__ __forceinline__ float block_suffix_scan(float v, float* sh) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float u = __shfl_down_sync(0xffffffffu, v, o);
+        if (lane + o < 32) v += u;
+    }
+    if (lane == 0) sh[w] = v;
+    __syncthreads();
+    float off = 0.0f;
+    for (int i = kThreads / 32 - 1; i > w; --i) off += sh[i];
+    __syncthreads();
+    return v + off;
+}
+// Sum over the CTA; every thread gets the total (fixed order).
+__device__ __forceinline__ float block_sum(float v, float* sh) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float s = 0.0f;
+    for (int i = 0; i < kThreads / 32; ++i) s += sh[i];
+    __syncthreads();
+    return s;
+}
+
+// Rows [0, Q) of a global row-major matrix (16-byte chunks) into a tile, rows
+// at or beyond `valid` zero-filled.  Lanes 0-7 take eight rows of one chunk so
+// that each quarter-warp writes 128 contiguous bytes of shared memory.
+template <int W, typename T>
+__device__ __forceinline__ void load_rows(unsigned char* tile, const T* base, int64_t row_stride, int valid) {
+    const uint32_t st = tc::smem_u32(tile);
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    constexpr int CPW = W / 4;
+    for (int wi = wid; wi < (Q / 8) * CPW; wi += kThreads / 32) {
+        const int r = (wi / CPW) * 8 + (lane & 7);
+        const int ch = (wi % CPW) * 4 + (lane >> 3);
+        const bool v = r < valid;
+        const T* src = base + (int64_t)(v ? r : 0) * row_stride + ch * 8;
+        tc::cp_async16_zfill(st + tc::tile_off(r, ch, W), src, v ? 16u : 0u);
+    }
+}
+// A 16 KB operand image copied linearly.
+__device__ __forceinline__ void load_image(unsigned char* tile, const unsigned char* src) {
+    const uint32_t st = tc::smem_u32(tile);
+    for (int i = threadIdx.x; i < (int)(kTileH / 16); i += kThreads) tc::cp_async16(st + i * 16, src + i * 16);
+}
+
+// Per-chunk step quantities of one head, thread s owning position s.
+struct Steps {
+    float raw;   // dt + bias (before the softplus)
+    float d;     // step (0 beyond the sequence)
+    float cd;    // running sum of d inside the chunk
+    float cs;    // A * cd
+};
+__device__ __forceinline__ Steps chunk_steps(const Args& a, int64_t b, int64_t h, int64_t c, float Ah,
+                                             float bias, float* scan_sh) {
+    Steps s;
+    const int64_t t = c * Q + threadIdx.x;
+    s.raw = 0.0f;
+    s.d = 0.0f;
+    if (t < a.length) {
+        s.raw = ld_dt(a, (b * a.length + t) * a.nheads + h) + bias;
+        s.d = (a.flags & SSM_SOFTPLUS) ? softplus_f(s.raw) : s.raw;
+    }
+    s.cd = block_incl_scan(s.d, scan_sh);
+    s.cs = Ah * s.cd;
+    return s;
+}
+
+// ====================================================================== F1 ==
+// One CTA per (b, h).  TMEM: H^T, lanes = state index n, columns = p.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) states_kernel(const Args a) {
+    extern __shared__ __align__(128) unsigned char sm[];
+    unsigned char* sB[2] = {sm, sm + kTileB};
+    unsigned char* sX = sm + 2 * kTileB;
+    unsigned char* sXW = sX + kTileX;
+    __shared__ float s_scan[4];
+    __shared__ float s_T;
+    __shared__ __align__(8) uint64_t mbar;
+    __shared__ uint32_t tbase;
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int64_t h = blockIdx.x, b = blockIdx.y, g = h / a.hpg;
+    const int64_t L = a.length, H = a.nheads, G = a.ngroups;
+    const float Ah = a.A[h];
+    const float bias = (a.flags & SSM_HAS_BIAS) ? a.dt_bias[h] : 0.0f;
+    const T* xg = reinterpret_cast<const T*>(a.x);
+    const T* Bgl = reinterpret_cast<const T*>(a.B);
+
+    if (warp == 0) tc::tmem_alloc(tc::smem_u32(&tbase), 64);
+    if (tid == 0) {
+        tc::mbar_init(tc::smem_u32(&mbar), 1);
+        tc::fence_mbar_init();
+    }
+    load_rows<WB>(sB[0], Bgl + (b * L * G + g) * N, G * N, (int)min64(Q, L));
+    load_rows<WX>(sX, xg + (b * L * H + h) * P, H * P, (int)min64(Q, L));
+    tc::cp_async_commit();
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tm = tbase;
+    const uint32_t row_addr = tm + ((uint32_t)(warp * 32) << 16);
+    {
+        float v[16];
+        for (int j = 0; j < P / 16; ++j) {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                const int p = j * 16 + k;
+                v[k] = (a.flags & SSM_HAS_INIT) ? a.init[((b * H + h) * P + p) * N + tid] : 0.0f;
+            }
+            tc::tmem_st16(row_addr + j * 16, v);
+        }
+        tc::tmem_wait_st();
+    }
+    const uint32_t id = tc::idesc_f16(Pk<T>::kFmt, 128, P, true, true);
+    uint32_t phase = 0;
+    bool ok = true;
+    unsigned char* Hout = a.Ht + (size_t)(b * H + h) * a.nc * kTileH;
+    for (int64_t c = 0; c < a.nc && ok; ++c) {
+        const int buf = (int)(c & 1);
+        const Steps st = chunk_steps(a, b, h, c, Ah, bias, s_scan);
+        if (tid == Q - 1) s_T = st.cs;
+        if (c > 0) {   // the previous chunk's GEMM read sXW and sB[buf ^ 1]
+            if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(11); ok = false; }
+            phase ^= 1;
+            tc::fence_after();
+        }
+        tc::cp_async_wait<0>();
+        ok = __syncthreads_and(ok);
+        if (!ok) break;
+        const float Tc = s_T;
+        const float w = exp2_mufu((Tc - st.cs) * kLog2e) * st.d;
+        // w o X, row s = tid
+#pragma unroll
+        for (int j = 0; j < WX; ++j) {
+            const uint4 q = *reinterpret_cast<const uint4*>(sX + tc::tile_off(tid, j, WX));
+            float f[8];
+            Pk<T>::unpack(q, f);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) f[k] *= w;
+            *reinterpret_cast<uint4*>(sXW + tc::tile_off(tid, j, WX)) = pack8<T>(f);
+        }
+        // emit H_c (row n = tid of H^T), then H^T <- exp(T) H^T
+        {
+            unsigned char* out = Hout + (size_t)c * kTileH;
+            const float eT = exp2_mufu(Tc * kLog2e);
+            for (int j = 0; j < P / 16; ++j) {
+                float v[16];
+                tc::tmem_ld16(row_addr + j * 16, v);
+                tc::tmem_wait_ld();
+                *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j, WH)) = pack8<T>(v);
+                *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j + 1, WH)) = pack8<T>(v + 8);
+#pragma unroll
+                for (int k = 0; k < 16; ++k) v[k] *= eT;
+                tc::tmem_st16(row_addr + j * 16, v);
+            }
+            tc::tmem_wait_st();
+        }
+        tc::fence_async_smem();
+        tc::fence_before();
+        __syncthreads();
+        if (c + 1 < a.nc) {
+            const int64_t t1 = (c + 1) * Q;
+            const int valid = (int)min64(Q, L - t1);
+            load_rows<WB>(sB[buf ^ 1], Bgl + ((b * L + t1) * G + g) * N, G * N, valid);
+            load_rows<WX>(sX, xg + ((b * L + t1) * H + h) * P, H * P, valid);
+        }
+        tc::cp_async_commit();
+        if (tid == 0) {
+            tc::fence_after();
+            const uint32_t aB = tc::smem_u32(sB[buf]), aX = tc::smem_u32(sXW);
+#pragma unroll
+            for (int ks = 0; ks < Q / 16; ++ks)
+                tc::mma_f16(tm, tc::desc_mn(aB, WB, 16 * ks), tc::desc_mn(aX, WX, 16 * ks), id, 1u);
+            tc::commit(tc::smem_u32(&mbar));
+        }
+    }
+    if (ok) {
+        if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(12); ok = false; }
+        tc::fence_after();
+    }
+    tc::cp_async_wait<0>();
+    ok = __syncthreads_and(ok);
+    if (ok) {
+        for (int j = 0; j < P / 16; ++j) {
+            float v[16];
+            tc::tmem_ld16(row_addr + j * 16, v);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int k = 0; k < 16; ++k) a.final_state[((b * H + h) * P + j * 16 + k) * N + tid] = v[k];
+        }
+    }
+    tc::fence_before();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tm, 64);
+}
+
+// Decay factors for the mask of one head of one chunk, shared by the CTA:
+// cs in log2 units, d, and cf_s = exp(cs_{e(s)} - cs_s) with e(s) the last
+// position of s's 16-block.  For l past that block exp(cs_l - cs_s) =
+// exp(cs_l - cs_{e(s)}) cf_s, and both factors are <= 1 when cs is
+// non-increasing; the diagonal 16 x 16 blocks use direct exponentials.
+struct MaskSh {
+    float cs2[Q];
+    float d[Q];
+    float cf[Q];
+};
+__device__ __forceinline__ void mask_factors(MaskSh& m, const Steps& st) {
+    const int s = threadIdx.x;
+    m.cs2[s] = st.cs * kLog2e;
+    m.d[s] = st.d;
+    __syncthreads();
+    m.cf[s] = exp2_mufu(m.cs2[s | 15] - m.cs2[s]);
+    __syncthreads();
+}
+
+// ====================================================================== F2 ==
+// One CTA per (b, group, chunk).  TMEM: G [0,128), Y intra [128,192),
+// C H^T [192,256).
+template <typename T>
+__global__ void __launch_bounds__(kThreads) outputs_kernel(const Args a) {
+    extern __shared__ __align__(128) unsigned char sm[];
+    unsigned char* sC = sm;
+    unsigned char* sM = sm + kTileB;          // B, then Mh
+    unsigned char* sX = sm + 2 * kTileB;
+    unsigned char* sH = sX + kTileX;
+    __shared__ MaskSh msh;
+    __shared__ float s_scan[4];
+    __shared__ __align__(8) uint64_t mbar;
+    __shared__ uint32_t tbase;
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int64_t c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int64_t L = a.length, H = a.nheads, G = a.ngroups;
+    const int64_t t0 = c * Q;
+    const int valid = (int)min64(Q, L - t0);
+    const T* xg = reinterpret_cast<const T*>(a.x);
+    const T* zg = reinterpret_cast<const T*>(a.z);
+    T* yg = reinterpret_cast<T*>(a.y);
+    T* ypg = reinterpret_cast<T*>(a.ypre);
+    const bool has_z = a.flags & SSM_HAS_Z, has_d = a.flags & SSM_HAS_D;
+    const bool d_per_head = a.flags & SSM_D_PER_HEAD;
+
+    if (warp == 0) tc::tmem_alloc(tc::smem_u32(&tbase), 256);
+    if (tid == 0) {
+        tc::mbar_init(tc::smem_u32(&mbar), 1);
+        tc::fence_mbar_init();
+    }
+    load_rows<WB>(sC, reinterpret_cast<const T*>(a.C) + ((b * L + t0) * G + g) * N, G * N, valid);
+    load_rows<WB>(sM, reinterpret_cast<const T*>(a.B) + ((b * L + t0) * G + g) * N, G * N, valid);
+    tc::cp_async_commit();
+    tc::cp_async_wait<0>();
+    tc::fence_async_smem();
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tm = tbase;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t aC = tc::smem_u32(sC), aM = tc::smem_u32(sM), aX = tc::smem_u32(sX), aH = tc::smem_u32(sH);
+    if (tid == 0) {
+        const uint32_t idg = tc::idesc_f16(Pk<T>::kFmt, 128, 128, false, false);
+#pragma unroll
+        for (int ks = 0; ks < N / 16; ++ks)
+            tc::mma_f16(tm, tc::desc_k(aC, WB, 2 * ks), tc::desc_k(aM, WB, 2 * ks), idg, ks > 0);
+        tc::commit(tc::smem_u32(&mbar));
+    }
+    uint32_t phase = 0;
+    bool ok = tc::mbar_wait(tc::smem_u32(&mbar), phase);
+    if (!ok) report(21);
+    phase ^= 1;
+    tc::fence_after();
+    ok = __syncthreads_and(ok);
+
+    const uint32_t idy = tc::idesc_f16(Pk<T>::kFmt, 128, P, false, true);
+    for (int64_t hh = 0; hh < a.hpg && ok; ++hh) {
+        const int64_t h = g * a.hpg + hh;
+        load_rows<WX>(sX, xg + ((b * L + t0) * H + h) * P, H * P, valid);
+        load_image(sH, a.Ht + ((size_t)(b * H + h) * a.nc + c) * kTileH);
+        tc::cp_async_commit();
+        const float Ah = a.A[h];
+        const float bias = (a.flags & SSM_HAS_BIAS) ? a.dt_bias[h] : 0.0f;
+        const Steps st = chunk_steps(a, b, h, c, Ah, bias, s_scan);
+        mask_factors(msh, st);
+        // Mh row l = tid into sM (B is no longer needed once G is in TMEM)
+        {
+            const int l = tid;
+            const float csl = msh.cs2[l];
+            for (int j = 0; j < Q / 16; ++j) {
+                uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+                if (16 * j <= 32 * warp + 31) {          // warp-uniform: tcgen05.ld is .sync.aligned
+                    float v[16];
+                    tc::tmem_ld16(tm + lane_off + 16 * j, v);
+                    tc::tmem_wait_ld();
+                    if (16 * j > l) {
+                        // whole block above the diagonal for this row: zeros
+                    } else if (16 * j + 15 < l) {
+                        const float rf = exp2_mufu(csl - msh.cs2[16 * j + 15]);
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) v[k] *= rf * msh.cf[16 * j + k] * msh.d[16 * j + k];
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) {
+                            const int s = 16 * j + k;
+                            v[k] = s <= l ? v[k] * exp2_mufu(csl - msh.cs2[s]) * msh.d[s] : 0.0f;
+                        }
+                    }
+                    if (16 * j <= l) {
+                        lo = pack8<T>(v);
+                        hi = pack8<T>(v + 8);
+                    }
+                }
+                *reinterpret_cast<uint4*>(sM + tc::tile_off(l, 2 * j, WB)) = lo;
+                *reinterpret_cast<uint4*>(sM + tc::tile_off(l, 2 * j + 1, WB)) = hi;
+            }
+        }
+        tc::cp_async_wait<0>();
+        tc::fence_async_smem();
+        tc::fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tc::fence_after();
+#pragma unroll
+            for (int ks = 0; ks < Q / 16; ++ks)
+                tc::mma_f16(tm + 128, tc::desc_k(aM, WB, 2 * ks), tc::desc_mn(aX, WX, 16 * ks), idy, ks > 0);
+#pragma unroll
+            for (int ks = 0; ks < N / 16; ++ks)
+                tc::mma_f16(tm + 192, tc::desc_k(aC, WB, 2 * ks), tc::desc_mn(aH, WH, 16 * ks), idy, ks > 0);
+            tc::commit(tc::smem_u32(&mbar));
+        }
+        if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(22); ok = false; }
+        phase ^= 1;
+        tc::fence_after();
+        ok = __syncthreads_and(ok);
+        if (ok) {
+            const int l = tid;
+            const bool live = l < valid;
+            const int64_t row = ((b * L + t0 + l) * H + h) * P;
+            const float el = exp2_mufu(msh.cs2[l]);
+            const float Dh = (has_d && !d_per_head) ? a.D[h] : 0.0f;
+            for (int j = 0; j < P / 16; ++j) {
+                float yi[16], ye[16];
+                tc::tmem_ld16(tm + lane_off + 128 + 16 * j, yi);
+                tc::tmem_ld16(tm + lane_off + 192 + 16 * j, ye);
+                tc::tmem_wait_ld();
+                if (!live) continue;
+                float xv[16];
+                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sX + tc::tile_off(l, 2 * j, WX)), xv);
+                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sX + tc::tile_off(l, 2 * j + 1, WX)), xv + 8);
+                float yv[16];
+#pragma unroll
+                for (int k = 0; k < 16; ++k) {
+                    const float Dk = has_d ? (d_per_head ? a.D[h * P + 16 * j + k] : Dh) : 0.0f;
+                    yv[k] = fmaf(el, ye[k], yi[k]) + Dk * xv[k];
+                }
+                if (has_z) {
+                    if (ypg) {
+                        *reinterpret_cast<uint4*>(ypg + row + 16 * j) = pack8<T>(yv);
+                        *reinterpret_cast<uint4*>(ypg + row + 16 * j + 8) = pack8<T>(yv + 8);
+                    }
+                    float zv[16];
+                    Pk<T>::unpack(*reinterpret_cast<const uint4*>(zg + row + 16 * j), zv);
+                    Pk<T>::unpack(*reinterpret_cast<const uint4*>(zg + row + 16 * j + 8), zv + 8);
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) yv[k] *= zv[k] * sigmoid_f(zv[k]);
+                }
+                *reinterpret_cast<uint4*>(yg + row + 16 * j) = pack8<T>(yv);
+                *reinterpret_cast<uint4*>(yg + row + 16 * j + 8) = pack8<T>(yv + 8);
+            }
+        }
+        tc::fence_before();
+        __syncthreads();
+    }
+    tc::cp_async_wait<0>();
+    tc::fence_before();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tm, 256);
+}
+
+// ====================================================================== B1 ==
+// One CTA per (b, h), chunks in reverse.  TMEM: dH^T [0,64), C H_c^T [64,128).
+template <typename T>
+__global__ void __launch_bounds__(kThreads) dstates_kernel(const Args a) {
+    extern __shared__ __align__(128) unsigned char sm[];
+    unsigned char* sC = sm;
+    unsigned char* sH = sm + kTileB;
+    unsigned char* sY = sm + kTileB + kTileH;   // dout, then exp(cs_l) dy_l
+    __shared__ float s_scan[4];
+    __shared__ float s_T;
+    __shared__ __align__(8) uint64_t mbar;
+    __shared__ uint32_t tbase;
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int64_t h = blockIdx.x, b = blockIdx.y, g = h / a.hpg;
+    const int64_t L = a.length, H = a.nheads, G = a.ngroups;
+    const float Ah = a.A[h];
+    const float bias = (a.flags & SSM_HAS_BIAS) ? a.dt_bias[h] : 0.0f;
+    const bool has_z = a.flags & SSM_HAS_Z;
+    const T* zg = reinterpret_cast<const T*>(a.z);
+    const T* dyg = reinterpret_cast<const T*>(a.dy);
+    const T* ypg = reinterpret_cast<const T*>(a.ypre);
+    T* dzg = reinterpret_cast<T*>(a.dz);
+    const unsigned char* Hin = a.Ht + (size_t)(b * H + h) * a.nc * kTileH;
+    unsigned char* dHout = a.dHt + (size_t)(b * H + h) * a.nc * kTileH;
+
+    if (warp == 0) tc::tmem_alloc(tc::smem_u32(&tbase), 128);
+    if (tid == 0) {
+        tc::mbar_init(tc::smem_u32(&mbar), 1);
+        tc::fence_mbar_init();
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tm = tbase;
+    const uint32_t row_addr = tm + ((uint32_t)(warp * 32) << 16);
+    {
+        float v[16];
+        for (int j = 0; j < P / 16; ++j) {
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+                v[k] = (a.flags & SSM_HAS_DSTATE) ? a.dfinal[((b * H + h) * P + j * 16 + k) * N + tid] : 0.0f;
+            tc::tmem_st16(row_addr + j * 16, v);
+        }
+        tc::tmem_wait_st();
+    }
+    const uint32_t idy = tc::idesc_f16(Pk<T>::kFmt, 128, P, false, true);
+    const uint32_t idh = tc::idesc_f16(Pk<T>::kFmt, 128, P, true, true);
+    const uint32_t aC = tc::smem_u32(sC), aY = tc::smem_u32(sY);
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int64_t c = a.nc - 1; c >= 0 && ok; --c) {
+        const int64_t t0 = c * Q;
+        const int valid = (int)min64(Q, L - t0);
+        load_rows<WB>(sC, reinterpret_cast<const T*>(a.C) + ((b * L + t0) * G + g) * N, G * N, valid);
+        load_image(sH, Hin + (size_t)c * kTileH);
+        load_rows<WX>(sY, dyg + ((b * L + t0) * H + h) * P, H * P, valid);
+        tc::cp_async_commit();
+        const Steps st = chunk_steps(a, b, h, c, Ah, bias, s_scan);
+        if (tid == Q - 1) s_T = st.cs;
+        tc::cp_async_wait<0>();
+        __syncthreads();
+        const float Tc = s_T;
+        // dy row l = tid: gate, then exp(cs_l) dy_l in place
+        {
+            const int l = tid;
+            const float el = exp2_mufu(st.cs * kLog2e);
+            const int64_t row = ((b * L + t0 + l) * H + h) * P;
+            for (int j = 0; j < WX; ++j) {
+                float f[8];
+                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(l, j, WX)), f);
+                if (has_z && l < valid) {
+                    float zv[8], yp[8], dz[8];
+                    Pk<T>::unpack(*reinterpret_cast<const uint4*>(zg + row + 8 * j), zv);
+                    if (dzg) Pk<T>::unpack(*reinterpret_cast<const uint4*>(ypg + row + 8 * j), yp);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const float sg = sigmoid_f(zv[k]);
+                        if (dzg) dz[k] = f[k] * yp[k] * sg * fmaf(zv[k], 1.0f - sg, 1.0f);
+                        f[k] *= zv[k] * sg;
+                    }
+                    if (dzg) *reinterpret_cast<uint4*>(dzg + row + 8 * j) = pack8<T>(dz);
+                }
+#pragma unroll
+                for (int k = 0; k < 8; ++k) f[k] *= el;
+                *reinterpret_cast<uint4*>(sY + tc::tile_off(l, j, WX)) = pack8<T>(f);
+            }
+        }
+        // dH_{c+1}: emit, <dH_{c+1}, H_c>, then dH^T <- exp(T) dH^T
+        float dt_part = 0.0f;
+        {
+            unsigned char* out = dHout + (size_t)c * kTileH;
+            const float eT = exp2_mufu(Tc * kLog2e);
+            for (int j = 0; j < P / 16; ++j) {
+                float v[16], hv[16];
+                tc::tmem_ld16(row_addr + j * 16, v);
+                tc::tmem_wait_ld();
+                *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j, WH)) = pack8<T>(v);
+                *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j + 1, WH)) = pack8<T>(v + 8);
+                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sH + tc::tile_off(tid, 2 * j, WH)), hv);
+                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sH + tc::tile_off(tid, 2 * j + 1, WH)), hv + 8);
+#pragma unroll
+                for (int k = 0; k < 16; ++k) {
+                    dt_part = fmaf(v[k], hv[k], dt_part);
+                    v[k] *= eT;
+                }
+                tc::tmem_st16(row_addr + j * 16, v);
+            }
+            tc::tmem_wait_st();
+        }
+        tc::fence_async_smem();
+        tc::fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tc::fence_after();
+            const uint32_t aH = tc::smem_u32(sH);
+#pragma unroll
+            for (int ks = 0; ks < N / 16; ++ks)
+                tc::mma_f16(tm + 64, tc::desc_k(aC, WB, 2 * ks), tc::desc_mn(aH, WH, 16 * ks), idy, ks > 0);
+#pragma unroll
+            for (int ks = 0; ks < Q / 16; ++ks)
+                tc::mma_f16(tm, tc::desc_mn(aC, WB, 16 * ks), tc::desc_mn(aY, WX, 16 * ks), idh, 1u);
+            tc::commit(tc::smem_u32(&mbar));
+        }
+        const float dTc = block_sum(dt_part, s_scan);
+        if (tid == 0) a.dT[(b * H + h) * a.nc + c] = exp2_mufu(Tc * kLog2e) * dTc;
+        if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(31); ok = false; }
+        phase ^= 1;
+        tc::fence_after();
+        ok = __syncthreads_and(ok);
+        if (ok) {
+            // d(loss)/d(cs_l) through the inter-chunk output: <exp(cs_l) dy_l, (C H_c^T)_l>
+            const int l = tid;
+            float acc = 0.0f;
+            for (int j = 0; j < P / 16; ++j) {
+                float ye[16], yv[16];
+                tc::tmem_ld16(row_addr + 64 + 16 * j, ye);
+                tc::tmem_wait_ld();
+                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(l, 2 * j, WX)), yv);
+                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(l, 2 * j + 1, WX)), yv + 8);
+#pragma unroll
+                for (int k = 0; k < 16; ++k) acc = fmaf(yv[k], ye[k], acc);
+            }
+            a.dcs_inter[(b * H + h) * a.nc * Q + t0 + l] = acc;
+        }
+        tc::fence_before();
+        ok = __syncthreads_and(ok);
+    }
+    tc::cp_async_wait<0>();
+    if (ok && (a.flags & SSM_HAS_INIT) && a.dinit) {
+        for (int j = 0; j < P / 16; ++j) {
+            float v[16];
+            tc::tmem_ld16(row_addr + j * 16, v);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int k = 0; k < 16; ++k) a.dinit[((b * H + h) * P + j * 16 + k) * N + tid] = v[k];
+        }
+    }
+    tc::fence_before();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tm, 128);
+}
+
+// Sum of 16 values over the 32 lanes of a warp, scattered: afterwards lane
+// 2m and 2m+1 both hold the total of value index k(lane) =
+// 8 b4 + 4 b3 + 2 b2 + b1 (b_i the bits of the lane).  Select-free halving.
+__device__ __forceinline__ float warp_colsum16(float* v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int half = 8, off = 16; half >= 1; half >>= 1, off >>= 1) {
+        const bool up = lane & off;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float keep = up ? v[half + i] : v[i];
+            const float send = up ? v[i] : v[half + i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+    }
+    return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
+// ====================================================================== B2 ==
+// One CTA per (b, group, chunk).  TMEM: G [0,128), dB [128,256), dC [256,384),
+// scratch [384,512): dY X^T, then Mh^T dY [384,448) and B dH^T [448,512).
+struct GradSh {
+    MaskSh m;
+    float col[kThreads / 32][Q];
+    float scan[4];
+    float T;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1) grads_kernel(const Args a) {
+    extern __shared__ __align__(128) unsigned char sm[];
+    unsigned char* sB = sm;
+    unsigned char* sC = sB + kTileB;
+    unsigned char* sM = sC + kTileB;            // Mh
+    unsigned char* sG = sM + kTileB;            // dG (masked)
+    unsigned char* sX = sG + kTileB;            // x, then exp(cs) dy
+    unsigned char* sY = sX + kTileX;            // dy (gated)
+    unsigned char* sXW = sY + kTileX;           // w o x
+    unsigned char* sH = sXW + kTileX;           // H_c^T
+    unsigned char* sD = sH + kTileH;            // dH_{c+1}^T
+    __shared__ GradSh sh;
+    __shared__ __align__(8) uint64_t mbar;
+    __shared__ uint32_t tbase;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int64_t L = a.length, H = a.nheads, G = a.ngroups;
+    const int64_t t0 = c * Q;
+    const int valid = (int)min64(Q, L - t0);
+    const T* xg = reinterpret_cast<const T*>(a.x);
+    const T* zg = reinterpret_cast<const T*>(a.z);
+    const T* dyg = reinterpret_cast<const T*>(a.dy);
+    T* dxg = reinterpret_cast<T*>(a.dx);
+    const bool has_z = a.flags & SSM_HAS_Z, has_d = a.flags & SSM_HAS_D;
+    const bool d_per_head = a.flags & SSM_D_PER_HEAD;
+
+    if (warp == 0) tc::tmem_alloc(tc::smem_u32(&tbase), 512);
+    if (tid == 0) {
+        tc::mbar_init(tc::smem_u32(&mbar), 1);
+        tc::fence_mbar_init();
+    }
+    load_rows<WB>(sC, reinterpret_cast<const T*>(a.C) + ((b * L + t0) * G + g) * N, G * N, valid);
+    load_rows<WB>(sB, reinterpret_cast<const T*>(a.B) + ((b * L + t0) * G + g) * N, G * N, valid);
+    tc::cp_async_commit();
+    tc::cp_async_wait<0>();
+    tc::fence_async_smem();
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tm = tbase;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t tG = tm, tdB = tm + 128, tdC = tm + 256, tS = tm + 384;
+    const uint32_t aB = tc::smem_u32(sB), aC = tc::smem_u32(sC), aM = tc::smem_u32(sM), aG = tc::smem_u32(sG);
+    const uint32_t aX = tc::smem_u32(sX), aY = tc::smem_u32(sY), aXW = tc::smem_u32(sXW);
+    const uint32_t aH = tc::smem_u32(sH), aD = tc::smem_u32(sD);
+    constexpr uint32_t fmt = Pk<T>::kFmt;
+    if (tid == 0) {
+        const uint32_t idg = tc::idesc_f16(fmt, 128, 128, false, false);
+#pragma unroll
+        for (int ks = 0; ks < N / 16; ++ks)
+            tc::mma_f16(tG, tc::desc_k(aC, WB, 2 * ks), tc::desc_k(aB, WB, 2 * ks), idg, ks > 0);
+        tc::commit(tc::smem_u32(&mbar));
+    }
+    uint32_t phase = 0;
+    bool ok = tc::mbar_wait(tc::smem_u32(&mbar), phase);
+    if (!ok) report(41);
+    phase ^= 1;
+    tc::fence_after();
+    ok = __syncthreads_and(ok);
+
+    for (int64_t hh = 0; hh < a.hpg && ok; ++hh) {
+        const int64_t h = g * a.hpg + hh;
+        const int64_t bhc = (b * H + h) * a.nc + c;
+        load_rows<WX>(sX, xg + ((b * L + t0) * H + h) * P, H * P, valid);
+        load_rows<WX>(sY, dyg + ((b * L + t0) * H + h) * P, H * P, valid);
+        load_image(sH, a.Ht + ((size_t)(b * H + h) * a.nc + c) * kTileH);
+        load_image(sD, a.dHt + (size_t)bhc * kTileH);
+        tc::cp_async_commit();
+        const float Ah = a.A[h];
+        const float bias = (a.flags & SSM_HAS_BIAS) ? a.dt_bias[h] : 0.0f;
+        const Steps st = chunk_steps(a, b, h, c, Ah, bias, sh.scan);
+        if (tid == Q - 1) sh.T = st.cs;
+        mask_factors(sh.m, st);
+        const float Tc = sh.T;
+        const int r = tid;   // the row this thread owns (l or s)
+        const int64_t grow = ((b * L + t0 + r) * H + h) * P;
+        tc::cp_async_wait<0>();
+        __syncthreads();
+        // gate dy in place
+        if (has_z && r < valid) {
+            for (int j = 0; j < WX; ++j) {
+                float f[8], zv[8];
+                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(r, j, WX)), f);
+                Pk<T>::unpack(*reinterpret_cast<const uint4*>(zg + grow + 8 * j), zv);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) f[k] *= zv[k] * sigmoid_f(zv[k]);
+                *reinterpret_cast<uint4*>(sY + tc::tile_off(r, j, WX)) = pack8<T>(f);
+            }
+        }
+        tc::fence_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            tc::fence_after();
+            const uint32_t idm = tc::idesc_f16(fmt, 128, 128, false, false);
+#pragma unroll
+            for (int ks = 0; ks < P / 16; ++ks)
+                tc::mma_f16(tS, tc::desc_k(aY, WX, 2 * ks), tc::desc_k(aX, WX, 2 * ks), idm, ks > 0);
+            tc::commit(tc::smem_u32(&mbar));
+        }
+        // while dY X^T runs: w o x, and the D gradient partial <dy_r, x_r>
+        float dD_head = 0.0f;
+        {
+            const float w = exp2_mufu((Tc - st.cs) * kLog2e) * st.d;
+            for (int j = 0; j < WX; ++j) {
+                float xv[8], yv[8];
+                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sX + tc::tile_off(r, j, WX)), xv);
+                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(r, j, WX)), yv);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    dD_head = fmaf(xv[k], yv[k], dD_head);
+                    xv[k] *= w;
+                }
+                *reinterpret_cast<uint4*>(sXW + tc::tile_off(r, j, WX)) = pack8<T>(xv);
+            }
+        }
+        if (has_d && d_per_head) {
+            // per (head, p): thread p < P sums over the rows (x and dy still in place)
+            if (tid < P) {
+                const int p = tid;
+                float s = 0.0f;
+                for (int rr = 0; rr < Q; ++rr) {
+                    const uint32_t off = tc::tile_off(rr, p >> 3, WX) + (p & 7) * 2;
+                    s = fmaf(ldf(reinterpret_cast<const T*>(sX + off)), ldf(reinterpret_cast<const T*>(sY + off)), s);
+                }
+                a.dD_part[bhc * P + p] = s;
+            }
+        }
+        if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(42); ok = false; }
+        phase ^= 1;
+        tc::fence_after();
+        ok = __syncthreads_and(ok);   // also: every thread is done reading sX before it is overwritten
+        if (!ok) break;
+        // mask pass, row l = r
+        float rowsum = 0.0f;
+        {
+            const int l = r;
+            const float csl = sh.m.cs2[l];
+            for (int j = 0; j < Q / 16; ++j) {
+                uint4 m0 = make_uint4(0, 0, 0, 0), m1 = m0, g0 = m0, g1 = m0;
+                float E[16];
+                if (16 * j <= 32 * warp + 31) {           // some row of this warp reaches block j
+                    float gv[16], dm[16];
+                    tc::tmem_ld16(tG + lane_off + 16 * j, gv);
+                    tc::tmem_ld16(tS + lane_off + 16 * j, dm);
+                    tc::tmem_wait_ld();
+                    float e[16];
+                    if (16 * j + 15 < l) {
+                        const float rf = exp2_mufu(csl - sh.m.cs2[16 * j + 15]);
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) e[k] = rf * sh.m.cf[16 * j + k];
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) {
+                            const int s = 16 * j + k;
+                            e[k] = s <= l ? exp2_mufu(csl - sh.m.cs2[s]) : 0.0f;
+                        }
+                    }
+                    float mh[16], dg[16];
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) {
+                        const float ed = e[k] * sh.m.d[16 * j + k];
+                        const float gd = gv[k] * dm[k];
+                        mh[k] = gv[k] * ed;
+                        dg[k] = dm[k] * ed;
+                        E[k] = gd * e[k];
+                        rowsum = fmaf(gd, ed, rowsum);
+                    }
+                    m0 = pack8<T>(mh); m1 = pack8<T>(mh + 8);
+                    g0 = pack8<T>(dg); g1 = pack8<T>(dg + 8);
+                    const float cs_sum = warp_colsum16(E);
+                    if (!(lane & 1)) {
+                        const int k = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 +
+                                      ((lane >> 1) & 1);
+                        sh.col[warp][16 * j + k] = cs_sum;
+                    }
+                } else if (lane < 16) {
+                    sh.col[warp][16 * j + lane] = 0.0f;
+                }
+                *reinterpret_cast<uint4*>(sM + tc::tile_off(l, 2 * j, WB)) = m0;
+                *reinterpret_cast<uint4*>(sM + tc::tile_off(l, 2 * j + 1, WB)) = m1;
+                *reinterpret_cast<uint4*>(sG + tc::tile_off(l, 2 * j, WB)) = g0;
+                *reinterpret_cast<uint4*>(sG + tc::tile_off(l, 2 * j + 1, WB)) = g1;
+            }
+            // exp(cs_l) dy_l into sX (row l only: this thread's own row)
+            const float el = exp2_mufu(csl);
+            for (int j = 0; j < WX; ++j) {
+                float f[8];
+                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(l, j, WX)), f);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) f[k] *= el;
+                *reinterpret_cast<uint4*>(sX + tc::tile_off(l, j, WX)) = pack8<T>(f);
+            }
+        }
+        tc::fence_async_smem();
+        tc::fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tc::fence_after();
+            const uint32_t i_mn_mn64 = tc::idesc_f16(fmt, 128, P, true, true);
+            const uint32_t i_k_mn64 = tc::idesc_f16(fmt, 128, P, false, true);
+            const uint32_t i_k_mn = tc::idesc_f16(fmt, 128, 128, false, true);
+            const uint32_t i_k_k = tc::idesc_f16(fmt, 128, 128, false, false);
+            const uint32_t i_mn_mn = tc::idesc_f16(fmt, 128, 128, true, true);
+            const uint32_t first = hh == 0 ? 0u : 1u;
+#pragma unroll
+            for (int ks = 0; ks < Q / 16; ++ks)   // Mh^T dY
+                tc::mma_f16(tS, tc::desc_mn(aM, WB, 16 * ks), tc::desc_mn(aY, WX, 16 * ks), i_mn_mn64, ks > 0);
+#pragma unroll
+            for (int ks = 0; ks < N / 16; ++ks)   // B dH^T
+                tc::mma_f16(tS + 64, tc::desc_k(aB, WB, 2 * ks), tc::desc_mn(aD, WH, 16 * ks), i_k_mn64, ks > 0);
+#pragma unroll
+            for (int ks = 0; ks < Q / 16; ++ks)   // dC += dG B
+                tc::mma_f16(tdC, tc::desc_k(aG, WB, 2 * ks), tc::desc_mn(aB, WB, 16 * ks), i_k_mn, ks > 0 ? 1u : first);
+#pragma unroll
+            for (int ks = 0; ks < P / 16; ++ks)   // dC += (exp(cs) dy) H
+                tc::mma_f16(tdC, tc::desc_k(aX, WX, 2 * ks), tc::desc_k(aH, WH, 2 * ks), i_k_k, 1u);
+#pragma unroll
+            for (int ks = 0; ks < Q / 16; ++ks)   // dB += dG^T C
+                tc::mma_f16(tdB, tc::desc_mn(aG, WB, 16 * ks), tc::desc_mn(aC, WB, 16 * ks), i_mn_mn, ks > 0 ? 1u : first);
+#pragma unroll
+            for (int ks = 0; ks < P / 16; ++ks)   // dB += (w o x) dH
+                tc::mma_f16(tdB, tc::desc_k(aXW, WX, 2 * ks), tc::desc_k(aD, WH, 2 * ks), i_k_k, 1u);
+            tc::commit(tc::smem_u32(&mbar));
+        }
+        // column sums of E over the rows
+        float colsum = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kThreads / 32; ++w) colsum += sh.col[w][r];
+        const float dD_sum = block_sum(dD_head, sh.scan);
+        if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(43); ok = false; }
+        phase ^= 1;
+        tc::fence_after();
+        ok = __syncthreads_and(ok);
+        if (!ok) break;
+        // epilogue, row s = r
+        float dcs = 0.0f, dd_direct = 0.0f, dv = 0.0f;
+        {
+            const int s = r;
+            const float eTs = exp2_mufu((Tc - st.cs) * kLog2e);
+            float v_s = 0.0f;
+            const float Dh = (has_d && !d_per_head) ? a.D[h] : 0.0f;
+            for (int j = 0; j < P / 16; ++j) {
+                float di[16], zz[16], xv[16], yv[16];
+                tc::tmem_ld16(tS + lane_off + 16 * j, di);
+                tc::tmem_ld16(tS + lane_off + 64 + 16 * j, zz);
+                tc::tmem_wait_ld();
+                if (s < valid) {
+                    Pk<T>::unpack(*reinterpret_cast<const uint4*>(xg + grow + 16 * j), xv);
+                    Pk<T>::unpack(*reinterpret_cast<const uint4*>(xg + grow + 16 * j + 8), xv + 8);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) xv[k] = 0.0f;
+                }
+                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(s, 2 * j, WX)), yv);
+                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(s, 2 * j + 1, WX)), yv + 8);
+                float dxv[16];
+#pragma unroll
+                for (int k = 0; k < 16; ++k) {
+                    v_s = fmaf(xv[k], zz[k], v_s);
+                    const float Dk = has_d ? (d_per_head ? a.D[h * P + 16 * j + k] : Dh) : 0.0f;
+                    dxv[k] = fmaf(st.d * eTs, zz[k], di[k]) + Dk * yv[k];   // Mh already carries d_s
+                }
+                if (s < valid) {
+                    *reinterpret_cast<uint4*>(dxg + grow + 16 * j) = pack8<T>(dxv);
+                    *reinterpret_cast<uint4*>(dxg + grow + 16 * j + 8) = pack8<T>(dxv + 8);
+                }
+            }
+            v_s *= eTs;
+            dv = st.d * v_s;
+            dcs = rowsum - st.d * colsum - dv + a.dcs_inter[bhc * Q + s];
+            dd_direct = colsum + v_s;
+        }
+        // d/dT_c = exp(T) <dH_{c+1}, H_c> + sum_s d_s v_s, added at the chunk's last position
+        const float dv_sum = block_sum(dv, sh.scan);
+        if (r == Q - 1) dcs += a.dT[bhc] + dv_sum;
+        const float suffix = block_suffix_scan(dcs, sh.scan);
+        const float dd = fmaf(Ah, suffix, dd_direct);
+        const float ddt = (a.flags & SSM_SOFTPLUS) ? dd * softplus_grad_f(st.raw) : dd;
+        if (r < valid) a.ddt[(b * L + t0 + r) * H + h] = ddt;
+        const float dA_sum = block_sum(dcs * st.cd, sh.scan);
+        const float db_sum = block_sum(r < valid ? ddt : 0.0f, sh.scan);
+        if (tid == 0) {
+            a.dA_part[bhc] = dA_sum;
+            a.db_part[bhc] = db_sum;
+            if (has_d && !d_per_head) a.dD_part[bhc] = dD_sum;
+        }
+        tc::fence_before();
+        __syncthreads();
+    }
+    if (ok) {
+        // dC rows l, dB rows s (fp32, valid rows only)
+        const int r = tid;
+        const bool live = r < valid;
+        float* dCr = a.dC + ((b * L + t0 + (live ? r : 0)) * G + g) * N;
+        float* dBr = a.dB + ((b * L + t0 + (live ? r : 0)) * G + g) * N;
+        for (int j = 0; j < N / 16; ++j) {
+            float vc[16], vb[16];
+            tc::tmem_ld16(tdC + lane_off + 16 * j, vc);   // all lanes: .sync.aligned
+            tc::tmem_ld16(tdB + lane_off + 16 * j, vb);
+            tc::tmem_wait_ld();
+            if (live) {
+#pragma unroll
+                for (int k = 0; k < 16; k += 4) {
+                    *reinterpret_cast<float4*>(dCr + 16 * j + k) = make_float4(vc[k], vc[k + 1], vc[k + 2], vc[k + 3]);
+                    *reinterpret_cast<float4*>(dBr + 16 * j + k) = make_float4(vb[k], vb[k + 1], vb[k + 2], vb[k + 3]);
+                }
+            }
+        }
+    }
+    tc::cp_async_wait<0>();
+    tc::fence_before();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tm, 512);
+}
+
+// dA, d dt_bias, dD over (batch, chunk), fixed order.
+__global__ void reduce_kernel(const Args a, float* dA, float* dbias, float* dD) {
+    const int64_t H = a.nheads;
+    const bool has_d = a.flags & SSM_HAS_D, d_per_head = a.flags & SSM_D_PER_HEAD;
+    const int64_t nd = has_d ? (d_per_head ? H * P : H) : 0;
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= 2 * H + nd) return;
+    float s = 0.0f;
+    if (i < 2 * H) {
+        const int64_t h = i % H;
+        const float* src = i < H ? a.dA_part : a.db_part;
+        for (int64_t b = 0; b < a.batch; ++b)
+            for (int64_t c = 0; c < a.nc; ++c) s += src[(b * H + h) * a.nc + c];
+        if (i < H) dA[h] = s;
+        else if (dbias) dbias[h] = s;
+    } else {
+        const int64_t k = i - 2 * H;
+        if (d_per_head) {
+            const int64_t h = k / P, p = k % P;
+            for (int64_t b = 0; b < a.batch; ++b)
+                for (int64_t c = 0; c < a.nc; ++c) s += a.dD_part[((b * H + h) * a.nc + c) * P + p];
+        } else {
+            for (int64_t b = 0; b < a.batch; ++b)
+                for (int64_t c = 0; c < a.nc; ++c) s += a.dD_part[(b * H + k) * a.nc + c];
+        }
+        dD[k] = s;
+    }
+}
+
+// ------------------------------------------------------------------ host ----
+constexpr size_t kSmemStates = 2 * kTileB + 2 * kTileX;
+constexpr size_t kSmemOutputs = 2 * kTileB + kTileX + kTileH;
+constexpr size_t kSmemDstates = kTileB + 2 * kTileH;
+constexpr size_t kSmemGrads = 4 * kTileB + 3 * kTileX + 2 * kTileH;
+
+bool eligible(const ssm_chunk_scan_params* p) {
+    return (p->dtype == SSM_BF16 || p->dtype == SSM_F16) && p->headdim == P && p->dstate == N &&
+           !(p->flags & SSM_CUDA_CORES);
+}
+
+static int64_t n_chunks(const ssm_chunk_scan_params* p) { return ceil_div(p->length, (int64_t)Q); }
+
+struct Saved { size_t ht, yp, total; };
+static Saved saved_layout(const ssm_chunk_scan_params* p) {
+    Saved s;
+    const int64_t BH = p->batch * p->nheads;
+    s.ht = align_up((size_t)(BH * n_chunks(p)) * kTileH, 256);
+    s.yp = (p->flags & SSM_HAS_Z) ? align_up((size_t)(p->batch * p->length * p->nheads * P) * 2, 256) : 0;
+    s.total = s.ht + s.yp;
+    return s;
+}
+struct Ws { size_t dh, dci, dt, part, dd, total; };
+static Ws ws_layout(const ssm_chunk_scan_params* p) {
+    Ws w;
+    const int64_t BH = p->batch * p->nheads, nc = n_chunks(p);
+    w.dh = align_up((size_t)(BH * nc) * kTileH, 256);
+    w.dci = align_up((size_t)(BH * nc * Q) * 4, 256);
+    w.dt = align_up((size_t)(BH * nc) * 4, 256);
+    w.part = w.dt;
+    w.dd = align_up((size_t)(BH * nc * P) * 4, 256);
+    w.total = w.dh + w.dci + w.dt + 2 * w.part + w.dd;
+    return w;
+}
+
+void sizes(const ssm_chunk_scan_params* p, size_t* saved_bytes, size_t* workspace_bytes) {
+    if (saved_bytes) *saved_bytes = saved_layout(p).total;
+    if (workspace_bytes) *workspace_bytes = ws_layout(p).total;
+}
+
+static void make_args(const ssm_chunk_scan_params* p, Args& a) {
+    a.batch = p->batch; a.length = p->length; a.nheads = p->nheads; a.ngroups = p->ngroups;
+    a.nc = n_chunks(p); a.hpg = p->nheads / p->ngroups;
+    a.flags = p->flags; a.dt_dtype = p->dt_dtype;
+    a.x = p->x; a.dt = p->dt; a.A = p->A; a.B = p->B; a.C = p->C; a.D = p->D; a.z = p->z;
+    a.dt_bias = p->dt_bias; a.init = p->initial_states;
+    a.y = p->y; a.final_state = p->final_state;
+    const Saved s = saved_layout(p);
+    unsigned char* sv = reinterpret_cast<unsigned char*>(p->saved);
+    a.Ht = sv;
+    a.ypre = (sv && s.yp) ? sv + s.ht : nullptr;
+    a.dy = p->dy; a.dfinal = p->dfinal; a.dx = p->dx; a.ddt = p->ddt; a.dB = p->dB; a.dC = p->dC;
+    a.dz = p->dz; a.dinit = p->dinitial;
+    a.dHt = nullptr; a.dcs_inter = a.dT = a.dA_part = a.db_part = a.dD_part = nullptr;
+}
+
+static bool aligned16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; }
+
+static int set_smem(const void* fn, size_t bytes) {
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
+        return check_launch("chunk_scan (tensor cores): smem attribute");
+    return SSM_OK;
+}
+
+template <typename T>
+static int run_fwd(const Args& a, cudaStream_t s) {
+    if (int e = set_smem((const void*)states_kernel<T>, kSmemStates)) return e;
+    if (int e = set_smem((const void*)outputs_kernel<T>, kSmemOutputs)) return e;
+    states_kernel<T><<<dim3((unsigned)a.nheads, (unsigned)a.batch), kThreads, kSmemStates, s>>>(a);
+    if (int e = check_launch("chunk_scan fwd (tensor cores): states")) return e;
+    outputs_kernel<T><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)a.batch), kThreads, kSmemOutputs, s>>>(a);
+    return check_launch("chunk_scan fwd (tensor cores): outputs");
+}
+
+template <typename T>
+static int run_bwd(const Args& a, const ssm_chunk_scan_params* p, cudaStream_t s) {
+    if (int e = set_smem((const void*)dstates_kernel<T>, kSmemDstates)) return e;
+    if (int e = set_smem((const void*)grads_kernel<T>, kSmemGrads)) return e;
+    dstates_kernel<T><<<dim3((unsigned)a.nheads, (unsigned)a.batch), kThreads, kSmemDstates, s>>>(a);
+    if (int e = check_launch("chunk_scan bwd (tensor cores): dstates")) return e;
+    grads_kernel<T><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)a.batch), kThreads, kSmemGrads, s>>>(a);
+    if (int e = check_launch("chunk_scan bwd (tensor cores): grads")) return e;
+    const bool has_d = p->flags & SSM_HAS_D, d_per_head = p->flags & SSM_D_PER_HEAD;
+    const int64_t total = 2 * p->nheads + (has_d ? (d_per_head ? p->nheads * P : p->nheads) : 0);
+    reduce_kernel<<<(unsigned)ceil_div(total, (int64_t)128), 128, 0, s>>>(
+        a, p->dA, (p->flags & SSM_HAS_BIAS) ? p->ddt_bias : nullptr, has_d ? p->dD : nullptr);
+    return check_launch("chunk_scan bwd (tensor cores): reduce");
+}
+
+int fwd(const ssm_chunk_scan_params* p, cudaStream_t s) {
+    if (!p->saved) return fail(SSM_ERR_INVALID, "chunk_scan fwd (tensor cores): null saved buffer");
+    if (!aligned16(p->x) || !aligned16(p->B) || !aligned16(p->C) || !aligned16(p->y) ||
+        ((p->flags & SSM_HAS_Z) && !aligned16(p->z)) || !aligned16(p->saved))
+        return fail(SSM_ERR_INVALID, "chunk_scan fwd (tensor cores): x, B, C, z, y and saved must be 16-byte aligned");
+    Args a;
+    make_args(p, a);
+    return p->dtype == SSM_BF16 ? run_fwd<__nv_bfloat16>(a, s) : run_fwd<__half>(a, s);
+}
+
+int bwd(const ssm_chunk_scan_params* p, cudaStream_t s) {
+    const Ws w = ws_layout(p);
+    if (!p->workspace || p->workspace_bytes < w.total)
+        return fail(SSM_ERR_WORKSPACE, "chunk_scan bwd: workspace too small");
+    if (!aligned16(p->x) || !aligned16(p->B) || !aligned16(p->C) || !aligned16(p->dy) || !aligned16(p->dx) ||
+        ((p->flags & SSM_HAS_Z) && (!aligned16(p->z) || !aligned16(p->dz))) || !aligned16(p->saved) ||
+        !aligned16(p->dB) || !aligned16(p->dC))
+        return fail(SSM_ERR_INVALID, "chunk_scan bwd (tensor cores): x, B, C, z, dy, dx, dz, dB, dC and saved must be 16-byte aligned");
+    Args a;
+    make_args(p, a);
+    if (!(p->flags & SSM_HAS_INIT)) a.dinit = nullptr;
+    char* ws = reinterpret_cast<char*>(p->workspace);
+    a.dHt = reinterpret_cast<unsigned char*>(ws);
+    a.dcs_inter = reinterpret_cast<float*>(ws + w.dh);
+    a.dT = reinterpret_cast<float*>(ws + w.dh + w.dci);
+    a.dA_part = reinterpret_cast<float*>(ws + w.dh + w.dci + w.dt);
+    a.db_part = reinterpret_cast<float*>(ws + w.dh + w.dci + w.dt + w.part);
+    a.dD_part = reinterpret_cast<float*>(ws + w.dh + w.dci + w.dt + 2 * w.part);
+    return p->dtype == SSM_BF16 ? run_bwd<__nv_bfloat16>(a, p, s) : run_bwd<__half>(a, p, s);
+}
+
+}  // namespace ssdtc
+}  // namespace ssm
+
+extern "C" int ssm_take_kernel_error(void) {
+    int v = 0;
+    const cudaError_t e = cudaMemcpyFromSymbol(&v, ssm::ssdtc::g_kernel_error, sizeof(int));
+    if (e != cudaSuccess) return -1;
+    if (v) {
+        const int zero = 0;
+        cudaMemcpyToSymbol(ssm::ssdtc::g_kernel_error, &zero, sizeof(int));
+    }
+    return v;
+}

@@ -32,10 +32,21 @@ import torch
 
 from .. import _native as nat
 
-__all__ = ["mamba2_chunk_scan", "last_path"]
+__all__ = ["mamba2_chunk_scan", "last_path", "set_tensor_cores"]
 
 _DTYPES = (torch.float32, torch.float16, torch.bfloat16)
 _path = "none"
+_tensor_cores = True
+
+
+def set_tensor_cores(enabled: bool) -> bool:
+    """Allow (default) or forbid the tensor-core kernels, which serve bf16/f16
+    inputs with d_head 64 and d_state 128; forbidden, those inputs run the
+    CUDA-core kernels like every other case.  Returns the previous setting.
+    The setting must not change between a forward and its backward."""
+    global _tensor_cores
+    prev, _tensor_cores = _tensor_cores, bool(enabled)
+    return prev
 
 
 def last_path():
@@ -56,6 +67,10 @@ def _params(x, dt, A, B, C, D, z, dt_bias, init, chunk_size, softplus):
                | (nat.D_PER_HEAD if D is not None and D.dim() == 2 else 0)
                | (nat.HAS_Z if z is not None else 0) | (nat.HAS_BIAS if dt_bias is not None else 0)
                | (nat.SOFTPLUS if softplus else 0) | (nat.HAS_INIT if init is not None else 0))
+    # the tensor-core kernels move 16-byte rows: odd views take the CUDA-core path
+    if not _tensor_cores or (x.device.type != "meta" and any(
+            t is not None and t.data_ptr() % 16 for t in (x, B, C, z))):
+        p.flags |= nat.CUDA_CORES
     if x.device.type == "meta":
         return p
     p.x, p.dt, p.A, p.B, p.C = (t.data_ptr() for t in (x, dt, A, B, C))
@@ -152,7 +167,10 @@ def _backward(ctx, dy, dfinal, dsaved):
     x, dt, A, B, C, D, z, dt_bias, init, saved = ctx.saved_tensors
     if dy is None:
         dy = torch.zeros_like(x)
-    grads = _bwd(dy.contiguous(), None if dfinal is None else dfinal.float().contiguous(),
+    dy = dy.contiguous()
+    if dy.data_ptr() % 16:
+        dy = dy.clone()
+    grads = _bwd(dy, None if dfinal is None else dfinal.float().contiguous(),
                  x, dt, A, B, C, D, z, dt_bias, init, saved, ctx.chunk_size, ctx.softplus)
     dx, ddt, dA, dB, dC, dD, dz, dbias, dinit = grads
     return (dx, ddt.to(dt.dtype), dA, dB.to(B.dtype), dC.to(C.dtype),

@@ -1,0 +1,168 @@
+"""Mamba-2 SSD chunk scan, tensor-core path (tcgen05 / TMEM), vs the fp64 oracle.
+
+The tensor-core kernels serve bf16/f16 inputs with d_head 64 and d_state 128
+(the Mamba-2 layer shape of BASELINE config 3); they round each GEMM operand to
+the input dtype and accumulate in fp32.  These tests check them the way the
+reference's verifier checks its fast path (benchmarks/verify_mamba2_chunk.py):
+forward outputs and final state over ragged lengths, group sizes and every
+option against the fp64 sequential recurrence (max|err| / max|ref|: bf16 2e-2,
+f16 2e-3), all nine gradients against fp64 autograd (norm-relative: bf16 3e-2,
+f16 5e-3), agreement with the CUDA-core kernels at the full config-3 size,
+bit-identical reruns, and that no kernel gave up on a bounded wait.
+"""
+
+import pytest
+import torch
+
+from oracle import ssm_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+P, N = 64, 128
+TOL_FWD = {torch.bfloat16: 2e-2, torch.float16: 2e-3}
+TOL_GRAD = {torch.bfloat16: 3e-2, torch.float16: 5e-3}
+NAMES = ("x", "dt", "A", "B", "C", "D", "z", "dt_bias", "initial_states")
+
+
+def _mod():
+    from metal_kernelops_b200.cv import mamba2_chunk
+    return mamba2_chunk
+
+
+def _inputs(batch, length, nheads, ngroups, seed, dtype, d_per_head=False):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(batch, length, nheads, P, generator=g)
+    dt = torch.randn(batch, length, nheads, generator=g) - 1.0
+    A = -(torch.rand(nheads, generator=g) * 4 + 0.5)
+    B = torch.randn(batch, length, ngroups, N, generator=g)
+    C = torch.randn(batch, length, ngroups, N, generator=g)
+    D = torch.randn(nheads, P, generator=g) if d_per_head else torch.randn(nheads, generator=g)
+    z = torch.randn(batch, length, nheads, P, generator=g)
+    bias = torch.randn(nheads, generator=g) * 0.5
+    init = torch.randn(batch, nheads, P, N, generator=g) * 0.2
+    vals = dict(x=x, dt=dt, A=A, B=B, C=C, D=D, z=z, dt_bias=bias, initial_states=init)
+    # x, B, C, z, dt in the run dtype; the oracle sees the same rounded values
+    for k in ("x", "dt", "B", "C", "z"):
+        vals[k] = vals[k].to(dtype)
+    return vals
+
+
+def _run(vals, device, cast, fn, opts, grad=False):
+    t = {k: (v.to(device) if k in ("x", "dt", "B", "C", "z") else v.to(device, cast))
+         for k, v in vals.items()}
+    if cast == torch.float64:
+        t = {k: v.double() for k, v in t.items()}
+    if grad:
+        t = {k: v.requires_grad_(True) for k, v in t.items()}
+    kw = {k: t[k] for k in opts}
+    y, s = fn(t["x"], t["dt"], t["A"], t["B"], t["C"], 256, dt_softplus=True, **kw)
+    return t, y, s
+
+
+SHAPES = [(1, 128, 2, 1), (2, 300, 4, 2), (1, 1000, 8, 2), (2, 77, 6, 3)]
+OPTS = [(), ("D", "z", "dt_bias", "initial_states")]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("oi", range(len(OPTS)))
+@pytest.mark.parametrize("si", range(len(SHAPES)))
+def test_tc_forward(si, oi, dtype):
+    m = _mod()
+    vals = _inputs(*SHAPES[si], seed=100 + si, dtype=dtype)
+    opts = OPTS[oi]
+    _, y, s = _run(vals, "cuda", torch.float32, m.mamba2_chunk_scan, opts)
+    _, yr, sr = _run(vals, "cpu", torch.float64, orc.mamba2_chunk_scan_ref, opts)
+    assert y.dtype == dtype
+    assert orc.max_rel(y.float().cpu(), yr) <= TOL_FWD[dtype]
+    assert orc.max_rel(s.float().cpu(), sr) <= TOL_FWD[dtype]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", [(2, 300, 4, 2), (1, 129, 4, 4)])
+def test_tc_gradients_all_inputs(shape, dtype):
+    m = _mod()
+    vals = _inputs(*shape, seed=7, dtype=dtype)
+    g = torch.Generator().manual_seed(8)
+    wy = torch.randn(shape[0], shape[1], shape[2], P, generator=g)
+    ws = torch.randn(shape[0], shape[2], P, N, generator=g)
+    opts = ("D", "z", "dt_bias", "initial_states")
+
+    def grads(device, cast, fn):
+        t, y, s = _run(vals, device, cast, fn, opts, grad=True)
+        loss = (y.to(cast) * wy.to(device, cast)).sum() + (s.to(cast) * ws.to(device, cast)).sum()
+        return torch.autograd.grad(loss, [t[k] for k in NAMES])
+
+    fast = grads("cuda", torch.float32, m.mamba2_chunk_scan)
+    slow = grads("cpu", torch.float64, orc.mamba2_chunk_scan_ref)
+    for name, gf, gs in zip(NAMES, fast, slow):
+        assert orc.norm_rel(gf.float().cpu(), gs) <= TOL_GRAD[dtype], name
+
+
+def test_tc_gradients_per_head_p_D_no_softplus():
+    m = _mod()
+    dtype = torch.bfloat16
+    vals = _inputs(1, 200, 4, 2, seed=9, dtype=dtype, d_per_head=True)
+    vals["dt"] = (vals["dt"].float().abs() * 0.05 + 0.01).to(dtype)
+    keys = ("x", "dt", "A", "B", "C", "D")
+
+    def grads(device, cast, fn):
+        t = {k: vals[k].to(device) if k in ("x", "dt", "B", "C") else vals[k].to(device, cast) for k in keys}
+        if cast == torch.float64:
+            t = {k: v.double() for k, v in t.items()}
+        t = {k: v.requires_grad_(True) for k, v in t.items()}
+        y, s = fn(t["x"], t["dt"], t["A"], t["B"], t["C"], 64, D=t["D"])
+        loss = y.to(cast).square().sum() + s.to(cast).square().sum()
+        return y, s, torch.autograd.grad(loss, [t[k] for k in keys])
+
+    y, s, fast = grads("cuda", torch.float32, m.mamba2_chunk_scan)
+    yr, sr, slow = grads("cpu", torch.float64, orc.mamba2_chunk_scan_ref)
+    assert orc.max_rel(y.float().detach().cpu(), yr.detach()) <= TOL_FWD[dtype]
+    for name, gf, gs in zip(keys, fast, slow):
+        assert orc.norm_rel(gf.float().cpu(), gs) <= TOL_GRAD[dtype], name
+
+
+def test_tc_deterministic_and_no_kernel_error():
+    m = _mod()
+    from metal_kernelops_b200 import _native as nat
+    vals = _inputs(2, 700, 8, 2, seed=11, dtype=torch.bfloat16)
+    runs = []
+    for _ in range(3):
+        t, y, s = _run(vals, "cuda", torch.float32, m.mamba2_chunk_scan, ("D", "dt_bias"), grad=True)
+        gr = torch.autograd.grad(y.float().sum() + s.float().sum(), [t[k] for k in ("x", "dt", "A", "B", "C")])
+        runs.append((y.detach(), s.detach()) + tuple(gr))
+    for vals_ in zip(*runs):
+        assert all(torch.equal(vals_[0], v) for v in vals_[1:])
+    torch.cuda.synchronize()
+    assert nat.lib().ssm_take_kernel_error() == 0
+
+
+def test_tc_and_cuda_cores_agree_at_config3():
+    """BASELINE config 3 at full size (B8 L8192 H80 P64 N128 G8, bf16): the
+    tensor-core forward and backward agree with the CUDA-core kernels (which
+    are exact to fp32 rounding) within the bf16 tolerances."""
+    m = _mod()
+    inp = orc.ssd_inputs(8, 8192, 80, 64, 128, 8)
+    dev = {k: v.cuda() for k, v in inp.items()}
+
+    def run(tensor_cores):
+        prev = m.set_tensor_cores(tensor_cores)
+        try:
+            leaves = [dev[k].clone().requires_grad_(True) for k in ("x", "dt", "A", "B", "C", "D", "dt_bias")]
+            x, dt, A, B, C, D, bias = leaves
+            y, s = m.mamba2_chunk_scan(x, dt, A, B, C, 256, D=D, dt_bias=bias, dt_softplus=True)
+            g = torch.autograd.grad((y.float() * dev["dy"].float()).sum(), leaves)
+            return [y.detach().float(), s.detach().float()] + [t.float() for t in g]
+        finally:
+            m.set_tensor_cores(prev)
+
+    fast = run(True)
+    exact = run(False)
+    names = ("y", "final", "dx", "ddt", "dA", "dB", "dC", "dD", "ddt_bias")
+    for name, a, b in zip(names, fast, exact):
+        assert torch.isfinite(a).all(), name
+        tol = 2e-2 if name in ("y", "final") else 3e-2
+        err = (orc.max_rel(a.cpu(), b.cpu()) if name in ("y", "final")
+               else orc.norm_rel(a.cpu(), b.cpu()))
+        assert err <= tol, (name, err)
+    from metal_kernelops_b200 import _native as nat
+    assert nat.lib().ssm_take_kernel_error() == 0
