@@ -198,19 +198,46 @@ struct Steps {
     float cd;    // running sum of d inside the chunk
     float cs;    // A * cd
 };
-__device__ __forceinline__ Steps chunk_steps(const Args& a, int64_t b, int64_t h, int64_t c, float Ah,
-                                             float bias, float* scan_sh) {
-    Steps s;
+// dt + bias of this thread's position of chunk c (0 beyond the sequence).
+__device__ __forceinline__ float raw_dt(const Args& a, int64_t b, int64_t h, int64_t c, float bias) {
     const int64_t t = c * Q + threadIdx.x;
-    s.raw = 0.0f;
-    s.d = 0.0f;
-    if (t < a.length) {
-        s.raw = ld_dt(a, (b * a.length + t) * a.nheads + h) + bias;
-        s.d = (a.flags & SSM_SOFTPLUS) ? softplus_f(s.raw) : s.raw;
-    }
+    return t < a.length ? ld_dt(a, (b * a.length + t) * a.nheads + h) + bias : 0.0f;
+}
+__device__ __forceinline__ Steps steps_of(const Args& a, float raw, int64_t c, float Ah, float* scan_sh) {
+    Steps s;
+    const bool valid = c * Q + threadIdx.x < a.length;
+    s.raw = raw;
+    s.d = valid ? ((a.flags & SSM_SOFTPLUS) ? softplus_f(raw) : raw) : 0.0f;
     s.cd = block_incl_scan(s.d, scan_sh);
     s.cs = Ah * s.cd;
     return s;
+}
+
+// dt + bias, A and D of up to kHeadsSh heads of a group for one chunk, loaded
+// together so that their global latency is paid once, not once per head.
+constexpr int kHeadsSh = 16;
+struct HeadSh {
+    float raw[kHeadsSh][Q + 1];     // dt + bias (padded row: conflict-free writes)
+    float A[kHeadsSh], D[kHeadsSh];
+};
+__device__ __forceinline__ void stage_heads(const Args& a, HeadSh& hs, int64_t b, int64_t g, int64_t c,
+                                            int64_t hh0, int n) {
+    const int64_t h0 = g * a.hpg + hh0;
+    const bool has_bias = a.flags & SSM_HAS_BIAS;
+    if ((int)threadIdx.x < n) {
+        hs.A[threadIdx.x] = a.A[h0 + threadIdx.x];
+        hs.D[threadIdx.x] = ((a.flags & SSM_HAS_D) && !(a.flags & SSM_D_PER_HEAD)) ? a.D[h0 + threadIdx.x] : 0.0f;
+    }
+    for (int i = threadIdx.x; i < n * Q; i += kThreads) {
+        const int pos = i / n, k = i % n;     // consecutive threads: consecutive heads of one position
+        const int64_t t = c * Q + pos;
+        float v = 0.0f;
+        if (t < a.length) v = ld_dt(a, (b * a.length + t) * a.nheads + h0 + k) + (has_bias ? a.dt_bias[h0 + k] : 0.0f);
+        hs.raw[k][pos] = v;
+    }
+}
+__device__ __forceinline__ Steps staged_steps(const Args& a, const HeadSh& hs, int k, int64_t c, float* scan_sh) {
+    return steps_of(a, hs.raw[k][threadIdx.x], c, hs.A[k], scan_sh);
 }
 
 // ====================================================================== F1 ==
@@ -263,9 +290,12 @@ __global__ void __launch_bounds__(kThreads) states_kernel(const Args a) {
     uint32_t phase = 0;
     bool ok = true;
     unsigned char* Hout = a.Ht + (size_t)(b * H + h) * a.nc * kTileH;
+    float raw_next = raw_dt(a, b, h, 0, bias);
     for (int64_t c = 0; c < a.nc && ok; ++c) {
         const int buf = (int)(c & 1);
-        const Steps st = chunk_steps(a, b, h, c, Ah, bias, s_scan);
+        const float raw = raw_next;
+        if (c + 1 < a.nc) raw_next = raw_dt(a, b, h, c + 1, bias);   // in flight during this chunk
+        const Steps st = steps_of(a, raw, c, Ah, s_scan);
         if (tid == Q - 1) s_T = st.cs;
         if (c > 0) {   // the previous chunk's GEMM read sXW and sB[buf ^ 1]
             if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(11); ok = false; }
@@ -372,6 +402,7 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const Args a) {
     unsigned char* sX = sm + 2 * kTileB;
     unsigned char* sH = sX + kTileX;
     __shared__ MaskSh msh;
+    __shared__ HeadSh hsh;
     __shared__ float s_scan[4];
     __shared__ __align__(8) uint64_t mbar;
     __shared__ uint32_t tbase;
@@ -424,9 +455,12 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const Args a) {
         load_rows<WX>(sX, xg + ((b * L + t0) * H + h) * P, H * P, valid);
         load_image(sH, a.Ht + ((size_t)(b * H + h) * a.nc + c) * kTileH);
         tc::cp_async_commit();
-        const float Ah = a.A[h];
-        const float bias = (a.flags & SSM_HAS_BIAS) ? a.dt_bias[h] : 0.0f;
-        const Steps st = chunk_steps(a, b, h, c, Ah, bias, s_scan);
+        const int hk = (int)(hh % kHeadsSh);
+        if (hk == 0) {
+            stage_heads(a, hsh, b, g, c, hh, (int)min64(kHeadsSh, a.hpg - hh));
+            __syncthreads();
+        }
+        const Steps st = staged_steps(a, hsh, hk, c, s_scan);
         mask_factors(msh, st);
         // Mh row l = tid into sM (B is no longer needed once G is in TMEM)
         {
@@ -483,7 +517,7 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const Args a) {
             const bool live = l < valid;
             const int64_t row = ((b * L + t0 + l) * H + h) * P;
             const float el = exp2_mufu(msh.cs2[l]);
-            const float Dh = (has_d && !d_per_head) ? a.D[h] : 0.0f;
+            const float Dh = hsh.D[hk];
             for (int j = 0; j < P / 16; ++j) {
                 float yi[16], ye[16];
                 tc::tmem_ld16(tm + lane_off + 128 + 16 * j, yi);
@@ -574,14 +608,17 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const Args a) {
     const uint32_t aC = tc::smem_u32(sC), aY = tc::smem_u32(sY);
     uint32_t phase = 0;
     bool ok = true;
+    float raw_next = raw_dt(a, b, h, a.nc - 1, bias);
     for (int64_t c = a.nc - 1; c >= 0 && ok; --c) {
+        const float raw = raw_next;
+        if (c > 0) raw_next = raw_dt(a, b, h, c - 1, bias);
         const int64_t t0 = c * Q;
         const int valid = (int)min64(Q, L - t0);
         load_rows<WB>(sC, reinterpret_cast<const T*>(a.C) + ((b * L + t0) * G + g) * N, G * N, valid);
         load_image(sH, Hin + (size_t)c * kTileH);
         load_rows<WX>(sY, dyg + ((b * L + t0) * H + h) * P, H * P, valid);
         tc::cp_async_commit();
-        const Steps st = chunk_steps(a, b, h, c, Ah, bias, s_scan);
+        const Steps st = steps_of(a, raw, c, Ah, s_scan);
         if (tid == Q - 1) s_T = st.cs;
         tc::cp_async_wait<0>();
         __syncthreads();
@@ -709,6 +746,7 @@ __device__ __forceinline__ float warp_colsum16(float* v) {
 // scratch [384,512): dY X^T, then Mh^T dY [384,448) and B dH^T [448,512).
 struct GradSh {
     MaskSh m;
+    HeadSh hs;
     float col[kThreads / 32][Q];
     float scan[4];
     float T;
@@ -784,9 +822,13 @@ __global__ void __launch_bounds__(kThreads, 1) grads_kernel(const Args a) {
         load_image(sH, a.Ht + ((size_t)(b * H + h) * a.nc + c) * kTileH);
         load_image(sD, a.dHt + (size_t)bhc * kTileH);
         tc::cp_async_commit();
-        const float Ah = a.A[h];
-        const float bias = (a.flags & SSM_HAS_BIAS) ? a.dt_bias[h] : 0.0f;
-        const Steps st = chunk_steps(a, b, h, c, Ah, bias, sh.scan);
+        const int hk = (int)(hh % kHeadsSh);
+        if (hk == 0) {
+            stage_heads(a, sh.hs, b, g, c, hh, (int)min64(kHeadsSh, a.hpg - hh));
+            __syncthreads();
+        }
+        const float Ah = sh.hs.A[hk];
+        const Steps st = staged_steps(a, sh.hs, hk, c, sh.scan);
         if (tid == Q - 1) sh.T = st.cs;
         mask_factors(sh.m, st);
         const float Tc = sh.T;
@@ -940,6 +982,16 @@ __global__ void __launch_bounds__(kThreads, 1) grads_kernel(const Args a) {
                 tc::mma_f16(tdB, tc::desc_k(aXW, WX, 2 * ks), tc::desc_k(aD, WH, 2 * ks), i_k_k, 1u);
             tc::commit(tc::smem_u32(&mbar));
         }
+        // global inputs of the epilogue, fetched while the GEMMs run
+        uint4 xr[WX];
+        {
+            const bool live = r < valid;
+#pragma unroll
+            for (int j = 0; j < WX; ++j)
+                xr[j] = live ? *reinterpret_cast<const uint4*>(xg + grow + 8 * j) : make_uint4(0, 0, 0, 0);
+        }
+        const float dci = a.dcs_inter[bhc * Q + r];
+        const float dTc = r == Q - 1 ? a.dT[bhc] : 0.0f;
         // column sums of E over the rows
         float colsum = 0.0f;
 #pragma unroll
@@ -956,19 +1008,14 @@ __global__ void __launch_bounds__(kThreads, 1) grads_kernel(const Args a) {
             const int s = r;
             const float eTs = exp2_mufu((Tc - st.cs) * kLog2e);
             float v_s = 0.0f;
-            const float Dh = (has_d && !d_per_head) ? a.D[h] : 0.0f;
+            const float Dh = sh.hs.D[hk];
             for (int j = 0; j < P / 16; ++j) {
                 float di[16], zz[16], xv[16], yv[16];
                 tc::tmem_ld16(tS + lane_off + 16 * j, di);
                 tc::tmem_ld16(tS + lane_off + 64 + 16 * j, zz);
                 tc::tmem_wait_ld();
-                if (s < valid) {
-                    Pk<T>::unpack(*reinterpret_cast<const uint4*>(xg + grow + 16 * j), xv);
-                    Pk<T>::unpack(*reinterpret_cast<const uint4*>(xg + grow + 16 * j + 8), xv + 8);
-                } else {
-#pragma unroll
-                    for (int k = 0; k < 16; ++k) xv[k] = 0.0f;
-                }
+                Pk<T>::unpack(xr[2 * j], xv);
+                Pk<T>::unpack(xr[2 * j + 1], xv + 8);
                 Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(s, 2 * j, WX)), yv);
                 Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(s, 2 * j + 1, WX)), yv + 8);
                 float dxv[16];
@@ -985,12 +1032,12 @@ __global__ void __launch_bounds__(kThreads, 1) grads_kernel(const Args a) {
             }
             v_s *= eTs;
             dv = st.d * v_s;
-            dcs = rowsum - st.d * colsum - dv + a.dcs_inter[bhc * Q + s];
+            dcs = rowsum - st.d * colsum - dv + dci;
             dd_direct = colsum + v_s;
         }
         // d/dT_c = exp(T) <dH_{c+1}, H_c> + sum_s d_s v_s, added at the chunk's last position
         const float dv_sum = block_sum(dv, sh.scan);
-        if (r == Q - 1) dcs += a.dT[bhc] + dv_sum;
+        if (r == Q - 1) dcs += dTc + dv_sum;
         const float suffix = block_suffix_scan(dcs, sh.scan);
         const float dd = fmaf(Ah, suffix, dd_direct);
         const float ddt = (a.flags & SSM_SOFTPLUS) ? dd * softplus_grad_f(st.raw) : dd;
