@@ -229,12 +229,19 @@ fwd_kernel(const Args a) {
         __syncthreads();
 
         if (a.ckpt != nullptr && (t0 % kChunk) == 0 && cvalid) {
-            float* cp = a.ckpt + ((b * a.nchunks + t0 / kChunk) * a.dim + d) * N;
+            float* cp = a.ckpt + ((b * a.nchunks + t0 / kChunk) * a.dim + d) * N + sub * NPT;
+            if (N % 4 == 0 && sub * NPT < N) {   // 16-byte aligned rows: vector stores
 #pragma unroll
-            for (int j = 0; j < NH; ++j) {
-                const int n = sub * NPT + 2 * j;
-                if (n < N) cp[n] = x2[j].x;
-                if (n + 1 < N) cp[n + 1] = x2[j].y;
+                for (int j = 0; j < NH; j += 2)
+                    if (sub * NPT + 2 * j < N)
+                        *reinterpret_cast<float4*>(cp + 2 * j) = make_float4(x2[j].x, x2[j].y, x2[j + 1].x, x2[j + 1].y);
+            } else {
+#pragma unroll
+                for (int j = 0; j < NH; ++j) {
+                    const int n = sub * NPT + 2 * j;
+                    if (n < N) cp[2 * j] = x2[j].x;
+                    if (n + 1 < N) cp[2 * j + 1] = x2[j].y;
+                }
             }
         }
 
