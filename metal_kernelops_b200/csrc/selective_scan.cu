@@ -30,6 +30,8 @@
 //    partial per CTA; a small kernel adds the partials and the per-batch
 //    dA/dD/d_bias partials in a fixed order.  No float atomics (the reference
 //    uses them, scan.py:226-227), so the backward is bit-reproducible.
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace ssm {
@@ -510,139 +512,146 @@ bwd_kernel(const Args a) {
         }
         __syncthreads();
 
-        // ---- pass A: forward recompute from the checkpoint -----------------
-        float2 x2[NH];
-        {
-            const float* cp = a.ckpt + ((b * a.nchunks + tile) * a.dim + d) * N;
-#pragma unroll
-            for (int j = 0; j < NH; ++j) {
-                const int n0 = sub * NPT + ((2 * j) ^ pm), n1 = sub * NPT + ((2 * j + 1) ^ pm);
-                x2[j] = make_float2((cvalid && n0 < N) ? cp[n0] : 0.0f,
-                                    (cvalid && n1 < N) ? cp[n1] : 0.0f);
-            }
-        }
-        const float2* vr = dvu + c * FS;
-        const float* gr = gs + c * FS;
-        for (int tb = 0; tb < len; tb += TS) {
-#pragma unroll
-            for (int j = 0; j < NH; ++j) sck[((tb / TS) * NH + j) * kThreads + tid] = x2[j];
-#pragma unroll
-            for (int jj = 0; jj < TS; ++jj) {
-                const int t = tb + jj;
-                if (t >= len) break;
-                const float2 v = vr[t];
-                const float dl = v.x * kLog2e;
-                const float2 dl2 = make_float2(dl, dl), du2 = make_float2(v.y, v.y);
-                const float gv = gr[t];
-                const float2 g2 = make_float2(gv, gv);
-                const float4* B4 = reinterpret_cast<const float4*>(Bp + t * NP);
-                const float4* C4 = reinterpret_cast<const float4*>(Cp + t * NP);
-                float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
-                float w[NPT];
-#pragma unroll
-                for (int qq = 0; qq < NPT / 4; ++qq) {
-                    const float4 bq = B4[qq ^ qx], cq = C4[qq ^ qx];
-                    const float2 a0 = __fmul2_rn(dl2, An2[2 * qq]);
-                    const float2 a1 = __fmul2_rn(dl2, An2[2 * qq + 1]);
-                    const float2 e0 = make_float2(exp2_mufu(a0.x), exp2_mufu(a0.y));
-                    const float2 e1 = make_float2(exp2_mufu(a1.x), exp2_mufu(a1.y));
-                    x2[2 * qq] = __ffma2_rn(e0, x2[2 * qq], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
-                    x2[2 * qq + 1] = __ffma2_rn(e1, x2[2 * qq + 1], __fmul2_rn(du2, make_float2(bq.z, bq.w)));
-                    acc0 = __ffma2_rn(x2[2 * qq], make_float2(cq.x, cq.y), acc0);
-                    acc1 = __ffma2_rn(x2[2 * qq + 1], make_float2(cq.z, cq.w), acc1);
-                    const float2 w0 = __fmul2_rn(g2, x2[2 * qq]);
-                    const float2 w1 = __fmul2_rn(g2, x2[2 * qq + 1]);
-                    w[4 * qq + 0] = w0.x;
-                    w[4 * qq + 1] = w0.y;
-                    w[4 * qq + 2] = w1.x;
-                    w[4 * qq + 3] = w1.y;
+        // The chunk's compute, instantiated for full chunks (no step checks)
+        // and for the ragged last chunk.
+        auto chunk_body = [&](auto full_tag) {
+            constexpr bool FULL = decltype(full_tag)::value;
+            // ---- pass A: forward recompute from the checkpoint -----------------
+            float2 x2[NH];
+            {
+                const float* cp = a.ckpt + ((b * a.nchunks + tile) * a.dim + d) * N;
+    #pragma unroll
+                for (int j = 0; j < NH; ++j) {
+                    const int n0 = sub * NPT + ((2 * j) ^ pm), n1 = sub * NPT + ((2 * j + 1) ^ pm);
+                    x2[j] = make_float2((cvalid && n0 < N) ? cp[n0] : 0.0f,
+                                        (cvalid && n1 < N) ? cp[n1] : 0.0f);
                 }
-                float ysum = (acc0.x + acc0.y) + (acc1.x + acc1.y);
-                ysum = sum_low_lanes<LPC>(ysum);
-                Sc::reduce(w);
-                if (own) {
-#pragma unroll
-                    for (int i = 0; i < KEPT; ++i) dCw[(warp * K + t) * NPW + sub * NPT + pm + i] = w[i];
-                }
-                if (sub == 0) yv[c * FS + t] = ysum;
             }
-        }
-
-        // ---- pass B: reverse over sub-blocks ---------------------------------
-        for (int sb = (len - 1) / TS; sb >= 0; --sb) {
-            const int tb = sb * TS;
-            const int nb = min(TS, len - tb);
-            float2 xh[TS][NH], ah[TS][NH];
-#pragma unroll
-            for (int j = 0; j < NH; ++j) x2[j] = sck[(sb * NH + j) * kThreads + tid];
-#pragma unroll
-            for (int jj = 0; jj < TS; ++jj) {
-                if (jj < nb) {
-                    const float2 v = vr[tb + jj];
+            const float2* vr = dvu + c * FS;
+            const float* gr = gs + c * FS;
+            for (int tb = 0; tb < (FULL ? K : len); tb += TS) {
+    #pragma unroll
+                for (int j = 0; j < NH; ++j) sck[((tb / TS) * NH + j) * kThreads + tid] = x2[j];
+    #pragma unroll
+                for (int jj = 0; jj < TS; ++jj) {
+                    const int t = tb + jj;
+                    if (!FULL && t >= len) break;
+                    const float2 v = vr[t];
                     const float dl = v.x * kLog2e;
                     const float2 dl2 = make_float2(dl, dl), du2 = make_float2(v.y, v.y);
-                    const float4* B4 = reinterpret_cast<const float4*>(Bp + (tb + jj) * NP);
-#pragma unroll
+                    const float gv = gr[t];
+                    const float2 g2 = make_float2(gv, gv);
+                    const float4* B4 = reinterpret_cast<const float4*>(Bp + t * NP);
+                    const float4* C4 = reinterpret_cast<const float4*>(Cp + t * NP);
+                    float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
+                    float w[NPT];
+    #pragma unroll
                     for (int qq = 0; qq < NPT / 4; ++qq) {
-                        const float4 bq = B4[qq ^ qx];
+                        const float4 bq = B4[qq ^ qx], cq = C4[qq ^ qx];
                         const float2 a0 = __fmul2_rn(dl2, An2[2 * qq]);
                         const float2 a1 = __fmul2_rn(dl2, An2[2 * qq + 1]);
                         const float2 e0 = make_float2(exp2_mufu(a0.x), exp2_mufu(a0.y));
                         const float2 e1 = make_float2(exp2_mufu(a1.x), exp2_mufu(a1.y));
-                        ah[jj][2 * qq] = e0;
-                        ah[jj][2 * qq + 1] = e1;
-                        xh[jj][2 * qq] = x2[2 * qq];
-                        xh[jj][2 * qq + 1] = x2[2 * qq + 1];
                         x2[2 * qq] = __ffma2_rn(e0, x2[2 * qq], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
                         x2[2 * qq + 1] = __ffma2_rn(e1, x2[2 * qq + 1], __fmul2_rn(du2, make_float2(bq.z, bq.w)));
+                        acc0 = __ffma2_rn(x2[2 * qq], make_float2(cq.x, cq.y), acc0);
+                        acc1 = __ffma2_rn(x2[2 * qq + 1], make_float2(cq.z, cq.w), acc1);
+                        const float2 w0 = __fmul2_rn(g2, x2[2 * qq]);
+                        const float2 w1 = __fmul2_rn(g2, x2[2 * qq + 1]);
+                        w[4 * qq + 0] = w0.x;
+                        w[4 * qq + 1] = w0.y;
+                        w[4 * qq + 2] = w1.x;
+                        w[4 * qq + 3] = w1.y;
                     }
-                }
-            }
-#pragma unroll
-            for (int jj = TS - 1; jj >= 0; --jj) {
-                if (jj < nb) {
-                    const int t = tb + jj;
-                    const float2 v = vr[t];
-                    const float gv = gr[t];
-                    const float2 g2 = make_float2(gv, gv), dv2 = make_float2(v.x, v.x);
-                    const float2 du2 = make_float2(v.y, v.y);
-                    const float4* B4 = reinterpret_cast<const float4*>(Bp + t * NP);
-                    const float4* C4 = reinterpret_cast<const float4*>(Cp + t * NP);
-                    float2 dua2 = make_float2(0.0f, 0.0f), dda2 = make_float2(0.0f, 0.0f);
-                    float w[NPT];
-#pragma unroll
-                    for (int qq = 0; qq < NPT / 4; ++qq) {
-                        const float4 bq = B4[qq ^ qx], cq = C4[qq ^ qx];
-                        const float2 bb[2] = {make_float2(bq.x, bq.y), make_float2(bq.z, bq.w)};
-                        const float2 cc2[2] = {make_float2(cq.x, cq.y), make_float2(cq.z, cq.w)};
-#pragma unroll
-                        for (int r = 0; r < 2; ++r) {
-                            const int j = 2 * qq + r;
-                            const float2 dh = __ffma2_rn(g2, cc2[r], q2[j]);
-                            const float2 tmp = __fmul2_rn(dh, __fmul2_rn(ah[jj][j], xh[jj][j]));
-                            dda2 = __ffma2_rn(tmp, An2[j], dda2);
-                            dA2[j] = __ffma2_rn(tmp, dv2, dA2[j]);
-                            dua2 = __ffma2_rn(dh, bb[r], dua2);
-                            const float2 wv = __fmul2_rn(dh, du2);
-                            w[2 * j] = wv.x;
-                            w[2 * j + 1] = wv.y;
-                            q2[j] = __fmul2_rn(dh, ah[jj][j]);
-                        }
-                    }
-                    const float duacc = sum_low_lanes<LPC>(dua2.x + dua2.y);
-                    const float ddacc = sum_low_lanes<LPC>(dda2.x + dda2.y);
+                    float ysum = (acc0.x + acc0.y) + (acc1.x + acc1.y);
+                    ysum = sum_low_lanes<LPC>(ysum);
                     Sc::reduce(w);
                     if (own) {
-#pragma unroll
-                        for (int i = 0; i < KEPT; ++i) dBw[(warp * K + t) * NPW + sub * NPT + pm + i] = w[i];
+    #pragma unroll
+                        for (int i = 0; i < KEPT; ++i) dCw[(warp * K + t) * NPW + sub * NPT + pm + i] = w[i];
                     }
-                    if (sub == 0) {
-                        dua[c * FS + t] = duacc;
-                        dda[c * FS + t] = ddacc;
+                    if (sub == 0) yv[c * FS + t] = ysum;
+                }
+            }
+
+            // ---- pass B: reverse over sub-blocks ---------------------------------
+            for (int sb = ((FULL ? K : len) - 1) / TS; sb >= 0; --sb) {
+                const int tb = sb * TS;
+                const int nb = FULL ? TS : min(TS, len - tb);
+                float2 xh[TS][NH], ah[TS][NH];
+    #pragma unroll
+                for (int j = 0; j < NH; ++j) x2[j] = sck[(sb * NH + j) * kThreads + tid];
+    #pragma unroll
+                for (int jj = 0; jj < TS; ++jj) {
+                    if (FULL || jj < nb) {
+                        const float2 v = vr[tb + jj];
+                        const float dl = v.x * kLog2e;
+                        const float2 dl2 = make_float2(dl, dl), du2 = make_float2(v.y, v.y);
+                        const float4* B4 = reinterpret_cast<const float4*>(Bp + (tb + jj) * NP);
+    #pragma unroll
+                        for (int qq = 0; qq < NPT / 4; ++qq) {
+                            const float4 bq = B4[qq ^ qx];
+                            const float2 a0 = __fmul2_rn(dl2, An2[2 * qq]);
+                            const float2 a1 = __fmul2_rn(dl2, An2[2 * qq + 1]);
+                            const float2 e0 = make_float2(exp2_mufu(a0.x), exp2_mufu(a0.y));
+                            const float2 e1 = make_float2(exp2_mufu(a1.x), exp2_mufu(a1.y));
+                            ah[jj][2 * qq] = e0;
+                            ah[jj][2 * qq + 1] = e1;
+                            xh[jj][2 * qq] = x2[2 * qq];
+                            xh[jj][2 * qq + 1] = x2[2 * qq + 1];
+                            x2[2 * qq] = __ffma2_rn(e0, x2[2 * qq], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
+                            x2[2 * qq + 1] = __ffma2_rn(e1, x2[2 * qq + 1], __fmul2_rn(du2, make_float2(bq.z, bq.w)));
+                        }
+                    }
+                }
+    #pragma unroll
+                for (int jj = TS - 1; jj >= 0; --jj) {
+                    if (FULL || jj < nb) {
+                        const int t = tb + jj;
+                        const float2 v = vr[t];
+                        const float gv = gr[t];
+                        const float2 g2 = make_float2(gv, gv), dv2 = make_float2(v.x, v.x);
+                        const float2 du2 = make_float2(v.y, v.y);
+                        const float4* B4 = reinterpret_cast<const float4*>(Bp + t * NP);
+                        const float4* C4 = reinterpret_cast<const float4*>(Cp + t * NP);
+                        float2 dua2 = make_float2(0.0f, 0.0f), dda2 = make_float2(0.0f, 0.0f);
+                        float w[NPT];
+    #pragma unroll
+                        for (int qq = 0; qq < NPT / 4; ++qq) {
+                            const float4 bq = B4[qq ^ qx], cq = C4[qq ^ qx];
+                            const float2 bb[2] = {make_float2(bq.x, bq.y), make_float2(bq.z, bq.w)};
+                            const float2 cc2[2] = {make_float2(cq.x, cq.y), make_float2(cq.z, cq.w)};
+    #pragma unroll
+                            for (int r = 0; r < 2; ++r) {
+                                const int j = 2 * qq + r;
+                                const float2 dh = __ffma2_rn(g2, cc2[r], q2[j]);
+                                const float2 tmp = __fmul2_rn(dh, __fmul2_rn(ah[jj][j], xh[jj][j]));
+                                dda2 = __ffma2_rn(tmp, An2[j], dda2);
+                                dA2[j] = __ffma2_rn(tmp, dv2, dA2[j]);
+                                dua2 = __ffma2_rn(dh, bb[r], dua2);
+                                const float2 wv = __fmul2_rn(dh, du2);
+                                w[2 * j] = wv.x;
+                                w[2 * j + 1] = wv.y;
+                                q2[j] = __fmul2_rn(dh, ah[jj][j]);
+                            }
+                        }
+                        const float duacc = sum_low_lanes<LPC>(dua2.x + dua2.y);
+                        const float ddacc = sum_low_lanes<LPC>(dda2.x + dda2.y);
+                        Sc::reduce(w);
+                        if (own) {
+    #pragma unroll
+                            for (int i = 0; i < KEPT; ++i) dBw[(warp * K + t) * NPW + sub * NPT + pm + i] = w[i];
+                        }
+                        if (sub == 0) {
+                            dua[c * FS + t] = duacc;
+                            dda[c * FS + t] = ddacc;
+                        }
                     }
                 }
             }
-        }
+        };
+        if (len == K) chunk_body(std::true_type{});
+        else chunk_body(std::false_type{});
         __syncthreads();
 
         // ---- phase C: element-wise gradients, coalesced stores ---------------
