@@ -129,6 +129,25 @@ __device__ __forceinline__ float ld_dt(const Args& a, int64_t i) {
 __device__ __forceinline__ void report(int code) { atomicCAS(&g_kernel_error, 0, code); }
 
 // ------------------------------------------------------------ block helpers --
+// Barrier over the whole CTA (NB = 0) or over the first NB threads only (named
+// barrier 1), for kernels whose compute warps run beside an MMA-issuing warp.
+template <int NB>
+__device__ __forceinline__ void gsync() {
+    if (NB) asm volatile("bar.sync 1, %0;" :: "n"(NB) : "memory");
+    else __syncthreads();
+}
+// True on each of the first NB threads iff `v` is true on all of them.
+template <int NB>
+__device__ __forceinline__ bool cg_all(bool v) {
+    uint32_t r;
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.and.pred p, 1, %2, q;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}\n" : "=r"(r) : "r"((uint32_t)v), "n"(NB) : "memory");
+    return r != 0;
+}
+// Warps taking part in a block-level helper.
+template <int NB> constexpr int group_warps() { return (NB ? NB : kThreads) / 32; }
+
+template <int NB = 0>
 __device__ __forceinline__ float block_incl_scan(float v, float* sh) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
@@ -137,12 +156,13 @@ __device__ __forceinline__ float block_incl_scan(float v, float* sh) {
         if (lane >= o) v += u;
     }
     if (lane == 31) sh[w] = v;
-    __syncthreads();
+    gsync<NB>();
     float off = 0.0f;
     for (int i = 0; i < w; ++i) off += sh[i];
-    __syncthreads();
+    gsync<NB>();
     return v + off;
 }
+template <int NB = 0>
 __device__ __forceinline__ float block_suffix_scan(float v, float* sh) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
@@ -151,33 +171,34 @@ __device__ __forceinline__ float block_suffix_scan(float v, float* sh) {
         if (lane + o < 32) v += u;
     }
     if (lane == 0) sh[w] = v;
-    __syncthreads();
+    gsync<NB>();
     float off = 0.0f;
-    for (int i = kThreads / 32 - 1; i > w; --i) off += sh[i];
-    __syncthreads();
+    for (int i = group_warps<NB>() - 1; i > w; --i) off += sh[i];
+    gsync<NB>();
     return v + off;
 }
 // Sum over the CTA; every thread gets the total (fixed order).
+template <int NB = 0>
 __device__ __forceinline__ float block_sum(float v, float* sh) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
-    __syncthreads();
+    gsync<NB>();
     float s = 0.0f;
-    for (int i = 0; i < kThreads / 32; ++i) s += sh[i];
-    __syncthreads();
+    for (int i = 0; i < group_warps<NB>(); ++i) s += sh[i];
+    gsync<NB>();
     return s;
 }
 
 // Rows [0, Q) of a global row-major matrix (16-byte chunks) into a tile, rows
 // at or beyond `valid` zero-filled.  Lanes 0-7 take eight rows of one chunk so
 // that each quarter-warp writes 128 contiguous bytes of shared memory.
-template <int W, typename T>
+template <int W, typename T, int NT = kThreads>
 __device__ __forceinline__ void load_rows(unsigned char* tile, const T* base, int64_t row_stride, int valid) {
     const uint32_t st = tc::smem_u32(tile);
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     constexpr int CPW = W / 4;
-    for (int wi = wid; wi < (Q / 8) * CPW; wi += kThreads / 32) {
+    for (int wi = wid; wi < (Q / 8) * CPW; wi += NT / 32) {
         const int r = (wi / CPW) * 8 + (lane & 7);
         const int ch = (wi % CPW) * 4 + (lane >> 3);
         const bool v = r < valid;
@@ -186,9 +207,10 @@ __device__ __forceinline__ void load_rows(unsigned char* tile, const T* base, in
     }
 }
 // A 16 KB operand image copied linearly.
+template <int NT = kThreads>
 __device__ __forceinline__ void load_image(unsigned char* tile, const unsigned char* src) {
     const uint32_t st = tc::smem_u32(tile);
-    for (int i = threadIdx.x; i < (int)(kTileH / 16); i += kThreads) tc::cp_async16(st + i * 16, src + i * 16);
+    for (int i = threadIdx.x; i < (int)(kTileH / 16); i += NT) tc::cp_async16(st + i * 16, src + i * 16);
 }
 
 // Per-chunk step quantities of one head, thread s owning position s.
@@ -203,12 +225,13 @@ __device__ __forceinline__ float raw_dt(const Args& a, int64_t b, int64_t h, int
     const int64_t t = c * Q + threadIdx.x;
     return t < a.length ? ld_dt(a, (b * a.length + t) * a.nheads + h) + bias : 0.0f;
 }
+template <int NB = 0>
 __device__ __forceinline__ Steps steps_of(const Args& a, float raw, int64_t c, float Ah, float* scan_sh) {
     Steps s;
-    const bool valid = c * Q + threadIdx.x < a.length;
+    const bool valid = threadIdx.x < Q && c * Q + threadIdx.x < a.length;
     s.raw = raw;
     s.d = valid ? ((a.flags & SSM_SOFTPLUS) ? softplus_f(raw) : raw) : 0.0f;
-    s.cd = block_incl_scan(s.d, scan_sh);
+    s.cd = block_incl_scan<NB>(s.d, scan_sh);
     s.cs = Ah * s.cd;
     return s;
 }
@@ -220,6 +243,7 @@ struct HeadSh {
     float raw[kHeadsSh][Q + 1];     // dt + bias (padded row: conflict-free writes)
     float A[kHeadsSh], D[kHeadsSh];
 };
+template <int NT = kThreads>
 __device__ __forceinline__ void stage_heads(const Args& a, HeadSh& hs, int64_t b, int64_t g, int64_t c,
                                             int64_t hh0, int n) {
     const int64_t h0 = g * a.hpg + hh0;
@@ -228,7 +252,7 @@ __device__ __forceinline__ void stage_heads(const Args& a, HeadSh& hs, int64_t b
         hs.A[threadIdx.x] = a.A[h0 + threadIdx.x];
         hs.D[threadIdx.x] = ((a.flags & SSM_HAS_D) && !(a.flags & SSM_D_PER_HEAD)) ? a.D[h0 + threadIdx.x] : 0.0f;
     }
-    for (int i = threadIdx.x; i < n * Q; i += kThreads) {
+    for (int i = threadIdx.x; i < n * Q; i += NT) {
         const int pos = i / n, k = i % n;     // consecutive threads: consecutive heads of one position
         const int64_t t = c * Q + pos;
         float v = 0.0f;
@@ -236,8 +260,9 @@ __device__ __forceinline__ void stage_heads(const Args& a, HeadSh& hs, int64_t b
         hs.raw[k][pos] = v;
     }
 }
+template <int NB = 0>
 __device__ __forceinline__ Steps staged_steps(const Args& a, const HeadSh& hs, int k, int64_t c, float* scan_sh) {
-    return steps_of(a, hs.raw[k][threadIdx.x], c, hs.A[k], scan_sh);
+    return steps_of<NB>(a, threadIdx.x < Q ? hs.raw[k][threadIdx.x] : 0.0f, c, hs.A[k], scan_sh);
 }
 
 // ====================================================================== F1 ==
@@ -324,7 +349,7 @@ __global__ void __launch_bounds__(kThreads) states_kernel(const Args a) {
             for (int j = 0; j < P / 16; ++j) {
                 float v[16];
                 tc::tmem_ld16(row_addr + j * 16, v);
-                tc::tmem_wait_ld();
+                tc::tmem_wait_ld(v);
                 *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j, WH)) = pack8<T>(v);
                 *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j + 1, WH)) = pack8<T>(v + 8);
 #pragma unroll
@@ -362,7 +387,7 @@ __global__ void __launch_bounds__(kThreads) states_kernel(const Args a) {
         for (int j = 0; j < P / 16; ++j) {
             float v[16];
             tc::tmem_ld16(row_addr + j * 16, v);
-            tc::tmem_wait_ld();
+            tc::tmem_wait_ld(v);
 #pragma unroll
             for (int k = 0; k < 16; ++k) a.final_state[((b * H + h) * P + j * 16 + k) * N + tid] = v[k];
         }
@@ -382,13 +407,16 @@ struct MaskSh {
     float d[Q];
     float cf[Q];
 };
+template <int NB = 0>
 __device__ __forceinline__ void mask_factors(MaskSh& m, const Steps& st) {
     const int s = threadIdx.x;
-    m.cs2[s] = st.cs * kLog2e;
-    m.d[s] = st.d;
-    __syncthreads();
-    m.cf[s] = exp2_mufu(m.cs2[s | 15] - m.cs2[s]);
-    __syncthreads();
+    if (s < Q) {
+        m.cs2[s] = st.cs * kLog2e;
+        m.d[s] = st.d;
+    }
+    gsync<NB>();
+    if (s < Q) m.cf[s] = exp2_mufu(m.cs2[s | 15] - m.cs2[s]);
+    gsync<NB>();
 }
 
 // ====================================================================== F2 ==
@@ -471,7 +499,7 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const Args a) {
                 if (16 * j <= 32 * warp + 31) {          // warp-uniform: tcgen05.ld is .sync.aligned
                     float v[16];
                     tc::tmem_ld16(tm + lane_off + 16 * j, v);
-                    tc::tmem_wait_ld();
+                    tc::tmem_wait_ld(v);
                     if (16 * j > l) {
                         // whole block above the diagonal for this row: zeros
                     } else if (16 * j + 15 < l) {
@@ -522,7 +550,8 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const Args a) {
                 float yi[16], ye[16];
                 tc::tmem_ld16(tm + lane_off + 128 + 16 * j, yi);
                 tc::tmem_ld16(tm + lane_off + 192 + 16 * j, ye);
-                tc::tmem_wait_ld();
+                tc::tmem_wait_ld(yi);
+                tc::tmem_pin(ye);
                 if (!live) continue;
                 float xv[16];
                 Pk<T>::unpack(*reinterpret_cast<const uint4*>(sX + tc::tile_off(l, 2 * j, WX)), xv);
@@ -656,7 +685,7 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const Args a) {
             for (int j = 0; j < P / 16; ++j) {
                 float v[16], hv[16];
                 tc::tmem_ld16(row_addr + j * 16, v);
-                tc::tmem_wait_ld();
+                tc::tmem_wait_ld(v);
                 *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j, WH)) = pack8<T>(v);
                 *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j + 1, WH)) = pack8<T>(v + 8);
                 Pk<T>::unpack(*reinterpret_cast<const uint4*>(sH + tc::tile_off(tid, 2 * j, WH)), hv);
@@ -697,7 +726,7 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const Args a) {
             for (int j = 0; j < P / 16; ++j) {
                 float ye[16], yv[16];
                 tc::tmem_ld16(row_addr + 64 + 16 * j, ye);
-                tc::tmem_wait_ld();
+                tc::tmem_wait_ld(ye);
                 Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(l, 2 * j, WX)), yv);
                 Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(l, 2 * j + 1, WX)), yv + 8);
 #pragma unroll
@@ -713,7 +742,7 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const Args a) {
         for (int j = 0; j < P / 16; ++j) {
             float v[16];
             tc::tmem_ld16(row_addr + j * 16, v);
-            tc::tmem_wait_ld();
+            tc::tmem_wait_ld(v);
 #pragma unroll
             for (int k = 0; k < 16; ++k) a.dinit[((b * H + h) * P + j * 16 + k) * N + tid] = v[k];
         }
@@ -742,18 +771,37 @@ __device__ __forceinline__ float warp_colsum16(float* v) {
 }
 
 // ====================================================================== B2 ==
-// One CTA per (b, group, chunk).  TMEM: G [0,128), dB [128,256), dC [256,384),
-// scratch [384,512): dY X^T, then Mh^T dY [384,448) and B dH^T [448,512).
+// One CTA per (b, group, chunk), warp-specialised: eight compute warps -- two
+// per TMEM lane quadrant, splitting each row's columns -- and one warp that
+// issues every tensor-core instruction.  Threads 0..127 also own one chunk
+// position each for the per-position scalar work.
+// TMEM: G [0,128), dB [128,256), dC [256,384), scratch S [384,512): dY X^T,
+// then Mh^T dY [384,448) and B dH^T [448,512).
+//
+// Hand-offs (mbarriers, one phase per head):
+//   bc   compute -> MMA   B and C tiles are in shared memory (once)
+//   in   compute -> MMA   this head's tiles are ready and S is free
+//   m1   MMA -> compute   dY X^T (and, for the first head, G) is in TMEM
+//   mask compute -> MMA   Mh, dG, exp(cs) dy, w o x written; S read
+//   m2   MMA -> compute   the eight GEMMs of the head are done
+// While the eight GEMMs run, the compute warps fetch the epilogue's global
+// inputs and compute the next head's step quantities; right after reading S
+// they start the next head's tile loads, which then overlap the epilogue.
+constexpr int kGC = 256;                       // compute threads
+constexpr int kGradThreads = kGC + 32;
+
 struct GradSh {
     MaskSh m;
     HeadSh hs;
-    float col[kThreads / 32][Q];
-    float scan[4];
-    float T;
+    float col[4][Q];          // column sums of E per TMEM quadrant
+    float rowp[2][Q];         // row sums of E d, per column half
+    float vp[2][Q];           // <x_s, Z_s> per column half
+    float scan[8];
+    float T[2];
 };
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) grads_kernel(const Args a) {
+__global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const Args a) {
     extern __shared__ __align__(128) unsigned char sm[];
     unsigned char* sB = sm;
     unsigned char* sC = sB + kTileB;
@@ -765,10 +813,14 @@ __global__ void __launch_bounds__(kThreads, 1) grads_kernel(const Args a) {
     unsigned char* sH = sXW + kTileX;           // H_c^T
     unsigned char* sD = sH + kTileH;            // dH_{c+1}^T
     __shared__ GradSh sh;
-    __shared__ __align__(8) uint64_t mbar;
+    __shared__ __align__(8) uint64_t bars[5];
     __shared__ uint32_t tbase;
+    enum { kBc = 0, kIn = 1, kM1 = 2, kMask = 3, kM2 = 4 };
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool mma_warp = warp == kGC / 32;
+    const int q = warp & 3, hf = (warp >> 2) & 1;      // TMEM quadrant, column half
+    const int r = q * 32 + lane;                       // TMEM row / tile row of this thread
     const int64_t c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int64_t L = a.length, H = a.nheads, G = a.ngroups;
     const int64_t t0 = c * Q;
@@ -779,303 +831,357 @@ __global__ void __launch_bounds__(kThreads, 1) grads_kernel(const Args a) {
     T* dxg = reinterpret_cast<T*>(a.dx);
     const bool has_z = a.flags & SSM_HAS_Z, has_d = a.flags & SSM_HAS_D;
     const bool d_per_head = a.flags & SSM_D_PER_HEAD;
+    const uint32_t bar0 = tc::smem_u32(&bars[0]);
+    auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
 
-    if (warp == 0) tc::tmem_alloc(tc::smem_u32(&tbase), 512);
+    auto load_head = [&](int64_t hh) {            // compute threads only
+        const int64_t h = g * a.hpg + hh;
+        const int64_t bhc = (b * H + h) * a.nc + c;
+        load_rows<WX, T, kGC>(sX, xg + ((b * L + t0) * H + h) * P, H * P, valid);
+        load_rows<WX, T, kGC>(sY, dyg + ((b * L + t0) * H + h) * P, H * P, valid);
+        load_image<kGC>(sH, a.Ht + ((size_t)(b * H + h) * a.nc + c) * kTileH);
+        load_image<kGC>(sD, a.dHt + (size_t)bhc * kTileH);
+        tc::cp_async_commit();
+    };
+
+    if (mma_warp) tc::tmem_alloc(tc::smem_u32(&tbase), 512);
     if (tid == 0) {
-        tc::mbar_init(tc::smem_u32(&mbar), 1);
+        tc::mbar_init(bar(kBc), kGC);
+        tc::mbar_init(bar(kIn), kGC);
+        tc::mbar_init(bar(kM1), 1);
+        tc::mbar_init(bar(kMask), kGC);
+        tc::mbar_init(bar(kM2), 1);
         tc::fence_mbar_init();
     }
-    load_rows<WB>(sC, reinterpret_cast<const T*>(a.C) + ((b * L + t0) * G + g) * N, G * N, valid);
-    load_rows<WB>(sB, reinterpret_cast<const T*>(a.B) + ((b * L + t0) * G + g) * N, G * N, valid);
-    tc::cp_async_commit();
-    tc::cp_async_wait<0>();
-    tc::fence_async_smem();
+    if (!mma_warp) {
+        load_rows<WB, T, kGC>(sC, reinterpret_cast<const T*>(a.C) + ((b * L + t0) * G + g) * N, G * N, valid);
+        load_rows<WB, T, kGC>(sB, reinterpret_cast<const T*>(a.B) + ((b * L + t0) * G + g) * N, G * N, valid);
+        tc::cp_async_commit();
+        load_head(0);
+    }
     tc::fence_before();
     __syncthreads();
     tc::fence_after();
     const uint32_t tm = tbase;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     const uint32_t tG = tm, tdB = tm + 128, tdC = tm + 256, tS = tm + 384;
     const uint32_t aB = tc::smem_u32(sB), aC = tc::smem_u32(sC), aM = tc::smem_u32(sM), aG = tc::smem_u32(sG);
     const uint32_t aX = tc::smem_u32(sX), aY = tc::smem_u32(sY), aXW = tc::smem_u32(sXW);
     const uint32_t aH = tc::smem_u32(sH), aD = tc::smem_u32(sD);
     constexpr uint32_t fmt = Pk<T>::kFmt;
-    if (tid == 0) {
-        const uint32_t idg = tc::idesc_f16(fmt, 128, 128, false, false);
-#pragma unroll
-        for (int ks = 0; ks < N / 16; ++ks)
-            tc::mma_f16(tG, tc::desc_k(aC, WB, 2 * ks), tc::desc_k(aB, WB, 2 * ks), idg, ks > 0);
-        tc::commit(tc::smem_u32(&mbar));
-    }
-    uint32_t phase = 0;
-    bool ok = tc::mbar_wait(tc::smem_u32(&mbar), phase);
-    if (!ok) report(41);
-    phase ^= 1;
-    tc::fence_after();
-    ok = __syncthreads_and(ok);
+    bool ok = true;
 
-    for (int64_t hh = 0; hh < a.hpg && ok; ++hh) {
-        const int64_t h = g * a.hpg + hh;
-        const int64_t bhc = (b * H + h) * a.nc + c;
-        load_rows<WX>(sX, xg + ((b * L + t0) * H + h) * P, H * P, valid);
-        load_rows<WX>(sY, dyg + ((b * L + t0) * H + h) * P, H * P, valid);
-        load_image(sH, a.Ht + ((size_t)(b * H + h) * a.nc + c) * kTileH);
-        load_image(sD, a.dHt + (size_t)bhc * kTileH);
-        tc::cp_async_commit();
-        const int hk = (int)(hh % kHeadsSh);
-        if (hk == 0) {
-            stage_heads(a, sh.hs, b, g, c, hh, (int)min64(kHeadsSh, a.hpg - hh));
-            __syncthreads();
-        }
-        const float Ah = sh.hs.A[hk];
-        const Steps st = staged_steps(a, sh.hs, hk, c, sh.scan);
-        if (tid == Q - 1) sh.T = st.cs;
-        mask_factors(sh.m, st);
-        const float Tc = sh.T;
-        const int r = tid;   // the row this thread owns (l or s)
-        const int64_t grow = ((b * L + t0 + r) * H + h) * P;
-        tc::cp_async_wait<0>();
-        __syncthreads();
-        // gate dy in place
-        if (has_z && r < valid) {
-            for (int j = 0; j < WX; ++j) {
-                float f[8], zv[8];
-                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(r, j, WX)), f);
-                Pk<T>::unpack(*reinterpret_cast<const uint4*>(zg + grow + 8 * j), zv);
+    if (mma_warp) {
+        // ------------------------------------------------------- MMA warp --
+        // lane 0 polls, the warp follows its outcome (uniform control flow)
+        auto wait_warp = [&](int i, uint32_t par) {
+            bool w = true;
+            if (lane == 0) w = tc::mbar_wait(bar(i), par);
+            return __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
+        };
+        ok = wait_warp(kBc, 0);
+        tc::fence_after();
+        if (ok && lane == 0) {
+            const uint32_t idg = tc::idesc_f16(fmt, 128, 128, false, false);
 #pragma unroll
-                for (int k = 0; k < 8; ++k) f[k] *= zv[k] * sigmoid_f(zv[k]);
-                *reinterpret_cast<uint4*>(sY + tc::tile_off(r, j, WX)) = pack8<T>(f);
-            }
+            for (int ks = 0; ks < N / 16; ++ks)
+                tc::mma_f16(tG, tc::desc_k(aC, WB, 2 * ks), tc::desc_k(aB, WB, 2 * ks), idg, ks > 0);
         }
-        tc::fence_async_smem();
-        __syncthreads();
-        if (tid == 0) {
+        __syncwarp();
+        for (int64_t hh = 0; hh < a.hpg && ok; ++hh) {
+            const uint32_t par = (uint32_t)(hh & 1);
+            if (!wait_warp(kIn, par)) { ok = false; break; }
             tc::fence_after();
-            const uint32_t idm = tc::idesc_f16(fmt, 128, 128, false, false);
+            if (lane == 0) {
+                const uint32_t idm = tc::idesc_f16(fmt, 128, 128, false, false);
 #pragma unroll
-            for (int ks = 0; ks < P / 16; ++ks)
-                tc::mma_f16(tS, tc::desc_k(aY, WX, 2 * ks), tc::desc_k(aX, WX, 2 * ks), idm, ks > 0);
-            tc::commit(tc::smem_u32(&mbar));
-        }
-        // while dY X^T runs: w o x, and the D gradient partial <dy_r, x_r>
-        float dD_head = 0.0f;
-        {
-            const float w = exp2_mufu((Tc - st.cs) * kLog2e) * st.d;
-            for (int j = 0; j < WX; ++j) {
-                float xv[8], yv[8];
-                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sX + tc::tile_off(r, j, WX)), xv);
-                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(r, j, WX)), yv);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    dD_head = fmaf(xv[k], yv[k], dD_head);
-                    xv[k] *= w;
-                }
-                *reinterpret_cast<uint4*>(sXW + tc::tile_off(r, j, WX)) = pack8<T>(xv);
+                for (int ks = 0; ks < P / 16; ++ks)
+                    tc::mma_f16(tS, tc::desc_k(aY, WX, 2 * ks), tc::desc_k(aX, WX, 2 * ks), idm, ks > 0);
+                tc::commit(bar(kM1));
             }
+            __syncwarp();
+            if (!wait_warp(kMask, par)) { ok = false; break; }
+            tc::fence_after();
+            if (lane == 0) {
+                const uint32_t i_mn_mn64 = tc::idesc_f16(fmt, 128, P, true, true);
+                const uint32_t i_k_mn64 = tc::idesc_f16(fmt, 128, P, false, true);
+                const uint32_t i_k_mn = tc::idesc_f16(fmt, 128, 128, false, true);
+                const uint32_t i_k_k = tc::idesc_f16(fmt, 128, 128, false, false);
+                const uint32_t i_mn_mn = tc::idesc_f16(fmt, 128, 128, true, true);
+                const uint32_t first = hh == 0 ? 0u : 1u;
+#pragma unroll
+                for (int ks = 0; ks < Q / 16; ++ks)   // Mh^T dY
+                    tc::mma_f16(tS, tc::desc_mn(aM, WB, 16 * ks), tc::desc_mn(aY, WX, 16 * ks), i_mn_mn64, ks > 0);
+#pragma unroll
+                for (int ks = 0; ks < N / 16; ++ks)   // B dH^T
+                    tc::mma_f16(tS + 64, tc::desc_k(aB, WB, 2 * ks), tc::desc_mn(aD, WH, 16 * ks), i_k_mn64, ks > 0);
+#pragma unroll
+                for (int ks = 0; ks < Q / 16; ++ks)   // dC += dG B
+                    tc::mma_f16(tdC, tc::desc_k(aG, WB, 2 * ks), tc::desc_mn(aB, WB, 16 * ks), i_k_mn, ks > 0 ? 1u : first);
+#pragma unroll
+                for (int ks = 0; ks < P / 16; ++ks)   // dC += (exp(cs) dy) H
+                    tc::mma_f16(tdC, tc::desc_k(aX, WX, 2 * ks), tc::desc_k(aH, WH, 2 * ks), i_k_k, 1u);
+#pragma unroll
+                for (int ks = 0; ks < Q / 16; ++ks)   // dB += dG^T C
+                    tc::mma_f16(tdB, tc::desc_mn(aG, WB, 16 * ks), tc::desc_mn(aC, WB, 16 * ks), i_mn_mn, ks > 0 ? 1u : first);
+#pragma unroll
+                for (int ks = 0; ks < P / 16; ++ks)   // dB += (w o x) dH
+                    tc::mma_f16(tdB, tc::desc_k(aXW, WX, 2 * ks), tc::desc_k(aD, WH, 2 * ks), i_k_k, 1u);
+                tc::commit(bar(kM2));
+            }
+            __syncwarp();
         }
-        if (has_d && d_per_head) {
-            // per (head, p): thread p < P sums over the rows (x and dy still in place)
-            if (tid < P) {
+        if (!ok && lane == 0) report(44);
+    } else {
+        // --------------------------------------------------- compute warps --
+        const bool pos_thread = tid < Q;           // owns chunk position s = tid
+        tc::cp_async_wait<1>();                    // B and C
+        tc::fence_async_smem();
+        tc::mbar_arrive(bar(kBc));
+        stage_heads<kGC>(a, sh.hs, b, g, c, 0, (int)min64(kHeadsSh, a.hpg));
+        gsync<kGC>();
+        Steps st = staged_steps<kGC>(a, sh.hs, 0, c, sh.scan);
+        if (tid == Q - 1) sh.T[0] = st.cs;
+        mask_factors<kGC>(sh.m, st);
+        const int j0 = hf * (WX / 2);              // this thread's half of an X-like row (chunks)
+        for (int64_t hh = 0; hh < a.hpg; ++hh) {
+            const uint32_t par = (uint32_t)(hh & 1);
+            const int64_t h = g * a.hpg + hh;
+            const int64_t bhc = (b * H + h) * a.nc + c;
+            const int hk = (int)(hh % kHeadsSh);
+            const float Ah = sh.hs.A[hk];
+            const float Dh = sh.hs.D[hk];
+            const float Tc = sh.T[hh & 1];
+            const int64_t grow = ((b * L + t0 + r) * H + h) * P;   // row r of x / dy / dx
+            tc::cp_async_wait<0>();
+            gsync<kGC>();
+            if (has_z && r < valid) {               // gate dy in place, own row half
+                for (int j = j0; j < j0 + WX / 2; ++j) {
+                    float f[8], zv[8];
+                    Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(r, j, WX)), f);
+                    Pk<T>::unpack(*reinterpret_cast<const uint4*>(zg + grow + 8 * j), zv);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) f[k] *= zv[k] * sigmoid_f(zv[k]);
+                    *reinterpret_cast<uint4*>(sY + tc::tile_off(r, j, WX)) = pack8<T>(f);
+                }
+            }
+            tc::fence_async_smem();
+            tc::mbar_arrive(bar(kIn));
+            if (has_z) gsync<kGC>();                // every gated row is in place before it is read
+            // while dY X^T runs: w o x, and the D gradient partial <dy, x>
+            float dD_head = 0.0f;
+            {
+                const float w = exp2_mufu(Tc * kLog2e - sh.m.cs2[r]) * sh.m.d[r];   // exp(T - cs_r) d_r
+                for (int j = j0; j < j0 + WX / 2; ++j) {
+                    float xv[8], yv[8];
+                    Pk<T>::unpack(*reinterpret_cast<const uint4*>(sX + tc::tile_off(r, j, WX)), xv);
+                    Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(r, j, WX)), yv);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        dD_head = fmaf(xv[k], yv[k], dD_head);
+                        xv[k] *= w;
+                    }
+                    *reinterpret_cast<uint4*>(sXW + tc::tile_off(r, j, WX)) = pack8<T>(xv);
+                }
+            }
+            if (has_d && d_per_head && tid < P) {
                 const int p = tid;
-                float s = 0.0f;
+                float s2 = 0.0f;
                 for (int rr = 0; rr < Q; ++rr) {
                     const uint32_t off = tc::tile_off(rr, p >> 3, WX) + (p & 7) * 2;
-                    s = fmaf(ldf(reinterpret_cast<const T*>(sX + off)), ldf(reinterpret_cast<const T*>(sY + off)), s);
+                    s2 = fmaf(ldf(reinterpret_cast<const T*>(sX + off)), ldf(reinterpret_cast<const T*>(sY + off)), s2);
                 }
-                a.dD_part[bhc * P + p] = s;
+                a.dD_part[bhc * P + p] = s2;
             }
-        }
-        if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(42); ok = false; }
-        phase ^= 1;
-        tc::fence_after();
-        ok = __syncthreads_and(ok);   // also: every thread is done reading sX before it is overwritten
-        if (!ok) break;
-        // mask pass, row l = r
-        float rowsum = 0.0f;
-        {
-            const int l = r;
-            const float csl = sh.m.cs2[l];
-            for (int j = 0; j < Q / 16; ++j) {
-                uint4 m0 = make_uint4(0, 0, 0, 0), m1 = m0, g0 = m0, g1 = m0;
-                float E[16];
-                if (16 * j <= 32 * warp + 31) {           // some row of this warp reaches block j
-                    float gv[16], dm[16];
-                    tc::tmem_ld16(tG + lane_off + 16 * j, gv);
-                    tc::tmem_ld16(tS + lane_off + 16 * j, dm);
-                    tc::tmem_wait_ld();
-                    float e[16];
-                    if (16 * j + 15 < l) {
-                        const float rf = exp2_mufu(csl - sh.m.cs2[16 * j + 15]);
+            if (!tc::mbar_wait(bar(kM1), par)) { report(42); ok = false; }
+            tc::fence_after();
+            ok = cg_all<kGC>(ok);                    // also: every thread is done reading sX
+            if (!ok) break;
+            // mask pass, row l = r: blocks of parity hf, up to the last one a row of this quadrant reaches
+            {
+                const int l = r;
+                const float csl = sh.m.cs2[l];
+                const int nj = min(Q / 16, 2 * q + 2);
+                float rowsum = 0.0f;
+                for (int j = hf; j < Q / 16; j += 2) {
+                    uint4 m0 = make_uint4(0, 0, 0, 0), m1 = m0, g0 = m0, g1 = m0;
+                    if (j < nj) {                              // warp-uniform
+                        float gv[16], dm[16], E[16];
+                        tc::tmem_ld16(tG + lane_off + 16 * j, gv);
+                        tc::tmem_ld16(tS + lane_off + 16 * j, dm);
+                        tc::tmem_wait_ld(gv);
+                        tc::tmem_pin(dm);
+                        float e[16];
+                        if (16 * j + 15 < l) {
+                            const float rf = exp2_mufu(csl - sh.m.cs2[16 * j + 15]);
 #pragma unroll
-                        for (int k = 0; k < 16; ++k) e[k] = rf * sh.m.cf[16 * j + k];
-                    } else {
+                            for (int k = 0; k < 16; ++k) e[k] = rf * sh.m.cf[16 * j + k];
+                        } else {
+#pragma unroll
+                            for (int k = 0; k < 16; ++k) {
+                                const int s = 16 * j + k;
+                                e[k] = s <= l ? exp2_mufu(csl - sh.m.cs2[s]) : 0.0f;
+                            }
+                        }
+                        float mh[16], dg[16];
 #pragma unroll
                         for (int k = 0; k < 16; ++k) {
-                            const int s = 16 * j + k;
-                            e[k] = s <= l ? exp2_mufu(csl - sh.m.cs2[s]) : 0.0f;
+                            const float ed = e[k] * sh.m.d[16 * j + k];
+                            const float gd = gv[k] * dm[k];
+                            mh[k] = gv[k] * ed;
+                            dg[k] = dm[k] * ed;
+                            E[k] = gd * e[k];
+                            rowsum = fmaf(gd, ed, rowsum);
                         }
+                        m0 = pack8<T>(mh); m1 = pack8<T>(mh + 8);
+                        g0 = pack8<T>(dg); g1 = pack8<T>(dg + 8);
+                        const float cs_sum = warp_colsum16(E);
+                        if (!(lane & 1)) {
+                            const int k = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 +
+                                          ((lane >> 1) & 1);
+                            sh.col[q][16 * j + k] = cs_sum;
+                        }
+                    } else if (lane < 16) {
+                        sh.col[q][16 * j + lane] = 0.0f;
                     }
-                    float mh[16], dg[16];
+                    *reinterpret_cast<uint4*>(sM + tc::tile_off(l, 2 * j, WB)) = m0;
+                    *reinterpret_cast<uint4*>(sM + tc::tile_off(l, 2 * j + 1, WB)) = m1;
+                    *reinterpret_cast<uint4*>(sG + tc::tile_off(l, 2 * j, WB)) = g0;
+                    *reinterpret_cast<uint4*>(sG + tc::tile_off(l, 2 * j + 1, WB)) = g1;
+                }
+                sh.rowp[hf][l] = rowsum;
+                // exp(cs_l) dy_l into sX (row l, this thread's half)
+                const float el = exp2_mufu(csl);
+                for (int j = j0; j < j0 + WX / 2; ++j) {
+                    float f[8];
+                    Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(l, j, WX)), f);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) f[k] *= el;
+                    *reinterpret_cast<uint4*>(sX + tc::tile_off(l, j, WX)) = pack8<T>(f);
+                }
+            }
+            tc::fence_async_smem();
+            tc::fence_before();
+            tc::mbar_arrive(bar(kMask));
+            // ---- while the eight GEMMs run ----
+            uint4 xr[WX / 2];
+            {
+                const bool live = r < valid;
+#pragma unroll
+                for (int j = 0; j < WX / 2; ++j)
+                    xr[j] = live ? *reinterpret_cast<const uint4*>(xg + grow + 8 * (j0 + j)) : make_uint4(0, 0, 0, 0);
+            }
+            const float dci = pos_thread ? a.dcs_inter[bhc * Q + tid] : 0.0f;
+            const float dTc = tid == Q - 1 ? a.dT[bhc] : 0.0f;
+            gsync<kGC>();                            // sh.col, sh.rowp complete
+            float colsum = 0.0f, rowsum = 0.0f;
+            if (pos_thread) {
+#pragma unroll
+                for (int w = 0; w < 4; ++w) colsum += sh.col[w][tid];
+                rowsum = sh.rowp[0][tid] + sh.rowp[1][tid];
+            }
+            const float dD_sum = block_sum<kGC>(dD_head, sh.scan);
+            Steps st_next = st;
+            if (hh + 1 < a.hpg) {
+                const int hk1 = (int)((hh + 1) % kHeadsSh);
+                if (hk1 == 0) {
+                    stage_heads<kGC>(a, sh.hs, b, g, c, hh + 1, (int)min64(kHeadsSh, a.hpg - hh - 1));
+                    gsync<kGC>();
+                }
+                st_next = staged_steps<kGC>(a, sh.hs, hk1, c, sh.scan);
+                if (tid == Q - 1) sh.T[(hh + 1) & 1] = st_next.cs;
+            }
+            if (!tc::mbar_wait(bar(kM2), par)) { report(43); ok = false; }
+            tc::fence_after();
+            ok = cg_all<kGC>(ok);
+            if (!ok) break;
+            // epilogue, row s = r, columns [32 hf, 32 hf + 32): the TMEM part first
+            {
+                const int s = r;
+                const float d_s = sh.m.d[s];
+                const float eTs = exp2_mufu(Tc * kLog2e - sh.m.cs2[s]);
+                float vpart = 0.0f;
+#pragma unroll
+                for (int jj = 0; jj < 2; ++jj) {
+                    const int col = 32 * hf + 16 * jj;
+                    float di[16], zz[16], xv[16], yv[16];
+                    tc::tmem_ld16(tS + lane_off + col, di);
+                    tc::tmem_ld16(tS + lane_off + 64 + col, zz);
+                    tc::tmem_wait_ld(di);
+                    tc::tmem_pin(zz);
+                    Pk<T>::unpack(xr[2 * jj], xv);
+                    Pk<T>::unpack(xr[2 * jj + 1], xv + 8);
+                    Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(s, col / 8, WX)), yv);
+                    Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(s, col / 8 + 1, WX)), yv + 8);
+                    float dxv[16];
 #pragma unroll
                     for (int k = 0; k < 16; ++k) {
-                        const float ed = e[k] * sh.m.d[16 * j + k];
-                        const float gd = gv[k] * dm[k];
-                        mh[k] = gv[k] * ed;
-                        dg[k] = dm[k] * ed;
-                        E[k] = gd * e[k];
-                        rowsum = fmaf(gd, ed, rowsum);
+                        vpart = fmaf(xv[k], zz[k], vpart);
+                        const float Dk = has_d ? (d_per_head ? a.D[h * P + col + k] : Dh) : 0.0f;
+                        dxv[k] = fmaf(d_s * eTs, zz[k], di[k]) + Dk * yv[k];   // Mh already carries d_s
                     }
-                    m0 = pack8<T>(mh); m1 = pack8<T>(mh + 8);
-                    g0 = pack8<T>(dg); g1 = pack8<T>(dg + 8);
-                    const float cs_sum = warp_colsum16(E);
-                    if (!(lane & 1)) {
-                        const int k = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 +
-                                      ((lane >> 1) & 1);
-                        sh.col[warp][16 * j + k] = cs_sum;
+                    if (s < valid) {
+                        *reinterpret_cast<uint4*>(dxg + grow + col) = pack8<T>(dxv);
+                        *reinterpret_cast<uint4*>(dxg + grow + col + 8) = pack8<T>(dxv + 8);
                     }
-                } else if (lane < 16) {
-                    sh.col[warp][16 * j + lane] = 0.0f;
                 }
-                *reinterpret_cast<uint4*>(sM + tc::tile_off(l, 2 * j, WB)) = m0;
-                *reinterpret_cast<uint4*>(sM + tc::tile_off(l, 2 * j + 1, WB)) = m1;
-                *reinterpret_cast<uint4*>(sG + tc::tile_off(l, 2 * j, WB)) = g0;
-                *reinterpret_cast<uint4*>(sG + tc::tile_off(l, 2 * j + 1, WB)) = g1;
+                sh.vp[hf][s] = vpart * eTs;
             }
-            // exp(cs_l) dy_l into sX (row l only: this thread's own row)
-            const float el = exp2_mufu(csl);
-            for (int j = 0; j < WX; ++j) {
-                float f[8];
-                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(l, j, WX)), f);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) f[k] *= el;
-                *reinterpret_cast<uint4*>(sX + tc::tile_off(l, j, WX)) = pack8<T>(f);
+            tc::fence_before();                      // S read: the next head's dY X^T may overwrite it
+            gsync<kGC>();                            // every thread is done with the tiles; sh.vp complete
+            if (hh + 1 < a.hpg) {
+                load_head(hh + 1);
+                mask_factors<kGC>(sh.m, st_next);    // the scalars below use st, not sh.m
             }
+            float dcs = 0.0f, dd_direct = 0.0f, dv = 0.0f;
+            if (pos_thread) {
+                const float v_s = sh.vp[0][tid] + sh.vp[1][tid];
+                dv = st.d * v_s;
+                dcs = rowsum - st.d * colsum - dv + dci;
+                dd_direct = colsum + v_s;
+            }
+            // d/dT_c = exp(T) <dH_{c+1}, H_c> + sum_s d_s v_s, added at the chunk's last position
+            const float dv_sum = block_sum<kGC>(dv, sh.scan);
+            if (tid == Q - 1) dcs += dTc + dv_sum;
+            const float suffix = block_suffix_scan<kGC>(dcs, sh.scan);
+            const float dd = fmaf(Ah, suffix, dd_direct);
+            const float ddt = (a.flags & SSM_SOFTPLUS) ? dd * softplus_grad_f(st.raw) : dd;
+            if (pos_thread && tid < valid) a.ddt[(b * L + t0 + tid) * H + h] = ddt;
+            const float dA_sum = block_sum<kGC>(pos_thread ? dcs * st.cd : 0.0f, sh.scan);
+            const float db_sum = block_sum<kGC>(pos_thread && tid < valid ? ddt : 0.0f, sh.scan);
+            if (tid == 0) {
+                a.dA_part[bhc] = dA_sum;
+                a.db_part[bhc] = db_sum;
+                if (has_d && !d_per_head) a.dD_part[bhc] = dD_sum;
+            }
+            st = st_next;
         }
-        tc::fence_async_smem();
-        tc::fence_before();
-        __syncthreads();
-        if (tid == 0) {
-            tc::fence_after();
-            const uint32_t i_mn_mn64 = tc::idesc_f16(fmt, 128, P, true, true);
-            const uint32_t i_k_mn64 = tc::idesc_f16(fmt, 128, P, false, true);
-            const uint32_t i_k_mn = tc::idesc_f16(fmt, 128, 128, false, true);
-            const uint32_t i_k_k = tc::idesc_f16(fmt, 128, 128, false, false);
-            const uint32_t i_mn_mn = tc::idesc_f16(fmt, 128, 128, true, true);
-            const uint32_t first = hh == 0 ? 0u : 1u;
-#pragma unroll
-            for (int ks = 0; ks < Q / 16; ++ks)   // Mh^T dY
-                tc::mma_f16(tS, tc::desc_mn(aM, WB, 16 * ks), tc::desc_mn(aY, WX, 16 * ks), i_mn_mn64, ks > 0);
-#pragma unroll
-            for (int ks = 0; ks < N / 16; ++ks)   // B dH^T
-                tc::mma_f16(tS + 64, tc::desc_k(aB, WB, 2 * ks), tc::desc_mn(aD, WH, 16 * ks), i_k_mn64, ks > 0);
-#pragma unroll
-            for (int ks = 0; ks < Q / 16; ++ks)   // dC += dG B
-                tc::mma_f16(tdC, tc::desc_k(aG, WB, 2 * ks), tc::desc_mn(aB, WB, 16 * ks), i_k_mn, ks > 0 ? 1u : first);
-#pragma unroll
-            for (int ks = 0; ks < P / 16; ++ks)   // dC += (exp(cs) dy) H
-                tc::mma_f16(tdC, tc::desc_k(aX, WX, 2 * ks), tc::desc_k(aH, WH, 2 * ks), i_k_k, 1u);
-#pragma unroll
-            for (int ks = 0; ks < Q / 16; ++ks)   // dB += dG^T C
-                tc::mma_f16(tdB, tc::desc_mn(aG, WB, 16 * ks), tc::desc_mn(aC, WB, 16 * ks), i_mn_mn, ks > 0 ? 1u : first);
-#pragma unroll
-            for (int ks = 0; ks < P / 16; ++ks)   // dB += (w o x) dH
-                tc::mma_f16(tdB, tc::desc_k(aXW, WX, 2 * ks), tc::desc_k(aD, WH, 2 * ks), i_k_k, 1u);
-            tc::commit(tc::smem_u32(&mbar));
-        }
-        // global inputs of the epilogue, fetched while the GEMMs run
-        uint4 xr[WX];
-        {
+        if (ok) {
+            // dC rows l, dB rows s (fp32, valid rows only), this thread's column half
             const bool live = r < valid;
+            float* dCr = a.dC + ((b * L + t0 + (live ? r : 0)) * G + g) * N;
+            float* dBr = a.dB + ((b * L + t0 + (live ? r : 0)) * G + g) * N;
+            for (int jj = 0; jj < N / 32; ++jj) {
+                const int col = 64 * hf + 16 * jj;
+                float vc[16], vb[16];
+                tc::tmem_ld16(tdC + lane_off + col, vc);   // all lanes: .sync.aligned
+                tc::tmem_ld16(tdB + lane_off + col, vb);
+                tc::tmem_wait_ld(vb);
+                tc::tmem_pin(vc);
+                if (live) {
 #pragma unroll
-            for (int j = 0; j < WX; ++j)
-                xr[j] = live ? *reinterpret_cast<const uint4*>(xg + grow + 8 * j) : make_uint4(0, 0, 0, 0);
-        }
-        const float dci = a.dcs_inter[bhc * Q + r];
-        const float dTc = r == Q - 1 ? a.dT[bhc] : 0.0f;
-        // column sums of E over the rows
-        float colsum = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kThreads / 32; ++w) colsum += sh.col[w][r];
-        const float dD_sum = block_sum(dD_head, sh.scan);
-        if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(43); ok = false; }
-        phase ^= 1;
-        tc::fence_after();
-        ok = __syncthreads_and(ok);
-        if (!ok) break;
-        // epilogue, row s = r
-        float dcs = 0.0f, dd_direct = 0.0f, dv = 0.0f;
-        {
-            const int s = r;
-            const float eTs = exp2_mufu((Tc - st.cs) * kLog2e);
-            float v_s = 0.0f;
-            const float Dh = sh.hs.D[hk];
-            for (int j = 0; j < P / 16; ++j) {
-                float di[16], zz[16], xv[16], yv[16];
-                tc::tmem_ld16(tS + lane_off + 16 * j, di);
-                tc::tmem_ld16(tS + lane_off + 64 + 16 * j, zz);
-                tc::tmem_wait_ld();
-                Pk<T>::unpack(xr[2 * j], xv);
-                Pk<T>::unpack(xr[2 * j + 1], xv + 8);
-                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(s, 2 * j, WX)), yv);
-                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(s, 2 * j + 1, WX)), yv + 8);
-                float dxv[16];
-#pragma unroll
-                for (int k = 0; k < 16; ++k) {
-                    v_s = fmaf(xv[k], zz[k], v_s);
-                    const float Dk = has_d ? (d_per_head ? a.D[h * P + 16 * j + k] : Dh) : 0.0f;
-                    dxv[k] = fmaf(st.d * eTs, zz[k], di[k]) + Dk * yv[k];   // Mh already carries d_s
-                }
-                if (s < valid) {
-                    *reinterpret_cast<uint4*>(dxg + grow + 16 * j) = pack8<T>(dxv);
-                    *reinterpret_cast<uint4*>(dxg + grow + 16 * j + 8) = pack8<T>(dxv + 8);
-                }
-            }
-            v_s *= eTs;
-            dv = st.d * v_s;
-            dcs = rowsum - st.d * colsum - dv + dci;
-            dd_direct = colsum + v_s;
-        }
-        // d/dT_c = exp(T) <dH_{c+1}, H_c> + sum_s d_s v_s, added at the chunk's last position
-        const float dv_sum = block_sum(dv, sh.scan);
-        if (r == Q - 1) dcs += dTc + dv_sum;
-        const float suffix = block_suffix_scan(dcs, sh.scan);
-        const float dd = fmaf(Ah, suffix, dd_direct);
-        const float ddt = (a.flags & SSM_SOFTPLUS) ? dd * softplus_grad_f(st.raw) : dd;
-        if (r < valid) a.ddt[(b * L + t0 + r) * H + h] = ddt;
-        const float dA_sum = block_sum(dcs * st.cd, sh.scan);
-        const float db_sum = block_sum(r < valid ? ddt : 0.0f, sh.scan);
-        if (tid == 0) {
-            a.dA_part[bhc] = dA_sum;
-            a.db_part[bhc] = db_sum;
-            if (has_d && !d_per_head) a.dD_part[bhc] = dD_sum;
-        }
-        tc::fence_before();
-        __syncthreads();
-    }
-    if (ok) {
-        // dC rows l, dB rows s (fp32, valid rows only)
-        const int r = tid;
-        const bool live = r < valid;
-        float* dCr = a.dC + ((b * L + t0 + (live ? r : 0)) * G + g) * N;
-        float* dBr = a.dB + ((b * L + t0 + (live ? r : 0)) * G + g) * N;
-        for (int j = 0; j < N / 16; ++j) {
-            float vc[16], vb[16];
-            tc::tmem_ld16(tdC + lane_off + 16 * j, vc);   // all lanes: .sync.aligned
-            tc::tmem_ld16(tdB + lane_off + 16 * j, vb);
-            tc::tmem_wait_ld();
-            if (live) {
-#pragma unroll
-                for (int k = 0; k < 16; k += 4) {
-                    *reinterpret_cast<float4*>(dCr + 16 * j + k) = make_float4(vc[k], vc[k + 1], vc[k + 2], vc[k + 3]);
-                    *reinterpret_cast<float4*>(dBr + 16 * j + k) = make_float4(vb[k], vb[k + 1], vb[k + 2], vb[k + 3]);
+                    for (int k = 0; k < 16; k += 4) {
+                        *reinterpret_cast<float4*>(dCr + col + k) = make_float4(vc[k], vc[k + 1], vc[k + 2], vc[k + 3]);
+                        *reinterpret_cast<float4*>(dBr + col + k) = make_float4(vb[k], vb[k + 1], vb[k + 2], vb[k + 3]);
+                    }
                 }
             }
         }
+        tc::cp_async_wait<0>();
     }
-    tc::cp_async_wait<0>();
     tc::fence_before();
     __syncthreads();
-    if (warp == 0) tc::tmem_dealloc(tm, 512);
+    if (mma_warp) tc::tmem_dealloc(tm, 512);
 }
 
 // dA, d dt_bias, dD over (batch, chunk), fixed order.
@@ -1187,7 +1293,7 @@ static int run_bwd(const Args& a, const ssm_chunk_scan_params* p, cudaStream_t s
     if (int e = set_smem((const void*)grads_kernel<T>, kSmemGrads)) return e;
     dstates_kernel<T><<<dim3((unsigned)a.nheads, (unsigned)a.batch), kThreads, kSmemDstates, s>>>(a);
     if (int e = check_launch("chunk_scan bwd (tensor cores): dstates")) return e;
-    grads_kernel<T><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)a.batch), kThreads, kSmemGrads, s>>>(a);
+    grads_kernel<T><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)a.batch), kGradThreads, kSmemGrads, s>>>(a);
     if (int e = check_launch("chunk_scan bwd (tensor cores): grads")) return e;
     const bool has_d = p->flags & SSM_HAS_D, d_per_head = p->flags & SSM_D_PER_HEAD;
     const int64_t total = 2 * p->nheads + (has_d ? (d_per_head ? p->nheads * P : p->nheads) : 0);
