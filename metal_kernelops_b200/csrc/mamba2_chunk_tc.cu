@@ -40,7 +40,11 @@
 // Operands are rounded to the input dtype before each GEMM (fp32 accumulate),
 // so the result carries the input dtype's rounding, as the reference's own
 // bf16/f16 runs do.
+#include <mutex>
 #include <string>
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include "common.cuh"
 #include "ssd_tc.h"
@@ -77,6 +81,11 @@ struct Args {
     float* dcs_inter;      // (b, h, nc * Q)
     float* dT;             // (b, h, nc)
     float* dA_part; float* db_part; float* dD_part;   // (b, h, nc) [x headdim]
+    // TMA descriptors of x, dy (X-like rows) and B, C (B-like rows); see encode_rows()
+    alignas(64) CUtensorMap tm_x;
+    alignas(64) CUtensorMap tm_dy;
+    alignas(64) CUtensorMap tm_B;
+    alignas(64) CUtensorMap tm_C;
 };
 
 // ----------------------------------------------------------- element types --
@@ -190,28 +199,33 @@ __device__ __forceinline__ float block_sum(float v, float* sh) {
     return s;
 }
 
-// Rows [0, Q) of a global row-major matrix (16-byte chunks) into a tile, rows
-// at or beyond `valid` zero-filled.  Lanes 0-7 take eight rows of one chunk so
-// that each quarter-warp writes 128 contiguous bytes of shared memory.
-template <int W, typename T, int NT = kThreads>
-__device__ __forceinline__ void load_rows(unsigned char* tile, const T* base, int64_t row_stride, int valid) {
-    const uint32_t st = tc::smem_u32(tile);
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    constexpr int CPW = W / 4;
-    for (int wi = wid; wi < (Q / 8) * CPW; wi += NT / 32) {
-        const int r = (wi / CPW) * 8 + (lane & 7);
-        const int ch = (wi % CPW) * 4 + (lane >> 3);
-        const bool v = r < valid;
-        const T* src = base + (int64_t)(v ? r : 0) * row_stride + ch * 8;
-        tc::cp_async16_zfill(st + tc::tile_off(r, ch, W), src, v ? 16u : 0u);
+// Dynamic shared memory, rounded up to 128 bytes: TMA tile destinations need
+// that alignment whatever the size of the kernel's static shared variables
+// (the launches reserve kSmemPad extra bytes).
+constexpr size_t kSmemPad = 128;
+__device__ __forceinline__ unsigned char* aligned_smem(unsigned char* raw) {
+    const uint32_t mis = tc::smem_u32(raw) & 127u;
+    return raw + ((128u - mis) & 127u);
+}
+
+// The Q rows of chunk c of head / group hg of batch b, from a tensor map made by
+// encode_rows(): Q/8 boxes of 8 rows, each landing as the 8-row group of core
+// matrices of the tile.  Rows past the sequence come back as zeros.  One thread
+// issues; the bytes (Q * W * 16) complete on `mbar`.
+template <int W>
+__device__ __forceinline__ void tma_rows(unsigned char* tile, const CUtensorMap& map, int64_t c, int64_t b,
+                                         int64_t hg, uint32_t mbar) {
+    if (reinterpret_cast<uintptr_t>(&map) & 63u) {   // descriptors must be 64-byte aligned: never issue
+        report(98);
+        return;
     }
-}
-// A 16 KB operand image copied linearly.
-template <int NT = kThreads>
-__device__ __forceinline__ void load_image(unsigned char* tile, const unsigned char* src) {
     const uint32_t st = tc::smem_u32(tile);
-    for (int i = threadIdx.x; i < (int)(kTileH / 16); i += NT) tc::cp_async16(st + i * 16, src + i * 16);
+#pragma unroll 4
+    for (int k = 0; k < Q / 8; ++k)
+        tc::tma_load5(st + k * W * 128, &map, 0, (int)(c * Q + 8 * k), 0, (int)b, (int)hg, mbar);
 }
+constexpr uint32_t kRowsX = Q * WX * 16;   // bytes of an X-like tile
+constexpr uint32_t kRowsB = Q * WB * 16;   // bytes of a B-like tile
 
 // Per-chunk step quantities of one head, thread s owning position s.
 struct Steps {
@@ -268,32 +282,41 @@ __device__ __forceinline__ Steps staged_steps(const Args& a, const HeadSh& hs, i
 // ====================================================================== F1 ==
 // One CTA per (b, h).  TMEM: H^T, lanes = state index n, columns = p.
 template <typename T>
-__global__ void __launch_bounds__(kThreads) states_kernel(const Args a) {
-    extern __shared__ __align__(128) unsigned char sm[];
-    unsigned char* sB[2] = {sm, sm + kTileB};
-    unsigned char* sX = sm + 2 * kTileB;
-    unsigned char* sXW = sX + kTileX;
+__global__ void __launch_bounds__(kThreads) states_kernel(const __grid_constant__ Args a) {
+    extern __shared__ __align__(128) unsigned char sm_raw[];
+    unsigned char* const sm = aligned_smem(sm_raw);
+    // double-buffered B and x tiles: chunk c + 1 loads while chunk c computes
+    unsigned char* const sB0 = sm;
+    unsigned char* const sX0 = sm + 2 * kTileB;
+    unsigned char* sXW = sX0 + 2 * kTileX;
     __shared__ float s_scan[4];
     __shared__ float s_T;
     __shared__ __align__(8) uint64_t mbar;
+    __shared__ __align__(8) uint64_t lbar[2];   // tiles of buffer 0 / 1 landed
     __shared__ uint32_t tbase;
 
     const int tid = threadIdx.x, warp = tid >> 5;
     const int64_t h = blockIdx.x, b = blockIdx.y, g = h / a.hpg;
-    const int64_t L = a.length, H = a.nheads, G = a.ngroups;
+    const int64_t H = a.nheads;
     const float Ah = a.A[h];
     const float bias = (a.flags & SSM_HAS_BIAS) ? a.dt_bias[h] : 0.0f;
-    const T* xg = reinterpret_cast<const T*>(a.x);
-    const T* Bgl = reinterpret_cast<const T*>(a.B);
+    uint32_t lpend[2] = {~0u, ~0u};           // parity of a load in flight per buffer (thread 0)
+    auto load_chunk = [&](int64_t c, int buf) {   // one thread
+        const uint32_t lb = tc::smem_u32(&lbar[buf]);
+        tc::mbar_expect_tx(lb, kRowsB + kRowsX);
+        tma_rows<WB>(sB0 + buf * kTileB, a.tm_B, c, b, g, lb);
+        tma_rows<WX>(sX0 + buf * kTileX, a.tm_x, c, b, h, lb);
+        lpend[buf] = (uint32_t)((c >> 1) & 1);
+    };
 
     if (warp == 0) tc::tmem_alloc(tc::smem_u32(&tbase), 64);
     if (tid == 0) {
         tc::mbar_init(tc::smem_u32(&mbar), 1);
+        tc::mbar_init(tc::smem_u32(&lbar[0]), 1);
+        tc::mbar_init(tc::smem_u32(&lbar[1]), 1);
         tc::fence_mbar_init();
+        load_chunk(0, 0);
     }
-    load_rows<WB>(sB[0], Bgl + (b * L * G + g) * N, G * N, (int)min64(Q, L));
-    load_rows<WX>(sX, xg + (b * L * H + h) * P, H * P, (int)min64(Q, L));
-    tc::cp_async_commit();
     tc::fence_before();
     __syncthreads();
     tc::fence_after();
@@ -318,16 +341,22 @@ __global__ void __launch_bounds__(kThreads) states_kernel(const Args a) {
     float raw_next = raw_dt(a, b, h, 0, bias);
     for (int64_t c = 0; c < a.nc && ok; ++c) {
         const int buf = (int)(c & 1);
+        unsigned char* const sB = sB0 + buf * kTileB;
+        unsigned char* const sX = sX0 + buf * kTileX;
         const float raw = raw_next;
         if (c + 1 < a.nc) raw_next = raw_dt(a, b, h, c + 1, bias);   // in flight during this chunk
         const Steps st = steps_of(a, raw, c, Ah, s_scan);
         if (tid == Q - 1) s_T = st.cs;
-        if (c > 0) {   // the previous chunk's GEMM read sXW and sB[buf ^ 1]
+        if (c > 0) {   // the previous chunk's GEMM read sXW and the other buffers
             if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(11); ok = false; }
             phase ^= 1;
             tc::fence_after();
         }
-        tc::cp_async_wait<0>();
+        ok = __syncthreads_and(ok);
+        if (!ok) break;
+        if (tid == 0 && c + 1 < a.nc) load_chunk(c + 1, buf ^ 1);   // a whole chunk ahead of its use
+        if (!tc::mbar_wait(tc::smem_u32(&lbar[buf]), (uint32_t)((c >> 1) & 1))) { report(13); ok = false; }
+        else if (tid == 0) lpend[buf] = ~0u;
         ok = __syncthreads_and(ok);
         if (!ok) break;
         const float Tc = s_T;
@@ -342,35 +371,32 @@ __global__ void __launch_bounds__(kThreads) states_kernel(const Args a) {
             for (int k = 0; k < 8; ++k) f[k] *= w;
             *reinterpret_cast<uint4*>(sXW + tc::tile_off(tid, j, WX)) = pack8<T>(f);
         }
-        // emit H_c (row n = tid of H^T), then H^T <- exp(T) H^T
+        // emit H_c (row n = tid of H^T), then H^T <- exp(T) H^T; one TMEM round trip
         {
             unsigned char* out = Hout + (size_t)c * kTileH;
             const float eT = exp2_mufu(Tc * kLog2e);
-            for (int j = 0; j < P / 16; ++j) {
-                float v[16];
-                tc::tmem_ld16(row_addr + j * 16, v);
-                tc::tmem_wait_ld(v);
-                *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j, WH)) = pack8<T>(v);
-                *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j + 1, WH)) = pack8<T>(v + 8);
+            float v[P / 16][16];
 #pragma unroll
-                for (int k = 0; k < 16; ++k) v[k] *= eT;
-                tc::tmem_st16(row_addr + j * 16, v);
+            for (int j = 0; j < P / 16; ++j) tc::tmem_ld16(row_addr + j * 16, v[j]);
+            tc::tmem_wait_ld(v[0]);
+#pragma unroll
+            for (int j = 1; j < P / 16; ++j) tc::tmem_pin(v[j]);
+#pragma unroll
+            for (int j = 0; j < P / 16; ++j) {
+                *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j, WH)) = pack8<T>(v[j]);
+                *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j + 1, WH)) = pack8<T>(v[j] + 8);
+#pragma unroll
+                for (int k = 0; k < 16; ++k) v[j][k] *= eT;
+                tc::tmem_st16(row_addr + j * 16, v[j]);
             }
             tc::tmem_wait_st();
         }
         tc::fence_async_smem();
         tc::fence_before();
         __syncthreads();
-        if (c + 1 < a.nc) {
-            const int64_t t1 = (c + 1) * Q;
-            const int valid = (int)min64(Q, L - t1);
-            load_rows<WB>(sB[buf ^ 1], Bgl + ((b * L + t1) * G + g) * N, G * N, valid);
-            load_rows<WX>(sX, xg + ((b * L + t1) * H + h) * P, H * P, valid);
-        }
-        tc::cp_async_commit();
         if (tid == 0) {
             tc::fence_after();
-            const uint32_t aB = tc::smem_u32(sB[buf]), aX = tc::smem_u32(sXW);
+            const uint32_t aB = tc::smem_u32(sB), aX = tc::smem_u32(sXW);
 #pragma unroll
             for (int ks = 0; ks < Q / 16; ++ks)
                 tc::mma_f16(tm, tc::desc_mn(aB, WB, 16 * ks), tc::desc_mn(aX, WX, 16 * ks), id, 1u);
@@ -381,7 +407,6 @@ __global__ void __launch_bounds__(kThreads) states_kernel(const Args a) {
         if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(12); ok = false; }
         tc::fence_after();
     }
-    tc::cp_async_wait<0>();
     ok = __syncthreads_and(ok);
     if (ok) {
         for (int j = 0; j < P / 16; ++j) {
@@ -391,6 +416,10 @@ __global__ void __launch_bounds__(kThreads) states_kernel(const Args a) {
 #pragma unroll
             for (int k = 0; k < 16; ++k) a.final_state[((b * H + h) * P + j * 16 + k) * N + tid] = v[k];
         }
+    }
+    if (tid == 0) {                            // no copy may land after exit
+        for (int i = 0; i < 2; ++i)
+            if (lpend[i] != ~0u) tc::mbar_wait(tc::smem_u32(&lbar[i]), lpend[i]);
     }
     tc::fence_before();
     __syncthreads();
@@ -423,8 +452,9 @@ __device__ __forceinline__ void mask_factors(MaskSh& m, const Steps& st) {
 // One CTA per (b, group, chunk).  TMEM: G [0,128), Y intra [128,192),
 // C H^T [192,256).
 template <typename T>
-__global__ void __launch_bounds__(kThreads) outputs_kernel(const Args a) {
-    extern __shared__ __align__(128) unsigned char sm[];
+__global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant__ Args a) {
+    extern __shared__ __align__(128) unsigned char sm_raw[];
+    unsigned char* const sm = aligned_smem(sm_raw);
     unsigned char* sC = sm;
     unsigned char* sM = sm + kTileB;          // B, then Mh
     unsigned char* sX = sm + 2 * kTileB;
@@ -433,37 +463,43 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const Args a) {
     __shared__ HeadSh hsh;
     __shared__ float s_scan[4];
     __shared__ __align__(8) uint64_t mbar;
+    __shared__ __align__(8) uint64_t lbar;    // tile loads, one phase per load
     __shared__ uint32_t tbase;
 
     const int tid = threadIdx.x, warp = tid >> 5;
     const int64_t c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
-    const int64_t L = a.length, H = a.nheads, G = a.ngroups;
+    const int64_t L = a.length, H = a.nheads;
     const int64_t t0 = c * Q;
     const int valid = (int)min64(Q, L - t0);
-    const T* xg = reinterpret_cast<const T*>(a.x);
     const T* zg = reinterpret_cast<const T*>(a.z);
     T* yg = reinterpret_cast<T*>(a.y);
     T* ypg = reinterpret_cast<T*>(a.ypre);
     const bool has_z = a.flags & SSM_HAS_Z, has_d = a.flags & SSM_HAS_D;
     const bool d_per_head = a.flags & SSM_D_PER_HEAD;
+    const uint32_t lb = tc::smem_u32(&lbar);
+    uint32_t lpend = ~0u;                     // parity of a load still in flight (thread 0)
 
     if (warp == 0) tc::tmem_alloc(tc::smem_u32(&tbase), 256);
     if (tid == 0) {
         tc::mbar_init(tc::smem_u32(&mbar), 1);
+        tc::mbar_init(lb, 1);
         tc::fence_mbar_init();
+        tc::mbar_expect_tx(lb, 2 * kRowsB);
+        tma_rows<WB>(sC, a.tm_C, c, b, g, lb);
+        tma_rows<WB>(sM, a.tm_B, c, b, g, lb);
+        lpend = 0;
     }
-    load_rows<WB>(sC, reinterpret_cast<const T*>(a.C) + ((b * L + t0) * G + g) * N, G * N, valid);
-    load_rows<WB>(sM, reinterpret_cast<const T*>(a.B) + ((b * L + t0) * G + g) * N, G * N, valid);
-    tc::cp_async_commit();
-    tc::cp_async_wait<0>();
-    tc::fence_async_smem();
+    __syncthreads();                          // the barriers are initialised before anyone waits
+    bool lok = tc::mbar_wait(lb, 0);
+    if (!lok) report(23);
+    else if (tid == 0) lpend = ~0u;
     tc::fence_before();
-    __syncthreads();
+    lok = __syncthreads_and(lok);
     tc::fence_after();
     const uint32_t tm = tbase;
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     const uint32_t aC = tc::smem_u32(sC), aM = tc::smem_u32(sM), aX = tc::smem_u32(sX), aH = tc::smem_u32(sH);
-    if (tid == 0) {
+    if (tid == 0 && lok) {
         const uint32_t idg = tc::idesc_f16(Pk<T>::kFmt, 128, 128, false, false);
 #pragma unroll
         for (int ks = 0; ks < N / 16; ++ks)
@@ -471,8 +507,8 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const Args a) {
         tc::commit(tc::smem_u32(&mbar));
     }
     uint32_t phase = 0;
-    bool ok = tc::mbar_wait(tc::smem_u32(&mbar), phase);
-    if (!ok) report(21);
+    bool ok = lok && tc::mbar_wait(tc::smem_u32(&mbar), phase);
+    if (lok && !ok) report(21);
     phase ^= 1;
     tc::fence_after();
     ok = __syncthreads_and(ok);
@@ -480,9 +516,13 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const Args a) {
     const uint32_t idy = tc::idesc_f16(Pk<T>::kFmt, 128, P, false, true);
     for (int64_t hh = 0; hh < a.hpg && ok; ++hh) {
         const int64_t h = g * a.hpg + hh;
-        load_rows<WX>(sX, xg + ((b * L + t0) * H + h) * P, H * P, valid);
-        load_image(sH, a.Ht + ((size_t)(b * H + h) * a.nc + c) * kTileH);
-        tc::cp_async_commit();
+        const uint32_t lpar = (uint32_t)((hh + 1) & 1);
+        if (tid == 0) {   // the previous head's GEMMs and epilogue are done with sX and sH
+            lpend = lpar;
+            tc::mbar_expect_tx(lb, kRowsX + kTileH);
+            tma_rows<WX>(sX, a.tm_x, c, b, h, lb);
+            tc::bulk_load(tc::smem_u32(sH), a.Ht + ((size_t)(b * H + h) * a.nc + c) * kTileH, kTileH, lb);
+        }
         const int hk = (int)(hh % kHeadsSh);
         if (hk == 0) {
             stage_heads(a, hsh, b, g, c, hh, (int)min64(kHeadsSh, a.hpg - hh));
@@ -522,10 +562,12 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const Args a) {
                 *reinterpret_cast<uint4*>(sM + tc::tile_off(l, 2 * j + 1, WB)) = hi;
             }
         }
-        tc::cp_async_wait<0>();
+        const bool lw = tc::mbar_wait(lb, lpar);      // this head's x and H_c
+        if (!lw) report(24);
+        else if (tid == 0) lpend = ~0u;
         tc::fence_async_smem();
         tc::fence_before();
-        __syncthreads();
+        if (!__syncthreads_and(lw)) { ok = false; break; }
         if (tid == 0) {
             tc::fence_after();
 #pragma unroll
@@ -580,7 +622,7 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const Args a) {
         tc::fence_before();
         __syncthreads();
     }
-    tc::cp_async_wait<0>();
+    if (tid == 0 && lpend != ~0u) tc::mbar_wait(lb, lpend);   // no copy may land after exit
     tc::fence_before();
     __syncthreads();
     if (warp == 0) tc::tmem_dealloc(tm, 256);
@@ -589,32 +631,36 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const Args a) {
 // ====================================================================== B1 ==
 // One CTA per (b, h), chunks in reverse.  TMEM: dH^T [0,64), C H_c^T [64,128).
 template <typename T>
-__global__ void __launch_bounds__(kThreads) dstates_kernel(const Args a) {
-    extern __shared__ __align__(128) unsigned char sm[];
+__global__ void __launch_bounds__(kThreads) dstates_kernel(const __grid_constant__ Args a) {
+    extern __shared__ __align__(128) unsigned char sm_raw[];
+    unsigned char* const sm = aligned_smem(sm_raw);
     unsigned char* sC = sm;
     unsigned char* sH = sm + kTileB;
     unsigned char* sY = sm + kTileB + kTileH;   // dout, then exp(cs_l) dy_l
     __shared__ float s_scan[4];
     __shared__ float s_T;
     __shared__ __align__(8) uint64_t mbar;
+    __shared__ __align__(8) uint64_t lbar;    // tile loads, one phase per chunk
     __shared__ uint32_t tbase;
 
     const int tid = threadIdx.x, warp = tid >> 5;
     const int64_t h = blockIdx.x, b = blockIdx.y, g = h / a.hpg;
-    const int64_t L = a.length, H = a.nheads, G = a.ngroups;
+    const int64_t L = a.length, H = a.nheads;
     const float Ah = a.A[h];
     const float bias = (a.flags & SSM_HAS_BIAS) ? a.dt_bias[h] : 0.0f;
     const bool has_z = a.flags & SSM_HAS_Z;
     const T* zg = reinterpret_cast<const T*>(a.z);
-    const T* dyg = reinterpret_cast<const T*>(a.dy);
     const T* ypg = reinterpret_cast<const T*>(a.ypre);
     T* dzg = reinterpret_cast<T*>(a.dz);
     const unsigned char* Hin = a.Ht + (size_t)(b * H + h) * a.nc * kTileH;
     unsigned char* dHout = a.dHt + (size_t)(b * H + h) * a.nc * kTileH;
 
     if (warp == 0) tc::tmem_alloc(tc::smem_u32(&tbase), 128);
+    const uint32_t lb = tc::smem_u32(&lbar);
+    uint32_t lpend = ~0u;                     // parity of a load still in flight (thread 0)
     if (tid == 0) {
         tc::mbar_init(tc::smem_u32(&mbar), 1);
+        tc::mbar_init(lb, 1);
         tc::fence_mbar_init();
     }
     tc::fence_before();
@@ -643,14 +689,20 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const Args a) {
         if (c > 0) raw_next = raw_dt(a, b, h, c - 1, bias);
         const int64_t t0 = c * Q;
         const int valid = (int)min64(Q, L - t0);
-        load_rows<WB>(sC, reinterpret_cast<const T*>(a.C) + ((b * L + t0) * G + g) * N, G * N, valid);
-        load_image(sH, Hin + (size_t)c * kTileH);
-        load_rows<WX>(sY, dyg + ((b * L + t0) * H + h) * P, H * P, valid);
-        tc::cp_async_commit();
+        const uint32_t lpar = (uint32_t)((a.nc - 1 - c) & 1);
+        if (tid == 0) {   // the previous chunk's GEMMs and passes are done with these tiles
+            tc::mbar_expect_tx(lb, kRowsB + kTileH + kRowsX);
+            tma_rows<WB>(sC, a.tm_C, c, b, g, lb);
+            tc::bulk_load(tc::smem_u32(sH), Hin + (size_t)c * kTileH, kTileH, lb);
+            tma_rows<WX>(sY, a.tm_dy, c, b, h, lb);
+            lpend = lpar;
+        }
         const Steps st = steps_of(a, raw, c, Ah, s_scan);
         if (tid == Q - 1) s_T = st.cs;
-        tc::cp_async_wait<0>();
-        __syncthreads();
+        const bool lw = tc::mbar_wait(lb, lpar);
+        if (!lw) report(32);
+        else if (tid == 0) lpend = ~0u;
+        if (!__syncthreads_and(lw)) { ok = false; break; }
         const float Tc = s_T;
         // dy row l = tid: gate, then exp(cs_l) dy_l in place
         {
@@ -682,20 +734,25 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const Args a) {
         {
             unsigned char* out = dHout + (size_t)c * kTileH;
             const float eT = exp2_mufu(Tc * kLog2e);
+            float v[P / 16][16];
+#pragma unroll
+            for (int j = 0; j < P / 16; ++j) tc::tmem_ld16(row_addr + j * 16, v[j]);
+            tc::tmem_wait_ld(v[0]);
+#pragma unroll
+            for (int j = 1; j < P / 16; ++j) tc::tmem_pin(v[j]);
+#pragma unroll
             for (int j = 0; j < P / 16; ++j) {
-                float v[16], hv[16];
-                tc::tmem_ld16(row_addr + j * 16, v);
-                tc::tmem_wait_ld(v);
-                *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j, WH)) = pack8<T>(v);
-                *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j + 1, WH)) = pack8<T>(v + 8);
+                float hv[16];
+                *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j, WH)) = pack8<T>(v[j]);
+                *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j + 1, WH)) = pack8<T>(v[j] + 8);
                 Pk<T>::unpack(*reinterpret_cast<const uint4*>(sH + tc::tile_off(tid, 2 * j, WH)), hv);
                 Pk<T>::unpack(*reinterpret_cast<const uint4*>(sH + tc::tile_off(tid, 2 * j + 1, WH)), hv + 8);
 #pragma unroll
                 for (int k = 0; k < 16; ++k) {
-                    dt_part = fmaf(v[k], hv[k], dt_part);
-                    v[k] *= eT;
+                    dt_part = fmaf(v[j][k], hv[k], dt_part);
+                    v[j][k] *= eT;
                 }
-                tc::tmem_st16(row_addr + j * 16, v);
+                tc::tmem_st16(row_addr + j * 16, v[j]);
             }
             tc::tmem_wait_st();
         }
@@ -723,21 +780,26 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const Args a) {
             // d(loss)/d(cs_l) through the inter-chunk output: <exp(cs_l) dy_l, (C H_c^T)_l>
             const int l = tid;
             float acc = 0.0f;
+            float ye4[P / 16][16];
+#pragma unroll
+            for (int j = 0; j < P / 16; ++j) tc::tmem_ld16(row_addr + 64 + 16 * j, ye4[j]);
+            tc::tmem_wait_ld(ye4[0]);
+#pragma unroll
+            for (int j = 1; j < P / 16; ++j) tc::tmem_pin(ye4[j]);
+#pragma unroll
             for (int j = 0; j < P / 16; ++j) {
-                float ye[16], yv[16];
-                tc::tmem_ld16(row_addr + 64 + 16 * j, ye);
-                tc::tmem_wait_ld(ye);
+                float yv[16];
                 Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(l, 2 * j, WX)), yv);
                 Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(l, 2 * j + 1, WX)), yv + 8);
 #pragma unroll
-                for (int k = 0; k < 16; ++k) acc = fmaf(yv[k], ye[k], acc);
+                for (int k = 0; k < 16; ++k) acc = fmaf(yv[k], ye4[j][k], acc);
             }
             a.dcs_inter[(b * H + h) * a.nc * Q + t0 + l] = acc;
         }
         tc::fence_before();
         ok = __syncthreads_and(ok);
     }
-    tc::cp_async_wait<0>();
+    if (tid == 0 && lpend != ~0u) tc::mbar_wait(lb, lpend);   // no copy may land after exit
     if (ok && (a.flags & SSM_HAS_INIT) && a.dinit) {
         for (int j = 0; j < P / 16; ++j) {
             float v[16];
@@ -801,8 +863,9 @@ struct GradSh {
 };
 
 template <typename T>
-__global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const Args a) {
-    extern __shared__ __align__(128) unsigned char sm[];
+__global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_constant__ Args a) {
+    extern __shared__ __align__(128) unsigned char sm_raw[];
+    unsigned char* const sm = aligned_smem(sm_raw);
     unsigned char* sB = sm;
     unsigned char* sC = sB + kTileB;
     unsigned char* sM = sC + kTileB;            // Mh
@@ -813,9 +876,9 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const Args a) {
     unsigned char* sH = sXW + kTileX;           // H_c^T
     unsigned char* sD = sH + kTileH;            // dH_{c+1}^T
     __shared__ GradSh sh;
-    __shared__ __align__(8) uint64_t bars[5];
+    __shared__ __align__(8) uint64_t bars[6];
     __shared__ uint32_t tbase;
-    enum { kBc = 0, kIn = 1, kM1 = 2, kMask = 3, kM2 = 4 };
+    enum { kBc = 0, kIn = 1, kM1 = 2, kMask = 3, kM2 = 4, kLh = 5 };   // kLh: a head's tiles landed
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool mma_warp = warp == kGC / 32;
@@ -823,40 +886,41 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const Args a) {
     const int r = q * 32 + lane;                       // TMEM row / tile row of this thread
     const int64_t c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int64_t L = a.length, H = a.nheads, G = a.ngroups;
+    (void)G;
     const int64_t t0 = c * Q;
     const int valid = (int)min64(Q, L - t0);
     const T* xg = reinterpret_cast<const T*>(a.x);
     const T* zg = reinterpret_cast<const T*>(a.z);
-    const T* dyg = reinterpret_cast<const T*>(a.dy);
     T* dxg = reinterpret_cast<T*>(a.dx);
     const bool has_z = a.flags & SSM_HAS_Z, has_d = a.flags & SSM_HAS_D;
     const bool d_per_head = a.flags & SSM_D_PER_HEAD;
     const uint32_t bar0 = tc::smem_u32(&bars[0]);
     auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
 
-    auto load_head = [&](int64_t hh) {            // compute threads only
+    uint32_t lpend = ~0u;                     // parity of a head load still in flight (thread 0)
+    auto load_head = [&](int64_t hh) {            // thread 0 only
         const int64_t h = g * a.hpg + hh;
         const int64_t bhc = (b * H + h) * a.nc + c;
-        load_rows<WX, T, kGC>(sX, xg + ((b * L + t0) * H + h) * P, H * P, valid);
-        load_rows<WX, T, kGC>(sY, dyg + ((b * L + t0) * H + h) * P, H * P, valid);
-        load_image<kGC>(sH, a.Ht + ((size_t)(b * H + h) * a.nc + c) * kTileH);
-        load_image<kGC>(sD, a.dHt + (size_t)bhc * kTileH);
-        tc::cp_async_commit();
+        tc::mbar_expect_tx(bar(kLh), 2 * kRowsX + 2 * kTileH);
+        tma_rows<WX>(sX, a.tm_x, c, b, h, bar(kLh));
+        tma_rows<WX>(sY, a.tm_dy, c, b, h, bar(kLh));
+        tc::bulk_load(tc::smem_u32(sH), a.Ht + ((size_t)(b * H + h) * a.nc + c) * kTileH, kTileH, bar(kLh));
+        tc::bulk_load(tc::smem_u32(sD), a.dHt + (size_t)bhc * kTileH, kTileH, bar(kLh));
+        lpend = (uint32_t)(hh & 1);
     };
 
     if (mma_warp) tc::tmem_alloc(tc::smem_u32(&tbase), 512);
     if (tid == 0) {
-        tc::mbar_init(bar(kBc), kGC);
+        tc::mbar_init(bar(kBc), 1);
         tc::mbar_init(bar(kIn), kGC);
         tc::mbar_init(bar(kM1), 1);
         tc::mbar_init(bar(kMask), kGC);
         tc::mbar_init(bar(kM2), 1);
+        tc::mbar_init(bar(kLh), 1);
         tc::fence_mbar_init();
-    }
-    if (!mma_warp) {
-        load_rows<WB, T, kGC>(sC, reinterpret_cast<const T*>(a.C) + ((b * L + t0) * G + g) * N, G * N, valid);
-        load_rows<WB, T, kGC>(sB, reinterpret_cast<const T*>(a.B) + ((b * L + t0) * G + g) * N, G * N, valid);
-        tc::cp_async_commit();
+        tc::mbar_expect_tx(bar(kBc), 2 * kRowsB);      // the MMA warp waits for these directly
+        tma_rows<WB>(sC, a.tm_C, c, b, g, bar(kBc));
+        tma_rows<WB>(sB, a.tm_B, c, b, g, bar(kBc));
         load_head(0);
     }
     tc::fence_before();
@@ -935,9 +999,6 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const Args a) {
     } else {
         // --------------------------------------------------- compute warps --
         const bool pos_thread = tid < Q;           // owns chunk position s = tid
-        tc::cp_async_wait<1>();                    // B and C
-        tc::fence_async_smem();
-        tc::mbar_arrive(bar(kBc));
         stage_heads<kGC>(a, sh.hs, b, g, c, 0, (int)min64(kHeadsSh, a.hpg));
         gsync<kGC>();
         Steps st = staged_steps<kGC>(a, sh.hs, 0, c, sh.scan);
@@ -953,8 +1014,13 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const Args a) {
             const float Dh = sh.hs.D[hk];
             const float Tc = sh.T[hh & 1];
             const int64_t grow = ((b * L + t0 + r) * H + h) * P;   // row r of x / dy / dx
-            tc::cp_async_wait<0>();
-            gsync<kGC>();
+            {
+                const bool lw = tc::mbar_wait(bar(kLh), par);   // this head's tiles
+                if (!lw) report(45);
+                else if (tid == 0) lpend = ~0u;
+                ok = cg_all<kGC>(lw);
+                if (!ok) break;
+            }
             if (has_z && r < valid) {               // gate dy in place, own row half
                 for (int j = j0; j < j0 + WX / 2; ++j) {
                     float f[8], zv[8];
@@ -1130,7 +1196,7 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const Args a) {
             tc::fence_before();                      // S read: the next head's dY X^T may overwrite it
             gsync<kGC>();                            // every thread is done with the tiles; sh.vp complete
             if (hh + 1 < a.hpg) {
-                load_head(hh + 1);
+                if (tid == 0) load_head(hh + 1);
                 mask_factors<kGC>(sh.m, st_next);    // the scalars below use st, not sh.m
             }
             float dcs = 0.0f, dd_direct = 0.0f, dv = 0.0f;
@@ -1177,7 +1243,10 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const Args a) {
                 }
             }
         }
-        tc::cp_async_wait<0>();
+        if (tid == 0) {                        // no copy may land after exit
+            if (lpend != ~0u) tc::mbar_wait(bar(kLh), lpend);
+            tc::mbar_wait(bar(kBc), 0);
+        }
     }
     tc::fence_before();
     __syncthreads();
@@ -1214,7 +1283,7 @@ __global__ void reduce_kernel(const Args a, float* dA, float* dbias, float* dD) 
 }
 
 // ------------------------------------------------------------------ host ----
-constexpr size_t kSmemStates = 2 * kTileB + 2 * kTileX;
+constexpr size_t kSmemStates = 2 * kTileB + 3 * kTileX;
 constexpr size_t kSmemOutputs = 2 * kTileB + kTileX + kTileH;
 constexpr size_t kSmemDstates = kTileB + 2 * kTileH;
 constexpr size_t kSmemGrads = 4 * kTileB + 3 * kTileX + 2 * kTileH;
@@ -1271,6 +1340,44 @@ static void make_args(const ssm_chunk_scan_params* p, Args& a) {
 
 static bool aligned16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; }
 
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime.
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+// Tensor map over the rows of a (batch, length, heads, width) bf16/f16 tensor
+// (x, dy: heads = nheads, width = headdim; B, C: heads = ngroups, width =
+// dstate) as the 5-D view (8 elements, row in the batch, 16-byte chunk, batch,
+// head): a box of (8, 8, width / 8, 1, 1) is one 8-row group of core matrices
+// of a tile (tile_off layout), and rows past `length` read as zeros.
+static int encode_rows(CUtensorMap* m, const void* base, int dtype, int64_t batch, int64_t length, int64_t heads,
+                       int64_t width) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return fail(SSM_ERR_CUDA, "chunk_scan (tensor cores): cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t es = 2;
+    cuuint64_t dim[5] = {8, (cuuint64_t)length, (cuuint64_t)(width / 8), (cuuint64_t)batch, (cuuint64_t)heads};
+    cuuint64_t str[4] = {(cuuint64_t)(heads * width) * es, 16, (cuuint64_t)(length * heads * width) * es,
+                         (cuuint64_t)width * es};
+    cuuint32_t box[5] = {8, 8, (cuuint32_t)(width / 8), 1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    const CUresult r = enc(m, dtype == SSM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
+                           const_cast<void*>(base), dim, str, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(SSM_ERR_CUDA, "chunk_scan (tensor cores): cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return SSM_OK;
+}
+
 static int set_smem(const void* fn, size_t bytes) {
     if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
         return check_launch("chunk_scan (tensor cores): smem attribute");
@@ -1279,21 +1386,21 @@ static int set_smem(const void* fn, size_t bytes) {
 
 template <typename T>
 static int run_fwd(const Args& a, cudaStream_t s) {
-    if (int e = set_smem((const void*)states_kernel<T>, kSmemStates)) return e;
-    if (int e = set_smem((const void*)outputs_kernel<T>, kSmemOutputs)) return e;
-    states_kernel<T><<<dim3((unsigned)a.nheads, (unsigned)a.batch), kThreads, kSmemStates, s>>>(a);
+    if (int e = set_smem((const void*)states_kernel<T>, kSmemStates + kSmemPad)) return e;
+    if (int e = set_smem((const void*)outputs_kernel<T>, kSmemOutputs + kSmemPad)) return e;
+    states_kernel<T><<<dim3((unsigned)a.nheads, (unsigned)a.batch), kThreads, kSmemStates + kSmemPad, s>>>(a);
     if (int e = check_launch("chunk_scan fwd (tensor cores): states")) return e;
-    outputs_kernel<T><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)a.batch), kThreads, kSmemOutputs, s>>>(a);
+    outputs_kernel<T><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)a.batch), kThreads, kSmemOutputs + kSmemPad, s>>>(a);
     return check_launch("chunk_scan fwd (tensor cores): outputs");
 }
 
 template <typename T>
 static int run_bwd(const Args& a, const ssm_chunk_scan_params* p, cudaStream_t s) {
-    if (int e = set_smem((const void*)dstates_kernel<T>, kSmemDstates)) return e;
-    if (int e = set_smem((const void*)grads_kernel<T>, kSmemGrads)) return e;
-    dstates_kernel<T><<<dim3((unsigned)a.nheads, (unsigned)a.batch), kThreads, kSmemDstates, s>>>(a);
+    if (int e = set_smem((const void*)dstates_kernel<T>, kSmemDstates + kSmemPad)) return e;
+    if (int e = set_smem((const void*)grads_kernel<T>, kSmemGrads + kSmemPad)) return e;
+    dstates_kernel<T><<<dim3((unsigned)a.nheads, (unsigned)a.batch), kThreads, kSmemDstates + kSmemPad, s>>>(a);
     if (int e = check_launch("chunk_scan bwd (tensor cores): dstates")) return e;
-    grads_kernel<T><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)a.batch), kGradThreads, kSmemGrads, s>>>(a);
+    grads_kernel<T><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)a.batch), kGradThreads, kSmemGrads + kSmemPad, s>>>(a);
     if (int e = check_launch("chunk_scan bwd (tensor cores): grads")) return e;
     const bool has_d = p->flags & SSM_HAS_D, d_per_head = p->flags & SSM_D_PER_HEAD;
     const int64_t total = 2 * p->nheads + (has_d ? (d_per_head ? p->nheads * P : p->nheads) : 0);
@@ -1309,6 +1416,9 @@ int fwd(const ssm_chunk_scan_params* p, cudaStream_t s) {
         return fail(SSM_ERR_INVALID, "chunk_scan fwd (tensor cores): x, B, C, z, y and saved must be 16-byte aligned");
     Args a;
     make_args(p, a);
+    if (int e = encode_rows(&a.tm_x, p->x, p->dtype, p->batch, p->length, p->nheads, P)) return e;
+    if (int e = encode_rows(&a.tm_B, p->B, p->dtype, p->batch, p->length, p->ngroups, N)) return e;
+    if (int e = encode_rows(&a.tm_C, p->C, p->dtype, p->batch, p->length, p->ngroups, N)) return e;
     return p->dtype == SSM_BF16 ? run_fwd<__nv_bfloat16>(a, s) : run_fwd<__half>(a, s);
 }
 
@@ -1330,6 +1440,10 @@ int bwd(const ssm_chunk_scan_params* p, cudaStream_t s) {
     a.dA_part = reinterpret_cast<float*>(ws + w.dh + w.dci + w.dt);
     a.db_part = reinterpret_cast<float*>(ws + w.dh + w.dci + w.dt + w.part);
     a.dD_part = reinterpret_cast<float*>(ws + w.dh + w.dci + w.dt + 2 * w.part);
+    if (int e = encode_rows(&a.tm_x, p->x, p->dtype, p->batch, p->length, p->nheads, P)) return e;
+    if (int e = encode_rows(&a.tm_dy, p->dy, p->dtype, p->batch, p->length, p->nheads, P)) return e;
+    if (int e = encode_rows(&a.tm_B, p->B, p->dtype, p->batch, p->length, p->ngroups, N)) return e;
+    if (int e = encode_rows(&a.tm_C, p->C, p->dtype, p->batch, p->length, p->ngroups, N)) return e;
     return p->dtype == SSM_BF16 ? run_bwd<__nv_bfloat16>(a, p, s) : run_bwd<__half>(a, p, s);
 }
 

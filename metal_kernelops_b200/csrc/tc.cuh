@@ -157,6 +157,28 @@ __device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, uint32
     return false;
 }
 
+// ------------------------------------------------------------ TMA copies --
+// Arrive on an mbarrier and add `bytes` to the transaction count its current
+// phase waits for (the copies below retire those bytes).
+__device__ __forceinline__ void mbar_expect_tx(uint32_t mbar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(mbar), "r"(bytes) : "memory");
+}
+// Tiled 5-D tensor load (one box) into this CTA's shared memory; no multicast.
+// The innermost coordinate must keep 16-byte alignment (every caller passes 0).
+__device__ __forceinline__ void tma_load5(uint32_t dst, const void* map, int c0, int c1, int c2, int c3, int c4,
+                                          uint32_t mbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4, %5, %6}], [%7];"
+        :: "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(mbar)
+        : "memory");
+}
+// Contiguous global -> shared copy of `bytes` (multiple of 16, both ends 16-byte aligned).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(dst), "l"(src), "r"(bytes), "r"(mbar) : "memory");
+}
+
 // ------------------------------------------------------------ async copies --
 __device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(saddr), "l"(g) : "memory");
