@@ -47,6 +47,8 @@ CONFIGS = {
 SSD_CONFIG = dict(batch=8, length=8192, nheads=80, headdim=64, dstate=128, ngroups=8, chunk=256,
                   seed=1003)
 DECODE_CONFIG = dict(batch=256, nheads=80, headdim=64, dstate=128, ngroups=8, seed=1004)
+# the reference's largest timed ss2d shape (measured/path_scan.json "b1_d96_56x56")
+SS2D_CONFIG = dict(batch=1, channels=96, groups=1, dstate=16, height=56, width=56, seed=1005)
 
 
 def _peaks():
@@ -115,7 +117,7 @@ class Clocks:
 # ---------------------------------------------------------------- scan op --
 
 def _scan_inputs(cfg, batch_lo, batch_hi, device):
-    from oracle.ssm_oracle import selective_scan_inputs
+    from metal_kernelops_b200.workloads import selective_scan_inputs
     # generate the full config on the host (seeded), keep this rank's rows
     full = selective_scan_inputs(cfg["batch"], cfg["dim"], cfg["length"], cfg["dstate"],
                                  cfg["groups"], seed=cfg["seed"], act_dtype=torch.bfloat16) \
@@ -131,7 +133,7 @@ def _scan_inputs(cfg, batch_lo, batch_hi, device):
 def _scan_inputs_rows(cfg, lo, hi):
     """Large configs: generate per batch row with a row-derived seed so every
     rank sees the same global tensor without materialising it whole."""
-    from oracle.ssm_oracle import selective_scan_inputs
+    from metal_kernelops_b200.workloads import selective_scan_inputs
     rows = [selective_scan_inputs(1, cfg["dim"], cfg["length"], cfg["dstate"], cfg["groups"],
                                   seed=cfg["seed"] * 1000 + b, act_dtype=torch.bfloat16)
             for b in range(lo, hi)]
@@ -343,7 +345,7 @@ def run_ssd(args, world, rank, device):
     import torch.distributed as dist
     import metal_kernelops_b200  # noqa: F401
     from metal_kernelops_b200.parallel import batch_slice
-    from oracle.ssm_oracle import ssd_inputs
+    from metal_kernelops_b200.workloads import ssd_inputs
     cfg = dict(SSD_CONFIG)
     if args.shape:
         cfg["batch"], cfg["length"] = (int(v) for v in args.shape.split(",")[:2])
@@ -394,7 +396,7 @@ def run_decode(args, world, rank, device):
     import torch.distributed as dist
     from metal_kernelops_b200.cv import mamba2_state_update
     from metal_kernelops_b200.parallel import batch_slice
-    from oracle.ssm_oracle import decode_inputs
+    from metal_kernelops_b200.workloads import decode_inputs
     cfg = dict(DECODE_CONFIG)
     rows = batch_slice(cfg["batch"], rank, world)
     host = decode_inputs(cfg["batch"], cfg["nheads"], cfg["headdim"], cfg["dstate"], cfg["ngroups"],
@@ -432,10 +434,63 @@ def run_decode(args, world, rank, device):
     }
 
 
+def run_ss2d(args, world, rank, device):
+    """VMamba four-path 2D scan fwd+bwd, fp32 as in the reference,
+    at the reference's largest timed shape (b1 d96 56x56, 16 states) unless
+    --shape batch,channels,height,width overrides it; batch sharded."""
+    import torch.distributed as dist
+    from metal_kernelops_b200.parallel import batch_slice
+    from metal_kernelops_b200.workloads import ss2d_inputs
+    cfg = dict(SS2D_CONFIG)
+    if args.shape:
+        cfg["batch"], cfg["channels"], cfg["height"], cfg["width"] = (int(v) for v in args.shape.split(","))
+    rows = batch_slice(cfg["batch"], rank, world)
+    u, dt, A, B, C = ss2d_inputs(cfg["batch"], cfg["channels"], cfg["groups"], cfg["dstate"],
+                                 cfg["height"], cfg["width"], seed=cfg["seed"])
+    u, dt, B, C = (t[rows].contiguous().to(device) for t in (u, dt, B, C))
+    A = A.to(device)
+    g = torch.Generator().manual_seed(cfg["seed"] + 1)
+    dy = torch.randn(u.shape, generator=g).to(device)
+    ops = torch.ops.b200ssm
+
+    def fwd():
+        return ops.ss2d_scan_fwd(u, dt, A, B, C, 1.0, True)
+
+    def step():
+        y, ck = fwd()
+        ops.ss2d_scan_bwd(dy, u, dt, A, B, C, ck, 1.0)
+
+    ms = _timed(step, args.steps, args.warmup, world, dist)
+    fwd_ms = _timed(fwd, args.steps, args.warmup, world, dist)
+    if rank != 0:
+        return None
+    b = rows.stop - rows.start
+    C_, G, N, H, W = (cfg[k] for k in ("channels", "groups", "dstate", "height", "width"))
+    L = H * W
+    units = cfg["batch"] * C_ * L
+    alg_bytes = b * (32 * C_ * L + 24 * G * N * L)
+    gbs = alg_bytes / (ms / 1e3) / 1e9
+    peaks, kind = _peaks()
+    return {
+        "metric": "ss2d four-path scan fwd+bwd B*C*H*W elems/s", "value": units / (ms / 1e3),
+        "unit": "elem/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp32", "data": "synthetic (seeded, reference verifier distributions)",
+        "config": {"workload": "VMamba ss2d four-path scan fwd+bwd", **cfg,
+                   "parallelism": f"dp{world} (batch shard)"},
+        "breakdown_ms": {"fwd": fwd_ms, "bwd": ms - fwd_ms},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"], "peak_source": kind,
+                     "alg_bytes_per_step": alg_bytes, "traffic": None},
+        "gpu_launches": 22 * args.steps,
+    }
+
+
 def cpu_baseline_scan(cfg, threads, budget_s=15.0):
     """The oracle (reference CPU code restated) on a bounded sample: one batch
     row, a slice of channels, the full sequence; fwd + bwd with autograd."""
-    from oracle.ssm_oracle import selective_scan_inputs, selective_scan_ref
+    from metal_kernelops_b200.workloads import selective_scan_inputs
+    from oracle.ssm_oracle import selective_scan_ref
     torch.set_num_threads(threads)
     channels = 64
     inp = selective_scan_inputs(1, channels, cfg["length"], cfg["dstate"], cfg["groups"],
@@ -464,7 +519,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--op", default="scan", choices=["scan", "ssd", "decode"])
+    ap.add_argument("--op", default="scan", choices=["scan", "ssd", "decode", "ss2d"])
     ap.add_argument("--config", type=int, default=2, choices=[1, 2])
     ap.add_argument("--shape", default=None,
                     help="batch,dim,seqlen override of the config (profiling runs on small cases)")
@@ -508,7 +563,7 @@ def main():
     if args.op == "scan":
         line = run_scan(args, world, rank, device)
     else:
-        line = (run_ssd if args.op == "ssd" else run_decode)(args, world, rank, device)
+        line = {"ssd": run_ssd, "decode": run_decode, "ss2d": run_ss2d}[args.op](args, world, rank, device)
     if rank == 0 and line is not None:
         if world == 1 and not args.no_cpu_baseline and args.op == "scan":
             line["cpu_baseline"] = cpu_baseline_scan(CONFIGS[args.config], threads)

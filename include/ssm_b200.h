@@ -241,6 +241,53 @@ int ssm_chunk_scan_sizes(const ssm_chunk_scan_params* p, size_t* saved_bytes,
 int ssm_chunk_scan_fwd(const ssm_chunk_scan_params* p, void* stream);
 int ssm_chunk_scan_bwd(const ssm_chunk_scan_params* p, void* stream);
 
+/* ------------------------------------------------------------------------- *
+ * VMamba four-path 2D selective scan (ss2d).
+ *
+ * Replaces `metal_kernelops.cv.ss2d_scan`
+ * (src/metal_kernelops/cv/path_scan.py:546-576): the forward `_PathScan.forward`
+ * (transpose_states / path_summaries / boundaries / path_scan / merge_paths)
+ * and the backward `_PathScan.backward` (:495-543: stacking copies, scan.py's
+ * three backward kernels, merge_paths folds).  Path k of pixel (h, w) is step
+ *   0: h*W + w    1: w*H + h    2: L-1-(h*W + w)    3: L-1-(w*H + h)
+ * (L = H*W); the four path outputs are added as (p0 + p2) + (p1 + p3) and
+ * multiplied by `scale` (1 for merge "sum", 0.25 for "mean").
+ *
+ *   u, dt, y, dout, du, ddt : (batch, channels, height, width), act_dtype
+ *   A                       : (channels, dstate) fp32;  dA (channels, dstate) fp32
+ *   B, C                    : (batch, groups, dstate, height, width), bc_dtype
+ *   dB, dC                  : (batch, groups, dstate, height, width) fp32
+ * The forward writes `checkpoints` (fp32, checkpoint_bytes) that the backward
+ * reads; the forward and the backward each take a workspace of the size
+ * ssm_ss2d_scan_sizes returns.
+ * ------------------------------------------------------------------------- */
+typedef struct ssm_ss2d_scan_params {
+    int64_t batch, channels, height, width, groups, dstate;
+    int32_t act_dtype;          /* ssm_dtype of u, dt, y, dout, du, ddt */
+    int32_t bc_dtype;           /* ssm_dtype of B and C                 */
+    float scale;                /* 1 (merge "sum") or 0.25 (merge "mean") */
+    const void* u;
+    const void* dt;
+    const float* A;
+    const void* B;
+    const void* C;
+    void* y;
+    float* checkpoints;         /* may be NULL in the forward: nothing saved */
+    const void* dout;
+    void* du;
+    void* ddt;
+    float* dA;
+    float* dB;
+    float* dC;
+    void* workspace;
+    size_t workspace_bytes;
+} ssm_ss2d_scan_params;
+
+int ssm_ss2d_scan_sizes(const ssm_ss2d_scan_params* p, size_t* checkpoint_bytes,
+                        size_t* fwd_workspace_bytes, size_t* bwd_workspace_bytes);
+int ssm_ss2d_scan_fwd(const ssm_ss2d_scan_params* p, void* stream);
+int ssm_ss2d_scan_bwd(const ssm_ss2d_scan_params* p, void* stream);
+
 /* Kernels that wait on an mbarrier give up after a bounded number of polls,
  * record a non-zero code in a per-device flag and return.  This reads the flag
  * of the current device (synchronising with it) and clears it; 0 means no

@@ -37,6 +37,7 @@ EXPORTS = (
     "ssm_state_update_bwd_noalloc",
     "ssm_chunk_scan_sizes", "ssm_chunk_scan_fwd", "ssm_chunk_scan_bwd",
     "ssm_take_kernel_error",
+    "ssm_ss2d_scan_sizes", "ssm_ss2d_scan_fwd", "ssm_ss2d_scan_bwd",
 )
 
 _I64, _I32, _U32, _P, _SZ = ctypes.c_int64, ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t
@@ -84,6 +85,18 @@ class ChunkScanParams(ctypes.Structure):
     ]
 
 
+class Ss2dScanParams(ctypes.Structure):
+    _fields_ = [
+        ("batch", _I64), ("channels", _I64), ("height", _I64), ("width", _I64),
+        ("groups", _I64), ("dstate", _I64),
+        ("act_dtype", _I32), ("bc_dtype", _I32), ("scale", ctypes.c_float),
+        ("u", _P), ("dt", _P), ("A", _P), ("B", _P), ("C", _P),
+        ("y", _P), ("checkpoints", _P),
+        ("dout", _P), ("du", _P), ("ddt", _P), ("dA", _P), ("dB", _P), ("dC", _P),
+        ("workspace", _P), ("workspace_bytes", _SZ),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -106,7 +119,8 @@ def lib():
             handle.ssm_last_error.argtypes = []
             for name, struct in (("selective_scan", SelectiveScanParams),
                                  ("state_update", StateUpdateParams),
-                                 ("chunk_scan", ChunkScanParams)):
+                                 ("chunk_scan", ChunkScanParams),
+                                 ("ss2d_scan", Ss2dScanParams)):
                 for suffix in ("fwd", "bwd"):
                     fn = getattr(handle, f"ssm_{name}_{suffix}")
                     fn.restype = ctypes.c_int
@@ -117,10 +131,14 @@ def lib():
                 ctypes.POINTER(StateUpdateParams), ctypes.POINTER(_SZ)]
             handle.ssm_chunk_scan_sizes.argtypes = [
                 ctypes.POINTER(ChunkScanParams), ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]
+            handle.ssm_ss2d_scan_sizes.argtypes = [
+                ctypes.POINTER(Ss2dScanParams), ctypes.POINTER(_SZ), ctypes.POINTER(_SZ),
+                ctypes.POINTER(_SZ)]
             handle.ssm_state_update_bwd_noalloc.restype = ctypes.c_int
             handle.ssm_state_update_bwd_noalloc.argtypes = [ctypes.POINTER(StateUpdateParams),
                                                             ctypes.c_void_p]
-            for name in ("ssm_selective_scan_sizes", "ssm_state_update_sizes", "ssm_chunk_scan_sizes"):
+            for name in ("ssm_selective_scan_sizes", "ssm_state_update_sizes", "ssm_chunk_scan_sizes",
+                         "ssm_ss2d_scan_sizes"):
                 getattr(handle, name).restype = ctypes.c_int
             handle.ssm_take_kernel_error.restype = ctypes.c_int
             handle.ssm_take_kernel_error.argtypes = []

@@ -163,7 +163,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, uint32
 __device__ __forceinline__ void mbar_expect_tx(uint32_t mbar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(mbar), "r"(bytes) : "memory");
 }
-// Tiled 5-D tensor load (one box) into this CTA's shared memory; no multicast.
+// Tiled 5-D tensor load (one box) into the issuing CTA's own shared memory.
 // The innermost coordinate must keep 16-byte alignment (every caller passes 0).
 __device__ __forceinline__ void tma_load5(uint32_t dst, const void* map, int c0, int c1, int c2, int c3, int c4,
                                           uint32_t mbar) {

@@ -2,12 +2,15 @@
 
 * ``mamba2_chunk_scan`` -- chunked SSD scan (cv/mamba2_chunk.py:617-678)
 * ``mamba2_state_update`` -- one decode step (cv/mamba2_state.py:759-819)
+* ``ss2d_scan``, ``path_orders`` -- VMamba four-path 2D selective scan
+  (cv/path_scan.py:153-163, :546-576), on the Mamba-1 scan kernels
 
-The reference's other ``cv`` families (causal conv1d, gated RMSNorm, VMamba
-path scan, NSA selection, RoIAlign) are outside this package's scope.
+The reference's other ``cv`` families (NSA selection, RoIAlign) are outside
+this package's scope.
 """
 
 from .mamba2_chunk import last_path, mamba2_chunk_scan
 from .mamba2_state import mamba2_state_update
+from .path_scan import path_orders, ss2d_scan
 
-__all__ = ["last_path", "mamba2_chunk_scan", "mamba2_state_update"]
+__all__ = ["last_path", "mamba2_chunk_scan", "mamba2_state_update", "path_orders", "ss2d_scan"]

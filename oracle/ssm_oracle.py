@@ -17,20 +17,28 @@ reference's does:
   ``:652-678`` (the chunked torch composition the reference runs off-MPS; it is
   the reference's CPU path and therefore the timed CPU baseline for SSD)
 * ``mamba2_state_update_ref``  <- ``src/metal_kernelops/cv/mamba2_state.py:822-849``
+* ``ss2d_scan_ref``            <- ``src/metal_kernelops/cv/path_scan.py:608-639``
+  (``ss2d_scan_reference``: four index-arithmetic path orders over
+  ``scan_functional``, merged as (p0 + p2) + (p1 + p3))
 * ``ssd_minimal_discrete``     <- ``benchmarks/verify_mamba2_chunk.py:185-216``
   (the published ``ssd_minimal_discrete`` listing of state-spaces/mamba, used
   by the reference as a known-answer cross-check)
 
-Input generators follow the seeds and value distributions of the hot-path
-configurations and of the reference's verifiers.
+The seeded input generators (hot-path configurations 0-4 and the reference
+verifiers' distributions) live in ``metal_kernelops_b200.workloads`` and are
+re-exported here for the tests.
 """
 
 from __future__ import annotations
 
-import math
 
 import torch
 import torch.nn.functional as F
+
+# seeded workload generators (BASELINE distributions); they live with the
+# package so that bench.py's GPU arm does not import this module
+from metal_kernelops_b200.workloads import (  # noqa: F401
+    decode_inputs, selective_scan_inputs, ss2d_inputs, ssd_inputs)
 
 __all__ = [
     "selective_scan_stepwise",
@@ -40,6 +48,9 @@ __all__ = [
     "mamba2_chunk_scan_composition",
     "mamba2_state_update_ref",
     "ssd_minimal_discrete",
+    "ss2d_path_orders",
+    "ss2d_scan_ref",
+    "ss2d_inputs",
     "max_rel",
     "norm_rel",
     "selective_scan_inputs",
@@ -139,6 +150,46 @@ def selective_scan_ref(u, dt, A, B, C, D=None, z=None, delta_bias=None,
     if z is not None:
         out = out * F.silu(z)
     return out
+
+
+# ---------------------------------------------------------------------------
+# VMamba four-path 2D scan
+# ---------------------------------------------------------------------------
+
+def ss2d_path_orders(height, width):
+    """Step -> flat pixel index of the four paths (``cv/path_scan.py:153-163``),
+    built from explicit index lists: row-major, column-major, and their reverses."""
+    row = [h * width + w for h in range(height) for w in range(width)]
+    col = [h * width + w for w in range(width) for h in range(height)]
+    return [torch.tensor(o, dtype=torch.long) for o in (row, col, row[::-1], col[::-1])]
+
+
+def ss2d_scan_ref(u, dt, A, B, C, merge="sum"):
+    """Four-path 2D selective scan (``ss2d_scan_reference``, path_scan.py:608-639).
+
+    u, dt: (batch, channels, height, width); A: (channels, states);
+    B, C: (batch, groups, states, height, width).  Each path permutes the
+    flattened map, runs ``scan_functional``, and scatters back; the merge is
+    (p0 + p2) + (p1 + p3), times 0.25 for ``merge="mean"``.
+    """
+    if merge not in ("sum", "mean"):
+        raise ValueError(f"merge must be one of ('sum', 'mean'), got {merge!r}")
+    batch, channels, height, width = u.shape
+    groups, states = B.shape[1], A.shape[1]
+    length = height * width
+    su = u.reshape(batch, channels, length)
+    sdt = dt.reshape(batch, channels, length)
+    sb = B.reshape(batch, groups, states, length)
+    sc = C.reshape(batch, groups, states, length)
+    restored = []
+    for order in ss2d_path_orders(height, width):
+        y = scan_functional(su.index_select(-1, order), sdt.index_select(-1, order), A,
+                            sb.index_select(-1, order), sc.index_select(-1, order))
+        restored.append(su.new_zeros(batch, channels, length).index_copy(-1, order, y))
+    total = (restored[0] + restored[2]) + (restored[1] + restored[3])
+    if merge == "mean":
+        total = total * 0.25
+    return total.reshape(batch, channels, height, width)
 
 
 # ---------------------------------------------------------------------------
@@ -352,64 +403,3 @@ def mamba2_state_update_ref(state, x, dt, A, B, C, D=None, z=None, dt_bias=None,
 # seeded inputs for the hot-path configurations
 # ---------------------------------------------------------------------------
 
-def _softplus_inv(v):
-    return math.log(math.expm1(v))
-
-
-def selective_scan_inputs(batch, dim, length, dstate, groups=1, seed=1000,
-                          act_dtype=torch.float32, delta_std=0.5):
-    """Config 0/1/2 distributions: u, z, B, C ~ N(0,1); delta ~ N(0, delta_std^2);
-    delta_bias ~ U(log(e^0.001-1), log(e^0.1-1)); A[d, n] = -(n+1); D ~ N(0,1);
-    dout ~ N(0,1).  Generated in fp32 on the CPU, then cast (activations and
-    B/C to ``act_dtype``; A, D, delta_bias stay fp32)."""
-    g = torch.Generator().manual_seed(seed)
-    u = torch.randn(batch, dim, length, generator=g)
-    delta = torch.randn(batch, dim, length, generator=g) * delta_std
-    lo, hi = _softplus_inv(0.001), _softplus_inv(0.1)
-    delta_bias = torch.rand(dim, generator=g) * (hi - lo) + lo
-    A = -torch.arange(1, dstate + 1, dtype=torch.float32).repeat(dim, 1)
-    B = torch.randn(batch, groups, dstate, length, generator=g)
-    C = torch.randn(batch, groups, dstate, length, generator=g)
-    D = torch.randn(dim, generator=g)
-    z = torch.randn(batch, dim, length, generator=g)
-    dout = torch.randn(batch, dim, length, generator=g)
-    cast = lambda t: t.to(act_dtype)  # noqa: E731
-    return dict(u=cast(u), delta=cast(delta), A=A, B=cast(B), C=cast(C), D=D,
-                z=cast(z), delta_bias=delta_bias, dout=cast(dout))
-
-
-def ssd_inputs(batch, length, nheads, headdim, dstate, ngroups, seed=1003,
-               dtype=torch.bfloat16):
-    """Config 3 distributions: x, B, C ~ N(0,1) in ``dtype``; raw dt fp32 ~ N(0,1)
-    with dt_bias[h] = softplus^-1(u_h), u_h log-uniform on [0.001, 0.1] and
-    dt_softplus=True; A = -U(1, 16) fp32; D ~ N(0,1) per head; dy ~ N(0,1)."""
-    g = torch.Generator().manual_seed(seed)
-    x = torch.randn(batch, length, nheads, headdim, generator=g)
-    dt = torch.randn(batch, length, nheads, generator=g)
-    lu = torch.rand(nheads, generator=g) * (math.log(0.1) - math.log(0.001)) + math.log(0.001)
-    dt_bias = torch.log(torch.expm1(torch.exp(lu)))
-    A = -(torch.rand(nheads, generator=g) * 15 + 1)
-    B = torch.randn(batch, length, ngroups, dstate, generator=g)
-    C = torch.randn(batch, length, ngroups, dstate, generator=g)
-    D = torch.randn(nheads, generator=g)
-    dy = torch.randn(batch, length, nheads, headdim, generator=g)
-    return dict(x=x.to(dtype), dt=dt, A=A, B=B.to(dtype), C=C.to(dtype), D=D,
-                dt_bias=dt_bias, dy=dy.to(dtype))
-
-
-def decode_inputs(batch, nheads, headdim, dstate, ngroups, seed=1004,
-                  dtype=torch.bfloat16):
-    """Config 4 distributions: fp32 state ~ N(0,1); x, B, C ~ N(0,1) in ``dtype``;
-    dt and A as in config 3 (dt per head, dt_softplus=True); D ~ N(0,1)."""
-    g = torch.Generator().manual_seed(seed)
-    state = torch.randn(batch, nheads, headdim, dstate, generator=g)
-    x = torch.randn(batch, nheads, headdim, generator=g)
-    dt = torch.randn(batch, nheads, generator=g)
-    lu = torch.rand(nheads, generator=g) * (math.log(0.1) - math.log(0.001)) + math.log(0.001)
-    dt_bias = torch.log(torch.expm1(torch.exp(lu)))
-    A = -(torch.rand(nheads, generator=g) * 15 + 1)
-    B = torch.randn(batch, ngroups, dstate, generator=g)
-    C = torch.randn(batch, ngroups, dstate, generator=g)
-    D = torch.randn(nheads, generator=g)
-    return dict(state=state, x=x.to(dtype), dt=dt, A=A, B=B.to(dtype), C=C.to(dtype),
-                D=D, dt_bias=dt_bias)

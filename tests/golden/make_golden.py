@@ -2,7 +2,9 @@
 
 Run once in a container that holds the reference source tree:
 
-    REFERENCE_SRC=<path to metal-kernelops>/src python tests/golden/make_golden.py
+    REFERENCE_SRC=<path to metal-kernelops>/src python tests/golden/make_golden.py [names...]
+
+(names: selective_scan, mamba2_chunk, mamba2_state, path_scan; default all)
 
 It imports dbydd/metal-kernelops 0.3.0 and evaluates, on seeded CPU inputs,
 the functions the hot path is defined by:
@@ -14,6 +16,8 @@ the functions the hot path is defined by:
 * ``metal_kernelops.cv.mamba2_chunk_scan_reference`` (cv/mamba2_chunk.py:681-723)
 * ``metal_kernelops.cv.mamba2_chunk_scan``  (the CPU composition, :617-678)
 * ``metal_kernelops.cv.mamba2_state_update_reference`` (cv/mamba2_state.py:822-849)
+* ``metal_kernelops.cv.path_scan.ss2d_scan_reference`` (cv/path_scan.py:608-639)
+  and ``path_orders`` (:153-163)
 
 The outputs go to ``tests/golden/*.pt``.  The test suite never imports the
 reference; it only reads these files.
@@ -33,9 +37,10 @@ from metal_kernelops import reference as stepwise  # noqa: E402
 from metal_kernelops.cv import mamba2_chunk_scan, mamba2_chunk_scan_reference  # noqa: E402
 from metal_kernelops.cv import mamba2_state_update_reference  # noqa: E402
 from metal_kernelops.cv.path_scan import _scan_reference  # noqa: E402
+from metal_kernelops.cv.path_scan import path_orders, ss2d_scan_reference  # noqa: E402
 
 sys.path.insert(0, str(HERE.parent.parent))
-from oracle.ssm_oracle import selective_scan_inputs  # noqa: E402
+from oracle.ssm_oracle import selective_scan_inputs, ss2d_inputs  # noqa: E402
 
 torch.set_num_threads(8)
 
@@ -180,10 +185,46 @@ def decode_cases():
     return cases
 
 
+def path_scan_cases():
+    """VMamba four-path scan: the reference verifier's shapes
+    (benchmarks/verify_path_scan.py:218-238), fp64, with gradients under a
+    seeded cotangent, plus the path orders of a few maps."""
+    shapes = {
+        "fb_1x3x3x2_5x7": ((1, 3, 3, 2, 5, 7), "sum"),
+        "fb_2x16x1x8_8x8": ((2, 16, 1, 8, 8, 8), "sum"),
+        "fb_2x8x2x4_6x5": ((2, 8, 2, 4, 6, 5), "sum"),
+        "five_states": ((1, 6, 2, 5, 13, 3), "sum"),
+        "mean_merge": ((1, 4, 1, 3, 4, 5), "mean"),
+        "single_row": ((1, 4, 1, 3, 1, 7), "sum"),
+        "single_column": ((1, 4, 1, 3, 7, 1), "sum"),
+        "thirty_two_states": ((1, 4, 2, 32, 5, 7), "sum"),
+    }
+    cases = {}
+    for idx, (name, (shape, merge)) in enumerate(shapes.items()):
+        args = ss2d_inputs(*shape, seed=500 + idx, dtype=torch.float64)
+        leaves = [_leaf(t) for t in args]
+        y = ss2d_scan_reference(*leaves, merge=merge)
+        gen = torch.Generator().manual_seed(600 + idx)
+        dy = torch.randn(y.shape, generator=gen, dtype=torch.float64)
+        grads = torch.autograd.grad(y, leaves, dy)
+        cases[name] = {"inputs": dict(zip(("u", "dt", "A", "B", "C"), args)), "merge": merge,
+                       "y": y.detach(), "dy": dy, "grads": dict(zip(("u", "dt", "A", "B", "C"), grads))}
+    cases["orders"] = {(h, w): path_orders(h, w) for h, w in ((4, 3), (1, 6), (6, 1), (5, 5), (3, 4))}
+    return cases
+
+
+MAKERS = {
+    "selective_scan": selective_scan_cases,
+    "mamba2_chunk": ssd_cases,
+    "mamba2_state": decode_cases,
+    "path_scan": path_scan_cases,
+}
+
+
 def main():
-    torch.save(selective_scan_cases(), HERE / "selective_scan.pt")
-    torch.save(ssd_cases(), HERE / "mamba2_chunk.pt")
-    torch.save(decode_cases(), HERE / "mamba2_state.pt")
+    wanted = sys.argv[1:] or list(MAKERS)
+    for name in wanted:
+        torch.save(MAKERS[name](), HERE / f"{name}.pt")
     for f in sorted(HERE.glob("*.pt")):
         print(f.name, f.stat().st_size)
 

@@ -153,3 +153,92 @@ def test_finite_differences_selective_scan():
             num = (float(f(**plus)) - float(f(**minus))) / (2 * step)
             ana = float(gr.reshape(-1)[pick])
             assert abs(num - ana) <= 1e-6 * max(1.0, abs(num)), (k, pick, num, ana)
+
+
+# ---------------------------------------------------------------------------
+# VMamba four-path scan (cv/path_scan.py)
+# ---------------------------------------------------------------------------
+
+SS2D_CASES = ["fb_1x3x3x2_5x7", "fb_2x16x1x8_8x8", "fb_2x8x2x4_6x5", "five_states",
+              "mean_merge", "single_row", "single_column", "thirty_two_states"]
+SS2D_NAMES = ("u", "dt", "A", "B", "C")
+
+
+@pytest.mark.parametrize("case", SS2D_CASES)
+def test_ss2d_reference(golden, case):
+    c = golden("path_scan")[case]
+    leaves = [c["inputs"][k].clone().requires_grad_(True) for k in SS2D_NAMES]
+    y = orc.ss2d_scan_ref(*leaves, merge=c["merge"])
+    _close(y, c["y"])
+    grads = torch.autograd.grad(y, leaves, c["dy"])
+    for k, g in zip(SS2D_NAMES, grads):
+        _close(g, c["grads"][k])
+
+
+def test_ss2d_path_orders(golden):
+    for (h, w), want in golden("path_scan")["orders"].items():
+        got = orc.ss2d_path_orders(h, w)
+        assert all(torch.equal(a, b) for a, b in zip(got, want)), (h, w)
+
+
+def test_ss2d_order_cumsum_kat():
+    """A = 0, dt = 1, B = C = 1 turns every path into a cumulative sum along
+    its order (verify_path_scan.py:125-159); expected values from plain index
+    lists."""
+    for height, width in ((4, 3), (1, 6), (6, 1), (5, 5)):
+        length = height * width
+        g = torch.Generator().manual_seed(height * 31 + width)
+        values = torch.randn(1, 1, length, generator=g, dtype=torch.float64)
+        expected = torch.zeros_like(values)
+        orders = [[h * width + w for h in range(height) for w in range(width)],
+                  [h * width + w for w in range(width) for h in range(height)]]
+        orders += [o[::-1] for o in orders]
+        for order in orders:
+            idx = torch.tensor(order)
+            seq = values[0, 0].index_select(0, idx).cumsum(0)
+            back = torch.empty_like(seq)
+            back[idx] = seq
+            expected[0, 0] += back
+        shape = (1, 1, height, width)
+        got = orc.ss2d_scan_ref(values.reshape(shape), torch.ones(shape, dtype=torch.float64),
+                                torch.zeros(1, 1, dtype=torch.float64),
+                                torch.ones(1, 1, 1, height, width, dtype=torch.float64),
+                                torch.ones(1, 1, 1, height, width, dtype=torch.float64))
+        _close(got, expected.reshape(shape), 1e-12)
+
+
+def test_ss2d_matches_stepwise_loop():
+    """The four-path oracle equals the triple-loop scan run on each permuted
+    sequence (verify_path_scan.py:162-188)."""
+    u, dt, A, B, C = orc.ss2d_inputs(2, 4, 2, 3, 3, 4, seed=7, dtype=torch.float64)
+    batch, channels, height, width = u.shape
+    length = height * width
+    fu, fdt = u.reshape(batch, channels, length), dt.reshape(batch, channels, length)
+    fb, fc = B.reshape(batch, 2, 3, length), C.reshape(batch, 2, 3, length)
+    restored = []
+    for order in orc.ss2d_path_orders(height, width):
+        seq = orc.selective_scan_stepwise(fu.index_select(-1, order), fdt.index_select(-1, order), A,
+                                          fb.index_select(-1, order).contiguous(),
+                                          fc.index_select(-1, order).contiguous())
+        restored.append(fu.new_zeros(batch, channels, length).index_copy(-1, order, seq))
+    want = ((restored[0] + restored[2]) + (restored[1] + restored[3])).reshape(u.shape)
+    _close(orc.ss2d_scan_ref(u, dt, A, B, C), want, 1e-12)
+
+
+@pytest.mark.parametrize("merge", ["sum", "mean"])
+def test_ss2d_finite_differences(merge):
+    """fp64 central differences on a 2x2 map (verify_path_scan.py:191-215)."""
+    args = orc.ss2d_inputs(1, 2, 1, 2, 2, 2, seed=13, dtype=torch.float64)
+    f = lambda *a: orc.ss2d_scan_ref(*a, merge=merge)  # noqa: E731
+    leaves = [t.clone().requires_grad_(True) for t in args]
+    analytic = torch.autograd.grad(f(*leaves), leaves, torch.ones_like(leaves[0]))
+    step = 1e-6
+    for i in range(len(args)):
+        for pick in range(min(3, args[i].numel())):
+            plus = [t.clone() for t in args]
+            minus = [t.clone() for t in args]
+            plus[i].reshape(-1)[pick] += step
+            minus[i].reshape(-1)[pick] -= step
+            num = (float(f(*plus).sum()) - float(f(*minus).sum())) / (2 * step)
+            ana = float(analytic[i].reshape(-1)[pick])
+            assert abs(num - ana) <= 1e-6 * max(abs(num), 1e-9) + 1e-9, (i, pick, num, ana)

@@ -63,6 +63,8 @@ def _run_pair(inp, dtype, opts=("D", "z", "delta_bias"), softplus=True, grads=Tr
     (1, 1, 1, 16, 1),       # single step, single channel
     (2, 130, 100, 16, 1),   # several channel tiles, ragged last tile
     (1, 64, 300, 4, 2),     # dstate 4, many chunks
+    (1, 16384, 40, 16, 1),  # 16384 rows: backward launch shape 8 states x 2 lanes
+    (2, 12800, 37, 16, 2),  # 25600 rows: forward and backward 8 x 2, ragged chunk
 ])
 def test_fp32_parity(shape):
     b, d, l, n, g = shape
