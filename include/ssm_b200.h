@@ -102,7 +102,9 @@ typedef struct ssm_selective_scan_params {
     float* dC;
     float* dD;                  /* may be NULL without SSM_HAS_D    */
     float* ddelta_bias;         /* may be NULL without SSM_HAS_BIAS */
-    /* scratch for the backward's deterministic partial sums */
+    /* scratch: the backward's deterministic partial sums, and the segment
+     * states of either pass (sizes from ssm_selective_scan_sizes /
+     * ssm_selective_scan_fwd_workspace) */
     void* workspace;
     size_t workspace_bytes;
 } ssm_selective_scan_params;
@@ -110,6 +112,11 @@ typedef struct ssm_selective_scan_params {
 /* Sizes of the forward's checkpoint buffer and of the backward's workspace. */
 int ssm_selective_scan_sizes(const ssm_selective_scan_params* p,
                              size_t* checkpoint_bytes, size_t* workspace_bytes);
+/* Workspace the forward needs (passed in `workspace`): zero unless the problem
+ * is too small to fill the GPU, in which case the forward cuts the sequence
+ * into segments and keeps their states there.  No counterpart in the
+ * reference (its forward always runs three chunked passes). */
+int ssm_selective_scan_fwd_workspace(const ssm_selective_scan_params* p, size_t* workspace_bytes);
 int ssm_selective_scan_fwd(const ssm_selective_scan_params* p, void* stream);
 int ssm_selective_scan_bwd(const ssm_selective_scan_params* p, void* stream);
 

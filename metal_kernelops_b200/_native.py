@@ -33,6 +33,7 @@ CUDA_CORES = 0x200
 EXPORTS = (
     "ssm_status_string", "ssm_last_error",
     "ssm_selective_scan_sizes", "ssm_selective_scan_fwd", "ssm_selective_scan_bwd",
+    "ssm_selective_scan_fwd_workspace",
     "ssm_state_update_sizes", "ssm_state_update_fwd", "ssm_state_update_bwd",
     "ssm_state_update_bwd_noalloc",
     "ssm_chunk_scan_sizes", "ssm_chunk_scan_fwd", "ssm_chunk_scan_bwd",
@@ -131,6 +132,8 @@ def lib():
                 ctypes.POINTER(StateUpdateParams), ctypes.POINTER(_SZ)]
             handle.ssm_chunk_scan_sizes.argtypes = [
                 ctypes.POINTER(ChunkScanParams), ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]
+            handle.ssm_selective_scan_fwd_workspace.argtypes = [
+                ctypes.POINTER(SelectiveScanParams), ctypes.POINTER(_SZ)]
             handle.ssm_ss2d_scan_sizes.argtypes = [
                 ctypes.POINTER(Ss2dScanParams), ctypes.POINTER(_SZ), ctypes.POINTER(_SZ),
                 ctypes.POINTER(_SZ)]
@@ -138,7 +141,7 @@ def lib():
             handle.ssm_state_update_bwd_noalloc.argtypes = [ctypes.POINTER(StateUpdateParams),
                                                             ctypes.c_void_p]
             for name in ("ssm_selective_scan_sizes", "ssm_state_update_sizes", "ssm_chunk_scan_sizes",
-                         "ssm_ss2d_scan_sizes"):
+                         "ssm_ss2d_scan_sizes", "ssm_selective_scan_fwd_workspace"):
                 getattr(handle, name).restype = ctypes.c_int
             handle.ssm_take_kernel_error.restype = ctypes.c_int
             handle.ssm_take_kernel_error.argtypes = []

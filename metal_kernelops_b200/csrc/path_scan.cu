@@ -230,9 +230,9 @@ static ssm_selective_scan_params stacked(const ssm_ss2d_scan_params* p) {
 }
 
 struct Layout {
-    size_t su, sdt, sB, sC, A4, ypaths;          // forward (and the backward's first five)
+    size_t su, sdt, sB, sC, A4, ypaths, fscan;   // forward (and the backward's first five)
     size_t sdy, dup, ddtp, dBp, dCp, dA4, scan;  // backward
-    size_t fwd_bytes, bwd_bytes, scan_ws, ckpt;
+    size_t fwd_bytes, bwd_bytes, scan_ws, scan_fws, ckpt;
 };
 
 static int layout(const ssm_ss2d_scan_params* p, Layout& o) {
@@ -241,10 +241,11 @@ static int layout(const ssm_ss2d_scan_params* p, Layout& o) {
     const size_t bc = (size_t)p->batch * 4 * p->groups * p->dstate * L * esize(p->bc_dtype);
     const size_t bc32 = (size_t)p->batch * 4 * p->groups * p->dstate * L * 4;
     const size_t a4 = (size_t)4 * p->channels * p->dstate * 4;
-    o.scan_ws = o.ckpt = 0;
+    o.scan_ws = o.scan_fws = o.ckpt = 0;
     if (!empty_problem(p)) {
         ssm_selective_scan_params s = stacked(p);
         if (int st = ssm_selective_scan_sizes(&s, &o.ckpt, &o.scan_ws)) return st;
+        if (int st = ssm_selective_scan_fwd_workspace(&s, &o.scan_fws)) return st;
     }
     size_t off = 0;
     auto take = [&](size_t bytes) { const size_t at = off; off = align_up(off + bytes, 256); return at; };
@@ -255,6 +256,7 @@ static int layout(const ssm_ss2d_scan_params* p, Layout& o) {
     o.A4 = take(a4);
     const size_t common_end = off;
     o.ypaths = take(act);
+    o.fscan = take(o.scan_fws);
     o.fwd_bytes = off;
     off = common_end;
     o.sdy = take(act);
@@ -328,6 +330,8 @@ extern "C" int ssm_ss2d_scan_fwd(const ssm_ss2d_scan_params* p, void* stream) {
     bind_inputs(s, o, ws);
     s.y = ws + o.ypaths;
     s.checkpoints = p->checkpoints;
+    s.workspace = ws + o.fscan;
+    s.workspace_bytes = o.scan_fws;
     if (int r = ssm_selective_scan_fwd(&s, stream)) return r;
     return merge(p->act_dtype, ws + o.ypaths, p->y, p->batch * p->channels, p->channels, (int)p->height,
                  (int)p->width, p->scale, st);

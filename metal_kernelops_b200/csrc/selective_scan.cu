@@ -47,6 +47,13 @@ struct Args {
     int64_t batch, dim, length, groups, dstate, per_group;
     int64_t nchunks;      // ceil(length / kChunk)
     int64_t nct;          // channel tiles per group
+    // Sequence segments: blockIdx.x = segment * nct + channel tile.  With
+    // nseg > 1 every segment of seg_chunks chunks runs as its own CTA, starting
+    // from the state (forward) or adjoint (backward) that a summary pass and a
+    // combine over segments left in seg_x: (batch, nseg, dim, dstate) fp32.
+    int64_t nseg, seg_chunks;
+    float* seg_x;
+    float* seg_p;         // decay product over each segment, same layout
     uint32_t flags;
     int bc_dtype;
     bool fast;            // 16-byte aligned rows: asynchronous copies allowed
@@ -139,7 +146,10 @@ struct FwdLayout {
     static constexpr size_t bytes = o_ch + 2 * CPC * 4;
 };
 
-template <typename T, int NPT, int LPC>
+// SUMMARY: the segment summary pass -- run the recurrence over this CTA's
+// segment from a zero state and write the end state and the decay product
+// (no outputs, no checkpoints, C unused).  Segment s < nseg - 1 only.
+template <typename T, int NPT, int LPC, bool SUMMARY>
 __global__ void __launch_bounds__(kThreads)
 fwd_kernel(const Args a) {
     constexpr int CPW = 32 / LPC;
@@ -167,7 +177,7 @@ fwd_kernel(const Args a) {
     const int warp = tid >> 5, lane = tid & 31;
     const int cw = lane / LPC, sub = lane % LPC;
     const int c = warp * CPW + cw;
-    const int64_t ct = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int64_t ct = blockIdx.x % a.nct, seg = blockIdx.x / a.nct, g = blockIdx.y, b = blockIdx.z;
     const int64_t dl0 = ct * CPC;
     const int rows = (int)min64(CPC, a.per_group - dl0);
     const int64_t d0 = g * a.per_group + dl0;
@@ -175,9 +185,10 @@ fwd_kernel(const Args a) {
     const bool cvalid = c < rows;
     const int64_t d = d0 + c;
     const int64_t N = a.dstate, L = a.length;
-    const bool has_d = a.flags & SSM_HAS_D, has_z = a.flags & SSM_HAS_Z;
+    const bool has_d = a.flags & SSM_HAS_D, has_z = !SUMMARY && (a.flags & SSM_HAS_Z);
     const bool has_bias = a.flags & SSM_HAS_BIAS, softplus = a.flags & SSM_SOFTPLUS;
     const int64_t bg = b * a.groups + g;
+    const int64_t sx = ((b * a.nseg + seg) * a.dim + d) * N;   // this channel's segment state
     const T* ug = reinterpret_cast<const T*>(a.u);
     const T* dg = reinterpret_cast<const T*>(a.delta);
     const T* zg = reinterpret_cast<const T*>(a.z);
@@ -187,17 +198,22 @@ fwd_kernel(const Args a) {
         Dch[i] = (has_d && i < rows) ? a.D[d0 + i] : 0.0f;
         bch[i] = (has_bias && i < rows) ? a.delta_bias[d0 + i] : 0.0f;
     }
-    float2 An2[NH], x2[NH];
+    float2 An2[NH], x2[NH], p2[NH];
+    const bool from_seg = !SUMMARY && a.nseg > 1;
 #pragma unroll
     for (int j = 0; j < NH; ++j) {
         const int n = sub * NPT + 2 * j;
         An2[j] = make_float2((cvalid && n < N) ? a.A[d * N + n] : 0.0f,
                              (cvalid && n + 1 < N) ? a.A[d * N + n + 1] : 0.0f);
-        x2[j] = make_float2(0.0f, 0.0f);
+        x2[j] = make_float2((from_seg && cvalid && n < N) ? a.seg_x[sx + n] : 0.0f,
+                            (from_seg && cvalid && n + 1 < N) ? a.seg_x[sx + n + 1] : 0.0f);
+        p2[j] = make_float2(1.0f, 1.0f);
     }
 
-    const int64_t ntiles = (L + TT - 1) / TT;
-    for (int64_t tile = 0; tile < ntiles; ++tile) {
+    static_assert(TT == kChunk, "forward tiles are checkpoint chunks");
+    const int64_t tile_lo = seg * a.seg_chunks;
+    const int64_t tile_hi = min64(tile_lo + a.seg_chunks, a.nchunks);
+    for (int64_t tile = tile_lo; tile < tile_hi; ++tile) {
         const int64_t t0 = tile * TT;
         const int len = (int)min64(TT, L - t0);
         __syncthreads();                       // previous tile's readers are done
@@ -205,7 +221,7 @@ fwd_kernel(const Args a) {
         stage_act<T, CPC, TT>(rd, dg, row0, rows, L, t0, len, a.fast);
         if (has_z) stage_act<T, CPC, TT>(rz, zg, row0, rows, L, t0, len, a.fast);
         stage_bc<NP, TT>(rbc, a.B, a.bc_dtype, bg, N, L, t0, len, a.fast);
-        stage_bc<NP, TT>(rbc + NP * (TT * 4 + 16), a.C, a.bc_dtype, bg, N, L, t0, len, a.fast);
+        if (!SUMMARY) stage_bc<NP, TT>(rbc + NP * (TT * 4 + 16), a.C, a.bc_dtype, bg, N, L, t0, len, a.fast);
         cp_async_commit();
         cp_async_wait<0>();
         __syncthreads();
@@ -226,9 +242,33 @@ fwd_kernel(const Args a) {
         for (int i = tid; i < NP * TT; i += kThreads) {
             const int t = i / NP, n = i % NP;
             Bs[t * NP + n] = raw_bc(rbc, n, t, TT, a.bc_dtype);
-            Cs[t * NP + n] = raw_bc(rbc + NP * (TT * 4 + 16), n, t, TT, a.bc_dtype);
+            if (!SUMMARY) Cs[t * NP + n] = raw_bc(rbc + NP * (TT * 4 + 16), n, t, TT, a.bc_dtype);
         }
         __syncthreads();
+
+        if (SUMMARY) {
+            // the recurrence from a zero state, and the product of the decays
+            const float2* vr = dvu + c * FS;
+#pragma unroll 4
+            for (int t = 0; t < len; ++t) {
+                const float2 v = vr[t];
+                const float2 dl2 = make_float2(v.x, v.x), du2 = make_float2(v.y, v.y);
+                const float4* B4 = reinterpret_cast<const float4*>(Bs + t * NP + sub * NPT);
+#pragma unroll
+                for (int q = 0; q < NPT / 4; ++q) {
+                    const float4 bq = B4[q];
+                    const float2 a0 = __fmul2_rn(dl2, An2[2 * q]);
+                    const float2 a1 = __fmul2_rn(dl2, An2[2 * q + 1]);
+                    const float2 e0 = make_float2(exp2_mufu(a0.x), exp2_mufu(a0.y));
+                    const float2 e1 = make_float2(exp2_mufu(a1.x), exp2_mufu(a1.y));
+                    x2[2 * q] = __ffma2_rn(e0, x2[2 * q], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
+                    x2[2 * q + 1] = __ffma2_rn(e1, x2[2 * q + 1], __fmul2_rn(du2, make_float2(bq.z, bq.w)));
+                    p2[2 * q] = __fmul2_rn(p2[2 * q], e0);
+                    p2[2 * q + 1] = __fmul2_rn(p2[2 * q + 1], e1);
+                }
+            }
+            continue;
+        }
 
         if (a.ckpt != nullptr && (t0 % kChunk) == 0 && cvalid) {
             float* cp = a.ckpt + ((b * a.nchunks + t0 / kChunk) * a.dim + d) * N + sub * NPT;
@@ -294,6 +334,34 @@ fwd_kernel(const Args a) {
                 stf(dst, o0);
                 stf(dst + 1, o1);
             }
+        }
+    }
+    if (SUMMARY && cvalid) {
+#pragma unroll
+        for (int j = 0; j < NH; ++j) {
+            const int n = sub * NPT + 2 * j;
+            if (n < N) { a.seg_x[sx + n] = x2[j].x; a.seg_p[sx + n] = p2[j].x; }
+            if (n + 1 < N) { a.seg_x[sx + n + 1] = x2[j].y; a.seg_p[sx + n + 1] = p2[j].y; }
+        }
+    }
+}
+
+// State entering every segment: x_in(0) = 0, x_in(s+1) = P(s) x_in(s) + x_end(s),
+// per (batch, channel, state), in segment order.  Overwrites seg_x in place.
+__global__ void combine_fwd_kernel(const Args a) {
+    const int64_t per = a.dim * a.dstate;
+    const int64_t total = a.batch * per;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = i / per, k = i - b * per;
+        float h = 0.0f;
+        for (int64_t s = 0; s < a.nseg; ++s) {
+            const int64_t at = (b * a.nseg + s) * per + k;
+            const bool last = s + 1 == a.nseg;
+            const float loc = last ? 0.0f : a.seg_x[at];
+            const float pr = last ? 0.0f : a.seg_p[at];
+            a.seg_x[at] = h;
+            h = fmaf(pr, h, loc);
         }
     }
 }
@@ -419,7 +487,7 @@ bwd_kernel(const Args a) {
     const int warp = tid >> 5, lane = tid & 31;
     const int cw = lane / LPC, sub = lane % LPC;
     const int c = warp * CPW + cw;
-    const int64_t ct = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int64_t ct = blockIdx.x % a.nct, seg = blockIdx.x / a.nct, g = blockIdx.y, b = blockIdx.z;
     const int64_t dl0 = ct * CPC;
     const int rows = (int)min64(CPC, a.per_group - dl0);
     const int64_t d0 = g * a.per_group + dl0;
@@ -430,6 +498,8 @@ bwd_kernel(const Args a) {
     const bool has_d = a.flags & SSM_HAS_D, has_z = a.flags & SSM_HAS_Z;
     const bool has_bias = a.flags & SSM_HAS_BIAS, softplus = a.flags & SSM_SOFTPLUS;
     const int64_t bg = b * a.groups + g;
+    const int64_t bs = b * a.nseg + seg;                 // (batch, segment) row of the partials
+    const int64_t sx = (bs * a.dim + d) * N;
     // this lane's state order: slot i holds state sub*NPT + (i ^ pm)
     const int pm = Sc::mask(lane);
     const bool own = Sc::owner(lane);
@@ -449,7 +519,9 @@ bwd_kernel(const Args a) {
         const int n0 = sub * NPT + ((2 * j) ^ pm), n1 = sub * NPT + ((2 * j + 1) ^ pm);
         An2[j] = make_float2((cvalid && n0 < N) ? a.A[d * N + n0] : 0.0f,
                              (cvalid && n1 < N) ? a.A[d * N + n1] : 0.0f);
-        q2[j] = make_float2(0.0f, 0.0f);
+        // the adjoint arriving from the segments to the right (zero at the end)
+        q2[j] = make_float2((a.nseg > 1 && cvalid && n0 < N) ? a.seg_x[sx + n0] : 0.0f,
+                            (a.nseg > 1 && cvalid && n1 < N) ? a.seg_x[sx + n1] : 0.0f);
         dA2[j] = make_float2(0.0f, 0.0f);
     }
 
@@ -463,7 +535,9 @@ bwd_kernel(const Args a) {
     float* dBp = a.dB_part + (bg * a.nct + ct) * N * L;
     float* dCp = a.dC_part + (bg * a.nct + ct) * N * L;
 
-    for (int64_t tile = a.nchunks - 1; tile >= 0; --tile) {
+    const int64_t tile_lo = seg * a.seg_chunks;
+    const int64_t tile_hi = min64(tile_lo + a.seg_chunks, a.nchunks);
+    for (int64_t tile = tile_hi - 1; tile >= tile_lo; --tile) {
         const int64_t t0 = tile * K;
         const int len = (int)min64(K, L - t0);
         __syncthreads();
@@ -732,7 +806,7 @@ bwd_kernel(const Args a) {
     __syncthreads();
 
     if (cvalid) {
-        float* dap = a.dA_part + (b * a.dim + d) * N;
+        float* dap = a.dA_part + (bs * a.dim + d) * N;
 #pragma unroll
         for (int j = 0; j < NH; ++j) {
             const int n0 = sub * NPT + ((2 * j) ^ pm), n1 = sub * NPT + ((2 * j + 1) ^ pm);
@@ -741,12 +815,166 @@ bwd_kernel(const Args a) {
         }
     }
     for (int i = tid; i < rows; i += kThreads) {
-        a.dD_part[b * a.dim + d0 + i] = accD[i];
-        a.db_part[b * a.dim + d0 + i] = accb[i];
+        a.dD_part[bs * a.dim + d0 + i] = accD[i];
+        a.db_part[bs * a.dim + d0 + i] = accb[i];
     }
 }
 
-// Sum the per-CTA dB/dC partials and the per-batch dA/dD/d_bias partials.
+// ------------------------------------------------- backward segment summary --
+template <typename T, int CPC, int NP>
+struct AdjLayout {
+    static constexpr int K = kChunk;
+    static constexpr int FS = K + 1;
+    static constexpr size_t o_raw = 0;                                        // [3][CPC][K] T
+    static constexpr size_t o_rbc = o_raw + 3 * CPC * K * sizeof(T);          // [NP][K*4+16] B
+    static constexpr size_t o_dv = o_rbc + NP * (K * 4 + 16);                 // [CPC][FS] float2
+    static constexpr size_t o_c = o_dv + (size_t)CPC * FS * 8;                // [K][NP] float
+    static constexpr size_t o_ch = o_c + (size_t)K * NP * 4;                  // [CPC] float
+    static constexpr size_t bytes = o_ch + CPC * 4;
+};
+
+// Segment s >= 1: run the adjoint recurrence of the scan backward over the
+// segment, from a zero adjoint at its end, q <- a_t (g_t C_t + q) with
+// a_t = exp(delta'_t A) and g_t the gradient reaching the scan output (dout
+// times the silu(z) gate); write the adjoint leaving the segment at its start
+// and the product of the decays.
+template <typename T, int NPT, int LPC>
+__global__ void __launch_bounds__(kThreads)
+adj_kernel(const Args a) {
+    constexpr int CPW = 32 / LPC;
+    constexpr int CPC = CPW * kWarps;
+    constexpr int NP = NPT * LPC;
+    constexpr int NH = NPT / 2;
+    constexpr int K = kChunk;
+    constexpr int FS = K + 1;
+    constexpr int HALF = K / 2;
+    using Lay = AdjLayout<T, CPC, NP>;
+
+    extern __shared__ __align__(16) unsigned char smem[];
+    T* rd = reinterpret_cast<T*>(smem + Lay::o_raw);
+    T* rg = rd + CPC * K;
+    T* rz = rd + 2 * CPC * K;
+    unsigned char* rbc = smem + Lay::o_rbc;
+    float2* dv = reinterpret_cast<float2*>(smem + Lay::o_dv);     // (delta' log2e, g)
+    float* Cs = reinterpret_cast<float*>(smem + Lay::o_c);
+    float* bch = reinterpret_cast<float*>(smem + Lay::o_ch);
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int cw = lane / LPC, sub = lane % LPC;
+    const int c = warp * CPW + cw;
+    const int64_t ct = blockIdx.x % a.nct, seg = blockIdx.x / a.nct + 1, g = blockIdx.y, b = blockIdx.z;
+    const int64_t dl0 = ct * CPC;
+    const int rows = (int)min64(CPC, a.per_group - dl0);
+    const int64_t d0 = g * a.per_group + dl0;
+    const int64_t row0 = b * a.dim + d0;
+    const bool cvalid = c < rows;
+    const int64_t d = d0 + c;
+    const int64_t N = a.dstate, L = a.length;
+    const bool has_z = a.flags & SSM_HAS_Z;
+    const bool has_bias = a.flags & SSM_HAS_BIAS, softplus = a.flags & SSM_SOFTPLUS;
+    const int64_t bg = b * a.groups + g;
+    const int64_t sx = ((b * a.nseg + seg) * a.dim + d) * N;
+    const T* dg = reinterpret_cast<const T*>(a.delta);
+    const T* gg = reinterpret_cast<const T*>(a.dout);
+    const T* zg = reinterpret_cast<const T*>(a.z);
+
+    for (int i = tid; i < CPC; i += kThreads) bch[i] = (has_bias && i < rows) ? a.delta_bias[d0 + i] : 0.0f;
+    float2 An2[NH], q2[NH], p2[NH];
+#pragma unroll
+    for (int j = 0; j < NH; ++j) {
+        const int n = sub * NPT + 2 * j;
+        An2[j] = make_float2((cvalid && n < N) ? a.A[d * N + n] : 0.0f,
+                             (cvalid && n + 1 < N) ? a.A[d * N + n + 1] : 0.0f);
+        q2[j] = make_float2(0.0f, 0.0f);
+        p2[j] = make_float2(1.0f, 1.0f);
+    }
+    const int64_t tile_lo = seg * a.seg_chunks;
+    const int64_t tile_hi = min64(tile_lo + a.seg_chunks, a.nchunks);
+    for (int64_t tile = tile_hi - 1; tile >= tile_lo; --tile) {
+        const int64_t t0 = tile * K;
+        const int len = (int)min64(K, L - t0);
+        __syncthreads();
+        stage_act<T, CPC, K>(rd, dg, row0, rows, L, t0, len, a.fast);
+        stage_act<T, CPC, K>(rg, gg, row0, rows, L, t0, len, a.fast);
+        if (has_z) stage_act<T, CPC, K>(rz, zg, row0, rows, L, t0, len, a.fast);
+        stage_bc<NP, K>(rbc, a.C, a.bc_dtype, bg, N, L, t0, len, a.fast);
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+        for (int i = tid; i < CPC * HALF; i += kThreads) {
+            const int cc = i / HALF, t = 2 * (i % HALF);
+            const float2 dr = Io2<T>::ld(&rd[cc * K + t]);
+            float2 go = Io2<T>::ld(&rg[cc * K + t]);
+            float d0v = dr.x + bch[cc], d1v = dr.y + bch[cc];
+            if (softplus) {
+                d0v = softplus_fast(d0v);
+                d1v = softplus_fast(d1v);
+            }
+            if (has_z) {
+                const float2 zr = Io2<T>::ld(&rz[cc * K + t]);
+                go.x *= zr.x * sigmoid_fast(zr.x);
+                go.y *= zr.y * sigmoid_fast(zr.y);
+            }
+            dv[cc * FS + t] = make_float2(d0v * kLog2e, go.x);
+            dv[cc * FS + t + 1] = make_float2(d1v * kLog2e, go.y);
+        }
+        for (int i = tid; i < NP * K; i += kThreads) {
+            const int t = i / NP, n = i % NP;
+            Cs[t * NP + n] = raw_bc(rbc, n, t, K, a.bc_dtype);
+        }
+        __syncthreads();
+        const float2* vr = dv + c * FS;
+#pragma unroll 4
+        for (int t = len - 1; t >= 0; --t) {
+            const float2 v = vr[t];
+            const float2 dl2 = make_float2(v.x, v.x), g2 = make_float2(v.y, v.y);
+            const float4* C4 = reinterpret_cast<const float4*>(Cs + t * NP + sub * NPT);
+#pragma unroll
+            for (int q = 0; q < NPT / 4; ++q) {
+                const float4 cq = C4[q];
+                const float2 a0 = __fmul2_rn(dl2, An2[2 * q]);
+                const float2 a1 = __fmul2_rn(dl2, An2[2 * q + 1]);
+                const float2 e0 = make_float2(exp2_mufu(a0.x), exp2_mufu(a0.y));
+                const float2 e1 = make_float2(exp2_mufu(a1.x), exp2_mufu(a1.y));
+                q2[2 * q] = __fmul2_rn(__ffma2_rn(g2, make_float2(cq.x, cq.y), q2[2 * q]), e0);
+                q2[2 * q + 1] = __fmul2_rn(__ffma2_rn(g2, make_float2(cq.z, cq.w), q2[2 * q + 1]), e1);
+                p2[2 * q] = __fmul2_rn(p2[2 * q], e0);
+                p2[2 * q + 1] = __fmul2_rn(p2[2 * q + 1], e1);
+            }
+        }
+    }
+    if (cvalid) {
+#pragma unroll
+        for (int j = 0; j < NH; ++j) {
+            const int n = sub * NPT + 2 * j;
+            if (n < N) { a.seg_x[sx + n] = q2[j].x; a.seg_p[sx + n] = p2[j].x; }
+            if (n + 1 < N) { a.seg_x[sx + n + 1] = q2[j].y; a.seg_p[sx + n + 1] = p2[j].y; }
+        }
+    }
+}
+
+// Adjoint arriving at the end of every segment: q_in(nseg-1) = 0,
+// q_in(s-1) = P(s) q_in(s) + q_out(s), in reverse segment order.  Overwrites
+// seg_x in place.
+__global__ void combine_bwd_kernel(const Args a) {
+    const int64_t per = a.dim * a.dstate;
+    const int64_t total = a.batch * per;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = i / per, k = i - b * per;
+        float q = 0.0f;
+        for (int64_t s = a.nseg - 1; s >= 0; --s) {
+            const int64_t at = (b * a.nseg + s) * per + k;
+            const float r = s == 0 ? 0.0f : a.seg_x[at];
+            const float pr = s == 0 ? 0.0f : a.seg_p[at];
+            a.seg_x[at] = q;
+            q = fmaf(pr, q, r);
+        }
+    }
+}
+
+// Sum the per-CTA dB/dC partials and the per-(batch, segment) dA/dD/d_bias partials.
 __global__ void reduce_kernel(const Args a, float* dB, float* dC, float* dA, float* dD, float* db) {
     const int64_t N = a.dstate, L = a.length;
     const int64_t nbc = a.batch * a.groups * N * L;
@@ -767,7 +995,7 @@ __global__ void reduce_kernel(const Args a, float* dB, float* dC, float* dA, flo
         } else if (i < nbc + nda) {
             const int64_t k = i - nbc;
             float s = 0.0f;
-            for (int64_t bb = 0; bb < a.batch; ++bb) s += a.dA_part[bb * nda + k];
+            for (int64_t bb = 0; bb < a.batch * a.nseg; ++bb) s += a.dA_part[bb * nda + k];
             dA[k] = s;
         } else {
             const int64_t k = i - nbc - nda;
@@ -775,7 +1003,7 @@ __global__ void reduce_kernel(const Args a, float* dB, float* dC, float* dA, flo
             const int64_t ch = is_d ? k : k - a.dim;
             const float* src = is_d ? a.dD_part : a.db_part;
             float s = 0.0f;
-            for (int64_t bb = 0; bb < a.batch; ++bb) s += src[bb * a.dim + ch];
+            for (int64_t bb = 0; bb < a.batch * a.nseg; ++bb) s += src[bb * a.dim + ch];
             float* dst = is_d ? dD : db;
             if (dst) dst[ch] = s;
         }
@@ -862,26 +1090,86 @@ static void make_args(const ssm_selective_scan_params* p, int cpc, Args& a) {
     a.y = p->y; a.ckpt = p->checkpoints;
     a.dout = p->dout; a.du = p->du; a.ddelta = p->ddelta; a.dz = p->dz;
     a.dB_part = a.dC_part = a.dA_part = a.dD_part = a.db_part = nullptr;
+    a.nseg = 1;
+    a.seg_chunks = a.nchunks;
+    a.seg_x = a.seg_p = nullptr;
 }
 
-struct WsLayout { size_t bc, da, dd, total; };
-static WsLayout ws_layout(const ssm_selective_scan_params* p, int64_t nct) {
+// ---------------------------------------------------- sequence segments ----
+// A CTA walks its channels' whole sequence, and its time is set by that
+// dependent chain, not by how many CTAs share the SM.  When batch x dim gives
+// fewer CTAs than half of the GPU's resident slots, the sequence is cut into
+// segments of at least kMinSegChunks chunks so that about one full wave runs;
+// each segment costs one extra summary pass over its steps.
+constexpr int64_t kMinSegChunks = 4;
+constexpr int kFwdPerSm = 6;   // resident forward CTAs per SM (registers / shared memory)
+constexpr int kBwdPerSm = 3;   // resident backward CTAs per SM
+
+static int64_t sm_count() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+        cudaGetLastError();   // no device here: clear the error, assume a B200
+        n = 148;
+    }
+    return n;
+}
+
+struct SegPlan { int64_t nseg, seg_chunks; };
+static SegPlan plan_segments(int64_t base_ctas, int64_t nchunks, int per_sm) {
+    const int64_t slots = sm_count() * per_sm;
+    if (base_ctas <= 0 || base_ctas * 2 > slots || nchunks < 2 * kMinSegChunks) return {1, nchunks};
+    const int64_t want = ceil_div(slots, base_ctas);
+    const int64_t sc = max64(ceil_div(nchunks, want), kMinSegChunks);
+    return {ceil_div(nchunks, sc), sc};
+}
+
+static SegPlan fwd_plan(const ssm_selective_scan_params* p, const Cfg& c) {
+    const int64_t nct = ceil_div(p->dim / p->groups, 32 / c.lpc * kWarps);
+    return plan_segments(nct * p->groups * p->batch, ceil_div(p->length, kChunk), kFwdPerSm);
+}
+static SegPlan bwd_plan(const ssm_selective_scan_params* p, const Cfg& c) {
+    const int64_t nct = ceil_div(p->dim / p->groups, 32 / c.lpc * kWarps);
+    return plan_segments(nct * p->groups * p->batch, ceil_div(p->length, kChunk), kBwdPerSm);
+}
+
+// seg_x and seg_p of a plan: (batch, nseg, dim, dstate) fp32 each
+static size_t seg_bytes(const ssm_selective_scan_params* p, const SegPlan& s) {
+    return s.nseg > 1 ? align_up((size_t)(p->batch * s.nseg * p->dim * p->dstate) * 4, 256) : 0;
+}
+
+struct WsLayout { size_t bc, da, dd, sg, total; };
+static WsLayout ws_layout(const ssm_selective_scan_params* p, int64_t nct, const SegPlan& sp) {
     WsLayout w;
     w.bc = align_up((size_t)(p->batch * p->groups * nct * p->dstate * p->length) * 4, 256);
-    w.da = align_up((size_t)(p->batch * p->dim * p->dstate) * 4, 256);
-    w.dd = align_up((size_t)(p->batch * p->dim) * 4, 256);
-    w.total = 2 * w.bc + w.da + 2 * w.dd;
+    w.da = align_up((size_t)(p->batch * sp.nseg * p->dim * p->dstate) * 4, 256);
+    w.dd = align_up((size_t)(p->batch * sp.nseg * p->dim) * 4, 256);
+    w.sg = seg_bytes(p, sp);
+    w.total = 2 * w.bc + w.da + 2 * w.dd + 2 * w.sg;
     return w;
+}
+
+static int combine_blocks(const Args& a) {
+    return (int)min64(ceil_div(a.batch * a.dim * a.dstate, 256), 148 * 8);
 }
 
 template <typename T, int NPT, int LPC>
 static int launch_fwd(const Args& a, cudaStream_t st) {
     constexpr int CPC = 32 / LPC * kWarps;
     const size_t sm = FwdLayout<T, CPC, NPT * LPC>::bytes;
-    auto k = fwd_kernel<T, NPT, LPC>;
+    if (a.nseg > 1) {
+        auto ks = fwd_kernel<T, NPT, LPC, true>;
+        if (cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
+            return check_launch("selective_scan fwd summary: smem attribute");
+        ks<<<dim3((unsigned)(a.nct * (a.nseg - 1)), (unsigned)a.groups, (unsigned)a.batch), kThreads, sm, st>>>(a);
+        if (int s = check_launch("selective_scan fwd summary")) return s;
+        combine_fwd_kernel<<<combine_blocks(a), 256, 0, st>>>(a);
+        if (int s = check_launch("selective_scan fwd combine")) return s;
+    }
+    auto k = fwd_kernel<T, NPT, LPC, false>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
         return check_launch("selective_scan fwd: smem attribute");
-    dim3 grid((unsigned)a.nct, (unsigned)a.groups, (unsigned)a.batch);
+    dim3 grid((unsigned)(a.nct * a.nseg), (unsigned)a.groups, (unsigned)a.batch);
     k<<<grid, kThreads, sm, st>>>(a);
     return check_launch("selective_scan fwd");
 }
@@ -889,11 +1177,21 @@ static int launch_fwd(const Args& a, cudaStream_t st) {
 template <typename T, int NPT, int LPC>
 static int launch_bwd(const Args& a, cudaStream_t st) {
     constexpr int CPC = 32 / LPC * kWarps;
+    if (a.nseg > 1) {
+        const size_t sa = AdjLayout<T, CPC, NPT * LPC>::bytes;
+        auto ka = adj_kernel<T, NPT, LPC>;
+        if (cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sa) != cudaSuccess)
+            return check_launch("selective_scan bwd summary: smem attribute");
+        ka<<<dim3((unsigned)(a.nct * (a.nseg - 1)), (unsigned)a.groups, (unsigned)a.batch), kThreads, sa, st>>>(a);
+        if (int s = check_launch("selective_scan bwd summary")) return s;
+        combine_bwd_kernel<<<combine_blocks(a), 256, 0, st>>>(a);
+        if (int s = check_launch("selective_scan bwd combine")) return s;
+    }
     const size_t sm = BwdLayout<T, CPC, NPT * LPC, NPT>::bytes;
     auto k = bwd_kernel<T, NPT, LPC>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
         return check_launch("selective_scan bwd: smem attribute");
-    dim3 grid((unsigned)a.nct, (unsigned)a.groups, (unsigned)a.batch);
+    dim3 grid((unsigned)(a.nct * a.nseg), (unsigned)a.groups, (unsigned)a.batch);
     k<<<grid, kThreads, sm, st>>>(a);
     return check_launch("selective_scan bwd");
 }
@@ -938,7 +1236,15 @@ extern "C" int ssm_selective_scan_sizes(const ssm_selective_scan_params* p,
     const int64_t nct = ceil_div(p->dim / p->groups, 32 / cb.lpc * kWarps);
     if (checkpoint_bytes)
         *checkpoint_bytes = (size_t)(p->batch * ceil_div(p->length, kChunk) * p->dim * p->dstate) * 4;
-    if (workspace_bytes) *workspace_bytes = ws_layout(p, nct).total;
+    if (workspace_bytes) *workspace_bytes = ws_layout(p, nct, bwd_plan(p, cb)).total;
+    return SSM_OK;
+}
+
+extern "C" int ssm_selective_scan_fwd_workspace(const ssm_selective_scan_params* p, size_t* workspace_bytes) {
+    if (int s = validate(p, 0)) return s;
+    Cfg c;
+    fwd_cfg(p->dstate, p->batch * p->dim, c);
+    if (workspace_bytes) *workspace_bytes = 2 * seg_bytes(p, fwd_plan(p, c));
     return SSM_OK;
 }
 
@@ -949,6 +1255,16 @@ extern "C" int ssm_selective_scan_fwd(const ssm_selective_scan_params* p, void* 
     fwd_cfg(p->dstate, p->batch * p->dim, c);
     Args a;
     make_args(p, 32 / c.lpc * kWarps, a);
+    const SegPlan sp = fwd_plan(p, c);
+    if (sp.nseg > 1) {
+        const size_t sg = seg_bytes(p, sp);
+        if (!p->workspace || p->workspace_bytes < 2 * sg)
+            return fail(SSM_ERR_WORKSPACE, "selective_scan fwd: workspace smaller than ssm_selective_scan_fwd_workspace");
+        a.nseg = sp.nseg;
+        a.seg_chunks = sp.seg_chunks;
+        a.seg_x = reinterpret_cast<float*>(p->workspace);
+        a.seg_p = reinterpret_cast<float*>(reinterpret_cast<char*>(p->workspace) + sg);
+    }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     switch (p->act_dtype) {
         case SSM_F32: return dispatch_fwd<float>(c, a, st);
@@ -974,7 +1290,8 @@ extern "C" int ssm_selective_scan_bwd(const ssm_selective_scan_params* p, void* 
     bwd_cfg(p->dstate, p->batch * p->dim, c);
     Args a;
     make_args(p, 32 / c.lpc * kWarps, a);
-    const WsLayout w = ws_layout(p, a.nct);
+    const SegPlan sp = bwd_plan(p, c);
+    const WsLayout w = ws_layout(p, a.nct, sp);
     if (!p->workspace || p->workspace_bytes < w.total)
         return fail(SSM_ERR_WORKSPACE, "selective_scan bwd: workspace too small");
     char* ws = reinterpret_cast<char*>(p->workspace);
@@ -983,6 +1300,12 @@ extern "C" int ssm_selective_scan_bwd(const ssm_selective_scan_params* p, void* 
     a.dA_part = reinterpret_cast<float*>(ws + 2 * w.bc);
     a.dD_part = reinterpret_cast<float*>(ws + 2 * w.bc + w.da);
     a.db_part = reinterpret_cast<float*>(ws + 2 * w.bc + w.da + w.dd);
+    a.nseg = sp.nseg;
+    a.seg_chunks = sp.seg_chunks;
+    if (sp.nseg > 1) {
+        a.seg_x = reinterpret_cast<float*>(ws + 2 * w.bc + w.da + 2 * w.dd);
+        a.seg_p = reinterpret_cast<float*>(ws + 2 * w.bc + w.da + 2 * w.dd + w.sg);
+    }
     int s;
     switch (p->act_dtype) {
         case SSM_F32: s = dispatch_bwd<float>(c, a, st); break;

@@ -69,10 +69,15 @@ def _fwd(u: torch.Tensor, delta: torch.Tensor, A: torch.Tensor, B: torch.Tensor,
          save: bool) -> tuple[torch.Tensor, torch.Tensor]:
     p = _params(u, delta, A, B, C, D, z, delta_bias, softplus)
     ck_bytes, _ = _sizes(p)
+    fw = nat._SZ()
+    nat.check(nat.lib().ssm_selective_scan_fwd_workspace(p, fw), "selective_scan")
     y = torch.empty_like(u)
     ckpt = torch.empty(ck_bytes // 4 if save else 0, dtype=torch.float32, device=u.device)
+    ws = torch.empty(fw.value, dtype=torch.uint8, device=u.device) if fw.value else None
     p.y = y.data_ptr()
     p.checkpoints = ckpt.data_ptr() if save and ckpt.numel() else None
+    if ws is not None:
+        p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
     nat.check(nat.lib().ssm_selective_scan_fwd(p, nat.stream_of(u)), "selective_scan")
     return y, ckpt
 

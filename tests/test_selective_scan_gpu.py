@@ -212,3 +212,22 @@ def test_errors():
     with pytest.raises(ValueError):   # dstate above the supported maximum
         mk.selective_scan(big, big, torch.zeros(4, 65, device="cuda"),
                           torch.zeros(1, 1, 65, 8, device="cuda"), torch.zeros(1, 1, 65, 8, device="cuda"))
+
+
+@pytest.mark.parametrize("shape,dtype", [
+    ((1, 8, 2000, 16, 1), torch.float32),     # one channel tile: 32 segments per pass
+    ((2, 24, 1999, 16, 3), torch.float32),    # ragged last chunk and segment, 3 groups
+    ((1, 4, 515, 32, 1), torch.float32),      # 32 states
+    ((1, 40, 1500, 16, 1), torch.bfloat16),
+])
+def test_sequence_segments(shape, dtype):
+    """Small batch x dim with long sequences: the kernels cut the sequence into
+    segments (a summary pass, a combine over segments, then every segment from
+    its entering state / adjoint).  Same oracle and tolerances as above."""
+    b, d, l, n, g = shape
+    inp = orc.selective_scan_inputs(b, d, l, n, g, seed=70 + l, act_dtype=dtype)
+    _run_pair(inp, dtype)
+    # bare scan: without the softplus the raw delta must stay positive, or
+    # exp(delta * A) overflows over a long sequence (in the oracle too)
+    bare = dict(inp, delta=(inp["delta"].float().abs() * 0.1 + 1e-3).to(dtype))
+    _run_pair(bare, dtype, opts=(), softplus=False)
