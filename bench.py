@@ -49,6 +49,8 @@ SSD_CONFIG = dict(batch=8, length=8192, nheads=80, headdim=64, dstate=128, ngrou
 DECODE_CONFIG = dict(batch=256, nheads=80, headdim=64, dstate=128, ngroups=8, seed=1004)
 # the reference's largest timed ss2d shape (measured/path_scan.json "b1_d96_56x56")
 SS2D_CONFIG = dict(batch=1, channels=96, groups=1, dstate=16, height=56, width=56, seed=1005)
+# the convolution in front of the scan at BASELINE config 2's layer shape
+CONV_CONFIG = dict(batch=16, channels=5120, length=4096, width=4, activation="silu", seed=1006)
 
 
 def _peaks():
@@ -486,6 +488,57 @@ def run_ss2d(args, world, rank, device):
     }
 
 
+def run_conv1d(args, world, rank, device):
+    """Causal depthwise conv1d fwd+bwd, bf16, K=4, SiLU, at the
+    Mamba-1 layer shape of BASELINE config 2 (x = (16, 5120, 4096)) unless
+    --shape batch,channels,length overrides it; batch sharded.  HBM-bound:
+    forward reads x and writes out, backward reads x and dout and writes dx."""
+    import torch.distributed as dist
+    from metal_kernelops_b200.parallel import batch_slice
+    cfg = dict(CONV_CONFIG)
+    if args.shape:
+        cfg["batch"], cfg["channels"], cfg["length"] = (int(v) for v in args.shape.split(","))
+    rows = batch_slice(cfg["batch"], rank, world)
+    b = rows.stop - rows.start
+    g = torch.Generator(device=device).manual_seed(cfg["seed"] + rank)
+    x = torch.randn(b, cfg["channels"], cfg["length"], generator=g, device=device).to(torch.bfloat16)
+    dout = torch.randn(b, cfg["channels"], cfg["length"], generator=g, device=device).to(torch.bfloat16)
+    w = torch.randn(cfg["channels"], cfg["width"], generator=g, device=device) * 0.5
+    bias = torch.randn(cfg["channels"], generator=g, device=device)
+    ops = torch.ops.b200ssm
+
+    def fwd():
+        return ops.causal_conv1d_fwd(x, w, bias, None, True, False)
+
+    def step():
+        fwd()
+        ops.causal_conv1d_bwd(dout, x, w, bias, None, True)
+
+    ms = _timed(step, args.steps, args.warmup, world, dist)
+    fwd_ms = _timed(fwd, args.steps, args.warmup, world, dist)
+    if rank != 0:
+        return None
+    n = cfg["batch"] * cfg["channels"] * cfg["length"]
+    alg_bytes = b * cfg["channels"] * cfg["length"] * 2 * 5
+    gbs = alg_bytes / (ms / 1e3) / 1e9
+    fwd_gbs = b * cfg["channels"] * cfg["length"] * 2 * 2 / (fwd_ms / 1e3) / 1e9
+    peaks, kind = _peaks()
+    return {
+        "metric": "causal conv1d fwd+bwd B*C*L elems/s", "value": n / (ms / 1e3),
+        "unit": "elem/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16 storage, fp32 compute", "data": "synthetic (seeded normal)",
+        "config": {"workload": "causal conv1d fwd+bwd (K=4, SiLU) at the config-2 layer shape", **cfg,
+                   "parallelism": f"dp{world} (batch shard)", "l2": "x 671 MB > L2"},
+        "breakdown_ms": {"fwd": fwd_ms, "bwd": ms - fwd_ms},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"], "peak_source": kind,
+                     "fwd_frac": fwd_gbs / peaks["hbm_gbs"],
+                     "alg_bytes_per_step": alg_bytes, "traffic": None},
+        "gpu_launches": 3 * args.steps,
+    }
+
+
 def cpu_baseline_scan(cfg, threads, budget_s=15.0):
     """The oracle (reference CPU code restated) on a bounded sample: one batch
     row, a slice of channels, the full sequence; fwd + bwd with autograd."""
@@ -519,7 +572,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--op", default="scan", choices=["scan", "ssd", "decode", "ss2d"])
+    ap.add_argument("--op", default="scan", choices=["scan", "ssd", "decode", "ss2d", "conv1d"])
     ap.add_argument("--config", type=int, default=2, choices=[1, 2])
     ap.add_argument("--shape", default=None,
                     help="batch,dim,seqlen override of the config (profiling runs on small cases)")
@@ -563,7 +616,8 @@ def main():
     if args.op == "scan":
         line = run_scan(args, world, rank, device)
     else:
-        line = {"ssd": run_ssd, "decode": run_decode, "ss2d": run_ss2d}[args.op](args, world, rank, device)
+        line = {"ssd": run_ssd, "decode": run_decode, "ss2d": run_ss2d,
+                "conv1d": run_conv1d}[args.op](args, world, rank, device)
     if rank == 0 and line is not None:
         if world == 1 and not args.no_cpu_baseline and args.op == "scan":
             line["cpu_baseline"] = cpu_baseline_scan(CONFIGS[args.config], threads)

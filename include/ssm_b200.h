@@ -295,6 +295,69 @@ int ssm_ss2d_scan_sizes(const ssm_ss2d_scan_params* p, size_t* checkpoint_bytes,
 int ssm_ss2d_scan_fwd(const ssm_ss2d_scan_params* p, void* stream);
 int ssm_ss2d_scan_bwd(const ssm_ss2d_scan_params* p, void* stream);
 
+/* ------------------------------------------------------------------------- *
+ * Causal depthwise conv1d (the convolution in front of the scan).
+ *
+ * Replaces `metal_kernelops.cv.causal_conv1d_fn` and `causal_conv1d_update`
+ * (src/metal_kernelops/cv/causal_conv1d.py:610-690, :690-756): the forward
+ * kernel `causal_conv1d_fwd` (:73-150), the fused backward
+ * `causal_conv1d_bwd` + `causal_conv1d_dwfinal` (:152-340, driven by
+ * `_CausalConv1d.backward` :540-607) and the decode kernel
+ * `causal_conv1d_update` (:342-385).
+ *
+ *   x, out, dout, dx                 : (batch, channels, length), dtype
+ *   weight (channels, width), bias (channels): fp32 (the wrapper converts)
+ *   initial_state, final_state, dinitial : (batch, channels, width - 1), dtype
+ *   dweight (channels, width), dbias (channels): fp32
+ * width (K) is 1..8.  Flags: SSM_HAS_BIAS, SSM_HAS_INIT, SSM_CONV_SILU.
+ * final_state may be NULL (not written).  The backward takes a workspace of
+ * ssm_causal_conv1d_sizes bytes; dweight/dbias may be NULL (not written).
+ * ------------------------------------------------------------------------- */
+#define SSM_CONV_SILU    0x400u /* conv1d: act = SiLU */
+
+typedef struct ssm_causal_conv1d_params {
+    int64_t batch, channels, length, width;
+    int32_t dtype;              /* ssm_dtype of x, out, states and their gradients */
+    uint32_t flags;
+    const void* x;
+    const float* weight;
+    const float* bias;
+    const void* initial_state;
+    void* out;
+    void* final_state;
+    const void* dout;
+    void* dx;
+    float* dweight;
+    float* dbias;
+    void* dinitial;
+    void* workspace;
+    size_t workspace_bytes;
+} ssm_causal_conv1d_params;
+
+int ssm_causal_conv1d_sizes(const ssm_causal_conv1d_params* p, size_t* workspace_bytes);
+int ssm_causal_conv1d_fwd(const ssm_causal_conv1d_params* p, void* stream);
+int ssm_causal_conv1d_bwd(const ssm_causal_conv1d_params* p, void* stream);
+
+/* Decode: `length` (q) new tokens per (batch, channel) row against a rolling
+ * state of state_len >= width - 1 columns, updated in place to
+ * cat(state, x)[..., -state_len:].  The state is addressed through its batch
+ * and channel strides (elements; the last stride is 1), so it may be a slice
+ * of a larger cache.  x and out are contiguous (batch, channels, length); the
+ * state has the same dtype. */
+typedef struct ssm_causal_conv1d_update_params {
+    int64_t batch, channels, length, width, state_len;
+    int64_t state_stride_batch, state_stride_channel;
+    int32_t dtype;
+    uint32_t flags;             /* SSM_HAS_BIAS | SSM_CONV_SILU */
+    void* state;
+    const void* x;
+    const float* weight;
+    const float* bias;
+    void* out;
+} ssm_causal_conv1d_update_params;
+
+int ssm_causal_conv1d_update(const ssm_causal_conv1d_update_params* p, void* stream);
+
 /* Kernels that wait on an mbarrier give up after a bounded number of polls,
  * record a non-zero code in a per-device flag and return.  This reads the flag
  * of the current device (synchronising with it) and clears it; 0 means no

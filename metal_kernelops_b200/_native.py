@@ -29,6 +29,7 @@ HAS_INIT = 0x40
 HAS_DY = 0x80
 HAS_DSTATE = 0x100
 CUDA_CORES = 0x200
+CONV_SILU = 0x400
 
 EXPORTS = (
     "ssm_status_string", "ssm_last_error",
@@ -39,6 +40,8 @@ EXPORTS = (
     "ssm_chunk_scan_sizes", "ssm_chunk_scan_fwd", "ssm_chunk_scan_bwd",
     "ssm_take_kernel_error",
     "ssm_ss2d_scan_sizes", "ssm_ss2d_scan_fwd", "ssm_ss2d_scan_bwd",
+    "ssm_causal_conv1d_sizes", "ssm_causal_conv1d_fwd", "ssm_causal_conv1d_bwd",
+    "ssm_causal_conv1d_update",
 )
 
 _I64, _I32, _U32, _P, _SZ = ctypes.c_int64, ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t
@@ -98,6 +101,26 @@ class Ss2dScanParams(ctypes.Structure):
     ]
 
 
+class CausalConv1dParams(ctypes.Structure):
+    _fields_ = [
+        ("batch", _I64), ("channels", _I64), ("length", _I64), ("width", _I64),
+        ("dtype", _I32), ("flags", _U32),
+        ("x", _P), ("weight", _P), ("bias", _P), ("initial_state", _P),
+        ("out", _P), ("final_state", _P),
+        ("dout", _P), ("dx", _P), ("dweight", _P), ("dbias", _P), ("dinitial", _P),
+        ("workspace", _P), ("workspace_bytes", _SZ),
+    ]
+
+
+class CausalConv1dUpdateParams(ctypes.Structure):
+    _fields_ = [
+        ("batch", _I64), ("channels", _I64), ("length", _I64), ("width", _I64), ("state_len", _I64),
+        ("state_stride_batch", _I64), ("state_stride_channel", _I64),
+        ("dtype", _I32), ("flags", _U32),
+        ("state", _P), ("x", _P), ("weight", _P), ("bias", _P), ("out", _P),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -121,7 +144,8 @@ def lib():
             for name, struct in (("selective_scan", SelectiveScanParams),
                                  ("state_update", StateUpdateParams),
                                  ("chunk_scan", ChunkScanParams),
-                                 ("ss2d_scan", Ss2dScanParams)):
+                                 ("ss2d_scan", Ss2dScanParams),
+                                 ("causal_conv1d", CausalConv1dParams)):
                 for suffix in ("fwd", "bwd"):
                     fn = getattr(handle, f"ssm_{name}_{suffix}")
                     fn.restype = ctypes.c_int
@@ -132,6 +156,9 @@ def lib():
                 ctypes.POINTER(StateUpdateParams), ctypes.POINTER(_SZ)]
             handle.ssm_chunk_scan_sizes.argtypes = [
                 ctypes.POINTER(ChunkScanParams), ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]
+            handle.ssm_causal_conv1d_sizes.argtypes = [ctypes.POINTER(CausalConv1dParams), ctypes.POINTER(_SZ)]
+            handle.ssm_causal_conv1d_update.restype = ctypes.c_int
+            handle.ssm_causal_conv1d_update.argtypes = [ctypes.POINTER(CausalConv1dUpdateParams), ctypes.c_void_p]
             handle.ssm_selective_scan_fwd_workspace.argtypes = [
                 ctypes.POINTER(SelectiveScanParams), ctypes.POINTER(_SZ)]
             handle.ssm_ss2d_scan_sizes.argtypes = [
@@ -141,7 +168,8 @@ def lib():
             handle.ssm_state_update_bwd_noalloc.argtypes = [ctypes.POINTER(StateUpdateParams),
                                                             ctypes.c_void_p]
             for name in ("ssm_selective_scan_sizes", "ssm_state_update_sizes", "ssm_chunk_scan_sizes",
-                         "ssm_ss2d_scan_sizes", "ssm_selective_scan_fwd_workspace"):
+                         "ssm_ss2d_scan_sizes", "ssm_selective_scan_fwd_workspace",
+                         "ssm_causal_conv1d_sizes"):
                 getattr(handle, name).restype = ctypes.c_int
             handle.ssm_take_kernel_error.restype = ctypes.c_int
             handle.ssm_take_kernel_error.argtypes = []

@@ -1450,6 +1450,8 @@ int bwd(const ssm_chunk_scan_params* p, cudaStream_t s) {
 }  // namespace ssdtc
 }  // namespace ssm
 
+int ssm_conv_take_error();   // causal_conv1d.cu: the conv1d kernels' flag
+
 extern "C" int ssm_take_kernel_error(void) {
     int v = 0;
     const cudaError_t e = cudaMemcpyFromSymbol(&v, ssm::ssdtc::g_kernel_error, sizeof(int));
@@ -1458,5 +1460,6 @@ extern "C" int ssm_take_kernel_error(void) {
         const int zero = 0;
         cudaMemcpyToSymbol(ssm::ssdtc::g_kernel_error, &zero, sizeof(int));
     }
-    return v;
+    const int c = ssm_conv_take_error();
+    return v ? v : c;
 }

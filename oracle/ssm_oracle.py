@@ -20,6 +20,10 @@ reference's does:
 * ``ss2d_scan_ref``            <- ``src/metal_kernelops/cv/path_scan.py:608-639``
   (``ss2d_scan_reference``: four index-arithmetic path orders over
   ``scan_functional``, merged as (p0 + p2) + (p1 + p3))
+* ``causal_conv1d_ref``        <- ``src/metal_kernelops/cv/causal_conv1d.py:480-518``
+  (explicit taps over ``cat(initial_state, x)``, bias, SiLU, final state)
+* ``causal_conv1d_update_ref`` <- ``src/metal_kernelops/cv/causal_conv1d.py:657-670``
+  (``_update_aten``: the decode step against a rolling state, in place)
 * ``ssd_minimal_discrete``     <- ``benchmarks/verify_mamba2_chunk.py:185-216``
   (the published ``ssd_minimal_discrete`` listing of state-spaces/mamba, used
   by the reference as a known-answer cross-check)
@@ -48,6 +52,8 @@ __all__ = [
     "mamba2_chunk_scan_composition",
     "mamba2_state_update_ref",
     "ssd_minimal_discrete",
+    "causal_conv1d_ref",
+    "causal_conv1d_update_ref",
     "ss2d_path_orders",
     "ss2d_scan_ref",
     "ss2d_inputs",
@@ -150,6 +156,59 @@ def selective_scan_ref(u, dt, A, B, C, D=None, z=None, delta_bias=None,
     if z is not None:
         out = out * F.silu(z)
     return out
+
+
+# ---------------------------------------------------------------------------
+# causal depthwise conv1d
+# ---------------------------------------------------------------------------
+
+def causal_conv1d_ref(x, weight, bias=None, activation=None, initial_state=None,
+                      return_final_state=False):
+    """Explicit-tap causal depthwise conv1d (``causal_conv1d_ref``,
+    cv/causal_conv1d.py:480-518): arithmetic in ``weight.dtype``, result in
+    ``x.dtype``, SiLU after the cast, final state = last K-1 columns of
+    ``cat(initial_state, x)``.  Differentiable."""
+    if weight.dim() == 3:
+        weight = weight[:, 0, :]
+    channels, width = weight.shape
+    taps = width - 1
+    length = x.shape[-1]
+    out_dtype, compute = x.dtype, weight.dtype
+    work = x.to(compute)
+    if initial_state is not None:
+        work = torch.cat([initial_state.to(compute), work], dim=-1)
+    else:
+        work = F.pad(work, (taps, 0))
+    out = None
+    for j in range(width):
+        term = work[..., j:j + length] * weight[:, j].view(1, channels, 1)
+        out = term if out is None else out + term
+    if bias is not None:
+        out = out + bias.to(compute).view(1, channels, 1)
+    final = work[..., length:].to(out_dtype) if return_final_state else None
+    out = out.to(out_dtype)
+    if activation is not None:
+        out = F.silu(out)
+    return (out, final) if return_final_state else out
+
+
+def causal_conv1d_update_ref(x, state, weight, bias=None, activation=None):
+    """Decode step (``_update_aten``, cv/causal_conv1d.py:657-670): convolve
+    ``cat(state, x)``, keep the last q outputs, and overwrite ``state`` in place
+    with the last ``s`` columns.  x is (batch, channels, q)."""
+    if weight.dim() == 3:
+        weight = weight[:, 0, :]
+    channels = weight.shape[0]
+    length = x.shape[-1]
+    compute = weight.dtype
+    joined = torch.cat([state.to(compute), x.to(compute)], dim=-1)
+    shift = bias.to(compute) if bias is not None else None
+    out = F.conv1d(joined, weight.unsqueeze(1), shift, groups=channels)
+    state.copy_(joined[..., -state.shape[-1]:])
+    out = out[..., -length:]
+    if activation is not None:
+        out = F.silu(out)
+    return out.to(x.dtype)
 
 
 # ---------------------------------------------------------------------------

@@ -4,7 +4,8 @@ Run once in a container that holds the reference source tree:
 
     REFERENCE_SRC=<path to metal-kernelops>/src python tests/golden/make_golden.py [names...]
 
-(names: selective_scan, mamba2_chunk, mamba2_state, path_scan; default all)
+(names: selective_scan, mamba2_chunk, mamba2_state, path_scan, causal_conv1d;
+default all)
 
 It imports dbydd/metal-kernelops 0.3.0 and evaluates, on seeded CPU inputs,
 the functions the hot path is defined by:
@@ -18,6 +19,8 @@ the functions the hot path is defined by:
 * ``metal_kernelops.cv.mamba2_state_update_reference`` (cv/mamba2_state.py:822-849)
 * ``metal_kernelops.cv.path_scan.ss2d_scan_reference`` (cv/path_scan.py:608-639)
   and ``path_orders`` (:153-163)
+* ``metal_kernelops.cv.causal_conv1d.causal_conv1d_ref`` (cv/causal_conv1d.py:480-518)
+  and ``_update_aten`` (:657-670)
 
 The outputs go to ``tests/golden/*.pt``.  The test suite never imports the
 reference; it only reads these files.
@@ -38,6 +41,7 @@ from metal_kernelops.cv import mamba2_chunk_scan, mamba2_chunk_scan_reference  #
 from metal_kernelops.cv import mamba2_state_update_reference  # noqa: E402
 from metal_kernelops.cv.path_scan import _scan_reference  # noqa: E402
 from metal_kernelops.cv.path_scan import path_orders, ss2d_scan_reference  # noqa: E402
+from metal_kernelops.cv import causal_conv1d as _cc  # noqa: E402
 
 sys.path.insert(0, str(HERE.parent.parent))
 from oracle.ssm_oracle import selective_scan_inputs, ss2d_inputs  # noqa: E402
@@ -213,11 +217,67 @@ def path_scan_cases():
     return cases
 
 
+def causal_conv1d_cases():
+    """The reference verifier's forward/gradient cases (benchmarks/
+    verify_causal_conv1d.py:171-182, with fewer channels so the fixture stays
+    small) and update cases (:185-193), fp64."""
+    cases = {}
+    shapes = {  # name: batch, channels, length, K, activation, initial state
+        "decode_1x128": (1, 128, 1, 4, "silu", True),
+        "short_2x64x16": (2, 64, 16, 4, "silu", False),
+        "prefill_1x8x300": (1, 8, 300, 4, "silu", True),
+        "prefill_2x8x129": (2, 8, 129, 4, None, False),
+        "narrow_2x8x200_k8": (2, 8, 200, 8, None, False),
+        "k1_2x16x33": (2, 16, 33, 1, None, True),
+        "k2_3x8x5": (3, 8, 5, 2, "silu", True),
+        "short_below_taps": (2, 8, 2, 4, "silu", True),
+    }
+    for idx, (name, (b, c, l, k, act, has_state)) in enumerate(shapes.items()):
+        g = torch.Generator().manual_seed(700 + idx)
+        x = torch.randn(b, c, l, generator=g, dtype=torch.float64)
+        w = torch.randn(c, 1, k, generator=g, dtype=torch.float64) * 0.5
+        bias = torch.randn(c, generator=g, dtype=torch.float64)
+        init = torch.randn(b, c, k - 1, generator=g, dtype=torch.float64) if has_state else None
+        leaves = [_leaf(t) for t in (x, w, bias, init)]
+        out, final = _cc.causal_conv1d_ref(leaves[0], leaves[1], leaves[2], act, leaves[3], True)
+        dout = torch.randn(out.shape, generator=g, dtype=torch.float64)
+        dfinal = torch.randn(final.shape, generator=g, dtype=torch.float64)
+        present = [t for t in leaves if t is not None]
+        grads = torch.autograd.grad((out * dout).sum() + (final * dfinal).sum(), present,
+                                    allow_unused=True)
+        names = [n for n, t in zip(("x", "weight", "bias", "initial_state"), leaves) if t is not None]
+        cases[name] = {"inputs": {"x": x, "weight": w, "bias": bias, "initial_state": init},
+                       "activation": act, "out": out.detach().clone(), "final": final.detach().clone(),
+                       "dout": dout, "dfinal": dfinal,
+                       "grads": {n: (gr.clone() if gr is not None else torch.zeros_like(t))
+                                 for n, gr, t in zip(names, grads, present)}}
+    updates = {  # name: batch, channels, q, K, activation, state columns
+        "update_1x256x1": (1, 256, 1, 4, "silu", 3),
+        "update_8x64x1": (8, 64, 1, 4, "silu", 3),
+        "update_1x128x4": (1, 128, 4, 4, "silu", 3),
+        "update_wide_state": (8, 64, 1, 4, "silu", 8),
+        "update_q_beyond_state": (2, 16, 5, 4, None, 3),
+        "update_k1": (2, 16, 1, 1, None, 0),
+    }
+    for idx, (name, (b, c, q, k, act, cols)) in enumerate(updates.items()):
+        g = torch.Generator().manual_seed(800 + idx)
+        x = torch.randn(b, c, q, generator=g, dtype=torch.float64)
+        state = torch.randn(b, c, cols, generator=g, dtype=torch.float64)
+        w = torch.randn(c, 1, k, generator=g, dtype=torch.float64) * 0.5
+        bias = torch.randn(c, generator=g, dtype=torch.float64)
+        st = state.clone()
+        out = _cc._update_aten(x, st, w[:, 0, :], bias, act)
+        cases[name] = {"inputs": {"x": x, "state": state, "weight": w, "bias": bias},
+                       "activation": act, "out": out.clone(), "new_state": st}
+    return cases
+
+
 MAKERS = {
     "selective_scan": selective_scan_cases,
     "mamba2_chunk": ssd_cases,
     "mamba2_state": decode_cases,
     "path_scan": path_scan_cases,
+    "causal_conv1d": causal_conv1d_cases,
 }
 
 

@@ -242,3 +242,90 @@ def test_ss2d_finite_differences(merge):
             num = (float(f(*plus).sum()) - float(f(*minus).sum())) / (2 * step)
             ana = float(analytic[i].reshape(-1)[pick])
             assert abs(num - ana) <= 1e-6 * max(abs(num), 1e-9) + 1e-9, (i, pick, num, ana)
+
+
+# ---------------------------------------------------------------------------
+# causal depthwise conv1d (cv/causal_conv1d.py)
+# ---------------------------------------------------------------------------
+
+CONV_CASES = ["decode_1x128", "short_2x64x16", "prefill_1x8x300", "prefill_2x8x129",
+              "narrow_2x8x200_k8", "k1_2x16x33", "k2_3x8x5", "short_below_taps"]
+CONV_UPDATES = ["update_1x256x1", "update_8x64x1", "update_1x128x4", "update_wide_state",
+                "update_q_beyond_state", "update_k1"]
+
+
+@pytest.mark.parametrize("case", CONV_CASES)
+def test_causal_conv1d_reference(golden, case):
+    c = golden("causal_conv1d")[case]
+    inp = c["inputs"]
+    names = [k for k in ("x", "weight", "bias", "initial_state") if inp[k] is not None]
+    leaves = {k: inp[k].clone().requires_grad_(True) for k in names}
+    out, final = orc.causal_conv1d_ref(leaves["x"], leaves["weight"], leaves["bias"], c["activation"],
+                                       leaves.get("initial_state"), True)
+    _close(out, c["out"])
+    _close(final, c["final"])
+    grads = torch.autograd.grad((out * c["dout"]).sum() + (final * c["dfinal"]).sum(),
+                                [leaves[k] for k in names], allow_unused=True)
+    for k, g in zip(names, grads):
+        _close(g if g is not None else torch.zeros_like(leaves[k]), c["grads"][k])
+
+
+@pytest.mark.parametrize("case", CONV_UPDATES)
+def test_causal_conv1d_update_reference(golden, case):
+    c = golden("causal_conv1d")[case]
+    inp = c["inputs"]
+    state = inp["state"].clone()
+    out = orc.causal_conv1d_update_ref(inp["x"], state, inp["weight"], inp["bias"], c["activation"])
+    _close(out, c["out"])
+    assert torch.equal(state, c["new_state"])
+
+
+def test_causal_conv1d_steps_match_full():
+    """Token-by-token and chunked decode reproduce the full-sequence forward and
+    its final state (verify_causal_conv1d.py:586-617), on the oracle."""
+    g = torch.Generator().manual_seed(51)
+    for batch, channels, length in ((2, 64, 9), (1, 16, 17), (3, 32, 4)):
+        w = torch.randn(channels, 1, 4, generator=g, dtype=torch.float64) * 0.5
+        bias = torch.randn(channels, generator=g, dtype=torch.float64)
+        x = torch.randn(batch, channels, length, generator=g, dtype=torch.float64)
+        state = torch.randn(batch, channels, 3, generator=g, dtype=torch.float64)
+        full, final = orc.causal_conv1d_ref(x, w, bias, "silu", state, True)
+        st = state.clone()
+        steps = torch.cat([orc.causal_conv1d_update_ref(x[..., t:t + 1], st, w, bias, "silu")
+                           for t in range(length)], dim=-1)
+        _close(steps, full, 1e-12)
+        _close(st, final, 0.0)
+        st = state.clone()
+        chunks = torch.cat([orc.causal_conv1d_update_ref(x[..., i:i + 3], st, w, bias, "silu")
+                            for i in range(0, length, 3)], dim=-1)
+        _close(chunks, full, 1e-12)
+        _close(st, final, 0.0)
+
+
+def test_causal_conv1d_finite_differences():
+    """fp64 central differences of all four inputs (verify_causal_conv1d.py:620-658)."""
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(2, 3, 7, generator=g, dtype=torch.float64)
+    w = torch.randn(3, 1, 4, generator=g, dtype=torch.float64)
+    bias = torch.randn(3, generator=g, dtype=torch.float64)
+    state = torch.randn(2, 3, 3, generator=g, dtype=torch.float64)
+    args = [x, w, bias, state]
+    leaves = [t.clone().requires_grad_(True) for t in args]
+    out, final = orc.causal_conv1d_ref(leaves[0], leaves[1], leaves[2], "silu", leaves[3], True)
+    so, sf = torch.randn(out.shape, generator=g, dtype=torch.float64), torch.randn(final.shape, generator=g, dtype=torch.float64)
+    analytic = torch.autograd.grad((out * so).sum() + (final * sf).sum(), leaves)
+
+    def loss(a):
+        o, f = orc.causal_conv1d_ref(a[0], a[1], a[2], "silu", a[3], True)
+        return float((o * so).sum() + (f * sf).sum())
+
+    eps = 1e-6
+    for i, t in enumerate(args):
+        num = torch.zeros_like(t)
+        for k in range(t.numel()):
+            plus = [a.clone() for a in args]
+            minus = [a.clone() for a in args]
+            plus[i].view(-1)[k] += eps
+            minus[i].view(-1)[k] -= eps
+            num.view(-1)[k] = (loss(plus) - loss(minus)) / (2 * eps)
+        assert float((num - analytic[i]).norm() / analytic[i].norm()) < 1e-7, i
