@@ -49,6 +49,9 @@ SSD_CONFIG = dict(batch=8, length=8192, nheads=80, headdim=64, dstate=128, ngrou
 DECODE_CONFIG = dict(batch=256, nheads=80, headdim=64, dstate=128, ngroups=8, seed=1004)
 # the reference's largest timed ss2d shape (measured/path_scan.json "b1_d96_56x56")
 SS2D_CONFIG = dict(batch=1, channels=96, groups=1, dstate=16, height=56, width=56, seed=1005)
+# the gated RMSNorm after the SSD scan at BASELINE config 3's layer shape
+# (rows = B*L = 8*8192, d_inner = 80*64, groups of d_inner / ngroups)
+GNORM_CONFIG = dict(rows=65536, features=5120, group_size=640, norm_before_gate=False, seed=1007)
 # the convolution in front of the scan at BASELINE config 2's layer shape
 CONV_CONFIG = dict(batch=16, channels=5120, length=4096, width=4, activation="silu", seed=1006)
 
@@ -539,6 +542,57 @@ def run_conv1d(args, world, rank, device):
     }
 
 
+def run_gnorm(args, world, rank, device):
+    """Gated RMSNorm fwd+bwd, bf16, gate before the norm, no bias,
+    at the Mamba-2 layer shape of BASELINE config 3; rows sharded.  HBM-bound:
+    forward reads x, z and writes out; backward reads x, z, dy and writes dx, dz."""
+    import torch.distributed as dist
+    from metal_kernelops_b200.parallel import batch_slice
+    cfg = dict(GNORM_CONFIG)
+    if args.shape:
+        cfg["rows"], cfg["features"], cfg["group_size"] = (int(v) for v in args.shape.split(","))
+    rows = batch_slice(cfg["rows"], rank, world)
+    n = rows.stop - rows.start
+    g = torch.Generator(device=device).manual_seed(cfg["seed"] + rank)
+    x = torch.randn(n, cfg["features"], generator=g, device=device).to(torch.bfloat16)
+    z = torch.randn(n, cfg["features"], generator=g, device=device).to(torch.bfloat16)
+    dy = torch.randn(n, cfg["features"], generator=g, device=device).to(torch.bfloat16)
+    w = torch.randn(cfg["features"], generator=g, device=device)
+    ops = torch.ops.b200ssm
+    gate = 2 if cfg["norm_before_gate"] else 1
+
+    def fwd():
+        return ops.gated_rmsnorm_fwd(x, w, None, z, 1e-5, cfg["group_size"], gate, True)
+
+    def step():
+        _, rstd = fwd()
+        ops.gated_rmsnorm_bwd(dy, x, w, None, z, rstd, 1e-5, cfg["group_size"], gate)
+
+    ms = _timed(step, args.steps, args.warmup, world, dist)
+    fwd_ms = _timed(fwd, args.steps, args.warmup, world, dist)
+    if rank != 0:
+        return None
+    elems = n * cfg["features"]
+    alg_bytes = elems * 2 * 8
+    gbs = alg_bytes / (ms / 1e3) / 1e9
+    peaks, kind = _peaks()
+    return {
+        "metric": "gated RMSNorm fwd+bwd rows*features elems/s",
+        "value": cfg["rows"] * cfg["features"] / (ms / 1e3),
+        "unit": "elem/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16 storage, fp32 compute", "data": "synthetic (seeded normal)",
+        "config": {"workload": "gated RMSNorm fwd+bwd at the config-3 layer shape", **cfg,
+                   "parallelism": f"dp{world} (row shard)", "l2": "x 671 MB > L2"},
+        "breakdown_ms": {"fwd": fwd_ms, "bwd": ms - fwd_ms},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"], "peak_source": kind,
+                     "fwd_frac": elems * 2 * 3 / (fwd_ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                     "alg_bytes_per_step": alg_bytes, "traffic": None},
+        "gpu_launches": 3 * args.steps,
+    }
+
+
 def cpu_baseline_scan(cfg, threads, budget_s=15.0):
     """The oracle (reference CPU code restated) on a bounded sample: one batch
     row, a slice of channels, the full sequence; fwd + bwd with autograd."""
@@ -572,7 +626,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--op", default="scan", choices=["scan", "ssd", "decode", "ss2d", "conv1d"])
+    ap.add_argument("--op", default="scan", choices=["scan", "ssd", "decode", "ss2d", "conv1d", "gnorm"])
     ap.add_argument("--config", type=int, default=2, choices=[1, 2])
     ap.add_argument("--shape", default=None,
                     help="batch,dim,seqlen override of the config (profiling runs on small cases)")
@@ -617,7 +671,7 @@ def main():
         line = run_scan(args, world, rank, device)
     else:
         line = {"ssd": run_ssd, "decode": run_decode, "ss2d": run_ss2d,
-                "conv1d": run_conv1d}[args.op](args, world, rank, device)
+                "conv1d": run_conv1d, "gnorm": run_gnorm}[args.op](args, world, rank, device)
     if rank == 0 and line is not None:
         if world == 1 and not args.no_cpu_baseline and args.op == "scan":
             line["cpu_baseline"] = cpu_baseline_scan(CONFIGS[args.config], threads)

@@ -358,6 +358,47 @@ typedef struct ssm_causal_conv1d_update_params {
 
 int ssm_causal_conv1d_update(const ssm_causal_conv1d_update_params* p, void* stream);
 
+/* ------------------------------------------------------------------------- *
+ * Gated RMSNorm (mamba's rms_norm_ref): the normalisation after the SSD scan.
+ *
+ * Replaces `metal_kernelops.cv.rmsnorm_gated`
+ * (src/metal_kernelops/cv/gated_norm.py:647-686): the fused forward and the
+ * analytic backward of `_GatedRMSNorm` (:563-644).
+ *
+ *   x, z, out, dy, dx, dz : (rows, features), dtype (z may be NULL: no gate)
+ *   weight, bias, dweight, dbias : (features,) fp32 (bias may be NULL)
+ *   rstd : (rows, features / group_size) fp32, written by the forward (may be
+ *          NULL there) and read by the backward
+ * gate: 0 none, 1 silu(z) multiplies x before the norm (norm_before_gate =
+ * False), 2 silu(z) multiplies the output (norm_before_gate = True).  Flags:
+ * SSM_HAS_BIAS.  The backward takes a workspace of ssm_gated_rmsnorm_sizes
+ * bytes; dweight/dbias may be NULL (not written).
+ * ------------------------------------------------------------------------- */
+typedef struct ssm_gated_rmsnorm_params {
+    int64_t rows, features, group_size;
+    int32_t dtype;
+    int32_t gate;
+    uint32_t flags;
+    float eps;
+    const void* x;
+    const void* z;
+    const float* weight;
+    const float* bias;
+    void* out;
+    float* rstd;
+    const void* dy;
+    void* dx;
+    void* dz;
+    float* dweight;
+    float* dbias;
+    void* workspace;
+    size_t workspace_bytes;
+} ssm_gated_rmsnorm_params;
+
+int ssm_gated_rmsnorm_sizes(const ssm_gated_rmsnorm_params* p, size_t* workspace_bytes);
+int ssm_gated_rmsnorm_fwd(const ssm_gated_rmsnorm_params* p, void* stream);
+int ssm_gated_rmsnorm_bwd(const ssm_gated_rmsnorm_params* p, void* stream);
+
 /* Kernels that wait on an mbarrier give up after a bounded number of polls,
  * record a non-zero code in a per-device flag and return.  This reads the flag
  * of the current device (synchronising with it) and clears it; 0 means no

@@ -42,6 +42,7 @@ EXPORTS = (
     "ssm_ss2d_scan_sizes", "ssm_ss2d_scan_fwd", "ssm_ss2d_scan_bwd",
     "ssm_causal_conv1d_sizes", "ssm_causal_conv1d_fwd", "ssm_causal_conv1d_bwd",
     "ssm_causal_conv1d_update",
+    "ssm_gated_rmsnorm_sizes", "ssm_gated_rmsnorm_fwd", "ssm_gated_rmsnorm_bwd",
 )
 
 _I64, _I32, _U32, _P, _SZ = ctypes.c_int64, ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t
@@ -121,6 +122,16 @@ class CausalConv1dUpdateParams(ctypes.Structure):
     ]
 
 
+class GatedRmsNormParams(ctypes.Structure):
+    _fields_ = [
+        ("rows", _I64), ("features", _I64), ("group_size", _I64),
+        ("dtype", _I32), ("gate", _I32), ("flags", _U32), ("eps", ctypes.c_float),
+        ("x", _P), ("z", _P), ("weight", _P), ("bias", _P), ("out", _P), ("rstd", _P),
+        ("dy", _P), ("dx", _P), ("dz", _P), ("dweight", _P), ("dbias", _P),
+        ("workspace", _P), ("workspace_bytes", _SZ),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -145,7 +156,8 @@ def lib():
                                  ("state_update", StateUpdateParams),
                                  ("chunk_scan", ChunkScanParams),
                                  ("ss2d_scan", Ss2dScanParams),
-                                 ("causal_conv1d", CausalConv1dParams)):
+                                 ("causal_conv1d", CausalConv1dParams),
+                                 ("gated_rmsnorm", GatedRmsNormParams)):
                 for suffix in ("fwd", "bwd"):
                     fn = getattr(handle, f"ssm_{name}_{suffix}")
                     fn.restype = ctypes.c_int
@@ -157,6 +169,7 @@ def lib():
             handle.ssm_chunk_scan_sizes.argtypes = [
                 ctypes.POINTER(ChunkScanParams), ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]
             handle.ssm_causal_conv1d_sizes.argtypes = [ctypes.POINTER(CausalConv1dParams), ctypes.POINTER(_SZ)]
+            handle.ssm_gated_rmsnorm_sizes.argtypes = [ctypes.POINTER(GatedRmsNormParams), ctypes.POINTER(_SZ)]
             handle.ssm_causal_conv1d_update.restype = ctypes.c_int
             handle.ssm_causal_conv1d_update.argtypes = [ctypes.POINTER(CausalConv1dUpdateParams), ctypes.c_void_p]
             handle.ssm_selective_scan_fwd_workspace.argtypes = [
@@ -169,7 +182,7 @@ def lib():
                                                             ctypes.c_void_p]
             for name in ("ssm_selective_scan_sizes", "ssm_state_update_sizes", "ssm_chunk_scan_sizes",
                          "ssm_ss2d_scan_sizes", "ssm_selective_scan_fwd_workspace",
-                         "ssm_causal_conv1d_sizes"):
+                         "ssm_causal_conv1d_sizes", "ssm_gated_rmsnorm_sizes"):
                 getattr(handle, name).restype = ctypes.c_int
             handle.ssm_take_kernel_error.restype = ctypes.c_int
             handle.ssm_take_kernel_error.argtypes = []

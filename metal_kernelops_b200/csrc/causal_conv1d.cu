@@ -80,35 +80,6 @@ template <typename H2, typename T> struct Vec16 {
 template <> struct Vec<__nv_bfloat16, 8> : Vec16<__nv_bfloat162, __nv_bfloat16> {};
 template <> struct Vec<__half, 8> : Vec16<__half2, __half> {};
 
-// SiLU and its derivative on the MUFU pipe, no IEEE division.  fp32 data:
-// sigmoid = rcp(1 + ex2(-a log2 e)) (two MUFU ops, ~3e-7 relative).  16-bit
-// data, whose results are rounded to 8 or 11 bits: sigmoid = (1 + tanh(a/2)) / 2
-// with PTX tanh.approx (one MUFU op, ~2^-11 relative), since the 16-bit forward
-// is otherwise issue-bound.
-__device__ __forceinline__ float tanh_mufu(float x) {
-    float y;
-    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-template <typename T>
-__device__ __forceinline__ float sigmoid_t(float a) {
-    if constexpr (sizeof(T) == 4) return sigmoid_fast(a);
-    else return fmaf(0.5f, tanh_mufu(0.5f * a), 0.5f);
-}
-template <typename T>
-__device__ __forceinline__ float silu_t(float a) {
-    if constexpr (sizeof(T) == 4) return a * sigmoid_fast(a);
-    else {
-        const float h = 0.5f * a;
-        return fmaf(h, tanh_mufu(h), h);
-    }
-}
-template <typename T>
-__device__ __forceinline__ float silu_grad_t(float a) {
-    const float s = sigmoid_t<T>(a);
-    return s * fmaf(a, 1.0f - s, 1.0f);
-}
-
 // z at x-position p of one row: the initial state left of 0, zero past L.
 template <typename T, int TAPS>
 __device__ __forceinline__ float zval(const T* xr, const T* ir, int64_t p, int64_t L) {

@@ -24,6 +24,8 @@ reference's does:
   (explicit taps over ``cat(initial_state, x)``, bias, SiLU, final state)
 * ``causal_conv1d_update_ref`` <- ``src/metal_kernelops/cv/causal_conv1d.py:657-670``
   (``_update_aten``: the decode step against a rolling state, in place)
+* ``rmsnorm_gated_ref``        <- ``src/metal_kernelops/cv/gated_norm.py:689-720``
+  (``rmsnorm_gated_reference``: mamba's ``rms_norm_ref`` in float64)
 * ``ssd_minimal_discrete``     <- ``benchmarks/verify_mamba2_chunk.py:185-216``
   (the published ``ssd_minimal_discrete`` listing of state-spaces/mamba, used
   by the reference as a known-answer cross-check)
@@ -53,6 +55,7 @@ __all__ = [
     "mamba2_state_update_ref",
     "ssd_minimal_discrete",
     "causal_conv1d_ref",
+    "rmsnorm_gated_ref",
     "causal_conv1d_update_ref",
     "ss2d_path_orders",
     "ss2d_scan_ref",
@@ -209,6 +212,31 @@ def causal_conv1d_update_ref(x, state, weight, bias=None, activation=None):
     if activation is not None:
         out = F.silu(out)
     return out.to(x.dtype)
+
+
+# ---------------------------------------------------------------------------
+# gated RMSNorm
+# ---------------------------------------------------------------------------
+
+def rmsnorm_gated_ref(x, weight, bias=None, z=None, eps=1e-5, group_size=None,
+                      norm_before_gate=True):
+    """mamba's ``rms_norm_ref`` (``rmsnorm_gated_reference``,
+    cv/gated_norm.py:689-720): gate before the mean or after the shift, biased
+    mean over groups of ``group_size``, evaluated in the inputs' dtype (call it
+    with float64 tensors).  Differentiable."""
+    features = x.shape[-1]
+    group = features if group_size is None else group_size
+    xf = x
+    if z is not None and not norm_before_gate:
+        xf = xf * F.silu(z)
+    grouped = xf.reshape(xf.shape[:-1] + (features // group, group))
+    rstd = torch.rsqrt(grouped.square().mean(-1, keepdim=True) + eps)
+    out = (grouped * rstd).reshape(xf.shape) * weight
+    if bias is not None:
+        out = out + bias
+    if z is not None and norm_before_gate:
+        out = out * F.silu(z)
+    return out
 
 
 # ---------------------------------------------------------------------------

@@ -4,8 +4,8 @@ Run once in a container that holds the reference source tree:
 
     REFERENCE_SRC=<path to metal-kernelops>/src python tests/golden/make_golden.py [names...]
 
-(names: selective_scan, mamba2_chunk, mamba2_state, path_scan, causal_conv1d;
-default all)
+(names: selective_scan, mamba2_chunk, mamba2_state, path_scan, causal_conv1d,
+gated_norm; default all)
 
 It imports dbydd/metal-kernelops 0.3.0 and evaluates, on seeded CPU inputs,
 the functions the hot path is defined by:
@@ -21,6 +21,7 @@ the functions the hot path is defined by:
   and ``path_orders`` (:153-163)
 * ``metal_kernelops.cv.causal_conv1d.causal_conv1d_ref`` (cv/causal_conv1d.py:480-518)
   and ``_update_aten`` (:657-670)
+* ``metal_kernelops.cv.gated_norm.rmsnorm_gated_reference`` (cv/gated_norm.py:689-720)
 
 The outputs go to ``tests/golden/*.pt``.  The test suite never imports the
 reference; it only reads these files.
@@ -42,6 +43,7 @@ from metal_kernelops.cv import mamba2_state_update_reference  # noqa: E402
 from metal_kernelops.cv.path_scan import _scan_reference  # noqa: E402
 from metal_kernelops.cv.path_scan import path_orders, ss2d_scan_reference  # noqa: E402
 from metal_kernelops.cv import causal_conv1d as _cc  # noqa: E402
+from metal_kernelops.cv.gated_norm import rmsnorm_gated_reference  # noqa: E402
 
 sys.path.insert(0, str(HERE.parent.parent))
 from oracle.ssm_oracle import selective_scan_inputs, ss2d_inputs  # noqa: E402
@@ -272,12 +274,51 @@ def causal_conv1d_cases():
     return cases
 
 
+def gated_norm_cases():
+    """The reference verifier's correctness cases (benchmarks/verify_gated_norm.py:
+    79-97, 121-131), with fewer rows so the fixture stays small, fp64, with
+    gradients under a seeded cotangent."""
+    shapes = {  # name: shape, group_size, bias, gate, norm_before_gate, eps
+        "whole_axis": ((4, 300), None, True, True, True, 1e-5),
+        "group_60": ((4, 300), 60, True, True, True, 1e-5),
+        "group_100_eps": ((4, 300), 100, True, True, True, 1e-6),
+        "group_150_before": ((4, 300), 150, True, True, False, 1e-5),
+        "no_bias": ((4, 300), None, False, True, True, 1e-5),
+        "no_gate": ((4, 300), None, True, False, True, 1e-5),
+        "group_60_before": ((4, 300), 60, True, True, False, 1e-5),
+        "eps_one": ((4, 300), None, True, True, True, 1.0),
+        "batched_3d": ((2, 3, 300), 100, True, True, True, 1e-5),
+        "batched_4d": ((2, 3, 2, 128), 32, True, True, True, 1e-5),
+        "narrow": ((1, 64), 16, True, True, False, 1e-5),
+        "wide_group": ((2, 2048), 1024, True, True, True, 1e-5),
+    }
+    cases = {}
+    for idx, (name, (shape, group, bias, gate, before, eps)) in enumerate(shapes.items()):
+        g = torch.Generator().manual_seed(900 + idx)
+        x = torch.randn(*shape, generator=g, dtype=torch.float64)
+        w = torch.randn(shape[-1], generator=g, dtype=torch.float64)
+        b = torch.randn(shape[-1], generator=g, dtype=torch.float64) if bias else None
+        z = torch.randn(*shape, generator=g, dtype=torch.float64) if gate else None
+        leaves = [_leaf(t) for t in (x, w, b, z)]
+        out = rmsnorm_gated_reference(leaves[0], leaves[1], leaves[2], leaves[3], eps=eps,
+                                      group_size=group, norm_before_gate=before)
+        dy = torch.randn(out.shape, generator=g, dtype=torch.float64)
+        present = [t for t in leaves if t is not None]
+        names = [n for n, t in zip(("x", "weight", "bias", "z"), leaves) if t is not None]
+        grads = torch.autograd.grad(out, present, dy)
+        cases[name] = {"inputs": {"x": x, "weight": w, "bias": b, "z": z}, "group_size": group,
+                       "norm_before_gate": before, "eps": eps, "out": out.detach().clone(),
+                       "dy": dy, "grads": {n: gr.clone() for n, gr in zip(names, grads)}}
+    return cases
+
+
 MAKERS = {
     "selective_scan": selective_scan_cases,
     "mamba2_chunk": ssd_cases,
     "mamba2_state": decode_cases,
     "path_scan": path_scan_cases,
     "causal_conv1d": causal_conv1d_cases,
+    "gated_norm": gated_norm_cases,
 }
 
 

@@ -329,3 +329,51 @@ def test_causal_conv1d_finite_differences():
             minus[i].view(-1)[k] -= eps
             num.view(-1)[k] = (loss(plus) - loss(minus)) / (2 * eps)
         assert float((num - analytic[i]).norm() / analytic[i].norm()) < 1e-7, i
+
+
+# ---------------------------------------------------------------------------
+# gated RMSNorm (cv/gated_norm.py)
+# ---------------------------------------------------------------------------
+
+GN_CASES = ["whole_axis", "group_60", "group_100_eps", "group_150_before", "no_bias", "no_gate",
+            "group_60_before", "eps_one", "batched_3d", "batched_4d", "narrow", "wide_group"]
+
+
+@pytest.mark.parametrize("case", GN_CASES)
+def test_gated_norm_reference(golden, case):
+    c = golden("gated_norm")[case]
+    inp = c["inputs"]
+    names = [k for k in ("x", "weight", "bias", "z") if inp[k] is not None]
+    leaves = {k: inp[k].clone().requires_grad_(True) for k in names}
+    out = orc.rmsnorm_gated_ref(leaves["x"], leaves["weight"], leaves.get("bias"), leaves.get("z"),
+                                eps=c["eps"], group_size=c["group_size"],
+                                norm_before_gate=c["norm_before_gate"])
+    _close(out, c["out"])
+    grads = torch.autograd.grad(out, [leaves[k] for k in names], c["dy"])
+    for k, g in zip(names, grads):
+        _close(g, c["grads"][k])
+
+
+@pytest.mark.parametrize("before", [True, False])
+def test_gated_norm_finite_differences(before):
+    """fp64 central differences of the oracle (verify_gated_norm.py:173-220)."""
+    g = torch.Generator().manual_seed(17)
+    x = torch.randn(3, 12, generator=g, dtype=torch.float64)
+    w = torch.randn(12, generator=g, dtype=torch.float64)
+    b = torch.randn(12, generator=g, dtype=torch.float64)
+    z = torch.randn(3, 12, generator=g, dtype=torch.float64)
+    args = [x, w, b, z]
+    f = lambda a: orc.rmsnorm_gated_ref(a[0], a[1], a[2], a[3], group_size=4,  # noqa: E731
+                                        norm_before_gate=before).square().sum()
+    leaves = [t.clone().requires_grad_(True) for t in args]
+    analytic = torch.autograd.grad(f(leaves), leaves)
+    eps = 1e-6
+    for i, t in enumerate(args):
+        for k in range(0, t.numel(), 5):
+            plus = [a.clone() for a in args]
+            minus = [a.clone() for a in args]
+            plus[i].view(-1)[k] += eps
+            minus[i].view(-1)[k] -= eps
+            num = (float(f(plus)) - float(f(minus))) / (2 * eps)
+            ana = float(analytic[i].view(-1)[k])
+            assert abs(num - ana) <= 1e-6 * max(1.0, abs(num)), (i, k, num, ana)
