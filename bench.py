@@ -593,6 +593,80 @@ def run_gnorm(args, world, rank, device):
     }
 
 
+BLOCK_CONFIG = dict(batch=8, length=8192, d_model=2560, nheads=80, headdim=64, dstate=128, ngroups=8,
+                    conv=4, chunk=256, seed=1008)
+
+
+def run_block(args, world, rank, device):
+    """One Mamba-2 layer, fwd + bwd + SGD step, bf16 autocast, at the shape of
+    BASELINE config 3 (d_inner = 80 x 64, state 128, 8 groups, 8 x 8192
+    tokens): in_proj (cuBLAS) -> causal conv1d + SiLU -> SSD chunk scan ->
+    gated RMSNorm -> out_proj (cuBLAS), the block of the reference's
+    integration verifier (benchmarks/verify_cv_integration.py:37-74) at layer
+    size.  Batch sharded; the metric is tokens per second."""
+    import torch.distributed as dist
+    from metal_kernelops_b200.cv import causal_conv1d_fn, mamba2_chunk_scan, rmsnorm_gated
+    from metal_kernelops_b200.parallel import batch_slice
+    cfg = dict(BLOCK_CONFIG)
+    if args.shape:
+        cfg["batch"], cfg["length"] = (int(v) for v in args.shape.split(",")[:2])
+    rows = batch_slice(cfg["batch"], rank, world)
+    b = rows.stop - rows.start
+    H, P, N, G, L = cfg["nheads"], cfg["headdim"], cfg["dstate"], cfg["ngroups"], cfg["length"]
+    inner, gn = H * P, G * N
+    torch.manual_seed(cfg["seed"])
+    in_proj = torch.nn.Linear(cfg["d_model"], 2 * inner + 2 * gn + H, device=device)
+    out_proj = torch.nn.Linear(inner, cfg["d_model"], device=device)
+    conv_w = torch.nn.Parameter(torch.randn(inner + 2 * gn, cfg["conv"], device=device) * .3)
+    conv_b = torch.nn.Parameter(torch.randn(inner + 2 * gn, device=device) * .1)
+    a_log = torch.nn.Parameter(torch.rand(H, device=device) * 2.7)
+    d_skip = torch.nn.Parameter(torch.ones(H, device=device))
+    dt_bias = torch.nn.Parameter(torch.randn(H, device=device) * .2 - 4.0)
+    norm_w = torch.nn.Parameter(torch.ones(inner, device=device))
+    params = list(in_proj.parameters()) + list(out_proj.parameters()) + [conv_w, conv_b, a_log, d_skip,
+                                                                          dt_bias, norm_w]
+    opt = torch.optim.SGD(params, lr=1e-4)
+    x = torch.randn(b, L, cfg["d_model"], device=device, generator=torch.Generator(device=device).manual_seed(
+        cfg["seed"] + rank)).to(torch.bfloat16)
+
+    def step():
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            zxbcdt = in_proj(x)
+            z = zxbcdt[..., :inner]
+            xbc = zxbcdt[..., inner:2 * inner + 2 * gn]
+            dt = zxbcdt[..., 2 * inner + 2 * gn:]
+            xbc = causal_conv1d_fn(xbc.transpose(1, 2), conv_w, conv_b, activation="silu").transpose(1, 2)
+            xs = xbc[..., :inner].reshape(b, L, H, P)
+            B = xbc[..., inner:inner + gn].reshape(b, L, G, N)
+            C = xbc[..., inner + gn:].reshape(b, L, G, N)
+            y, _ = mamba2_chunk_scan(xs, dt, -torch.exp(a_log), B, C, chunk_size=cfg["chunk"], D=d_skip,
+                                     dt_bias=dt_bias, dt_softplus=True)
+            y = rmsnorm_gated(y.reshape(b, L, inner), norm_w, z=z, group_size=inner // G, norm_before_gate=False)
+            loss = out_proj(y).float().square().mean()
+        loss.backward()
+        if world > 1:
+            for prm in params:
+                dist.all_reduce(prm.grad)
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+
+    ms = _timed(step, args.steps, args.warmup, world, dist)
+    if rank != 0:
+        return None
+    tokens = cfg["batch"] * L
+    flops_gemm = 6 * tokens * (cfg["d_model"] * (2 * inner + 2 * gn + H) + inner * cfg["d_model"])
+    return {
+        "metric": "Mamba-2 layer fwd+bwd+SGD tokens/s", "value": tokens / (ms / 1e3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16 autocast (fp32 master weights)", "data": "synthetic (seeded normal), random-init weights",
+        "config": {"workload": "Mamba-2 layer at BASELINE config 3 shape", **cfg,
+                   "parallelism": f"dp{world} (batch shard, gradient all-reduce)"},
+        "projection_gemm_tflop_per_step": flops_gemm / 1e12,
+        "gpu_launches": None,
+    }
+
+
 def cpu_baseline_scan(cfg, threads, budget_s=15.0):
     """The oracle (reference CPU code restated) on a bounded sample: one batch
     row, a slice of channels, the full sequence; fwd + bwd with autograd."""
@@ -626,7 +700,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--op", default="scan", choices=["scan", "ssd", "decode", "ss2d", "conv1d", "gnorm"])
+    ap.add_argument("--op", default="scan", choices=["scan", "ssd", "decode", "ss2d", "conv1d", "gnorm", "block"])
     ap.add_argument("--config", type=int, default=2, choices=[1, 2])
     ap.add_argument("--shape", default=None,
                     help="batch,dim,seqlen override of the config (profiling runs on small cases)")
@@ -671,7 +745,8 @@ def main():
         line = run_scan(args, world, rank, device)
     else:
         line = {"ssd": run_ssd, "decode": run_decode, "ss2d": run_ss2d,
-                "conv1d": run_conv1d, "gnorm": run_gnorm}[args.op](args, world, rank, device)
+                "conv1d": run_conv1d, "gnorm": run_gnorm, "block": run_block}[args.op](args, world, rank,
+                                                                                        device)
     if rank == 0 and line is not None:
         if world == 1 and not args.no_cpu_baseline and args.op == "scan":
             line["cpu_baseline"] = cpu_baseline_scan(CONFIGS[args.config], threads)
