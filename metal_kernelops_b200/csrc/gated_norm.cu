@@ -120,14 +120,21 @@ __device__ __forceinline__ float elem_c1(float xv, float zv, float dv, float w, 
 
 // ------------------------------------------------------------- warp path --
 // Lane slot s = k * 32 + lane (k < NV) covers elements [s V, s V + V).  The
-// group's weight and bias sit in shared memory (GP = 32 NV V floats each).
+// group's weight and bias sit in shared memory (GP = 32 NV V floats each) in
+// lane-major order -- element i of slot (k, lane) at (k V + i) * 32 + lane --
+// so a warp's accesses to one (k, i) hit 32 consecutive banks.
+template <int V>
+__device__ __forceinline__ int lane_major(int f) {
+    const int s = f / V, i = f - s * V;
+    return ((s >> 5) * V + i) * 32 + (s & 31);
+}
 template <int V, int NV>
 __device__ __forceinline__ void stage_wb(const Args& a, int64_t g, float* ws, float* bs) {
     constexpr int GP = 32 * NV * V;
-    for (int i = threadIdx.x; i < GP; i += kThreads) {
-        const bool in = i < a.group;
-        ws[i] = in ? a.w[g * a.group + i] : 0.0f;
-        bs[i] = (in && a.has_bias) ? a.b[g * a.group + i] : 0.0f;
+    for (int f = threadIdx.x; f < GP; f += kThreads) {
+        const bool in = f < a.group;
+        ws[lane_major<V>(f)] = in ? a.w[g * a.group + f] : 0.0f;
+        bs[lane_major<V>(f)] = (in && a.has_bias) ? a.b[g * a.group + f] : 0.0f;
     }
 }
 
@@ -177,7 +184,8 @@ fwd_kernel(const Args a) {
             float o[V];
 #pragma unroll
             for (int i = 0; i < V; ++i) {
-                const float y = fmaf(xv[k][i] * r, ws[e0 + i], bs[e0 + i]);
+                const int q = (k * V + i) * 32 + lane;
+                const float y = fmaf(xv[k][i] * r, ws[q], bs[q]);
                 o[i] = a.gate == kGateAfter ? y * gt[k][i] : y;
             }
             VecIo<T, V>::st(out + base + e0, o);
@@ -186,7 +194,7 @@ fwd_kernel(const Args a) {
 }
 
 // Backward warp path.  Dynamic shared memory: w[GP], b[GP], then per warp the
-// dw and db column sums of its rows (acc[warp][2][GP]).
+// dw and db column sums of its rows (acc[warp][2][GP]), all lane-major.
 template <typename T, int V, int NV>
 __global__ void __launch_bounds__(kThreads)
 bwd_kernel(const Args a) {
@@ -230,7 +238,8 @@ bwd_kernel(const Args a) {
                 for (int i = 0; i < V; ++i) { xv[k][i] = 0.0f; dv[k][i] = 0.0f; zv[k][i] = 0.0f; }
             }
 #pragma unroll
-            for (int i = 0; i < V; ++i) c1 += elem_c1<T>(xv[k][i], zv[k][i], dv[k][i], ws[e0 + i], r, a.gate);
+            for (int i = 0; i < V; ++i)
+                c1 += elem_c1<T>(xv[k][i], zv[k][i], dv[k][i], ws[(k * V + i) * 32 + lane], r, a.gate);
         }
         c1 = warp_sum(c1) / (float)G;
 #pragma unroll
@@ -240,11 +249,12 @@ bwd_kernel(const Args a) {
             float ox[V], oz[V];
 #pragma unroll
             for (int i = 0; i < V; ++i) {
-                const ElemGrad e = elem_grad<T>(xv[k][i], zv[k][i], dv[k][i], ws[e0 + i], bs[e0 + i], r, c1, a.gate);
+                const int q = (k * V + i) * 32 + lane;
+                const ElemGrad e = elem_grad<T>(xv[k][i], zv[k][i], dv[k][i], ws[q], bs[q], r, c1, a.gate);
                 ox[i] = e.dx;
                 oz[i] = e.dz;
-                acc_w[e0 + i] = fmaf(e.dy0, e.xh, acc_w[e0 + i]);
-                acc_b[e0 + i] += e.dy0;
+                acc_w[q] = fmaf(e.dy0, e.xh, acc_w[q]);
+                acc_b[q] += e.dy0;
             }
             VecIo<T, V>::st(dx + base + e0, ox);
             if (a.gate != kGateNone) VecIo<T, V>::st(dz + base + e0, oz);
@@ -252,15 +262,16 @@ bwd_kernel(const Args a) {
     }
     __syncthreads();
     // this row block's column partials: the warps' sums in a fixed order
-    for (int i = threadIdx.x; i < G; i += kThreads) {
+    for (int f = threadIdx.x; f < G; f += kThreads) {
+        const int q0 = lane_major<V>(f);
         float sw = 0.0f, sb = 0.0f;
 #pragma unroll
         for (int q = 0; q < kWarps; ++q) {
-            sw += sm[2 * GP + q * 2 * GP + i];
-            sb += sm[2 * GP + q * 2 * GP + GP + i];
+            sw += sm[2 * GP + q * 2 * GP + q0];
+            sb += sm[2 * GP + q * 2 * GP + GP + q0];
         }
-        a.dw_part[blockIdx.x * F + g * G + i] = sw;
-        if (a.db_part != nullptr) a.db_part[blockIdx.x * F + g * G + i] = sb;
+        a.dw_part[blockIdx.x * F + g * G + f] = sw;
+        if (a.db_part != nullptr) a.db_part[blockIdx.x * F + g * G + f] = sb;
     }
 }
 
