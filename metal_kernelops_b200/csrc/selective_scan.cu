@@ -355,13 +355,23 @@ __global__ void combine_fwd_kernel(const Args a) {
          i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t b = i / per, k = i - b * per;
         float h = 0.0f;
-        for (int64_t s = 0; s < a.nseg; ++s) {
-            const int64_t at = (b * a.nseg + s) * per + k;
-            const bool last = s + 1 == a.nseg;
-            const float loc = last ? 0.0f : a.seg_x[at];
-            const float pr = last ? 0.0f : a.seg_p[at];
-            a.seg_x[at] = h;
-            h = fmaf(pr, h, loc);
+        // blocks of 8 segments: the loads first (independent), then the chain
+        for (int64_t s0 = 0; s0 < a.nseg; s0 += 8) {
+            float loc[8], pr[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int64_t s = s0 + j;
+                const int64_t at = (b * a.nseg + s) * per + k;
+                const bool body = s + 1 < a.nseg;
+                loc[j] = body ? a.seg_x[at] : 0.0f;
+                pr[j] = body ? a.seg_p[at] : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int64_t s = s0 + j;
+                if (s < a.nseg) a.seg_x[(b * a.nseg + s) * per + k] = h;
+                h = fmaf(pr[j], h, loc[j]);
+            }
         }
     }
 }
@@ -964,12 +974,23 @@ __global__ void combine_bwd_kernel(const Args a) {
          i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t b = i / per, k = i - b * per;
         float q = 0.0f;
-        for (int64_t s = a.nseg - 1; s >= 0; --s) {
-            const int64_t at = (b * a.nseg + s) * per + k;
-            const float r = s == 0 ? 0.0f : a.seg_x[at];
-            const float pr = s == 0 ? 0.0f : a.seg_p[at];
-            a.seg_x[at] = q;
-            q = fmaf(pr, q, r);
+        // blocks of 8 segments from the end: the loads first, then the chain
+        for (int64_t s0 = a.nseg - 1; s0 >= 0; s0 -= 8) {
+            float r[8], pr[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int64_t s = s0 - j;
+                const bool body = s >= 1;
+                const int64_t at = (b * a.nseg + (body ? s : 0)) * per + k;
+                r[j] = body ? a.seg_x[at] : 0.0f;
+                pr[j] = body ? a.seg_p[at] : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int64_t s = s0 - j;
+                if (s >= 0) a.seg_x[(b * a.nseg + s) * per + k] = q;
+                q = fmaf(pr[j], q, r[j]);
+            }
         }
     }
 }
