@@ -323,8 +323,8 @@ fwd_kernel(const Args a) {
             float o1 = fmaf(ur.y, Dch[cc], dvu[cc * FS + t + 1].x);
             if (has_z) {
                 const float2 zr = Io2<T>::ld(&rz[cc * TT + t]);
-                o0 *= zr.x * sigmoid_fast(zr.x);
-                o1 *= zr.y * sigmoid_fast(zr.y);
+                o0 *= zr.x * sigmoid_t<T>(zr.x);
+                o1 *= zr.y * sigmoid_t<T>(zr.y);
             }
             T* dst = &yg[(row0 + cc) * L + t0 + t];
             if (a.fast || t + 1 >= len) {      // fast: even L, aligned pair
@@ -447,8 +447,9 @@ struct BwdLayout {
     static constexpr size_t o_bc = (o_f + 4 * (size_t)CPC * FS * 4 + 15) / 16 * 16;  // [2][4][CS]
     static constexpr size_t o_w = o_bc + 2 * 4 * CS * 4;                      // [2][kWarps][K][NP+1]
     static constexpr size_t o_sck = o_w + 2 * (size_t)kWarps * K * (NP + 1) * 4;  // [K/TS][NPT/2][thr] f2
-    static constexpr size_t o_ch = o_sck + (size_t)(K / kTS) * NPT * kThreads * 4;  // [4][CPC]
-    static constexpr size_t bytes = o_ch + 4 * CPC * 4;
+    static constexpr size_t o_ch = o_sck + (size_t)(K / kTS) * NPT * kThreads * 4;  // [2][CPC]
+    static constexpr size_t o_acc = o_ch + 2 * CPC * 4;                       // [2][CPC * K/2]
+    static constexpr size_t bytes = o_acc + 2 * (size_t)CPC * (K / 2) * 4;
 };
 
 template <typename T, int NPT, int LPC>
@@ -490,8 +491,10 @@ bwd_kernel(const Args a) {
     float2* sck = reinterpret_cast<float2*>(smem + Lay::o_sck);
     float* Dch = reinterpret_cast<float*>(smem + Lay::o_ch);
     float* bch = Dch + CPC;
-    float* accD = bch + CPC;      // running sum of dD per channel
-    float* accb = accD + CPC;     // running sum of d bias per channel
+    // running sums of dD and d bias, one slot per phase-C work item (channel,
+    // step pair): each slot has one owning thread, folded per channel at the end
+    float* accD = reinterpret_cast<float*>(smem + Lay::o_acc);
+    float* accb = accD + CPC * HALF;
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -520,6 +523,8 @@ bwd_kernel(const Args a) {
     for (int i = tid; i < CPC; i += kThreads) {
         Dch[i] = (has_d && i < rows) ? a.D[d0 + i] : 0.0f;
         bch[i] = (has_bias && i < rows) ? a.delta_bias[d0 + i] : 0.0f;
+    }
+    for (int i = tid; i < CPC * HALF; i += kThreads) {
         accD[i] = 0.0f;
         accb[i] = 0.0f;
     }
@@ -576,8 +581,8 @@ bwd_kernel(const Args a) {
             dvu[cc * FS + t + 1] = make_float2(d1v, d1v * ur.y);
             if (has_z) {
                 const float2 zr = Io2<T>::ld(&rz[cc * K + t]);
-                go.x *= zr.x * sigmoid_fast(zr.x);
-                go.y *= zr.y * sigmoid_fast(zr.y);
+                go.x *= zr.x * sigmoid_t<T>(zr.x);
+                go.y *= zr.y * sigmoid_t<T>(zr.y);
             }
             gs[cc * FS + t] = go.x;
             gs[cc * FS + t + 1] = go.y;
@@ -764,10 +769,13 @@ bwd_kernel(const Args a) {
                     const float duacc = dua[cc * FS + tt];
                     o_du[k] = fmaf(v.x, duacc, gv * Dv);
                     float ddt = fmaf(uu[k], duacc, dda[cc * FS + tt]);
-                    if (softplus) ddt *= softplus_grad_fast(draw[k] + bch[cc]);
+                    if (softplus) {
+                        const float xs = draw[k] + bch[cc];
+                        ddt *= xs > 20.0f ? 1.0f : sigmoid_t<T>(xs);     // softplus' (threshold 20)
+                    }
                     o_dd[k] = ddt;
                     if (has_z) {
-                        const float sg = sigmoid_fast(zz[k]);
+                        const float sg = sigmoid_t<T>(zz[k]);
                         o_dz[k] = gg2[k] * fmaf(uu[k], Dv, yv[cc * FS + tt]) * sg * fmaf(zz[k], 1.0f - sg, 1.0f);
                     }
                     if (tt < len) {
@@ -791,15 +799,8 @@ bwd_kernel(const Args a) {
                     }
                 }
             }
-#pragma unroll
-            for (int o = HALF / 2; o > 0; o >>= 1) {
-                pD += __shfl_xor_sync(0xffffffffu, pD, o);
-                pb += __shfl_xor_sync(0xffffffffu, pb, o);
-            }
-            if ((lane % HALF) == 0) {
-                accD[cc] += pD;
-                accb[cc] += pb;
-            }
+            accD[i] += pD;                    // this thread's own slot
+            accb[i] += pb;
         }
         for (int i = tid; i < N * len; i += kThreads) {
             const int n = i / len, t = i % len;
@@ -825,8 +826,14 @@ bwd_kernel(const Args a) {
         }
     }
     for (int i = tid; i < rows; i += kThreads) {
-        a.dD_part[bs * a.dim + d0 + i] = accD[i];
-        a.db_part[bs * a.dim + d0 + i] = accb[i];
+        float sd = 0.0f, sb = 0.0f;
+#pragma unroll
+        for (int h = 0; h < HALF; ++h) {
+            sd += accD[i * HALF + h];
+            sb += accb[i * HALF + h];
+        }
+        a.dD_part[bs * a.dim + d0 + i] = sd;
+        a.db_part[bs * a.dim + d0 + i] = sb;
     }
 }
 
@@ -923,8 +930,8 @@ adj_kernel(const Args a) {
             }
             if (has_z) {
                 const float2 zr = Io2<T>::ld(&rz[cc * K + t]);
-                go.x *= zr.x * sigmoid_fast(zr.x);
-                go.y *= zr.y * sigmoid_fast(zr.y);
+                go.x *= zr.x * sigmoid_t<T>(zr.x);
+                go.y *= zr.y * sigmoid_t<T>(zr.y);
             }
             dv[cc * FS + t] = make_float2(d0v * kLog2e, go.x);
             dv[cc * FS + t + 1] = make_float2(d1v * kLog2e, go.y);
