@@ -13,15 +13,14 @@
 //     dweight[j]  = sum_{b, t} g[t] z[t + j],   dbias = sum_{b, t} g[t]
 //
 // The work is bytes, not flops (2 K flops per element), so the kernels are
-// built for HBM: persistent warps walk (row, 512-element segment) items, each
-// lane owning 16 consecutive elements read and written as two 16-byte vectors
-// (a scalar variant serves rows that are not 16-byte aligned), with the next
-// item's loads issued before the current item is computed.  The taps-wide
-// halos either side come from the neighbouring lanes by shuffle, so each
-// element is loaded once.  The backward recomputes the pre-activation from x
-// instead of saving it, and reduces dweight / dbias per item in a fixed order
-// into partials that a second kernel folds per channel, so results are
-// bit-reproducible.
+// built for HBM.  Rows of 16-byte aligned bytes stream through a ring of
+// shared-memory stages filled by bulk asynchronous copies (the bulk-copy
+// pipeline path below), computed with paired fp32 instructions; other rows
+// take a plain path, a warp per 512-element segment with the taps-wide halos
+// from the neighbouring lanes by shuffle.  The backward recomputes the
+// pre-activation from x instead of saving it, and leaves dweight / dbias as
+// partials that a second kernel folds per channel in a fixed order, so
+// results are reproducible.
 #include "common.cuh"
 #include "tc.cuh"
 
@@ -34,11 +33,13 @@ constexpr int kMaxWidth = 8;
 struct Args {
     int64_t batch, channels, length, rows;    // rows = batch * channels
     int64_t nchunks, chunk;                   // chunks per row, elements per chunk
+    int64_t slots;                            // dweight / dbias partials per chunk
+    int64_t per;                              // bulk: items per CTA
     uint32_t flags;
     const void* x; const float* w; const float* bias; const void* init;
     void* out; void* final_state;
     const void* dout; void* dx; void* dinit;
-    float* partial;                           // (rows, nchunks, K + 1)
+    float* partial;                           // (rows, nchunks, slots, K + 1)
 };
 
 constexpr uint32_t kHasBias = SSM_HAS_BIAS, kSilu = SSM_CONV_SILU, kHasInit = SSM_HAS_INIT;
@@ -267,16 +268,31 @@ bwd_plain_kernel(const Args a) {
 
 // ------------------------------------------------- bulk-copy pipeline path --
 // Rows whose bytes are 16-byte aligned: persistent CTAs walk (row, tile of
-// kTile elements) items.  One thread issues a bulk asynchronous copy of each
-// item's tile -- with up to 8 elements of halo either side -- into one of
-// kStages shared-memory stages, completing on the stage's mbarrier, so the next
-// items' bytes stream in while the current tile is computed; every thread then
-// owns 16 elements of the tile.  Waits are bounded: a wait that runs out
-// records an error code (ssm_take_kernel_error) and the CTA stops after
-// draining the copies it issued.
+// kTile elements) items through a ring of kStages shared-memory stages.  A
+// stage holds the item's tile (x, and dout for the backward) with up to kHalo
+// elements of halo either side, landed by bulk asynchronous copies that
+// complete on the stage's mbarrier.  The warps of a CTA never wait for one
+// another: each polls the stage's mbarrier itself (bounded), reads its part,
+// and counts itself off the stage; the last of the CTA's warps to finish a
+// stage issues the copy of the stage's next item.  A wait that runs out
+// records an error code (ssm_take_kernel_error) and the warp stops; the CTA
+// then drains the copies it issued.
+//
+// Items are numbered channel-major, it = (c * batch + b) * nchunks + tile, and
+// each CTA walks one contiguous range of `per` of them, so that it passes
+// through few channels: a warp keeps the channel's weights, and in the
+// backward its dweight / dbias sums, in registers across the channel's items
+// and reduces the sums once per run of a channel.
+//
+// Thread t owns the 8-element groups at 8 t and kTile/2 + 8 t of a tile (each
+// warp-wide 16-byte access covers 512 contiguous bytes), carried as the two
+// lanes of float2 arithmetic.  Weights and bias are halved (exact) so that the
+// pre-activation comes out as a / 2, the form the paired SiLU takes.
 constexpr int kTile = kThreads * 16;   // 4096 elements
+constexpr int kHalf = kTile / 2;
 constexpr int kHalo = 8;
 constexpr int kStages = 3;
+constexpr int kWarps = kThreads / 32;
 
 __device__ int g_conv_error;
 
@@ -284,20 +300,40 @@ template <typename T, int NT>
 struct BulkLayout {
     static constexpr int SPAN = kHalo + kTile + kHalo;             // elements per stage and tensor
     static constexpr size_t stage_bytes = (size_t)SPAN * sizeof(T) * NT;
-    static constexpr size_t mbar_off = stage_bytes * kStages;
-    static constexpr size_t bytes = mbar_off + 8 * kStages;
+    static constexpr size_t mbar_off = stage_bytes * kStages;      // kStages mbarriers
+    static constexpr size_t done_off = mbar_off + 8 * kStages;     // kStages warp counters
+    static constexpr size_t issued_off = done_off + 4 * kStages;   // kStages copies issued
+    static constexpr size_t bytes = issued_off + 4 * kStages;
 };
 
-// Copy item `it`'s tile(s) into stage `st`: elements [t0 - front, t0 + n + back)
+// A bulk item's (channel, batch, tile), stepped without divisions.  The host
+// keeps rows * nchunks below 2^31.
+struct Cursor {
+    uint32_t c, b, tile;
+    __device__ void set(const Args& a, int64_t it) {
+        const uint32_t i = (uint32_t)it, nc = (uint32_t)a.nchunks, pc = (uint32_t)(a.batch * a.nchunks);
+        c = i / pc;
+        const uint32_t r = i - c * pc;
+        b = r / nc;
+        tile = r - b * nc;
+    }
+    __device__ void next(const Args& a) {
+        if (++tile == (uint32_t)a.nchunks) {
+            tile = 0;
+            if (++b == (uint32_t)a.batch) { b = 0; ++c; }
+        }
+    }
+    __device__ int64_t row(const Args& a) const { return (int64_t)b * a.channels + c; }
+    __device__ int64_t t0() const { return (int64_t)tile * kTile; }
+};
+
+// Copy the item at `q` into stage `st`: elements [t0 - front, t0 + n + back)
 // of the row land at stage offset kHalo - front.
 template <typename T, int NT>
-__device__ __forceinline__ void issue_tile(const Args& a, unsigned char* smem, int st, int64_t it,
+__device__ __forceinline__ void issue_tile(const Args& a, unsigned char* smem, int st, const Cursor& q,
                                            const void* s0, const void* s1) {
     using Lay = BulkLayout<T, NT>;
-    const int64_t L = a.length;
-    int64_t row, tile, c;
-    item_coords(a, it, row, tile, c);
-    const int64_t t0 = tile * kTile;
+    const int64_t L = a.length, row = q.row(a), t0 = q.t0();
     const int64_t n = min64(kTile, L - t0);
     const int front = t0 >= kHalo ? kHalo : 0;
     const int back = NT > 1 ? (int)min64(kHalo, L - t0 - n) : 0;
@@ -312,7 +348,153 @@ __device__ __forceinline__ void issue_tile(const Args& a, unsigned char* smem, i
                              (size_t)(kHalo - front) * sizeof(T);
         tc::bulk_load(tc::smem_u32(dst), g, bytes, mbar);
     }
+    reinterpret_cast<int*>(smem + Lay::issued_off)[st] += 1;
 }
+
+// The stage ring of one CTA, whose items are [first, first + count).
+template <typename T, int NT>
+struct Ring {
+    unsigned char* smem;
+    int64_t first;
+    int count;
+    __device__ uint32_t mbar(int st) const { return tc::smem_u32(smem + BulkLayout<T, NT>::mbar_off + 8 * st); }
+    __device__ void init(const Args& a, const void* s0, const void* s1) const {
+        if (threadIdx.x == 0) {
+            for (int s = 0; s < kStages; ++s) {
+                tc::mbar_init(mbar(s), 1);
+                reinterpret_cast<int*>(smem + BulkLayout<T, NT>::done_off)[s] = 0;
+                reinterpret_cast<int*>(smem + BulkLayout<T, NT>::issued_off)[s] = 0;
+            }
+            tc::fence_mbar_init();
+            Cursor q;
+            q.set(a, first);
+            for (int s = 0; s < kStages && s < count; ++s, q.next(a)) issue_tile<T, NT>(a, smem, s, q, s0, s1);
+        }
+        __syncthreads();
+    }
+    // every lane polls; warp-uniform result
+    __device__ bool wait(int st, int use) const {
+        const bool ok = tc::mbar_wait(mbar(st), (uint32_t)(use & 1));
+        return __all_sync(0xffffffffu, ok);
+    }
+    // The calling warp is done reading stage `st` for its k-th item (the
+    // stage's use-th); the CTA's last warp to get here issues the item
+    // kStages further on, at `ahead`.
+    __device__ void release(const Args& a, int st, int use, int k, const Cursor& ahead, const void* s0,
+                            const void* s1) const {
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) {
+            int* done = reinterpret_cast<int*>(smem + BulkLayout<T, NT>::done_off) + st;
+            __threadfence_block();
+            const int prev = atomicAdd(done, 1);
+            if (prev == (use + 1) * kWarps - 1) {
+                __threadfence_block();
+                if (k + kStages < count) issue_tile<T, NT>(a, smem, st, ahead, s0, s1);
+            }
+        }
+    }
+    // After every warp has left its loop: wait (bounded) for the last copy
+    // issued into each stage, so that none lands after the CTA exits.
+    __device__ void drain() const {
+        __syncthreads();
+        if (threadIdx.x == 0)
+            for (int s = 0; s < kStages; ++s) {
+                const int m = reinterpret_cast<const int*>(smem + BulkLayout<T, NT>::issued_off)[s];
+                if (m > 0) tc::mbar_wait(mbar(s), (uint32_t)((m - 1) & 1));
+            }
+    }
+};
+
+// v[i] = x at tile position p - 8 + i for i < 16 (the 8 elements before group p
+// and the group), zero at or past n.  s points at tile position 0 of a stage
+// (16-byte aligned, kHalo elements of front halo); p is a multiple of 8.
+template <typename T>
+__device__ __forceinline__ void load_span(const T* s, int p, int n, float* v) {
+    if (p + 8 <= n) {
+        Vec<T, 8>::ld(s + p - 8, v);
+        Vec<T, 8>::ld(s + p, v + 8);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = p - 8 + i < n ? ldf(s + p - 8 + i) : 0.0f;
+    }
+}
+// The thread's two groups at p0 (lane .x) and p1 (lane .y): z[m] = x at
+// p - TAPS + m for m < TAPS + 8.  Positions left of a row start are garbage
+// here; the caller replaces them (they are read by thread 0 only).
+template <typename T, int TAPS>
+__device__ __forceinline__ void load_x_pair(const T* s, int p0, int p1, int n, float2* z) {
+    float a[16], b[16];
+    load_span<T>(s, p0, n, a);
+    load_span<T>(s, p1, n, b);
+#pragma unroll
+    for (int m = 0; m < TAPS + 8; ++m) z[m] = make_float2(a[8 - TAPS + m], b[8 - TAPS + m]);
+}
+// g[i] = s at p + i for i < 8 (zero at or past n), both groups.
+template <typename T>
+__device__ __forceinline__ void load_pair8(const T* s, int p0, int p1, int n, float2* g) {
+    float a[8], b[8];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int p = u ? p1 : p0;
+        float* v = u ? b : a;
+        if (p + 8 <= n) Vec<T, 8>::ld(s + p, v);
+        else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = p + i < n ? ldf(s + p + i) : 0.0f;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) g[i] = make_float2(a[i], b[i]);
+}
+template <typename T>
+__device__ __forceinline__ void store_pair8(T* r, int p0, int p1, int n, const float2* o) {
+    float a[8], b[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { a[i] = o[i].x; b[i] = o[i].y; }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int p = u ? p1 : p0;
+        const float* v = u ? b : a;
+        if (p + 8 <= n) Vec<T, 8>::st(r + p, v);
+        else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (p + i < n) stf(r + p + i, v[i]);
+        }
+    }
+}
+
+// A channel's halved weights and bias.
+template <int K>
+struct ChannelConst {
+    float2 wh[K], bh;
+    __device__ void load(const Args& a, uint32_t c) {
+#pragma unroll
+        for (int j = 0; j < K; ++j) wh[j] = f2(0.5f * a.w[(int64_t)c * K + j]);
+        bh = f2((a.flags & kHasBias) ? 0.5f * a.bias[c] : 0.0f);
+    }
+};
+
+// Thread 0 of a row-start item: the taps elements left of position 0 (the
+// initial state, or zeros), loaded before the stage wait and put in place of
+// the stage's unwritten front halo.
+template <typename T, int TAPS>
+struct RowStart {
+    float v[TAPS > 0 ? TAPS : 1];
+    __device__ void load(const Args& a, int64_t row, int64_t t0) {
+        if (TAPS > 0 && t0 == 0 && threadIdx.x == 0) {
+            const T* ir = (a.flags & kHasInit) ? static_cast<const T*>(a.init) + row * TAPS : nullptr;
+#pragma unroll
+            for (int i = 0; i < TAPS; ++i) v[i] = ir ? ldf(ir + i) : 0.0f;
+        }
+    }
+    __device__ void apply(float2* z, int64_t t0) const {
+        if (TAPS > 0 && t0 == 0 && threadIdx.x == 0) {
+#pragma unroll
+            for (int i = 0; i < TAPS; ++i) z[i].x = v[i];
+        }
+    }
+};
 
 template <typename T, int K>
 __global__ void __launch_bounds__(kThreads)
@@ -321,76 +503,44 @@ fwd_bulk_kernel(const Args a) {
     using Lay = BulkLayout<T, 1>;
     extern __shared__ __align__(128) unsigned char smem[];
     const int64_t items = a.rows * a.nchunks, L = a.length;
-    const int tid = threadIdx.x, lane = tid & 31;
-    if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) tc::mbar_init(tc::smem_u32(smem + Lay::mbar_off + 8 * s), 1);
-        tc::fence_mbar_init();
-    }
-    __syncthreads();
-    if (tid == 0)
-        for (int s = 0; s < kStages; ++s) {
-            const int64_t it = blockIdx.x + (int64_t)s * gridDim.x;
-            if (it < items) issue_tile<T, 1>(a, smem, s, it, a.x, nullptr);
+    const int64_t first = (int64_t)blockIdx.x * a.per;
+    const Ring<T, 1> ring{smem, first, (int)max64(0, min64(a.per, items - first))};
+    const int tid = threadIdx.x;
+    ring.init(a, a.x, nullptr);
+    const bool silu = a.flags & kSilu;
+    const int p0 = tid * 8, p1 = kHalf + tid * 8;
+    Cursor cur, ahead;
+    cur.set(a, first);
+    ahead.set(a, first + kStages);
+    ChannelConst<K> cc;
+    uint32_t wc = 0xffffffffu;
+    int st = 0, use = 0;
+    for (int k = 0; k < ring.count; ++k) {
+        const int64_t row = cur.row(a), t0 = cur.t0();
+        const int n = (int)min64(kTile, L - t0);
+        if (cur.c != wc) {
+            cc.load(a, cur.c);
+            wc = cur.c;
         }
-    bool ok = true;
-    int64_t k = 0;
-    for (int64_t it = blockIdx.x; it < items; it += gridDim.x, ++k) {
-        const int st = (int)(k % kStages);
-        const uint32_t par = (uint32_t)((k / kStages) & 1);
-        // one thread polls; the rest wait at the barrier without issuing
-        if (tid == 0) ok = tc::mbar_wait(tc::smem_u32(smem + Lay::mbar_off + 8 * st), par);
-        ok = __syncthreads_and(ok);
-        if (!ok) { if (tid == 0) atomicCAS(&g_conv_error, 0, 61); break; }
-        int64_t row, tl, c;
-        item_coords(a, it, row, tl, c);
-        const int64_t t0 = tl * kTile;
-        const int64_t n = min64(kTile, L - t0);
-        const T* tile = reinterpret_cast<const T*>(smem + st * Lay::stage_bytes) + kHalo;   // tile[p], p >= -front
-        float w[K];
-#pragma unroll
-        for (int j = 0; j < K; ++j) w[j] = a.w[c * K + j];
-        const float bv = (a.flags & kHasBias) ? a.bias[c] : 0.0f;
-        const T* ir = (a.flags & kHasInit) ? static_cast<const T*>(a.init) + row * TAPS : nullptr;
-        // thread tid owns the 8-element groups at 8 tid and kTile/2 + 8 tid, so
-        // each warp-wide 16-byte store covers 512 contiguous bytes
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int p0 = u * (kTile / 2) + tid * 8;
-            float z[TAPS + 8];
-            const bool whole = p0 + 8 <= n;
-            if (whole) {
-                Vec<T, 8>::ld(tile + p0, z + TAPS);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) z[TAPS + i] = p0 + i < n ? ldf(tile + p0 + i) : 0.0f;
-            }
-#pragma unroll
-            for (int i = 0; i < TAPS; ++i) {
-                const float up = __shfl_up_sync(0xffffffffu, z[8 + i], 1);
-                float v;
-                if (lane > 0) v = up;
-                else if (t0 + p0 == 0) v = ir ? ldf(ir + i) : 0.0f;
-                else v = ldf(tile + p0 - TAPS + i);
-                z[i] = v;
-            }
-            if (p0 < n) {
-                float o[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    float acc = bv;
-#pragma unroll
-                    for (int j = 0; j < K; ++j) acc = fmaf(w[j], z[i + j], acc);
-                    o[i] = (a.flags & kSilu) ? silu_t<T>(acc) : acc;
-                }
-                T* dst = static_cast<T*>(a.out) + row * L + t0 + p0;
-                if (whole) Vec<T, 8>::st(dst, o);
-                else {
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        if (p0 + i < n) stf(dst + i, o[i]);
-                }
-            }
+        RowStart<T, TAPS> rs;
+        rs.load(a, row, t0);
+        if (!ring.wait(st, use)) {
+            if ((tid & 31) == 0) atomicCAS(&g_conv_error, 0, 61);
+            break;
         }
+        const T* xs = reinterpret_cast<const T*>(smem + st * Lay::stage_bytes) + kHalo;
+        float2 z[TAPS + 8], o[8];
+        load_x_pair<T, TAPS>(xs, p0, p1, n, z);
+        ring.release(a, st, use, k, ahead, a.x, nullptr);
+        rs.apply(z, t0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float2 hp = cc.bh;
+#pragma unroll
+            for (int j = 0; j < K; ++j) hp = fma2(cc.wh[j], z[i + j], hp);
+            o[i] = silu ? silu2_half<T>(hp) : add2(hp, hp);
+        }
+        store_pair8<T>(static_cast<T*>(a.out) + row * L + t0, p0, p1, n, o);
         if (a.final_state != nullptr && t0 == 0 && tid == 0) {
             const T* xr = static_cast<const T*>(a.x) + row * L;
             const T* ir = (a.flags & kHasInit) ? static_cast<const T*>(a.init) + row * TAPS : nullptr;
@@ -398,139 +548,164 @@ fwd_bulk_kernel(const Args a) {
 #pragma unroll
             for (int i = 0; i < TAPS; ++i) stf(fr + i, zval<T, TAPS>(xr, ir, L - TAPS + i, L));
         }
-        __syncthreads();                          // every thread is done with the stage
-        if (tid == 0) {
-            const int64_t nit = it + (int64_t)kStages * gridDim.x;
-            if (nit < items) issue_tile<T, 1>(a, smem, st, nit, a.x, nullptr);
-        }
+        cur.next(a);
+        ahead.next(a);
+        if (++st == kStages) { st = 0; ++use; }
     }
-    if (!ok && tid == 0) {
-        // drain: wait (bounded) for every copy this CTA issued and has not consumed
-        for (int64_t it = blockIdx.x + k * (int64_t)gridDim.x, j = k;
-             it < items && j < k + kStages; it += gridDim.x, ++j)
-            tc::mbar_wait(tc::smem_u32(smem + Lay::mbar_off + 8 * (j % kStages)), (uint32_t)((j / kStages) & 1));
+    ring.drain();
+}
+
+// 2 dout silu'(pre) (or 2 dout without the activation) at tile positions q0
+// (.x) and q1 (.y), read one by one from the stage; positions at or past
+// `lim` give 0.  For the warp-boundary halo of the backward.
+template <typename T, int K>
+__device__ __forceinline__ float2 grad2_at(const T* xs, const T* ds, int q0, int q1, int lim, bool silu,
+                                           const ChannelConst<K>& cc) {
+    const bool v0 = q0 < lim, v1 = q1 < lim;
+    const float2 d = make_float2(v0 ? ldf(ds + q0) : 0.0f, v1 ? ldf(ds + q1) : 0.0f);
+    if (!silu) return add2(d, d);
+    float2 hp = cc.bh;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+        const int o = j - (K - 1);
+        hp = fma2(cc.wh[j], make_float2(v0 ? ldf(xs + q0 + o) : 0.0f, v1 ? ldf(xs + q1 + o) : 0.0f), hp);
+    }
+    return silu_grad2_half<T>(hp, d);
+}
+
+// One warp's dweight / dbias sums of a channel run (doubled, both lanes) into
+// the partial slot of (run's first item, warp).
+template <int K>
+__device__ __forceinline__ void flush_run(const Args& a, int64_t run0, float2* acc) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float* part = a.partial + (run0 * kWarps + warp) * (K + 1);
+#pragma unroll
+    for (int j = 0; j <= K; ++j) {
+        float d = 0.5f * (acc[j].x + acc[j].y);
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o2);
+        if (lane == 0) part[j] = d;
+        acc[j] = f2(0.0f);
     }
 }
 
+// Backward over one stage, in the forward's thread layout and paired lanes.
+// Phase 1 turns dout into the doubled gradient 2 g = 2 dout silu'(pre) of the
+// thread's positions.  Each lane needs the taps positions right of its groups:
+// the next lane's first ones (a shuffle) or, for lane 31, the positions after
+// the warp's 256-element runs, which belong to the next warp, to the tile's
+// second half or (last warp) to the next tile; lanes 32 - taps .. 31 compute
+// those from the stage (zero past the row) and lane 31 takes them by shuffle.
+// Phase 2 forms dx = sum_j (w_j / 2)(2 g) and accumulates the dweight / dbias
+// products of the channel run.
 template <typename T, int K>
 __global__ void __launch_bounds__(kThreads)
 bwd_bulk_kernel(const Args a) {
     constexpr int TAPS = K - 1;
     using Lay = BulkLayout<T, 2>;
-    __shared__ float red[kThreads / 32][K + 1];
     extern __shared__ __align__(128) unsigned char smem[];
     const int64_t items = a.rows * a.nchunks, L = a.length;
+    const int64_t first = (int64_t)blockIdx.x * a.per;
+    const Ring<T, 2> ring{smem, first, (int)max64(0, min64(a.per, items - first))};
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) tc::mbar_init(tc::smem_u32(smem + Lay::mbar_off + 8 * s), 1);
-        tc::fence_mbar_init();
-    }
-    __syncthreads();
-    if (tid == 0)
-        for (int s = 0; s < kStages; ++s) {
-            const int64_t it = blockIdx.x + (int64_t)s * gridDim.x;
-            if (it < items) issue_tile<T, 2>(a, smem, s, it, a.x, a.dout);
-        }
+    ring.init(a, a.x, a.dout);
+    const bool silu = a.flags & kSilu;
+    const int p0 = tid * 8, p1 = kHalf + tid * 8;
+    Cursor cur, ahead;
+    cur.set(a, first);
+    ahead.set(a, first + kStages);
+    ChannelConst<K> cc;
+    uint32_t wc = 0xffffffffu;
+    int64_t run0 = first;
+    float2 acc[K + 1];
+#pragma unroll
+    for (int j = 0; j <= K; ++j) acc[j] = f2(0.0f);
+    int st = 0, use = 0;
     bool ok = true;
-    int64_t k = 0;
-    for (int64_t it = blockIdx.x; it < items; it += gridDim.x, ++k) {
-        const int st = (int)(k % kStages);
-        const uint32_t par = (uint32_t)((k / kStages) & 1);
-        // one thread polls; the rest wait at the barrier without issuing
-        if (tid == 0) ok = tc::mbar_wait(tc::smem_u32(smem + Lay::mbar_off + 8 * st), par);
-        ok = __syncthreads_and(ok);
-        if (!ok) { if (tid == 0) atomicCAS(&g_conv_error, 0, 62); break; }
-        int64_t row, tl, c;
-        item_coords(a, it, row, tl, c);
-        const int64_t t0 = tl * kTile;
-        const int64_t n = min64(kTile, L - t0);
-        const int64_t rem = L - t0;                // valid positions from the tile start
-        const T* xt = reinterpret_cast<const T*>(smem + st * Lay::stage_bytes) + kHalo;
-        const T* dt = xt + Lay::SPAN;
-        float w[K];
+    for (int k = 0; k < ring.count; ++k) {
+        const int64_t row = cur.row(a), t0 = cur.t0();
+        const int n = (int)min64(kTile, L - t0);
+        if (cur.c != wc) {
+            if (k > 0) flush_run<K>(a, run0, acc);
+            run0 = first + k;
+            cc.load(a, cur.c);
+            wc = cur.c;
+        }
+        RowStart<T, TAPS> rs;
+        rs.load(a, row, t0);
+        if (!ring.wait(st, use)) {
+            if (lane == 0) atomicCAS(&g_conv_error, 0, 62);
+            ok = false;
+            break;
+        }
+        const T* xs = reinterpret_cast<const T*>(smem + st * Lay::stage_bytes) + kHalo;
+        const T* ds = xs + Lay::SPAN;
+        float2 z[TAPS + 8], g[8 + TAPS];
+        load_x_pair<T, TAPS>(xs, p0, p1, n, z);
+        load_pair8<T>(ds, p0, p1, n, g);
+        float2 ex = f2(0.0f);                     // lane 32 - taps + i: right halo position i of the warp
+        if (TAPS > 0 && lane >= 32 - TAPS) {
+            // positions valid in the stage: the tile and, for a full tile, its
+            // back halo up to the row's end
+            const int lim = n + (int)min64(kHalo, L - t0 - n);
+            const int q = 256 * (warp + 1) + lane - (32 - TAPS);
+            ex = grad2_at<T, K>(xs, ds, q, kHalf + q, lim, silu, cc);
+        }
+        ring.release(a, st, use, k, ahead, a.x, a.dout);
+        rs.apply(z, t0);
 #pragma unroll
-        for (int j = 0; j < K; ++j) w[j] = a.w[c * K + j];
-        const float bv = (a.flags & kHasBias) ? a.bias[c] : 0.0f;
-        const T* ir = (a.flags & kHasInit) ? static_cast<const T*>(a.init) + row * TAPS : nullptr;
-        float dw[K + 1];
+        for (int i = 0; i < 8; ++i) {
+            if (silu) {
+                float2 hp = cc.bh;
 #pragma unroll
-        for (int j = 0; j <= K; ++j) dw[j] = 0.0f;
-        // thread tid owns the 8-element groups at 8 tid and kTile/2 + 8 tid
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int p0 = u * (kTile / 2) + tid * 8;
-            float z[8 + 2 * TAPS], g[8 + TAPS];
-            const bool whole = p0 + 8 <= n;
-            if (whole) {
-                Vec<T, 8>::ld(xt + p0, z + TAPS);
-                Vec<T, 8>::ld(dt + p0, g);
+                for (int j = 0; j < K; ++j) hp = fma2(cc.wh[j], z[i + j], hp);
+                g[i] = silu_grad2_half<T>(hp, g[i]);
             } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    z[TAPS + i] = p0 + i < n ? ldf(xt + p0 + i) : 0.0f;
-                    g[i] = p0 + i < n ? ldf(dt + p0 + i) : 0.0f;
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < TAPS; ++i) {
-                const float up = __shfl_up_sync(0xffffffffu, z[8 + i], 1);
-                const float xdn = __shfl_down_sync(0xffffffffu, z[TAPS + i], 1);
-                const float gdn = __shfl_down_sync(0xffffffffu, g[i], 1);
-                float v;
-                if (lane > 0) v = up;
-                else if (t0 + p0 == 0) v = ir ? ldf(ir + i) : 0.0f;
-                else v = ldf(xt + p0 - TAPS + i);
-                z[i] = v;
-                // past this group: the next lane's group, or (last lane) the next
-                // warp's, the back halo, or zero past the row
-                const int q = p0 + 8 + i;
-                const bool in = q < rem;
-                z[TAPS + 8 + i] = lane < 31 ? xdn : (in ? ldf(xt + q) : 0.0f);
-                g[8 + i] = lane < 31 ? gdn : (in ? ldf(dt + q) : 0.0f);
-            }
-            if (p0 < n) {
-                float o[8], dwl[K + 1];
-                conv_bwd_lane<T, K, 8>(w, bv, a.flags & kSilu, z, g, o, dwl);
-#pragma unroll
-                for (int j = 0; j <= K; ++j) dw[j] += dwl[j];
-                T* dst = static_cast<T*>(a.dx) + row * L + t0 + p0;
-                if (whole) Vec<T, 8>::st(dst, o);
-                else {
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        if (p0 + i < n) stf(dst + i, o[i]);
-                }
-                if (TAPS > 0 && t0 + p0 == 0 && a.dinit != nullptr)
-                    dinit_row<T, K>(static_cast<T*>(a.dinit) + row * TAPS, w, g);
+                g[i] = add2(g[i], g[i]);
             }
         }
 #pragma unroll
-        for (int j = 0; j <= K; ++j) {
+        for (int i = 0; i < TAPS; ++i) {
+            const float nx = __shfl_down_sync(0xffffffffu, g[i].x, 1), ny = __shfl_down_sync(0xffffffffu, g[i].y, 1);
+            const float ax = __shfl_sync(0xffffffffu, ex.x, 32 - TAPS + i);
+            const float ay = __shfl_sync(0xffffffffu, ex.y, 32 - TAPS + i);
+            g[8 + i] = lane == 31 ? make_float2(ax, ay) : make_float2(nx, ny);
+        }
+        float2 o[8];
 #pragma unroll
-            for (int o2 = 16; o2 > 0; o2 >>= 1) dw[j] += __shfl_xor_sync(0xffffffffu, dw[j], o2);
-            if (lane == 0) red[warp][j] = dw[j];
-        }
-        __syncthreads();                          // stage and red[] complete
-        if (tid <= K) {
-            float sum = 0.0f;
+        for (int i = 0; i < 8; ++i) {
+            float2 s = mul2(cc.wh[0], g[i + TAPS]);
 #pragma unroll
-            for (int q = 0; q < kThreads / 32; ++q) sum += red[q][tid];
-            a.partial[it * (K + 1) + tid] = sum;
+            for (int j = 1; j < K; ++j) s = fma2(cc.wh[j], g[i + TAPS - j], s);
+            o[i] = s;
         }
-        if (tid == 0) {
-            const int64_t nit = it + (int64_t)kStages * gridDim.x;
-            if (nit < items) issue_tile<T, 2>(a, smem, st, nit, a.x, a.dout);
+        store_pair8<T>(static_cast<T*>(a.dx) + row * L + t0, p0, p1, n, o);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            acc[K] = add2(acc[K], g[i]);
+#pragma unroll
+            for (int j = 0; j < K; ++j) acc[j] = fma2(g[i], z[i + j], acc[j]);
         }
-        __syncthreads();                          // red[] is free again
+        if (TAPS > 0 && t0 == 0 && tid == 0 && a.dinit != nullptr) {
+            T* dir = static_cast<T*>(a.dinit) + row * TAPS;
+#pragma unroll
+            for (int p = 0; p < TAPS; ++p) {
+                float s = 0.0f;
+#pragma unroll
+                for (int j = 0; j <= p; ++j) s = fmaf(cc.wh[j].x, g[p - j].x, s);
+                stf(dir + p, s);
+            }
+        }
+        cur.next(a);
+        ahead.next(a);
+        if (++st == kStages) { st = 0; ++use; }
     }
-    if (!ok && tid == 0) {
-        for (int64_t it = blockIdx.x + k * (int64_t)gridDim.x, j = k;
-             it < items && j < k + kStages; it += gridDim.x, ++j)
-            tc::mbar_wait(tc::smem_u32(smem + Lay::mbar_off + 8 * (j % kStages)), (uint32_t)((j / kStages) & 1));
-    }
+    if (ok && ring.count > 0) flush_run<K>(a, run0, acc);
+    ring.drain();
 }
 
-// dweight[c, j] and dbias[c]: partials of every (batch, chunk) of channel c.
+// dweight[c, j] and dbias[c]: partials of every (batch, chunk, slot) of channel
+// c, summed in a fixed order.
 template <int K>
 __global__ void finalize_kernel(const Args a, float* dweight, float* dbias) {
     const int64_t total = a.channels * (K + 1);
@@ -540,8 +715,33 @@ __global__ void finalize_kernel(const Args a, float* dweight, float* dbias) {
         const int j = (int)(i - c * (K + 1));
         float s = 0.0f;
         for (int64_t b = 0; b < a.batch; ++b) {
-            const float* p = a.partial + ((b * a.channels + c) * a.nchunks) * (K + 1) + j;
-            for (int64_t k = 0; k < a.nchunks; ++k) s += p[k * (K + 1)];
+            const int64_t m = a.nchunks * a.slots;
+            const float* p = a.partial + ((b * a.channels + c) * m) * (K + 1) + j;
+            for (int64_t k = 0; k < m; ++k) s += p[k * (K + 1)];
+        }
+        if (j < K) {
+            if (dweight) dweight[c * K + j] = s;
+        } else if (dbias) {
+            dbias[c] = s;
+        }
+    }
+}
+
+// dweight / dbias of the bulk path: channel c's items [c B', (c + 1) B')
+// (B' = batch * nchunks) fall into the ranges [k per, (k + 1) per) of one or
+// more CTAs; each such run left one partial per warp at its first item.
+// Summed in a fixed order.
+template <int K>
+__global__ void finalize_runs_kernel(const Args a, float* dweight, float* dbias) {
+    const int64_t total = a.channels * (K + 1), bp = a.batch * a.nchunks;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t c = i / (K + 1);
+        const int j = (int)(i - c * (K + 1));
+        float s = 0.0f;
+        for (int64_t r = c * bp; r < (c + 1) * bp; r = (r / a.per + 1) * a.per) {
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) s += a.partial[(r * kWarps + w) * (K + 1) + j];
         }
         if (j < K) {
             if (dweight) dweight[c * K + j] = s;
@@ -618,16 +818,19 @@ static void plan(const ssm_causal_conv1d_params* p, bool bulk, Args& a) {
     a.rows = p->batch * p->channels;
     a.chunk = bulk ? kTile : kSeg;
     a.nchunks = max64(1, ceil_div(p->length, a.chunk));
+    a.slots = bulk ? kWarps : 1;
     a.flags = p->flags;
     a.x = p->x; a.w = p->weight; a.bias = p->bias; a.init = p->initial_state;
     a.out = p->out; a.final_state = p->final_state;
     a.dout = p->dout; a.dx = p->dx; a.dinit = p->dinitial;
     a.partial = nullptr;
+    a.per = 0;
 }
 
-// Persistent grid: resident CTAs of the kernel on every SM, at most one per item.
+// Persistent grid: resident CTAs of the kernel on every SM, at most one per
+// item; sets a.per, the items of each CTA's contiguous range.
 template <typename F>
-static unsigned persistent_grid(F kernel, size_t smem, const Args& a) {
+static unsigned persistent_grid(F kernel, size_t smem, Args& a) {
     int dev = 0, sms = 148, per = 1;
     if (cudaGetDevice(&dev) == cudaSuccess)
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -635,17 +838,21 @@ static unsigned persistent_grid(F kernel, size_t smem, const Args& a) {
         cudaGetLastError();
         per = 1;
     }
-    return (unsigned)max64(1, min64((int64_t)sms * per, a.rows * a.nchunks));
+    const int64_t items = a.rows * a.nchunks;
+    const int64_t grid = max64(1, min64((int64_t)sms * per, items));
+    a.per = ceil_div(items, grid);
+    return (unsigned)ceil_div(items, a.per);
 }
 
 template <typename T, int K>
-static int launch_fwd(const Args& a, bool bulk, cudaStream_t st) {
+static int launch_fwd(Args a, bool bulk, cudaStream_t st) {
     if (bulk) {
         const size_t sm = BulkLayout<T, 1>::bytes;
         auto k = fwd_bulk_kernel<T, K>;
         if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
             return check_launch("causal_conv1d fwd: smem attribute");
-        k<<<persistent_grid(k, sm, a), kThreads, sm, st>>>(a);
+        const unsigned grid = persistent_grid(k, sm, a);
+        k<<<grid, kThreads, sm, st>>>(a);
     } else {
         fwd_plain_kernel<T, K><<<(unsigned)ceil_div(a.rows * a.nchunks, kThreads / 32), kThreads, 0, st>>>(a);
     }
@@ -653,19 +860,22 @@ static int launch_fwd(const Args& a, bool bulk, cudaStream_t st) {
 }
 
 template <typename T, int K>
-static int launch_bwd(const Args& a, bool bulk, float* dweight, float* dbias, cudaStream_t st) {
+static int launch_bwd(Args a, bool bulk, float* dweight, float* dbias, cudaStream_t st) {
     if (bulk) {
         const size_t sm = BulkLayout<T, 2>::bytes;
         auto k = bwd_bulk_kernel<T, K>;
         if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
             return check_launch("causal_conv1d bwd: smem attribute");
-        k<<<persistent_grid(k, sm, a), kThreads, sm, st>>>(a);
+        const unsigned grid = persistent_grid(k, sm, a);
+        k<<<grid, kThreads, sm, st>>>(a);
     } else {
         bwd_plain_kernel<T, K><<<(unsigned)ceil_div(a.rows * a.nchunks, kThreads / 32), kThreads, 0, st>>>(a);
     }
     if (int s = check_launch("causal_conv1d bwd")) return s;
     const int64_t total = a.channels * (K + 1);
-    finalize_kernel<K><<<(unsigned)min64(ceil_div(total, 256), 148 * 8), 256, 0, st>>>(a, dweight, dbias);
+    const unsigned fgrid = (unsigned)min64(ceil_div(total, 256), 148 * 8);
+    if (bulk) finalize_runs_kernel<K><<<fgrid, 256, 0, st>>>(a, dweight, dbias);
+    else finalize_kernel<K><<<fgrid, 256, 0, st>>>(a, dweight, dbias);
     return check_launch("causal_conv1d bwd finalize");
 }
 
@@ -720,9 +930,11 @@ using namespace ssm::conv;
 
 extern "C" int ssm_causal_conv1d_sizes(const ssm_causal_conv1d_params* p, size_t* workspace_bytes) {
     if (int s = validate(p)) return s;
-    Args a;
-    plan(p, false, a);   // the plain path has the most items
-    if (workspace_bytes) *workspace_bytes = (size_t)(a.rows * a.nchunks * (p->width + 1)) * 4;
+    Args a, b;
+    plan(p, false, a);
+    plan(p, true, b);
+    const int64_t slots = max64(a.nchunks * a.slots, b.nchunks * b.slots);
+    if (workspace_bytes) *workspace_bytes = (size_t)(a.rows * slots * (p->width + 1)) * 4;
     return SSM_OK;
 }
 
@@ -780,7 +992,7 @@ extern "C" int ssm_causal_conv1d_bwd(const ssm_causal_conv1d_params* p, void* st
     if (!p->x || !p->weight || !p->dout || !p->dx || ((p->flags & SSM_HAS_BIAS) && !p->bias) ||
         ((p->flags & SSM_HAS_INIT) && !p->initial_state))
         return fail(SSM_ERR_INVALID, "causal_conv1d bwd: null pointer");
-    const size_t need = (size_t)(a.rows * a.nchunks * (K + 1)) * 4;
+    const size_t need = (size_t)(a.rows * a.nchunks * a.slots * (K + 1)) * 4;
     if (p->workspace == nullptr || p->workspace_bytes < need)
         return fail(SSM_ERR_WORKSPACE, "causal_conv1d bwd: workspace smaller than ssm_causal_conv1d_sizes");
     a.partial = static_cast<float*>(p->workspace);

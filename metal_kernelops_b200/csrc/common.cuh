@@ -137,6 +137,47 @@ __device__ __forceinline__ float silu_grad_t(float a) {
     return s * fmaf(a, 1.0f - s, 1.0f);
 }
 
+// ---------------------------------------------------------- paired fp32 ----
+// Two independent fp32 lanes per instruction (the sm_100 paired FMA / MUL /
+// ADD): each lane is rounded exactly as the scalar fmaf, * or + rounds it, so a
+// kernel that carries two independent element streams as the .x / .y of a
+// float2 halves its FMA-pipe instructions without changing a result.
+__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+
+// SiLU of two pre-activations given as halves hp = a / 2 (an exact power-of-two
+// scaling): the values silu_t<T>(a) returns.
+template <typename T>
+__device__ __forceinline__ float2 silu2_half(float2 hp) {
+    if constexpr (sizeof(T) == 4) {
+        const float2 m = mul2(hp, f2(-2.0f * kLog2e));
+        const float2 d = add2(make_float2(exp2_mufu(m.x), exp2_mufu(m.y)), f2(1.0f));
+        return mul2(add2(hp, hp), make_float2(rcp_mufu(d.x), rcp_mufu(d.y)));
+    } else {
+        return fma2(hp, make_float2(tanh_mufu(hp.x), tanh_mufu(hp.y)), hp);
+    }
+}
+
+// 2 g silu'(a) for two lanes from hp = a / 2, with silu'(a) = s (1 + a (1 - s)).
+// 16-bit data: s = (1 + t) / 2 with t = tanh(hp), so the doubled gradient is
+// g (1 + t) (1 + hp (1 - t)).  fp32 data: s = rcp(1 + 2^(-a log2 e)).
+template <typename T>
+__device__ __forceinline__ float2 silu_grad2_half(float2 hp, float2 g) {
+    if constexpr (sizeof(T) == 4) {
+        const float2 m = mul2(hp, f2(-2.0f * kLog2e));
+        const float2 d = add2(make_float2(exp2_mufu(m.x), exp2_mufu(m.y)), f2(1.0f));
+        const float2 s = make_float2(rcp_mufu(d.x), rcp_mufu(d.y));
+        const float2 q = fma2(add2(hp, hp), fma2(s, f2(-1.0f), f2(1.0f)), f2(1.0f));
+        return mul2(add2(g, g), mul2(s, q));
+    } else {
+        const float2 t = make_float2(tanh_mufu(hp.x), tanh_mufu(hp.y));
+        const float2 q = fma2(hp, fma2(t, f2(-1.0f), f2(1.0f)), f2(1.0f));
+        return mul2(mul2(g, add2(t, f2(1.0f))), q);
+    }
+}
+
 // paired loads/stores of two consecutive elements as float2
 template <typename T> struct Io2;
 template <> struct Io2<float> {
