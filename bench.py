@@ -301,6 +301,18 @@ def run_scan(args, world, rank, device):
     bwd_gbs = bwd_b / (bwd_ms / 1e3) / 1e9
     fwd_gbs = fwd_b / (fwd_ms / 1e3) / 1e9
     step_gbs = (fwd_b + bwd_b) / ((fwd_ms + bwd_ms) / 1e3) / 1e9
+    # The compute floor the kernels sit against: one MUFU ex2 per element-state
+    # in the forward, two in the backward (pass A recompute + sub-block
+    # replay), at 16 per clock per SM and the SM clock sampled under load.
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    mhz = (ck_info or {}).get("sm_mhz") or 1965.0
+    ex2_per_s = sms * 16 * mhz * 1e6
+    es = b * d * l * n
+    fwd_floor, bwd_floor = es / ex2_per_s * 1e3, 2 * es / ex2_per_s * 1e3
+    mufu = {"pipe": "XU (MUFU ex2), 16 per clock per SM", "sm_mhz": mhz,
+            "ex2_per_element_state": {"fwd": 1, "bwd": 2},
+            "fwd_floor_ms": fwd_floor, "bwd_floor_ms": bwd_floor,
+            "fwd_frac": fwd_floor / fwd_ms, "bwd_frac": bwd_floor / bwd_ms}
     return {
         "metric": "selective-scan fwd+bwd B*L*D elems/s",
         "value": value,
@@ -325,7 +337,8 @@ def run_scan(args, world, rank, device):
                      "traffic": _traffic("selective_scan_bwd"),
                      "alg_bytes_per_launch": bwd_b,
                      "fwd": {"achieved": fwd_gbs, "frac": fwd_gbs / peaks["hbm_gbs"]},
-                     "fwd_bwd": {"achieved": step_gbs, "frac": step_gbs / peaks["hbm_gbs"]}},
+                     "fwd_bwd": {"achieved": step_gbs, "frac": step_gbs / peaks["hbm_gbs"]},
+                     "mufu_floor": mufu},
         "e2e": {"value": units / (e2e_ms / 1e3), "unit": "elem/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": ("metal_kernelops_b200.selective_scan + autograd, pinned host buffers, "
