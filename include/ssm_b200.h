@@ -170,6 +170,11 @@ typedef struct ssm_state_update_params {
     float* ddt_bias;
     void* workspace;
     size_t workspace_bytes;
+    /* forward only: with SSM_IO_DTYPE in flags, x, B, C and z are stored in
+     * io_dtype (an ssm_dtype) instead of `dtype` -- e.g. bf16 activations
+     * against an fp32 state, read without a widening copy; state, dt and y
+     * stay in `dtype`. */
+    int32_t io_dtype;
 } ssm_state_update_params;
 
 int ssm_state_update_sizes(const ssm_state_update_params* p, size_t* workspace_bytes);
@@ -314,6 +319,7 @@ int ssm_ss2d_scan_bwd(const ssm_ss2d_scan_params* p, void* stream);
  * ssm_causal_conv1d_sizes bytes; dweight/dbias may be NULL (not written).
  * ------------------------------------------------------------------------- */
 #define SSM_CONV_SILU    0x400u /* conv1d: act = SiLU */
+#define SSM_IO_DTYPE     0x800u /* decode forward: x, B, C, z in io_dtype       */
 
 typedef struct ssm_causal_conv1d_params {
     int64_t batch, channels, length, width;

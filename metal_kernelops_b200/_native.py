@@ -30,6 +30,7 @@ HAS_DY = 0x80
 HAS_DSTATE = 0x100
 CUDA_CORES = 0x200
 CONV_SILU = 0x400
+IO_DTYPE = 0x800
 
 EXPORTS = (
     "ssm_status_string", "ssm_last_error",
@@ -72,6 +73,7 @@ class StateUpdateParams(ctypes.Structure):
         ("grad_state", _P), ("dx", _P), ("ddt", _P), ("dA", _P), ("dB", _P), ("dC", _P),
         ("dD", _P), ("dz", _P), ("ddt_bias", _P),
         ("workspace", _P), ("workspace_bytes", _SZ),
+        ("io_dtype", _I32),
     ]
 
 

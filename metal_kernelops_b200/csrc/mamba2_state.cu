@@ -106,7 +106,8 @@ __device__ __forceinline__ float warp_sum(float v) {
 // about 96 KB of state reads in flight per SM.
 constexpr int kFwdRows = 8;
 
-template <typename T, int VEC>
+// T: state, dt and y; TI: x, B, C and z (T, or 16-bit against an fp32 state).
+template <typename T, typename TI, int VEC>
 __global__ void __launch_bounds__(kThreads, 3)
 fwd_kernel(const Args a) {
     extern __shared__ float s_rows[];   // [2][headdim]: decay, d*x
@@ -120,11 +121,11 @@ fwd_kernel(const Args a) {
     const bool d_per_head = a.flags & SSM_D_PER_HEAD, has_z = a.flags & SSM_HAS_Z;
     const T* st = reinterpret_cast<const T*>(a.state) + bh * (int64_t)P * N;
     T* ns = reinterpret_cast<T*>(a.new_state) + bh * (int64_t)P * N;
-    const T* Bg = reinterpret_cast<const T*>(a.B) + (b * a.ngroups + g) * N;
-    const T* Cg = reinterpret_cast<const T*>(a.C) + (b * a.ngroups + g) * N;
-    const T* xg = reinterpret_cast<const T*>(a.x) + bh * (int64_t)P;
+    const TI* Bg = reinterpret_cast<const TI*>(a.B) + (b * a.ngroups + g) * N;
+    const TI* Cg = reinterpret_cast<const TI*>(a.C) + (b * a.ngroups + g) * N;
+    const TI* xg = reinterpret_cast<const TI*>(a.x) + bh * (int64_t)P;
     const T* dtg = reinterpret_cast<const T*>(a.dt);
-    const T* zg = reinterpret_cast<const T*>(a.z) + bh * (int64_t)P;
+    const TI* zg = reinterpret_cast<const TI*>(a.z) + bh * (int64_t)P;
     T* yg = reinterpret_cast<T*>(a.y) + bh * (int64_t)P;
     const float Ah = a.A[h];
     const float bias = has_bias ? a.dt_bias[h] : 0.0f;
@@ -150,8 +151,8 @@ fwd_kernel(const Args a) {
             for (int r = 0; r < kFwdRows; ++r)
                 if (r < nr) Vec<T, VEC>::ld(st + (p0 + r) * N + n, sv[r]);
             float bv[VEC], cv[VEC];
-            Vec<T, VEC>::ld(Bg + n, bv);
-            Vec<T, VEC>::ld(Cg + n, cv);
+            Vec<TI, VEC>::ld(Bg + n, bv);
+            Vec<TI, VEC>::ld(Cg + n, cv);
 #pragma unroll
             for (int r = 0; r < kFwdRows; ++r) {
                 if (r < nr) {
@@ -392,6 +393,11 @@ static int validate(const ssm_state_update_params* p, int mode) {
         return fail(SSM_ERR_INVALID, "state_update: bad sizes");
     if (p->nheads % p->ngroups) return fail(SSM_ERR_INVALID, "state_update: ngroups must divide nheads");
     if (p->dtype < 0 || p->dtype > 2) return fail(SSM_ERR_UNSUPPORTED, "state_update: unknown dtype");
+    if ((p->flags & SSM_IO_DTYPE) && p->io_dtype != p->dtype) {
+        if (mode != 1) return fail(SSM_ERR_UNSUPPORTED, "state_update: io_dtype is for the forward only");
+        if (p->dtype != SSM_F32 || (p->io_dtype != SSM_BF16 && p->io_dtype != SSM_F16))
+            return fail(SSM_ERR_UNSUPPORTED, "state_update: io_dtype must be bf16/f16 against an fp32 state");
+    }
     if (p->dstate > 32 * 4 * 8) return fail(SSM_ERR_UNSUPPORTED, "state_update: dstate above 1024");
     if (p->batch * p->nheads > 0x7fffffffLL) return fail(SSM_ERR_UNSUPPORTED, "state_update: batch*nheads too large");
     const bool empty = p->batch == 0 || p->headdim == 0;
@@ -425,16 +431,16 @@ static Ws ws_layout(const ssm_state_update_params* p) {
 
 static bool aligned16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; }
 
-template <typename T>
+template <typename T, typename TI>
 static int launch_fwd(const Args& a, bool vec, cudaStream_t s) {
     const unsigned grid = (unsigned)(a.batch * a.nheads);
     const size_t smem = 2 * (size_t)a.headdim * sizeof(float);
     if (vec) {
-        if (smem > 48 * 1024) cudaFuncSetAttribute(fwd_kernel<T, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        fwd_kernel<T, 4><<<grid, kThreads, smem, s>>>(a);
+        if (smem > 48 * 1024) cudaFuncSetAttribute(fwd_kernel<T, TI, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        fwd_kernel<T, TI, 4><<<grid, kThreads, smem, s>>>(a);
     } else {
-        if (smem > 48 * 1024) cudaFuncSetAttribute(fwd_kernel<T, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        fwd_kernel<T, 1><<<grid, kThreads, smem, s>>>(a);
+        if (smem > 48 * 1024) cudaFuncSetAttribute(fwd_kernel<T, TI, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        fwd_kernel<T, TI, 1><<<grid, kThreads, smem, s>>>(a);
     }
     return check_launch("state_update fwd");
 }
@@ -456,16 +462,22 @@ extern "C" int ssm_state_update_fwd(const ssm_state_update_params* p, void* stre
     if (p->batch == 0 || p->headdim == 0) return SSM_OK;
     Args a;
     make_args(p, a);
-    const size_t esz = p->dtype == SSM_F32 ? 4 : 2;
-    // 4-element vectors need dstate % 4 == 0 and 4*esz-byte aligned rows
+    const int io = (p->flags & SSM_IO_DTYPE) ? p->io_dtype : p->dtype;
+    const size_t esz = p->dtype == SSM_F32 ? 4 : 2, isz = io == SSM_F32 ? 4 : 2;
+    // 4-element vectors need dstate % 4 == 0 and 4*size-byte aligned rows
     const bool vec = p->dstate % 4 == 0 &&
-                     ((reinterpret_cast<uintptr_t>(p->state) | reinterpret_cast<uintptr_t>(p->new_state) |
-                       reinterpret_cast<uintptr_t>(p->B) | reinterpret_cast<uintptr_t>(p->C)) % (4 * esz)) == 0;
+                     ((reinterpret_cast<uintptr_t>(p->state) | reinterpret_cast<uintptr_t>(p->new_state)) %
+                      (4 * esz)) == 0 &&
+                     ((reinterpret_cast<uintptr_t>(p->B) | reinterpret_cast<uintptr_t>(p->C)) % (4 * isz)) == 0;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (io != p->dtype) {   // validated: 16-bit inputs against an fp32 state
+        if (io == SSM_BF16) return launch_fwd<float, __nv_bfloat16>(a, vec, s);
+        return launch_fwd<float, __half>(a, vec, s);
+    }
     switch (p->dtype) {
-        case SSM_F32: return launch_fwd<float>(a, vec, s);
-        case SSM_BF16: return launch_fwd<__nv_bfloat16>(a, vec, s);
-        default: return launch_fwd<__half>(a, vec, s);
+        case SSM_F32: return launch_fwd<float, float>(a, vec, s);
+        case SSM_BF16: return launch_fwd<__nv_bfloat16, __nv_bfloat16>(a, vec, s);
+        default: return launch_fwd<__half, __half>(a, vec, s);
     }
 }
 

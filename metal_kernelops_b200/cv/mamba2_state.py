@@ -15,7 +15,9 @@ B, C (batch, ngroups, dstate); D (nheads,) or (nheads, dim); dt_bias (nheads,).
 Contract kept from the reference (:26-31, :565-598, :805-819): ``state`` is
 never modified unless it is passed as ``out_state``; ``out_state`` is written
 in place, must match ``state`` in shape and dtype, be contiguous and not require
-grad; x, dt, B, C, z are cast to ``state.dtype`` and A, D, dt_bias to float32;
+grad; x, dt, B, C, z are cast to ``state.dtype`` and A, D, dt_bias to float32
+(without grad, 16-bit x, B, C, z against a float32 state are widened inside
+the kernel instead -- the same exact conversion, without the copies);
 the backward computes in float32 and casts each gradient back to its input's
 dtype; without any input requiring grad the kernel is called directly (the
 decode-loop path).  ``ValueError`` on contract violations, CPU tensors
@@ -59,6 +61,9 @@ def _params(state, x, dt, A, B, C, D, z, dt_bias, softplus):
 def _launch(state, x, dt, A, B, C, D, z, dt_bias, softplus, new_state):
     y = torch.empty(state.shape[:3], dtype=state.dtype, device=state.device)
     p = _params(state, x, dt, A, B, C, D, z, dt_bias, softplus)
+    if x.dtype != state.dtype:      # x, B, C (and z) read in their own dtype
+        p.flags |= nat.IO_DTYPE
+        p.io_dtype = nat.dtype_code(x.dtype)
     p.new_state, p.y = new_state.data_ptr(), y.data_ptr()
     nat.check(nat.lib().ssm_state_update_fwd(p, nat.stream_of(state)), "mamba2_state_update")
     return y
@@ -220,8 +225,17 @@ def mamba2_state_update(state, x, dt, A, B, C, D=None, z=None, dt_bias=None,
     if state.dtype not in _DTYPES:
         raise ValueError(f"state must be float32, float16 or bfloat16, got {state.dtype}")
     dtype = state.dtype
-    x, dt, B, C = (t.to(dtype) for t in (x, dt, B, C))
-    z = z.to(dtype) if z is not None else None
+    needs_grad = torch.is_grad_enabled() and any(
+        t is not None and t.requires_grad for t in (state, x, dt, A, B, C, D, z, dt_bias))
+    # The forward kernel reads 16-bit x, B, C (and z) against an fp32 state
+    # directly; everything else is brought to the state's dtype.
+    io = (not needs_grad and dtype == torch.float32 and x.dtype in (torch.bfloat16, torch.float16)
+          and B.dtype == x.dtype and C.dtype == x.dtype and (z is None or z.dtype == x.dtype))
+    if io:
+        dt = dt.to(dtype)
+    else:
+        x, dt, B, C = (t.to(dtype) for t in (x, dt, B, C))
+        z = z.to(dtype) if z is not None else None
     A = A.float()
     D = D.float() if D is not None else None
     dt_bias = dt_bias.float() if dt_bias is not None else None
@@ -231,8 +245,6 @@ def mamba2_state_update(state, x, dt, A, B, C, D=None, z=None, dt_bias=None,
     dt_bias = dt_bias.contiguous() if dt_bias is not None else None
     state_c = state.contiguous()
 
-    needs_grad = torch.is_grad_enabled() and any(
-        t is not None and t.requires_grad for t in (state, x, dt, A, B, C, D, z, dt_bias))
     if not needs_grad:
         if out_state is None:
             return torch.ops.b200ssm.state_update_fwd(state_c, x, dt, A, B, C, D, z, dt_bias,

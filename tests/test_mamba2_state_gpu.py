@@ -223,3 +223,23 @@ def test_config4_step_in_place():
     scale = max(want_y.abs().max().item(), want_s.abs().max().item())
     assert (s[b].cpu().double() - want_s).abs().max().item() <= 1e-5 * max(scale, 1)
     assert (y[b].float().cpu().double() - want_y).abs().max().item() <= 1e-5 * max(scale, 1)
+
+
+@pytest.mark.parametrize("io", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape,use_z", [((3, 8, 16, 64, 2), True), ((2, 4, 5, 7, 2), False)],
+                         ids=["vec", "odd-dstate"])
+def test_io_dtype_matches_widened_inputs(io, shape, use_z):
+    """16-bit x, B, C, z against an fp32 state are read as they are (no
+    widening copies); widening bf16/fp16 to fp32 is exact, so the results equal
+    the call on pre-widened inputs bit for bit."""
+    upd = _mk()
+    st, x, dt, A, B, C, D, z, bias = build(*shape, use_z=use_z)
+    x, B, C = (t.to(io) for t in (x, B, C))
+    z = z.to(io) if z is not None else None
+    cu = [None if t is None else t.cuda() for t in (st, x, dt, A, B, C, D, z, bias)]
+    wide = [None if t is None else t.float() for t in cu]
+    with torch.no_grad():
+        y1, s1 = upd(*cu, dt_softplus=True)
+        y2, s2 = upd(*wide, dt_softplus=True)
+    assert y1.dtype == torch.float32 and s1.dtype == torch.float32
+    assert torch.equal(y1, y2) and torch.equal(s1, s2)
