@@ -534,32 +534,40 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
         {
             const int l = tid;
             const float csl = msh.cs2[l];
-            for (int j = 0; j < Q / 16; ++j) {
-                uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
-                if (16 * j <= 32 * warp + 31) {          // warp-uniform: tcgen05.ld is .sync.aligned
-                    float v[16];
-                    tc::tmem_ld16(tm + lane_off + 16 * j, v);
-                    tc::tmem_wait_ld(v);
-                    if (16 * j > l) {
-                        // whole block above the diagonal for this row: zeros
-                    } else if (16 * j + 15 < l) {
-                        const float rf = exp2_mufu(csl - msh.cs2[16 * j + 15]);
-#pragma unroll
-                        for (int k = 0; k < 16; ++k) v[k] *= rf * msh.cf[16 * j + k] * msh.d[16 * j + k];
-                    } else {
-#pragma unroll
-                        for (int k = 0; k < 16; ++k) {
-                            const int s = 16 * j + k;
-                            v[k] = s <= l ? v[k] * exp2_mufu(csl - msh.cs2[s]) * msh.d[s] : 0.0f;
-                        }
-                    }
-                    if (16 * j <= l) {
-                        lo = pack8<T>(v);
-                        hi = pack8<T>(v + 8);
-                    }
+            // blocks j, j + 1 per TMEM wait; a warp's last live block 2 warp + 1
+            // is odd, so a pair is live or dead as a whole (warp-uniform:
+            // tcgen05.ld is .sync.aligned)
+            for (int j0 = 0; j0 < Q / 16; j0 += 2) {
+                float v[2][16];
+                const bool live = 16 * j0 <= 32 * warp + 31;
+                if (live) {
+                    tc::tmem_ld16(tm + lane_off + 16 * j0, v[0]);
+                    tc::tmem_ld16(tm + lane_off + 16 * j0 + 16, v[1]);
+                    tc::tmem_wait_ld(v[0]);
+                    tc::tmem_pin(v[1]);
                 }
-                *reinterpret_cast<uint4*>(sM + tc::tile_off(l, 2 * j, WB)) = lo;
-                *reinterpret_cast<uint4*>(sM + tc::tile_off(l, 2 * j + 1, WB)) = hi;
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int j = j0 + u;
+                    uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+                    if (live && 16 * j <= l) {
+                        if (16 * j + 15 < l) {
+                            const float rf = exp2_mufu(csl - msh.cs2[16 * j + 15]);
+#pragma unroll
+                            for (int k = 0; k < 16; ++k) v[u][k] *= rf * msh.cf[16 * j + k] * msh.d[16 * j + k];
+                        } else {
+#pragma unroll
+                            for (int k = 0; k < 16; ++k) {
+                                const int s = 16 * j + k;
+                                v[u][k] = s <= l ? v[u][k] * exp2_mufu(csl - msh.cs2[s]) * msh.d[s] : 0.0f;
+                            }
+                        }
+                        lo = pack8<T>(v[u]);
+                        hi = pack8<T>(v[u] + 8);
+                    }
+                    *reinterpret_cast<uint4*>(sM + tc::tile_off(l, 2 * j, WB)) = lo;
+                    *reinterpret_cast<uint4*>(sM + tc::tile_off(l, 2 * j + 1, WB)) = hi;
+                }
             }
         }
         const bool lw = tc::mbar_wait(lb, lpar);      // this head's x and H_c
@@ -578,6 +586,14 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
                 tc::mma_f16(tm + 192, tc::desc_k(aC, WB, 2 * ks), tc::desc_mn(aH, WH, 16 * ks), idy, ks > 0);
             tc::commit(tc::smem_u32(&mbar));
         }
+        // this row's gate inputs, loaded while the GEMMs run (the waits below
+        // order every later memory access after them)
+        const int64_t row = ((b * L + t0 + tid) * H + h) * P;
+        uint4 zr[P / 8];
+        if (has_z && tid < valid) {
+#pragma unroll
+            for (int q = 0; q < P / 8; ++q) zr[q] = *reinterpret_cast<const uint4*>(zg + row + 8 * q);
+        }
         if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(22); ok = false; }
         phase ^= 1;
         tc::fence_after();
@@ -585,9 +601,9 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
         if (ok) {
             const int l = tid;
             const bool live = l < valid;
-            const int64_t row = ((b * L + t0 + l) * H + h) * P;
             const float el = exp2_mufu(msh.cs2[l]);
             const float Dh = hsh.D[hk];
+#pragma unroll
             for (int j = 0; j < P / 16; ++j) {
                 float yi[16], ye[16];
                 tc::tmem_ld16(tm + lane_off + 128 + 16 * j, yi);
@@ -610,8 +626,8 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
                         *reinterpret_cast<uint4*>(ypg + row + 16 * j + 8) = pack8<T>(yv + 8);
                     }
                     float zv[16];
-                    Pk<T>::unpack(*reinterpret_cast<const uint4*>(zg + row + 16 * j), zv);
-                    Pk<T>::unpack(*reinterpret_cast<const uint4*>(zg + row + 16 * j + 8), zv + 8);
+                    Pk<T>::unpack(zr[2 * j], zv);
+                    Pk<T>::unpack(zr[2 * j + 1], zv + 8);
 #pragma unroll
                     for (int k = 0; k < 16; ++k) yv[k] *= zv[k] * sigmoid_f(zv[k]);
                 }
@@ -630,7 +646,9 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
 
 // ====================================================================== B1 ==
 // One CTA per (b, h), chunks in reverse.  TMEM: dH^T [0,64), C H_c^T [64,128).
-template <typename T>
+// GATED: z given (a separate instantiation, so that the ungated one carries no
+// registers for the gate inputs it prefetches).
+template <typename T, bool GATED>
 __global__ void __launch_bounds__(kThreads) dstates_kernel(const __grid_constant__ Args a) {
     extern __shared__ __align__(128) unsigned char sm_raw[];
     unsigned char* const sm = aligned_smem(sm_raw);
@@ -648,7 +666,7 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const __grid_constant
     const int64_t L = a.length, H = a.nheads;
     const float Ah = a.A[h];
     const float bias = (a.flags & SSM_HAS_BIAS) ? a.dt_bias[h] : 0.0f;
-    const bool has_z = a.flags & SSM_HAS_Z;
+    const bool has_z = GATED;
     const T* zg = reinterpret_cast<const T*>(a.z);
     const T* ypg = reinterpret_cast<const T*>(a.ypre);
     T* dzg = reinterpret_cast<T*>(a.dz);
@@ -699,6 +717,16 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const __grid_constant
         }
         const Steps st = steps_of(a, raw, c, Ah, s_scan);
         if (tid == Q - 1) s_T = st.cs;
+        // the gate inputs of row l = tid, loaded while the tiles land
+        const int64_t row = ((b * L + t0 + tid) * H + h) * P;
+        uint4 zr[WX], ypr[WX];
+        if (has_z && tid < valid) {
+#pragma unroll
+            for (int j = 0; j < WX; ++j) {
+                zr[j] = *reinterpret_cast<const uint4*>(zg + row + 8 * j);
+                if (dzg) ypr[j] = *reinterpret_cast<const uint4*>(ypg + row + 8 * j);
+            }
+        }
         const bool lw = tc::mbar_wait(lb, lpar);
         if (!lw) report(32);
         else if (tid == 0) lpend = ~0u;
@@ -708,14 +736,14 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const __grid_constant
         {
             const int l = tid;
             const float el = exp2_mufu(st.cs * kLog2e);
-            const int64_t row = ((b * L + t0 + l) * H + h) * P;
+#pragma unroll
             for (int j = 0; j < WX; ++j) {
                 float f[8];
                 Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(l, j, WX)), f);
                 if (has_z && l < valid) {
                     float zv[8], yp[8], dz[8];
-                    Pk<T>::unpack(*reinterpret_cast<const uint4*>(zg + row + 8 * j), zv);
-                    if (dzg) Pk<T>::unpack(*reinterpret_cast<const uint4*>(ypg + row + 8 * j), yp);
+                    Pk<T>::unpack(zr[j], zv);
+                    if (dzg) Pk<T>::unpack(ypr[j], yp);
 #pragma unroll
                     for (int k = 0; k < 8; ++k) {
                         const float sg = sigmoid_f(zv[k]);
@@ -1396,9 +1424,13 @@ static int run_fwd(const Args& a, cudaStream_t s) {
 
 template <typename T>
 static int run_bwd(const Args& a, const ssm_chunk_scan_params* p, cudaStream_t s) {
-    if (int e = set_smem((const void*)dstates_kernel<T>, kSmemDstates + kSmemPad)) return e;
+    if (int e = set_smem((const void*)dstates_kernel<T, false>, kSmemDstates + kSmemPad)) return e;
+    if (int e = set_smem((const void*)dstates_kernel<T, true>, kSmemDstates + kSmemPad)) return e;
     if (int e = set_smem((const void*)grads_kernel<T>, kSmemGrads + kSmemPad)) return e;
-    dstates_kernel<T><<<dim3((unsigned)a.nheads, (unsigned)a.batch), kThreads, kSmemDstates + kSmemPad, s>>>(a);
+    if (a.flags & SSM_HAS_Z)
+        dstates_kernel<T, true><<<dim3((unsigned)a.nheads, (unsigned)a.batch), kThreads, kSmemDstates + kSmemPad, s>>>(a);
+    else
+        dstates_kernel<T, false><<<dim3((unsigned)a.nheads, (unsigned)a.batch), kThreads, kSmemDstates + kSmemPad, s>>>(a);
     if (int e = check_launch("chunk_scan bwd (tensor cores): dstates")) return e;
     grads_kernel<T><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)a.batch), kGradThreads, kSmemGrads + kSmemPad, s>>>(a);
     if (int e = check_launch("chunk_scan bwd (tensor cores): grads")) return e;
