@@ -399,6 +399,11 @@ typedef struct ssm_gated_rmsnorm_params {
     float* dbias;
     void* workspace;
     size_t workspace_bytes;
+    /* elements between consecutive rows of x and of z (0: `features`, the
+     * contiguous layout); features are contiguous within a row.  Lets z (and
+     * x) be column slices of a wider projection output.  out, dy, dx and dz
+     * are contiguous. */
+    int64_t x_row_stride, z_row_stride;
 } ssm_gated_rmsnorm_params;
 
 int ssm_gated_rmsnorm_sizes(const ssm_gated_rmsnorm_params* p, size_t* workspace_bytes);

@@ -131,6 +131,7 @@ class GatedRmsNormParams(ctypes.Structure):
         ("x", _P), ("z", _P), ("weight", _P), ("bias", _P), ("out", _P), ("rstd", _P),
         ("dy", _P), ("dx", _P), ("dz", _P), ("dweight", _P), ("dbias", _P),
         ("workspace", _P), ("workspace_bytes", _SZ),
+        ("x_row_stride", _I64), ("z_row_stride", _I64),
     ]
 
 

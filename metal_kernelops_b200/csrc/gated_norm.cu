@@ -44,6 +44,7 @@ constexpr int kGateNone = 0, kGateBefore = 1, kGateAfter = 2;
 
 struct Args {
     int64_t rows, features, group, ngroups;
+    int64_t xs, zs;                       // row strides of x and z (elements)
     int64_t row_blocks, rows_per_block;
     float eps;
     int gate;
@@ -235,7 +236,7 @@ struct RowRing {
     static constexpr size_t bytes = (size_t)2 * NT * GP * sizeof(T);   // per warp
     T* base;
     __device__ const T* at(int b, int t, int e0) const { return base + (b * NT + t) * GP + e0; }
-    __device__ void issue(int b, const T* const* src, int64_t off, int64_t G) const {
+    __device__ void issue(int b, const T* const* src, const int64_t* off, int64_t G) const {
         const int lane = threadIdx.x & 31;
         __syncwarp();                             // the lane's reads of stage b are done
 #pragma unroll
@@ -245,8 +246,8 @@ struct RowRing {
 #pragma unroll
                 for (int t = 0; t < NT; ++t) {
                     const uint32_t d = tc::smem_u32(base + (b * NT + t) * GP + e0);
-                    if constexpr (V * sizeof(T) == 16) tc::cp_async16(d, src[t] + off + e0);
-                    else tc::cp_async8(d, src[t] + off + e0);
+                    if constexpr (V * sizeof(T) == 16) tc::cp_async16(d, src[t] + off[t] + e0);
+                    else tc::cp_async8(d, src[t] + off[t] + e0);
                 }
             }
         }
@@ -275,11 +276,14 @@ fwd_kernel(const Args a) {
     stage_wb<GP>(a, g, ws, bs);
     __syncthreads();
     const float inv_g = 1.0f / (float)G;
+    // row offsets of x and z
+    auto offs = [&](int64_t row, int64_t* o) { o[0] = row * a.xs + g * G; o[1] = row * a.zs + g * G; };
     int b = 0;
-    if (r0 + warp < r1) ring.issue(0, src, (r0 + warp) * F + g * G, G);
+    int64_t off[2];
+    if (r0 + warp < r1) { offs(r0 + warp, off); ring.issue(0, src, off, G); }
     for (int64_t row = r0 + warp; row < r1; row += kWarps, b ^= 1) {
         const int64_t base = row * F + g * G;
-        if (row + kWarps < r1) ring.issue(b ^ 1, src, base + kWarps * F, G);
+        if (row + kWarps < r1) { offs(row + kWarps, off); ring.issue(b ^ 1, src, off, G); }
         else tc::cp_async_commit();              // keep one group per row
         tc::cp_async_wait<1>();
         float2 xb[NV][M], gt[NV][M];
@@ -370,12 +374,19 @@ bwd_kernel(const Args a) {
 #pragma unroll
         for (int m = 0; m < M; ++m) dwa[k][m] = f2(0.0f);
 
+    // row offsets of x, dy and z
+    auto offs = [&](int64_t row, int64_t* o) {
+        o[0] = row * a.xs + g * G;
+        o[1] = row * F + g * G;
+        o[2] = row * a.zs + g * G;
+    };
     int b = 0;
-    if (r0 + warp < r1) ring.issue(0, src, (r0 + warp) * F + g * G, G);
+    int64_t off[3];
+    if (r0 + warp < r1) { offs(r0 + warp, off); ring.issue(0, src, off, G); }
     for (int64_t row = r0 + warp; row < r1; row += kWarps, b ^= 1) {
         const int64_t base = row * F + g * G;
         const float r = a.rstd[row * a.ngroups + g];
-        if (row + kWarps < r1) ring.issue(b ^ 1, src, base + kWarps * F, G);
+        if (row + kWarps < r1) { offs(row + kWarps, off); ring.issue(b ^ 1, src, off, G); }
         else tc::cp_async_commit();
         tc::cp_async_wait<1>();
         const float2 r2 = f2(r);
@@ -491,12 +502,12 @@ fwd_stream_kernel(const Args a) {
     const T* z = static_cast<const T*>(a.z);
     T* out = static_cast<T*>(a.out);
     for (int64_t row = r0; row < r1; ++row) {
-        const int64_t base = row * F + g * G;
+        const int64_t base = row * F + g * G, xb = row * a.xs + g * G, zb = row * a.zs + g * G;
         float ss = 0.0f;
         for (int64_t e0 = (int64_t)threadIdx.x * V; e0 < G; e0 += (int64_t)kThreads * V) {
             float xv[V], zv[V];
-            VecIo<T, V>::ld(x + base + e0, xv);
-            if (a.gate == kGateBefore) VecIo<T, V>::ld(z + base + e0, zv);
+            VecIo<T, V>::ld(x + xb + e0, xv);
+            if (a.gate == kGateBefore) VecIo<T, V>::ld(z + zb + e0, zv);
 #pragma unroll
             for (int i = 0; i < V; ++i) {
                 const float xb = a.gate == kGateBefore ? xv[i] * zv[i] * sigmoid_t<T>(zv[i]) : xv[i];
@@ -508,8 +519,8 @@ fwd_stream_kernel(const Args a) {
         if (a.rstd != nullptr && threadIdx.x == 0) a.rstd[row * a.ngroups + g] = r;
         for (int64_t e0 = (int64_t)threadIdx.x * V; e0 < G; e0 += (int64_t)kThreads * V) {
             float xv[V], zv[V], o[V];
-            VecIo<T, V>::ld(x + base + e0, xv);
-            if (a.gate != kGateNone) VecIo<T, V>::ld(z + base + e0, zv);
+            VecIo<T, V>::ld(x + xb + e0, xv);
+            if (a.gate != kGateNone) VecIo<T, V>::ld(z + zb + e0, zv);
 #pragma unroll
             for (int i = 0; i < V; ++i) {
                 const float gt = a.gate != kGateNone ? zv[i] * sigmoid_t<T>(zv[i]) : 1.0f;
@@ -543,14 +554,14 @@ bwd_stream_kernel(const Args a) {
             if (dbp) dbp[e0 + i] = 0.0f;
         }
     for (int64_t row = r0; row < r1; ++row) {
-        const int64_t base = row * F + g * G;
+        const int64_t base = row * F + g * G, xb = row * a.xs + g * G, zb = row * a.zs + g * G;
         const float r = a.rstd[row * a.ngroups + g];
         float c1 = 0.0f;
         for (int64_t e0 = (int64_t)threadIdx.x * V; e0 < G; e0 += (int64_t)kThreads * V) {
             float xv[V], zv[V], dv[V];
-            VecIo<T, V>::ld(x + base + e0, xv);
+            VecIo<T, V>::ld(x + xb + e0, xv);
             VecIo<T, V>::ld(dy + base + e0, dv);
-            if (a.gate != kGateNone) VecIo<T, V>::ld(z + base + e0, zv);
+            if (a.gate != kGateNone) VecIo<T, V>::ld(z + zb + e0, zv);
 #pragma unroll
             for (int i = 0; i < V; ++i)
                 c1 += elem_c1<T>(xv[i], a.gate != kGateNone ? zv[i] : 0.0f, dv[i], a.w[g * G + e0 + i], r, a.gate);
@@ -558,9 +569,9 @@ bwd_stream_kernel(const Args a) {
         c1 = block_sum(c1, red) / (float)G;
         for (int64_t e0 = (int64_t)threadIdx.x * V; e0 < G; e0 += (int64_t)kThreads * V) {
             float xv[V], zv[V], dv[V], ox[V], oz[V];
-            VecIo<T, V>::ld(x + base + e0, xv);
+            VecIo<T, V>::ld(x + xb + e0, xv);
             VecIo<T, V>::ld(dy + base + e0, dv);
-            if (a.gate != kGateNone) VecIo<T, V>::ld(z + base + e0, zv);
+            if (a.gate != kGateNone) VecIo<T, V>::ld(z + zb + e0, zv);
 #pragma unroll
             for (int i = 0; i < V; ++i) {
                 const int64_t f = g * G + e0 + i;
@@ -599,6 +610,8 @@ static int validate(const ssm_gated_rmsnorm_params* p) {
     if (p->dtype < SSM_F32 || p->dtype > SSM_F16) return fail(SSM_ERR_UNSUPPORTED, "rmsnorm_gated: dtype");
     if (p->gate < kGateNone || p->gate > kGateAfter) return fail(SSM_ERR_INVALID, "rmsnorm_gated: gate mode");
     if (p->features / p->group_size > 65535) return fail(SSM_ERR_UNSUPPORTED, "rmsnorm_gated: too many groups");
+    if ((p->x_row_stride && p->x_row_stride < p->features) || (p->z_row_stride && p->z_row_stride < p->features))
+        return fail(SSM_ERR_INVALID, "rmsnorm_gated: a row stride is below features");
     return SSM_OK;
 }
 
@@ -609,6 +622,10 @@ struct Shape { int v, nv, sv; };
 static bool aligned(const void* p, int64_t bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
 static bool ptrs_ok(const ssm_gated_rmsnorm_params* p, bool bwd, int64_t bytes) {
     if (!aligned(p->x, bytes) || (p->gate && !aligned(p->z, bytes))) return false;
+    const int64_t esz = p->dtype == SSM_F32 ? 4 : 2;
+    const int64_t xs = p->x_row_stride ? p->x_row_stride : p->features;
+    const int64_t zs = p->z_row_stride ? p->z_row_stride : p->features;
+    if ((xs * esz) % bytes || (p->gate && (zs * esz) % bytes) || (p->features * esz) % bytes) return false;
     if (!bwd) return aligned(p->out, bytes);
     return aligned(p->dy, bytes) && aligned(p->dx, bytes) && (!p->gate || aligned(p->dz, bytes));
 }
@@ -685,6 +702,8 @@ static void plan(const ssm_gated_rmsnorm_params* p, Args& a) {
     a.features = p->features;
     a.group = p->group_size;
     a.ngroups = p->features / p->group_size;
+    a.xs = p->x_row_stride ? p->x_row_stride : p->features;
+    a.zs = p->z_row_stride ? p->z_row_stride : p->features;
     const int64_t want = 148 * 4 * 4;
     const int64_t per_group = max64(1, ceil_div(want, a.ngroups));
     a.rows_per_block = max64(kWarps, ceil_div(max64(a.rows, 1), per_group));

@@ -46,6 +46,9 @@ def _params(x, weight, bias, z, eps, group, gate):
     p.eps = eps
     p.x, p.weight = x.data_ptr(), weight.data_ptr()
     p.z = z.data_ptr() if z is not None else None
+    # row strides (0: contiguous; a single row's stride is never used)
+    p.x_row_stride = x.stride(0) if x.shape[0] > 1 else 0
+    p.z_row_stride = z.stride(0) if z is not None and z.shape[0] > 1 else 0
     p.bias = bias.data_ptr() if bias is not None else None
     return p
 
@@ -54,7 +57,7 @@ def _params(x, weight, bias, z, eps, group, gate):
 def _fwd(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], z: Optional[torch.Tensor],
          eps: float, group: int, gate: int, save: bool) -> tuple[torch.Tensor, torch.Tensor]:
     p = _params(x, weight, bias, z, eps, group, gate)
-    out = torch.empty_like(x)
+    out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
     rstd = torch.empty((x.shape[0] * (x.shape[1] // group)) if save else 0, dtype=torch.float32,
                        device=x.device)
     p.out = out.data_ptr()
@@ -65,8 +68,8 @@ def _fwd(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], z:
 
 @_fwd.register_fake
 def _(x, weight, bias, z, eps, group, gate, save):
-    return torch.empty_like(x), x.new_empty((x.shape[0] * (x.shape[1] // group)) if save else 0,
-                                            dtype=torch.float32)
+    return x.new_empty(x.shape), x.new_empty((x.shape[0] * (x.shape[1] // group)) if save else 0,
+                                             dtype=torch.float32)
 
 
 @torch.library.custom_op("b200ssm::gated_rmsnorm_bwd", mutates_args=(), device_types="cuda")
@@ -76,8 +79,8 @@ def _bwd(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, bias: Optional
     p = _params(x, weight, bias, z, eps, group, gate)
     ws_bytes = nat._SZ()
     nat.check(nat.lib().ssm_gated_rmsnorm_sizes(p, ws_bytes), "rmsnorm_gated backward")
-    dx = torch.empty_like(x)
-    dz = torch.empty_like(z) if z is not None else x.new_empty(0)
+    dx = x.new_empty(x.shape)
+    dz = z.new_empty(z.shape) if z is not None else x.new_empty(0)
     dw = torch.empty(x.shape[1], dtype=torch.float32, device=x.device)
     db = torch.empty(x.shape[1] if bias is not None else 0, dtype=torch.float32, device=x.device)
     ws = torch.empty(max(ws_bytes.value, 1), dtype=torch.uint8, device=x.device)
@@ -94,9 +97,9 @@ def _bwd(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, bias: Optional
 @_bwd.register_fake
 def _(dy, x, weight, bias, z, rstd, eps, group, gate):
     f32 = dict(dtype=torch.float32)
-    return (torch.empty_like(x), x.new_empty(x.shape[1], **f32),
+    return (x.new_empty(x.shape), x.new_empty(x.shape[1], **f32),
             x.new_empty(x.shape[1] if bias is not None else 0, **f32),
-            torch.empty_like(z) if z is not None else x.new_empty(0))
+            z.new_empty(z.shape) if z is not None else x.new_empty(0))
 
 
 def _setup(ctx, inputs, output):
@@ -116,6 +119,16 @@ def _backward(ctx, dout, drstd):
 
 
 _fwd.register_autograd(_backward, setup_context=_setup)
+
+
+def _rows(t, features):
+    """t as (rows, features) with contiguous features: a view when its rows are
+    evenly spaced and do not overlap (a column slice of a wider projection
+    output, say), else a contiguous copy."""
+    t2 = t.reshape(-1, features)
+    if t2.stride(1) == 1 and (t2.shape[0] <= 1 or t2.stride(0) >= features):
+        return t2
+    return t2.contiguous()
 
 
 def rmsnorm_gated(x, weight, bias=None, z=None, eps=1e-5, group_size=None, norm_before_gate=True):
@@ -162,8 +175,8 @@ def rmsnorm_gated(x, weight, bias=None, z=None, eps=1e-5, group_size=None, norm_
     if x.numel() == 0:
         return x.new_empty(x.shape)
     shape = x.shape
-    x2 = x.reshape(-1, features).contiguous()
-    z2 = z.to(x.dtype).reshape(-1, features).contiguous() if z is not None else None
+    x2 = _rows(x, features)
+    z2 = _rows(z.to(x.dtype), features) if z is not None else None
     w32 = weight.float().contiguous()
     b32 = bias.float().contiguous() if bias is not None else None
     gate = _GATE_NONE if z is None else (_GATE_AFTER if norm_before_gate else _GATE_BEFORE)

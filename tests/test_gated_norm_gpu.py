@@ -183,3 +183,40 @@ def test_deterministic():
         runs.append((out.detach(),) + torch.autograd.grad(out.float().square().sum(), leaves))
     for vals in zip(*runs):
         assert all(torch.equal(vals[0], v) for v in vals[1:])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("norm_before_gate", [False, True])
+def test_column_slices(dtype, norm_before_gate):
+    """x and z as column slices of wider projection outputs (the Mamba-2 layer's
+    z is such a slice) are read through their row strides, not copied: forward
+    and every gradient equal the call on contiguous copies bit for bit when the
+    rows keep 16-byte alignment, and match the fp64 oracle when they do not."""
+    gn = _gn()
+    rows, feat, group = 96, 640, 320
+    for extra, exact in ((64, True), (3, False)):
+        wide_x = _make((rows, feat + extra), dtype, 71)
+        wide_z = _make((rows, 2 * feat + extra), dtype, 72)
+        w = _make((feat,), torch.float32, 73)
+        dy = _make((rows, feat), dtype, 74)
+        runs = []
+        for contiguous in (False, True):
+            x = wide_x[:, extra // 2:extra // 2 + feat].detach()
+            z = wide_z[:, feat:2 * feat].detach()
+            if contiguous:
+                x, z = x.contiguous(), z.contiguous()
+            x.requires_grad_(True)
+            z.requires_grad_(True)
+            wl = w.clone().requires_grad_(True)
+            out = gn.rmsnorm_gated(x, wl, z=z, group_size=group, norm_before_gate=norm_before_gate)
+            out.backward(dy)
+            runs.append([t.detach().clone() for t in (out, x.grad, z.grad, wl.grad)])
+        if exact:
+            for a_, b_ in zip(*runs):
+                assert torch.equal(a_, b_)
+        else:
+            x = wide_x[:, extra // 2:extra // 2 + feat]
+            z = wide_z[:, feat:2 * feat]
+            ref = orc.rmsnorm_gated_ref(x.double().cpu(), w.double().cpu(), z=z.double().cpu(),
+                                        group_size=group, norm_before_gate=norm_before_gate)
+            assert _fwd_ok(runs[0][0], ref, dtype)
