@@ -320,6 +320,7 @@ int ssm_ss2d_scan_bwd(const ssm_ss2d_scan_params* p, void* stream);
  * ------------------------------------------------------------------------- */
 #define SSM_CONV_SILU    0x400u /* conv1d: act = SiLU */
 #define SSM_IO_DTYPE     0x800u /* decode forward: x, B, C, z in io_dtype       */
+#define SSM_CHANNEL_LAST 0x1000u /* conv1d: x, out, dout, dx stored (batch, length, channels) */
 
 typedef struct ssm_causal_conv1d_params {
     int64_t batch, channels, length, width;
@@ -338,6 +339,13 @@ typedef struct ssm_causal_conv1d_params {
     void* dinitial;
     void* workspace;
     size_t workspace_bytes;
+    /* With SSM_CHANNEL_LAST: x, out, dout and dx are stored (batch, length,
+     * channels) -- element (b, c, t) at (b * length + t) * row_stride + c --
+     * with x_row_stride / dout_row_stride elements between rows of x / dout
+     * (0: channels) and out / dx dense.  Rows and the base pointers 8-byte
+     * aligned, channels a multiple of 8 bytes' worth of elements; no initial
+     * or final state. */
+    int64_t x_row_stride, dout_row_stride;
 } ssm_causal_conv1d_params;
 
 int ssm_causal_conv1d_sizes(const ssm_causal_conv1d_params* p, size_t* workspace_bytes);

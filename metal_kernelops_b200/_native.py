@@ -31,6 +31,7 @@ HAS_DSTATE = 0x100
 CUDA_CORES = 0x200
 CONV_SILU = 0x400
 IO_DTYPE = 0x800
+CHANNEL_LAST = 0x1000
 
 EXPORTS = (
     "ssm_status_string", "ssm_last_error",
@@ -112,6 +113,7 @@ class CausalConv1dParams(ctypes.Structure):
         ("out", _P), ("final_state", _P),
         ("dout", _P), ("dx", _P), ("dweight", _P), ("dbias", _P), ("dinitial", _P),
         ("workspace", _P), ("workspace_bytes", _SZ),
+        ("x_row_stride", _I64), ("dout_row_stride", _I64),
     ]
 
 

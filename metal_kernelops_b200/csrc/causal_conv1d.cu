@@ -36,6 +36,7 @@ struct Args {
     int64_t slots;                            // dweight / dbias partials per chunk
     int64_t per;                              // bulk: items per CTA
     uint32_t flags;
+    int64_t xs, ds;                           // channel-last: row strides of x and dout
     const void* x; const float* w; const float* bias; const void* init;
     void* out; void* final_state;
     const void* dout; void* dx; void* dinit;
@@ -751,6 +752,235 @@ __global__ void finalize_runs_kernel(const Args a, float* dweight, float* dbias)
     }
 }
 
+// ------------------------------------------------------- channel-last path --
+// x, out, dout and dx stored (batch, length, channels) -- the layout a
+// Mamba block's input projection produces, where the (batch, channels,
+// length) operand is a transposed view: element (b, c, t) at
+// (b length + t) rs + c, with rs the row stride (x and dout may be column
+// slices of wider rows; out and dx are written densely).  A thread owns V
+// consecutive channels (one 8-byte vector per row) and a run of kRun steps,
+// which it walks in order with the taps-wide window of earlier rows in a ring
+// of registers, so each row is read once (plus the taps rows before the run);
+// a warp's 32 vectors are 256 contiguous bytes of a row.  A CTA is 32 lanes
+// (32 V channels) x 8 warps (8 consecutive runs).  The ring slots are
+// compile-time indices: the step loop is unrolled by K, and row t sits in slot
+// (t - t_begin) mod K.
+constexpr int kRun = 64;
+constexpr int kClWarps = kThreads / 32;
+
+template <typename T>
+struct ClVec {
+    static constexpr int V = 8 / (int)sizeof(T);   // channels per thread
+    static constexpr int M = V / 2;                // channel pairs
+    static __device__ __forceinline__ void ld(const T* p, float2* v) {
+        const uint2 q = *reinterpret_cast<const uint2*>(p);
+        if constexpr (sizeof(T) == 4) {
+            v[0] = make_float2(__uint_as_float(q.x), __uint_as_float(q.y));
+        } else {
+            v[0] = Io2<T>::ld(reinterpret_cast<const T*>(&q.x));
+            v[1] = Io2<T>::ld(reinterpret_cast<const T*>(&q.y));
+        }
+    }
+    static __device__ __forceinline__ void st(T* p, const float2* v) {
+        uint2 q;
+        if constexpr (sizeof(T) == 4) {
+            q = make_uint2(__float_as_uint(v[0].x), __float_as_uint(v[0].y));
+        } else {
+            Io2<T>::st(reinterpret_cast<T*>(&q.x), v[0]);
+            Io2<T>::st(reinterpret_cast<T*>(&q.y), v[1]);
+        }
+        *reinterpret_cast<uint2*>(p) = q;
+    }
+};
+
+// Halved weights and bias of the thread's channel pairs.
+template <typename T, int K>
+__device__ __forceinline__ void cl_weights(const Args& a, int64_t c0, float2 (&wh)[K][ClVec<T>::M],
+                                           float2 (&bh)[ClVec<T>::M]) {
+#pragma unroll
+    for (int m = 0; m < ClVec<T>::M; ++m) {
+        const int64_t c = c0 + 2 * m;
+#pragma unroll
+        for (int j = 0; j < K; ++j) wh[j][m] = make_float2(0.5f * a.w[c * K + j], 0.5f * a.w[(c + 1) * K + j]);
+        bh[m] = (a.flags & kHasBias) ? make_float2(0.5f * a.bias[c], 0.5f * a.bias[c + 1]) : f2(0.0f);
+    }
+}
+
+template <typename T, int K>
+__global__ void __launch_bounds__(kThreads)
+fwd_cl_kernel(const Args a) {
+    constexpr int M = ClVec<T>::M, V = ClVec<T>::V, TAPS = K - 1;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t c0 = ((int64_t)blockIdx.x * 32 + lane) * V;
+    const int64_t b = blockIdx.z, L = a.length;
+    const int64_t t_begin = ((int64_t)blockIdx.y * kClWarps + warp) * kRun;
+    if (c0 >= a.channels || t_begin >= L) return;
+    const int64_t t_end = min64(t_begin + kRun, L);
+    const T* x = static_cast<const T*>(a.x) + b * L * a.xs + c0;
+    T* out = static_cast<T*>(a.out) + b * L * a.channels + c0;
+    float2 wh[K][M], bh[M];
+    cl_weights<T, K>(a, c0, wh, bh);
+    const bool silu = a.flags & kSilu;
+    float2 ring[K][M];
+#pragma unroll
+    for (int i = 1; i < K; ++i) {          // rows t_begin - K + i in slot i
+        const int64_t t = t_begin - K + i;
+        if (t >= 0) ClVec<T>::ld(x + t * a.xs, ring[i]);
+        else {
+#pragma unroll
+            for (int m = 0; m < M; ++m) ring[i][m] = f2(0.0f);
+        }
+    }
+    for (int64_t t0 = t_begin; t0 < t_end; t0 += K) {
+#pragma unroll
+        for (int u = 0; u < K; ++u) {       // row t0 + u in slot u
+            const int64_t t = t0 + u;
+            if (t >= t_end) break;
+            ClVec<T>::ld(x + t * a.xs, ring[u]);
+            float2 o[M];
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                float2 hp = bh[m];
+#pragma unroll
+                for (int j = 0; j < K; ++j) hp = fma2(wh[j][m], ring[(u + 1 + j) % K][m], hp);   // row t - TAPS + j
+                o[m] = silu ? silu2_half<T>(hp) : add2(hp, hp);
+            }
+            ClVec<T>::st(out + t * a.channels, o);
+        }
+    }
+    (void)TAPS;
+}
+
+// Backward: for u = t_begin .. t_end + taps - 1 the thread forms the doubled
+// gradient g(u) = 2 dout(u) silu'(pre(u)) (0 past the row) from the x ring
+// (rows u - taps .. u) and keeps it in a ring of its own; dx(u - taps) =
+// sum_j (w_j / 2) g(u - j) once u - taps >= t_begin, and the dweight / dbias
+// products of the run's own steps.  The CTA's warps add their sums in a fixed
+// order into one partial per (batch, CTA row block, channel).
+template <typename T, int K>
+__global__ void __launch_bounds__(kThreads)
+bwd_cl_kernel(const Args a) {
+    constexpr int M = ClVec<T>::M, V = ClVec<T>::V, TAPS = K - 1;
+    __shared__ float red[kClWarps][32 * V][K + 1];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t c0 = ((int64_t)blockIdx.x * 32 + lane) * V;
+    const int64_t b = blockIdx.z, L = a.length;
+    const int64_t t_begin = ((int64_t)blockIdx.y * kClWarps + warp) * kRun;
+    const bool live = c0 < a.channels && t_begin < L;
+    float2 acc[K + 1][M];
+#pragma unroll
+    for (int j = 0; j <= K; ++j)
+#pragma unroll
+        for (int m = 0; m < M; ++m) acc[j][m] = f2(0.0f);
+    if (live) {
+        const int64_t t_end = min64(t_begin + kRun, L);
+        const T* x = static_cast<const T*>(a.x) + b * L * a.xs + c0;
+        const T* dout = static_cast<const T*>(a.dout) + b * L * a.ds + c0;
+        T* dx = static_cast<T*>(a.dx) + b * L * a.channels + c0;
+        float2 wh[K][M], bh[M];
+        cl_weights<T, K>(a, c0, wh, bh);
+        const bool silu = a.flags & kSilu;
+        float2 xr[K][M], gr[K][M];
+#pragma unroll
+        for (int i = 1; i < K; ++i) {
+            const int64_t t = t_begin - K + i;
+            if (t >= 0) ClVec<T>::ld(x + t * a.xs, xr[i]);
+            else {
+#pragma unroll
+                for (int m = 0; m < M; ++m) xr[i][m] = f2(0.0f);
+            }
+#pragma unroll
+            for (int m = 0; m < M; ++m) gr[i][m] = f2(0.0f);   // g before the run: unused
+        }
+        const int64_t u_end = t_end + TAPS;
+        for (int64_t u0 = t_begin; u0 < u_end; u0 += K) {
+#pragma unroll
+            for (int k = 0; k < K; ++k) {   // step u = u0 + k in slot k
+                const int64_t u = u0 + k;
+                if (u >= u_end) break;
+                float2 g[M];
+                if (u < L) {
+                    ClVec<T>::ld(x + u * a.xs, xr[k]);
+                    ClVec<T>::ld(dout + u * a.ds, g);
+#pragma unroll
+                    for (int m = 0; m < M; ++m) {
+                        if (silu) {
+                            float2 hp = bh[m];
+#pragma unroll
+                            for (int j = 0; j < K; ++j) hp = fma2(wh[j][m], xr[(k + 1 + j) % K][m], hp);
+                            g[m] = silu_grad2_half<T>(hp, g[m]);
+                        } else {
+                            g[m] = add2(g[m], g[m]);
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int m = 0; m < M; ++m) { g[m] = f2(0.0f); xr[k][m] = f2(0.0f); }
+                }
+#pragma unroll
+                for (int m = 0; m < M; ++m) gr[k][m] = g[m];
+                if (u < t_end) {
+#pragma unroll
+                    for (int m = 0; m < M; ++m) {
+                        acc[K][m] = add2(acc[K][m], g[m]);
+#pragma unroll
+                        for (int j = 0; j < K; ++j) acc[j][m] = fma2(g[m], xr[(k + 1 + j) % K][m], acc[j][m]);
+                    }
+                }
+                if (u - TAPS >= t_begin) {
+                    float2 o[M];
+#pragma unroll
+                    for (int m = 0; m < M; ++m) {
+                        float2 s = mul2(wh[0][m], gr[k][m]);            // j = 0: g(u)
+#pragma unroll
+                        for (int j = 1; j < K; ++j) s = fma2(wh[j][m], gr[(k + K - j) % K][m], s);
+                        o[m] = s;
+                    }
+                    ClVec<T>::st(dx + (u - TAPS) * a.channels, o);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j <= K; ++j)
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            red[warp][lane * V + 2 * m][j] = 0.5f * acc[j][m].x;
+            red[warp][lane * V + 2 * m + 1][j] = 0.5f * acc[j][m].y;
+        }
+    __syncthreads();
+    const int64_t nrb = (L + kClWarps * kRun - 1) / (kClWarps * kRun);
+    float* part = a.partial + ((b * nrb + blockIdx.y) * a.channels + (int64_t)blockIdx.x * 32 * V) * (K + 1);
+    for (int i = threadIdx.x; i < 32 * V * (K + 1); i += kThreads) {
+        const int cl = i / (K + 1), j = i - cl * (K + 1);
+        if ((int64_t)blockIdx.x * 32 * V + cl >= a.channels) continue;
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kClWarps; ++w) s += red[w][cl][j];
+        part[i] = s;
+    }
+}
+
+// dweight / dbias of the channel-last backward: the partials of every
+// (batch, row block) of channel c, in order.
+template <int K>
+__global__ void finalize_cl_kernel(const Args a, float* dweight, float* dbias) {
+    const int64_t total = a.channels * (K + 1);
+    const int64_t nrb = (a.length + kClWarps * kRun - 1) / (kClWarps * kRun);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        float s = 0.0f;
+        for (int64_t k = 0; k < a.batch * nrb; ++k) s += a.partial[k * total + i];
+        const int64_t c = i / (K + 1);
+        const int j = (int)(i - c * (K + 1));
+        if (j < K) {
+            if (dweight) dweight[c * K + j] = s;
+        } else if (dbias) {
+            dbias[c] = s;
+        }
+    }
+}
+
 // ------------------------------------------------------------------- decode --
 // One thread per (batch, channel): q new tokens against a rolling state of
 // `span` >= taps columns addressed through its strides (a cache slice), then
@@ -819,6 +1049,8 @@ static void plan(const ssm_causal_conv1d_params* p, bool bulk, Args& a) {
     a.chunk = bulk ? kTile : kSeg;
     a.nchunks = max64(1, ceil_div(p->length, a.chunk));
     a.slots = bulk ? kWarps : 1;
+    a.xs = p->x_row_stride ? p->x_row_stride : p->channels;
+    a.ds = p->dout_row_stride ? p->dout_row_stride : p->channels;
     a.flags = p->flags;
     a.x = p->x; a.w = p->weight; a.bias = p->bias; a.init = p->initial_state;
     a.out = p->out; a.final_state = p->final_state;
@@ -918,6 +1150,33 @@ template <typename T, int K> struct BwdRun {
         return launch_bwd<T, K>(*a, bulk, dw, db, st);
     }
 };
+template <typename T, int K>
+static int launch_fwd_cl(const Args& a, cudaStream_t st) {
+    constexpr int V = ClVec<T>::V;
+    const dim3 grid((unsigned)ceil_div(a.channels, 32 * V), (unsigned)ceil_div(a.length, (int64_t)kClWarps * kRun),
+                    (unsigned)a.batch);
+    fwd_cl_kernel<T, K><<<grid, kThreads, 0, st>>>(a);
+    return check_launch("causal_conv1d fwd (channel-last)");
+}
+
+template <typename T, int K>
+static int launch_bwd_cl(const Args& a, float* dweight, float* dbias, cudaStream_t st) {
+    constexpr int V = ClVec<T>::V;
+    const dim3 grid((unsigned)ceil_div(a.channels, 32 * V), (unsigned)ceil_div(a.length, (int64_t)kClWarps * kRun),
+                    (unsigned)a.batch);
+    bwd_cl_kernel<T, K><<<grid, kThreads, 0, st>>>(a);
+    if (int s = check_launch("causal_conv1d bwd (channel-last)")) return s;
+    const int64_t total = a.channels * (K + 1);
+    finalize_cl_kernel<K><<<(unsigned)min64(ceil_div(total, 256), 148 * 8), 256, 0, st>>>(a, dweight, dbias);
+    return check_launch("causal_conv1d bwd (channel-last) finalize");
+}
+
+template <typename T, int K> struct ClFwdRun {
+    static int run(const Args* a, cudaStream_t st) { return launch_fwd_cl<T, K>(*a, st); }
+};
+template <typename T, int K> struct ClBwdRun {
+    static int run(const Args* a, float* dw, float* db, cudaStream_t st) { return launch_bwd_cl<T, K>(*a, dw, db, st); }
+};
 template <typename T, int K> struct UpdRun {
     static int run(const ssm_causal_conv1d_update_params* p, cudaStream_t st) { return launch_update<T, K>(p, st); }
 };
@@ -928,8 +1187,33 @@ template <typename T, int K> struct UpdRun {
 using namespace ssm;
 using namespace ssm::conv;
 
+// The channel-last layout's requirements (SSM_CHANNEL_LAST).
+static int cl_check(const ssm_causal_conv1d_params* p, bool bwd) {
+    const int64_t esz = p->dtype == SSM_F32 ? 4 : 2, v = 8 / esz;
+    const int64_t xs = p->x_row_stride ? p->x_row_stride : p->channels;
+    const int64_t ds = p->dout_row_stride ? p->dout_row_stride : p->channels;
+    if ((p->flags & SSM_HAS_INIT) || p->final_state || (bwd && p->dinitial))
+        return fail(SSM_ERR_UNSUPPORTED, "causal_conv1d channel-last: no initial or final state");
+    if (p->channels % v || xs < p->channels || (bwd && ds < p->channels) || (xs * esz) % 8 || (ds * esz) % 8)
+        return fail(SSM_ERR_UNSUPPORTED, "causal_conv1d channel-last: channels and row strides need 8-byte rows");
+    auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 7) == 0; };
+    if (!al(p->x) || (!bwd && !al(p->out)) || (bwd && (!al(p->dout) || !al(p->dx))))
+        return fail(SSM_ERR_UNSUPPORTED, "causal_conv1d channel-last: pointers must be 8-byte aligned");
+    if (ceil_div(max64(p->length, 1), (int64_t)kClWarps * kRun) > 65535 || p->batch > 65535)
+        return fail(SSM_ERR_UNSUPPORTED, "causal_conv1d channel-last: length or batch too large");
+    return SSM_OK;
+}
+static size_t cl_workspace(const ssm_causal_conv1d_params* p) {
+    return (size_t)(p->batch * ceil_div(max64(p->length, 1), (int64_t)kClWarps * kRun) * p->channels *
+                    (p->width + 1)) * 4;
+}
+
 extern "C" int ssm_causal_conv1d_sizes(const ssm_causal_conv1d_params* p, size_t* workspace_bytes) {
     if (int s = validate(p)) return s;
+    if (p->flags & SSM_CHANNEL_LAST) {
+        if (workspace_bytes) *workspace_bytes = cl_workspace(p);
+        return SSM_OK;
+    }
     Args a, b;
     plan(p, false, a);
     plan(p, true, b);
@@ -955,6 +1239,13 @@ extern "C" int ssm_causal_conv1d_fwd(const ssm_causal_conv1d_params* p, void* st
         ((p->flags & SSM_HAS_INIT) && !p->initial_state))
         return fail(SSM_ERR_INVALID, "causal_conv1d fwd: null pointer");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (p->flags & SSM_CHANNEL_LAST) {
+        if (int s = cl_check(p, false)) return s;
+        if (p->length == 0) return SSM_OK;
+        Args a;
+        plan(p, false, a);
+        return by_type_width<ClFwdRun>(p->dtype, (int)p->width, (const Args*)&a, st);
+    }
     const bool bulk = bulk_ok(p, false);
     Args a;
     plan(p, bulk, a);
@@ -992,6 +1283,14 @@ extern "C" int ssm_causal_conv1d_bwd(const ssm_causal_conv1d_params* p, void* st
     if (!p->x || !p->weight || !p->dout || !p->dx || ((p->flags & SSM_HAS_BIAS) && !p->bias) ||
         ((p->flags & SSM_HAS_INIT) && !p->initial_state))
         return fail(SSM_ERR_INVALID, "causal_conv1d bwd: null pointer");
+    if (p->flags & SSM_CHANNEL_LAST) {
+        if (int s = cl_check(p, true)) return s;
+        if (p->workspace == nullptr || p->workspace_bytes < cl_workspace(p))
+            return fail(SSM_ERR_WORKSPACE, "causal_conv1d bwd: workspace smaller than ssm_causal_conv1d_sizes");
+        a.partial = static_cast<float*>(p->workspace);
+        return by_type_width<ClBwdRun>(p->dtype, (int)K, (const Args*)&a, p->dweight,
+                                       (p->flags & SSM_HAS_BIAS) ? p->dbias : nullptr, st);
+    }
     const size_t need = (size_t)(a.rows * a.nchunks * a.slots * (K + 1)) * 4;
     if (p->workspace == nullptr || p->workspace_bytes < need)
         return fail(SSM_ERR_WORKSPACE, "causal_conv1d bwd: workspace smaller than ssm_causal_conv1d_sizes");

@@ -152,6 +152,95 @@ def _backward(ctx, dout, dfinal):
 _fwd.register_autograd(_backward, setup_context=_setup)
 
 
+# --------------------------------------------------------- channel-last path --
+# x given as a (batch, channels, length) view of (batch, length, channels)
+# memory -- the transpose of a Mamba block's input-projection output, possibly
+# a column slice of it -- runs on kernels that read that layout directly, so
+# the operand is never copied; the output comes back as the same kind of view.
+
+def _cl_rows(t):
+    """(batch, length, channels) tensor t usable by the channel-last kernels:
+    unit channel stride, evenly spaced rows, 8-byte aligned."""
+    b, length, c = t.shape
+    es = t.element_size()
+    if t.stride(2) != 1 or (c * es) % 8 or t.data_ptr() % 8:
+        return False
+    rs = t.stride(1) if length > 1 else c
+    if rs < c or (rs * es) % 8:
+        return False
+    return b <= 1 or t.stride(0) == length * rs
+
+
+def _params_cl(xt, weight, bias, silu):
+    p = nat.CausalConv1dParams()
+    p.batch, p.length, p.channels = xt.shape
+    p.width = weight.shape[1]
+    p.dtype = nat.dtype_code(xt.dtype)
+    p.flags = nat.CHANNEL_LAST | (nat.HAS_BIAS if bias is not None else 0) | (nat.CONV_SILU if silu else 0)
+    p.x, p.weight = xt.data_ptr(), weight.data_ptr()
+    p.bias = bias.data_ptr() if bias is not None else None
+    p.x_row_stride = xt.stride(1) if xt.shape[1] > 1 else 0
+    return p
+
+
+@torch.library.custom_op("b200ssm::causal_conv1d_cl_fwd", mutates_args=(), device_types="cuda")
+def _fwd_cl(xt: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], silu: bool) -> torch.Tensor:
+    """xt: (batch, length, channels) with unit channel stride; the result is dense."""
+    p = _params_cl(xt, weight, bias, silu)
+    out = xt.new_empty(xt.shape)
+    p.out = out.data_ptr()
+    nat.check(nat.lib().ssm_causal_conv1d_fwd(p, nat.stream_of(xt)), "causal_conv1d")
+    return out
+
+
+@_fwd_cl.register_fake
+def _(xt, weight, bias, silu):
+    return xt.new_empty(xt.shape)
+
+
+@torch.library.custom_op("b200ssm::causal_conv1d_cl_bwd", mutates_args=(), device_types="cuda")
+def _bwd_cl(dout: torch.Tensor, xt: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor],
+            silu: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    p = _params_cl(xt, weight, bias, silu)
+    p.dout_row_stride = dout.stride(1) if dout.shape[1] > 1 else 0
+    ws_bytes = nat._SZ()
+    nat.check(nat.lib().ssm_causal_conv1d_sizes(p, ws_bytes), "causal_conv1d backward")
+    dx = xt.new_empty(xt.shape)
+    dweight = torch.empty(weight.shape, dtype=torch.float32, device=xt.device)
+    dbias = torch.empty(weight.shape[0] if bias is not None else 0, dtype=torch.float32, device=xt.device)
+    ws = torch.empty(max(ws_bytes.value, 1), dtype=torch.uint8, device=xt.device)
+    p.dout, p.dx = dout.data_ptr(), dx.data_ptr()
+    p.dweight = dweight.data_ptr()
+    p.dbias = dbias.data_ptr() if bias is not None else None
+    p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+    nat.check(nat.lib().ssm_causal_conv1d_bwd(p, nat.stream_of(xt)), "causal_conv1d backward")
+    return dx, dweight, dbias
+
+
+@_bwd_cl.register_fake
+def _(dout, xt, weight, bias, silu):
+    f32 = dict(dtype=torch.float32)
+    return (xt.new_empty(xt.shape), weight.new_empty(weight.shape, **f32),
+            weight.new_empty(weight.shape[0] if bias is not None else 0, **f32))
+
+
+def _setup_cl(ctx, inputs, output):
+    xt, weight, bias, silu = inputs
+    ctx.save_for_backward(xt, weight, bias)
+    ctx.silu = silu
+
+
+def _backward_cl(ctx, dout):
+    xt, weight, bias = ctx.saved_tensors
+    if not _cl_rows(dout):
+        dout = dout.contiguous()
+    dx, dweight, dbias = _bwd_cl(dout, xt, weight, bias, ctx.silu)
+    return dx, dweight, dbias if bias is not None else None, None
+
+
+_fwd_cl.register_autograd(_backward_cl, setup_context=_setup_cl)
+
+
 def _final_state(x, init, taps):
     """The last ``taps`` columns of ``cat(init, x)`` (reference :468-477), through
     torch ops so that gradients reach x and init."""
@@ -189,6 +278,14 @@ def causal_conv1d_fn(x, weight, bias=None, activation=None, initial_state=None, 
     if width > MAX_WIDTH:
         raise ValueError(f"causal_conv1d: kernel width must be at most {MAX_WIDTH}, got {width}")
     taps = width - 1
+    silu = activation is not None
+    if initial_state is None and x.numel() and x.shape[2] > 1 and _cl_rows(x.transpose(1, 2)):
+        w32 = weight.float().contiguous()
+        b32 = bias.float().contiguous() if bias is not None else None
+        out = torch.ops.b200ssm.causal_conv1d_cl_fwd(x.transpose(1, 2), w32, b32, silu).transpose(1, 2)
+        if return_final_state:
+            return out, _final_state(x, None, taps)
+        return out
     work = x.contiguous()
     # a width-1 kernel has no state: (batch, channels, 0) carries nothing
     init = initial_state.to(x.dtype).contiguous() if initial_state is not None and taps else None
@@ -201,7 +298,6 @@ def causal_conv1d_fn(x, weight, bias=None, activation=None, initial_state=None, 
         if return_final_state:
             return out, _final_state(work, init, taps)
         return out
-    silu = activation is not None
     if return_final_state and not grads:
         out, final = torch.ops.b200ssm.causal_conv1d_fwd(work, w32, b32, init, silu, True)
         return out, final

@@ -261,3 +261,53 @@ def test_deterministic():
         runs.append((out.detach(),) + torch.autograd.grad(out.float().square().sum(), leaves))
     for vals in zip(*runs):
         assert all(torch.equal(vals[0], v) for v in vals[1:])
+
+
+CL_CASES = [  # name, batch, channels, length, K, activation, dtype, extra columns of the wider rows
+    ("cl-bf16-2x256x1000-k4", 2, 256, 1000, 4, "silu", torch.bfloat16, 40),
+    ("cl-f32-3x40x777-k3", 3, 40, 777, 3, "silu", torch.float32, 4),
+    ("cl-unaligned-f32-2x40x300-k4", 2, 40, 300, 4, "silu", torch.float32, 6),  # 12-byte offset: copied
+    ("cl-f16-1x128x70-k8", 1, 128, 70, 8, None, torch.float16, 8),
+    ("cl-f32-2x64x33-k1", 2, 64, 33, 1, None, torch.float32, 0),
+    ("cl-bf16-4x136x3-k4", 4, 136, 3, 4, "silu", torch.bfloat16, 16),       # shorter than the taps
+    ("cl-bf16-2x512x1100-k2", 2, 512, 1100, 2, "silu", torch.bfloat16, 64),   # runs across row blocks
+]
+
+
+@pytest.mark.parametrize("case", CL_CASES, ids=[c[0] for c in CL_CASES])
+def test_channel_last(case):
+    """x as the transpose of a column slice of wider (batch, length, columns)
+    rows -- a Mamba block's in-projection output -- is read in place by the
+    channel-last kernels: out equals the contiguous call bit for bit (same tap
+    order and activation), dx too where that call takes the bulk path (the
+    unaligned-row path's 16-bit SiLU' rounds differently), and every value and
+    gradient matches the fp64 oracle."""
+    name, b, c, l, k, act, dtype, extra = case
+    cc = _cc()
+    w = _make((c, 1, k), dtype, 11, 0.5)
+    bias = _make((c,), dtype, 12)
+    wide = _make((b, l, c + extra), dtype, 13)
+    g = torch.Generator().manual_seed(14)
+    dout = torch.randn((b, c, l), generator=g, dtype=torch.float64)
+    runs = []
+    for contiguous in (False, True):
+        x = wide[:, :, extra // 2:extra // 2 + c].transpose(1, 2).detach()
+        if contiguous:
+            x = x.contiguous()
+        x.requires_grad_(True)
+        wl, bl = w.clone().requires_grad_(True), bias.clone().requires_grad_(True)
+        out = cc.causal_conv1d_fn(x, wl, bl, act)
+        if not contiguous:                          # channel-last result unless the slice is misaligned
+            assert (out.stride(1) == 1) == ((extra // 2 * wide.element_size()) % 8 == 0)
+        grads = torch.autograd.grad((out.double() * dout.cuda()).sum(), [x, wl, bl])
+        runs.append((out.detach(), *grads))
+    assert torch.equal(runs[0][0], runs[1][0])
+    if (l * wide.element_size()) % 16 == 0:
+        assert torch.equal(runs[0][1], runs[1][1])
+    x64 = wide[:, :, extra // 2:extra // 2 + c].transpose(1, 2).double().cpu().requires_grad_(True)
+    w64, b64 = w.double().cpu().requires_grad_(True), bias.double().cpu().requires_grad_(True)
+    rout = orc.causal_conv1d_ref(x64, w64, b64, act)
+    rgrads = torch.autograd.grad((rout * dout).sum(), [x64, w64, b64])
+    assert _rel(runs[0][0], rout) <= VALUE[dtype]
+    for name_, a, r in zip(("x", "weight", "bias"), runs[0][1:], rgrads):
+        assert _rel(a, r) <= GRAD[dtype], (name_, _rel(a, r))
