@@ -246,6 +246,13 @@ typedef struct ssm_chunk_scan_params {
     float* saved;
     void* workspace;
     size_t workspace_bytes;
+    /* Elements between consecutive tokens of x and of B / C (0: the dense
+     * nheads * headdim and ngroups * dstate); heads (groups) and their
+     * headdim (dstate) elements stay packed within a token, and the batch
+     * stride is length tokens.  x and B / C may so be column slices of one
+     * wider (batch, length, columns) buffer.  Tensor-core path only (16-byte
+     * multiples); the CUDA-core path returns SSM_ERR_UNSUPPORTED for them. */
+    int64_t x_token_stride, bc_token_stride;
 } ssm_chunk_scan_params;
 
 int ssm_chunk_scan_sizes(const ssm_chunk_scan_params* p, size_t* saved_bytes,

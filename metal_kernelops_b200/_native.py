@@ -90,6 +90,7 @@ class ChunkScanParams(ctypes.Structure):
         ("dx", _P), ("ddt", _P), ("dA", _P), ("dB", _P), ("dC", _P), ("dD", _P), ("dz", _P),
         ("ddt_bias", _P), ("dinitial", _P),
         ("saved", _P), ("workspace", _P), ("workspace_bytes", _SZ),
+        ("x_token_stride", _I64), ("bc_token_stride", _I64),
     ]
 
 

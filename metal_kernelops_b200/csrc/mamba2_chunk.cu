@@ -618,6 +618,15 @@ static int validate(const ssm_chunk_scan_params* p, int mode) {
         return fail(SSM_ERR_INVALID, "chunk_scan: null saved-state buffer");
     if (mode == 2 && !empty && (!p->dy || !p->dx || !p->ddt || !p->dA || !p->dB || !p->dC))
         return fail(SSM_ERR_INVALID, "chunk_scan bwd: null gradient pointer");
+    const int64_t xd = p->nheads * p->headdim, bcd = p->ngroups * p->dstate;
+    if ((p->x_token_stride && p->x_token_stride != xd) || (p->bc_token_stride && p->bc_token_stride != bcd)) {
+        if (!ssdtc::eligible(p))
+            return fail(SSM_ERR_UNSUPPORTED, "chunk_scan: token strides need the tensor-core path");
+        const int64_t xs = p->x_token_stride ? p->x_token_stride : xd;
+        const int64_t bs = p->bc_token_stride ? p->bc_token_stride : bcd;
+        if (xs < xd || bs < bcd || xs % 8 || bs % 8)
+            return fail(SSM_ERR_UNSUPPORTED, "chunk_scan: token strides must cover a token, in 16-byte steps");
+    }
     return SSM_OK;
 }
 

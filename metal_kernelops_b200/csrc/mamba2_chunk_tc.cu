@@ -68,6 +68,7 @@ __device__ int g_kernel_error;
 
 struct Args {
     int64_t batch, length, nheads, ngroups, nc, hpg;
+    int64_t xts;           // elements between tokens of x
     uint32_t flags;
     int dt_dtype;
     const void* x; const void* dt; const float* A; const void* B; const void* C;
@@ -1041,7 +1042,8 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
             const float Ah = sh.hs.A[hk];
             const float Dh = sh.hs.D[hk];
             const float Tc = sh.T[hh & 1];
-            const int64_t grow = ((b * L + t0 + r) * H + h) * P;   // row r of x / dy / dx
+            const int64_t grow = ((b * L + t0 + r) * H + h) * P;   // row r of dy / dx / z
+            const int64_t xrow = (b * L + t0 + r) * a.xts + h * P;  // row r of x
             {
                 const bool lw = tc::mbar_wait(bar(kLh), par);   // this head's tiles
                 if (!lw) report(45);
@@ -1163,7 +1165,7 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
                 const bool live = r < valid;
 #pragma unroll
                 for (int j = 0; j < WX / 2; ++j)
-                    xr[j] = live ? *reinterpret_cast<const uint4*>(xg + grow + 8 * (j0 + j)) : make_uint4(0, 0, 0, 0);
+                    xr[j] = live ? *reinterpret_cast<const uint4*>(xg + xrow + 8 * (j0 + j)) : make_uint4(0, 0, 0, 0);
             }
             const float dci = pos_thread ? a.dcs_inter[bhc * Q + tid] : 0.0f;
             const float dTc = tid == Q - 1 ? a.dT[bhc] : 0.0f;
@@ -1354,6 +1356,7 @@ static void make_args(const ssm_chunk_scan_params* p, Args& a) {
     a.batch = p->batch; a.length = p->length; a.nheads = p->nheads; a.ngroups = p->ngroups;
     a.nc = n_chunks(p); a.hpg = p->nheads / p->ngroups;
     a.flags = p->flags; a.dt_dtype = p->dt_dtype;
+    a.xts = p->x_token_stride ? p->x_token_stride : p->nheads * P;
     a.x = p->x; a.dt = p->dt; a.A = p->A; a.B = p->B; a.C = p->C; a.D = p->D; a.z = p->z;
     a.dt_bias = p->dt_bias; a.init = p->initial_states;
     a.y = p->y; a.final_state = p->final_state;
@@ -1388,13 +1391,13 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // head): a box of (8, 8, width / 8, 1, 1) is one 8-row group of core matrices
 // of a tile (tile_off layout), and rows past `length` read as zeros.
 static int encode_rows(CUtensorMap* m, const void* base, int dtype, int64_t batch, int64_t length, int64_t heads,
-                       int64_t width) {
+                       int64_t width, int64_t token_stride = 0) {
     auto enc = tensor_map_encoder();
     if (!enc) return fail(SSM_ERR_CUDA, "chunk_scan (tensor cores): cuTensorMapEncodeTiled unavailable");
     const cuuint64_t es = 2;
     cuuint64_t dim[5] = {8, (cuuint64_t)length, (cuuint64_t)(width / 8), (cuuint64_t)batch, (cuuint64_t)heads};
-    cuuint64_t str[4] = {(cuuint64_t)(heads * width) * es, 16, (cuuint64_t)(length * heads * width) * es,
-                         (cuuint64_t)width * es};
+    const int64_t ts = token_stride ? token_stride : heads * width;   // elements between tokens
+    cuuint64_t str[4] = {(cuuint64_t)ts * es, 16, (cuuint64_t)(length * ts) * es, (cuuint64_t)width * es};
     cuuint32_t box[5] = {8, 8, (cuuint32_t)(width / 8), 1, 1};
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     const CUresult r = enc(m, dtype == SSM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
@@ -1448,9 +1451,9 @@ int fwd(const ssm_chunk_scan_params* p, cudaStream_t s) {
         return fail(SSM_ERR_INVALID, "chunk_scan fwd (tensor cores): x, B, C, z, y and saved must be 16-byte aligned");
     Args a;
     make_args(p, a);
-    if (int e = encode_rows(&a.tm_x, p->x, p->dtype, p->batch, p->length, p->nheads, P)) return e;
-    if (int e = encode_rows(&a.tm_B, p->B, p->dtype, p->batch, p->length, p->ngroups, N)) return e;
-    if (int e = encode_rows(&a.tm_C, p->C, p->dtype, p->batch, p->length, p->ngroups, N)) return e;
+    if (int e = encode_rows(&a.tm_x, p->x, p->dtype, p->batch, p->length, p->nheads, P, p->x_token_stride)) return e;
+    if (int e = encode_rows(&a.tm_B, p->B, p->dtype, p->batch, p->length, p->ngroups, N, p->bc_token_stride)) return e;
+    if (int e = encode_rows(&a.tm_C, p->C, p->dtype, p->batch, p->length, p->ngroups, N, p->bc_token_stride)) return e;
     return p->dtype == SSM_BF16 ? run_fwd<__nv_bfloat16>(a, s) : run_fwd<__half>(a, s);
 }
 
@@ -1472,10 +1475,10 @@ int bwd(const ssm_chunk_scan_params* p, cudaStream_t s) {
     a.dA_part = reinterpret_cast<float*>(ws + w.dh + w.dci + w.dt);
     a.db_part = reinterpret_cast<float*>(ws + w.dh + w.dci + w.dt + w.part);
     a.dD_part = reinterpret_cast<float*>(ws + w.dh + w.dci + w.dt + 2 * w.part);
-    if (int e = encode_rows(&a.tm_x, p->x, p->dtype, p->batch, p->length, p->nheads, P)) return e;
+    if (int e = encode_rows(&a.tm_x, p->x, p->dtype, p->batch, p->length, p->nheads, P, p->x_token_stride)) return e;
     if (int e = encode_rows(&a.tm_dy, p->dy, p->dtype, p->batch, p->length, p->nheads, P)) return e;
-    if (int e = encode_rows(&a.tm_B, p->B, p->dtype, p->batch, p->length, p->ngroups, N)) return e;
-    if (int e = encode_rows(&a.tm_C, p->C, p->dtype, p->batch, p->length, p->ngroups, N)) return e;
+    if (int e = encode_rows(&a.tm_B, p->B, p->dtype, p->batch, p->length, p->ngroups, N, p->bc_token_stride)) return e;
+    if (int e = encode_rows(&a.tm_C, p->C, p->dtype, p->batch, p->length, p->ngroups, N, p->bc_token_stride)) return e;
     return p->dtype == SSM_BF16 ? run_bwd<__nv_bfloat16>(a, p, s) : run_bwd<__half>(a, p, s);
 }
 

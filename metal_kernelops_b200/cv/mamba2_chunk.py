@@ -71,6 +71,9 @@ def _params(x, dt, A, B, C, D, z, dt_bias, init, chunk_size, softplus):
     if not _tensor_cores or (x.device.type != "meta" and any(
             t is not None and t.data_ptr() % 16 for t in (x, B, C, z))):
         p.flags |= nat.CUDA_CORES
+    # token strides (0 for one token: never used)
+    p.x_token_stride = x.stride(1) if x.shape[1] > 1 else 0
+    p.bc_token_stride = B.stride(1) if B.shape[1] > 1 else 0
     if x.device.type == "meta":
         return p
     p.x, p.dt, p.A, p.B, p.C = (t.data_ptr() for t in (x, dt, A, B, C))
@@ -95,7 +98,7 @@ def _fwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Tensor, C:
     p = _params(x, dt, A, B, C, D, z, dt_bias, init, chunk_size, softplus)
     saved_bytes, ws_bytes = _sizes(p)
     batch, length, nheads, headdim = x.shape
-    y = torch.empty_like(x)
+    y = x.new_empty(x.shape)
     final = torch.empty(batch, nheads, headdim, B.shape[3], dtype=torch.float32, device=x.device)
     saved = torch.empty(saved_bytes // 4, dtype=torch.float32, device=x.device)
     p.y, p.final_state, p.saved = y.data_ptr(), final.data_ptr(), saved.data_ptr()
@@ -107,7 +110,7 @@ def _fwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Tensor, C:
 def _(x, dt, A, B, C, D, z, dt_bias, init, chunk_size, softplus, save):
     batch, length, nheads, headdim = x.shape
     saved_bytes, _ = _sizes(_params(x, dt, A, B, C, D, z, dt_bias, init, chunk_size, softplus))
-    return (torch.empty_like(x), x.new_empty(batch, nheads, headdim, B.shape[3], dtype=torch.float32),
+    return (x.new_empty(x.shape), x.new_empty(batch, nheads, headdim, B.shape[3], dtype=torch.float32),
             x.new_empty(saved_bytes // 4, dtype=torch.float32))
 
 
@@ -120,14 +123,14 @@ def _bwd(dy: torch.Tensor, dfinal: Optional[torch.Tensor], x: torch.Tensor, dt: 
     _, ws_bytes = _sizes(p)
     dev = x.device
     f32 = dict(dtype=torch.float32, device=dev)
-    dx = torch.empty_like(x)
+    dx = x.new_empty(x.shape)
     ddt = torch.empty(dt.shape, **f32)
     dA = torch.empty(A.shape, **f32)
     dB = torch.empty(B.shape, **f32)
     dC = torch.empty(C.shape, **f32)
     # absent gradients: distinct empty tensors (custom-op returns may not alias)
     dD = torch.empty(D.shape if D is not None else (0,), **f32)
-    dz = torch.empty_like(x) if z is not None else x.new_empty(0)
+    dz = x.new_empty(x.shape) if z is not None else x.new_empty(0)
     dbias = torch.empty(A.shape if dt_bias is not None else (0,), **f32)
     dinit = torch.empty(init.shape if init is not None else (0,), **f32)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
@@ -151,8 +154,8 @@ def _bwd(dy: torch.Tensor, dfinal: Optional[torch.Tensor], x: torch.Tensor, dt: 
 def _(dy, dfinal, x, dt, A, B, C, D, z, dt_bias, init, saved, chunk_size, softplus):
     f = lambda t: t.new_empty(t.shape, dtype=torch.float32)  # noqa: E731
     e = lambda: x.new_empty(0, dtype=torch.float32)  # noqa: E731
-    return [torch.empty_like(x), f(dt), f(A), f(B), f(C), f(D) if D is not None else e(),
-            torch.empty_like(x) if z is not None else x.new_empty(0),
+    return [x.new_empty(x.shape), f(dt), f(A), f(B), f(C), f(D) if D is not None else e(),
+            x.new_empty(x.shape) if z is not None else x.new_empty(0),
             f(A) if dt_bias is not None else e(), f(init) if init is not None else e()]
 
 
@@ -229,6 +232,19 @@ def _check(x, dt, A, B, C, D, z, dt_bias, initial_states, chunk_size):
     return initial_states
 
 
+def _token_rows(t):
+    """(batch, length, heads, width) t that the tensor-core kernels can read
+    through its token stride: heads and width packed, tokens evenly spaced in
+    16-byte steps, batches length tokens apart, 16-byte aligned."""
+    b, length, heads, width = t.shape
+    if t.stride(3) != 1 or t.stride(2) != width or t.data_ptr() % 16:
+        return False
+    ts = t.stride(1) if length > 1 else heads * width
+    if ts < heads * width or (ts * t.element_size()) % 16:
+        return False
+    return b <= 1 or t.stride(0) == length * ts
+
+
 def mamba2_chunk_scan(x, dt, A, B, C, chunk_size=64, D=None, z=None, dt_bias=None,
                       dt_softplus=False, initial_states=None):
     """Exact Mamba-2 chunked SSD scan (reference cv/mamba2_chunk.py:617-678).
@@ -239,9 +255,17 @@ def mamba2_chunk_scan(x, dt, A, B, C, chunk_size=64, D=None, z=None, dt_bias=Non
     global _path
     initial_states = _check(x, dt, A, B, C, D, z, dt_bias, initial_states, chunk_size)
     dtype = x.dtype
-    x = x.contiguous()
-    B = B.to(dtype).contiguous()
-    C = C.to(dtype).contiguous()
+    B = B.to(dtype)
+    C = C.to(dtype)
+    # the tensor-core path reads x and B / C through their token strides (column
+    # slices of a wider projection or convolution output need no copy; B and C
+    # share one stride); anything else is made dense
+    tc = (_tensor_cores and dtype in (torch.bfloat16, torch.float16) and x.shape[3] == 64
+          and B.shape[3] == 128)
+    if not (tc and _token_rows(x)):
+        x = x.contiguous()
+    if not (tc and _token_rows(B) and _token_rows(C) and B.stride() == C.stride()):
+        B, C = B.contiguous(), C.contiguous()
     z = z.to(dtype).contiguous() if z is not None else None
     dt = (dt if dt.dtype in _DTYPES else dt.float()).contiguous()
     A = A.float().contiguous()

@@ -166,3 +166,36 @@ def test_tc_and_cuda_cores_agree_at_config3():
         assert err <= tol, (name, err)
     from metal_kernelops_b200 import _native as nat
     assert nat.lib().ssm_take_kernel_error() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_tc_token_strided_inputs(dtype):
+    """x, B and C as column slices of one wider (batch, length, columns)
+    buffer -- the Mamba-2 layer's convolution output -- are read through their
+    token strides by the tensor maps and the x-row loads, not copied: y, the
+    final state and every gradient equal the call on dense copies bit for bit."""
+    mod = _mod()
+    b, length, h, g = 2, 300, 8, 2
+    inner, gn, pad = h * P, g * N, 24
+    gen = torch.Generator().manual_seed(77)
+    wide = (torch.randn(b, length, inner + 2 * gn + pad, generator=gen)).to("cuda", dtype)
+    dt = (torch.randn(b, length, h, generator=gen) - 1.0).to("cuda", dtype)
+    A = -(torch.rand(h, generator=gen) * 4 + 0.5).cuda()
+    D = torch.randn(h, generator=gen).cuda()
+    bias = (torch.randn(h, generator=gen) * 0.5).cuda()
+    dy = torch.randn(b, length, h, P, generator=gen).to("cuda", dtype)
+    runs = []
+    for dense in (False, True):
+        x = wide[..., :inner].reshape(b, length, h, P).detach()
+        B = wide[..., inner:inner + gn].reshape(b, length, g, N).detach()
+        C = wide[..., inner + gn:inner + 2 * gn].reshape(b, length, g, N).detach()
+        if dense:
+            x, B, C = x.contiguous(), B.contiguous(), C.contiguous()
+        leaves = [t.requires_grad_(True) for t in (x, B, C)]
+        y, fin = mod.mamba2_chunk_scan(leaves[0], dt, A, leaves[1], leaves[2], chunk_size=64, D=D,
+                                       dt_bias=bias, dt_softplus=True)
+        grads = torch.autograd.grad((y.float() * dy.float()).sum() + fin.float().sum(), leaves)
+        runs.append((y.detach(), fin.detach(), *grads))
+    assert mod.last_path() == "cuda"
+    for a_, b_ in zip(*runs):
+        assert torch.equal(a_, b_)
