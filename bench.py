@@ -645,7 +645,9 @@ def run_block(args, world, rank, device):
     tokens): in_proj (cuBLAS) -> causal conv1d + SiLU -> SSD chunk scan ->
     gated RMSNorm -> out_proj (cuBLAS), the block of the reference's
     integration verifier (benchmarks/verify_cv_integration.py:37-74) at layer
-    size.  Batch sharded; the metric is tokens per second."""
+    size, with the in-projection output split once (as Mamba-2 layer code
+    does) where the verifier slices it three times.  Batch sharded; the metric
+    is tokens per second."""
     import torch.distributed as dist
     from metal_kernelops_b200.cv import causal_conv1d_fn, mamba2_chunk_scan, rmsnorm_gated
     from metal_kernelops_b200.parallel import batch_slice
@@ -674,9 +676,9 @@ def run_block(args, world, rank, device):
     def step():
         with torch.autocast("cuda", dtype=torch.bfloat16):
             zxbcdt = in_proj(x)
-            z = zxbcdt[..., :inner]
-            xbc = zxbcdt[..., inner:2 * inner + 2 * gn]
-            dt = zxbcdt[..., 2 * inner + 2 * gn:]
+            # one split (its backward is one concatenation) rather than three
+            # slices (three zero-filled full-width gradients summed)
+            z, xbc, dt = torch.split(zxbcdt, [inner, inner + 2 * gn, H], dim=-1)
             xbc = causal_conv1d_fn(xbc.transpose(1, 2), conv_w, conv_b, activation="silu").transpose(1, 2)
             xs = xbc[..., :inner].reshape(b, L, H, P)
             B = xbc[..., inner:inner + gn].reshape(b, L, G, N)
