@@ -781,6 +781,14 @@ struct ClVec {
             v[1] = Io2<T>::ld(reinterpret_cast<const T*>(&q.y));
         }
     }
+    static __device__ __forceinline__ void from_raw(uint2 q, float2* v) {
+        if constexpr (sizeof(T) == 4) {
+            v[0] = make_float2(__uint_as_float(q.x), __uint_as_float(q.y));
+        } else {
+            v[0] = Io2<T>::ld(reinterpret_cast<const T*>(&q.x));
+            v[1] = Io2<T>::ld(reinterpret_cast<const T*>(&q.y));
+        }
+    }
     static __device__ __forceinline__ void st(T* p, const float2* v) {
         uint2 q;
         if constexpr (sizeof(T) == 4) {
@@ -806,11 +814,18 @@ __device__ __forceinline__ void cl_weights(const Args& a, int64_t c0, float2 (&w
     }
 }
 
+// Each thread streams its rows through a private ring of kClDepth slots in
+// shared memory, filled by 8-byte asynchronous copies issued kClDepth rows
+// ahead of use (one commit group per row), so many rows are in flight
+// without registers; a thread reads back only what it copied itself.
+constexpr int kClDepth = 16;
+
 template <typename T, int K>
 __global__ void __launch_bounds__(kThreads)
 fwd_cl_kernel(const Args a) {
-    constexpr int M = ClVec<T>::M, V = ClVec<T>::V, TAPS = K - 1;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int M = ClVec<T>::M, V = ClVec<T>::V;
+    extern __shared__ __align__(16) uint2 cl_stage[];       // [kClDepth][kThreads]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t c0 = ((int64_t)blockIdx.x * 32 + lane) * V;
     const int64_t b = blockIdx.z, L = a.length;
     const int64_t t_begin = ((int64_t)blockIdx.y * kClWarps + warp) * kRun;
@@ -818,6 +833,12 @@ fwd_cl_kernel(const Args a) {
     const int64_t t_end = min64(t_begin + kRun, L);
     const T* x = static_cast<const T*>(a.x) + b * L * a.xs + c0;
     T* out = static_cast<T*>(a.out) + b * L * a.channels + c0;
+    auto slot = [&](int64_t t) { return tc::smem_u32(&cl_stage[(int)((t - t_begin) % kClDepth) * kThreads + tid]); };
+#pragma unroll
+    for (int i = 0; i < kClDepth; ++i) {
+        if (t_begin + i < t_end) tc::cp_async8(slot(t_begin + i), x + (t_begin + i) * a.xs);
+        tc::cp_async_commit();
+    }
     float2 wh[K][M], bh[M];
     cl_weights<T, K>(a, c0, wh, bh);
     const bool silu = a.flags & kSilu;
@@ -836,33 +857,40 @@ fwd_cl_kernel(const Args a) {
         for (int u = 0; u < K; ++u) {       // row t0 + u in slot u
             const int64_t t = t0 + u;
             if (t >= t_end) break;
-            ClVec<T>::ld(x + t * a.xs, ring[u]);
+            tc::cp_async_wait<kClDepth - 1>();
+            const uint2 q = cl_stage[(int)((t - t_begin) % kClDepth) * kThreads + tid];
+            ClVec<T>::from_raw(q, ring[u]);
+            // refill the slot just read (its value is in registers now)
+            if (t + kClDepth < t_end) tc::cp_async8(slot(t), x + (t + kClDepth) * a.xs);
+            tc::cp_async_commit();
             float2 o[M];
 #pragma unroll
             for (int m = 0; m < M; ++m) {
                 float2 hp = bh[m];
 #pragma unroll
-                for (int j = 0; j < K; ++j) hp = fma2(wh[j][m], ring[(u + 1 + j) % K][m], hp);   // row t - TAPS + j
+                for (int j = 0; j < K; ++j) hp = fma2(wh[j][m], ring[(u + 1 + j) % K][m], hp);   // row t - taps + j
                 o[m] = silu ? silu2_half<T>(hp) : add2(hp, hp);
             }
             ClVec<T>::st(out + t * a.channels, o);
         }
     }
-    (void)TAPS;
+    tc::cp_async_wait<0>();
 }
 
 // Backward: for u = t_begin .. t_end + taps - 1 the thread forms the doubled
 // gradient g(u) = 2 dout(u) silu'(pre(u)) (0 past the row) from the x ring
 // (rows u - taps .. u) and keeps it in a ring of its own; dx(u - taps) =
 // sum_j (w_j / 2) g(u - j) once u - taps >= t_begin, and the dweight / dbias
-// products of the run's own steps.  The CTA's warps add their sums in a fixed
-// order into one partial per (batch, CTA row block, channel).
+// products of the run's own steps.  x and dout rows stream through the
+// thread's shared-memory ring like the forward's.  The CTA's warps add their
+// sums in a fixed order (in the ring's space, after the loop) into one
+// partial per (batch, CTA row block, channel).
 template <typename T, int K>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, K <= 4 ? 2 : 1)
 bwd_cl_kernel(const Args a) {
     constexpr int M = ClVec<T>::M, V = ClVec<T>::V, TAPS = K - 1;
-    __shared__ float red[kClWarps][32 * V][K + 1];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    extern __shared__ __align__(16) uint2 cl_stage[];       // [kClDepth][2][kThreads]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t c0 = ((int64_t)blockIdx.x * 32 + lane) * V;
     const int64_t b = blockIdx.z, L = a.length;
     const int64_t t_begin = ((int64_t)blockIdx.y * kClWarps + warp) * kRun;
@@ -874,9 +902,20 @@ bwd_cl_kernel(const Args a) {
         for (int m = 0; m < M; ++m) acc[j][m] = f2(0.0f);
     if (live) {
         const int64_t t_end = min64(t_begin + kRun, L);
+        const int64_t u_end = t_end + TAPS, u_load = min64(u_end, L);   // rows staged: [t_begin, u_load)
         const T* x = static_cast<const T*>(a.x) + b * L * a.xs + c0;
         const T* dout = static_cast<const T*>(a.dout) + b * L * a.ds + c0;
         T* dx = static_cast<T*>(a.dx) + b * L * a.channels + c0;
+        auto sidx = [&](int64_t u, int k) { return ((int)((u - t_begin) % kClDepth) * 2 + k) * kThreads + tid; };
+        auto issue = [&](int64_t u) {
+            tc::cp_async8(tc::smem_u32(&cl_stage[sidx(u, 0)]), x + u * a.xs);
+            tc::cp_async8(tc::smem_u32(&cl_stage[sidx(u, 1)]), dout + u * a.ds);
+        };
+#pragma unroll
+        for (int i = 0; i < kClDepth; ++i) {
+            if (t_begin + i < u_load) issue(t_begin + i);
+            tc::cp_async_commit();
+        }
         float2 wh[K][M], bh[M];
         cl_weights<T, K>(a, c0, wh, bh);
         const bool silu = a.flags & kSilu;
@@ -892,16 +931,17 @@ bwd_cl_kernel(const Args a) {
 #pragma unroll
             for (int m = 0; m < M; ++m) gr[i][m] = f2(0.0f);   // g before the run: unused
         }
-        const int64_t u_end = t_end + TAPS;
         for (int64_t u0 = t_begin; u0 < u_end; u0 += K) {
 #pragma unroll
             for (int k = 0; k < K; ++k) {   // step u = u0 + k in slot k
                 const int64_t u = u0 + k;
                 if (u >= u_end) break;
                 float2 g[M];
+                tc::cp_async_wait<kClDepth - 1>();
                 if (u < L) {
-                    ClVec<T>::ld(x + u * a.xs, xr[k]);
-                    ClVec<T>::ld(dout + u * a.ds, g);
+                    ClVec<T>::from_raw(cl_stage[sidx(u, 0)], xr[k]);
+                    ClVec<T>::from_raw(cl_stage[sidx(u, 1)], g);
+                    if (u + kClDepth < u_load) issue(u + kClDepth);
 #pragma unroll
                     for (int m = 0; m < M; ++m) {
                         if (silu) {
@@ -917,6 +957,7 @@ bwd_cl_kernel(const Args a) {
 #pragma unroll
                     for (int m = 0; m < M; ++m) { g[m] = f2(0.0f); xr[k][m] = f2(0.0f); }
                 }
+                tc::cp_async_commit();
 #pragma unroll
                 for (int m = 0; m < M; ++m) gr[k][m] = g[m];
                 if (u < t_end) {
@@ -940,23 +981,27 @@ bwd_cl_kernel(const Args a) {
                 }
             }
         }
+        tc::cp_async_wait<0>();
     }
+    __syncthreads();                               // every ring is idle: its space takes the fold
+    float* red = reinterpret_cast<float*>(cl_stage);   // [kClWarps][32 V][K + 1]
+    constexpr int RW = 32 * V * (K + 1);
 #pragma unroll
     for (int j = 0; j <= K; ++j)
 #pragma unroll
         for (int m = 0; m < M; ++m) {
-            red[warp][lane * V + 2 * m][j] = 0.5f * acc[j][m].x;
-            red[warp][lane * V + 2 * m + 1][j] = 0.5f * acc[j][m].y;
+            red[warp * RW + (lane * V + 2 * m) * (K + 1) + j] = 0.5f * acc[j][m].x;
+            red[warp * RW + (lane * V + 2 * m + 1) * (K + 1) + j] = 0.5f * acc[j][m].y;
         }
     __syncthreads();
     const int64_t nrb = (L + kClWarps * kRun - 1) / (kClWarps * kRun);
     float* part = a.partial + ((b * nrb + blockIdx.y) * a.channels + (int64_t)blockIdx.x * 32 * V) * (K + 1);
-    for (int i = threadIdx.x; i < 32 * V * (K + 1); i += kThreads) {
-        const int cl = i / (K + 1), j = i - cl * (K + 1);
+    for (int i = threadIdx.x; i < RW; i += kThreads) {
+        const int cl = i / (K + 1);
         if ((int64_t)blockIdx.x * 32 * V + cl >= a.channels) continue;
         float s = 0.0f;
 #pragma unroll
-        for (int w = 0; w < kClWarps; ++w) s += red[w][cl][j];
+        for (int w = 0; w < kClWarps; ++w) s += red[w * RW + i];
         part[i] = s;
     }
 }
@@ -1155,7 +1200,7 @@ static int launch_fwd_cl(const Args& a, cudaStream_t st) {
     constexpr int V = ClVec<T>::V;
     const dim3 grid((unsigned)ceil_div(a.channels, 32 * V), (unsigned)ceil_div(a.length, (int64_t)kClWarps * kRun),
                     (unsigned)a.batch);
-    fwd_cl_kernel<T, K><<<grid, kThreads, 0, st>>>(a);
+    fwd_cl_kernel<T, K><<<grid, kThreads, (size_t)kClDepth * kThreads * 8, st>>>(a);
     return check_launch("causal_conv1d fwd (channel-last)");
 }
 
@@ -1164,7 +1209,12 @@ static int launch_bwd_cl(const Args& a, float* dweight, float* dbias, cudaStream
     constexpr int V = ClVec<T>::V;
     const dim3 grid((unsigned)ceil_div(a.channels, 32 * V), (unsigned)ceil_div(a.length, (int64_t)kClWarps * kRun),
                     (unsigned)a.batch);
-    bwd_cl_kernel<T, K><<<grid, kThreads, 0, st>>>(a);
+    const size_t sm = (size_t)kClDepth * 2 * kThreads * 8;   // also holds the fold
+    static_assert((size_t)kClDepth * 2 * kThreads * 8 >= (size_t)kClWarps * 32 * ClVec<T>::V * (K + 1) * 4,
+                  "the dweight fold fits in the ring space");
+    if (cudaFuncSetAttribute(bwd_cl_kernel<T, K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
+        return check_launch("causal_conv1d bwd (channel-last): smem attribute");
+    bwd_cl_kernel<T, K><<<grid, kThreads, sm, st>>>(a);
     if (int s = check_launch("causal_conv1d bwd (channel-last)")) return s;
     const int64_t total = a.channels * (K + 1);
     finalize_cl_kernel<K><<<(unsigned)min64(ceil_div(total, 256), 148 * 8), 256, 0, st>>>(a, dweight, dbias);
