@@ -31,13 +31,21 @@ def test_library_exports_every_declared_symbol():
     assert lib.ssm_status_string(0) == b"ok"
 
 
+def _STRUCTS(nat):
+    return (("ssm_selective_scan_params", nat.SelectiveScanParams),
+            ("ssm_state_update_params", nat.StateUpdateParams),
+            ("ssm_chunk_scan_params", nat.ChunkScanParams),
+            ("ssm_ss2d_scan_params", nat.Ss2dScanParams),
+            ("ssm_causal_conv1d_params", nat.CausalConv1dParams),
+            ("ssm_causal_conv1d_update_params", nat.CausalConv1dUpdateParams),
+            ("ssm_gated_rmsnorm_params", nat.GatedRmsNormParams))
+
+
 def test_struct_layouts_match_header():
     """Field order and count of the ctypes mirrors equal the C structs."""
     from metal_kernelops_b200 import _native as nat
     text = HEADER.read_text()
-    for cname, struct in (("ssm_selective_scan_params", nat.SelectiveScanParams),
-                          ("ssm_state_update_params", nat.StateUpdateParams),
-                          ("ssm_chunk_scan_params", nat.ChunkScanParams)):
+    for cname, struct in _STRUCTS(nat):
         body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), text, re.S).group(1)
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
         fields = []
@@ -49,6 +57,33 @@ def test_struct_layouts_match_header():
             for n in names.split(","):
                 fields.append(n.strip().lstrip("*").strip())
         assert [f for f, _ in struct._fields_] == fields, cname
+
+
+def test_struct_offsets_match_c_compiler(tmp_path):
+    """Every field offset and struct size of the ctypes mirrors equals what a C
+    compiler makes of the header (gcc on a generated probe program)."""
+    import shutil
+    import subprocess
+    from metal_kernelops_b200 import _native as nat
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    lines = ['#include <stdio.h>', '#include "ssm_b200.h"', "int main(void) {"]
+    want = []
+    for cname, struct in _STRUCTS(nat):
+        lines.append(f'printf("%zu\\n", sizeof({cname}));')
+        want.append(ctypes.sizeof(struct))
+        for name, _ in struct._fields_:
+            lines.append(f'printf("%zu\\n", offsetof({cname}, {name}));')
+            want.append(getattr(struct, name).offset)
+    lines += ["return 0;", "}"]
+    src = tmp_path / "probe.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "probe"
+    subprocess.run([gcc, "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], check=True, capture_output=True,
+                                          text=True).stdout.split()]
+    assert got == want
 
 
 def test_invalid_arguments_rejected_by_abi():
