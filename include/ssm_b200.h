@@ -89,8 +89,10 @@ typedef struct ssm_selective_scan_params {
     const float* delta_bias;    /* may be NULL without SSM_HAS_BIAS */
     /* forward output */
     void* y;
-    /* chunk-entering states, fp32, written by the forward and read by the
-     * backward (NULL in the forward = inference, nothing saved) */
+    /* saved for the backward (checkpoint_bytes, 16-byte aligned): the fp32
+     * states entering every 4-step sub-block, then the scan output before the
+     * D skip and the gate in act_dtype.  Written by the forward and read by
+     * the backward (NULL in the forward = inference, nothing saved) */
     float* checkpoints;
     /* backward */
     const void* dout;

@@ -18,12 +18,13 @@
 //  * Tiles of u/delta/z(/dout) and of B/C are staged in shared memory with
 //    cp.async (16-byte asynchronous copies, double-buffered in the forward).
 //    B and C are converted to fp32 [t][n] and read as broadcasts.
-//  * The forward stores the state entering every kChunk-step chunk
-//    (fp32 "checkpoints", 1 byte per element per direction at N=16).  The
-//    backward walks chunks in reverse: pass A recomputes the chunk from its
-//    checkpoint (y for dz, dC, sub-checkpoints every kTS steps); pass B replays
-//    each sub-block from its sub-checkpoint with states and decays kept in
-//    registers and runs the adjoint recurrence backwards (du, ddelta, dA, dB).
+//  * The forward stores the state entering every kTS-step sub-block (fp32
+//    "checkpoints", 1 byte per element-state per direction) and the scan
+//    output before the skip and gate, in the activation dtype (for dz).  The
+//    backward walks kChunk-step chunks in reverse: it replays each sub-block
+//    from its checkpoint with states and decays kept in registers and runs the
+//    adjoint recurrence backwards (du, ddelta, dA, dB, and dC from the
+//    replayed states).
 //    Two exps per element-state in the backward, one in the forward.
 //  * dB/dC are reduced over the warp's channels with a butterfly
 //    reduce-scatter, over the CTA's warps in shared memory, and written as one
@@ -60,6 +61,8 @@ struct Args {
     const void* u; const void* delta; const float* A; const void* B; const void* C;
     const float* D; const void* z; const float* delta_bias;
     void* y; float* ckpt;
+    int64_t nsub;         // sub-checkpoints per row: nchunks * kChunk / kTS
+    int64_t ysave_off;    // bytes from ckpt to the saved scan output (activation dtype)
     const void* dout; void* du; void* ddelta; void* dz;
     float* dB_part; float* dC_part;   // (batch*groups*nct, dstate, length)
     float* dA_part;                   // (batch, dim, dstate)
@@ -270,27 +273,33 @@ fwd_kernel(const Args a) {
             continue;
         }
 
-        if (a.ckpt != nullptr && (t0 % kChunk) == 0 && cvalid) {
-            float* cp = a.ckpt + ((b * a.nchunks + t0 / kChunk) * a.dim + d) * N + sub * NPT;
+        // the state entering sub-block s (every kTS steps), for the backward;
+        // streaming stores, so the saved states do not push the B/C tiles that
+        // every CTA of the batch re-reads out of L2
+        auto store_ckpt = [&](int64_t s) {
+            float* cp = a.ckpt + ((b * a.nsub + s) * a.dim + d) * N + sub * NPT;
             if (N % 4 == 0 && sub * NPT < N) {   // 16-byte aligned rows: vector stores
 #pragma unroll
                 for (int j = 0; j < NH; j += 2)
                     if (sub * NPT + 2 * j < N)
-                        *reinterpret_cast<float4*>(cp + 2 * j) = make_float4(x2[j].x, x2[j].y, x2[j + 1].x, x2[j + 1].y);
+                        __stcs(reinterpret_cast<float4*>(cp + 2 * j),
+                               make_float4(x2[j].x, x2[j].y, x2[j + 1].x, x2[j + 1].y));
             } else {
 #pragma unroll
                 for (int j = 0; j < NH; ++j) {
                     const int n = sub * NPT + 2 * j;
-                    if (n < N) cp[2 * j] = x2[j].x;
-                    if (n + 1 < N) cp[2 * j + 1] = x2[j].y;
+                    if (n < N) __stcs(&cp[2 * j], x2[j].x);
+                    if (n + 1 < N) __stcs(&cp[2 * j + 1], x2[j].y);
                 }
             }
-        }
+        };
+        const bool save = a.ckpt != nullptr && cvalid;
 
         // phase 1: the recurrence, two states per packed instruction
         float2* vr = dvu + c * FS;
 #pragma unroll 4
         for (int t = 0; t < len; ++t) {
+            if (save && (t % kTS) == 0) store_ckpt((t0 + t) / kTS);
             const float2 v = vr[t];
             const float2 dl2 = make_float2(v.x, v.x), du2 = make_float2(v.y, v.y);
             const float4* B4 = reinterpret_cast<const float4*>(Bs + t * NP + sub * NPT);
@@ -314,13 +323,27 @@ fwd_kernel(const Args a) {
         }
         __syncthreads();
 
-        // phase 2: skip, gate, store (two steps per iteration, coalesced along t)
+        // phase 2: skip, gate, store (two steps per iteration, coalesced along t);
+        // with checkpoints, also the scan output before the skip and the gate
+        // (the backward's dz needs it)
+        T* ysv = a.ckpt != nullptr ? reinterpret_cast<T*>(reinterpret_cast<char*>(a.ckpt) + a.ysave_off) : nullptr;
         for (int i = tid; i < CPC * (TT / 2); i += kThreads) {
             const int cc = i / (TT / 2), t = 2 * (i % (TT / 2));
             if (cc >= rows || t >= len) continue;
             const float2 ur = Io2<T>::ld(&ru[cc * TT + t]);
-            float o0 = fmaf(ur.x, Dch[cc], dvu[cc * FS + t].x);
-            float o1 = fmaf(ur.y, Dch[cc], dvu[cc * FS + t + 1].x);
+            const float y0 = dvu[cc * FS + t].x, y1 = dvu[cc * FS + t + 1].x;
+            if (ysv != nullptr) {
+                T* ys = &ysv[(row0 + cc) * L + t0 + t];
+                if (a.fast || t + 1 >= len) {
+                    if (t + 1 < len) Io2<T>::st(ys, make_float2(y0, y1));
+                    else stf(ys, y0);
+                } else {
+                    stf(ys, y0);
+                    stf(ys + 1, y1);
+                }
+            }
+            float o0 = fmaf(ur.x, Dch[cc], y0);
+            float o1 = fmaf(ur.y, Dch[cc], y1);
             if (has_z) {
                 const float2 zr = Io2<T>::ld(&rz[cc * TT + t]);
                 o0 *= zr.x * sigmoid_t<T>(zr.x);
@@ -437,14 +460,14 @@ template <typename T, int CPC, int NP, int NPT>
 struct BwdLayout {
     static constexpr int K = kChunk;
     static constexpr int FS = K + 1;
-    static constexpr size_t o_raw = 0;                                        // [4][CPC][K] T
-    static constexpr size_t o_rbc = o_raw + 4 * CPC * K * sizeof(T);          // [2][NP][K*4+16] B
+    static constexpr size_t o_raw = 0;                                        // [5][CPC][K] T
+    static constexpr size_t o_rbc = o_raw + 5 * CPC * K * sizeof(T);          // [2][NP][K*4+16] B
     static constexpr size_t o_dvu = o_rbc + 2 * NP * (K * 4 + 16);            // [CPC][FS] float2
-    static constexpr size_t o_f = o_dvu + (size_t)CPC * FS * 8;               // [4][CPC][FS] float
+    static constexpr size_t o_f = o_dvu + (size_t)CPC * FS * 8;               // [3][CPC][FS] float
     // four permuted copies of B (then C), copy stride = K*NP + 16 floats so the
     // copies start 64 bytes apart modulo 128 and a warp's reads spread over banks
     static constexpr int CS = K * NP + 16;
-    static constexpr size_t o_bc = (o_f + 4 * (size_t)CPC * FS * 4 + 15) / 16 * 16;  // [2][4][CS]
+    static constexpr size_t o_bc = (o_f + 3 * (size_t)CPC * FS * 4 + 15) / 16 * 16;  // [2][4][CS]
     static constexpr size_t o_w = o_bc + 2 * 4 * CS * 4;                      // [2][kWarps][K][NP+1]
     static constexpr size_t o_sck = o_w + 2 * (size_t)kWarps * K * (NP + 1) * 4;  // [K/TS][NPT/2][thr] f2
     static constexpr size_t o_ch = o_sck + (size_t)(K / kTS) * NPT * kThreads * 4;  // [2][CPC]
@@ -477,11 +500,11 @@ bwd_kernel(const Args a) {
     T* rd = raw + CPC * K;        // delta
     T* rz = raw + 2 * CPC * K;    // z
     T* rg = raw + 3 * CPC * K;    // dout
+    T* ry = raw + 4 * CPC * K;    // scan output before skip and gate (saved by the forward)
     unsigned char* rbc = smem + Lay::o_rbc;
     float2* dvu = reinterpret_cast<float2*>(smem + Lay::o_dvu);   // (delta', delta'*u)
     float* gs = reinterpret_cast<float*>(smem + Lay::o_f);        // gradient seen by the scan
-    float* yv = gs + CPC * FS;                                    // scan output (pass A)
-    float* dua = yv + CPC * FS;                                   // sum_n dh*B (pass B)
+    float* dua = gs + CPC * FS;                                   // sum_n dh*B (pass B)
     float* dda = dua + CPC * FS;                                  // sum_n dh*a*x_prev*A (pass B)
     constexpr int CS = Lay::CS;
     float* Bs = reinterpret_cast<float*>(smem + Lay::o_bc);       // [4 perms][CS]: [K][NP] + pad
@@ -544,6 +567,7 @@ bwd_kernel(const Args a) {
     const T* dg = reinterpret_cast<const T*>(a.delta);
     const T* zg = reinterpret_cast<const T*>(a.z);
     const T* gg = reinterpret_cast<const T*>(a.dout);
+    const T* ysg = reinterpret_cast<const T*>(reinterpret_cast<const char*>(a.ckpt) + a.ysave_off);
     T* dug = reinterpret_cast<T*>(a.du);
     T* ddg = reinterpret_cast<T*>(a.ddelta);
     T* dzg = reinterpret_cast<T*>(a.dz);
@@ -560,9 +584,25 @@ bwd_kernel(const Args a) {
         stage_act<T, CPC, K>(rd, dg, row0, rows, L, t0, len, a.fast);
         if (has_z) stage_act<T, CPC, K>(rz, zg, row0, rows, L, t0, len, a.fast);
         stage_act<T, CPC, K>(rg, gg, row0, rows, L, t0, len, a.fast);
+        stage_act<T, CPC, K>(ry, ysg, row0, rows, L, t0, len, a.fast);
         stage_bc<NP, K>(rbc, a.B, a.bc_dtype, bg, N, L, t0, len, a.fast);
         stage_bc<NP, K>(rbc + NP * (K * 4 + 16), a.C, a.bc_dtype, bg, N, L, t0, len, a.fast);
         cp_async_commit();
+        {   // the states entering the chunk's sub-blocks (saved by the forward),
+            // in this lane's state order; each thread reads back only its own
+            const int nsb = (len + TS - 1) / TS;
+#pragma unroll
+            for (int sb = 0; sb < K / TS; ++sb) {
+                const float* cp = a.ckpt + ((b * a.nsub + tile * (K / TS) + sb) * a.dim + d) * N;
+                const bool live = cvalid && sb < nsb;
+#pragma unroll
+                for (int j = 0; j < NH; ++j) {
+                    const int n0 = sub * NPT + ((2 * j) ^ pm), n1 = sub * NPT + ((2 * j + 1) ^ pm);
+                    sck[(sb * NH + j) * kThreads + tid] =
+                        make_float2((live && n0 < N) ? __ldcs(&cp[n0]) : 0.0f, (live && n1 < N) ? __ldcs(&cp[n1]) : 0.0f);
+                }
+            }
+        }
         cp_async_wait<0>();
         __syncthreads();
 
@@ -605,63 +645,9 @@ bwd_kernel(const Args a) {
         // and for the ragged last chunk.
         auto chunk_body = [&](auto full_tag) {
             constexpr bool FULL = decltype(full_tag)::value;
-            // ---- pass A: forward recompute from the checkpoint -----------------
             float2 x2[NH];
-            {
-                const float* cp = a.ckpt + ((b * a.nchunks + tile) * a.dim + d) * N;
-    #pragma unroll
-                for (int j = 0; j < NH; ++j) {
-                    const int n0 = sub * NPT + ((2 * j) ^ pm), n1 = sub * NPT + ((2 * j + 1) ^ pm);
-                    x2[j] = make_float2((cvalid && n0 < N) ? cp[n0] : 0.0f,
-                                        (cvalid && n1 < N) ? cp[n1] : 0.0f);
-                }
-            }
             const float2* vr = dvu + c * FS;
             const float* gr = gs + c * FS;
-            for (int tb = 0; tb < (FULL ? K : len); tb += TS) {
-    #pragma unroll
-                for (int j = 0; j < NH; ++j) sck[((tb / TS) * NH + j) * kThreads + tid] = x2[j];
-    #pragma unroll
-                for (int jj = 0; jj < TS; ++jj) {
-                    const int t = tb + jj;
-                    if (!FULL && t >= len) break;
-                    const float2 v = vr[t];
-                    const float dl = v.x * kLog2e;
-                    const float2 dl2 = make_float2(dl, dl), du2 = make_float2(v.y, v.y);
-                    const float gv = gr[t];
-                    const float2 g2 = make_float2(gv, gv);
-                    const float4* B4 = reinterpret_cast<const float4*>(Bp + t * NP);
-                    const float4* C4 = reinterpret_cast<const float4*>(Cp + t * NP);
-                    float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
-                    float w[NPT];
-    #pragma unroll
-                    for (int qq = 0; qq < NPT / 4; ++qq) {
-                        const float4 bq = B4[qq ^ qx], cq = C4[qq ^ qx];
-                        const float2 a0 = __fmul2_rn(dl2, An2[2 * qq]);
-                        const float2 a1 = __fmul2_rn(dl2, An2[2 * qq + 1]);
-                        const float2 e0 = make_float2(exp2_mufu(a0.x), exp2_mufu(a0.y));
-                        const float2 e1 = make_float2(exp2_mufu(a1.x), exp2_mufu(a1.y));
-                        x2[2 * qq] = __ffma2_rn(e0, x2[2 * qq], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
-                        x2[2 * qq + 1] = __ffma2_rn(e1, x2[2 * qq + 1], __fmul2_rn(du2, make_float2(bq.z, bq.w)));
-                        acc0 = __ffma2_rn(x2[2 * qq], make_float2(cq.x, cq.y), acc0);
-                        acc1 = __ffma2_rn(x2[2 * qq + 1], make_float2(cq.z, cq.w), acc1);
-                        const float2 w0 = __fmul2_rn(g2, x2[2 * qq]);
-                        const float2 w1 = __fmul2_rn(g2, x2[2 * qq + 1]);
-                        w[4 * qq + 0] = w0.x;
-                        w[4 * qq + 1] = w0.y;
-                        w[4 * qq + 2] = w1.x;
-                        w[4 * qq + 3] = w1.y;
-                    }
-                    float ysum = (acc0.x + acc0.y) + (acc1.x + acc1.y);
-                    ysum = sum_low_lanes<LPC>(ysum);
-                    Sc::reduce(w);
-                    if (own) {
-    #pragma unroll
-                        for (int i = 0; i < KEPT; ++i) dCw[(warp * K + t) * NPW + sub * NPT + pm + i] = w[i];
-                    }
-                    if (sub == 0) yv[c * FS + t] = ysum;
-                }
-            }
 
             // ---- pass B: reverse over sub-blocks ---------------------------------
             for (int sb = ((FULL ? K : len) - 1) / TS; sb >= 0; --sb) {
@@ -731,6 +717,21 @@ bwd_kernel(const Args a) {
     #pragma unroll
                             for (int i = 0; i < KEPT; ++i) dBw[(warp * K + t) * NPW + sub * NPT + pm + i] = w[i];
                         }
+                        // dC from the state after step t: the next step's entering
+                        // state, or the replay's end state for the block's last step
+                        const bool last = FULL ? (jj == TS - 1) : (jj == nb - 1);
+    #pragma unroll
+                        for (int j = 0; j < NH; ++j) {
+                            const float2 xt = (jj + 1 < TS && !last) ? xh[jj + 1 < TS ? jj + 1 : jj][j] : x2[j];
+                            const float2 wv = __fmul2_rn(g2, xt);
+                            w[2 * j] = wv.x;
+                            w[2 * j + 1] = wv.y;
+                        }
+                        Sc::reduce(w);
+                        if (own) {
+    #pragma unroll
+                            for (int i = 0; i < KEPT; ++i) dCw[(warp * K + t) * NPW + sub * NPT + pm + i] = w[i];
+                        }
                         if (sub == 0) {
                             dua[c * FS + t] = duacc;
                             dda[c * FS + t] = ddacc;
@@ -776,7 +777,7 @@ bwd_kernel(const Args a) {
                     o_dd[k] = ddt;
                     if (has_z) {
                         const float sg = sigmoid_t<T>(zz[k]);
-                        o_dz[k] = gg2[k] * fmaf(uu[k], Dv, yv[cc * FS + tt]) * sg * fmaf(zz[k], 1.0f - sg, 1.0f);
+                        o_dz[k] = gg2[k] * fmaf(uu[k], Dv, ldf(&ry[cc * K + tt])) * sg * fmaf(zz[k], 1.0f - sg, 1.0f);
                     }
                     if (tt < len) {
                         pD = fmaf(gv, uu[k], pD);
@@ -1103,6 +1104,18 @@ static int validate(const ssm_selective_scan_params* p, int mode) {
 
 static bool aligned16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; }
 
+// The checkpoint buffer: the fp32 states entering every kTS-step sub-block,
+// (batch, sub-block, dim, dstate), then the scan output before the skip and
+// the gate, (batch, dim, length) in the activation dtype.
+static size_t ckpt_state_bytes(const ssm_selective_scan_params* p) {
+    const int64_t nsub = ceil_div(p->length, kChunk) * (kChunk / kTS);
+    return align_up((size_t)(p->batch * nsub * p->dim * p->dstate) * 4, 256);
+}
+static size_t ckpt_bytes(const ssm_selective_scan_params* p) {
+    const size_t ae = p->act_dtype == SSM_F32 ? 4 : 2;
+    return ckpt_state_bytes(p) + align_up((size_t)(p->batch * p->dim * p->length) * ae, 256);
+}
+
 static void make_args(const ssm_selective_scan_params* p, int cpc, Args& a) {
     a.batch = p->batch; a.dim = p->dim; a.length = p->length; a.groups = p->groups;
     a.dstate = p->dstate; a.per_group = p->dim / p->groups;
@@ -1112,10 +1125,13 @@ static void make_args(const ssm_selective_scan_params* p, int cpc, Args& a) {
     const int64_t ae = p->act_dtype == SSM_F32 ? 4 : 2, be = p->bc_dtype == SSM_F32 ? 4 : 2;
     a.fast = (p->length * ae) % 16 == 0 && (p->length * be) % 16 == 0 && aligned16(p->u) &&
              aligned16(p->delta) && aligned16(p->B) && aligned16(p->C) &&
-             (!(p->flags & SSM_HAS_Z) || aligned16(p->z)) && (p->dout == nullptr || aligned16(p->dout));
+             (!(p->flags & SSM_HAS_Z) || aligned16(p->z)) && (p->dout == nullptr || aligned16(p->dout)) &&
+             (p->checkpoints == nullptr || aligned16(p->checkpoints));
     a.u = p->u; a.delta = p->delta; a.A = p->A; a.B = p->B; a.C = p->C;
     a.D = p->D; a.z = p->z; a.delta_bias = p->delta_bias;
     a.y = p->y; a.ckpt = p->checkpoints;
+    a.nsub = a.nchunks * (kChunk / kTS);
+    a.ysave_off = (int64_t)ckpt_state_bytes(p);
     a.dout = p->dout; a.du = p->du; a.ddelta = p->ddelta; a.dz = p->dz;
     a.dB_part = a.dC_part = a.dA_part = a.dD_part = a.db_part = nullptr;
     a.nseg = 1;
@@ -1263,7 +1279,7 @@ extern "C" int ssm_selective_scan_sizes(const ssm_selective_scan_params* p,
     bwd_cfg(p->dstate, p->batch * p->dim, cb);
     const int64_t nct = ceil_div(p->dim / p->groups, 32 / cb.lpc * kWarps);
     if (checkpoint_bytes)
-        *checkpoint_bytes = (size_t)(p->batch * ceil_div(p->length, kChunk) * p->dim * p->dstate) * 4;
+        *checkpoint_bytes = ckpt_bytes(p);
     if (workspace_bytes) *workspace_bytes = ws_layout(p, nct, bwd_plan(p, cb)).total;
     return SSM_OK;
 }

@@ -34,6 +34,8 @@ import torch
 from . import _native as nat
 
 CHUNK = 16
+"""Steps per chunk of the backward's reverse walk."""
+SUB_BLOCK = 4
 """Steps between the states the forward saves for the backward."""
 
 __all__ = ["CHUNK", "selective_scan", "selective_scan_fn", "scan_cuda"]
@@ -85,7 +87,12 @@ def _fwd(u: torch.Tensor, delta: torch.Tensor, A: torch.Tensor, B: torch.Tensor,
 @_fwd.register_fake
 def _(u, delta, A, B, C, D, z, delta_bias, softplus, save):
     batch, dim, length = u.shape
-    n = batch * (-(-length // CHUNK)) * dim * A.shape[1] if save else 0
+    if save:   # sub-block states, then the saved scan output (both 256-byte padded)
+        states = batch * (-(-length // CHUNK)) * (CHUNK // SUB_BLOCK) * dim * A.shape[1] * 4
+        ybytes = batch * dim * length * u.element_size()
+        n = (-(-states // 256) * 256 + -(-ybytes // 256) * 256) // 4
+    else:
+        n = 0
     return torch.empty_like(u), u.new_empty(n, dtype=torch.float32)
 
 
