@@ -140,10 +140,13 @@ def _setup(ctx, inputs, output):
     x, weight, bias, init, silu, want_final = inputs
     ctx.save_for_backward(x, weight, bias, init)
     ctx.silu = silu
+    ctx.set_materialize_grads(False)     # no zero-filled gradient for the final state
 
 
 def _backward(ctx, dout, dfinal):
     x, weight, bias, init = ctx.saved_tensors
+    if dout is None:
+        return (None,) * 6
     dx, dweight, dbias, dinit = _bwd(dout.contiguous(), x, weight, bias, init, ctx.silu)
     return (dx, dweight, dbias if bias is not None else None,
             dinit if init is not None else None, None, None)

@@ -107,12 +107,15 @@ def _setup(ctx, inputs, output):
     _, rstd = output
     ctx.save_for_backward(x, weight, bias, z, rstd)
     ctx.eps, ctx.group, ctx.gate = eps, group, gate
+    ctx.set_materialize_grads(False)     # no zero-filled gradient for rstd
 
 
 def _backward(ctx, dout, drstd):
     x, weight, bias, z, rstd = ctx.saved_tensors
     if rstd.numel() == 0 and x.numel() != 0:
         raise RuntimeError("rmsnorm_gated: the forward did not save its statistics (save=False)")
+    if dout is None:
+        return (None,) * 8
     dx, dw, db, dz = _bwd(dout.contiguous(), x, weight, bias, z, rstd, ctx.eps, ctx.group, ctx.gate)
     return (dx, dw, db if bias is not None else None, dz if z is not None else None,
             None, None, None, None)

@@ -164,6 +164,9 @@ def _setup(ctx, inputs, output):
     _, _, saved = output
     ctx.save_for_backward(x, dt, A, B, C, D, z, dt_bias, init, saved)
     ctx.chunk_size, ctx.softplus = chunk_size, softplus
+    # unused outputs (the saved chunk states, an unused final state) arrive as
+    # None instead of zero-filled buffers of their size
+    ctx.set_materialize_grads(False)
 
 
 def _backward(ctx, dy, dfinal, dsaved):

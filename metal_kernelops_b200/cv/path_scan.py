@@ -181,12 +181,15 @@ def _setup(ctx, inputs, output):
     _, ckpt = output
     ctx.save_for_backward(u, dt, A, B, C, ckpt)
     ctx.scale = scale
+    ctx.set_materialize_grads(False)     # no zero-filled gradient for the saved states
 
 
 def _backward(ctx, dy, dckpt):
     u, dt, A, B, C, ckpt = ctx.saved_tensors
     if ckpt.numel() == 0:
         raise RuntimeError("ss2d_scan: the forward did not save its states (save=False)")
+    if dy is None:
+        return (None,) * 7
     du, ddt, dA, dB, dC = _bwd(dy.contiguous(), u, dt, A, B, C, ckpt, ctx.scale)
     return du, ddt, dA, dB.to(B.dtype), dC.to(C.dtype), None, None
 

@@ -142,6 +142,9 @@ def _setup(ctx, inputs, output):
     _, ckpt = output
     ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, ckpt)
     ctx.softplus = softplus
+    # the saved-states output never receives a gradient: without this, autograd
+    # would zero-fill a buffer of its size before every backward
+    ctx.set_materialize_grads(False)
     ctx.flags = (D is not None, z is not None, delta_bias is not None)
 
 
@@ -149,6 +152,8 @@ def _backward(ctx, dy, dckpt):
     u, delta, A, B, C, D, z, delta_bias, ckpt = ctx.saved_tensors
     if ckpt.numel() == 0 and u.numel() != 0:
         raise RuntimeError("selective_scan: the forward did not save its states (save=False)")
+    if dy is None:
+        return (None,) * 10
     du, ddelta, dA, dB, dC, dD, dz, dbias = _bwd(
         dy.contiguous(), u, delta, A, B, C, D, z, delta_bias, ckpt, ctx.softplus)
     has_d, has_z, has_b = ctx.flags
