@@ -40,6 +40,7 @@ from __future__ import annotations
 import torch
 
 from .. import _native as nat
+from ..scan import checkpoint_numel
 
 __all__ = ["MAX_STATES", "MERGE_MODES", "path_orders", "ss2d_scan"]
 
@@ -143,7 +144,8 @@ def _fwd(u: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Tensor, C:
 @_fwd.register_fake
 def _(u, dt, A, B, C, scale, save):
     batch, channels, height, width = u.shape
-    n = batch * (-(-(height * width) // 16)) * 4 * channels * A.shape[1] if save else 0
+    # the four paths run as one Mamba-1 problem of 4 x channels rows
+    n = checkpoint_numel(batch, 4 * channels, height * width, A.shape[1], u.element_size()) if save else 0
     return torch.empty_like(u), u.new_empty(n, dtype=torch.float32)
 
 

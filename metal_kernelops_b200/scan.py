@@ -84,15 +84,20 @@ def _fwd(u: torch.Tensor, delta: torch.Tensor, A: torch.Tensor, B: torch.Tensor,
     return y, ckpt
 
 
+def checkpoint_numel(batch: int, dim: int, length: int, dstate: int, act_size: int) -> int:
+    """fp32 elements of the forward's saved-for-backward buffer (the size
+    ``ssm_selective_scan_sizes`` returns): the states entering every
+    SUB_BLOCK-step block, then the scan output in the activation dtype, each
+    padded to 256 bytes."""
+    states = batch * (-(-length // CHUNK)) * (CHUNK // SUB_BLOCK) * dim * dstate * 4
+    ybytes = batch * dim * length * act_size
+    return (-(-states // 256) * 256 + -(-ybytes // 256) * 256) // 4
+
+
 @_fwd.register_fake
 def _(u, delta, A, B, C, D, z, delta_bias, softplus, save):
     batch, dim, length = u.shape
-    if save:   # sub-block states, then the saved scan output (both 256-byte padded)
-        states = batch * (-(-length // CHUNK)) * (CHUNK // SUB_BLOCK) * dim * A.shape[1] * 4
-        ybytes = batch * dim * length * u.element_size()
-        n = (-(-states // 256) * 256 + -(-ybytes // 256) * 256) // 4
-    else:
-        n = 0
+    n = checkpoint_numel(batch, dim, length, A.shape[1], u.element_size()) if save else 0
     return torch.empty_like(u), u.new_empty(n, dtype=torch.float32)
 
 
