@@ -152,8 +152,11 @@ struct FwdLayout {
 // SUMMARY: the segment summary pass -- run the recurrence over this CTA's
 // segment from a zero state and write the end state and the decay product
 // (no outputs, no checkpoints, C unused).  Segment s < nseg - 1 only.
+// Up to 8 states per lane the main pass fits 56 registers, so 9 CTAs share an
+// SM (1332 slots): a batch-16 x 5120-channel grid of 1280 CTAs runs as one
+// wave instead of a full wave plus a 96-CTA tail.
 template <typename T, int NPT, int LPC, bool SUMMARY>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, (NPT <= 8 && !SUMMARY) ? 9 : 1)
 fwd_kernel(const Args a) {
     constexpr int CPW = 32 / LPC;
     constexpr int CPC = CPW * kWarps;
