@@ -90,9 +90,10 @@ typedef struct ssm_selective_scan_params {
     /* forward output */
     void* y;
     /* saved for the backward (checkpoint_bytes, 16-byte aligned): the fp32
-     * states entering every 4-step sub-block, then the scan output before the
-     * D skip and the gate in act_dtype.  Written by the forward and read by
-     * the backward (NULL in the forward = inference, nothing saved) */
+     * states entering every 4-step sub-block, then (with SSM_HAS_Z) the scan
+     * output before the D skip and the gate in act_dtype.  Written by the
+     * forward and read by the backward (NULL in the forward = inference,
+     * nothing saved) */
     float* checkpoints;
     /* backward */
     const void* dout;

@@ -19,8 +19,9 @@
 //    cp.async (16-byte asynchronous copies, double-buffered in the forward).
 //    B and C are converted to fp32 [t][n] and read as broadcasts.
 //  * The forward stores the state entering every kTS-step sub-block (fp32
-//    "checkpoints", 1 byte per element-state per direction) and the scan
-//    output before the skip and gate, in the activation dtype (for dz).  The
+//    "checkpoints", 1 byte per element-state per direction) and, when there is
+//    a gate, the scan output before the skip and gate in the activation dtype
+//    (for dz).  The
 //    backward walks kChunk-step chunks in reverse: it replays each sub-block
 //    from its checkpoint with states and decays kept in registers and runs the
 //    adjoint recurrence backwards (du, ddelta, dA, dB, and dC from the
@@ -327,9 +328,10 @@ fwd_kernel(const Args a) {
         __syncthreads();
 
         // phase 2: skip, gate, store (two steps per iteration, coalesced along t);
-        // with checkpoints, also the scan output before the skip and the gate
-        // (the backward's dz needs it)
-        T* ysv = a.ckpt != nullptr ? reinterpret_cast<T*>(reinterpret_cast<char*>(a.ckpt) + a.ysave_off) : nullptr;
+        // with checkpoints and a gate, also the scan output before the skip and
+        // the gate (the backward's dz needs it)
+        T* ysv = (a.ckpt != nullptr && has_z)
+                     ? reinterpret_cast<T*>(reinterpret_cast<char*>(a.ckpt) + a.ysave_off) : nullptr;
         for (int i = tid; i < CPC * (TT / 2); i += kThreads) {
             const int cc = i / (TT / 2), t = 2 * (i % (TT / 2));
             if (cc >= rows || t >= len) continue;
@@ -503,7 +505,7 @@ bwd_kernel(const Args a) {
     T* rd = raw + CPC * K;        // delta
     T* rz = raw + 2 * CPC * K;    // z
     T* rg = raw + 3 * CPC * K;    // dout
-    T* ry = raw + 4 * CPC * K;    // scan output before skip and gate (saved by the forward)
+    T* ry = raw + 4 * CPC * K;    // scan output before skip and gate (saved by the forward; gated only)
     unsigned char* rbc = smem + Lay::o_rbc;
     float2* dvu = reinterpret_cast<float2*>(smem + Lay::o_dvu);   // (delta', delta'*u)
     float* gs = reinterpret_cast<float*>(smem + Lay::o_f);        // gradient seen by the scan
@@ -587,7 +589,7 @@ bwd_kernel(const Args a) {
         stage_act<T, CPC, K>(rd, dg, row0, rows, L, t0, len, a.fast);
         if (has_z) stage_act<T, CPC, K>(rz, zg, row0, rows, L, t0, len, a.fast);
         stage_act<T, CPC, K>(rg, gg, row0, rows, L, t0, len, a.fast);
-        stage_act<T, CPC, K>(ry, ysg, row0, rows, L, t0, len, a.fast);
+        if (has_z) stage_act<T, CPC, K>(ry, ysg, row0, rows, L, t0, len, a.fast);
         stage_bc<NP, K>(rbc, a.B, a.bc_dtype, bg, N, L, t0, len, a.fast);
         stage_bc<NP, K>(rbc + NP * (K * 4 + 16), a.C, a.bc_dtype, bg, N, L, t0, len, a.fast);
         cp_async_commit();
