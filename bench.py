@@ -427,7 +427,9 @@ def run_ssd(args, world, rank, device):
     b = rows.stop - rows.start
     L, H, P, N, G, Q = (cfg[k] for k in ("length", "nheads", "headdim", "dstate", "ngroups", "chunk"))
     nc = L // Q
-    # causal-minimal algorithmic flops, forward + backward
+    # causal-minimal algorithmic flops, forward + backward: per chunk the C B^T
+    # products of each group and the masked (Q x Q) x (Q x P) products plus the
+    # chunk-state terms of each head
     flops = b * nc * (3 * G * Q * Q * N + H * (3 * Q * Q * P + 12 * Q * N * P))
     alg_bytes = b * L * (H * P * 2 * 4 + 2 * G * N * 2 * 2 + H * 4 * 2) + b * H * P * N * 4
     peaks, kind = _peaks()
@@ -492,7 +494,7 @@ def run_decode(args, world, rank, device):
 
 
 def run_ss2d(args, world, rank, device):
-    """VMamba four-path 2D scan fwd+bwd (SURVEY 8f), fp32 as in the reference,
+    """VMamba four-path 2D scan fwd+bwd, fp32 as in the reference,
     at the reference's largest timed shape (b1 d96 56x56, 16 states) unless
     --shape batch,channels,height,width overrides it; batch sharded."""
     import torch.distributed as dist
@@ -544,7 +546,7 @@ def run_ss2d(args, world, rank, device):
 
 
 def run_conv1d(args, world, rank, device):
-    """Causal depthwise conv1d fwd+bwd (SURVEY 8f), bf16, K=4, SiLU, at the
+    """Causal depthwise conv1d fwd+bwd, bf16, K=4, SiLU, at the
     Mamba-1 layer shape of BASELINE config 2 (x = (16, 5120, 4096)) unless
     --shape batch,channels,length overrides it; batch sharded.  HBM-bound:
     forward reads x and writes out, backward reads x and dout and writes dx."""
@@ -595,7 +597,7 @@ def run_conv1d(args, world, rank, device):
 
 
 def run_gnorm(args, world, rank, device):
-    """Gated RMSNorm fwd+bwd (SURVEY 8f), bf16, gate before the norm, no bias,
+    """Gated RMSNorm fwd+bwd, bf16, gate before the norm, no bias,
     at the Mamba-2 layer shape of BASELINE config 3; rows sharded.  HBM-bound:
     forward reads x, z and writes out; backward reads x, z, dy and writes dx, dz."""
     import torch.distributed as dist

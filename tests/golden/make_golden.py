@@ -35,7 +35,9 @@ import torch
 import torch.nn.functional as F
 
 HERE = pathlib.Path(__file__).resolve().parent
-sys.path.insert(0, os.environ.get("REFERENCE_SRC", "/root/reference/src"))
+if not os.environ.get("REFERENCE_SRC"):
+    sys.exit("set REFERENCE_SRC to the reference's src directory (the one holding metal_kernelops/)")
+sys.path.insert(0, os.environ["REFERENCE_SRC"])
 
 from metal_kernelops import reference as stepwise  # noqa: E402
 from metal_kernelops.cv import mamba2_chunk_scan, mamba2_chunk_scan_reference  # noqa: E402
