@@ -1110,15 +1110,16 @@ static int validate(const ssm_selective_scan_params* p, int mode) {
 static bool aligned16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; }
 
 // The checkpoint buffer: the fp32 states entering every kTS-step sub-block,
-// (batch, sub-block, dim, dstate), then the scan output before the skip and
-// the gate, (batch, dim, length) in the activation dtype.
+// (batch, sub-block, dim, dstate), then, with a gate, the scan output before
+// the skip and the gate, (batch, dim, length) in the activation dtype.
 static size_t ckpt_state_bytes(const ssm_selective_scan_params* p) {
     const int64_t nsub = ceil_div(p->length, kChunk) * (kChunk / kTS);
     return align_up((size_t)(p->batch * nsub * p->dim * p->dstate) * 4, 256);
 }
 static size_t ckpt_bytes(const ssm_selective_scan_params* p) {
     const size_t ae = p->act_dtype == SSM_F32 ? 4 : 2;
-    return ckpt_state_bytes(p) + align_up((size_t)(p->batch * p->dim * p->length) * ae, 256);
+    const size_t ysave = (p->flags & SSM_HAS_Z) ? (size_t)(p->batch * p->dim * p->length) * ae : 0;
+    return ckpt_state_bytes(p) + align_up(ysave, 256);
 }
 
 static void make_args(const ssm_selective_scan_params* p, int cpc, Args& a) {

@@ -84,20 +84,21 @@ def _fwd(u: torch.Tensor, delta: torch.Tensor, A: torch.Tensor, B: torch.Tensor,
     return y, ckpt
 
 
-def checkpoint_numel(batch: int, dim: int, length: int, dstate: int, act_size: int) -> int:
+def checkpoint_numel(batch: int, dim: int, length: int, dstate: int, act_size: int,
+                     gated: bool) -> int:
     """fp32 elements of the forward's saved-for-backward buffer (the size
     ``ssm_selective_scan_sizes`` returns): the states entering every
-    SUB_BLOCK-step block, then the scan output in the activation dtype, each
-    padded to 256 bytes."""
+    SUB_BLOCK-step block, then, with a gate, the scan output in the activation
+    dtype, each padded to 256 bytes."""
     states = batch * (-(-length // CHUNK)) * (CHUNK // SUB_BLOCK) * dim * dstate * 4
-    ybytes = batch * dim * length * act_size
+    ybytes = batch * dim * length * act_size if gated else 0
     return (-(-states // 256) * 256 + -(-ybytes // 256) * 256) // 4
 
 
 @_fwd.register_fake
 def _(u, delta, A, B, C, D, z, delta_bias, softplus, save):
     batch, dim, length = u.shape
-    n = checkpoint_numel(batch, dim, length, A.shape[1], u.element_size()) if save else 0
+    n = checkpoint_numel(batch, dim, length, A.shape[1], u.element_size(), z is not None) if save else 0
     return torch.empty_like(u), u.new_empty(n, dtype=torch.float32)
 
 

@@ -101,9 +101,10 @@ def test_invalid_arguments_rejected_by_abi():
     assert lib.ssm_state_update_fwd(q, None) == nat.SSM_ERR_INVALID
 
 
+@pytest.mark.parametrize("gated", [False, True])
 @pytest.mark.parametrize("shape", [(2, 8, 64, 16, 2), (3, 24, 37, 4, 4), (1, 5, 1, 16, 2),
                                    (2, 16, 0, 16, 2), (4, 96, 3136, 16, 4)])
-def test_checkpoint_numel_matches_library_size(shape):
+def test_checkpoint_numel_matches_library_size(shape, gated):
     """The fake-tensor size of the saved-for-backward buffer equals the size
     the library asks for (a host-only query), for the scan and for ss2d."""
     from metal_kernelops_b200 import _native as nat
@@ -113,17 +114,18 @@ def test_checkpoint_numel_matches_library_size(shape):
     p = nat.SelectiveScanParams()
     p.batch, p.dim, p.length, p.groups, p.dstate = batch, dim, length, 1, dstate
     p.act_dtype = p.bc_dtype = {4: nat.dtype_code(torch.float32), 2: nat.dtype_code(torch.bfloat16)}[esz]
+    p.flags = nat.HAS_Z if gated else 0
     ck, ws = nat._SZ(), nat._SZ()
     assert lib.ssm_selective_scan_sizes(p, ck, ws) == nat.SSM_OK
-    assert checkpoint_numel(batch, dim, length, dstate, esz) * 4 == ck.value
-    if length and length % 8 == 0:   # ss2d: a (height, 8) map, four paths per channel
+    assert checkpoint_numel(batch, dim, length, dstate, esz, gated) * 4 == ck.value
+    if length and length % 8 == 0 and not gated:   # ss2d: a (height, 8) map, four paths per channel
         q = nat.Ss2dScanParams()
         q.batch, q.channels, q.height, q.width, q.groups, q.dstate = batch, dim, length // 8, 8, 1, dstate
         q.act_dtype = q.bc_dtype = p.act_dtype
         q.scale = 1.0
         ck2, fw, bw = nat._SZ(), nat._SZ(), nat._SZ()
         assert lib.ssm_ss2d_scan_sizes(q, ck2, fw, bw) == nat.SSM_OK
-        assert checkpoint_numel(batch, 4 * dim, length, dstate, esz) * 4 == ck2.value
+        assert checkpoint_numel(batch, 4 * dim, length, dstate, esz, False) * 4 == ck2.value
 
 
 def test_selective_scan_contract_on_cpu():
