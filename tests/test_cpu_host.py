@@ -128,6 +128,26 @@ def test_checkpoint_numel_matches_library_size(shape, gated):
         assert checkpoint_numel(batch, 4 * dim, length, dstate, esz, False) * 4 == ck2.value
 
 
+@pytest.mark.parametrize("batch,dim,length,segmented", [
+    (16, 5120, 4096, False),   # config 2: 1280 CTAs fill the GPU, one pass per channel tile
+    (2, 5120, 4096, True),     # per-GPU work at 8 GPUs: the sequence is cut into segments
+    (1, 8, 2000, True),        # one channel tile over a long sequence
+    (1, 8, 100, False),        # too short to cut (fewer than 8 chunks)
+])
+def test_sequence_segment_planning(batch, dim, length, segmented):
+    """The host plans sequence segments (and asks for forward scratch for
+    them) only when the channel tiles leave most of the GPU idle.  Host-only:
+    without a device the library plans for 148 SMs."""
+    from metal_kernelops_b200 import _native as nat
+    lib = nat.lib()
+    p = nat.SelectiveScanParams()
+    p.batch, p.dim, p.length, p.groups, p.dstate = batch, dim, length, 1, 16
+    p.act_dtype = p.bc_dtype = nat.dtype_code(torch.bfloat16)
+    fw = nat._SZ()
+    assert lib.ssm_selective_scan_fwd_workspace(p, fw) == nat.SSM_OK
+    assert (fw.value > 0) == segmented
+
+
 def test_selective_scan_contract_on_cpu():
     import metal_kernelops_b200 as mk
     u = torch.zeros(1, 4, 8)
