@@ -112,7 +112,10 @@ typedef struct ssm_selective_scan_params {
     size_t workspace_bytes;
 } ssm_selective_scan_params;
 
-/* Sizes of the forward's checkpoint buffer and of the backward's workspace. */
+/* Sizes of the forward's checkpoint buffer and of the backward's workspace,
+ * for exactly these params: shapes, dtypes and flags (the checkpoint buffer
+ * holds the saved scan output only with SSM_HAS_Z), so query with the flags
+ * the forward will be called with. */
 int ssm_selective_scan_sizes(const ssm_selective_scan_params* p,
                              size_t* checkpoint_bytes, size_t* workspace_bytes);
 /* Workspace the forward needs (passed in `workspace`): zero unless the problem
