@@ -41,9 +41,9 @@ namespace sscan {
 
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
-constexpr int kChunk = 16;  // checkpoint interval == backward chunk
+constexpr int kChunk = 16;  // backward chunk (staged tile, walked in reverse)
 constexpr int kFT = 16;     // forward tile
-constexpr int kTS = 4;      // backward sub-block
+constexpr int kTS = 4;      // backward sub-block == interval of the saved states
 
 struct Args {
     int64_t batch, dim, length, groups, dstate, per_group;
