@@ -1045,7 +1045,7 @@ __global__ void reduce_kernel(const Args a, float* dB, float* dC, float* dA, flo
 }
 
 // ------------------------------------------------------------------- host ----
-struct Cfg { int npt, lpc; };
+struct Cfg { int npt = 4, lpc = 4; };   // launch shape; dstate > 64 is refused before use
 
 // States per thread and lanes per channel.  Fewer lanes per channel mean fewer
 // shuffles per step; more lanes mean more threads, which small batch*dim
