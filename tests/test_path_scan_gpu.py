@@ -24,6 +24,7 @@ def _mod():
 
 
 def _rel(got, want):
+    got, want = got.detach(), want.detach()
     den = float(want.norm())
     if den == 0.0:
         return 0.0 if float(got.norm()) == 0.0 else float("inf")
