@@ -138,15 +138,9 @@ def _scan_inputs(cfg, batch_lo, batch_hi, device):
 def _scan_inputs_rows(cfg, lo, hi):
     """Large configs: generate per batch row with a row-derived seed so every
     rank sees the same global tensor without materialising it whole."""
-    from metal_kernelops_b200.workloads import selective_scan_inputs
-    rows = [selective_scan_inputs(1, cfg["dim"], cfg["length"], cfg["dstate"], cfg["groups"],
-                                  seed=cfg["seed"] * 1000 + b, act_dtype=torch.bfloat16)
-            for b in range(lo, hi)]
-    out = {k: torch.cat([r[k] for r in rows]) for k in ("u", "delta", "z", "dout", "B", "C")}
-    base = selective_scan_inputs(1, cfg["dim"], 1, cfg["dstate"], cfg["groups"], seed=cfg["seed"])
-    for k in ("A", "D", "delta_bias"):
-        out[k] = base[k]
-    return out
+    from metal_kernelops_b200.workloads import selective_scan_rows
+    return selective_scan_rows(cfg["dim"], cfg["length"], cfg["dstate"], cfg["groups"], cfg["seed"],
+                               lo, hi, act_dtype=torch.bfloat16)
 
 
 def _config(args):
@@ -154,6 +148,20 @@ def _config(args):
     if args.shape:
         cfg["batch"], cfg["dim"], cfg["length"] = (int(v) for v in args.shape.split(","))
     return cfg
+
+
+def _scan_config(args, cfg, world):
+    """The workload description both arms print (so the driver sees one config)."""
+    per = batch_slice_len(cfg["batch"], world)
+    return {"workload": f"mamba1 selective scan fwd+bwd, BASELINE config {args.config}",
+            "global_batch": cfg["batch"], "batch_per_gpu": per, "dim": cfg["dim"],
+            "seq_len": cfg["length"], "dstate": cfg["dstate"], "groups": cfg["groups"],
+            "parallelism": f"dp{world} (batch shard)", "l2": "inputs > L2 (126 MB), no flush"}
+
+
+def batch_slice_len(batch, world):
+    """Rows of rank 0 (the largest shard) when ``batch`` is split over ``world``."""
+    return -(-batch // world)
 
 
 def _scan_alg_bytes(b, d, l, n, g, s_a=2):
@@ -335,10 +343,7 @@ def run_scan(args, world, rank, device):
         "vs_baseline": None,
         "dtype": "bf16 storage, fp32 compute",
         "data": "synthetic (seeded, BASELINE config distributions)",
-        "config": {"workload": f"mamba1 selective scan fwd+bwd, BASELINE config {args.config}",
-                   "global_batch": cfg["batch"], "batch_per_gpu": b, "dim": d, "seq_len": l,
-                   "dstate": n, "groups": g, "parallelism": f"dp{world} (batch shard)",
-                   "l2": "inputs > L2 (126 MB), no flush"},
+        "config": _scan_config(args, cfg, world),
         "breakdown_ms": {"fwd": fwd_ms, "bwd": bwd_ms, "allreduce": ar_ms},
         "roofline": {"bound": "hbm", "kernel": "selective_scan bwd (bwd_kernel + reduce)",
                      "achieved": bwd_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -396,31 +401,57 @@ def _timed(fn, steps, warmup, world, dist):
     return ms
 
 
-def run_ssd(args, world, rank, device):
+def run_ssd(args, world, rank, device, shape=None):
     """Mamba-2 SSD chunk scan fwd+bwd, B8 L8192 H80 P64 N128
-    G8 chunk 256, bf16 x/B/C, fp32 dt/A/D, dt_softplus; batch sharded."""
+    G8 chunk 256, bf16 x/B/C, fp32 dt/A/D, dt_softplus; batch sharded, with the
+    shared-parameter gradients (dA, dD, d dt_bias) summed over the ranks by one
+    all-reduce of a flat fp32 bucket inside every timed step."""
     import torch.distributed as dist
     import metal_kernelops_b200  # noqa: F401
-    from metal_kernelops_b200.parallel import batch_slice
+    from metal_kernelops_b200.parallel import ParamGradBucket, batch_slice
     from metal_kernelops_b200.workloads import ssd_inputs
     cfg = dict(SSD_CONFIG)
-    if args.shape:
-        cfg["batch"], cfg["length"] = (int(v) for v in args.shape.split(",")[:2])
+    if shape:
+        cfg["batch"], cfg["length"] = (int(v) for v in shape.split(",")[:2])
     rows = batch_slice(cfg["batch"], rank, world)
     host = ssd_inputs(cfg["batch"], cfg["length"], cfg["nheads"], cfg["headdim"], cfg["dstate"],
                       cfg["ngroups"], seed=cfg["seed"])
     for k in ("x", "dt", "B", "C", "dy"):
         host[k] = host[k][rows].contiguous()
     dev = {k: v.to(device) for k, v in host.items()}
+    del host
     ops = torch.ops.b200ssm
+    bucket = ParamGradBucket([dev["A"].shape, dev["D"].shape, dev["dt_bias"].shape], device)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    split = {"fwd": 0.0, "bwd": 0.0, "allreduce": 0.0, "n": 0}
 
-    def step():
+    def step(record=False):
+        if record:
+            ev[0].record()
         y, fin, saved = ops.chunk_scan_fwd(dev["x"], dev["dt"], dev["A"], dev["B"], dev["C"], dev["D"],
                                            None, dev["dt_bias"], None, cfg["chunk"], True, True)
-        ops.chunk_scan_bwd(dev["dy"], None, dev["x"], dev["dt"], dev["A"], dev["B"], dev["C"], dev["D"],
-                           None, dev["dt_bias"], None, saved, cfg["chunk"], True)
+        if record:
+            ev[1].record()
+        g = ops.chunk_scan_bwd(dev["dy"], None, dev["x"], dev["dt"], dev["A"], dev["B"], dev["C"], dev["D"],
+                               None, dev["dt_bias"], None, saved, cfg["chunk"], True)
+        if record:
+            ev[2].record()
+        if world > 1:
+            bucket.reduce([g[2], g[5], g[7]])
+        if record:
+            ev[3].record()
 
     ms = _timed(step, args.steps, args.warmup, world, dist)
+    # one more step with events between the phases (outside the timed region)
+    step(record=True)
+    torch.cuda.synchronize()
+    brk = {"fwd": ev[0].elapsed_time(ev[1]), "bwd": ev[1].elapsed_time(ev[2]),
+           "allreduce": ev[2].elapsed_time(ev[3])}
+    if world > 1:
+        t = torch.tensor([brk["fwd"], brk["bwd"], brk["allreduce"]], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        brk = dict(zip(("fwd", "bwd", "allreduce"), t.tolist()))
+    del dev, bucket
     if rank != 0:
         return None
     units = cfg["batch"] * cfg["length"] * cfg["nheads"] * cfg["headdim"]
@@ -440,12 +471,16 @@ def run_ssd(args, world, rank, device):
         "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16 storage, fp32 compute", "data": "synthetic (seeded, BASELINE config 3)",
         "config": {"workload": "mamba2 SSD chunk scan fwd+bwd, BASELINE config 3", **cfg,
-                   "parallelism": f"dp{world} (batch shard)"},
+                   "batch_per_gpu": b, "parallelism": f"dp{world} (batch shard)",
+                   "l2": "x 671 MB > L2, no flush"},
+        "breakdown_ms": brk,
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops"], "peak_source": kind,
                      "alg_flops_per_step": flops,
-                     "hbm_frac": alg_bytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], "traffic": None},
-        "gpu_launches": 8 * args.steps,
+                     "hbm_frac": alg_bytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                     "traffic": _traffic("ssd_step")},
+        # states, outputs (forward); dstates, grads, parameter reduce (backward)
+        "gpu_launches": 5 * args.steps,
     }
 
 
@@ -463,6 +498,7 @@ def run_decode(args, world, rank, device):
     for k in ("state", "x", "dt", "B", "C"):
         host[k] = host[k][rows].contiguous()
     dev = {k: v.to(device) for k, v in host.items()}
+    del host
     state = dev["state"]
 
     def step():
@@ -471,6 +507,7 @@ def run_decode(args, world, rank, device):
                                 dt_bias=dev["dt_bias"], dt_softplus=True, out_state=state)
 
     ms = _timed(step, args.steps, args.warmup, world, dist)
+    del dev, state
     if rank != 0:
         return None
     b = rows.stop - rows.start
@@ -485,10 +522,11 @@ def run_decode(args, world, rank, device):
         "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "fp32 state, bf16 x/B/C", "data": "synthetic (seeded, BASELINE config 4)",
         "config": {"workload": "mamba2 decode update, BASELINE config 4 (in place)", **cfg,
-                   "parallelism": f"dp{world} (batch shard)", "l2": "state 671 MB > L2"},
+                   "batch_per_gpu": b, "parallelism": f"dp{world} (batch shard)",
+                   "l2": "state 671 MB > L2, no flush"},
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": gbs / peaks["hbm_gbs"], "peak_source": kind,
-                     "alg_bytes_per_launch": alg_bytes, "traffic": None},
+                     "alg_bytes_per_launch": alg_bytes, "traffic": _traffic("decode_step")},
         "gpu_launches": args.steps,
     }
 
@@ -737,7 +775,7 @@ def cpu_baseline_scan(cfg, threads, budget_s=15.0):
     while True:
         leaves = [inp[k].clone().requires_grad_(True) for k in names]
         y = selective_scan_ref(*leaves[:5], D=leaves[5], z=leaves[6], delta_bias=leaves[7],
-                               delta_softplus=True)
+                               delta_softplus=True, stepping="index")
         torch.autograd.grad(y, leaves, inp["dout"])
         done += 1
         units += channels * cfg["length"]
@@ -746,8 +784,65 @@ def cpu_baseline_scan(cfg, threads, budget_s=15.0):
     el = time.perf_counter() - t_start
     return {"value": units / el, "unit": "elem/s", "cores": threads, "kind": "port",
             "sample": f"1 batch row x {channels} channels x {cfg['length']} steps "
-                      f"(dstate {cfg['dstate']}), fp32 fwd+bwd via autograd, {done} pass(es), "
-                      f"{el:.1f} s"}
+                      f"(dstate {cfg['dstate']}), the reference's per-step stepping, "
+                      f"fp32 fwd+bwd via autograd, {done} pass(es), {el:.1f} s",
+            "sample_fraction": channels / (cfg["batch"] * cfg["dim"])}
+
+
+def cpu_baseline_ssd(threads, budget_s=40.0):
+    """The reference's CPU path for the SSD chunk scan -- its torch composition
+    (``cv/mamba2_chunk.py:447-533, :652-678``, restated in the oracle), fp32,
+    forward + backward by autograd -- on one batch row of config 3 at the full
+    sequence length (rows are independent, so the rate is that of the whole
+    batch)."""
+    from metal_kernelops_b200.workloads import ssd_inputs
+    from oracle.ssm_oracle import mamba2_chunk_scan_composition
+    torch.set_num_threads(threads)
+    c = SSD_CONFIG
+    inp = ssd_inputs(1, c["length"], c["nheads"], c["headdim"], c["dstate"], c["ngroups"], seed=c["seed"],
+                     dtype=torch.float32)
+    names = ("x", "dt", "A", "B", "C", "D", "dt_bias")
+    done, t_start = 0, time.perf_counter()
+    while True:
+        lv = {k: inp[k].clone().requires_grad_(True) for k in names}
+        y, _ = mamba2_chunk_scan_composition(lv["x"], lv["dt"], lv["A"], lv["B"], lv["C"], c["chunk"],
+                                             D=lv["D"], dt_bias=lv["dt_bias"], dt_softplus=True)
+        torch.autograd.grad((y * inp["dy"]).sum(), list(lv.values()))
+        done += 1
+        if time.perf_counter() - t_start > budget_s / 2 or done >= 2:
+            break
+    el = time.perf_counter() - t_start
+    units = done * c["length"] * c["nheads"] * c["headdim"]
+    return {"value": units / el, "unit": "elem/s", "cores": threads, "kind": "port",
+            "sample": f"1 of {c['batch']} batch rows x {c['length']} steps (full sequence), "
+                      f"reference torch composition, fp32 fwd+bwd via autograd, {done} pass(es), {el:.1f} s",
+            "sample_fraction": 1.0 / c["batch"]}
+
+
+def cpu_baseline_decode(threads, steps=4):
+    """The reference's decode update on the CPU (``cv/mamba2_state.py:822-849``,
+    restated in the oracle), fp32, at the full config-4 shape, for a few
+    steps (the metric is a per-step rate)."""
+    from metal_kernelops_b200.workloads import decode_inputs
+    from oracle.ssm_oracle import mamba2_state_update_ref
+    torch.set_num_threads(threads)
+    c = DECODE_CONFIG
+    d = decode_inputs(c["batch"], c["nheads"], c["headdim"], c["dstate"], c["ngroups"], seed=c["seed"],
+                      dtype=torch.float32)
+    st = d["state"]
+    t_start = time.perf_counter()
+    for _ in range(steps):
+        _, st = mamba2_state_update_ref(st, d["x"], d["dt"], d["A"], d["B"], d["C"], D=d["D"],
+                                        dt_bias=d["dt_bias"], dt_softplus=True)
+    el = time.perf_counter() - t_start
+    units = steps * c["batch"] * c["nheads"] * c["headdim"] * c["dstate"]
+    return {"value": units / el, "unit": "elem/s", "cores": threads, "kind": "port",
+            "sample": f"{steps} decode steps at the full config-4 shape, fp32, {el:.1f} s",
+            "sample_fraction": steps / 1024}
+
+
+SUB_KEYS = ("metric", "value", "unit", "ms_per_step", "dtype", "config", "breakdown_ms", "roofline",
+            "gpu_launches", "cpu_baseline")
 
 
 def main():
@@ -761,6 +856,8 @@ def main():
     ap.add_argument("--shape", default=None,
                     help="batch,dim,seqlen override of the config (profiling runs on small cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra-ops", action="store_true",
+                    help="scan line only (no ssd / decode sub-objects)")
     args = ap.parse_args()
     world, rank, local = _dist()
     threads = len(os.sched_getaffinity(0))
@@ -780,9 +877,11 @@ def main():
             "unit": "elem/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": units / v * 1e3, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-            "config": {"workload": f"mamba1 selective scan fwd+bwd, BASELINE config {args.config}",
-                       "global_batch": cfg["batch"], "dim": cfg["dim"], "seq_len": cfg["length"],
-                       "dstate": cfg["dstate"], "parallelism": "host CPU"},
+            "config": _scan_config(args, cfg, args.gpus),
+            "host": f"{threads} host CPU threads (the reference has no CUDA path)",
+            # each step times a sample of the workload; the step time is the
+            # sample's rate applied to the whole configuration
+            "extrapolated_from_fraction": timed[0]["sample_fraction"],
             "cpu_baseline": {**timed[0], "value": v},
             "e2e": {"value": v, "unit": "elem/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }
@@ -796,16 +895,40 @@ def main():
     else:
         torch.cuda.set_device(0)
     device = torch.device("cuda", torch.cuda.current_device())
+    want_cpu = world == 1 and not args.no_cpu_baseline
 
     if args.op == "scan":
         line = run_scan(args, world, rank, device)
-    else:
-        line = {"ssd": run_ssd, "decode": run_decode, "ss2d": run_ss2d,
-                "conv1d": run_conv1d, "gnorm": run_gnorm, "block": run_block}[args.op](args, world, rank,
-                                                                                        device)
-    if rank == 0 and line is not None:
-        if world == 1 and not args.no_cpu_baseline and args.op == "scan":
+        if rank == 0 and want_cpu:
             line["cpu_baseline"] = cpu_baseline_scan(CONFIGS[args.config], threads)
+        if not args.no_extra_ops and not args.shape:
+            # the other two hot-path kernel groups at their BASELINE configs,
+            # same N, same timing rules (every rank takes part in both)
+            torch.cuda.empty_cache()
+            for name, fn, base in (("ssd", run_ssd, cpu_baseline_ssd), ("decode", run_decode, cpu_baseline_decode)):
+                sub = fn(args, world, rank, device)
+                torch.cuda.empty_cache()
+                if rank == 0:
+                    if want_cpu:
+                        sub["cpu_baseline"] = base(threads)
+                    line[name] = {k: sub[k] for k in SUB_KEYS if k in sub}
+                    line["gpu_launches"] += sub["gpu_launches"]
+    elif args.op == "ssd":
+        line = run_ssd(args, world, rank, device, shape=args.shape)
+        if rank == 0 and want_cpu:
+            line["cpu_baseline"] = cpu_baseline_ssd(threads)
+    elif args.op == "decode":
+        line = run_decode(args, world, rank, device)
+        if rank == 0 and want_cpu:
+            line["cpu_baseline"] = cpu_baseline_decode(threads)
+    else:
+        line = {"ss2d": run_ss2d, "conv1d": run_conv1d, "gnorm": run_gnorm,
+                "block": run_block}[args.op](args, world, rank, device)
+    # no kernel gave up on a bounded wait during any of the timed work (the
+    # ops' status words; raises if one did, so no number is printed)
+    import metal_kernelops_b200 as mk
+    mk.check_errors()
+    if rank == 0 and line is not None:
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

@@ -110,6 +110,10 @@ typedef struct ssm_selective_scan_params {
      * ssm_selective_scan_fwd_workspace) */
     void* workspace;
     size_t workspace_bytes;
+    /* optional device word (NULL: none), the same slot every op's params
+     * carry; this op's kernels have no waits that can give up and never
+     * write it. */
+    int32_t* status;
 } ssm_selective_scan_params;
 
 /* Sizes of the forward's checkpoint buffer and of the backward's workspace,
@@ -181,6 +185,10 @@ typedef struct ssm_state_update_params {
      * against an fp32 state, read without a widening copy; state, dt and y
      * stay in `dtype`. */
     int32_t io_dtype;
+    /* optional device word (NULL: none), the same slot every op's params
+     * carry; this op's kernels have no waits that can give up and never
+     * write it. */
+    int32_t* status;
 } ssm_state_update_params;
 
 int ssm_state_update_sizes(const ssm_state_update_params* p, size_t* workspace_bytes);
@@ -259,6 +267,11 @@ typedef struct ssm_chunk_scan_params {
      * wider (batch, length, columns) buffer.  Tensor-core path only (16-byte
      * multiples); the CUDA-core path returns SSM_ERR_UNSUPPORTED for them. */
     int64_t x_token_stride, bc_token_stride;
+    /* optional device word (NULL: none).  A kernel of this op that gives up
+     * on a bounded wait writes its non-zero code here (the first failure
+     * wins; the word is never cleared by the library), besides the per-device
+     * flag that ssm_take_kernel_error reads.  Start it at 0. */
+    int32_t* status;
 } ssm_chunk_scan_params;
 
 int ssm_chunk_scan_sizes(const ssm_chunk_scan_params* p, size_t* saved_bytes,
@@ -306,6 +319,10 @@ typedef struct ssm_ss2d_scan_params {
     float* dC;
     void* workspace;
     size_t workspace_bytes;
+    /* optional device word (NULL: none), the same slot every op's params
+     * carry; this op's kernels have no waits that can give up and never
+     * write it. */
+    int32_t* status;
 } ssm_ss2d_scan_params;
 
 int ssm_ss2d_scan_sizes(const ssm_ss2d_scan_params* p, size_t* checkpoint_bytes,
@@ -359,6 +376,11 @@ typedef struct ssm_causal_conv1d_params {
      * aligned, channels a multiple of 8 bytes' worth of elements; no initial
      * or final state. */
     int64_t x_row_stride, dout_row_stride;
+    /* optional device word (NULL: none).  A kernel of this op that gives up
+     * on a bounded wait writes its non-zero code here (the first failure
+     * wins; the word is never cleared by the library), besides the per-device
+     * flag that ssm_take_kernel_error reads.  Start it at 0. */
+    int32_t* status;
 } ssm_causal_conv1d_params;
 
 int ssm_causal_conv1d_sizes(const ssm_causal_conv1d_params* p, size_t* workspace_bytes);
@@ -381,6 +403,10 @@ typedef struct ssm_causal_conv1d_update_params {
     const float* weight;
     const float* bias;
     void* out;
+    /* optional device word (NULL: none), the same slot every op's params
+     * carry; this op's kernels have no waits that can give up and never
+     * write it. */
+    int32_t* status;
 } ssm_causal_conv1d_update_params;
 
 int ssm_causal_conv1d_update(const ssm_causal_conv1d_update_params* p, void* stream);
@@ -425,6 +451,10 @@ typedef struct ssm_gated_rmsnorm_params {
      * x) be column slices of a wider projection output.  out, dy, dx and dz
      * are contiguous. */
     int64_t x_row_stride, z_row_stride;
+    /* optional device word (NULL: none), the same slot every op's params
+     * carry; this op's kernels have no waits that can give up and never
+     * write it. */
+    int32_t* status;
 } ssm_gated_rmsnorm_params;
 
 int ssm_gated_rmsnorm_sizes(const ssm_gated_rmsnorm_params* p, size_t* workspace_bytes);
@@ -432,10 +462,20 @@ int ssm_gated_rmsnorm_fwd(const ssm_gated_rmsnorm_params* p, void* stream);
 int ssm_gated_rmsnorm_bwd(const ssm_gated_rmsnorm_params* p, void* stream);
 
 /* Kernels that wait on an mbarrier give up after a bounded number of polls,
- * record a non-zero code in a per-device flag and return.  This reads the flag
- * of the current device (synchronising with it) and clears it; 0 means no
- * kernel gave up.  Reference: none (the Metal kernels have no such waits). */
+ * record a non-zero code in a per-device flag (and in the call's `status`
+ * word, when given) and return.  This reads the flag of the current device
+ * (synchronising with it) and clears it; 0 means no kernel gave up.
+ * Reference: none (the Metal kernels have no such waits). */
 int ssm_take_kernel_error(void);
+
+/* Self-test of the failure path: one CTA waits, with the library's bounded
+ * wait limited to `polls` polls, on a shared-memory mbarrier that nothing
+ * arrives at (no copy is in flight), gives up, writes SSM_KERR_SELFTEST into
+ * *status and returns.  The per-device flag is left alone.  Lets a caller (and
+ * the tests) check that a wait which runs out surfaces as a status instead of
+ * a hang, and that the context stays usable.  Reference: none. */
+#define SSM_KERR_SELFTEST 99
+int ssm_selftest_bounded_wait(int32_t* status, uint32_t polls, void* stream);
 
 #ifdef __cplusplus
 }

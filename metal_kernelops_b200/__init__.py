@@ -21,7 +21,8 @@ path: CPU tensors raise ``ValueError``.
 
 from .scan import CHUNK, scan_cuda, selective_scan, selective_scan_fn
 from . import cv  # noqa: F401  (registers the Mamba-2 ops)
+from ._native import check_errors
 
-__all__ = ["CHUNK", "cv", "scan_cuda", "selective_scan", "selective_scan_fn"]
+__all__ = ["CHUNK", "check_errors", "cv", "scan_cuda", "selective_scan", "selective_scan_fn"]
 
 __version__ = "0.1.0"

@@ -40,7 +40,7 @@ EXPORTS = (
     "ssm_state_update_sizes", "ssm_state_update_fwd", "ssm_state_update_bwd",
     "ssm_state_update_bwd_noalloc",
     "ssm_chunk_scan_sizes", "ssm_chunk_scan_fwd", "ssm_chunk_scan_bwd",
-    "ssm_take_kernel_error",
+    "ssm_take_kernel_error", "ssm_selftest_bounded_wait",
     "ssm_ss2d_scan_sizes", "ssm_ss2d_scan_fwd", "ssm_ss2d_scan_bwd",
     "ssm_causal_conv1d_sizes", "ssm_causal_conv1d_fwd", "ssm_causal_conv1d_bwd",
     "ssm_causal_conv1d_update",
@@ -60,6 +60,7 @@ class SelectiveScanParams(ctypes.Structure):
         ("dout", _P), ("du", _P), ("ddelta", _P), ("dz", _P),
         ("dA", _P), ("dB", _P), ("dC", _P), ("dD", _P), ("ddelta_bias", _P),
         ("workspace", _P), ("workspace_bytes", _SZ),
+        ("status", _P),
     ]
 
 
@@ -75,6 +76,7 @@ class StateUpdateParams(ctypes.Structure):
         ("dD", _P), ("dz", _P), ("ddt_bias", _P),
         ("workspace", _P), ("workspace_bytes", _SZ),
         ("io_dtype", _I32),
+        ("status", _P),
     ]
 
 
@@ -91,6 +93,7 @@ class ChunkScanParams(ctypes.Structure):
         ("ddt_bias", _P), ("dinitial", _P),
         ("saved", _P), ("workspace", _P), ("workspace_bytes", _SZ),
         ("x_token_stride", _I64), ("bc_token_stride", _I64),
+        ("status", _P),
     ]
 
 
@@ -103,6 +106,7 @@ class Ss2dScanParams(ctypes.Structure):
         ("y", _P), ("checkpoints", _P),
         ("dout", _P), ("du", _P), ("ddt", _P), ("dA", _P), ("dB", _P), ("dC", _P),
         ("workspace", _P), ("workspace_bytes", _SZ),
+        ("status", _P),
     ]
 
 
@@ -115,6 +119,7 @@ class CausalConv1dParams(ctypes.Structure):
         ("dout", _P), ("dx", _P), ("dweight", _P), ("dbias", _P), ("dinitial", _P),
         ("workspace", _P), ("workspace_bytes", _SZ),
         ("x_row_stride", _I64), ("dout_row_stride", _I64),
+        ("status", _P),
     ]
 
 
@@ -124,6 +129,7 @@ class CausalConv1dUpdateParams(ctypes.Structure):
         ("state_stride_batch", _I64), ("state_stride_channel", _I64),
         ("dtype", _I32), ("flags", _U32),
         ("state", _P), ("x", _P), ("weight", _P), ("bias", _P), ("out", _P),
+        ("status", _P),
     ]
 
 
@@ -135,6 +141,7 @@ class GatedRmsNormParams(ctypes.Structure):
         ("dy", _P), ("dx", _P), ("dz", _P), ("dweight", _P), ("dbias", _P),
         ("workspace", _P), ("workspace_bytes", _SZ),
         ("x_row_stride", _I64), ("z_row_stride", _I64),
+        ("status", _P),
     ]
 
 
@@ -192,6 +199,8 @@ def lib():
                 getattr(handle, name).restype = ctypes.c_int
             handle.ssm_take_kernel_error.restype = ctypes.c_int
             handle.ssm_take_kernel_error.argtypes = []
+            handle.ssm_selftest_bounded_wait.restype = ctypes.c_int
+            handle.ssm_selftest_bounded_wait.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]
             _lib = handle
     return _lib
 
@@ -225,3 +234,58 @@ def ptr(t):
 
 def stream_of(t: torch.Tensor) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+# --------------------------------------------------------------- status words --
+# One int32 device word per op family and device, zero-initialised once from
+# the caching allocator and handed to every call of that op (params.status).
+# A kernel that gives up on a bounded wait writes its code there; nothing is
+# cleared until ``check_errors`` reads the words.  Reading is lazy -- one small
+# device-to-host copy when the caller asks -- so the ops never synchronise.
+STATUS_SLOTS = ("selective_scan", "state_update", "chunk_scan", "ss2d_scan", "causal_conv1d",
+                "causal_conv1d_update", "gated_rmsnorm", "selftest")
+_status = {}
+
+
+def _status_buffer(device: torch.device) -> torch.Tensor:
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _status.get(key)
+    if buf is None:
+        buf = torch.zeros(len(STATUS_SLOTS), dtype=torch.int32, device=torch.device("cuda", key))
+        _status[key] = buf
+    return buf
+
+
+def status_word(device: torch.device, op: str) -> int:
+    """Device address of ``op``'s status word on ``device`` (for params.status)."""
+    buf = _status_buffer(device)
+    return buf.data_ptr() + 4 * STATUS_SLOTS.index(op)
+
+
+def check_errors(device=None) -> None:
+    """Read the status words of ``device`` (every device used so far when
+    None), clear them, and raise ``RuntimeError`` if a kernel gave up on a
+    bounded wait since the last check.  Synchronises with those devices."""
+    keys = list(_status) if device is None else [torch.device(device).index or 0]
+    failed = []
+    for key in keys:
+        buf = _status.get(key)
+        if buf is None:
+            continue
+        vals = buf.cpu().tolist()
+        if any(vals):
+            buf.zero_()
+            failed += [f"{op} (code {v}) on cuda:{key}" for op, v in zip(STATUS_SLOTS, vals) if v]
+    if failed:
+        raise NativeError("a kernel gave up on a bounded wait; its outputs are invalid: " + ", ".join(failed))
+
+
+def selftest_bounded_wait(device=None, polls: int = 16) -> None:
+    """Launch the library's failure-path self-test on ``device``: a wait on an
+    mbarrier that nothing completes, limited to ``polls`` polls, which gives
+    up and writes its code into the self-test status word."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        check(lib().ssm_selftest_bounded_wait(ctypes.c_void_p(status_word(dev, "selftest")),
+                                              ctypes.c_uint32(polls), stream), "selftest_bounded_wait")

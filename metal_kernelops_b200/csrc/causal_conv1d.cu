@@ -41,6 +41,7 @@ struct Args {
     void* out; void* final_state;
     const void* dout; void* dx; void* dinit;
     float* partial;                           // (rows, nchunks, slots, K + 1)
+    int* status;                              // the call's optional status word
 };
 
 constexpr uint32_t kHasBias = SSM_HAS_BIAS, kSilu = SSM_CONV_SILU, kHasInit = SSM_HAS_INIT;
@@ -297,6 +298,13 @@ constexpr int kWarps = kThreads / 32;
 
 __device__ int g_conv_error;
 
+// A bounded wait ran out: record the code in the device's flag and in the
+// call's status word; the first failure wins.
+__device__ __forceinline__ void report(const Args& a, int code) {
+    atomicCAS(&g_conv_error, 0, code);
+    if (a.status) atomicCAS(a.status, 0, code);
+}
+
 template <typename T, int NT>
 struct BulkLayout {
     static constexpr int SPAN = kHalo + kTile + kHalo;             // elements per stage and tensor
@@ -526,7 +534,7 @@ fwd_bulk_kernel(const Args a) {
         RowStart<T, TAPS> rs;
         rs.load(a, row, t0);
         if (!ring.wait(st, use)) {
-            if ((tid & 31) == 0) atomicCAS(&g_conv_error, 0, 61);
+            if ((tid & 31) == 0) report(a, 61);
             break;
         }
         const T* xs = reinterpret_cast<const T*>(smem + st * Lay::stage_bytes) + kHalo;
@@ -635,7 +643,7 @@ bwd_bulk_kernel(const Args a) {
         RowStart<T, TAPS> rs;
         rs.load(a, row, t0);
         if (!ring.wait(st, use)) {
-            if (lane == 0) atomicCAS(&g_conv_error, 0, 62);
+            if (lane == 0) report(a, 62);
             ok = false;
             break;
         }
@@ -1102,6 +1110,7 @@ static void plan(const ssm_causal_conv1d_params* p, bool bulk, Args& a) {
     a.dout = p->dout; a.dx = p->dx; a.dinit = p->dinitial;
     a.partial = nullptr;
     a.per = 0;
+    a.status = p->status;
 }
 
 // Persistent grid: resident CTAs of the kernel on every SM, at most one per

@@ -82,6 +82,7 @@ struct Args {
     float* dcs_inter;      // (b, h, nc * Q)
     float* dT;             // (b, h, nc)
     float* dA_part; float* db_part; float* dD_part;   // (b, h, nc) [x headdim]
+    int* status;           // the call's optional status word (params.status)
     // TMA descriptors of x, dy (X-like rows) and B, C (B-like rows); see encode_rows()
     alignas(64) CUtensorMap tm_x;
     alignas(64) CUtensorMap tm_dy;
@@ -136,7 +137,13 @@ __device__ __forceinline__ float ld_dt(const Args& a, int64_t i) {
     }
 }
 
-__device__ __forceinline__ void report(int code) { atomicCAS(&g_kernel_error, 0, code); }
+// A bounded wait ran out (or a copy could not be issued): record the code in
+// the device's flag and in the call's status word; the first failure wins.
+__device__ __forceinline__ void report(int* status, int code) {
+    atomicCAS(&g_kernel_error, 0, code);
+    if (status) atomicCAS(status, 0, code);
+}
+__device__ __forceinline__ void report(const Args& a, int code) { report(a.status, code); }
 
 // ------------------------------------------------------------ block helpers --
 // Barrier over the whole CTA (NB = 0) or over the first NB threads only (named
@@ -215,9 +222,9 @@ __device__ __forceinline__ unsigned char* aligned_smem(unsigned char* raw) {
 // issues; the bytes (Q * W * 16) complete on `mbar`.
 template <int W>
 __device__ __forceinline__ void tma_rows(unsigned char* tile, const CUtensorMap& map, int64_t c, int64_t b,
-                                         int64_t hg, uint32_t mbar) {
+                                         int64_t hg, uint32_t mbar, int* status) {
     if (reinterpret_cast<uintptr_t>(&map) & 63u) {   // descriptors must be 64-byte aligned: never issue
-        report(98);
+        report(status, 98);
         return;
     }
     const uint32_t st = tc::smem_u32(tile);
@@ -305,8 +312,8 @@ __global__ void __launch_bounds__(kThreads) states_kernel(const __grid_constant_
     auto load_chunk = [&](int64_t c, int buf) {   // one thread
         const uint32_t lb = tc::smem_u32(&lbar[buf]);
         tc::mbar_expect_tx(lb, kRowsB + kRowsX);
-        tma_rows<WB>(sB0 + buf * kTileB, a.tm_B, c, b, g, lb);
-        tma_rows<WX>(sX0 + buf * kTileX, a.tm_x, c, b, h, lb);
+        tma_rows<WB>(sB0 + buf * kTileB, a.tm_B, c, b, g, lb, a.status);
+        tma_rows<WX>(sX0 + buf * kTileX, a.tm_x, c, b, h, lb, a.status);
         lpend[buf] = (uint32_t)((c >> 1) & 1);
     };
 
@@ -349,14 +356,14 @@ __global__ void __launch_bounds__(kThreads) states_kernel(const __grid_constant_
         const Steps st = steps_of(a, raw, c, Ah, s_scan);
         if (tid == Q - 1) s_T = st.cs;
         if (c > 0) {   // the previous chunk's GEMM read sXW and the other buffers
-            if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(11); ok = false; }
+            if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(a, 11); ok = false; }
             phase ^= 1;
             tc::fence_after();
         }
         ok = __syncthreads_and(ok);
         if (!ok) break;
         if (tid == 0 && c + 1 < a.nc) load_chunk(c + 1, buf ^ 1);   // a whole chunk ahead of its use
-        if (!tc::mbar_wait(tc::smem_u32(&lbar[buf]), (uint32_t)((c >> 1) & 1))) { report(13); ok = false; }
+        if (!tc::mbar_wait(tc::smem_u32(&lbar[buf]), (uint32_t)((c >> 1) & 1))) { report(a, 13); ok = false; }
         else if (tid == 0) lpend[buf] = ~0u;
         ok = __syncthreads_and(ok);
         if (!ok) break;
@@ -405,7 +412,7 @@ __global__ void __launch_bounds__(kThreads) states_kernel(const __grid_constant_
         }
     }
     if (ok) {
-        if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(12); ok = false; }
+        if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(a, 12); ok = false; }
         tc::fence_after();
     }
     ok = __syncthreads_and(ok);
@@ -486,13 +493,13 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
         tc::mbar_init(lb, 1);
         tc::fence_mbar_init();
         tc::mbar_expect_tx(lb, 2 * kRowsB);
-        tma_rows<WB>(sC, a.tm_C, c, b, g, lb);
-        tma_rows<WB>(sM, a.tm_B, c, b, g, lb);
+        tma_rows<WB>(sC, a.tm_C, c, b, g, lb, a.status);
+        tma_rows<WB>(sM, a.tm_B, c, b, g, lb, a.status);
         lpend = 0;
     }
     __syncthreads();                          // the barriers are initialised before anyone waits
     bool lok = tc::mbar_wait(lb, 0);
-    if (!lok) report(23);
+    if (!lok) report(a, 23);
     else if (tid == 0) lpend = ~0u;
     tc::fence_before();
     lok = __syncthreads_and(lok);
@@ -509,7 +516,7 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
     }
     uint32_t phase = 0;
     bool ok = lok && tc::mbar_wait(tc::smem_u32(&mbar), phase);
-    if (lok && !ok) report(21);
+    if (lok && !ok) report(a, 21);
     phase ^= 1;
     tc::fence_after();
     ok = __syncthreads_and(ok);
@@ -521,7 +528,7 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
         if (tid == 0) {   // the previous head's GEMMs and epilogue are done with sX and sH
             lpend = lpar;
             tc::mbar_expect_tx(lb, kRowsX + kTileH);
-            tma_rows<WX>(sX, a.tm_x, c, b, h, lb);
+            tma_rows<WX>(sX, a.tm_x, c, b, h, lb, a.status);
             tc::bulk_load(tc::smem_u32(sH), a.Ht + ((size_t)(b * H + h) * a.nc + c) * kTileH, kTileH, lb);
         }
         const int hk = (int)(hh % kHeadsSh);
@@ -572,7 +579,7 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
             }
         }
         const bool lw = tc::mbar_wait(lb, lpar);      // this head's x and H_c
-        if (!lw) report(24);
+        if (!lw) report(a, 24);
         else if (tid == 0) lpend = ~0u;
         tc::fence_async_smem();
         tc::fence_before();
@@ -595,7 +602,7 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
 #pragma unroll
             for (int q = 0; q < P / 8; ++q) zr[q] = *reinterpret_cast<const uint4*>(zg + row + 8 * q);
         }
-        if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(22); ok = false; }
+        if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(a, 22); ok = false; }
         phase ^= 1;
         tc::fence_after();
         ok = __syncthreads_and(ok);
@@ -711,9 +718,9 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const __grid_constant
         const uint32_t lpar = (uint32_t)((a.nc - 1 - c) & 1);
         if (tid == 0) {   // the previous chunk's GEMMs and passes are done with these tiles
             tc::mbar_expect_tx(lb, kRowsB + kTileH + kRowsX);
-            tma_rows<WB>(sC, a.tm_C, c, b, g, lb);
+            tma_rows<WB>(sC, a.tm_C, c, b, g, lb, a.status);
             tc::bulk_load(tc::smem_u32(sH), Hin + (size_t)c * kTileH, kTileH, lb);
-            tma_rows<WX>(sY, a.tm_dy, c, b, h, lb);
+            tma_rows<WX>(sY, a.tm_dy, c, b, h, lb, a.status);
             lpend = lpar;
         }
         const Steps st = steps_of(a, raw, c, Ah, s_scan);
@@ -729,7 +736,7 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const __grid_constant
             }
         }
         const bool lw = tc::mbar_wait(lb, lpar);
-        if (!lw) report(32);
+        if (!lw) report(a, 32);
         else if (tid == 0) lpend = ~0u;
         if (!__syncthreads_and(lw)) { ok = false; break; }
         const float Tc = s_T;
@@ -801,7 +808,7 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const __grid_constant
         }
         const float dTc = block_sum(dt_part, s_scan);
         if (tid == 0) a.dT[(b * H + h) * a.nc + c] = exp2_mufu(Tc * kLog2e) * dTc;
-        if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(31); ok = false; }
+        if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(a, 31); ok = false; }
         phase ^= 1;
         tc::fence_after();
         ok = __syncthreads_and(ok);
@@ -931,8 +938,8 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
         const int64_t h = g * a.hpg + hh;
         const int64_t bhc = (b * H + h) * a.nc + c;
         tc::mbar_expect_tx(bar(kLh), 2 * kRowsX + 2 * kTileH);
-        tma_rows<WX>(sX, a.tm_x, c, b, h, bar(kLh));
-        tma_rows<WX>(sY, a.tm_dy, c, b, h, bar(kLh));
+        tma_rows<WX>(sX, a.tm_x, c, b, h, bar(kLh), a.status);
+        tma_rows<WX>(sY, a.tm_dy, c, b, h, bar(kLh), a.status);
         tc::bulk_load(tc::smem_u32(sH), a.Ht + ((size_t)(b * H + h) * a.nc + c) * kTileH, kTileH, bar(kLh));
         tc::bulk_load(tc::smem_u32(sD), a.dHt + (size_t)bhc * kTileH, kTileH, bar(kLh));
         lpend = (uint32_t)(hh & 1);
@@ -948,8 +955,8 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
         tc::mbar_init(bar(kLh), 1);
         tc::fence_mbar_init();
         tc::mbar_expect_tx(bar(kBc), 2 * kRowsB);      // the MMA warp waits for these directly
-        tma_rows<WB>(sC, a.tm_C, c, b, g, bar(kBc));
-        tma_rows<WB>(sB, a.tm_B, c, b, g, bar(kBc));
+        tma_rows<WB>(sC, a.tm_C, c, b, g, bar(kBc), a.status);
+        tma_rows<WB>(sB, a.tm_B, c, b, g, bar(kBc), a.status);
         load_head(0);
     }
     tc::fence_before();
@@ -1024,7 +1031,7 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
             }
             __syncwarp();
         }
-        if (!ok && lane == 0) report(44);
+        if (!ok && lane == 0) report(a, 44);
     } else {
         // --------------------------------------------------- compute warps --
         const bool pos_thread = tid < Q;           // owns chunk position s = tid
@@ -1046,7 +1053,7 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
             const int64_t xrow = (b * L + t0 + r) * a.xts + h * P;  // row r of x
             {
                 const bool lw = tc::mbar_wait(bar(kLh), par);   // this head's tiles
-                if (!lw) report(45);
+                if (!lw) report(a, 45);
                 else if (tid == 0) lpend = ~0u;
                 ok = cg_all<kGC>(lw);
                 if (!ok) break;
@@ -1089,7 +1096,7 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
                 }
                 a.dD_part[bhc * P + p] = s2;
             }
-            if (!tc::mbar_wait(bar(kM1), par)) { report(42); ok = false; }
+            if (!tc::mbar_wait(bar(kM1), par)) { report(a, 42); ok = false; }
             tc::fence_after();
             ok = cg_all<kGC>(ok);                    // also: every thread is done reading sX
             if (!ok) break;
@@ -1187,7 +1194,7 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
                 st_next = staged_steps<kGC>(a, sh.hs, hk1, c, sh.scan);
                 if (tid == Q - 1) sh.T[(hh + 1) & 1] = st_next.cs;
             }
-            if (!tc::mbar_wait(bar(kM2), par)) { report(43); ok = false; }
+            if (!tc::mbar_wait(bar(kM2), par)) { report(a, 43); ok = false; }
             tc::fence_after();
             ok = cg_all<kGC>(ok);
             if (!ok) break;
@@ -1360,6 +1367,7 @@ static void make_args(const ssm_chunk_scan_params* p, Args& a) {
     a.x = p->x; a.dt = p->dt; a.A = p->A; a.B = p->B; a.C = p->C; a.D = p->D; a.z = p->z;
     a.dt_bias = p->dt_bias; a.init = p->initial_states;
     a.y = p->y; a.final_state = p->final_state;
+    a.status = p->status;
     const Saved s = saved_layout(p);
     unsigned char* sv = reinterpret_cast<unsigned char*>(p->saved);
     a.Ht = sv;
@@ -1485,7 +1493,32 @@ int bwd(const ssm_chunk_scan_params* p, cudaStream_t s) {
 }  // namespace ssdtc
 }  // namespace ssm
 
+namespace ssm {
+namespace ssdtc {
+// The failure path of every bounded wait, exercised on purpose: one thread
+// initialises an mbarrier that expects one arrival, nothing ever arrives and
+// no copy is in flight, so tc::mbar_wait (the helper every pipeline here uses)
+// runs out after `polls` polls; the kernel then records the code in the
+// caller's status word and returns.
+__global__ void selftest_wait_kernel(int* status, uint32_t polls) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    const uint32_t mb = tc::smem_u32(&bar);
+    tc::mbar_init(mb, 1);
+    if (!tc::mbar_wait(mb, 0, polls)) atomicCAS(status, 0, SSM_KERR_SELFTEST);
+}
+}  // namespace ssdtc
+}  // namespace ssm
+
 int ssm_conv_take_error();   // causal_conv1d.cu: the conv1d kernels' flag
+
+extern "C" int ssm_selftest_bounded_wait(int32_t* status, uint32_t polls, void* stream) {
+    if (!status) return ssm::fail(SSM_ERR_INVALID, "selftest_bounded_wait: null status word");
+    if (polls == 0 || polls > (1u << 20))
+        return ssm::fail(SSM_ERR_INVALID, "selftest_bounded_wait: polls must be in 1..2^20");
+    ssm::ssdtc::selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(status, polls);
+    return ssm::check_launch("selftest_bounded_wait");
+}
 
 extern "C" int ssm_take_kernel_error(void) {
     int v = 0;

@@ -21,6 +21,9 @@
 #include <mutex>
 #include <string>
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 
 namespace ssm {
@@ -544,9 +547,12 @@ extern "C" int ssm_state_update_bwd(const ssm_state_update_params* p, void* stre
 //
 // Only host code needs the array's device address.  In host code the symbol
 // `g_static_scratch` names a host-side stand-in, not device memory, so its
-// address is looked up with cudaGetSymbolAddress once per device (with that
-// device current) on the first call made on that device, and cached.  That
-// first call should therefore happen before any stream capture.
+// address is looked up with cudaGetSymbolAddress in the context current on the
+// calling thread, on the first call made in that context, and cached under the
+// context's unique id (cuCtxGetId: never reused within the process).  A new
+// context -- after cudaDeviceReset, or a different context made current through
+// the driver API -- therefore gets its own lookup instead of a stale address.
+// The first call in a context should happen before any stream capture.
 //
 // All calls on a device share the one array, and it keeps whatever the last
 // call left in it.  The backward writes every scratch element it later reads
@@ -559,25 +565,63 @@ namespace supd {
 constexpr size_t kStaticScratchBytes = SSM_STATE_UPDATE_STATIC_SCRATCH_BYTES;
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
+// (context id, device address of g_static_scratch in it); a fixed table, so
+// the lookup allocates nothing either; when full, the oldest entry is replaced
+constexpr int kCtxSlots = 64;
+struct CtxAddr { unsigned long long id; void* addr; };
 static std::mutex g_static_mu;
-static void* g_static_addr[256];   // device address of g_static_scratch, per device ordinal
+static CtxAddr g_static_addr[kCtxSlots];
+static int g_static_used = 0, g_static_next = 0;
+
+static PFN_cuCtxGetCurrent_v4000 g_ctx_current = nullptr;
+static PFN_cuCtxGetId_v12000 g_ctx_id = nullptr;
+
+// The unique id of the context current on this thread (0 when none is).
+static int current_context_id(unsigned long long* id) {
+    if (!g_ctx_current || !g_ctx_id) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !f)
+            return fail(SSM_ERR_CUDA, "state_update bwd_noalloc: cuCtxGetCurrent unavailable");
+        g_ctx_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(f);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !f)
+            return fail(SSM_ERR_CUDA, "state_update bwd_noalloc: cuCtxGetId unavailable");
+        g_ctx_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(f);
+    }
+    CUcontext ctx = nullptr;
+    if (g_ctx_current(&ctx) != CUDA_SUCCESS)
+        return fail(SSM_ERR_CUDA, "state_update bwd_noalloc: cuCtxGetCurrent failed");
+    *id = 0;
+    if (ctx && g_ctx_id(ctx, id) != CUDA_SUCCESS)
+        return fail(SSM_ERR_CUDA, "state_update bwd_noalloc: cuCtxGetId failed");
+    return SSM_OK;
+}
 
 static int static_scratch(void** out) {
-    int dev = -1;
-    const cudaError_t ge = cudaGetDevice(&dev);
-    if (ge != cudaSuccess)
-        return fail(SSM_ERR_CUDA, std::string("state_update bwd_noalloc: cudaGetDevice: ") + cudaGetErrorString(ge));
-    if (dev < 0 || dev >= 256) return fail(SSM_ERR_UNSUPPORTED, "state_update bwd_noalloc: device ordinal above 255");
     std::lock_guard<std::mutex> lock(g_static_mu);
-    if (g_static_addr[dev] == nullptr) {
-        void* addr = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&addr, g_static_scratch);
-        if (e != cudaSuccess || addr == nullptr)
-            return fail(SSM_ERR_CUDA, std::string("state_update bwd_noalloc: cudaGetSymbolAddress: ") +
-                                          cudaGetErrorString(e));
-        g_static_addr[dev] = addr;
+    unsigned long long id = 0;
+    if (int s = current_context_id(&id)) return s;
+    for (int i = 0; id != 0 && i < g_static_used; ++i)
+        if (g_static_addr[i].id == id) {
+            *out = g_static_addr[i].addr;
+            return SSM_OK;
+        }
+    // first call in this context (or none is current yet: the runtime makes the
+    // device's primary context current during the lookup)
+    void* addr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&addr, g_static_scratch);
+    if (e != cudaSuccess || addr == nullptr)
+        return fail(SSM_ERR_CUDA, std::string("state_update bwd_noalloc: cudaGetSymbolAddress: ") +
+                                      cudaGetErrorString(e));
+    if (id == 0 && (current_context_id(&id) != SSM_OK || id == 0)) {
+        *out = addr;          // no context id to cache it under: use it uncached
+        return SSM_OK;
     }
-    *out = g_static_addr[dev];
+    const int slot = g_static_used < kCtxSlots ? g_static_used++ : (g_static_next++ % kCtxSlots);
+    g_static_addr[slot] = {id, addr};
+    *out = addr;
     return SSM_OK;
 }
 

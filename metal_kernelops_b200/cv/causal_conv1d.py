@@ -97,6 +97,7 @@ def _fwd(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor],
     final = x.new_empty((x.shape[0], x.shape[1], weight.shape[1] - 1) if want_final else (0,))
     p.out = out.data_ptr()
     p.final_state = final.data_ptr() if want_final and final.numel() else None
+    p.status = nat.status_word(x.device, "causal_conv1d")
     nat.check(nat.lib().ssm_causal_conv1d_fwd(p, nat.stream_of(x)), "causal_conv1d")
     return out, final
 
@@ -124,6 +125,7 @@ def _bwd(dout: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, bias: Option
     p.dbias = dbias.data_ptr() if bias is not None else None
     p.dinitial = dinit.data_ptr() if init is not None and dinit.numel() else None
     p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+    p.status = nat.status_word(x.device, "causal_conv1d")
     nat.check(nat.lib().ssm_causal_conv1d_bwd(p, nat.stream_of(x)), "causal_conv1d backward")
     return dx, dweight, dbias, dinit
 
@@ -192,6 +194,7 @@ def _fwd_cl(xt: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor]
     p = _params_cl(xt, weight, bias, silu)
     out = xt.new_empty(xt.shape)
     p.out = out.data_ptr()
+    p.status = nat.status_word(xt.device, "causal_conv1d")
     nat.check(nat.lib().ssm_causal_conv1d_fwd(p, nat.stream_of(xt)), "causal_conv1d")
     return out
 
@@ -216,6 +219,7 @@ def _bwd_cl(dout: torch.Tensor, xt: torch.Tensor, weight: torch.Tensor, bias: Op
     p.dweight = dweight.data_ptr()
     p.dbias = dbias.data_ptr() if bias is not None else None
     p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+    p.status = nat.status_word(xt.device, "causal_conv1d")
     nat.check(nat.lib().ssm_causal_conv1d_bwd(p, nat.stream_of(xt)), "causal_conv1d backward")
     return dx, dweight, dbias
 
@@ -324,6 +328,7 @@ def _update(x: torch.Tensor, state: torch.Tensor, weight: torch.Tensor, bias: Op
     p.state, p.x, p.weight = state.data_ptr(), x.data_ptr(), weight.data_ptr()
     p.bias = bias.data_ptr() if bias is not None else None
     p.out = out.data_ptr()
+    p.status = nat.status_word(x.device, "causal_conv1d_update")
     nat.check(nat.lib().ssm_causal_conv1d_update(p, nat.stream_of(x)), "causal_conv1d_update")
     return out
 

@@ -62,6 +62,7 @@ def _fwd(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], z:
                        device=x.device)
     p.out = out.data_ptr()
     p.rstd = rstd.data_ptr() if save and rstd.numel() else None
+    p.status = nat.status_word(x.device, "gated_rmsnorm")
     nat.check(nat.lib().ssm_gated_rmsnorm_fwd(p, nat.stream_of(x)), "rmsnorm_gated")
     return out, rstd
 
@@ -90,6 +91,7 @@ def _bwd(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, bias: Optional
     p.dweight = dw.data_ptr()
     p.dbias = db.data_ptr() if bias is not None else None
     p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+    p.status = nat.status_word(x.device, "gated_rmsnorm")
     nat.check(nat.lib().ssm_gated_rmsnorm_bwd(p, nat.stream_of(x)), "rmsnorm_gated backward")
     return dx, dw, db, dz
 

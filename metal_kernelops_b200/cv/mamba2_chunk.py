@@ -102,6 +102,7 @@ def _fwd(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Tensor, C:
     final = torch.empty(batch, nheads, headdim, B.shape[3], dtype=torch.float32, device=x.device)
     saved = torch.empty(saved_bytes // 4, dtype=torch.float32, device=x.device)
     p.y, p.final_state, p.saved = y.data_ptr(), final.data_ptr(), saved.data_ptr()
+    p.status = nat.status_word(x.device, "chunk_scan")
     nat.check(nat.lib().ssm_chunk_scan_fwd(p, nat.stream_of(x)), "mamba2_chunk_scan")
     return y, final, saved
 
@@ -146,6 +147,7 @@ def _bwd(dy: torch.Tensor, dfinal: Optional[torch.Tensor], x: torch.Tensor, dt: 
     p.ddt_bias = dbias.data_ptr() if dt_bias is not None else None
     p.dinitial = dinit.data_ptr() if init is not None else None
     p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+    p.status = nat.status_word(x.device, "chunk_scan")
     nat.check(nat.lib().ssm_chunk_scan_bwd(p, nat.stream_of(x)), "mamba2_chunk_scan backward")
     return [dx, ddt, dA, dB, dC, dD, dz, dbias, dinit]
 

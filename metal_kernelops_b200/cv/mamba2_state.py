@@ -65,6 +65,7 @@ def _launch(state, x, dt, A, B, C, D, z, dt_bias, softplus, new_state):
         p.flags |= nat.IO_DTYPE
         p.io_dtype = nat.dtype_code(x.dtype)
     p.new_state, p.y = new_state.data_ptr(), y.data_ptr()
+    p.status = nat.status_word(state.device, "state_update")
     nat.check(nat.lib().ssm_state_update_fwd(p, nat.stream_of(state)), "mamba2_state_update")
     return y
 
@@ -130,6 +131,7 @@ def _bwd(state: torch.Tensor, x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor
     p.dz = dz.data_ptr() if z is not None else None
     p.ddt_bias = dbias.data_ptr() if dt_bias is not None else None
     p.workspace, p.workspace_bytes = work.data_ptr(), work.numel()
+    p.status = nat.status_word(state.device, "state_update")
     nat.check(nat.lib().ssm_state_update_bwd(p, nat.stream_of(state)), "mamba2_state_update backward")
     return [g_state, dx, ddt, dA, dB, dC, dD, dz, dbias]
 

@@ -137,6 +137,7 @@ def _fwd(u: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Tensor, C:
     p.y = y.data_ptr()
     p.checkpoints = ckpt.data_ptr() if save and ckpt.numel() else None
     p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+    p.status = nat.status_word(u.device, "ss2d_scan")
     nat.check(nat.lib().ssm_ss2d_scan_fwd(p, nat.stream_of(u)), "ss2d_scan")
     return y, ckpt
 
@@ -168,6 +169,7 @@ def _bwd(dout: torch.Tensor, u: torch.Tensor, dt: torch.Tensor, A: torch.Tensor,
     p.du, p.ddt = du.data_ptr(), ddt.data_ptr()
     p.dA, p.dB, p.dC = dA.data_ptr(), dB.data_ptr(), dC.data_ptr()
     p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+    p.status = nat.status_word(u.device, "ss2d_scan")
     nat.check(nat.lib().ssm_ss2d_scan_bwd(p, nat.stream_of(u)), "ss2d_scan backward")
     return du, ddt, dA, dB, dC
 

@@ -80,6 +80,7 @@ def _fwd(u: torch.Tensor, delta: torch.Tensor, A: torch.Tensor, B: torch.Tensor,
     p.checkpoints = ckpt.data_ptr() if save and ckpt.numel() else None
     if ws is not None:
         p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+    p.status = nat.status_word(u.device, "selective_scan")
     nat.check(nat.lib().ssm_selective_scan_fwd(p, nat.stream_of(u)), "selective_scan")
     return y, ckpt
 
@@ -129,6 +130,7 @@ def _bwd(dout: torch.Tensor, u: torch.Tensor, delta: torch.Tensor, A: torch.Tens
     p.dD = dD.data_ptr() if D is not None else None
     p.ddelta_bias = dbias.data_ptr() if delta_bias is not None else None
     p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+    p.status = nat.status_word(u.device, "selective_scan")
     nat.check(nat.lib().ssm_selective_scan_bwd(p, nat.stream_of(u)), "selective_scan backward")
     return du, ddelta, dA, dB, dC, dD, dz, dbias
 

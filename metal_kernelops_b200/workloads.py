@@ -12,7 +12,7 @@ import math
 
 import torch
 
-__all__ = ["selective_scan_inputs", "ssd_inputs", "decode_inputs", "ss2d_inputs"]
+__all__ = ["selective_scan_inputs", "selective_scan_rows", "ssd_inputs", "decode_inputs", "ss2d_inputs"]
 
 
 def _softplus_inv(v):
@@ -39,6 +39,21 @@ def selective_scan_inputs(batch, dim, length, dstate, groups=1, seed=1000,
     cast = lambda t: t.to(act_dtype)  # noqa: E731
     return dict(u=cast(u), delta=cast(delta), A=A, B=cast(B), C=cast(C), D=D,
                 z=cast(z), delta_bias=delta_bias, dout=cast(dout))
+
+
+def selective_scan_rows(dim, length, dstate, groups, seed, lo, hi, act_dtype=torch.bfloat16):
+    """Batch rows ``lo:hi`` of a large selective-scan configuration (config 2:
+    335 M elements per activation) without materialising the whole batch: row
+    ``b`` comes from its own generator seeded ``seed * 1000 + b``, and the
+    shared parameters A, D, delta_bias from ``seed``, so every rank (and every
+    test) sees the same global tensors whatever slice it generates."""
+    rows = [selective_scan_inputs(1, dim, length, dstate, groups, seed=seed * 1000 + b,
+                                  act_dtype=act_dtype) for b in range(lo, hi)]
+    out = {k: torch.cat([r[k] for r in rows]) for k in ("u", "delta", "z", "dout", "B", "C")}
+    base = selective_scan_inputs(1, dim, 1, dstate, groups, seed=seed)
+    for k in ("A", "D", "delta_bias"):
+        out[k] = base[k]
+    return out
 
 
 def ssd_inputs(batch, length, nheads, headdim, dstate, ngroups, seed=1003,

@@ -120,11 +120,19 @@ def selective_scan_stepwise(u, dt, A, B, C):
     return y
 
 
-def scan_functional(u, dt, A, B, C):
+def scan_functional(u, dt, A, B, C, stepping="unbind"):
     """Differentiable stepwise scan (``cv/path_scan.py:579-605``).
 
     The state is rebuilt every step instead of written in place, so autograd
     can differentiate it.  Vectorised over (batch, channel, state).
+
+    ``stepping="index"`` takes each step's slices exactly as the reference
+    does (``x[:, :, t]`` on the inputs, B and C of the step expanded to the
+    channels per step); autograd then builds a full-size zero gradient per
+    step and slice, which is the reference's own cost and what the timed CPU
+    baseline measures.  ``stepping="unbind"`` (the parity default) takes the
+    same per-step values from ``unbind``, whose backward is one stack, so long
+    sequences stay linear in time; the arithmetic is identical.
     """
     batch, dim, length = u.shape
     dstate = A.shape[1]
@@ -132,19 +140,27 @@ def scan_functional(u, dt, A, B, C):
     width = dim // groups if groups else 0
     if length == 0 or dim == 0 or batch == 0:
         return u.new_zeros(batch, dim, length) + 0.0 * (u.sum() + dt.sum() + A.sum() + B.sum() + C.sum())
-    Bx = B.repeat_interleave(width, dim=1)        # (batch, dim, dstate, length)
-    Cx = C.repeat_interleave(width, dim=1)
+    if stepping == "index":
+        step_of = lambda t: (dt[:, :, t], u[:, :, t],  # noqa: E731
+                             B[:, :, :, t].repeat_interleave(width, dim=1),
+                             C[:, :, :, t].repeat_interleave(width, dim=1))
+    elif stepping == "unbind":
+        dts, us, Bs, Cs = dt.unbind(-1), u.unbind(-1), B.unbind(-1), C.unbind(-1)
+        step_of = lambda t: (dts[t], us[t], Bs[t].repeat_interleave(width, dim=1),  # noqa: E731
+                             Cs[t].repeat_interleave(width, dim=1))
+    else:
+        raise ValueError(f"unknown stepping {stepping!r}")
     state = u.new_zeros(batch, dim, dstate)
     out = []
     for t in range(length):
-        d_t = dt[:, :, t]
-        state = torch.exp(d_t.unsqueeze(-1) * A) * state + (d_t * u[:, :, t]).unsqueeze(-1) * Bx[..., t]
-        out.append((state * Cx[..., t]).sum(-1))
+        d_t, u_t, b_t, c_t = step_of(t)
+        state = torch.exp(d_t.unsqueeze(-1) * A) * state + (d_t * u_t).unsqueeze(-1) * b_t
+        out.append((state * c_t).sum(-1))
     return torch.stack(out, dim=-1)
 
 
 def selective_scan_ref(u, dt, A, B, C, D=None, z=None, delta_bias=None,
-                       delta_softplus=False):
+                       delta_softplus=False, stepping="unbind"):
     """The full Mamba-1 op of ``scan.py:295-320`` over ``scan_functional``.
 
     bias add, softplus (torch's threshold-20 rule), scan, ``+ u*D``, ``* silu(z)``.
@@ -153,7 +169,7 @@ def selective_scan_ref(u, dt, A, B, C, D=None, z=None, delta_bias=None,
         dt = dt + delta_bias[..., None]
     if delta_softplus:
         dt = F.softplus(dt)
-    out = scan_functional(u, dt, A, B, C)
+    out = scan_functional(u, dt, A, B, C, stepping=stepping)
     if D is not None:
         out = out + u * D[..., None]
     if z is not None:

@@ -38,3 +38,18 @@ def golden():
         return torch.load(GOLDEN / f"{name}.pt", weights_only=False)
 
     return load
+
+
+@pytest.fixture(autouse=True)
+def _kernel_status(request):
+    """After every GPU test: no kernel gave up on a bounded wait (the ops'
+    status words, read lazily by ``check_errors``)."""
+    yield
+    if "gpu" not in request.keywords:
+        return
+    import torch
+    if not torch.cuda.is_available():
+        return
+    from metal_kernelops_b200 import _native as nat
+    if nat._lib is not None:
+        nat.check_errors()

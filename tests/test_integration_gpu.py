@@ -7,7 +7,7 @@ and a VMamba-style four-path block, runs them once through the CPU references
 and once through the fused device ops, and compares the loss, every parameter
 gradient and one SGD step.  Here the CPU side is the fp64 oracle and the device
 side this package's CUDA ops; the limits are the verifier's (loss 5e-5,
-gradients rtol 2e-4 / atol 2e-5) for fp32, and norm-relative 3e-2 for a bf16
+gradients rtol 2e-4 / atol 2e-5) for fp32, and norm-relative 2e-2 for a bf16
 block at the Mamba-2 head shape (head dim 64, state 128: the tensor-core SSD).
 """
 
@@ -143,7 +143,7 @@ def test_mamba2_block_bf16_tensor_core_shape():
     norm-relative limit."""
     make = lambda: Mamba2Block(d_model=128, heads=4, head_dim=64, d_state=128, ngroups=1, chunk=64)  # noqa: E731
     cpu, dev = _pair(make, 19)
-    _check_step(cpu, dev, torch.randn(2, 160, 128), loss_tol=3e-2, rtol=3e-2, dtype=torch.bfloat16)
+    _check_step(cpu, dev, torch.randn(2, 160, 128), loss_tol=2e-2, rtol=2e-2, dtype=torch.bfloat16)
 
 
 def test_path_block_verifier_shape():

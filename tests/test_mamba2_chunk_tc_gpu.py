@@ -6,9 +6,11 @@ the input dtype and accumulate in fp32.  These tests check them the way the
 reference's verifier checks its fast path (benchmarks/verify_mamba2_chunk.py):
 forward outputs and final state over ragged lengths, group sizes and every
 option against the fp64 sequential recurrence (max|err| / max|ref|: bf16 2e-2,
-f16 2e-3), all nine gradients against fp64 autograd (norm-relative: bf16 3e-2,
-f16 5e-3), agreement with the CUDA-core kernels at the full config-3 size,
-bit-identical reruns, and that no kernel gave up on a bounded wait.
+f16 2e-3), all nine gradients against fp64 autograd (norm-relative: bf16 2e-2,
+the north-star bf16 limit, f16 5e-3), a gradient slice of the full config-3
+problem against the fp64 oracle, agreement with the CUDA-core kernels at the
+full config-3 size, bit-identical reruns, and that no kernel gave up on a
+bounded wait.
 """
 
 import pytest
@@ -20,7 +22,7 @@ pytestmark = pytest.mark.gpu
 
 P, N = 64, 128
 TOL_FWD = {torch.bfloat16: 2e-2, torch.float16: 2e-3}
-TOL_GRAD = {torch.bfloat16: 3e-2, torch.float16: 5e-3}
+TOL_GRAD = {torch.bfloat16: 2e-2, torch.float16: 5e-3}
 NAMES = ("x", "dt", "A", "B", "C", "D", "z", "dt_bias", "initial_states")
 
 
@@ -160,10 +162,54 @@ def test_tc_and_cuda_cores_agree_at_config3():
     names = ("y", "final", "dx", "ddt", "dA", "dB", "dC", "dD", "ddt_bias")
     for name, a, b in zip(names, fast, exact):
         assert torch.isfinite(a).all(), name
-        tol = 2e-2 if name in ("y", "final") else 3e-2
+        tol = 2e-2
         err = (orc.max_rel(a.cpu(), b.cpu()) if name in ("y", "final")
                else orc.norm_rel(a.cpu(), b.cpu()))
         assert err <= tol, (name, err)
+    from metal_kernelops_b200 import _native as nat
+    assert nat.lib().ssm_take_kernel_error() == 0
+
+
+def test_config3_gradient_slice_vs_oracle():
+    """BASELINE config 3 at full size (B8 L8192 H80 P64 N128 G8, bf16, the
+    bench's inputs) through the tensor-core kernels, with the upstream
+    gradient kept only on batch row 5, the first 512 steps and the ten heads
+    of group 3 (zero elsewhere).  Rows and groups are independent and the scan
+    is causal, so y on that slice and every gradient -- dx, d dt, dB, dC and the
+    shared dA, dD, d dt_bias of those heads -- equal the fp64 oracle run on the
+    slice alone, and every other gradient entry is zero."""
+    m = _mod()
+    inp = orc.ssd_inputs(8, 8192, 80, 64, 128, 8)
+    r, t, g = 5, 512, 3
+    heads = slice(10 * g, 10 * g + 10)
+    keys = ("x", "dt", "A", "B", "C", "D", "dt_bias")
+    dev = {k: inp[k].cuda().requires_grad_(True) for k in keys}
+    y, _ = m.mamba2_chunk_scan(dev["x"], dev["dt"], dev["A"], dev["B"], dev["C"], 256, D=dev["D"],
+                               dt_bias=dev["dt_bias"], dt_softplus=True)
+    assert m.last_path() == "cuda"
+    dy = torch.zeros_like(inp["dy"])
+    dy[r, :t, heads] = inp["dy"][r, :t, heads]
+    got = dict(zip(keys, torch.autograd.grad(y, [dev[k] for k in keys], dy.cuda())))
+
+    sl = {"x": inp["x"][r:r + 1, :t, heads], "dt": inp["dt"][r:r + 1, :t, heads], "A": inp["A"][heads],
+          "B": inp["B"][r:r + 1, :t, g:g + 1], "C": inp["C"][r:r + 1, :t, g:g + 1], "D": inp["D"][heads],
+          "dt_bias": inp["dt_bias"][heads]}
+    ref = {k: v.double().requires_grad_(True) for k, v in sl.items()}
+    yr, _ = orc.mamba2_chunk_scan_ref(ref["x"], ref["dt"], ref["A"], ref["B"], ref["C"], 256, D=ref["D"],
+                                      dt_bias=ref["dt_bias"], dt_softplus=True)
+    assert orc.max_rel(y[r:r + 1, :t, heads].detach().float().cpu(), yr) <= 2e-2
+    want = dict(zip(keys, torch.autograd.grad(yr, [ref[k] for k in keys],
+                                              dy[r:r + 1, :t, heads].double())))
+    where = {"x": (slice(r, r + 1), slice(0, t), heads), "dt": (slice(r, r + 1), slice(0, t), heads),
+             "B": (slice(r, r + 1), slice(0, t), slice(g, g + 1)),
+             "C": (slice(r, r + 1), slice(0, t), slice(g, g + 1)),
+             "A": (heads,), "D": (heads,), "dt_bias": (heads,)}
+    for k in keys:
+        gk = got[k].float()
+        assert orc.norm_rel(gk[where[k]].cpu(), want[k]) <= 2e-2, k
+        rest = gk.clone()
+        rest[where[k]] = 0
+        assert not rest.any(), f"d{k} outside the slice"
     from metal_kernelops_b200 import _native as nat
     assert nat.lib().ssm_take_kernel_error() == 0
 

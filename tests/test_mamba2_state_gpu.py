@@ -1,8 +1,9 @@
 """Mamba-2 decode state update: CUDA kernels vs the fp64 oracle (GPU).
 
 Mirrors the reference's verifier (benchmarks/verify_mamba2_state.py): the
-17-case option matrix (:552-570) with its tolerances (fp32 1e-5, fp16 5e-3,
-bf16 3e-2; forward max|err| <= tol * max(scale, 1), gradients norm-relative),
+17-case option matrix (:552-570) with its tolerances (fp32 1e-5, fp16 5e-3;
+bf16 held to the north-star 2e-2 where the verifier allows 3e-2; forward
+max|err| <= tol * max(scale, 1), gradients norm-relative),
 the aliasing/``out_state`` contract and error cases (:196-264), one-output
 adjoints (:169-193) and bit-determinism over 3 runs (:267-302).
 """
@@ -14,7 +15,7 @@ from oracle import ssm_oracle as orc
 
 pytestmark = pytest.mark.gpu
 
-TOL = {torch.float32: 1e-5, torch.float16: 5e-3, torch.bfloat16: 3e-2}
+TOL = {torch.float32: 1e-5, torch.float16: 5e-3, torch.bfloat16: 2e-2}
 NAMES = ("state", "x", "dt", "A", "B", "C", "D", "z", "dt_bias")
 
 

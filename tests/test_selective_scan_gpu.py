@@ -155,48 +155,77 @@ def test_inference_saves_nothing():
     assert y.shape == (1, 8, 40)
 
 
-def test_config1_full_size_slices():
-    """Config 1 at full size (B8 D1536 L2048 N16, bf16).  The oracle checks a
-    slice of channels (channels are independent given B, C), and dB/dC are
-    checked by linearity: the sum over channel slices of their dB equals the
-    full dB."""
+def _slice_oracle(inp, rows, ch, dout):
+    """fp64 oracle of the channels ``ch`` over the batch rows ``rows``
+    (channels are independent given B and C): y and every input gradient."""
+    sl = {"u": inp["u"][rows, ch], "delta": inp["delta"][rows, ch], "A": inp["A"][ch],
+          "B": inp["B"][rows], "C": inp["C"][rows], "D": inp["D"][ch],
+          "z": inp["z"][rows, ch], "delta_bias": inp["delta_bias"][ch]}
+    ref = {k: v.double().requires_grad_(True) for k, v in sl.items()}
+    yr = orc.selective_scan_ref(ref["u"], ref["delta"], ref["A"], ref["B"], ref["C"], D=ref["D"],
+                                z=ref["z"], delta_bias=ref["delta_bias"], delta_softplus=True)
+    gr = torch.autograd.grad(yr, [ref[k] for k in NAMES], dout[rows, ch].double())
+    return yr.detach(), dict(zip(NAMES, gr))
+
+
+def _full_size_check(inp, ch, prefix_row, prefix_len):
+    """Forward and backward of a full-size bf16 problem on the GPU, then:
+
+    * y, du, ddelta, dz of the channels ``ch`` over every batch row, and the
+      shared-parameter gradients dA, dD, d delta_bias of those channels (the
+      values the multi-GPU all-reduce sums), against the fp64 oracle of that
+      channel slice over all rows;
+    * dB and dC -- sums over every channel -- through a second backward of the
+      same forward whose upstream gradient is zero except on batch row
+      ``prefix_row`` for its first ``prefix_len`` steps: the scan is causal, so
+      those gradients equal the oracle's on that row's prefix over all
+      channels, and every other gradient entry is zero."""
     mk = _mk()
-    inp = orc.selective_scan_inputs(8, 1536, 2048, 16, 1, seed=1001, act_dtype=torch.bfloat16)
     dev = {k: inp[k].cuda().requires_grad_(True) for k in NAMES}
     y = mk.selective_scan(dev["u"], dev["delta"], dev["A"], dev["B"], dev["C"], D=dev["D"],
                           z=dev["z"], delta_bias=dev["delta_bias"], delta_softplus=True)
     assert torch.isfinite(y).all()
-    g = torch.autograd.grad(y, [dev[k] for k in NAMES], inp["dout"].cuda())
+    g = torch.autograd.grad(y, [dev[k] for k in NAMES], inp["dout"].cuda(), retain_graph=True)
     grads = dict(zip(NAMES, g))
     for k, v in grads.items():
         assert torch.isfinite(v.float()).all(), k
-    # oracle on batch row 3, channels 100..131
-    b, ch = 3, slice(100, 132)
-    sl = {"u": inp["u"][b:b + 1, ch], "delta": inp["delta"][b:b + 1, ch], "A": inp["A"][ch],
-          "B": inp["B"][b:b + 1], "C": inp["C"][b:b + 1], "D": inp["D"][ch],
-          "z": inp["z"][b:b + 1, ch], "delta_bias": inp["delta_bias"][ch]}
-    ref = {k: v.double().requires_grad_(True) for k, v in sl.items()}
-    yr = orc.selective_scan_ref(ref["u"], ref["delta"], ref["A"], ref["B"], ref["C"], D=ref["D"],
-                                z=ref["z"], delta_bias=ref["delta_bias"], delta_softplus=True)
-    assert orc.max_rel(y[b:b + 1, ch].float().cpu(), yr) <= 2e-2
-    gr = torch.autograd.grad(yr, [ref["u"], ref["delta"], ref["z"]],
-                             inp["dout"][b:b + 1, ch].double())
-    for k, want in zip(("u", "delta", "z"), gr):
-        assert orc.norm_rel(grads[k][b:b + 1, ch].float().cpu(), want) <= 2e-2, k
-    # linearity of dB/dC over channel slices
-    parts_B = torch.zeros_like(grads["B"], dtype=torch.float32)
-    parts_C = torch.zeros_like(grads["C"], dtype=torch.float32)
-    for lo in range(0, 1536, 512):
-        s = slice(lo, lo + 512)
-        sub = {k: (dev[k][:, s] if k in ("u", "delta", "z") else dev[k][s] if k in
-                   ("A", "D", "delta_bias") else dev[k]).detach().requires_grad_(True) for k in NAMES}
-        ys = mk.selective_scan(sub["u"], sub["delta"], sub["A"], sub["B"], sub["C"], D=sub["D"],
-                               z=sub["z"], delta_bias=sub["delta_bias"], delta_softplus=True)
-        gb, gc = torch.autograd.grad(ys, [sub["B"], sub["C"]], inp["dout"][:, s].cuda())
-        parts_B += gb.float()
-        parts_C += gc.float()
-    assert orc.norm_rel(parts_B.cpu(), grads["B"].float().cpu()) <= 2e-2
-    assert orc.norm_rel(parts_C.cpu(), grads["C"].float().cpu()) <= 2e-2
+    rows = slice(0, inp["u"].shape[0])
+    yr, gr = _slice_oracle(inp, rows, ch, inp["dout"])
+    assert orc.max_rel(y[rows, ch].float().cpu(), yr) <= 2e-2
+    for k in ("u", "delta", "z"):
+        assert orc.norm_rel(grads[k][rows, ch].float().cpu(), gr[k]) <= 2e-2, k
+    for k in ("A", "D", "delta_bias"):
+        assert orc.norm_rel(grads[k][ch].float().cpu(), gr[k]) <= 2e-2, k
+
+    mask = torch.zeros_like(inp["dout"])
+    b, t = prefix_row, prefix_len
+    mask[b, :, :t] = inp["dout"][b, :, :t]
+    g2 = dict(zip(NAMES, torch.autograd.grad(y, [dev[k] for k in NAMES], mask.cuda())))
+    pre = {k: (v[b:b + 1, ..., :t] if k in ("u", "delta", "z", "B", "C") else v) for k, v in inp.items()}
+    pre["dout"] = inp["dout"][b:b + 1, :, :t]
+    _, gp = _slice_oracle(pre, slice(0, 1), slice(None), pre["dout"])
+    for k in ("B", "C", "u", "delta", "z"):
+        got = g2[k][b:b + 1, ..., :t].float().cpu()
+        assert orc.norm_rel(got, gp[k]) <= 2e-2, f"prefix d{k}"
+        rest = g2[k].float().clone()
+        rest[b, ..., :t] = 0
+        assert not rest.any(), f"d{k} outside the prefix"
+
+
+def test_config1_full_size_slices():
+    """BASELINE config 1 at full size (B8 D1536 L2048 N16, bf16, seed 1001)."""
+    inp = orc.selective_scan_inputs(8, 1536, 2048, 16, 1, seed=1001, act_dtype=torch.bfloat16)
+    _full_size_check(inp, slice(100, 132), prefix_row=3, prefix_len=512)
+
+
+def test_config2_full_size_slices():
+    """BASELINE config 2 -- the bench's headline workload -- at full size
+    (B16 D5120 L4096 N16, bf16) on exactly the inputs ``bench.py`` times
+    (``workloads.selective_scan_rows``, seed 1002): the launch shape, the
+    saved-state layout and the partial reductions of the timed kernels."""
+    from metal_kernelops_b200.workloads import selective_scan_rows
+    inp = selective_scan_rows(5120, 4096, 16, 1, 1002, 0, 16)
+    _full_size_check(inp, slice(2000, 2032), prefix_row=5, prefix_len=256)
 
 
 def test_errors():
