@@ -49,6 +49,8 @@ typedef enum ssm_dtype {
 #define SSM_HAS_DSTATE   0x100u /* backward: gradient of the state output given */
 #define SSM_CUDA_CORES   0x200u /* SSD: run the CUDA-core kernels even where the tensor-core
                                    path applies (bf16/f16, headdim 64, dstate 128)          */
+#define SSM_SCAN_PLAIN   0x2000u /* selective scan: run the plain-staging kernels even where
+                                    the TMA-staged ones apply (same results bit for bit)    */
 
 /* Human-readable text for a status code, and the message of the last failure
  * on the calling thread (empty if none). */

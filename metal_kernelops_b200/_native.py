@@ -32,6 +32,7 @@ CUDA_CORES = 0x200
 CONV_SILU = 0x400
 IO_DTYPE = 0x800
 CHANNEL_LAST = 0x1000
+SCAN_PLAIN = 0x2000
 
 EXPORTS = (
     "ssm_status_string", "ssm_last_error",

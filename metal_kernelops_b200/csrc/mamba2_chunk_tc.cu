@@ -1511,6 +1511,7 @@ __global__ void selftest_wait_kernel(int* status, uint32_t polls) {
 }  // namespace ssm
 
 int ssm_conv_take_error();   // causal_conv1d.cu: the conv1d kernels' flag
+int ssm_scan_take_error();   // selective_scan_tma.cu: the TMA scan kernels' flag
 
 extern "C" int ssm_selftest_bounded_wait(int32_t* status, uint32_t polls, void* stream) {
     if (!status) return ssm::fail(SSM_ERR_INVALID, "selftest_bounded_wait: null status word");
@@ -1529,5 +1530,6 @@ extern "C" int ssm_take_kernel_error(void) {
         cudaMemcpyToSymbol(ssm::ssdtc::g_kernel_error, &zero, sizeof(int));
     }
     const int c = ssm_conv_take_error();
-    return v ? v : c;
+    const int sc = ssm_scan_take_error();
+    return v ? v : c ? c : sc;
 }

@@ -226,6 +226,7 @@ static ssm_selective_scan_params stacked(const ssm_ss2d_scan_params* p) {
     s.act_dtype = p->act_dtype;
     s.bc_dtype = p->bc_dtype;
     s.flags = 0;
+    s.status = p->status;
     return s;
 }
 

@@ -34,41 +34,11 @@
 //    uses them, scan.py:226-227), so the backward is bit-reproducible.
 #include <type_traits>
 
-#include "common.cuh"
+#include "sscan.cuh"
 
 namespace ssm {
 namespace sscan {
 
-constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;
-constexpr int kChunk = 16;  // backward chunk (staged tile, walked in reverse)
-constexpr int kFT = 16;     // forward tile
-constexpr int kTS = 4;      // backward sub-block == interval of the saved states
-
-struct Args {
-    int64_t batch, dim, length, groups, dstate, per_group;
-    int64_t nchunks;      // ceil(length / kChunk)
-    int64_t nct;          // channel tiles per group
-    // Sequence segments: blockIdx.x = segment * nct + channel tile.  With
-    // nseg > 1 every segment of seg_chunks chunks runs as its own CTA, starting
-    // from the state (forward) or adjoint (backward) that a summary pass and a
-    // combine over segments left in seg_x: (batch, nseg, dim, dstate) fp32.
-    int64_t nseg, seg_chunks;
-    float* seg_x;
-    float* seg_p;         // decay product over each segment, same layout
-    uint32_t flags;
-    int bc_dtype;
-    bool fast;            // 16-byte aligned rows: asynchronous copies allowed
-    const void* u; const void* delta; const float* A; const void* B; const void* C;
-    const float* D; const void* z; const float* delta_bias;
-    void* y; float* ckpt;
-    int64_t nsub;         // sub-checkpoints per row: nchunks * kChunk / kTS
-    int64_t ysave_off;    // bytes from ckpt to the saved scan output (activation dtype)
-    const void* dout; void* du; void* ddelta; void* dz;
-    float* dB_part; float* dC_part;   // (batch*groups*nct, dstate, length)
-    float* dA_part;                   // (batch, dim, dstate)
-    float* dD_part; float* db_part;   // (batch, dim)
-};
 
 // ---------------------------------------------------------- async copies ----
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -405,61 +375,6 @@ __global__ void combine_fwd_kernel(const Args a) {
 }
 
 // ----------------------------------------------------------------- backward --
-// The cross-channel sums dB[t][n] and dC[t][n] are butterfly reduce-scatters
-// over the lanes that hold the same states of different channels (lane bits
-// [LO, 5)).  Each lane stores its NPT states in a lane-dependent order -- slot
-// i holds state (i XOR mask) -- chosen so that at every level both partners
-// keep the LOWER half of their slots and send the upper half: a level is then
-// one shuffle and one add per value, with no selects.  After the scatter
-// levels slot i < kept holds the full sum for state (i + mask); the remaining
-// levels (past log2(NPT)) are plain all-reduces, and `owner` marks the one
-// lane of each duplicate set that writes.
-template <int V, int LO>
-struct Scatter {
-    static constexpr int kept() {
-        int cur = V;
-        for (int bit = 4; bit >= LO; --bit)
-            if (cur > 1) cur /= 2;
-        return cur;
-    }
-    static __device__ __forceinline__ int mask(int lane) {
-        int m = 0, cur = V;
-#pragma unroll
-        for (int bit = 4; bit >= LO; --bit) {
-            if (cur > 1) {
-                cur /= 2;
-                if ((lane >> bit) & 1) m |= cur;
-            }
-        }
-        return m;
-    }
-    static __device__ __forceinline__ bool owner(int lane) {
-        int cur = V;
-        bool own = true;
-#pragma unroll
-        for (int bit = 4; bit >= LO; --bit) {
-            if (cur > 1) cur /= 2;
-            else if ((lane >> bit) & 1) own = false;
-        }
-        return own;
-    }
-    static __device__ __forceinline__ void reduce(float (&v)[V]) {
-        int cur = V;
-#pragma unroll
-        for (int bit = 4; bit >= LO; --bit) {
-            const int o = 1 << bit;
-            if (cur > 1) {
-                const int h = cur / 2;
-#pragma unroll
-                for (int i = 0; i < V / 2; ++i)
-                    if (i < h) v[i] += __shfl_xor_sync(0xffffffffu, v[h + i], o);
-                cur = h;
-            } else {
-                v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
-            }
-        }
-    }
-};
 
 template <typename T, int CPC, int NP, int NPT>
 struct BwdLayout {
@@ -1045,7 +960,6 @@ __global__ void reduce_kernel(const Args a, float* dB, float* dC, float* dA, flo
 }
 
 // ------------------------------------------------------------------- host ----
-struct Cfg { int npt = 4, lpc = 4; };   // launch shape; dstate > 64 is refused before use
 
 // States per thread and lanes per channel.  Fewer lanes per channel mean fewer
 // shuffles per step; more lanes mean more threads, which small batch*dim
@@ -1137,12 +1051,14 @@ static void make_args(const ssm_selective_scan_params* p, int cpc, Args& a) {
     a.D = p->D; a.z = p->z; a.delta_bias = p->delta_bias;
     a.y = p->y; a.ckpt = p->checkpoints;
     a.nsub = a.nchunks * (kChunk / kTS);
+    a.ck_stride = p->dim * p->dstate;
     a.ysave_off = (int64_t)ckpt_state_bytes(p);
     a.dout = p->dout; a.du = p->du; a.ddelta = p->ddelta; a.dz = p->dz;
     a.dB_part = a.dC_part = a.dA_part = a.dD_part = a.db_part = nullptr;
     a.nseg = 1;
     a.seg_chunks = a.nchunks;
     a.seg_x = a.seg_p = nullptr;
+    a.status = p->status;
 }
 
 // ---------------------------------------------------- sequence segments ----
@@ -1203,19 +1119,25 @@ static int combine_blocks(const Args& a) {
     return (int)min64(ceil_div(a.batch * a.dim * a.dstate, 256), 148 * 8);
 }
 
+// The segment passes of the forward (nseg > 1): summary of every segment but
+// the last, then the combine that leaves each segment's entering state.
 template <typename T, int NPT, int LPC>
-static int launch_fwd(const Args& a, cudaStream_t st) {
+static int launch_fwd_segments(const Args& a, cudaStream_t st) {
     constexpr int CPC = 32 / LPC * kWarps;
     const size_t sm = FwdLayout<T, CPC, NPT * LPC>::bytes;
-    if (a.nseg > 1) {
-        auto ks = fwd_kernel<T, NPT, LPC, true>;
-        if (cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
-            return check_launch("selective_scan fwd summary: smem attribute");
-        ks<<<dim3((unsigned)(a.nct * (a.nseg - 1)), (unsigned)a.groups, (unsigned)a.batch), kThreads, sm, st>>>(a);
-        if (int s = check_launch("selective_scan fwd summary")) return s;
-        combine_fwd_kernel<<<combine_blocks(a), 256, 0, st>>>(a);
-        if (int s = check_launch("selective_scan fwd combine")) return s;
-    }
+    auto ks = fwd_kernel<T, NPT, LPC, true>;
+    if (cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
+        return check_launch("selective_scan fwd summary: smem attribute");
+    ks<<<dim3((unsigned)(a.nct * (a.nseg - 1)), (unsigned)a.groups, (unsigned)a.batch), kThreads, sm, st>>>(a);
+    if (int s = check_launch("selective_scan fwd summary")) return s;
+    combine_fwd_kernel<<<combine_blocks(a), 256, 0, st>>>(a);
+    return check_launch("selective_scan fwd combine");
+}
+
+template <typename T, int NPT, int LPC>
+static int launch_fwd_main(const Args& a, cudaStream_t st) {
+    constexpr int CPC = 32 / LPC * kWarps;
+    const size_t sm = FwdLayout<T, CPC, NPT * LPC>::bytes;
     auto k = fwd_kernel<T, NPT, LPC, false>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
         return check_launch("selective_scan fwd: smem attribute");
@@ -1224,19 +1146,24 @@ static int launch_fwd(const Args& a, cudaStream_t st) {
     return check_launch("selective_scan fwd");
 }
 
+// The segment passes of the backward (nseg > 1): adjoint summary of every
+// segment but the first, then the reverse combine.
 template <typename T, int NPT, int LPC>
-static int launch_bwd(const Args& a, cudaStream_t st) {
+static int launch_bwd_segments(const Args& a, cudaStream_t st) {
     constexpr int CPC = 32 / LPC * kWarps;
-    if (a.nseg > 1) {
-        const size_t sa = AdjLayout<T, CPC, NPT * LPC>::bytes;
-        auto ka = adj_kernel<T, NPT, LPC>;
-        if (cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sa) != cudaSuccess)
-            return check_launch("selective_scan bwd summary: smem attribute");
-        ka<<<dim3((unsigned)(a.nct * (a.nseg - 1)), (unsigned)a.groups, (unsigned)a.batch), kThreads, sa, st>>>(a);
-        if (int s = check_launch("selective_scan bwd summary")) return s;
-        combine_bwd_kernel<<<combine_blocks(a), 256, 0, st>>>(a);
-        if (int s = check_launch("selective_scan bwd combine")) return s;
-    }
+    const size_t sa = AdjLayout<T, CPC, NPT * LPC>::bytes;
+    auto ka = adj_kernel<T, NPT, LPC>;
+    if (cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sa) != cudaSuccess)
+        return check_launch("selective_scan bwd summary: smem attribute");
+    ka<<<dim3((unsigned)(a.nct * (a.nseg - 1)), (unsigned)a.groups, (unsigned)a.batch), kThreads, sa, st>>>(a);
+    if (int s = check_launch("selective_scan bwd summary")) return s;
+    combine_bwd_kernel<<<combine_blocks(a), 256, 0, st>>>(a);
+    return check_launch("selective_scan bwd combine");
+}
+
+template <typename T, int NPT, int LPC>
+static int launch_bwd_main(const Args& a, cudaStream_t st) {
+    constexpr int CPC = 32 / LPC * kWarps;
     const size_t sm = BwdLayout<T, CPC, NPT * LPC, NPT>::bytes;
     auto k = bwd_kernel<T, NPT, LPC>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
@@ -1246,29 +1173,53 @@ static int launch_bwd(const Args& a, cudaStream_t st) {
     return check_launch("selective_scan bwd");
 }
 
+// which: 0 = segment passes, 1 = main pass
 template <typename T>
-static int dispatch_fwd(const Cfg& c, const Args& a, cudaStream_t st) {
+static int dispatch_fwd(const Cfg& c, const Args& a, cudaStream_t st, int which) {
+#define SSM_FWD_CASE(NPT_, LPC_) \
+    case NPT_ * 100 + LPC_: \
+        return which ? launch_fwd_main<T, NPT_, LPC_>(a, st) : launch_fwd_segments<T, NPT_, LPC_>(a, st);
     switch (c.npt * 100 + c.lpc) {
-        case 401: return launch_fwd<T, 4, 1>(a, st);
-        case 402: return launch_fwd<T, 4, 2>(a, st);
-        case 404: return launch_fwd<T, 4, 4>(a, st);
-        case 801: return launch_fwd<T, 8, 1>(a, st);
-        case 802: return launch_fwd<T, 8, 2>(a, st);
-        case 804: return launch_fwd<T, 8, 4>(a, st);
-        case 1602: return launch_fwd<T, 16, 2>(a, st);
-        default: return launch_fwd<T, 16, 4>(a, st);
+        SSM_FWD_CASE(4, 1)
+        SSM_FWD_CASE(4, 2)
+        SSM_FWD_CASE(4, 4)
+        SSM_FWD_CASE(8, 1)
+        SSM_FWD_CASE(8, 2)
+        SSM_FWD_CASE(8, 4)
+        SSM_FWD_CASE(16, 2)
+        default: return which ? launch_fwd_main<T, 16, 4>(a, st) : launch_fwd_segments<T, 16, 4>(a, st);
     }
+#undef SSM_FWD_CASE
 }
 
 template <typename T>
-static int dispatch_bwd(const Cfg& c, const Args& a, cudaStream_t st) {
+static int dispatch_bwd(const Cfg& c, const Args& a, cudaStream_t st, int which) {
+#define SSM_BWD_CASE(NPT_, LPC_) \
+    case NPT_ * 100 + LPC_: \
+        return which ? launch_bwd_main<T, NPT_, LPC_>(a, st) : launch_bwd_segments<T, NPT_, LPC_>(a, st);
     switch (c.npt * 100 + c.lpc) {
-        case 401: return launch_bwd<T, 4, 1>(a, st);
-        case 404: return launch_bwd<T, 4, 4>(a, st);
-        case 801: return launch_bwd<T, 8, 1>(a, st);
-        case 802: return launch_bwd<T, 8, 2>(a, st);
-        case 804: return launch_bwd<T, 8, 4>(a, st);
-        default: return launch_bwd<T, 8, 8>(a, st);
+        SSM_BWD_CASE(4, 1)
+        SSM_BWD_CASE(4, 4)
+        SSM_BWD_CASE(8, 1)
+        SSM_BWD_CASE(8, 2)
+        SSM_BWD_CASE(8, 4)
+        default: return which ? launch_bwd_main<T, 8, 8>(a, st) : launch_bwd_segments<T, 8, 8>(a, st);
+    }
+#undef SSM_BWD_CASE
+}
+
+static int by_dtype_fwd(int dtype, const Cfg& c, const Args& a, cudaStream_t st, int which) {
+    switch (dtype) {
+        case SSM_F32: return dispatch_fwd<float>(c, a, st, which);
+        case SSM_BF16: return dispatch_fwd<__nv_bfloat16>(c, a, st, which);
+        default: return dispatch_fwd<__half>(c, a, st, which);
+    }
+}
+static int by_dtype_bwd(int dtype, const Cfg& c, const Args& a, cudaStream_t st, int which) {
+    switch (dtype) {
+        case SSM_F32: return dispatch_bwd<float>(c, a, st, which);
+        case SSM_BF16: return dispatch_bwd<__nv_bfloat16>(c, a, st, which);
+        default: return dispatch_bwd<__half>(c, a, st, which);
     }
 }
 
@@ -1316,11 +1267,11 @@ extern "C" int ssm_selective_scan_fwd(const ssm_selective_scan_params* p, void* 
         a.seg_p = reinterpret_cast<float*>(reinterpret_cast<char*>(p->workspace) + sg);
     }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    switch (p->act_dtype) {
-        case SSM_F32: return dispatch_fwd<float>(c, a, st);
-        case SSM_BF16: return dispatch_fwd<__nv_bfloat16>(c, a, st);
-        default: return dispatch_fwd<__half>(c, a, st);
-    }
+    if (a.nseg > 1)
+        if (int s = by_dtype_fwd(p->act_dtype, c, a, st, 0)) return s;
+    const int s = fwd_tma(p, c, a, st);       // the TMA-staged main pass where it applies
+    if (s != SSM_ERR_UNSUPPORTED) return s;
+    return by_dtype_fwd(p->act_dtype, c, a, st, 1);
 }
 
 extern "C" int ssm_selective_scan_bwd(const ssm_selective_scan_params* p, void* stream) {
@@ -1356,12 +1307,10 @@ extern "C" int ssm_selective_scan_bwd(const ssm_selective_scan_params* p, void* 
         a.seg_x = reinterpret_cast<float*>(ws + 2 * w.bc + w.da + 2 * w.dd);
         a.seg_p = reinterpret_cast<float*>(ws + 2 * w.bc + w.da + 2 * w.dd + w.sg);
     }
-    int s;
-    switch (p->act_dtype) {
-        case SSM_F32: s = dispatch_bwd<float>(c, a, st); break;
-        case SSM_BF16: s = dispatch_bwd<__nv_bfloat16>(c, a, st); break;
-        default: s = dispatch_bwd<__half>(c, a, st); break;
-    }
+    if (a.nseg > 1)
+        if (int s = by_dtype_bwd(p->act_dtype, c, a, st, 0)) return s;
+    int s = bwd_tma(p, c, a, st);             // the TMA-staged main pass where it applies
+    if (s == SSM_ERR_UNSUPPORTED) s = by_dtype_bwd(p->act_dtype, c, a, st, 1);
     if (s) return s;
     const int64_t total = p->batch * p->groups * p->dstate * p->length + p->dim * p->dstate + 2 * p->dim;
     const int blocks = (int)min64(ceil_div(total, 256), 148 * 16);

@@ -38,13 +38,27 @@ CHUNK = 16
 SUB_BLOCK = 4
 """Steps between the states the forward saves for the backward."""
 
-__all__ = ["CHUNK", "selective_scan", "selective_scan_fn", "scan_cuda"]
+__all__ = ["CHUNK", "selective_scan", "selective_scan_fn", "scan_cuda", "set_tma_staging"]
+
+_plain_staging = False
+
+
+def set_tma_staging(enabled: bool) -> bool:
+    """Choose the kernels' tile staging: True (the default) lets every problem
+    whose rows are 16-byte aligned run the TMA-staged kernels; False runs the
+    plain-staging kernels everywhere.  Both compute the same results bit for
+    bit.  Returns the previous setting."""
+    global _plain_staging
+    prev = not _plain_staging
+    _plain_staging = not enabled
+    return prev
 
 
 def _params(u, delta, A, B, C, D, z, delta_bias, softplus):
     batch, dim, length = u.shape
     flags = ((nat.HAS_D if D is not None else 0) | (nat.HAS_Z if z is not None else 0)
-             | (nat.HAS_BIAS if delta_bias is not None else 0) | (nat.SOFTPLUS if softplus else 0))
+             | (nat.HAS_BIAS if delta_bias is not None else 0) | (nat.SOFTPLUS if softplus else 0)
+             | (nat.SCAN_PLAIN if _plain_staging else 0))
     p = nat.SelectiveScanParams()
     p.batch, p.dim, p.length = batch, dim, length
     p.groups, p.dstate = B.shape[1], A.shape[1]
