@@ -319,15 +319,16 @@ def run_scan(args, world, rank, device):
     fwd_gbs = fwd_b / (fwd_ms / 1e3) / 1e9
     step_gbs = (fwd_b + bwd_b) / ((fwd_ms + bwd_ms) / 1e3) / 1e9
     # The compute floor the kernels sit against: one MUFU ex2 per element-state
-    # in the forward and one in the backward (the sub-block replay from the
-    # saved states), at 16 per clock per SM and the SM clock sampled under load.
+    # in the forward and two in the backward (the sub-block replay from the
+    # saved states, and the adjoint, which recomputes the decays), at 16 per
+    # clock per SM and the SM clock sampled under load.
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     mhz = (ck_info or {}).get("sm_mhz") or 1965.0
     ex2_per_s = sms * 16 * mhz * 1e6
     es = b * d * l * n
-    fwd_floor, bwd_floor = es / ex2_per_s * 1e3, es / ex2_per_s * 1e3
+    fwd_floor, bwd_floor = es / ex2_per_s * 1e3, 2 * es / ex2_per_s * 1e3
     mufu = {"pipe": "XU (MUFU ex2), 16 per clock per SM", "sm_mhz": mhz,
-            "ex2_per_element_state": {"fwd": 1, "bwd": 1},
+            "ex2_per_element_state": {"fwd": 1, "bwd": 2},
             "fwd_floor_ms": fwd_floor, "bwd_floor_ms": bwd_floor,
             "fwd_frac": fwd_floor / fwd_ms, "bwd_frac": bwd_floor / bwd_ms}
     return {

@@ -20,6 +20,14 @@ int check_launch(const char* what) {
     return fail(SSM_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
+int ensure_context(const char* what) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaSetDevice(dev);   // initialises the primary context and makes it current
+    if (e == cudaSuccess) return SSM_OK;
+    return fail(SSM_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
 }  // namespace ssm
 
 extern "C" const char* ssm_status_string(int status) {

@@ -16,6 +16,11 @@ namespace ssm {
 void set_error(const std::string& msg);
 int fail(int status, const std::string& msg);
 int check_launch(const char* what);
+// Make the current device's primary context current on the calling thread
+// (through the runtime) before a driver-API call that needs one, such as
+// cuTensorMapEncodeTiled.  A thread whose first CUDA call is into this library
+// -- torch runs backward passes on its own autograd thread -- has none yet.
+int ensure_context(const char* what);
 
 // ------------------------------------------------------------ dtype I/O ----
 template <typename T> struct Io;

@@ -1402,6 +1402,7 @@ static int encode_rows(CUtensorMap* m, const void* base, int dtype, int64_t batc
                        int64_t width, int64_t token_stride = 0) {
     auto enc = tensor_map_encoder();
     if (!enc) return fail(SSM_ERR_CUDA, "chunk_scan (tensor cores): cuTensorMapEncodeTiled unavailable");
+    if (int s = ensure_context("chunk_scan (tensor cores)")) return s;
     const cuuint64_t es = 2;
     cuuint64_t dim[5] = {8, (cuuint64_t)length, (cuuint64_t)(width / 8), (cuuint64_t)batch, (cuuint64_t)heads};
     const int64_t ts = token_stride ? token_stride : heads * width;   // elements between tokens

@@ -559,7 +559,11 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
                     }
                 }
                 slot ^= 1;
-                float2 xh[TS][NH], ah[TS][NH];
+                // the replay keeps the states entering each step; the
+                // adjoint recomputes each step's decays (two exponentials per
+                // element-state: a decay history would cost 32 more registers
+                // and spill at this kernel's 3-CTA register budget)
+                float2 xh[TS][NH];
 #pragma unroll
                 for (int jj = 0; jj < TS; ++jj) {
                     if (FULL || jj < nb) {
@@ -574,8 +578,6 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
                             const float2 a1 = __fmul2_rn(dl2, An2[2 * qq + 1]);
                             const float2 e0 = make_float2(exp2_mufu(a0.x), exp2_mufu(a0.y));
                             const float2 e1 = make_float2(exp2_mufu(a1.x), exp2_mufu(a1.y));
-                            ah[jj][2 * qq] = e0;
-                            ah[jj][2 * qq + 1] = e1;
                             xh[jj][2 * qq] = x2[2 * qq];
                             xh[jj][2 * qq + 1] = x2[2 * qq + 1];
                             x2[2 * qq] = __ffma2_rn(e0, x2[2 * qq], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
@@ -594,6 +596,8 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
                         const float4* B4 = reinterpret_cast<const float4*>(Bp + t * NP);
                         const float4* C4 = reinterpret_cast<const float4*>(Cp + t * NP);
                         float2 dua2 = make_float2(0.0f, 0.0f), dda2 = make_float2(0.0f, 0.0f);
+                        const float dlr = v.x * kLog2e;
+                        const float2 dlr2 = make_float2(dlr, dlr);
                         float w[NPT];
 #pragma unroll
                         for (int qq = 0; qq < NPT / 4; ++qq) {
@@ -603,15 +607,17 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
 #pragma unroll
                             for (int r = 0; r < 2; ++r) {
                                 const int j = 2 * qq + r;
+                                const float2 ar = __fmul2_rn(dlr2, An2[j]);
+                                const float2 aj = make_float2(exp2_mufu(ar.x), exp2_mufu(ar.y));
                                 const float2 dh = __ffma2_rn(g2, cc2[r], q2[j]);
-                                const float2 tmp = __fmul2_rn(dh, __fmul2_rn(ah[jj][j], xh[jj][j]));
+                                const float2 tmp = __fmul2_rn(dh, __fmul2_rn(aj, xh[jj][j]));
                                 dda2 = __ffma2_rn(tmp, An2[j], dda2);
                                 dA2[j] = __ffma2_rn(tmp, dv2, dA2[j]);
                                 dua2 = __ffma2_rn(dh, bb[r], dua2);
                                 const float2 wv = __fmul2_rn(dh, du2);
                                 w[2 * j] = wv.x;
                                 w[2 * j + 1] = wv.y;
-                                q2[j] = __fmul2_rn(dh, ah[jj][j]);
+                                q2[j] = __fmul2_rn(dh, aj);
                             }
                         }
                         const float duacc = sum_low_lanes<LPC>(dua2.x + dua2.y);
@@ -882,6 +888,7 @@ static int dispatch_bwd_tma(const Cfg& c, const TmaArgs& ta, cudaStream_t st) {
 
 int fwd_tma(const ssm_selective_scan_params* p, const Cfg& c, const Args& a, cudaStream_t st) {
     if (!tma_ok(p, c, false)) return SSM_ERR_UNSUPPORTED;
+    if (int s = ensure_context("selective_scan fwd (TMA)")) return s;
     const int cpc = 32 / c.lpc * kWarps, np = c.npt * c.lpc;
     TmaArgs ta;
     ta.a = a;
@@ -902,6 +909,7 @@ int fwd_tma(const ssm_selective_scan_params* p, const Cfg& c, const Args& a, cud
 
 int bwd_tma(const ssm_selective_scan_params* p, const Cfg& c, const Args& a, cudaStream_t st) {
     if (!tma_ok(p, c, true)) return SSM_ERR_UNSUPPORTED;
+    if (int s = ensure_context("selective_scan bwd (TMA)")) return s;
     const int cpc = 32 / c.lpc * kWarps, np = c.npt * c.lpc;
     TmaArgs ta;
     ta.a = a;

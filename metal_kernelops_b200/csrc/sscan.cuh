@@ -80,6 +80,8 @@ struct Scatter {
         }
         return own;
     }
+    // Levels that keep two or more values add them in pairs with one paired
+    // fp32 add (each lane rounds exactly as the scalar add).
     static __device__ __forceinline__ void reduce(float (&v)[V]) {
         int cur = V;
 #pragma unroll
@@ -87,9 +89,19 @@ struct Scatter {
             const int o = 1 << bit;
             if (cur > 1) {
                 const int h = cur / 2;
+                if (h >= 2) {
 #pragma unroll
-                for (int i = 0; i < V / 2; ++i)
-                    if (i < h) v[i] += __shfl_xor_sync(0xffffffffu, v[h + i], o);
+                    for (int i = 0; i < V / 2; i += 2)
+                        if (i + 1 < h) {
+                            const float2 r = make_float2(__shfl_xor_sync(0xffffffffu, v[h + i], o),
+                                                         __shfl_xor_sync(0xffffffffu, v[h + i + 1], o));
+                            const float2 s = __fadd2_rn(make_float2(v[i], v[i + 1]), r);
+                            v[i] = s.x;
+                            v[i + 1] = s.y;
+                        }
+                } else {
+                    v[0] += __shfl_xor_sync(0xffffffffu, v[1], o);
+                }
                 cur = h;
             } else {
                 v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);

@@ -294,3 +294,48 @@ def test_tma_and_plain_staging_identical(shape, dtype, opts):
             scan_mod.set_tma_staging(prev)
     for name, a, b_ in zip(("y",) + tuple(use), *runs):
         assert torch.equal(a, b_), name
+
+
+def test_backward_first_cuda_call_on_a_fresh_thread():
+    """torch runs backward passes on its own autograd thread, and the scan's
+    backward may be the first CUDA call made there, before any CUDA context is
+    current on that thread.  The C-ABI backward, called from a brand-new
+    thread with every buffer prepared on the main thread, must run (the TMA
+    path encodes its tensor maps only after making the device's context
+    current) and equal the same call made on the main thread bit for bit."""
+    import threading
+    from metal_kernelops_b200 import _native as nat
+    from metal_kernelops_b200 import scan as scan_mod
+    inp = orc.selective_scan_inputs(2, 64, 256, 16, 1, seed=21, act_dtype=torch.bfloat16)
+    dev = {k: inp[k].cuda() for k in NAMES + ("dout",)}
+    y, ck = torch.ops.b200ssm.selective_scan_fwd(dev["u"], dev["delta"], dev["A"], dev["B"], dev["C"],
+                                                 dev["D"], dev["z"], dev["delta_bias"], True, True)
+
+    def prepared():
+        p = scan_mod._params(dev["u"], dev["delta"], dev["A"], dev["B"], dev["C"], dev["D"], dev["z"],
+                             dev["delta_bias"], True)
+        _, ws_bytes = scan_mod._sizes(p)
+        out = {k: torch.empty_like(dev["u"]) for k in ("du", "ddelta", "dz")}
+        out.update({"dA": torch.empty_like(dev["A"]), "dB": torch.empty(dev["B"].shape, device="cuda"),
+                    "dC": torch.empty(dev["C"].shape, device="cuda"), "dD": torch.empty_like(dev["D"]),
+                    "ddelta_bias": torch.empty_like(dev["delta_bias"])})
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+        p.checkpoints, p.dout = ck.data_ptr(), dev["dout"].data_ptr()
+        for k, v in out.items():
+            setattr(p, k, v.data_ptr())
+        p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+        return p, out, ws
+
+    p_main, out_main, ws_main = prepared()
+    stream = nat.stream_of(dev["u"])
+    nat.check(nat.lib().ssm_selective_scan_bwd(p_main, stream), "main thread")
+    p_thr, out_thr, ws_thr = prepared()
+    torch.cuda.synchronize()
+    status = {}
+    th = threading.Thread(target=lambda: status.setdefault("s", nat.lib().ssm_selective_scan_bwd(p_thr, stream)))
+    th.start()
+    th.join()
+    assert status["s"] == nat.SSM_OK, nat.lib().ssm_last_error()
+    torch.cuda.synchronize()
+    for k in out_main:
+        assert torch.equal(out_main[k], out_thr[k]), k
