@@ -14,12 +14,13 @@
 //   y_l      = (Mh X)_l + exp(cs_l) (C H_c^T)_l + D x_l          [* silu(z_l)]
 //   H_{c+1}  = exp(T) H_c + sum_s exp(T - cs_s) d_s x_s B_s^T    (P x N)
 //
-// Kernels.  Forward: `states` (one CTA per (b, h), sequential over chunks)
-// accumulates H^T (dstate x headdim) in TMEM -- the chunk GEMM
-// H^T += B^T (w o X) runs on the tensor core, the exp(T) rescale between
-// chunks on the CUDA cores -- and writes every entering state H_c as a 16 KB
-// operand image (bf16/f16, the shared-memory tile layout of tc.cuh), so that
-// the consumers copy it linearly.  `outputs` (one CTA per (b, group, chunk))
+// Kernels.  Forward: `states2` (one CTA per (b, h), sequential over chunks,
+// warp-specialised) computes each chunk's own contribution B^T (w o X) on the
+// tensor core into a TMEM buffer, ahead of the recurrence, while the CUDA
+// cores carry H^T (dstate x headdim) in registers -- H_{c+1} = exp(T) H_c +
+// B^T (w o X) -- and write every entering state H_c as a 16 KB operand image
+// (bf16/f16, the shared-memory tile layout of tc.cuh), so that the consumers
+// copy it linearly.  `outputs` (one CTA per (b, group, chunk))
 // computes G once, then for each head of the group the decay-masked Mh into
 // shared memory and the two output GEMMs Mh X and C H_c^T.
 //
@@ -287,151 +288,188 @@ __device__ __forceinline__ Steps staged_steps(const Args& a, const HeadSh& hs, i
     return steps_of<NB>(a, threadIdx.x < Q ? hs.raw[k][threadIdx.x] : 0.0f, c, hs.A[k], scan_sh);
 }
 
-// ====================================================================== F1 ==
-// One CTA per (b, h).  TMEM: H^T, lanes = state index n, columns = p.
+// ===================================================================== F1b ==
+// The forward state pass, warp-specialised, with the chunk-state GEMMs off the
+// sequential chain.  One CTA per (b, h), chunks in order.  Four compute warps:
+// thread n carries row n of H^T (64 fp32 values) in registers; per chunk c it
+// scales its position's row of X_c in place to w o X_c, and then folds the
+// previous chunk's contribution into H after emitting H_{c-1}:
+// H_c = exp(T_{c-1}) H_{c-1} + S_{c-1}.  One producer warp issues every copy
+// and GEMM: the tensor core computes each chunk's own S_c = B_c^T (w o X_c)
+// into one of two TMEM buffers (64 columns each), so no GEMM waits on the
+// recurrence and no compute warp waits on a copy being issued.  Hand-offs are
+// mbarriers: tiles landed (copy -> compute, copy -> GEMM), w o X ready
+// (compute -> GEMM, 128 arrivals), S ready (GEMM -> compute and -> the next
+// copies into its buffers), S buffer read (compute -> GEMM, 128 arrivals).
+// Two tile buffers for X and B (96 KB), 128 TMEM columns: two CTAs per SM.
+constexpr int kStThreads = kThreads + 32;
+constexpr size_t kSmemStates2 = 2 * kTileB + 2 * kTileX;
+
 template <typename T>
-__global__ void __launch_bounds__(kThreads) states_kernel(const __grid_constant__ Args a) {
+__global__ void __launch_bounds__(kStThreads, 2) states2_kernel(const __grid_constant__ Args a) {
     extern __shared__ __align__(128) unsigned char sm_raw[];
     unsigned char* const sm = aligned_smem(sm_raw);
-    // double-buffered B and x tiles: chunk c + 1 loads while chunk c computes
     unsigned char* const sB0 = sm;
     unsigned char* const sX0 = sm + 2 * kTileB;
-    unsigned char* sXW = sX0 + 2 * kTileX;
     __shared__ float s_scan[4];
-    __shared__ float s_T;
-    __shared__ __align__(8) uint64_t mbar;
-    __shared__ __align__(8) uint64_t lbar[2];   // tiles of buffer 0 / 1 landed
+    __shared__ float s_T[2];
+    __shared__ __align__(8) uint64_t lbx[2];    // X tile of buffer i landed
+    __shared__ __align__(8) uint64_t lbb[2];    // B tile of buffer i landed
+    __shared__ __align__(8) uint64_t xw[2];     // w o X of buffer i written (128 arrivals)
+    __shared__ __align__(8) uint64_t sbar[2];   // the GEMM into S buffer i done
+    __shared__ __align__(8) uint64_t sfree[2];  // S buffer i read by the compute warps (128 arrivals)
     __shared__ uint32_t tbase;
+    __shared__ volatile int s_abort;
 
     const int tid = threadIdx.x, warp = tid >> 5;
+    const bool producer = warp == kThreads / 32;
     const int64_t h = blockIdx.x, b = blockIdx.y, g = h / a.hpg;
-    const int64_t H = a.nheads;
-    const float Ah = a.A[h];
-    const float bias = (a.flags & SSM_HAS_BIAS) ? a.dt_bias[h] : 0.0f;
-    uint32_t lpend[2] = {~0u, ~0u};           // parity of a load in flight per buffer (thread 0)
-    auto load_chunk = [&](int64_t c, int buf) {   // one thread
-        const uint32_t lb = tc::smem_u32(&lbar[buf]);
-        tc::mbar_expect_tx(lb, kRowsB + kRowsX);
-        tma_rows<WB>(sB0 + buf * kTileB, a.tm_B, c, b, g, lb, a.status);
-        tma_rows<WX>(sX0 + buf * kTileX, a.tm_x, c, b, h, lb, a.status);
-        lpend[buf] = (uint32_t)((c >> 1) & 1);
-    };
+    const int64_t H = a.nheads, nc = a.nc;
+    auto bar = [](uint64_t* m, int i) { return tc::smem_u32(&m[i]); };
 
-    if (warp == 0) tc::tmem_alloc(tc::smem_u32(&tbase), 64);
     if (tid == 0) {
-        tc::mbar_init(tc::smem_u32(&mbar), 1);
-        tc::mbar_init(tc::smem_u32(&lbar[0]), 1);
-        tc::mbar_init(tc::smem_u32(&lbar[1]), 1);
+        for (int i = 0; i < 2; ++i) {
+            tc::mbar_init(bar(lbx, i), 1);
+            tc::mbar_init(bar(lbb, i), 1);
+            tc::mbar_init(bar(xw, i), kThreads);
+            tc::mbar_init(bar(sbar, i), 1);
+            tc::mbar_init(bar(sfree, i), kThreads);
+        }
+        s_abort = 0;
         tc::fence_mbar_init();
-        load_chunk(0, 0);
     }
+    if (producer) tc::tmem_alloc(tc::smem_u32(&tbase), 128);
     tc::fence_before();
     __syncthreads();
     tc::fence_after();
     const uint32_t tm = tbase;
-    const uint32_t row_addr = tm + ((uint32_t)(warp * 32) << 16);
-    {
-        float v[16];
-        for (int j = 0; j < P / 16; ++j) {
+
+    if (producer) {
+        if ((tid & 31) == 0) {
+            const uint32_t id = tc::idesc_f16(Pk<T>::kFmt, 128, P, true, true);
+            uint32_t xpend[2] = {~0u, ~0u}, bpend[2] = {~0u, ~0u}, mpend[2] = {~0u, ~0u};
+            bool ok = true;
+            auto load = [&](int64_t c) {
+                const int buf = (int)(c & 1);
+                const uint32_t par = (uint32_t)((c >> 1) & 1);
+                tc::mbar_expect_tx(bar(lbx, buf), kRowsX);
+                tma_rows<WX>(sX0 + buf * kTileX, a.tm_x, c, b, h, bar(lbx, buf), a.status);
+                tc::mbar_expect_tx(bar(lbb, buf), kRowsB);
+                tma_rows<WB>(sB0 + buf * kTileB, a.tm_B, c, b, g, bar(lbb, buf), a.status);
+                xpend[buf] = bpend[buf] = par;
+            };
+            load(0);
+            for (int64_t c = 0; c < nc && ok; ++c) {
+                const int buf = (int)(c & 1);
+                const uint32_t par = (uint32_t)((c >> 1) & 1);
+                if (c + 1 < nc) {             // chunk c + 1's tiles, once the GEMM of c - 1 is done with its buffers
+                    const int nb = buf ^ 1;
+                    if (c >= 1) {
+                        if (!tc::mbar_wait(bar(sbar, nb), (uint32_t)(((c - 1) >> 1) & 1))) { report(a, 81); ok = false; break; }
+                        mpend[nb] = ~0u;
+                    }
+                    load(c + 1);
+                }
+                // the GEMM of c: w o X written, B landed, the S buffer read
+                if (!tc::mbar_wait(bar(xw, buf), par)) { report(a, 82); ok = false; break; }
+                xpend[buf] = ~0u;             // the compute warps waited for it
+                if (!tc::mbar_wait(bar(lbb, buf), par)) { report(a, 83); ok = false; break; }
+                bpend[buf] = ~0u;
+                if (c >= 2 && !tc::mbar_wait(bar(sfree, buf), (uint32_t)(((c - 2) >> 1) & 1))) {
+                    report(a, 84); ok = false; break;
+                }
+                tc::fence_after();
+                const uint32_t aB = tc::smem_u32(sB0 + buf * kTileB), aX = tc::smem_u32(sX0 + buf * kTileX);
+                const uint32_t dst = tm + (uint32_t)(buf * P);
 #pragma unroll
-            for (int k = 0; k < 16; ++k) {
-                const int p = j * 16 + k;
-                v[k] = (a.flags & SSM_HAS_INIT) ? a.init[((b * H + h) * P + p) * N + tid] : 0.0f;
+                for (int ks = 0; ks < Q / 16; ++ks)
+                    tc::mma_f16(dst, tc::desc_mn(aB, WB, 16 * ks), tc::desc_mn(aX, WX, 16 * ks), id, ks > 0);
+                tc::commit(bar(sbar, buf));
+                mpend[buf] = par;
+                if (s_abort) { ok = false; break; }
             }
-            tc::tmem_st16(row_addr + j * 16, v);
+            if (!ok) s_abort = 1;
+            // no copy may land and no GEMM may run after exit
+            for (int i = 0; i < 2; ++i) {
+                if (xpend[i] != ~0u) tc::mbar_wait(bar(lbx, i), xpend[i]);
+                if (bpend[i] != ~0u) tc::mbar_wait(bar(lbb, i), bpend[i]);
+                if (mpend[i] != ~0u) tc::mbar_wait(bar(sbar, i), mpend[i]);
+            }
         }
-        tc::tmem_wait_st();
-    }
-    const uint32_t id = tc::idesc_f16(Pk<T>::kFmt, 128, P, true, true);
-    uint32_t phase = 0;
-    bool ok = true;
-    unsigned char* Hout = a.Ht + (size_t)(b * H + h) * a.nc * kTileH;
-    float raw_next = raw_dt(a, b, h, 0, bias);
-    for (int64_t c = 0; c < a.nc && ok; ++c) {
-        const int buf = (int)(c & 1);
-        unsigned char* const sB = sB0 + buf * kTileB;
-        unsigned char* const sX = sX0 + buf * kTileX;
-        const float raw = raw_next;
-        if (c + 1 < a.nc) raw_next = raw_dt(a, b, h, c + 1, bias);   // in flight during this chunk
-        const Steps st = steps_of(a, raw, c, Ah, s_scan);
-        if (tid == Q - 1) s_T = st.cs;
-        if (c > 0) {   // the previous chunk's GEMM read sXW and the other buffers
-            if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(a, 11); ok = false; }
-            phase ^= 1;
+        __syncwarp();
+    } else {
+        const float Ah = a.A[h];
+        const float bias = (a.flags & SSM_HAS_BIAS) ? a.dt_bias[h] : 0.0f;
+        const uint32_t row_addr = tm + ((uint32_t)(warp * 32) << 16);
+        unsigned char* Hout = a.Ht + (size_t)(b * H + h) * nc * kTileH;
+        float hr[P];                            // row n = tid of H^T
+#pragma unroll
+        for (int p = 0; p < P; ++p)
+            hr[p] = (a.flags & SSM_HAS_INIT) ? a.init[((b * H + h) * P + p) * N + tid] : 0.0f;
+        bool ok = true;
+        // emit H_c, then fold in S_c from TMEM buffer c & 1
+        auto consume = [&](int64_t c) -> bool {
+            const int buf = (int)(c & 1);
+            if (!tc::mbar_wait(bar(sbar, buf), (uint32_t)((c >> 1) & 1))) { report(a, 85); return false; }
             tc::fence_after();
-        }
-        ok = __syncthreads_and(ok);
-        if (!ok) break;
-        if (tid == 0 && c + 1 < a.nc) load_chunk(c + 1, buf ^ 1);   // a whole chunk ahead of its use
-        if (!tc::mbar_wait(tc::smem_u32(&lbar[buf]), (uint32_t)((c >> 1) & 1))) { report(a, 13); ok = false; }
-        else if (tid == 0) lpend[buf] = ~0u;
-        ok = __syncthreads_and(ok);
-        if (!ok) break;
-        const float Tc = s_T;
-        const float w = exp2_mufu((Tc - st.cs) * kLog2e) * st.d;
-        // w o X, row s = tid
-#pragma unroll
-        for (int j = 0; j < WX; ++j) {
-            const uint4 q = *reinterpret_cast<const uint4*>(sX + tc::tile_off(tid, j, WX));
-            float f[8];
-            Pk<T>::unpack(q, f);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) f[k] *= w;
-            *reinterpret_cast<uint4*>(sXW + tc::tile_off(tid, j, WX)) = pack8<T>(f);
-        }
-        // emit H_c (row n = tid of H^T), then H^T <- exp(T) H^T; one TMEM round trip
-        {
             unsigned char* out = Hout + (size_t)c * kTileH;
-            const float eT = exp2_mufu(Tc * kLog2e);
-            float v[P / 16][16];
+            const float eT = exp2_mufu(s_T[buf] * kLog2e);
+            float sv[P / 16][16];
 #pragma unroll
-            for (int j = 0; j < P / 16; ++j) tc::tmem_ld16(row_addr + j * 16, v[j]);
-            tc::tmem_wait_ld(v[0]);
+            for (int j = 0; j < P / 16; ++j) tc::tmem_ld16(row_addr + (uint32_t)(buf * P) + j * 16, sv[j]);
+            tc::tmem_wait_ld(sv[0]);
 #pragma unroll
-            for (int j = 1; j < P / 16; ++j) tc::tmem_pin(v[j]);
+            for (int j = 1; j < P / 16; ++j) tc::tmem_pin(sv[j]);
+            tc::fence_before();
+            tc::mbar_arrive(bar(sfree, buf));
 #pragma unroll
             for (int j = 0; j < P / 16; ++j) {
-                *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j, WH)) = pack8<T>(v[j]);
-                *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j + 1, WH)) = pack8<T>(v[j] + 8);
+                *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j, WH)) = pack8<T>(hr + 16 * j);
+                *reinterpret_cast<uint4*>(out + tc::tile_off(tid, 2 * j + 1, WH)) = pack8<T>(hr + 16 * j + 8);
 #pragma unroll
-                for (int k = 0; k < 16; ++k) v[j][k] *= eT;
-                tc::tmem_st16(row_addr + j * 16, v[j]);
+                for (int k = 0; k < 16; ++k) hr[16 * j + k] = fmaf(eT, hr[16 * j + k], sv[j][k]);
             }
-            tc::tmem_wait_st();
-        }
-        tc::fence_async_smem();
-        tc::fence_before();
-        __syncthreads();
-        if (tid == 0) {
-            tc::fence_after();
-            const uint32_t aB = tc::smem_u32(sB), aX = tc::smem_u32(sXW);
+            return true;
+        };
+        float raw_next = raw_dt(a, b, h, 0, bias);
+        for (int64_t c = 0; c < nc && ok; ++c) {
+            const int buf = (int)(c & 1);
+            const float raw = raw_next;
+            if (c + 1 < nc) raw_next = raw_dt(a, b, h, c + 1, bias);   // in flight during this chunk
+            const Steps st = steps_of<kThreads>(a, raw, c, Ah, s_scan);
+            if (tid == Q - 1) s_T[buf] = st.cs;
+            bool w_ok = tc::mbar_wait(bar(lbx, buf), (uint32_t)((c >> 1) & 1));
+            if (!w_ok) report(a, 86);
+            ok = cg_all<kThreads>(w_ok && !s_abort);   // also publishes s_T
+            if (!ok) break;
+            unsigned char* const sX = sX0 + buf * kTileX;
+            const float w = exp2_mufu((s_T[buf] - st.cs) * kLog2e) * st.d;
 #pragma unroll
-            for (int ks = 0; ks < Q / 16; ++ks)
-                tc::mma_f16(tm, tc::desc_mn(aB, WB, 16 * ks), tc::desc_mn(aX, WX, 16 * ks), id, 1u);
-            tc::commit(tc::smem_u32(&mbar));
-        }
-    }
-    if (ok) {
-        if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(a, 12); ok = false; }
-        tc::fence_after();
-    }
-    ok = __syncthreads_and(ok);
-    if (ok) {
-        for (int j = 0; j < P / 16; ++j) {
-            float v[16];
-            tc::tmem_ld16(row_addr + j * 16, v);
-            tc::tmem_wait_ld(v);
+            for (int j = 0; j < WX; ++j) {
+                uint4* q = reinterpret_cast<uint4*>(sX + tc::tile_off(tid, j, WX));
+                float f[8];
+                Pk<T>::unpack(*q, f);
 #pragma unroll
-            for (int k = 0; k < 16; ++k) a.final_state[((b * H + h) * P + j * 16 + k) * N + tid] = v[k];
+                for (int k = 0; k < 8; ++k) f[k] *= w;
+                *q = pack8<T>(f);
+            }
+            tc::fence_async_smem();
+            tc::mbar_arrive(bar(xw, buf));
+            if (c > 0 && !consume(c - 1)) ok = false;
+            ok = cg_all<kThreads>(ok && !s_abort);
         }
-    }
-    if (tid == 0) {                            // no copy may land after exit
-        for (int i = 0; i < 2; ++i)
-            if (lpend[i] != ~0u) tc::mbar_wait(tc::smem_u32(&lbar[i]), lpend[i]);
+        if (ok) ok = consume(nc - 1);
+        ok = cg_all<kThreads>(ok);
+        if (ok) {
+#pragma unroll
+            for (int p = 0; p < P; ++p) a.final_state[((b * H + h) * P + p) * N + tid] = hr[p];
+        } else {
+            s_abort = 1;
+        }
     }
     tc::fence_before();
     __syncthreads();
-    if (warp == 0) tc::tmem_dealloc(tm, 64);
+    if (producer) tc::tmem_dealloc(tm, 128);
 }
 
 // Decay factors for the mask of one head of one chunk, shared by the CTA:
@@ -1320,7 +1358,6 @@ __global__ void reduce_kernel(const Args a, float* dA, float* dbias, float* dD) 
 }
 
 // ------------------------------------------------------------------ host ----
-constexpr size_t kSmemStates = 2 * kTileB + 3 * kTileX;
 constexpr size_t kSmemOutputs = 2 * kTileB + kTileX + kTileH;
 constexpr size_t kSmemDstates = kTileB + 2 * kTileH;
 constexpr size_t kSmemGrads = 4 * kTileB + 3 * kTileX + 2 * kTileH;
@@ -1426,9 +1463,9 @@ static int set_smem(const void* fn, size_t bytes) {
 
 template <typename T>
 static int run_fwd(const Args& a, cudaStream_t s) {
-    if (int e = set_smem((const void*)states_kernel<T>, kSmemStates + kSmemPad)) return e;
+    if (int e = set_smem((const void*)states2_kernel<T>, kSmemStates2 + kSmemPad)) return e;
     if (int e = set_smem((const void*)outputs_kernel<T>, kSmemOutputs + kSmemPad)) return e;
-    states_kernel<T><<<dim3((unsigned)a.nheads, (unsigned)a.batch), kThreads, kSmemStates + kSmemPad, s>>>(a);
+    states2_kernel<T><<<dim3((unsigned)a.nheads, (unsigned)a.batch), kStThreads, kSmemStates2 + kSmemPad, s>>>(a);
     if (int e = check_launch("chunk_scan fwd (tensor cores): states")) return e;
     outputs_kernel<T><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)a.batch), kThreads, kSmemOutputs + kSmemPad, s>>>(a);
     return check_launch("chunk_scan fwd (tensor cores): outputs");
