@@ -185,6 +185,8 @@ def run_scan(args, world, rank, device):
                                            ("u", "delta", "A", "B", "C", "D", "z", "delta_bias", "dout"))
     ops = torch.ops.b200ssm
     bucket = ParamGradBucket([A.shape, D.shape, bias.shape], device)
+    from metal_kernelops_b200.scan import checkpoint_numel
+    saved_bytes = 4 * checkpoint_numel(per, cfg["dim"], cfg["length"], cfg["dstate"], 2, True, args.lean)
 
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
 
@@ -192,11 +194,11 @@ def run_scan(args, world, rank, device):
         e = ev[i] if i is not None else None
         if e:
             e[0].record()
-        y, ck = ops.selective_scan_fwd(u, delta, A, B, C, D, z, bias, True, True)
+        y, ck = ops.selective_scan_fwd(u, delta, A, B, C, D, z, bias, True, True, args.lean)
         if e:
             e[1].record()
         du, dd, dA, dB, dC, dD, dz, db = ops.selective_scan_bwd(dout, u, delta, A, B, C, D, z, bias,
-                                                                ck, True)
+                                                                ck, True, args.lean)
         if e:
             e[2].record()
         if world > 1:
@@ -244,6 +246,8 @@ def run_scan(args, world, rank, device):
     # own pinned host buffers.  The host reads them after the timed steps
     # rather than waiting for each, so the next step's input copies queue
     # behind the previous step's compute (the dependencies are device events).
+    from metal_kernelops_b200 import scan as scan_mod
+    scan_mod.set_lean_backward(args.lean)
     pinned = {k: v.pin_memory() for k, v in host.items()}
     e2e_steps = max(1, min(args.steps, 5))
     names = ("u", "delta", "A", "B", "C", "D", "z", "delta_bias")
@@ -346,6 +350,9 @@ def run_scan(args, world, rank, device):
         "data": "synthetic (seeded, BASELINE config distributions)",
         "config": _scan_config(args, cfg, world),
         "breakdown_ms": {"fwd": fwd_ms, "bwd": bwd_ms, "allreduce": ar_ms},
+        "saved_for_backward": {"mode": "lean (states every 16 steps)" if args.lean else
+                               "states every 4 steps + scan output",
+                               "bytes": saved_bytes},
         "roofline": {"bound": "hbm", "kernel": "selective_scan bwd (bwd_kernel + reduce)",
                      "achieved": bwd_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": bwd_gbs / peaks["hbm_gbs"], "peak_source": peak_kind,
@@ -859,6 +866,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra-ops", action="store_true",
                     help="scan line only (no ssd / decode sub-objects)")
+    ap.add_argument("--lean", action="store_true",
+                    help="scan: the memory-lean backward (states saved every 16 steps, the rest recomputed)")
     args = ap.parse_args()
     world, rank, local = _dist()
     threads = len(os.sched_getaffinity(0))

@@ -51,6 +51,10 @@ typedef enum ssm_dtype {
                                    path applies (bf16/f16, headdim 64, dstate 128)          */
 #define SSM_SCAN_PLAIN   0x2000u /* selective scan: run the plain-staging kernels even where
                                     the TMA-staged ones apply (same results bit for bit)    */
+#define SSM_SCAN_LEAN    0x4000u /* selective scan: the forward saves only the state entering
+                                    every 16-step chunk (4 * dstate bytes per 16 steps, no
+                                    scan output); the backward recomputes the rest.  Pass the
+                                    same flag to the size query, the forward and the backward */
 
 /* Human-readable text for a status code, and the message of the last failure
  * on the calling thread (empty if none). */
@@ -93,9 +97,10 @@ typedef struct ssm_selective_scan_params {
     void* y;
     /* saved for the backward (checkpoint_bytes, 16-byte aligned): the fp32
      * states entering every 4-step sub-block, then (with SSM_HAS_Z) the scan
-     * output before the D skip and the gate in act_dtype.  Written by the
-     * forward and read by the backward (NULL in the forward = inference,
-     * nothing saved) */
+     * output before the D skip and the gate in act_dtype; with SSM_SCAN_LEAN
+     * only the states entering every 16-step chunk.  Written by the forward
+     * and read by the backward (NULL in the forward = inference, nothing
+     * saved) */
     float* checkpoints;
     /* backward */
     const void* dout;

@@ -33,6 +33,7 @@ CONV_SILU = 0x400
 IO_DTYPE = 0x800
 CHANNEL_LAST = 0x1000
 SCAN_PLAIN = 0x2000
+SCAN_LEAN = 0x4000
 
 EXPORTS = (
     "ssm_status_string", "ssm_last_error",

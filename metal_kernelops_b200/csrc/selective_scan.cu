@@ -248,7 +248,7 @@ fwd_kernel(const Args a) {
             continue;
         }
 
-        // the state entering sub-block s (every kTS steps), for the backward;
+        // the state entering sub-block s (every ck_every steps), for the backward;
         // streaming stores, so the saved states do not push the B/C tiles that
         // every CTA of the batch re-reads out of L2
         auto store_ckpt = [&](int64_t s) {
@@ -274,7 +274,7 @@ fwd_kernel(const Args a) {
         float2* vr = dvu + c * FS;
 #pragma unroll 4
         for (int t = 0; t < len; ++t) {
-            if (save && (t % kTS) == 0) store_ckpt((t0 + t) / kTS);
+            if (save && (t & (a.ck_every - 1)) == 0) store_ckpt((t0 + t) / a.ck_every);
             const float2 v = vr[t];
             const float2 dl2 = make_float2(v.x, v.x), du2 = make_float2(v.y, v.y);
             const float4* B4 = reinterpret_cast<const float4*>(Bs + t * NP + sub * NPT);
@@ -301,7 +301,7 @@ fwd_kernel(const Args a) {
         // phase 2: skip, gate, store (two steps per iteration, coalesced along t);
         // with checkpoints and a gate, also the scan output before the skip and
         // the gate (the backward's dz needs it)
-        T* ysv = (a.ckpt != nullptr && has_z)
+        T* ysv = (a.ckpt != nullptr && has_z && !a.lean)
                      ? reinterpret_cast<T*>(reinterpret_cast<char*>(a.ckpt) + a.ysave_off) : nullptr;
         for (int i = tid; i < CPC * (TT / 2); i += kThreads) {
             const int cc = i / (TT / 2), t = 2 * (i % (TT / 2));
@@ -505,7 +505,7 @@ bwd_kernel(const Args a) {
         stage_act<T, CPC, K>(rd, dg, row0, rows, L, t0, len, a.fast);
         if (has_z) stage_act<T, CPC, K>(rz, zg, row0, rows, L, t0, len, a.fast);
         stage_act<T, CPC, K>(rg, gg, row0, rows, L, t0, len, a.fast);
-        if (has_z) stage_act<T, CPC, K>(ry, ysg, row0, rows, L, t0, len, a.fast);
+        if (has_z && !a.lean) stage_act<T, CPC, K>(ry, ysg, row0, rows, L, t0, len, a.fast);
         stage_bc<NP, K>(rbc, a.B, a.bc_dtype, bg, N, L, t0, len, a.fast);
         stage_bc<NP, K>(rbc + NP * (K * 4 + 16), a.C, a.bc_dtype, bg, N, L, t0, len, a.fast);
         cp_async_commit();
@@ -514,8 +514,10 @@ bwd_kernel(const Args a) {
             const int nsb = (len + TS - 1) / TS;
 #pragma unroll
             for (int sb = 0; sb < K / TS; ++sb) {
-                const float* cp = a.ckpt + ((b * a.nsub + tile * (K / TS) + sb) * a.dim + d) * N;
-                const bool live = cvalid && sb < nsb;
+                // lean mode: one saved state per chunk, in slot 0
+                const int64_t s = a.lean ? tile : tile * (K / TS) + sb;
+                const float* cp = a.ckpt + ((b * a.nsub + s) * a.dim + d) * N;
+                const bool live = cvalid && (a.lean ? sb == 0 : sb < nsb);
 #pragma unroll
                 for (int j = 0; j < NH; ++j) {
                     const int n0 = sub * NPT + ((2 * j) ^ pm), n1 = sub * NPT + ((2 * j + 1) ^ pm);
@@ -580,7 +582,28 @@ bwd_kernel(const Args a) {
                 // and spill at this kernel's 3-CTA register budget)
                 float2 xh[TS][NH];
     #pragma unroll
-                for (int j = 0; j < NH; ++j) x2[j] = sck[(sb * NH + j) * kThreads + tid];
+                for (int j = 0; j < NH; ++j) x2[j] = sck[((a.lean ? 0 : sb) * NH + j) * kThreads + tid];
+                if (a.lean) {    // the chunk's entering state, replayed over the sub-blocks before sb
+                    for (int pb = 0; pb < sb; ++pb) {
+    #pragma unroll
+                        for (int jj = 0; jj < TS; ++jj) {
+                            const float2 v = vr[pb * TS + jj];
+                            const float dl = v.x * kLog2e;
+                            const float2 dl2 = make_float2(dl, dl), du2 = make_float2(v.y, v.y);
+                            const float4* B4 = reinterpret_cast<const float4*>(Bp + (pb * TS + jj) * NP);
+    #pragma unroll
+                            for (int qq = 0; qq < NPT / 4; ++qq) {
+                                const float4 bq = B4[qq ^ qx];
+                                const float2 a0 = __fmul2_rn(dl2, An2[2 * qq]);
+                                const float2 a1 = __fmul2_rn(dl2, An2[2 * qq + 1]);
+                                const float2 e0 = make_float2(exp2_mufu(a0.x), exp2_mufu(a0.y));
+                                const float2 e1 = make_float2(exp2_mufu(a1.x), exp2_mufu(a1.y));
+                                x2[2 * qq] = __ffma2_rn(e0, x2[2 * qq], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
+                                x2[2 * qq + 1] = __ffma2_rn(e1, x2[2 * qq + 1], __fmul2_rn(du2, make_float2(bq.z, bq.w)));
+                            }
+                        }
+                    }
+                }
     #pragma unroll
                 for (int jj = 0; jj < TS; ++jj) {
                     if (FULL || jj < nb) {
@@ -599,6 +622,18 @@ bwd_kernel(const Args a) {
                             xh[jj][2 * qq + 1] = x2[2 * qq + 1];
                             x2[2 * qq] = __ffma2_rn(e0, x2[2 * qq], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
                             x2[2 * qq + 1] = __ffma2_rn(e1, x2[2 * qq + 1], __fmul2_rn(du2, make_float2(bq.z, bq.w)));
+                        }
+                        if (a.lean && has_z) {   // the scan output <x_t, C_t> of this step, for dz
+                            const float4* C4 = reinterpret_cast<const float4*>(Cp + (tb + jj) * NP);
+                            float2 acc = make_float2(0.0f, 0.0f);
+    #pragma unroll
+                            for (int qq = 0; qq < NPT / 4; ++qq) {
+                                const float4 cq = C4[qq ^ qx];
+                                acc = __ffma2_rn(x2[2 * qq], make_float2(cq.x, cq.y), acc);
+                                acc = __ffma2_rn(x2[2 * qq + 1], make_float2(cq.z, cq.w), acc);
+                            }
+                            const float yv = sum_low_lanes<LPC>(acc.x + acc.y);
+                            if (sub == 0) stf(&ry[c * K + tb + jj], yv);
                         }
                     }
                 }
@@ -1032,14 +1067,18 @@ static bool aligned16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 
 
 // The checkpoint buffer: the fp32 states entering every kTS-step sub-block,
 // (batch, sub-block, dim, dstate), then, with a gate, the scan output before
-// the skip and the gate, (batch, dim, length) in the activation dtype.
+// the skip and the gate, (batch, dim, length) in the activation dtype.  Lean
+// mode: the states entering every kChunk-step chunk only, (batch, chunk, dim,
+// dstate); the backward recomputes the sub-block states and the scan output.
+static int ck_every(const ssm_selective_scan_params* p) { return (p->flags & SSM_SCAN_LEAN) ? kChunk : kTS; }
 static size_t ckpt_state_bytes(const ssm_selective_scan_params* p) {
-    const int64_t nsub = ceil_div(p->length, kChunk) * (kChunk / kTS);
+    const int64_t nsub = ceil_div(p->length, kChunk) * (kChunk / ck_every(p));
     return align_up((size_t)(p->batch * nsub * p->dim * p->dstate) * 4, 256);
 }
 static size_t ckpt_bytes(const ssm_selective_scan_params* p) {
     const size_t ae = p->act_dtype == SSM_F32 ? 4 : 2;
-    const size_t ysave = (p->flags & SSM_HAS_Z) ? (size_t)(p->batch * p->dim * p->length) * ae : 0;
+    const size_t ysave = ((p->flags & SSM_HAS_Z) && !(p->flags & SSM_SCAN_LEAN))
+                             ? (size_t)(p->batch * p->dim * p->length) * ae : 0;
     return ckpt_state_bytes(p) + align_up(ysave, 256);
 }
 
@@ -1057,7 +1096,9 @@ static void make_args(const ssm_selective_scan_params* p, int cpc, Args& a) {
     a.u = p->u; a.delta = p->delta; a.A = p->A; a.B = p->B; a.C = p->C;
     a.D = p->D; a.z = p->z; a.delta_bias = p->delta_bias;
     a.y = p->y; a.ckpt = p->checkpoints;
-    a.nsub = a.nchunks * (kChunk / kTS);
+    a.ck_every = ck_every(p);
+    a.lean = (p->flags & SSM_SCAN_LEAN) != 0;
+    a.nsub = a.nchunks * (kChunk / a.ck_every);
     a.ck_stride = p->dim * p->dstate;
     a.ysave_off = (int64_t)ckpt_state_bytes(p);
     a.dout = p->dout; a.du = p->du; a.ddelta = p->ddelta; a.dz = p->dz;

@@ -162,7 +162,7 @@ fwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
     const int64_t N = a.dstate, L = a.length;
     const bool has_d = a.flags & SSM_HAS_D, has_z = a.flags & SSM_HAS_Z;
     const bool has_bias = a.flags & SSM_HAS_BIAS, softplus = a.flags & SSM_SOFTPLUS;
-    const bool save_y = a.ckpt != nullptr && has_z;
+    const bool save_y = a.ckpt != nullptr && has_z && !a.lean;
     const int64_t bg = b * a.groups + g;
     const int64_t sx = ((b * a.nseg + seg) * a.dim + d) * N;
     const uint32_t mb = tc::smem_u32(bar);
@@ -199,7 +199,8 @@ fwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
     }
     // this thread's saved states: (batch, sub-block, dim, dstate), 16-byte stores
     const int64_t sub_stride = a.dim * N;
-    float* ck = a.ckpt ? a.ckpt + ((b * a.nsub + tile_lo * (K / kTS)) * a.dim + d) * N + sub * NPT : nullptr;
+    float* ck = a.ckpt ? a.ckpt + ((b * a.nsub + tile_lo * (K / a.ck_every)) * a.dim + d) * N + sub * NPT
+                       : nullptr;
     const bool save = a.ckpt != nullptr && cvalid;
 
     for (int64_t tile = tile_lo; tile < tile_hi; ++tile) {
@@ -266,7 +267,16 @@ fwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
             for (int j = 0; j < NH; j += 2)
                 __stcs(reinterpret_cast<float4*>(cp + 2 * j), make_float4(x2[j].x, x2[j].y, x2[j + 1].x, x2[j + 1].y));
         };
-        if (len == K) {
+        if (a.lean) {                          // the state entering the chunk only
+            if (save) store_ckpt(0);
+            if (len == K) {
+#pragma unroll
+                for (int t = 0; t < K; ++t) step(t);
+            } else {
+#pragma unroll 1
+                for (int t = 0; t < len; ++t) step(t);
+            }
+        } else if (len == K) {
 #pragma unroll
             for (int t = 0; t < K; ++t) {
                 if (t % kTS == 0 && save) store_ckpt(t / kTS);
@@ -279,7 +289,7 @@ fwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
                 step(t);
             }
         }
-        if (ck) ck += (K / kTS) * sub_stride;
+        if (ck) ck += (K / a.ck_every) * sub_stride;
         __syncthreads();
 
         // phase 2: skip and gate; y goes over u, the saved scan output over
@@ -338,7 +348,12 @@ struct BwdTmaLayout {
     static constexpr size_t bytes = o_bar + 32;
 };
 
-template <typename T, int NPT, int LPC>
+// LEAN: the forward saved only the state entering each chunk; each sub-block's
+// entering state is replayed from it (0, 4, 8, 12 extra steps for the four
+// sub-blocks of a chunk), and the scan output before the gate, which dz needs,
+// is recomputed in the sub-block replay into the tile slot the saved output
+// would have used.
+template <typename T, int NPT, int LPC, bool LEAN>
 __global__ void __launch_bounds__(kThreads, 3)
 bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
     const Args& a = ta.a;
@@ -398,7 +413,7 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
     const float* Bp = Bs + (pm & 3) * CS + sub * NPT;
     const float* Cp = Cs + (pm & 3) * CS + sub * NPT;
     const int qx = pm >> 2;
-    const uint32_t tx = (uint32_t)((has_z ? 5 : 3) * CPC * K * sizeof(T) + 2 * NP * K * sizeof(T));
+    const uint32_t tx = (uint32_t)((has_z ? (LEAN ? 4 : 5) : 3) * CPC * K * sizeof(T) + 2 * NP * K * sizeof(T));
 
     auto bufp = [&](int buf, size_t off) { return smem + (size_t)buf * Lay::buf + off; };
     auto issue = [&](int64_t tile, int buf) {   // thread 0: one chunk's input tiles
@@ -410,7 +425,7 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
         tma_load4(tc::smem_u32(bufp(buf, Lay::o_g)), &ta.m_g, t0, (int)dl0, (int)g, (int)b, m);
         if (has_z) {
             tma_load4(tc::smem_u32(bufp(buf, Lay::o_z)), &ta.m_z, t0, (int)dl0, (int)g, (int)b, m);
-            tma_load4(tc::smem_u32(bufp(buf, Lay::o_y)), &ta.m_ys, t0, (int)dl0, (int)g, (int)b, m);
+            if (!LEAN) tma_load4(tc::smem_u32(bufp(buf, Lay::o_y)), &ta.m_ys, t0, (int)dl0, (int)g, (int)b, m);
         }
         tma_load3(tc::smem_u32(bufp(buf, Lay::o_B)), &ta.m_B, t0, 0, (int)bg, m);
         tma_load3(tc::smem_u32(bufp(buf, Lay::o_C)), &ta.m_C, t0, 0, (int)bg, m);
@@ -429,9 +444,10 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
     // filled one sub-block ahead by its own 16-byte copies (zeros for invalid
     // channels); sub-blocks are consumed in decreasing global order, from the
     // CTA's last one down to its first (tile_lo * K / TS)
+    // (LEAN: one saved state per chunk, the same ring one chunk ahead)
     const int last_len = (int)min64(K, L - (tile_hi - 1) * K);
-    const int64_t s_first = (tile_hi - 1) * (K / TS) + (last_len + TS - 1) / TS - 1;
-    int nleft = (int)(s_first - tile_lo * (K / TS));       // sub-blocks still to fetch after the first
+    const int64_t s_first = LEAN ? tile_hi - 1 : (tile_hi - 1) * (K / TS) + (last_len + TS - 1) / TS - 1;
+    int nleft = (int)(s_first - (LEAN ? tile_lo : tile_lo * (K / TS)));   // saved states still to fetch
     int slot = 0;
     const float* ckp = a.ckpt + ((b * a.nsub + s_first) * a.dim + (cvalid ? d : d0)) * N + sub * NPT;
     auto fetch = [&](int sl) {              // the sub-block ckp points at, into slot sl
@@ -530,15 +546,58 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
         }
         __syncthreads();
 
+        T* const ryw = reinterpret_cast<T*>(bufp(buf, Lay::o_y));   // LEAN: recomputed scan output
         auto chunk_body = [&](auto full_tag) {
             constexpr bool FULL = decltype(full_tag)::value;
             float2 x2[NH];
             const float2* vr = dvu + c * FS;
             const float* gr = gs + c * FS;
+            int cslot = 0;
+            if constexpr (LEAN) {     // the chunk's entering state (the next chunk's copy started first)
+                if (nleft > 0) {
+                    ckp -= a.ck_stride;
+                    fetch(slot ^ 1);
+                    --nleft;
+                } else {
+                    tc::cp_async_commit();
+                }
+                tc::cp_async_wait<1>();
+                cslot = slot;
+                slot ^= 1;
+            }
 
             for (int sb = ((FULL ? K : len) - 1) / TS; sb >= 0; --sb) {
                 const int tb = sb * TS;
                 const int nb = FULL ? TS : min(TS, len - tb);
+                if constexpr (LEAN) {
+                    // the chunk's entering state, replayed over the sub-blocks before sb
+                    const float* src = sck + ((size_t)cslot * NQ * kThreads + tid) * 4;
+#pragma unroll
+                    for (int j = 0; j < NH; ++j) {
+                        const int e0 = (2 * j) ^ pm, e1 = (2 * j + 1) ^ pm;
+                        x2[j] = make_float2(src[(e0 >> 2) * kThreads * 4 + (e0 & 3)],
+                                            src[(e1 >> 2) * kThreads * 4 + (e1 & 3)]);
+                    }
+                    for (int pb = 0; pb < sb; ++pb) {
+#pragma unroll
+                        for (int jj = 0; jj < TS; ++jj) {
+                            const float2 v = vr[pb * TS + jj];
+                            const float dl = v.x * kLog2e;
+                            const float2 dl2 = make_float2(dl, dl), du2 = make_float2(v.y, v.y);
+                            const float4* B4 = reinterpret_cast<const float4*>(Bp + (pb * TS + jj) * NP);
+#pragma unroll
+                            for (int qq = 0; qq < NPT / 4; ++qq) {
+                                const float4 bq = B4[qq ^ qx];
+                                const float2 a0 = __fmul2_rn(dl2, An2[2 * qq]);
+                                const float2 a1 = __fmul2_rn(dl2, An2[2 * qq + 1]);
+                                const float2 e0 = make_float2(exp2_mufu(a0.x), exp2_mufu(a0.y));
+                                const float2 e1 = make_float2(exp2_mufu(a1.x), exp2_mufu(a1.y));
+                                x2[2 * qq] = __ffma2_rn(e0, x2[2 * qq], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
+                                x2[2 * qq + 1] = __ffma2_rn(e1, x2[2 * qq + 1], __fmul2_rn(du2, make_float2(bq.z, bq.w)));
+                            }
+                        }
+                    }
+                } else {
                 // this sub-block's entering states (its copies are done: the
                 // next sub-block's are started first)
                 if (nleft > 0) {
@@ -559,6 +618,7 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
                     }
                 }
                 slot ^= 1;
+                }
                 // the replay keeps the states entering each step; the
                 // adjoint recomputes each step's decays (two exponentials per
                 // element-state: a decay history would cost 32 more registers
@@ -582,6 +642,18 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
                             xh[jj][2 * qq + 1] = x2[2 * qq + 1];
                             x2[2 * qq] = __ffma2_rn(e0, x2[2 * qq], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
                             x2[2 * qq + 1] = __ffma2_rn(e1, x2[2 * qq + 1], __fmul2_rn(du2, make_float2(bq.z, bq.w)));
+                        }
+                        if (LEAN && has_z) {   // the scan output <x_t, C_t> of this step, for dz
+                            const float4* C4 = reinterpret_cast<const float4*>(Cp + (tb + jj) * NP);
+                            float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll
+                            for (int qq = 0; qq < NPT / 4; ++qq) {
+                                const float4 cq = C4[qq ^ qx];
+                                acc = __ffma2_rn(x2[2 * qq], make_float2(cq.x, cq.y), acc);
+                                acc = __ffma2_rn(x2[2 * qq + 1], make_float2(cq.z, cq.w), acc);
+                            }
+                            const float yv = sum_low_lanes<LPC>(acc.x + acc.y);
+                            if (sub == 0) stf(&ryw[c * K + tb + jj], yv);
                         }
                     }
                 }
@@ -850,7 +922,7 @@ template <typename T, int NPT, int LPC>
 static int run_bwd_tma(const TmaArgs& ta, cudaStream_t st) {
     constexpr int CPC = 32 / LPC * kWarps;
     const size_t sm = BwdTmaLayout<T, CPC, NPT * LPC, NPT>::bytes + 128;
-    auto k = bwd_tma_kernel<T, NPT, LPC>;
+    auto k = ta.a.lean ? bwd_tma_kernel<T, NPT, LPC, true> : bwd_tma_kernel<T, NPT, LPC, false>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
         return check_launch("selective_scan bwd (TMA): smem attribute");
     const Args& a = ta.a;
@@ -896,7 +968,7 @@ int fwd_tma(const ssm_selective_scan_params* p, const Cfg& c, const Args& a, cud
     if (int s = encode_act(&ta.m_d, p->delta, p, cpc)) return s;
     if (int s = encode_act(&ta.m_z, (p->flags & SSM_HAS_Z) ? p->z : p->u, p, cpc)) return s;
     if (int s = encode_act(&ta.m_o0, p->y, p, cpc)) return s;
-    const void* ys = p->checkpoints ? reinterpret_cast<const char*>(p->checkpoints) + a.ysave_off : p->y;
+    const void* ys = (p->checkpoints && !a.lean) ? reinterpret_cast<const char*>(p->checkpoints) + a.ysave_off : p->y;
     if (int s = encode_act(&ta.m_ys, ys, p, cpc)) return s;
     if (int s = encode_bc(&ta.m_B, p->B, p, np)) return s;
     if (int s = encode_bc(&ta.m_C, p->C, p, np)) return s;
@@ -919,7 +991,7 @@ int bwd_tma(const ssm_selective_scan_params* p, const Cfg& c, const Args& a, cud
     if (int s = encode_act(&ta.m_z, z ? p->z : p->u, p, cpc)) return s;
     if (int s = encode_act(&ta.m_g, p->dout, p, cpc)) return s;
     const void* ys = reinterpret_cast<const char*>(p->checkpoints) + a.ysave_off;
-    if (int s = encode_act(&ta.m_ys, z ? ys : p->u, p, cpc)) return s;
+    if (int s = encode_act(&ta.m_ys, (z && !a.lean) ? ys : p->u, p, cpc)) return s;
     if (int s = encode_bc(&ta.m_B, p->B, p, np)) return s;
     if (int s = encode_bc(&ta.m_C, p->C, p, np)) return s;
     if (int s = encode_act(&ta.m_o0, p->du, p, cpc)) return s;

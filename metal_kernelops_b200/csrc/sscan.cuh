@@ -34,6 +34,8 @@ struct Args {
     void* y; float* ckpt;
     int64_t nsub;         // sub-checkpoints per row: nchunks * kChunk / kTS
     int64_t ck_stride;    // floats between consecutive sub-checkpoints of a row: dim * dstate
+    int ck_every;         // steps between saved states: kTS, or kChunk in the lean mode
+    bool lean;            // SSM_SCAN_LEAN: states every chunk, no saved scan output
     int64_t ysave_off;    // bytes from ckpt to the saved scan output (activation dtype)
     const void* dout; void* du; void* ddelta; void* dz;
     float* dB_part; float* dC_part;   // (batch*groups*nct, dstate, length)

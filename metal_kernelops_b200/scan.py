@@ -38,9 +38,26 @@ CHUNK = 16
 SUB_BLOCK = 4
 """Steps between the states the forward saves for the backward."""
 
-__all__ = ["CHUNK", "selective_scan", "selective_scan_fn", "scan_cuda", "set_tma_staging"]
+__all__ = ["CHUNK", "selective_scan", "selective_scan_fn", "scan_cuda", "set_tma_staging",
+           "set_lean_backward"]
 
 _plain_staging = False
+_lean = False
+
+
+def set_lean_backward(enabled: bool) -> bool:
+    """Choose what the forward saves for the backward.  False (the default):
+    the state entering every SUB_BLOCK steps and, with a gate, the scan output
+    -- 4 * dstate / SUB_BLOCK + 2 bytes per (batch, channel, step) element at
+    bf16 (18 at dstate 16).  True: only the state entering every CHUNK steps
+    (4 at dstate 16); the backward replays the rest from it, at about a
+    quarter more backward time.  Applies to calls made after it; each call's
+    backward follows the mode of its own forward.  Returns the previous
+    setting."""
+    global _lean
+    prev = _lean
+    _lean = bool(enabled)
+    return prev
 
 
 def set_tma_staging(enabled: bool) -> bool:
@@ -54,11 +71,11 @@ def set_tma_staging(enabled: bool) -> bool:
     return prev
 
 
-def _params(u, delta, A, B, C, D, z, delta_bias, softplus):
+def _params(u, delta, A, B, C, D, z, delta_bias, softplus, lean=False):
     batch, dim, length = u.shape
     flags = ((nat.HAS_D if D is not None else 0) | (nat.HAS_Z if z is not None else 0)
              | (nat.HAS_BIAS if delta_bias is not None else 0) | (nat.SOFTPLUS if softplus else 0)
-             | (nat.SCAN_PLAIN if _plain_staging else 0))
+             | (nat.SCAN_PLAIN if _plain_staging else 0) | (nat.SCAN_LEAN if lean else 0))
     p = nat.SelectiveScanParams()
     p.batch, p.dim, p.length = batch, dim, length
     p.groups, p.dstate = B.shape[1], A.shape[1]
@@ -82,8 +99,8 @@ def _sizes(p):
 def _fwd(u: torch.Tensor, delta: torch.Tensor, A: torch.Tensor, B: torch.Tensor,
          C: torch.Tensor, D: Optional[torch.Tensor], z: Optional[torch.Tensor],
          delta_bias: Optional[torch.Tensor], softplus: bool,
-         save: bool) -> tuple[torch.Tensor, torch.Tensor]:
-    p = _params(u, delta, A, B, C, D, z, delta_bias, softplus)
+         save: bool, lean: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
+    p = _params(u, delta, A, B, C, D, z, delta_bias, softplus, lean)
     ck_bytes, _ = _sizes(p)
     fw = nat._SZ()
     nat.check(nat.lib().ssm_selective_scan_fwd_workspace(p, fw), "selective_scan")
@@ -100,20 +117,22 @@ def _fwd(u: torch.Tensor, delta: torch.Tensor, A: torch.Tensor, B: torch.Tensor,
 
 
 def checkpoint_numel(batch: int, dim: int, length: int, dstate: int, act_size: int,
-                     gated: bool) -> int:
+                     gated: bool, lean: bool = False) -> int:
     """fp32 elements of the forward's saved-for-backward buffer (the size
     ``ssm_selective_scan_sizes`` returns): the states entering every
     SUB_BLOCK-step block, then, with a gate, the scan output in the activation
-    dtype, each padded to 256 bytes."""
-    states = batch * (-(-length // CHUNK)) * (CHUNK // SUB_BLOCK) * dim * dstate * 4
-    ybytes = batch * dim * length * act_size if gated else 0
+    dtype, each padded to 256 bytes; in the lean mode the states entering
+    every CHUNK-step chunk only."""
+    every = CHUNK if lean else SUB_BLOCK
+    states = batch * (-(-length // CHUNK)) * (CHUNK // every) * dim * dstate * 4
+    ybytes = batch * dim * length * act_size if gated and not lean else 0
     return (-(-states // 256) * 256 + -(-ybytes // 256) * 256) // 4
 
 
 @_fwd.register_fake
-def _(u, delta, A, B, C, D, z, delta_bias, softplus, save):
+def _(u, delta, A, B, C, D, z, delta_bias, softplus, save, lean=False):
     batch, dim, length = u.shape
-    n = checkpoint_numel(batch, dim, length, A.shape[1], u.element_size(), z is not None) if save else 0
+    n = checkpoint_numel(batch, dim, length, A.shape[1], u.element_size(), z is not None, lean) if save else 0
     return torch.empty_like(u), u.new_empty(n, dtype=torch.float32)
 
 
@@ -121,9 +140,9 @@ def _(u, delta, A, B, C, D, z, delta_bias, softplus, save):
 def _bwd(dout: torch.Tensor, u: torch.Tensor, delta: torch.Tensor, A: torch.Tensor,
          B: torch.Tensor, C: torch.Tensor, D: Optional[torch.Tensor], z: Optional[torch.Tensor],
          delta_bias: Optional[torch.Tensor], ckpt: torch.Tensor,
-         softplus: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
-                                  torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
-    p = _params(u, delta, A, B, C, D, z, delta_bias, softplus)
+         softplus: bool, lean: bool = False) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                                                      torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    p = _params(u, delta, A, B, C, D, z, delta_bias, softplus, lean)
     _, ws_bytes = _sizes(p)
     dev = u.device
     du = torch.empty_like(u)
@@ -150,7 +169,7 @@ def _bwd(dout: torch.Tensor, u: torch.Tensor, delta: torch.Tensor, A: torch.Tens
 
 
 @_bwd.register_fake
-def _(dout, u, delta, A, B, C, D, z, delta_bias, ckpt, softplus):
+def _(dout, u, delta, A, B, C, D, z, delta_bias, ckpt, softplus, lean=False):
     f32 = dict(dtype=torch.float32)
     return (torch.empty_like(u), torch.empty_like(u), A.new_empty(A.shape, **f32),
             B.new_empty(B.shape, **f32), C.new_empty(C.shape, **f32),
@@ -160,10 +179,11 @@ def _(dout, u, delta, A, B, C, D, z, delta_bias, ckpt, softplus):
 
 
 def _setup(ctx, inputs, output):
-    u, delta, A, B, C, D, z, delta_bias, softplus, save = inputs
+    u, delta, A, B, C, D, z, delta_bias, softplus, save = inputs[:10]
     _, ckpt = output
     ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, ckpt)
     ctx.softplus = softplus
+    ctx.lean = bool(inputs[10]) if len(inputs) > 10 else False
     # the saved-states output never receives a gradient: without this, autograd
     # would zero-fill a buffer of its size before every backward
     ctx.set_materialize_grads(False)
@@ -175,12 +195,12 @@ def _backward(ctx, dy, dckpt):
     if ckpt.numel() == 0 and u.numel() != 0:
         raise RuntimeError("selective_scan: the forward did not save its states (save=False)")
     if dy is None:
-        return (None,) * 10
+        return (None,) * 11
     du, ddelta, dA, dB, dC, dD, dz, dbias = _bwd(
-        dy.contiguous(), u, delta, A, B, C, D, z, delta_bias, ckpt, ctx.softplus)
+        dy.contiguous(), u, delta, A, B, C, D, z, delta_bias, ckpt, ctx.softplus, ctx.lean)
     has_d, has_z, has_b = ctx.flags
     return (du, ddelta, dA, dB.to(B.dtype), dC.to(C.dtype),
-            dD if has_d else None, dz if has_z else None, dbias if has_b else None, None, None)
+            dD if has_d else None, dz if has_z else None, dbias if has_b else None, None, None, None)
 
 
 _fwd.register_autograd(_backward, setup_context=_setup)
@@ -247,7 +267,7 @@ def selective_scan(u, dt, A, B, C, D=None, z=None, delta_bias=None, delta_softpl
     save = torch.is_grad_enabled() and any(
         t is not None and t.requires_grad for t in (u, dt, A, B, C, D, z, delta_bias))
     y, _ = torch.ops.b200ssm.selective_scan_fwd(u, dt, A, B, C, D, z, delta_bias,
-                                                bool(delta_softplus), bool(save))
+                                                bool(delta_softplus), bool(save), _lean)
     return y
 
 

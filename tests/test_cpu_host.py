@@ -118,6 +118,14 @@ def test_checkpoint_numel_matches_library_size(shape, gated):
     ck, ws = nat._SZ(), nat._SZ()
     assert lib.ssm_selective_scan_sizes(p, ck, ws) == nat.SSM_OK
     assert checkpoint_numel(batch, dim, length, dstate, esz, gated) * 4 == ck.value
+    # the lean mode: states every 16 steps, no saved scan output
+    p.flags |= nat.SCAN_LEAN
+    assert lib.ssm_selective_scan_sizes(p, ck, ws) == nat.SSM_OK
+    assert checkpoint_numel(batch, dim, length, dstate, esz, gated, lean=True) * 4 == ck.value
+    if length:
+        full = checkpoint_numel(batch, dim, length, dstate, esz, gated)
+        assert ck.value < full * 4
+    p.flags &= ~nat.SCAN_LEAN
     if length and length % 8 == 0 and not gated:   # ss2d: a (height, 8) map, four paths per channel
         q = nat.Ss2dScanParams()
         q.batch, q.channels, q.height, q.width, q.groups, q.dstate = batch, dim, length // 8, 8, 1, dstate

@@ -168,7 +168,7 @@ def _slice_oracle(inp, rows, ch, dout):
     return yr.detach(), dict(zip(NAMES, gr))
 
 
-def _full_size_check(inp, ch, prefix_row, prefix_len):
+def _full_size_check(inp, ch, prefix_row, prefix_len, lean=False):
     """Forward and backward of a full-size bf16 problem on the GPU, then:
 
     * y, du, ddelta, dz of the channels ``ch`` over every batch row, and the
@@ -181,9 +181,14 @@ def _full_size_check(inp, ch, prefix_row, prefix_len):
       those gradients equal the oracle's on that row's prefix over all
       channels, and every other gradient entry is zero."""
     mk = _mk()
+    from metal_kernelops_b200 import scan as scan_mod
     dev = {k: inp[k].cuda().requires_grad_(True) for k in NAMES}
-    y = mk.selective_scan(dev["u"], dev["delta"], dev["A"], dev["B"], dev["C"], D=dev["D"],
-                          z=dev["z"], delta_bias=dev["delta_bias"], delta_softplus=True)
+    prev = scan_mod.set_lean_backward(lean)
+    try:
+        y = mk.selective_scan(dev["u"], dev["delta"], dev["A"], dev["B"], dev["C"], D=dev["D"],
+                              z=dev["z"], delta_bias=dev["delta_bias"], delta_softplus=True)
+    finally:
+        scan_mod.set_lean_backward(prev)
     assert torch.isfinite(y).all()
     g = torch.autograd.grad(y, [dev[k] for k in NAMES], inp["dout"].cuda(), retain_graph=True)
     grads = dict(zip(NAMES, g))
@@ -218,14 +223,21 @@ def test_config1_full_size_slices():
     _full_size_check(inp, slice(100, 132), prefix_row=3, prefix_len=512)
 
 
-def test_config2_full_size_slices():
+@pytest.fixture(scope="module")
+def config2_inputs():
+    from metal_kernelops_b200.workloads import selective_scan_rows
+    return selective_scan_rows(5120, 4096, 16, 1, 1002, 0, 16)
+
+
+@pytest.mark.parametrize("lean", [False, True], ids=["saved_states", "lean"])
+def test_config2_full_size_slices(config2_inputs, lean):
     """BASELINE config 2 -- the bench's headline workload -- at full size
     (B16 D5120 L4096 N16, bf16) on exactly the inputs ``bench.py`` times
     (``workloads.selective_scan_rows``, seed 1002): the launch shape, the
-    saved-state layout and the partial reductions of the timed kernels."""
-    from metal_kernelops_b200.workloads import selective_scan_rows
-    inp = selective_scan_rows(5120, 4096, 16, 1, 1002, 0, 16)
-    _full_size_check(inp, slice(2000, 2032), prefix_row=5, prefix_len=256)
+    saved-state layout and the partial reductions of the timed kernels, in
+    both backward modes (states saved every 4 steps; the lean mode's states
+    every 16 steps with the rest recomputed)."""
+    _full_size_check(config2_inputs, slice(2000, 2032), prefix_row=5, prefix_len=256, lean=lean)
 
 
 def test_errors():
@@ -339,3 +351,48 @@ def test_backward_first_cuda_call_on_a_fresh_thread():
     torch.cuda.synchronize()
     for k in out_main:
         assert torch.equal(out_main[k], out_thr[k]), k
+
+
+@pytest.mark.parametrize("shape,dtype,plain", [
+    ((6, 4096, 128, 16, 1), torch.bfloat16, False),    # TMA path, 8 states x 2 lanes
+    ((2, 64, 256, 16, 1), torch.bfloat16, False),      # TMA path, segments
+    ((2, 24, 1000, 16, 3), torch.float32, False),      # ragged last chunk
+    ((2, 64, 250, 16, 1), torch.bfloat16, True),       # plain path (unaligned rows)
+    ((2, 32, 512, 32, 1), torch.float32, True),        # plain path, 32 states
+])
+def test_lean_backward_matches_saved_states(shape, dtype, plain):
+    """The lean mode saves the state entering every 16-step chunk only and
+    replays the rest in the backward with the same arithmetic: every gradient
+    but dz equals the default mode's bit for bit; dz (from the recomputed
+    scan output, summed in another order) agrees to the activation dtype's
+    rounding; the saved buffer is a quarter of the states and no output."""
+    mk = _mk()
+    from metal_kernelops_b200 import scan as scan_mod
+    b, d, l, n, g = shape
+    inp = orc.selective_scan_inputs(b, d, l, n, g, seed=400 + l, act_dtype=dtype)
+    runs, saved = [], []
+    prev_tma = scan_mod.set_tma_staging(not plain)
+    try:
+        for lean in (False, True):
+            prev = scan_mod.set_lean_backward(lean)
+            try:
+                dev = {k: inp[k].cuda().requires_grad_(True) for k in NAMES}
+                y = mk.selective_scan(dev["u"], dev["delta"], dev["A"], dev["B"], dev["C"], D=dev["D"],
+                                      z=dev["z"], delta_bias=dev["delta_bias"], delta_softplus=True)
+                gr = torch.autograd.grad(y, list(dev.values()), inp["dout"].cuda())
+                runs.append(dict(zip(("y",) + NAMES, [y.detach()] + list(gr))))
+                _, ck = torch.ops.b200ssm.selective_scan_fwd(dev["u"], dev["delta"], dev["A"], dev["B"], dev["C"],
+                                                             dev["D"], dev["z"], dev["delta_bias"], True, True, lean)
+                saved.append(ck.numel())
+            finally:
+                scan_mod.set_lean_backward(prev)
+    finally:
+        scan_mod.set_tma_staging(prev_tma)
+    full, lean_ = runs
+    for k in ("y",) + NAMES:
+        if k == "z":
+            assert orc.norm_rel(lean_[k].float().cpu(), full[k].float().cpu()) <= 1e-2 if dtype != torch.float32 \
+                else orc.norm_rel(lean_[k].cpu(), full[k].cpu()) <= 1e-6, k
+        else:
+            assert torch.equal(lean_[k], full[k]), k
+    assert saved[1] < saved[0] / 3
