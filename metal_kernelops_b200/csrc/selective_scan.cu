@@ -1012,7 +1012,10 @@ __global__ void reduce_kernel(const Args a, float* dB, float* dC, float* dA, flo
 static bool fwd_cfg(int64_t N, int64_t rows, Cfg& c) {
     if (N <= 4) c = {4, 1};
     else if (N <= 8) c = rows >= 49152 ? Cfg{8, 1} : Cfg{4, 2};
-    else if (N <= 16) c = rows >= 24576 ? Cfg{8, 2} : Cfg{4, 4};
+    // from 8192 to 16384 rows the sequence is cut into segments (fwd_plan),
+    // and the wider lane tile with more segments measured faster than 4 x 4
+    // with fewer (batch 2 x 5120 channels: 0.72 -> 0.58 ms)
+    else if (N <= 16) c = (rows >= 24576 || (rows >= 8192 && rows < 16384)) ? Cfg{8, 2} : Cfg{4, 4};
     else if (N <= 32) c = rows >= 24576 ? Cfg{16, 2} : Cfg{8, 4};
     else if (N <= 64) c = {16, 4};
     else return false;
@@ -1021,7 +1024,8 @@ static bool fwd_cfg(int64_t N, int64_t rows, Cfg& c) {
 static bool bwd_cfg(int64_t N, int64_t rows, Cfg& c) {
     if (N <= 4) c = {4, 1};
     else if (N <= 8) c = {8, 1};
-    else if (N <= 16) c = rows >= 16384 ? Cfg{8, 2} : Cfg{4, 4};
+    // from 8192 rows: segments (bwd_plan) rather than a narrower tile
+    else if (N <= 16) c = rows >= 8192 ? Cfg{8, 2} : Cfg{4, 4};
     else if (N <= 32) c = {8, 4};
     else if (N <= 64) c = {8, 8};
     else return false;
@@ -1142,9 +1146,21 @@ static SegPlan fwd_plan(const ssm_selective_scan_params* p, const Cfg& c) {
     const int64_t nct = ceil_div(p->dim / p->groups, 32 / c.lpc * kWarps);
     return plan_segments(nct * p->groups * p->batch, ceil_div(p->length, kChunk), kFwdPerSm);
 }
+// The backward cuts the sequence whenever the grid would not fill every
+// resident slot once, and then aims at about kBwdTargetPerSm CTAs per SM: at
+// batch 2 and 4 x 5120 channels x 4096 steps (the per-GPU share of BASELINE
+// config 2 at 8 and 4 GPUs) that measured 1.47 -> 1.11 ms and 2.24 -> 2.10 ms;
+// the adjoint summary pass it adds costs less than the idle slots it fills.
+constexpr int kBwdTargetPerSm = 8;
 static SegPlan bwd_plan(const ssm_selective_scan_params* p, const Cfg& c) {
     const int64_t nct = ceil_div(p->dim / p->groups, 32 / c.lpc * kWarps);
-    return plan_segments(nct * p->groups * p->batch, ceil_div(p->length, kChunk), kBwdPerSm);
+    const int64_t base = nct * p->groups * p->batch, nchunks = ceil_div(p->length, kChunk);
+    if (p->batch * p->dim < 8192)            // tiny problems (the four-path scan's planes)
+        return plan_segments(base, nchunks, kBwdPerSm);
+    if (base <= 0 || base >= sm_count() * kBwdPerSm || nchunks < 2 * kMinSegChunks) return {1, nchunks};
+    const int64_t want = ceil_div(sm_count() * kBwdTargetPerSm, base);
+    const int64_t sc = max64(ceil_div(nchunks, want), kMinSegChunks);
+    return {ceil_div(nchunks, sc), sc};
 }
 
 // seg_x and seg_p of a plan: (batch, nseg, dim, dstate) fp32 each

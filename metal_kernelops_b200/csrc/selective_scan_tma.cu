@@ -121,7 +121,8 @@ struct FwdTmaLayout {
 // chunks walked in order, one copy of every tile in flight per CTA (a tile's
 // buffer holds its outputs until their stores have read it; nine CTAs share an
 // SM, so copies of one overlap the compute of the others).
-template <typename T, int NPT, int LPC>
+// LEAN: save only the state entering each chunk, and no scan output.
+template <typename T, int NPT, int LPC, bool LEAN>
 __global__ void __launch_bounds__(kThreads, NPT <= 8 ? 9 : 1)
 fwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
     const Args& a = ta.a;
@@ -162,7 +163,7 @@ fwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
     const int64_t N = a.dstate, L = a.length;
     const bool has_d = a.flags & SSM_HAS_D, has_z = a.flags & SSM_HAS_Z;
     const bool has_bias = a.flags & SSM_HAS_BIAS, softplus = a.flags & SSM_SOFTPLUS;
-    const bool save_y = a.ckpt != nullptr && has_z && !a.lean;
+    const bool save_y = a.ckpt != nullptr && has_z && !LEAN;
     const int64_t bg = b * a.groups + g;
     const int64_t sx = ((b * a.nseg + seg) * a.dim + d) * N;
     const uint32_t mb = tc::smem_u32(bar);
@@ -199,7 +200,7 @@ fwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
     }
     // this thread's saved states: (batch, sub-block, dim, dstate), 16-byte stores
     const int64_t sub_stride = a.dim * N;
-    float* ck = a.ckpt ? a.ckpt + ((b * a.nsub + tile_lo * (K / a.ck_every)) * a.dim + d) * N + sub * NPT
+    float* ck = a.ckpt ? a.ckpt + ((b * a.nsub + tile_lo * (LEAN ? 1 : K / kTS)) * a.dim + d) * N + sub * NPT
                        : nullptr;
     const bool save = a.ckpt != nullptr && cvalid;
 
@@ -267,7 +268,7 @@ fwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
             for (int j = 0; j < NH; j += 2)
                 __stcs(reinterpret_cast<float4*>(cp + 2 * j), make_float4(x2[j].x, x2[j].y, x2[j + 1].x, x2[j + 1].y));
         };
-        if (a.lean) {                          // the state entering the chunk only
+        if constexpr (LEAN) {                  // the state entering the chunk only
             if (save) store_ckpt(0);
             if (len == K) {
 #pragma unroll
@@ -289,7 +290,7 @@ fwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
                 step(t);
             }
         }
-        if (ck) ck += (K / a.ck_every) * sub_stride;
+        if (ck) ck += (LEAN ? 1 : K / kTS) * sub_stride;
         __syncthreads();
 
         // phase 2: skip and gate; y goes over u, the saved scan output over
@@ -910,7 +911,7 @@ template <typename T, int NPT, int LPC>
 static int run_fwd_tma(const TmaArgs& ta, cudaStream_t st) {
     constexpr int CPC = 32 / LPC * kWarps;
     const size_t sm = FwdTmaLayout<T, CPC, NPT * LPC>::bytes + 128;
-    auto k = fwd_tma_kernel<T, NPT, LPC>;
+    auto k = ta.a.lean ? fwd_tma_kernel<T, NPT, LPC, true> : fwd_tma_kernel<T, NPT, LPC, false>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
         return check_launch("selective_scan fwd (TMA): smem attribute");
     const Args& a = ta.a;
