@@ -118,8 +118,10 @@ typedef struct ssm_selective_scan_params {
     void* workspace;
     size_t workspace_bytes;
     /* optional device word (NULL: none), the same slot every op's params
-     * carry; this op's kernels have no waits that can give up and never
-     * write it. */
+     * carry: a TMA-staged kernel whose tile wait gives up (a bounded mbarrier
+     * wait) writes its error code here and in the per-device flag that
+     * ssm_take_kernel_error reads; the plain-staging kernels have no such
+     * waits.  Start it at 0. */
     int32_t* status;
 } ssm_selective_scan_params;
 
