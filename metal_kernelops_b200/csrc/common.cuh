@@ -84,29 +84,29 @@ __device__ __forceinline__ float sigmoid_fast(float x) {
     return rcp_mufu(1.0f + exp2_mufu(-x * kLog2e));
 }
 
-// log1p(s) for s in [0, 1] from the area-hyperbolic-tangent series
+// softplus(x) = max(x, 0) + log1p(exp(-|x|)), with torch's threshold rule
+// (x > 20 returns x).  log1p(s) for s = exp(-|x|) in (0, 1] comes from the
+// area-hyperbolic-tangent series
 //   log(1 + s) = 2 artanh(w) = 2 (w + w^3/3 + w^5/5 + ...),  w = s / (2 + s) <= 1/3,
 // truncated after the w^15 term (relative truncation error < 2e-9), so it keeps
-// full relative accuracy for tiny s where log(1 + s) would lose it.
-__device__ __forceinline__ float log1p_unit(float s) {
-    const float w = s * rcp_mufu(2.0f + s);
-    const float w2 = w * w;
-    float p = 1.0f / 15.0f;
-    p = fmaf(p, w2, 1.0f / 13.0f);
-    p = fmaf(p, w2, 1.0f / 11.0f);
-    p = fmaf(p, w2, 1.0f / 9.0f);
-    p = fmaf(p, w2, 1.0f / 7.0f);
-    p = fmaf(p, w2, 1.0f / 5.0f);
-    p = fmaf(p, w2, 1.0f / 3.0f);
-    p = fmaf(p, w2, 1.0f);
-    return 2.0f * w * p;
-}
-
-// softplus(x) = max(x, 0) + log1p(exp(-|x|)), with torch's threshold rule
-// (x > 20 returns x).  Two MUFU ops and ~15 FMA-pipe instructions.
+// full relative accuracy for tiny s where log(1 + s) would lose it.  Every
+// rounding step is an explicit intrinsic, so the paired form below rounds each
+// lane exactly as this one does (no compiler contraction can differ between
+// them).  Two MUFU ops and ~14 FMA-pipe instructions.
 __device__ __forceinline__ float softplus_fast(float x) {
-    if (x > 20.0f) return x;
-    return fmaxf(x, 0.0f) + log1p_unit(exp2_mufu(-fabsf(x) * kLog2e));
+    const float e = exp2_mufu(__fmul_rn(-fabsf(x), kLog2e));
+    const float w = __fmul_rn(e, rcp_mufu(__fadd_rn(2.0f, e)));
+    const float w2 = __fmul_rn(w, w);
+    float p = 1.0f / 15.0f;
+    p = __fmaf_rn(p, w2, 1.0f / 13.0f);
+    p = __fmaf_rn(p, w2, 1.0f / 11.0f);
+    p = __fmaf_rn(p, w2, 1.0f / 9.0f);
+    p = __fmaf_rn(p, w2, 1.0f / 7.0f);
+    p = __fmaf_rn(p, w2, 1.0f / 5.0f);
+    p = __fmaf_rn(p, w2, 1.0f / 3.0f);
+    p = __fmaf_rn(p, w2, 1.0f);
+    const float r = __fmaf_rn(__fadd_rn(w, w), p, fmaxf(x, 0.0f));
+    return x > 20.0f ? x : r;
 }
 // d softplus / dx (torch's backward: 1 above the threshold).
 __device__ __forceinline__ float softplus_grad_fast(float x) {
@@ -151,6 +151,38 @@ __device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 __device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+
+// softplus_fast of two lanes, each rounded exactly as the scalar form rounds it.
+__device__ __forceinline__ float2 softplus2_fast(float2 x) {
+    const float2 e = make_float2(exp2_mufu(__fmul_rn(-fabsf(x.x), kLog2e)),
+                                 exp2_mufu(__fmul_rn(-fabsf(x.y), kLog2e)));
+    const float2 den = add2(f2(2.0f), e);
+    const float2 w = mul2(e, make_float2(rcp_mufu(den.x), rcp_mufu(den.y)));
+    const float2 w2 = mul2(w, w);
+    float2 p = f2(1.0f / 15.0f);
+    p = fma2(p, w2, f2(1.0f / 13.0f));
+    p = fma2(p, w2, f2(1.0f / 11.0f));
+    p = fma2(p, w2, f2(1.0f / 9.0f));
+    p = fma2(p, w2, f2(1.0f / 7.0f));
+    p = fma2(p, w2, f2(1.0f / 5.0f));
+    p = fma2(p, w2, f2(1.0f / 3.0f));
+    p = fma2(p, w2, f2(1.0f));
+    const float2 r = fma2(add2(w, w), p, make_float2(fmaxf(x.x, 0.0f), fmaxf(x.y, 0.0f)));
+    return make_float2(x.x > 20.0f ? x.x : r.x, x.y > 20.0f ? x.y : r.y);
+}
+
+// sigmoid_t<T> of two lanes, each rounded exactly as the scalar form rounds it.
+template <typename T>
+__device__ __forceinline__ float2 sigmoid2_t(float2 a) {
+    if constexpr (sizeof(T) == 4) {
+        const float2 m = mul2(a, f2(-kLog2e));
+        const float2 d = add2(f2(1.0f), make_float2(exp2_mufu(m.x), exp2_mufu(m.y)));
+        return make_float2(rcp_mufu(d.x), rcp_mufu(d.y));
+    } else {
+        const float2 h = mul2(a, f2(0.5f));
+        return fma2(f2(0.5f), make_float2(tanh_mufu(h.x), tanh_mufu(h.y)), f2(0.5f));
+    }
+}
 
 // SiLU of two pre-activations given as halves hp = a / 2 (an exact power-of-two
 // scaling): the values silu_t<T>(a) returns.

@@ -19,8 +19,9 @@
 //    computed from (each element is read and then written by one thread), and
 //    one thread issues a tensor store per tile; the stores clip at the tensor
 //    edges.
-//  * The backward's saved states come through a two-slot ring of per-thread
-//    16-byte cp.async copies, one sub-block ahead, so no thread waits on them.
+//  * The backward's saved states come through a two-slot ring of 16-byte
+//    cp.async copies, one sub-block ahead, each warp copying its own channels'
+//    states in contiguous 512-byte rows, so no thread waits on them.
 //  * Every per-chunk loop runs a compile-time number of iterations with index
 //    arithmetic in shifts and constant offsets.
 //
@@ -223,13 +224,11 @@ fwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
             const int cc = (tid >> 3) + 16 * k, t = 2 * (tid & 7);
             const float2 dr = Io2<T>::ld(&rd[cc * K + t]);
             const float2 ur = Io2<T>::ld(&ru[cc * K + t]);
-            float d0v = dr.x + bch[cc], d1v = dr.y + bch[cc];
-            if (softplus) {
-                d0v = softplus_fast(d0v);
-                d1v = softplus_fast(d1v);
-            }
-            dvu[cc * FS + t] = make_float2(d0v * kLog2e, d0v * ur.x);
-            dvu[cc * FS + t + 1] = make_float2(d1v * kLog2e, d1v * ur.y);
+            float2 dv = add2(dr, f2(bch[cc]));
+            if (softplus) dv = softplus2_fast(dv);
+            const float2 dl = mul2(dv, f2(kLog2e)), du = mul2(dv, ur);
+            dvu[cc * FS + t] = make_float2(dl.x, du.x);
+            dvu[cc * FS + t + 1] = make_float2(dl.y, du.y);
         }
         for (int i = tid; i < NP * K; i += kThreads) {
             const int t = i / NP, n = i % NP;
@@ -293,22 +292,21 @@ fwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
         if (ck) ck += (LEAN ? 1 : K / kTS) * sub_stride;
         __syncthreads();
 
-        // phase 2: skip and gate; y goes over u, the saved scan output over
-        // delta (both dead for this chunk), then one tensor store each
+        // phase 2: skip and gate (two steps per item as paired lanes); y goes
+        // over u, the saved scan output over delta (both dead for this chunk),
+        // then one tensor store each
 #pragma unroll
         for (int k = 0; k < CPC / 16; ++k) {
             const int cc = (tid >> 3) + 16 * k, t = 2 * (tid & 7);
             const float2 ur = Io2<T>::ld(&ru[cc * K + t]);
-            const float y0 = dvu[cc * FS + t].x, y1 = dvu[cc * FS + t + 1].x;
-            if (save_y) Io2<T>::st(&rd[cc * K + t], make_float2(y0, y1));
-            float o0 = fmaf(ur.x, Dch[cc], y0);
-            float o1 = fmaf(ur.y, Dch[cc], y1);
+            const float2 yv = make_float2(dvu[cc * FS + t].x, dvu[cc * FS + t + 1].x);
+            if (save_y) Io2<T>::st(&rd[cc * K + t], yv);
+            float2 o = fma2(ur, f2(Dch[cc]), yv);
             if (has_z) {
                 const float2 zr = Io2<T>::ld(&rz[cc * K + t]);
-                o0 *= zr.x * sigmoid_t<T>(zr.x);
-                o1 *= zr.y * sigmoid_t<T>(zr.y);
+                o = mul2(o, mul2(zr, sigmoid2_t<T>(zr)));
             }
-            Io2<T>::st(&ru[cc * K + t], make_float2(o0, o1));
+            Io2<T>::st(&ru[cc * K + t], o);
         }
         tc::fence_async_smem();
         __syncthreads();
@@ -441,21 +439,33 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
         issue(tile_hi - 1, 0);
     }
 
-    // saved states: a two-slot ring of this thread's NPT states per sub-block,
-    // filled one sub-block ahead by its own 16-byte copies (zeros for invalid
-    // channels); sub-blocks are consumed in decreasing global order, from the
-    // CTA's last one down to its first (tile_lo * K / TS)
-    // (LEAN: one saved state per chunk, the same ring one chunk ahead)
+    // saved states: a two-slot ring of each thread's NPT states per sub-block
+    // (16-byte chunk q of thread tid at [slot][q][tid]), filled one sub-block
+    // ahead; sub-blocks are consumed in decreasing global order, from the CTA's
+    // last one down to its first (tile_lo * K / TS)
+    // (LEAN: one saved state per chunk, the same ring one chunk ahead).
+    // Each warp copies its own channels' states, 512 contiguous bytes per copy
+    // instruction: 16-byte piece k = q * 32 + lane of the warp's CPW x NP floats
+    // goes to the slot of the lane that uses it (zeros for invalid channels).
+    // Lanes then read copies other lanes made: a __syncwarp follows each wait,
+    // and one precedes each refill of a slot the warp has read.
     const int last_len = (int)min64(K, L - (tile_hi - 1) * K);
     const int64_t s_first = LEAN ? tile_hi - 1 : (tile_hi - 1) * (K / TS) + (last_len + TS - 1) / TS - 1;
     int nleft = (int)(s_first - (LEAN ? tile_lo : tile_lo * (K / TS)));   // saved states still to fetch
     int slot = 0;
-    const float* ckp = a.ckpt + ((b * a.nsub + s_first) * a.dim + (cvalid ? d : d0)) * N + sub * NPT;
+    const float* ckp = a.ckpt + ((b * a.nsub + s_first) * a.dim + d0) * N;   // the CTA's first channel
     auto fetch = [&](int sl) {              // the sub-block ckp points at, into slot sl
-        const uint32_t dst = tc::smem_u32(sck + ((size_t)sl * NQ * kThreads + tid) * 4);
+        constexpr int PPC = NP / 4;         // 16-byte pieces per channel
 #pragma unroll
-        for (int q = 0; q < NQ; ++q)
-            tc::cp_async16_zfill(dst + q * kThreads * 16, ckp + 4 * q, cvalid ? 16u : 0u);
+        for (int q = 0; q < NQ; ++q) {
+            const int k = q * 32 + lane;
+            const int cwk = k / PPC, pc = k % PPC;
+            const int ch = warp * CPW + cwk;
+            const uint32_t dst = tc::smem_u32(
+                sck + (((size_t)sl * NQ + pc % NQ) * kThreads + warp * 32 + cwk * LPC + pc / NQ) * 4);
+            const bool ok = ch < rows;
+            tc::cp_async16_zfill(dst, ckp + (ok ? ch * NP + 4 * pc : 0), ok ? 16u : 0u);
+        }
         tc::cp_async_commit();
     };
     fetch(0);
@@ -510,24 +520,22 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
         const T* rB = reinterpret_cast<const T*>(bufp(buf, Lay::o_B));
         const T* rC = reinterpret_cast<const T*>(bufp(buf, Lay::o_C));
 
-        // phase 0: per-step scalars (two steps per item)
+        // phase 0: per-step scalars, two steps per item as the lanes of paired
+        // fp32 instructions (each lane rounds as the scalar form does)
 #pragma unroll
         for (int k = 0; k < CPC / 16; ++k) {
             const int cc = (tid >> 3) + 16 * k, t = 2 * (tid & 7);
             const float2 dr = Io2<T>::ld(&rd[cc * K + t]);
             const float2 ur = Io2<T>::ld(&ru[cc * K + t]);
             float2 go = Io2<T>::ld(&rg[cc * K + t]);
-            float d0v = dr.x + bch[cc], d1v = dr.y + bch[cc];
-            if (softplus) {
-                d0v = softplus_fast(d0v);
-                d1v = softplus_fast(d1v);
-            }
-            dvu[cc * FS + t] = make_float2(d0v, d0v * ur.x);
-            dvu[cc * FS + t + 1] = make_float2(d1v, d1v * ur.y);
+            float2 dv = add2(dr, f2(bch[cc]));
+            if (softplus) dv = softplus2_fast(dv);
+            const float2 du = mul2(dv, ur);
+            dvu[cc * FS + t] = make_float2(dv.x, du.x);
+            dvu[cc * FS + t + 1] = make_float2(dv.y, du.y);
             if (has_z) {
                 const float2 zr = Io2<T>::ld(&rz[cc * K + t]);
-                go.x *= zr.x * sigmoid_t<T>(zr.x);
-                go.y *= zr.y * sigmoid_t<T>(zr.y);
+                go = mul2(go, mul2(zr, sigmoid2_t<T>(zr)));
             }
             gs[cc * FS + t] = go.x;
             gs[cc * FS + t + 1] = go.y;
@@ -555,6 +563,7 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
             const float* gr = gs + c * FS;
             int cslot = 0;
             if constexpr (LEAN) {     // the chunk's entering state (the next chunk's copy started first)
+                __syncwarp();
                 if (nleft > 0) {
                     ckp -= a.ck_stride;
                     fetch(slot ^ 1);
@@ -563,6 +572,7 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
                     tc::cp_async_commit();
                 }
                 tc::cp_async_wait<1>();
+                __syncwarp();
                 cslot = slot;
                 slot ^= 1;
             }
@@ -601,6 +611,7 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
                 } else {
                 // this sub-block's entering states (its copies are done: the
                 // next sub-block's are started first)
+                __syncwarp();
                 if (nleft > 0) {
                     ckp -= a.ck_stride;
                     fetch(slot ^ 1);
@@ -609,6 +620,7 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
                     tc::cp_async_commit();
                 }
                 tc::cp_async_wait<1>();
+                __syncwarp();
                 {
                     const float* src = sck + ((size_t)slot * NQ * kThreads + tid) * 4;
 #pragma unroll
@@ -727,47 +739,46 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
 
         // phase C: element-wise gradients, written over the tiles they came
         // from (du over u, ddelta over delta, dz over z), then tensor stores
+        // (two steps per item as the lanes of paired fp32 instructions; each
+        // lane rounds as the plain-staging kernel's scalar form does)
 #pragma unroll
         for (int k = 0; k < CPC / 16; ++k) {
             const int cc = (tid >> 3) + 16 * k, t = 2 * (tid & 7);
             const int i = tid + kThreads * k;
-            float pD = 0.0f, pb = 0.0f;
             const float2 ur = Io2<T>::ld(&ru[cc * K + t]);
             const float Dv = Dch[cc];
-            float o_du[2], o_dd[2], o_dz[2] = {0.0f, 0.0f};
-            const float uu[2] = {ur.x, ur.y};
-            float2 dr = make_float2(0.0f, 0.0f), zr = make_float2(0.0f, 0.0f), gor = make_float2(0.0f, 0.0f);
-            if (softplus) dr = Io2<T>::ld(&rd[cc * K + t]);
+            const float2 dv = make_float2(dvu[cc * FS + t].x, dvu[cc * FS + t + 1].x);
+            const float2 gv = make_float2(gs[cc * FS + t], gs[cc * FS + t + 1]);
+            const float2 dsum = make_float2(dua[cc * FS + t], dua[cc * FS + t + 1]);
+            const float2 o_du = fma2(dv, dsum, mul2(gv, f2(Dv)));
+            float2 ddt = fma2(ur, dsum, make_float2(dda[cc * FS + t], dda[cc * FS + t + 1]));
+            if (softplus) {                   // softplus' (threshold 20)
+                const float2 xs = add2(Io2<T>::ld(&rd[cc * K + t]), f2(bch[cc]));
+                const float2 sg = sigmoid2_t<T>(xs);
+                ddt = mul2(ddt, make_float2(xs.x > 20.0f ? 1.0f : sg.x, xs.y > 20.0f ? 1.0f : sg.y));
+            }
+            float2 o_dz = make_float2(0.0f, 0.0f);
             if (has_z) {
-                zr = Io2<T>::ld(&rz[cc * K + t]);
-                gor = Io2<T>::ld(&rg[cc * K + t]);
+                const float2 zr = Io2<T>::ld(&rz[cc * K + t]);
+                const float2 sg = sigmoid2_t<T>(zr);
+                const float2 pre = fma2(ur, f2(Dv), Io2<T>::ld(&ry[cc * K + t]));
+                o_dz = mul2(mul2(mul2(Io2<T>::ld(&rg[cc * K + t]), pre), sg),
+                            fma2(zr, fma2(sg, f2(-1.0f), f2(1.0f)), f2(1.0f)));
             }
-            const float draw[2] = {dr.x, dr.y}, zz[2] = {zr.x, zr.y}, gg2[2] = {gor.x, gor.y};
-#pragma unroll
-            for (int kk = 0; kk < 2; ++kk) {
-                const int tt = t + kk;
-                const float2 v = dvu[cc * FS + tt];
-                const float gv = gs[cc * FS + tt];
-                const float duacc = dua[cc * FS + tt];
-                o_du[kk] = fmaf(v.x, duacc, gv * Dv);
-                float ddt = fmaf(uu[kk], duacc, dda[cc * FS + tt]);
-                if (softplus) {
-                    const float xs = draw[kk] + bch[cc];
-                    ddt *= xs > 20.0f ? 1.0f : sigmoid_t<T>(xs);     // softplus' (threshold 20)
+            float pD = 0.0f, pb = 0.0f;
+            if (cc < rows) {
+                if (t < len) {
+                    pD = fmaf(gv.x, ur.x, pD);
+                    pb += ddt.x;
                 }
-                o_dd[kk] = ddt;
-                if (has_z) {
-                    const float sg = sigmoid_t<T>(zz[kk]);
-                    o_dz[kk] = gg2[kk] * fmaf(uu[kk], Dv, ldf(&ry[cc * K + tt])) * sg * fmaf(zz[kk], 1.0f - sg, 1.0f);
-                }
-                if (tt < len && cc < rows) {
-                    pD = fmaf(gv, uu[kk], pD);
-                    pb += ddt;
+                if (t + 1 < len) {
+                    pD = fmaf(gv.y, ur.y, pD);
+                    pb += ddt.y;
                 }
             }
-            Io2<T>::st(&ru[cc * K + t], make_float2(o_du[0], o_du[1]));
-            Io2<T>::st(&rd[cc * K + t], make_float2(o_dd[0], o_dd[1]));
-            if (has_z) Io2<T>::st(&rz[cc * K + t], make_float2(o_dz[0], o_dz[1]));
+            Io2<T>::st(&ru[cc * K + t], o_du);
+            Io2<T>::st(&rd[cc * K + t], ddt);
+            if (has_z) Io2<T>::st(&rz[cc * K + t], o_dz);
             accD[i] += pD;                    // this thread's own slot
             accb[i] += pb;
         }
