@@ -419,8 +419,10 @@ def run_ssd(args, world, rank, device, shape=None):
     from metal_kernelops_b200.parallel import ParamGradBucket, batch_slice
     from metal_kernelops_b200.workloads import ssd_inputs
     cfg = dict(SSD_CONFIG)
-    if shape:
-        cfg["batch"], cfg["length"] = (int(v) for v in shape.split(",")[:2])
+    if shape:   # batch,length[,nheads,headdim,dstate,ngroups]
+        vals = [int(v) for v in shape.split(",")]
+        for k, v in zip(("batch", "length", "nheads", "headdim", "dstate", "ngroups"), vals):
+            cfg[k] = v
     rows = batch_slice(cfg["batch"], rank, world)
     host = ssd_inputs(cfg["batch"], cfg["length"], cfg["nheads"], cfg["headdim"], cfg["dstate"],
                       cfg["ngroups"], seed=cfg["seed"])
@@ -478,7 +480,7 @@ def run_ssd(args, world, rank, device, shape=None):
         "unit": "elem/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16 storage, fp32 compute", "data": "synthetic (seeded, BASELINE config 3)",
-        "config": {"workload": "mamba2 SSD chunk scan fwd+bwd, BASELINE config 3", **cfg,
+        "config": {"workload": "mamba2 SSD chunk scan fwd+bwd, " + ("shape override" if shape else "BASELINE config 3"), **cfg,
                    "batch_per_gpu": b, "parallelism": f"dp{world} (batch shard)",
                    "l2": "x 671 MB > L2, no flush"},
         "breakdown_ms": brk,
@@ -862,7 +864,8 @@ def main():
     ap.add_argument("--op", default="scan", choices=["scan", "ssd", "decode", "ss2d", "conv1d", "gnorm", "block"])
     ap.add_argument("--config", type=int, default=2, choices=[1, 2])
     ap.add_argument("--shape", default=None,
-                    help="batch,dim,seqlen override of the config (profiling runs on small cases)")
+                    help="override of the config (profiling runs, other shapes): scan batch,dim,seqlen; "
+                         "ssd batch,length[,nheads,headdim,dstate,ngroups]")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra-ops", action="store_true",
                     help="scan line only (no ssd / decode sub-objects)")

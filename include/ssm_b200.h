@@ -48,7 +48,8 @@ typedef enum ssm_dtype {
 #define SSM_HAS_DY       0x80u  /* backward: gradient of y given                */
 #define SSM_HAS_DSTATE   0x100u /* backward: gradient of the state output given */
 #define SSM_CUDA_CORES   0x200u /* SSD: run the CUDA-core kernels even where the tensor-core
-                                   path applies (bf16/f16, headdim 64, dstate 128)          */
+                                   path applies (bf16/f16; headdim a multiple of 8 up to 64,
+                                   128 or 256; dstate a multiple of 8 up to 128)            */
 #define SSM_SCAN_PLAIN   0x2000u /* selective scan: run the plain-staging kernels even where
                                     the TMA-staged ones apply (same results bit for bit)    */
 #define SSM_SCAN_LEAN    0x4000u /* selective scan: the forward saves only the state entering

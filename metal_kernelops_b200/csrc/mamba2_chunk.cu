@@ -607,7 +607,7 @@ static int validate(const ssm_chunk_scan_params* p, int mode) {
     if (p->nheads % p->ngroups) return fail(SSM_ERR_INVALID, "chunk_scan: ngroups must divide nheads");
     if (p->dtype < 0 || p->dtype > 2 || p->dt_dtype < 0 || p->dt_dtype > 2)
         return fail(SSM_ERR_UNSUPPORTED, "chunk_scan: unknown dtype");
-    if (pick_q(p->length, p->headdim, p->dstate) == 0)
+    if (!ssdtc::eligible(p) && pick_q(p->length, p->headdim, p->dstate) == 0)
         return fail(SSM_ERR_UNSUPPORTED, "chunk_scan: headdim/dstate too large for the kernels");
     const bool empty = p->batch == 0 || p->length == 0;
     if (mode >= 1 && !empty && (!p->x || !p->dt || !p->A || !p->B || !p->C))

@@ -2,8 +2,11 @@
 //
 // Reference behaviour: src/metal_kernelops/cv/mamba2_chunk.py:617-723 (the
 // public op) and its chunk factorisation :15-31 / :447-533.  This path serves
-// bf16 and f16 inputs with headdim 64 and dstate 128 (the Mamba-2 layer shape);
-// every other case runs the CUDA-core kernels of mamba2_chunk.cu.  The internal
+// bf16 and f16 inputs whose headdim is a multiple of 8 up to 64, or 128 or
+// 256, and whose dstate is a multiple of 8 up to 128; the tiles are
+// 64 columns by 128 states (the Mamba-2 layer shape), smaller shapes fill them
+// with zeros, and a wider head runs as several 64-column virtual heads.  Every
+// other case runs the CUDA-core kernels of mamba2_chunk.cu.  The internal
 // chunk is Q = 128 positions whatever chunk_size the caller asks for (the
 // result does not depend on it).
 //
@@ -68,21 +71,31 @@ constexpr uint32_t kTileH = N * P * 2;
 __device__ int g_kernel_error;
 
 struct Args {
-    int64_t batch, length, nheads, ngroups, nc, hpg;
+    int64_t batch, length, nheads, ngroups, nc;
+    // The tiles are P = 64 columns by N = 128 states.  A head whose headdim is a
+    // multiple of 64 above 64 runs as pr "virtual heads" of 64 columns each
+    // (columns of x, y and of the state are independent, and every gradient
+    // that sums over columns is a sum of the virtual heads' parts); a smaller
+    // headdim (a multiple of 8) and a dstate below 128 (a multiple of 8) fill
+    // the tiles' leading columns / states, the rest reading as zeros.
+    int64_t hv, pr;        // virtual heads (nheads * pr), virtual heads per head (1, 2 or 4)
+    int prs;               // log2(pr): virtual head v belongs to head v >> prs
+    int64_t hpg;           // virtual heads per group
+    int64_t pa, pw, na;    // the caller's headdim, data columns per virtual head (min(pa, 64)), dstate
     int64_t xts;           // elements between tokens of x
     uint32_t flags;
     int dt_dtype;
     const void* x; const void* dt; const float* A; const void* B; const void* C;
     const float* D; const void* z; const float* dt_bias; const float* init;
     void* y; float* final_state;
-    unsigned char* Ht;     // (b, h, c) H_c^T tiles, the state entering chunk c
-    void* ypre;            // (b, l, h, p) pre-gate output, saved when z is given
+    unsigned char* Ht;     // (b, virtual head, c) H_c^T tiles, the state entering chunk c
+    void* ypre;            // (b, l, virtual head, P) pre-gate output, saved when z is given
     const void* dy; const float* dfinal;
     void* dx; float* ddt; float* dB; float* dC; void* dz; float* dinit;
-    unsigned char* dHt;    // (b, h, c) dH_{c+1}^T tiles
-    float* dcs_inter;      // (b, h, nc * Q)
-    float* dT;             // (b, h, nc)
-    float* dA_part; float* db_part; float* dD_part;   // (b, h, nc) [x headdim]
+    unsigned char* dHt;    // (b, virtual head, c) dH_{c+1}^T tiles
+    float* dcs_inter;      // (b, virtual head, nc * Q)
+    float* dT;             // (b, virtual head, nc)
+    float* dA_part; float* db_part; float* dD_part;   // (b, virtual head, nc) [x P]
     int* status;           // the call's optional status word (params.status)
     // TMA descriptors of x, dy (X-like rows) and B, C (B-like rows); see encode_rows()
     alignas(64) CUtensorMap tm_x;
@@ -128,6 +141,29 @@ template <typename T>
 __device__ __forceinline__ uint4 pack8(const float* f) {
     return make_uint4(Pk<T>::pack2(f[0], f[1]), Pk<T>::pack2(f[2], f[3]), Pk<T>::pack2(f[4], f[5]),
                       Pk<T>::pack2(f[6], f[7]));
+}
+
+// Shape accessors.  PAD = false is the tile shape itself (headdim 64, dstate
+// 128: compile-time constants, no virtual heads); PAD = true reads the
+// caller's shape from the arguments.
+template <bool PAD> __device__ __forceinline__ int pw_of(const Args& a) { return PAD ? (int)a.pw : P; }
+template <bool PAD> __device__ __forceinline__ int64_t na_of(const Args& a) { return PAD ? a.na : N; }
+template <bool PAD> __device__ __forceinline__ int64_t head_of(const Args& a, int64_t v) { return PAD ? v >> a.prs : v; }
+
+// Element offsets of virtual head v.  Row of token t in a dense (b, l, heads,
+// headdim) tensor (z, y, dy, dx, dz): virtual head v's columns start at v * pw.
+template <bool PAD>
+__device__ __forceinline__ int64_t row_off(const Args& a, int64_t b, int64_t t, int64_t v) {
+    return (b * a.length + t) * a.nheads * (PAD ? a.pa : P) + v * pw_of<PAD>(a);
+}
+// Row of token t in the saved pre-gate output (internal, P columns per virtual head).
+__device__ __forceinline__ int64_t prow_off(const Args& a, int64_t b, int64_t t, int64_t v) {
+    return ((b * a.length + t) * a.hv + v) * P;
+}
+// Row p (p < pw) of virtual head v in a (b, heads, headdim, dstate) state tensor.
+template <bool PAD>
+__device__ __forceinline__ int64_t state_off(const Args& a, int64_t b, int64_t v, int64_t p) {
+    return ((b * a.hv + v) * pw_of<PAD>(a) + p) * na_of<PAD>(a);
 }
 
 __device__ __forceinline__ float ld_dt(const Args& a, int64_t i) {
@@ -243,7 +279,8 @@ struct Steps {
     float cd;    // running sum of d inside the chunk
     float cs;    // A * cd
 };
-// dt + bias of this thread's position of chunk c (0 beyond the sequence).
+// dt + bias of this thread's position of chunk c (0 beyond the sequence); h is
+// a head of the caller's problem (not a virtual head).
 __device__ __forceinline__ float raw_dt(const Args& a, int64_t b, int64_t h, int64_t c, float bias) {
     const int64_t t = c * Q + threadIdx.x;
     return t < a.length ? ld_dt(a, (b * a.length + t) * a.nheads + h) + bias : 0.0f;
@@ -269,17 +306,18 @@ struct HeadSh {
 template <int NT = kThreads>
 __device__ __forceinline__ void stage_heads(const Args& a, HeadSh& hs, int64_t b, int64_t g, int64_t c,
                                             int64_t hh0, int n) {
-    const int64_t h0 = g * a.hpg + hh0;
+    const int64_t h0 = g * a.hpg + hh0;       // first virtual head
     const bool has_bias = a.flags & SSM_HAS_BIAS;
     if ((int)threadIdx.x < n) {
-        hs.A[threadIdx.x] = a.A[h0 + threadIdx.x];
-        hs.D[threadIdx.x] = ((a.flags & SSM_HAS_D) && !(a.flags & SSM_D_PER_HEAD)) ? a.D[h0 + threadIdx.x] : 0.0f;
+        const int64_t h = (h0 + threadIdx.x) >> a.prs;
+        hs.A[threadIdx.x] = a.A[h];
+        hs.D[threadIdx.x] = ((a.flags & SSM_HAS_D) && !(a.flags & SSM_D_PER_HEAD)) ? a.D[h] : 0.0f;
     }
     for (int i = threadIdx.x; i < n * Q; i += NT) {
         const int pos = i / n, k = i % n;     // consecutive threads: consecutive heads of one position
-        const int64_t t = c * Q + pos;
+        const int64_t t = c * Q + pos, h = (h0 + k) >> a.prs;
         float v = 0.0f;
-        if (t < a.length) v = ld_dt(a, (b * a.length + t) * a.nheads + h0 + k) + (has_bias ? a.dt_bias[h0 + k] : 0.0f);
+        if (t < a.length) v = ld_dt(a, (b * a.length + t) * a.nheads + h) + (has_bias ? a.dt_bias[h] : 0.0f);
         hs.raw[k][pos] = v;
     }
 }
@@ -305,7 +343,7 @@ __device__ __forceinline__ Steps staged_steps(const Args& a, const HeadSh& hs, i
 constexpr int kStThreads = kThreads + 32;
 constexpr size_t kSmemStates2 = 2 * kTileB + 2 * kTileX;
 
-template <typename T>
+template <typename T, bool PAD>
 __global__ void __launch_bounds__(kStThreads, 2) states2_kernel(const __grid_constant__ Args a) {
     extern __shared__ __align__(128) unsigned char sm_raw[];
     unsigned char* const sm = aligned_smem(sm_raw);
@@ -323,8 +361,8 @@ __global__ void __launch_bounds__(kStThreads, 2) states2_kernel(const __grid_con
 
     const int tid = threadIdx.x, warp = tid >> 5;
     const bool producer = warp == kThreads / 32;
-    const int64_t h = blockIdx.x, b = blockIdx.y, g = h / a.hpg;
-    const int64_t H = a.nheads, nc = a.nc;
+    const int64_t h = blockIdx.x, b = blockIdx.y, g = h / a.hpg;   // h: virtual head
+    const int64_t H = a.hv, nc = a.nc;
     auto bar = [](uint64_t* m, int i) { return tc::smem_u32(&m[i]); };
 
     if (tid == 0) {
@@ -398,14 +436,16 @@ __global__ void __launch_bounds__(kStThreads, 2) states2_kernel(const __grid_con
         }
         __syncwarp();
     } else {
-        const float Ah = a.A[h];
-        const float bias = (a.flags & SSM_HAS_BIAS) ? a.dt_bias[h] : 0.0f;
+        const int64_t hh = head_of<PAD>(a, h);  // the caller's head
+        const float Ah = a.A[hh];
+        const float bias = (a.flags & SSM_HAS_BIAS) ? a.dt_bias[hh] : 0.0f;
         const uint32_t row_addr = tm + ((uint32_t)(warp * 32) << 16);
         unsigned char* Hout = a.Ht + (size_t)(b * H + h) * nc * kTileH;
+        const bool nrow = tid < na_of<PAD>(a);  // state n = tid exists (else its row stays 0)
         float hr[P];                            // row n = tid of H^T
 #pragma unroll
         for (int p = 0; p < P; ++p)
-            hr[p] = (a.flags & SSM_HAS_INIT) ? a.init[((b * H + h) * P + p) * N + tid] : 0.0f;
+            hr[p] = ((a.flags & SSM_HAS_INIT) && nrow && p < pw_of<PAD>(a)) ? a.init[state_off<PAD>(a, b, h, p) + tid] : 0.0f;
         bool ok = true;
         // emit H_c, then fold in S_c from TMEM buffer c & 1
         auto consume = [&](int64_t c) -> bool {
@@ -431,11 +471,11 @@ __global__ void __launch_bounds__(kStThreads, 2) states2_kernel(const __grid_con
             }
             return true;
         };
-        float raw_next = raw_dt(a, b, h, 0, bias);
+        float raw_next = raw_dt(a, b, hh, 0, bias);
         for (int64_t c = 0; c < nc && ok; ++c) {
             const int buf = (int)(c & 1);
             const float raw = raw_next;
-            if (c + 1 < nc) raw_next = raw_dt(a, b, h, c + 1, bias);   // in flight during this chunk
+            if (c + 1 < nc) raw_next = raw_dt(a, b, hh, c + 1, bias);   // in flight during this chunk
             const Steps st = steps_of<kThreads>(a, raw, c, Ah, s_scan);
             if (tid == Q - 1) s_T[buf] = st.cs;
             bool w_ok = tc::mbar_wait(bar(lbx, buf), (uint32_t)((c >> 1) & 1));
@@ -460,10 +500,11 @@ __global__ void __launch_bounds__(kStThreads, 2) states2_kernel(const __grid_con
         }
         if (ok) ok = consume(nc - 1);
         ok = cg_all<kThreads>(ok);
-        if (ok) {
+        if (ok && nrow) {
 #pragma unroll
-            for (int p = 0; p < P; ++p) a.final_state[((b * H + h) * P + p) * N + tid] = hr[p];
-        } else {
+            for (int p = 0; p < P; ++p)
+                if (p < pw_of<PAD>(a)) a.final_state[state_off<PAD>(a, b, h, p) + tid] = hr[p];
+        } else if (!ok) {
             s_abort = 1;
         }
     }
@@ -497,7 +538,7 @@ __device__ __forceinline__ void mask_factors(MaskSh& m, const Steps& st) {
 // ====================================================================== F2 ==
 // One CTA per (b, group, chunk).  TMEM: G [0,128), Y intra [128,192),
 // C H^T [192,256).
-template <typename T>
+template <typename T, bool PAD>
 __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant__ Args a) {
     extern __shared__ __align__(128) unsigned char sm_raw[];
     unsigned char* const sm = aligned_smem(sm_raw);
@@ -514,9 +555,10 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
 
     const int tid = threadIdx.x, warp = tid >> 5;
     const int64_t c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
-    const int64_t L = a.length, H = a.nheads;
+    const int64_t H = a.hv;
     const int64_t t0 = c * Q;
-    const int valid = (int)min64(Q, L - t0);
+    const int valid = (int)min64(Q, a.length - t0);
+    const int pw = pw_of<PAD>(a);
     const T* zg = reinterpret_cast<const T*>(a.z);
     T* yg = reinterpret_cast<T*>(a.y);
     T* ypg = reinterpret_cast<T*>(a.ypre);
@@ -634,11 +676,12 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
         }
         // this row's gate inputs, loaded while the GEMMs run (the waits below
         // order every later memory access after them)
-        const int64_t row = ((b * L + t0 + tid) * H + h) * P;
+        const int64_t row = row_off<PAD>(a, b, t0 + tid, h), prow = prow_off(a, b, t0 + tid, h);
         uint4 zr[P / 8];
         if (has_z && tid < valid) {
 #pragma unroll
-            for (int q = 0; q < P / 8; ++q) zr[q] = *reinterpret_cast<const uint4*>(zg + row + 8 * q);
+            for (int q = 0; q < P / 8; ++q)
+                zr[q] = 8 * q < pw ? *reinterpret_cast<const uint4*>(zg + row + 8 * q) : make_uint4(0, 0, 0, 0);
         }
         if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(a, 22); ok = false; }
         phase ^= 1;
@@ -663,13 +706,14 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
                 float yv[16];
 #pragma unroll
                 for (int k = 0; k < 16; ++k) {
-                    const float Dk = has_d ? (d_per_head ? a.D[h * P + 16 * j + k] : Dh) : 0.0f;
+                    const float Dk = has_d ? (d_per_head ? (16 * j + k < pw ? a.D[h * pw + 16 * j + k] : 0.0f) : Dh)
+                                           : 0.0f;
                     yv[k] = fmaf(el, ye[k], yi[k]) + Dk * xv[k];
                 }
                 if (has_z) {
                     if (ypg) {
-                        *reinterpret_cast<uint4*>(ypg + row + 16 * j) = pack8<T>(yv);
-                        *reinterpret_cast<uint4*>(ypg + row + 16 * j + 8) = pack8<T>(yv + 8);
+                        *reinterpret_cast<uint4*>(ypg + prow + 16 * j) = pack8<T>(yv);
+                        *reinterpret_cast<uint4*>(ypg + prow + 16 * j + 8) = pack8<T>(yv + 8);
                     }
                     float zv[16];
                     Pk<T>::unpack(zr[2 * j], zv);
@@ -677,8 +721,8 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
 #pragma unroll
                     for (int k = 0; k < 16; ++k) yv[k] *= zv[k] * sigmoid_f(zv[k]);
                 }
-                *reinterpret_cast<uint4*>(yg + row + 16 * j) = pack8<T>(yv);
-                *reinterpret_cast<uint4*>(yg + row + 16 * j + 8) = pack8<T>(yv + 8);
+                if (16 * j < pw) *reinterpret_cast<uint4*>(yg + row + 16 * j) = pack8<T>(yv);
+                if (16 * j + 8 < pw) *reinterpret_cast<uint4*>(yg + row + 16 * j + 8) = pack8<T>(yv + 8);
             }
         }
         tc::fence_before();
@@ -694,7 +738,7 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
 // One CTA per (b, h), chunks in reverse.  TMEM: dH^T [0,64), C H_c^T [64,128).
 // GATED: z given (a separate instantiation, so that the ungated one carries no
 // registers for the gate inputs it prefetches).
-template <typename T, bool GATED>
+template <typename T, bool GATED, bool PAD>
 __global__ void __launch_bounds__(kThreads) dstates_kernel(const __grid_constant__ Args a) {
     extern __shared__ __align__(128) unsigned char sm_raw[];
     unsigned char* const sm = aligned_smem(sm_raw);
@@ -708,10 +752,12 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const __grid_constant
     __shared__ uint32_t tbase;
 
     const int tid = threadIdx.x, warp = tid >> 5;
-    const int64_t h = blockIdx.x, b = blockIdx.y, g = h / a.hpg;
-    const int64_t L = a.length, H = a.nheads;
-    const float Ah = a.A[h];
-    const float bias = (a.flags & SSM_HAS_BIAS) ? a.dt_bias[h] : 0.0f;
+    const int64_t h = blockIdx.x, b = blockIdx.y, g = h / a.hpg;   // h: virtual head
+    const int64_t L = a.length, H = a.hv, hh = head_of<PAD>(a, h);   // hh: the caller's head
+    const int pw = pw_of<PAD>(a);
+    const bool nrow = tid < na_of<PAD>(a);    // state n = tid exists
+    const float Ah = a.A[hh];
+    const float bias = (a.flags & SSM_HAS_BIAS) ? a.dt_bias[hh] : 0.0f;
     const bool has_z = GATED;
     const T* zg = reinterpret_cast<const T*>(a.z);
     const T* ypg = reinterpret_cast<const T*>(a.ypre);
@@ -737,7 +783,8 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const __grid_constant
         for (int j = 0; j < P / 16; ++j) {
 #pragma unroll
             for (int k = 0; k < 16; ++k)
-                v[k] = (a.flags & SSM_HAS_DSTATE) ? a.dfinal[((b * H + h) * P + j * 16 + k) * N + tid] : 0.0f;
+                v[k] = ((a.flags & SSM_HAS_DSTATE) && nrow && j * 16 + k < pw)
+                           ? a.dfinal[state_off<PAD>(a, b, h, j * 16 + k) + tid] : 0.0f;
             tc::tmem_st16(row_addr + j * 16, v);
         }
         tc::tmem_wait_st();
@@ -747,10 +794,10 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const __grid_constant
     const uint32_t aC = tc::smem_u32(sC), aY = tc::smem_u32(sY);
     uint32_t phase = 0;
     bool ok = true;
-    float raw_next = raw_dt(a, b, h, a.nc - 1, bias);
+    float raw_next = raw_dt(a, b, hh, a.nc - 1, bias);
     for (int64_t c = a.nc - 1; c >= 0 && ok; --c) {
         const float raw = raw_next;
-        if (c > 0) raw_next = raw_dt(a, b, h, c - 1, bias);
+        if (c > 0) raw_next = raw_dt(a, b, hh, c - 1, bias);
         const int64_t t0 = c * Q;
         const int valid = (int)min64(Q, L - t0);
         const uint32_t lpar = (uint32_t)((a.nc - 1 - c) & 1);
@@ -764,13 +811,13 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const __grid_constant
         const Steps st = steps_of(a, raw, c, Ah, s_scan);
         if (tid == Q - 1) s_T = st.cs;
         // the gate inputs of row l = tid, loaded while the tiles land
-        const int64_t row = ((b * L + t0 + tid) * H + h) * P;
+        const int64_t row = row_off<PAD>(a, b, t0 + tid, h), prow = prow_off(a, b, t0 + tid, h);
         uint4 zr[WX], ypr[WX];
         if (has_z && tid < valid) {
 #pragma unroll
             for (int j = 0; j < WX; ++j) {
-                zr[j] = *reinterpret_cast<const uint4*>(zg + row + 8 * j);
-                if (dzg) ypr[j] = *reinterpret_cast<const uint4*>(ypg + row + 8 * j);
+                zr[j] = 8 * j < pw ? *reinterpret_cast<const uint4*>(zg + row + 8 * j) : make_uint4(0, 0, 0, 0);
+                if (dzg) ypr[j] = *reinterpret_cast<const uint4*>(ypg + prow + 8 * j);
             }
         }
         const bool lw = tc::mbar_wait(lb, lpar);
@@ -796,7 +843,7 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const __grid_constant
                         if (dzg) dz[k] = f[k] * yp[k] * sg * fmaf(zv[k], 1.0f - sg, 1.0f);
                         f[k] *= zv[k] * sg;
                     }
-                    if (dzg) *reinterpret_cast<uint4*>(dzg + row + 8 * j) = pack8<T>(dz);
+                    if (dzg && 8 * j < pw) *reinterpret_cast<uint4*>(dzg + row + 8 * j) = pack8<T>(dz);
                 }
 #pragma unroll
                 for (int k = 0; k < 8; ++k) f[k] *= el;
@@ -877,10 +924,11 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const __grid_constant
     if (ok && (a.flags & SSM_HAS_INIT) && a.dinit) {
         for (int j = 0; j < P / 16; ++j) {
             float v[16];
-            tc::tmem_ld16(row_addr + j * 16, v);
+            tc::tmem_ld16(row_addr + j * 16, v);   // all lanes: .sync.aligned
             tc::tmem_wait_ld(v);
 #pragma unroll
-            for (int k = 0; k < 16; ++k) a.dinit[((b * H + h) * P + j * 16 + k) * N + tid] = v[k];
+            for (int k = 0; k < 16; ++k)
+                if (nrow && j * 16 + k < pw) a.dinit[state_off<PAD>(a, b, h, j * 16 + k) + tid] = v[k];
         }
     }
     tc::fence_before();
@@ -936,7 +984,7 @@ struct GradSh {
     float T[2];
 };
 
-template <typename T>
+template <typename T, bool PAD>
 __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_constant__ Args a) {
     extern __shared__ __align__(128) unsigned char sm_raw[];
     unsigned char* const sm = aligned_smem(sm_raw);
@@ -959,8 +1007,9 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
     const int q = warp & 3, hf = (warp >> 2) & 1;      // TMEM quadrant, column half
     const int r = q * 32 + lane;                       // TMEM row / tile row of this thread
     const int64_t c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
-    const int64_t L = a.length, H = a.nheads, G = a.ngroups;
-    (void)G;
+    const int64_t L = a.length, H = a.hv, G = a.ngroups;
+    const int pw = pw_of<PAD>(a);
+    const int64_t na = na_of<PAD>(a);
     const int64_t t0 = c * Q;
     const int valid = (int)min64(Q, L - t0);
     const T* xg = reinterpret_cast<const T*>(a.x);
@@ -1079,6 +1128,8 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
         if (tid == Q - 1) sh.T[0] = st.cs;
         mask_factors<kGC>(sh.m, st);
         const int j0 = hf * (WX / 2);              // this thread's half of an X-like row (chunks)
+        float ddt_acc = 0.0f;
+        (void)ddt_acc;
         for (int64_t hh = 0; hh < a.hpg; ++hh) {
             const uint32_t par = (uint32_t)(hh & 1);
             const int64_t h = g * a.hpg + hh;
@@ -1087,8 +1138,8 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
             const float Ah = sh.hs.A[hk];
             const float Dh = sh.hs.D[hk];
             const float Tc = sh.T[hh & 1];
-            const int64_t grow = ((b * L + t0 + r) * H + h) * P;   // row r of dy / dx / z
-            const int64_t xrow = (b * L + t0 + r) * a.xts + h * P;  // row r of x
+            const int64_t grow = row_off<PAD>(a, b, t0 + r, h);     // row r of dx / z
+            const int64_t xrow = (b * L + t0 + r) * a.xts + h * pw;  // row r of x
             {
                 const bool lw = tc::mbar_wait(bar(kLh), par);   // this head's tiles
                 if (!lw) report(a, 45);
@@ -1097,7 +1148,7 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
                 if (!ok) break;
             }
             if (has_z && r < valid) {               // gate dy in place, own row half
-                for (int j = j0; j < j0 + WX / 2; ++j) {
+                for (int j = j0; j < j0 + WX / 2 && 8 * j < pw; ++j) {
                     float f[8], zv[8];
                     Pk<T>::unpack(*reinterpret_cast<const uint4*>(sY + tc::tile_off(r, j, WX)), f);
                     Pk<T>::unpack(*reinterpret_cast<const uint4*>(zg + grow + 8 * j), zv);
@@ -1210,7 +1261,8 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
                 const bool live = r < valid;
 #pragma unroll
                 for (int j = 0; j < WX / 2; ++j)
-                    xr[j] = live ? *reinterpret_cast<const uint4*>(xg + xrow + 8 * (j0 + j)) : make_uint4(0, 0, 0, 0);
+                    xr[j] = live && 8 * (j0 + j) < pw ? *reinterpret_cast<const uint4*>(xg + xrow + 8 * (j0 + j))
+                                                      : make_uint4(0, 0, 0, 0);
             }
             const float dci = pos_thread ? a.dcs_inter[bhc * Q + tid] : 0.0f;
             const float dTc = tid == Q - 1 ? a.dT[bhc] : 0.0f;
@@ -1258,12 +1310,12 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
 #pragma unroll
                     for (int k = 0; k < 16; ++k) {
                         vpart = fmaf(xv[k], zz[k], vpart);
-                        const float Dk = has_d ? (d_per_head ? a.D[h * P + col + k] : Dh) : 0.0f;
+                        const float Dk = has_d ? (d_per_head ? (col + k < pw ? a.D[h * pw + col + k] : 0.0f) : Dh) : 0.0f;
                         dxv[k] = fmaf(d_s * eTs, zz[k], di[k]) + Dk * yv[k];   // Mh already carries d_s
                     }
                     if (s < valid) {
-                        *reinterpret_cast<uint4*>(dxg + grow + col) = pack8<T>(dxv);
-                        *reinterpret_cast<uint4*>(dxg + grow + col + 8) = pack8<T>(dxv + 8);
+                        if (col < pw) *reinterpret_cast<uint4*>(dxg + grow + col) = pack8<T>(dxv);
+                        if (col + 8 < pw) *reinterpret_cast<uint4*>(dxg + grow + col + 8) = pack8<T>(dxv + 8);
                     }
                 }
                 sh.vp[hf][s] = vpart * eTs;
@@ -1287,7 +1339,15 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
             const float suffix = block_suffix_scan<kGC>(dcs, sh.scan);
             const float dd = fmaf(Ah, suffix, dd_direct);
             const float ddt = (a.flags & SSM_SOFTPLUS) ? dd * softplus_grad_f(st.raw) : dd;
-            if (pos_thread && tid < valid) a.ddt[(b * L + t0 + tid) * H + h] = ddt;
+            if constexpr (PAD) {
+                // a head's virtual heads are consecutive here: their d dt parts add up
+                const int64_t vk = h & (a.pr - 1);
+                ddt_acc = vk == 0 ? ddt : ddt_acc + ddt;
+                if (vk == a.pr - 1 && pos_thread && tid < valid)
+                    a.ddt[(b * L + t0 + tid) * a.nheads + (h >> a.prs)] = ddt_acc;
+            } else if (pos_thread && tid < valid) {
+                a.ddt[(b * L + t0 + tid) * a.nheads + h] = ddt;
+            }
             const float dA_sum = block_sum<kGC>(pos_thread ? dcs * st.cd : 0.0f, sh.scan);
             const float db_sum = block_sum<kGC>(pos_thread && tid < valid ? ddt : 0.0f, sh.scan);
             if (tid == 0) {
@@ -1300,8 +1360,8 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
         if (ok) {
             // dC rows l, dB rows s (fp32, valid rows only), this thread's column half
             const bool live = r < valid;
-            float* dCr = a.dC + ((b * L + t0 + (live ? r : 0)) * G + g) * N;
-            float* dBr = a.dB + ((b * L + t0 + (live ? r : 0)) * G + g) * N;
+            float* dCr = a.dC + ((b * L + t0 + (live ? r : 0)) * G + g) * na;
+            float* dBr = a.dB + ((b * L + t0 + (live ? r : 0)) * G + g) * na;
             for (int jj = 0; jj < N / 32; ++jj) {
                 const int col = 64 * hf + 16 * jj;
                 float vc[16], vb[16];
@@ -1312,6 +1372,7 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
                 if (live) {
 #pragma unroll
                     for (int k = 0; k < 16; k += 4) {
+                        if (col + k >= na) break;     // dstate is a multiple of 8
                         *reinterpret_cast<float4*>(dCr + col + k) = make_float4(vc[k], vc[k + 1], vc[k + 2], vc[k + 3]);
                         *reinterpret_cast<float4*>(dBr + col + k) = make_float4(vb[k], vb[k + 1], vb[k + 2], vb[k + 3]);
                     }
@@ -1328,11 +1389,11 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
     if (mma_warp) tc::tmem_dealloc(tm, 512);
 }
 
-// dA, d dt_bias, dD over (batch, chunk), fixed order.
+// dA, d dt_bias, dD over (batch, chunk, the head's virtual heads), fixed order.
 __global__ void reduce_kernel(const Args a, float* dA, float* dbias, float* dD) {
-    const int64_t H = a.nheads;
+    const int64_t H = a.nheads, HV = a.hv, pr = a.pr;
     const bool has_d = a.flags & SSM_HAS_D, d_per_head = a.flags & SSM_D_PER_HEAD;
-    const int64_t nd = has_d ? (d_per_head ? H * P : H) : 0;
+    const int64_t nd = has_d ? (d_per_head ? H * a.pa : H) : 0;
     const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (i >= 2 * H + nd) return;
     float s = 0.0f;
@@ -1340,18 +1401,21 @@ __global__ void reduce_kernel(const Args a, float* dA, float* dbias, float* dD) 
         const int64_t h = i % H;
         const float* src = i < H ? a.dA_part : a.db_part;
         for (int64_t b = 0; b < a.batch; ++b)
-            for (int64_t c = 0; c < a.nc; ++c) s += src[(b * H + h) * a.nc + c];
+            for (int64_t k = 0; k < pr; ++k)
+                for (int64_t c = 0; c < a.nc; ++c) s += src[(b * HV + h * pr + k) * a.nc + c];
         if (i < H) dA[h] = s;
         else if (dbias) dbias[h] = s;
     } else {
         const int64_t k = i - 2 * H;
         if (d_per_head) {
-            const int64_t h = k / P, p = k % P;
+            const int64_t h = k / a.pa, pc = k % a.pa;
+            const int64_t v = h * pr + pc / a.pw, p = pc % a.pw;   // virtual head, its column
             for (int64_t b = 0; b < a.batch; ++b)
-                for (int64_t c = 0; c < a.nc; ++c) s += a.dD_part[((b * H + h) * a.nc + c) * P + p];
+                for (int64_t c = 0; c < a.nc; ++c) s += a.dD_part[((b * HV + v) * a.nc + c) * P + p];
         } else {
             for (int64_t b = 0; b < a.batch; ++b)
-                for (int64_t c = 0; c < a.nc; ++c) s += a.dD_part[(b * H + k) * a.nc + c];
+                for (int64_t kk = 0; kk < pr; ++kk)
+                    for (int64_t c = 0; c < a.nc; ++c) s += a.dD_part[(b * HV + k * pr + kk) * a.nc + c];
         }
         dD[k] = s;
     }
@@ -1362,26 +1426,31 @@ constexpr size_t kSmemOutputs = 2 * kTileB + kTileX + kTileH;
 constexpr size_t kSmemDstates = kTileB + 2 * kTileH;
 constexpr size_t kSmemGrads = 4 * kTileB + 3 * kTileX + 2 * kTileH;
 
+// bf16 / f16 with a headdim that is a multiple of 8 up to 64, or 128 or 256
+// (two or four virtual heads), and a dstate that is a multiple of 8 up to 128.
 bool eligible(const ssm_chunk_scan_params* p) {
-    return (p->dtype == SSM_BF16 || p->dtype == SSM_F16) && p->headdim == P && p->dstate == N &&
+    const int64_t pa = p->headdim, na = p->dstate;
+    const bool pd = (pa >= 8 && pa <= P && pa % 8 == 0) || pa == 2 * P || pa == 4 * P;
+    return (p->dtype == SSM_BF16 || p->dtype == SSM_F16) && pd && na >= 8 && na <= N && na % 8 == 0 &&
            !(p->flags & SSM_CUDA_CORES);
 }
+static int64_t virt_per_head(const ssm_chunk_scan_params* p) { return p->headdim > P ? p->headdim / P : 1; }
 
 static int64_t n_chunks(const ssm_chunk_scan_params* p) { return ceil_div(p->length, (int64_t)Q); }
 
 struct Saved { size_t ht, yp, total; };
 static Saved saved_layout(const ssm_chunk_scan_params* p) {
     Saved s;
-    const int64_t BH = p->batch * p->nheads;
+    const int64_t BH = p->batch * p->nheads * virt_per_head(p);
     s.ht = align_up((size_t)(BH * n_chunks(p)) * kTileH, 256);
-    s.yp = (p->flags & SSM_HAS_Z) ? align_up((size_t)(p->batch * p->length * p->nheads * P) * 2, 256) : 0;
+    s.yp = (p->flags & SSM_HAS_Z) ? align_up((size_t)(BH * p->length * P) * 2, 256) : 0;
     s.total = s.ht + s.yp;
     return s;
 }
 struct Ws { size_t dh, dci, dt, part, dd, total; };
 static Ws ws_layout(const ssm_chunk_scan_params* p) {
     Ws w;
-    const int64_t BH = p->batch * p->nheads, nc = n_chunks(p);
+    const int64_t BH = p->batch * p->nheads * virt_per_head(p), nc = n_chunks(p);
     w.dh = align_up((size_t)(BH * nc) * kTileH, 256);
     w.dci = align_up((size_t)(BH * nc * Q) * 4, 256);
     w.dt = align_up((size_t)(BH * nc) * 4, 256);
@@ -1398,9 +1467,12 @@ void sizes(const ssm_chunk_scan_params* p, size_t* saved_bytes, size_t* workspac
 
 static void make_args(const ssm_chunk_scan_params* p, Args& a) {
     a.batch = p->batch; a.length = p->length; a.nheads = p->nheads; a.ngroups = p->ngroups;
-    a.nc = n_chunks(p); a.hpg = p->nheads / p->ngroups;
+    a.nc = n_chunks(p);
+    a.pr = virt_per_head(p); a.prs = a.pr == 4 ? 2 : a.pr == 2 ? 1 : 0;
+    a.hv = p->nheads * a.pr; a.hpg = p->nheads / p->ngroups * a.pr;
+    a.pa = p->headdim; a.pw = min64(p->headdim, P); a.na = p->dstate;
     a.flags = p->flags; a.dt_dtype = p->dt_dtype;
-    a.xts = p->x_token_stride ? p->x_token_stride : p->nheads * P;
+    a.xts = p->x_token_stride ? p->x_token_stride : p->nheads * p->headdim;
     a.x = p->x; a.dt = p->dt; a.A = p->A; a.B = p->B; a.C = p->C; a.D = p->D; a.z = p->z;
     a.dt_bias = p->dt_bias; a.init = p->initial_states;
     a.y = p->y; a.final_state = p->final_state;
@@ -1431,12 +1503,13 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 // Tensor map over the rows of a (batch, length, heads, width) bf16/f16 tensor
-// (x, dy: heads = nheads, width = headdim; B, C: heads = ngroups, width =
-// dstate) as the 5-D view (8 elements, row in the batch, 16-byte chunk, batch,
-// head): a box of (8, 8, width / 8, 1, 1) is one 8-row group of core matrices
-// of a tile (tile_off layout), and rows past `length` read as zeros.
+// (x, dy: heads = virtual heads, width = their data columns; B, C: heads =
+// ngroups, width = dstate) as the 5-D view (8 elements, row in the batch,
+// 16-byte chunk, batch, head): a box of (8, 8, tile_width / 8, 1, 1) is one
+// 8-row group of core matrices of a tile (tile_off layout); rows past
+// `length` and chunks past `width` read as zeros.
 static int encode_rows(CUtensorMap* m, const void* base, int dtype, int64_t batch, int64_t length, int64_t heads,
-                       int64_t width, int64_t token_stride = 0) {
+                       int64_t width, int64_t tile_width, int64_t token_stride = 0) {
     auto enc = tensor_map_encoder();
     if (!enc) return fail(SSM_ERR_CUDA, "chunk_scan (tensor cores): cuTensorMapEncodeTiled unavailable");
     if (int s = ensure_context("chunk_scan (tensor cores)")) return s;
@@ -1444,7 +1517,7 @@ static int encode_rows(CUtensorMap* m, const void* base, int dtype, int64_t batc
     cuuint64_t dim[5] = {8, (cuuint64_t)length, (cuuint64_t)(width / 8), (cuuint64_t)batch, (cuuint64_t)heads};
     const int64_t ts = token_stride ? token_stride : heads * width;   // elements between tokens
     cuuint64_t str[4] = {(cuuint64_t)ts * es, 16, (cuuint64_t)(length * ts) * es, (cuuint64_t)width * es};
-    cuuint32_t box[5] = {8, 8, (cuuint32_t)(width / 8), 1, 1};
+    cuuint32_t box[5] = {8, 8, (cuuint32_t)(tile_width / 8), 1, 1};
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     const CUresult r = enc(m, dtype == SSM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
                            const_cast<void*>(base), dim, str, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -1461,33 +1534,45 @@ static int set_smem(const void* fn, size_t bytes) {
     return SSM_OK;
 }
 
-template <typename T>
+template <typename T, bool PAD>
 static int run_fwd(const Args& a, cudaStream_t s) {
-    if (int e = set_smem((const void*)states2_kernel<T>, kSmemStates2 + kSmemPad)) return e;
-    if (int e = set_smem((const void*)outputs_kernel<T>, kSmemOutputs + kSmemPad)) return e;
-    states2_kernel<T><<<dim3((unsigned)a.nheads, (unsigned)a.batch), kStThreads, kSmemStates2 + kSmemPad, s>>>(a);
+    if (int e = set_smem((const void*)states2_kernel<T, PAD>, kSmemStates2 + kSmemPad)) return e;
+    if (int e = set_smem((const void*)outputs_kernel<T, PAD>, kSmemOutputs + kSmemPad)) return e;
+    states2_kernel<T, PAD><<<dim3((unsigned)a.hv, (unsigned)a.batch), kStThreads, kSmemStates2 + kSmemPad, s>>>(a);
     if (int e = check_launch("chunk_scan fwd (tensor cores): states")) return e;
-    outputs_kernel<T><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)a.batch), kThreads, kSmemOutputs + kSmemPad, s>>>(a);
+    outputs_kernel<T, PAD><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)a.batch), kThreads, kSmemOutputs + kSmemPad, s>>>(a);
     return check_launch("chunk_scan fwd (tensor cores): outputs");
 }
 
-template <typename T>
+template <typename T, bool PAD>
 static int run_bwd(const Args& a, const ssm_chunk_scan_params* p, cudaStream_t s) {
-    if (int e = set_smem((const void*)dstates_kernel<T, false>, kSmemDstates + kSmemPad)) return e;
-    if (int e = set_smem((const void*)dstates_kernel<T, true>, kSmemDstates + kSmemPad)) return e;
-    if (int e = set_smem((const void*)grads_kernel<T>, kSmemGrads + kSmemPad)) return e;
+    if (int e = set_smem((const void*)dstates_kernel<T, false, PAD>, kSmemDstates + kSmemPad)) return e;
+    if (int e = set_smem((const void*)dstates_kernel<T, true, PAD>, kSmemDstates + kSmemPad)) return e;
+    if (int e = set_smem((const void*)grads_kernel<T, PAD>, kSmemGrads + kSmemPad)) return e;
     if (a.flags & SSM_HAS_Z)
-        dstates_kernel<T, true><<<dim3((unsigned)a.nheads, (unsigned)a.batch), kThreads, kSmemDstates + kSmemPad, s>>>(a);
+        dstates_kernel<T, true, PAD><<<dim3((unsigned)a.hv, (unsigned)a.batch), kThreads, kSmemDstates + kSmemPad, s>>>(a);
     else
-        dstates_kernel<T, false><<<dim3((unsigned)a.nheads, (unsigned)a.batch), kThreads, kSmemDstates + kSmemPad, s>>>(a);
+        dstates_kernel<T, false, PAD><<<dim3((unsigned)a.hv, (unsigned)a.batch), kThreads, kSmemDstates + kSmemPad, s>>>(a);
     if (int e = check_launch("chunk_scan bwd (tensor cores): dstates")) return e;
-    grads_kernel<T><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)a.batch), kGradThreads, kSmemGrads + kSmemPad, s>>>(a);
+    grads_kernel<T, PAD><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)a.batch), kGradThreads, kSmemGrads + kSmemPad, s>>>(a);
     if (int e = check_launch("chunk_scan bwd (tensor cores): grads")) return e;
     const bool has_d = p->flags & SSM_HAS_D, d_per_head = p->flags & SSM_D_PER_HEAD;
-    const int64_t total = 2 * p->nheads + (has_d ? (d_per_head ? p->nheads * P : p->nheads) : 0);
+    const int64_t total = 2 * p->nheads + (has_d ? (d_per_head ? p->nheads * p->headdim : p->nheads) : 0);
     reduce_kernel<<<(unsigned)ceil_div(total, (int64_t)128), 128, 0, s>>>(
         a, p->dA, (p->flags & SSM_HAS_BIAS) ? p->ddt_bias : nullptr, has_d ? p->dD : nullptr);
     return check_launch("chunk_scan bwd (tensor cores): reduce");
+}
+
+// The tile shape itself (headdim 64, dstate 128) runs kernels with that shape
+// compiled in; every other eligible shape the padded / virtual-head ones.
+static bool padded(const Args& a) { return !(a.pa == P && a.na == N); }
+template <typename T>
+static int run_fwd_any(const Args& a, cudaStream_t s) {
+    return padded(a) ? run_fwd<T, true>(a, s) : run_fwd<T, false>(a, s);
+}
+template <typename T>
+static int run_bwd_any(const Args& a, const ssm_chunk_scan_params* p, cudaStream_t s) {
+    return padded(a) ? run_bwd<T, true>(a, p, s) : run_bwd<T, false>(a, p, s);
 }
 
 int fwd(const ssm_chunk_scan_params* p, cudaStream_t s) {
@@ -1497,10 +1582,10 @@ int fwd(const ssm_chunk_scan_params* p, cudaStream_t s) {
         return fail(SSM_ERR_INVALID, "chunk_scan fwd (tensor cores): x, B, C, z, y and saved must be 16-byte aligned");
     Args a;
     make_args(p, a);
-    if (int e = encode_rows(&a.tm_x, p->x, p->dtype, p->batch, p->length, p->nheads, P, p->x_token_stride)) return e;
-    if (int e = encode_rows(&a.tm_B, p->B, p->dtype, p->batch, p->length, p->ngroups, N, p->bc_token_stride)) return e;
-    if (int e = encode_rows(&a.tm_C, p->C, p->dtype, p->batch, p->length, p->ngroups, N, p->bc_token_stride)) return e;
-    return p->dtype == SSM_BF16 ? run_fwd<__nv_bfloat16>(a, s) : run_fwd<__half>(a, s);
+    if (int e = encode_rows(&a.tm_x, p->x, p->dtype, p->batch, p->length, a.hv, a.pw, P, a.xts)) return e;
+    if (int e = encode_rows(&a.tm_B, p->B, p->dtype, p->batch, p->length, p->ngroups, a.na, N, p->bc_token_stride)) return e;
+    if (int e = encode_rows(&a.tm_C, p->C, p->dtype, p->batch, p->length, p->ngroups, a.na, N, p->bc_token_stride)) return e;
+    return p->dtype == SSM_BF16 ? run_fwd_any<__nv_bfloat16>(a, s) : run_fwd_any<__half>(a, s);
 }
 
 int bwd(const ssm_chunk_scan_params* p, cudaStream_t s) {
@@ -1521,11 +1606,11 @@ int bwd(const ssm_chunk_scan_params* p, cudaStream_t s) {
     a.dA_part = reinterpret_cast<float*>(ws + w.dh + w.dci + w.dt);
     a.db_part = reinterpret_cast<float*>(ws + w.dh + w.dci + w.dt + w.part);
     a.dD_part = reinterpret_cast<float*>(ws + w.dh + w.dci + w.dt + 2 * w.part);
-    if (int e = encode_rows(&a.tm_x, p->x, p->dtype, p->batch, p->length, p->nheads, P, p->x_token_stride)) return e;
-    if (int e = encode_rows(&a.tm_dy, p->dy, p->dtype, p->batch, p->length, p->nheads, P)) return e;
-    if (int e = encode_rows(&a.tm_B, p->B, p->dtype, p->batch, p->length, p->ngroups, N, p->bc_token_stride)) return e;
-    if (int e = encode_rows(&a.tm_C, p->C, p->dtype, p->batch, p->length, p->ngroups, N, p->bc_token_stride)) return e;
-    return p->dtype == SSM_BF16 ? run_bwd<__nv_bfloat16>(a, p, s) : run_bwd<__half>(a, p, s);
+    if (int e = encode_rows(&a.tm_x, p->x, p->dtype, p->batch, p->length, a.hv, a.pw, P, a.xts)) return e;
+    if (int e = encode_rows(&a.tm_dy, p->dy, p->dtype, p->batch, p->length, a.hv, a.pw, P, p->nheads * p->headdim)) return e;
+    if (int e = encode_rows(&a.tm_B, p->B, p->dtype, p->batch, p->length, p->ngroups, a.na, N, p->bc_token_stride)) return e;
+    if (int e = encode_rows(&a.tm_C, p->C, p->dtype, p->batch, p->length, p->ngroups, a.na, N, p->bc_token_stride)) return e;
+    return p->dtype == SSM_BF16 ? run_bwd_any<__nv_bfloat16>(a, p, s) : run_bwd_any<__half>(a, p, s);
 }
 
 }  // namespace ssdtc

@@ -32,18 +32,28 @@ import torch
 
 from .. import _native as nat
 
-__all__ = ["mamba2_chunk_scan", "last_path", "set_tensor_cores"]
+__all__ = ["mamba2_chunk_scan", "last_path", "set_tensor_cores", "tc_shape"]
 
 _DTYPES = (torch.float32, torch.float16, torch.bfloat16)
 _path = "none"
 _tensor_cores = True
 
 
+def tc_shape(d_head: int, d_state: int) -> bool:
+    """Whether the tensor-core kernels serve this head shape (with bf16/f16
+    inputs): d_head a multiple of 8 up to 64, or 128 or 256, and d_state a
+    multiple of 8 up to 128.  Other shapes and fp32 inputs run the CUDA-core
+    kernels."""
+    pd = (8 <= d_head <= 64 and d_head % 8 == 0) or d_head in (128, 256)
+    return pd and 8 <= d_state <= 128 and d_state % 8 == 0
+
+
 def set_tensor_cores(enabled: bool) -> bool:
     """Allow (default) or forbid the tensor-core kernels, which serve bf16/f16
-    inputs with d_head 64 and d_state 128; forbidden, those inputs run the
-    CUDA-core kernels like every other case.  Returns the previous setting.
-    The setting must not change between a forward and its backward."""
+    inputs whose head shape :func:`tc_shape` accepts; forbidden, those inputs
+    run the CUDA-core kernels like every other case.  Returns the previous
+    setting.  The setting must not change between a forward and its
+    backward."""
     global _tensor_cores
     prev, _tensor_cores = _tensor_cores, bool(enabled)
     return prev
@@ -265,8 +275,7 @@ def mamba2_chunk_scan(x, dt, A, B, C, chunk_size=64, D=None, z=None, dt_bias=Non
     # the tensor-core path reads x and B / C through their token strides (column
     # slices of a wider projection or convolution output need no copy; B and C
     # share one stride); anything else is made dense
-    tc = (_tensor_cores and dtype in (torch.bfloat16, torch.float16) and x.shape[3] == 64
-          and B.shape[3] == 128)
+    tc = _tensor_cores and dtype in (torch.bfloat16, torch.float16) and tc_shape(x.shape[3], B.shape[3])
     if not (tc and _token_rows(x)):
         x = x.contiguous()
     if not (tc and _token_rows(B) and _token_rows(C) and B.stride() == C.stride()):

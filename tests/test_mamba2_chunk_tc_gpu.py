@@ -1,7 +1,10 @@
 """Mamba-2 SSD chunk scan, tensor-core path (tcgen05 / TMEM), vs the fp64 oracle.
 
-The tensor-core kernels serve bf16/f16 inputs with d_head 64 and d_state 128
-(the Mamba-2 layer shape of BASELINE config 3); they round each GEMM operand to
+The tensor-core kernels serve bf16/f16 inputs with d_head a multiple of 8 up to
+64, or 128 or 256, and d_state a multiple of 8 up to 128 (tiles of the
+Mamba-2 layer shape of BASELINE config 3, d_head 64 and d_state 128, which
+smaller heads fill with zeros and wider heads split into 64-column virtual
+heads); they round each GEMM operand to
 the input dtype and accumulate in fp32.  These tests check them the way the
 reference's verifier checks its fast path (benchmarks/verify_mamba2_chunk.py):
 forward outputs and final state over ragged lengths, group sizes and every
@@ -31,17 +34,17 @@ def _mod():
     return mamba2_chunk
 
 
-def _inputs(batch, length, nheads, ngroups, seed, dtype, d_per_head=False):
+def _inputs(batch, length, nheads, ngroups, seed, dtype, d_per_head=False, p=P, n=N):
     g = torch.Generator().manual_seed(seed)
-    x = torch.randn(batch, length, nheads, P, generator=g)
+    x = torch.randn(batch, length, nheads, p, generator=g)
     dt = torch.randn(batch, length, nheads, generator=g) - 1.0
     A = -(torch.rand(nheads, generator=g) * 4 + 0.5)
-    B = torch.randn(batch, length, ngroups, N, generator=g)
-    C = torch.randn(batch, length, ngroups, N, generator=g)
-    D = torch.randn(nheads, P, generator=g) if d_per_head else torch.randn(nheads, generator=g)
-    z = torch.randn(batch, length, nheads, P, generator=g)
+    B = torch.randn(batch, length, ngroups, n, generator=g)
+    C = torch.randn(batch, length, ngroups, n, generator=g)
+    D = torch.randn(nheads, p, generator=g) if d_per_head else torch.randn(nheads, generator=g)
+    z = torch.randn(batch, length, nheads, p, generator=g)
     bias = torch.randn(nheads, generator=g) * 0.5
-    init = torch.randn(batch, nheads, P, N, generator=g) * 0.2
+    init = torch.randn(batch, nheads, p, n, generator=g) * 0.2
     vals = dict(x=x, dt=dt, A=A, B=B, C=C, D=D, z=z, dt_bias=bias, initial_states=init)
     # x, B, C, z, dt in the run dtype; the oracle sees the same rounded values
     for k in ("x", "dt", "B", "C", "z"):
@@ -245,3 +248,58 @@ def test_tc_token_strided_inputs(dtype):
     assert mod.last_path() == "cuda"
     for a_, b_ in zip(*runs):
         assert torch.equal(a_, b_)
+
+
+# head shapes other than 64 x 128: zero-filled tiles (d_head < 64, d_state < 128)
+# and 64-column virtual heads (d_head 128, 256); (d_head, d_state, heads, groups)
+WIDE = [(64, 64, 4, 2), (32, 128, 4, 2), (128, 128, 4, 2), (32, 64, 6, 3), (128, 64, 2, 1),
+        (256, 128, 2, 2), (16, 16, 4, 4), (40, 72, 3, 1)]
+
+
+@pytest.mark.parametrize("wi", range(len(WIDE)))
+def test_tc_other_head_shapes_forward_and_gradients(wi):
+    """Every option (gate, D per head or per column, bias, initial state, a
+    d_state gradient) against the fp64 oracle; the tensor-core path must be the
+    one that ran (a CUDA-core fallback would pass the same checks)."""
+    m = _mod()
+    dtype = torch.bfloat16
+    p, n, heads, groups = WIDE[wi]
+    assert m.tc_shape(p, n)
+    d_per_head = wi % 2 == 1
+    vals = _inputs(2, 300, heads, groups, seed=300 + wi, dtype=dtype, d_per_head=d_per_head, p=p, n=n)
+    g = torch.Generator().manual_seed(301 + wi)
+    wy = torch.randn(2, 300, heads, p, generator=g)
+    ws = torch.randn(2, heads, p, n, generator=g)
+    opts = ("D", "z", "dt_bias", "initial_states")
+
+    def grads(device, cast, fn):
+        t, y, s = _run(vals, device, cast, fn, opts, grad=True)
+        loss = (y.to(cast) * wy.to(device, cast)).sum() + (s.to(cast) * ws.to(device, cast)).sum()
+        return y.detach(), s.detach(), torch.autograd.grad(loss, [t[k] for k in NAMES])
+
+    y, s, fast = grads("cuda", torch.float32, m.mamba2_chunk_scan)
+    yr, sr, slow = grads("cpu", torch.float64, orc.mamba2_chunk_scan_ref)
+    assert y.shape == (2, 300, heads, p) and s.shape == (2, heads, p, n)
+    assert orc.max_rel(y.float().cpu(), yr) <= TOL_FWD[dtype]
+    assert orc.max_rel(s.float().cpu(), sr) <= TOL_FWD[dtype]
+    for name, gf, gs in zip(NAMES, fast, slow):
+        assert gf.shape == gs.shape, name
+        assert orc.norm_rel(gf.float().cpu(), gs) <= TOL_GRAD[dtype], name
+
+
+def test_tc_other_head_shapes_take_the_tensor_cores():
+    """The shapes above run on the tensor cores: forcing the CUDA-core kernels
+    gives results within rounding but not bit-identical to them (the two paths
+    round GEMM operands differently), while two tensor-core runs are."""
+    m = _mod()
+    vals = _inputs(1, 200, 4, 2, seed=77, dtype=torch.bfloat16, p=128, n=64)
+    _, y1, _ = _run(vals, "cuda", torch.float32, m.mamba2_chunk_scan, ("D", "dt_bias"))
+    _, y2, _ = _run(vals, "cuda", torch.float32, m.mamba2_chunk_scan, ("D", "dt_bias"))
+    prev = m.set_tensor_cores(False)
+    try:
+        _, yc, _ = _run(vals, "cuda", torch.float32, m.mamba2_chunk_scan, ("D", "dt_bias"))
+    finally:
+        m.set_tensor_cores(prev)
+    assert torch.equal(y1, y2)
+    assert not torch.equal(y1, yc)
+    assert orc.max_rel(y1.float().cpu(), yc.float().cpu()) <= 2e-2
