@@ -15,9 +15,9 @@ this package's scope.
 
 from .causal_conv1d import causal_conv1d_fn, causal_conv1d_update
 from .gated_norm import rmsnorm_gated
-from .mamba2_chunk import last_path, mamba2_chunk_scan
+from .mamba2_chunk import last_path, mamba2_chunk_scan, tc_shape
 from .mamba2_state import mamba2_state_update
 from .path_scan import path_orders, ss2d_scan
 
 __all__ = ["causal_conv1d_fn", "causal_conv1d_update", "last_path", "mamba2_chunk_scan",
-           "mamba2_state_update", "path_orders", "rmsnorm_gated", "ss2d_scan"]
+           "mamba2_state_update", "path_orders", "rmsnorm_gated", "ss2d_scan", "tc_shape"]
