@@ -1,9 +1,11 @@
 // Mamba-1 selective scan, TMA-staged forward and backward (sm_100a).
 //
 // Same algorithm and the same arithmetic, operation for operation, as the
-// plain-staging kernels of selective_scan.cu (so both give identical results);
-// what changes is how tiles reach and leave shared memory, and the per-chunk
-// bookkeeping around the recurrence:
+// plain-staging kernels of selective_scan.cu (so both give identical results;
+// the one exception is the dstate-16 backward of sscan_bwd2.cuh, whose sums
+// over channels and states associate differently); what changes is how tiles
+// reach and leave shared memory, and the per-chunk bookkeeping around the
+// recurrence:
 //
 //  * Every activation tile (u, delta, z, dout, the saved scan output: CPC
 //    channels x kChunk steps) and every B / C tile (NP states x kChunk steps)
@@ -562,6 +564,7 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
             const float2* vr = dvu + c * FS;
             const float* gr = gs + c * FS;
             int cslot = 0;
+            (void)cslot;
             if constexpr (LEAN) {     // the chunk's entering state (the next chunk's copy started first)
                 __syncwarp();
                 if (nleft > 0) {
@@ -847,6 +850,9 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
     if (tid == 0) bulk_wait_all();
 }
 
+#include "sscan_bwd2.cuh"
+
+
 // --------------------------------------------------------------------- host --
 static PFN_cuTensorMapEncodeTiled_v12000 encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -942,6 +948,18 @@ static int run_bwd_tma(const TmaArgs& ta, cudaStream_t st) {
     return check_launch("selective_scan bwd (TMA)");
 }
 
+// dstate 16 at 8 states x 2 lanes per channel: the two-channels-per-lane kernel
+template <typename T>
+static int run_bwd2_tma(const TmaArgs& ta, cudaStream_t st) {
+    const size_t sm = BwdTmaLayout<T, 64, 16, 8>::bytes + 128;
+    auto k = ta.a.lean ? bwd2_tma_kernel<T, true> : bwd2_tma_kernel<T, false>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
+        return check_launch("selective_scan bwd (TMA): smem attribute");
+    const Args& a = ta.a;
+    k<<<dim3((unsigned)(a.nct * a.nseg), (unsigned)a.groups, (unsigned)a.batch), kThreads, sm, st>>>(ta);
+    return check_launch("selective_scan bwd (TMA)");
+}
+
 template <typename T>
 static int dispatch_fwd_tma(const Cfg& c, const TmaArgs& ta, cudaStream_t st) {
     switch (c.npt * 100 + c.lpc) {
@@ -963,7 +981,7 @@ static int dispatch_bwd_tma(const Cfg& c, const TmaArgs& ta, cudaStream_t st) {
         case 401: return run_bwd_tma<T, 4, 1>(ta, st);
         case 404: return run_bwd_tma<T, 4, 4>(ta, st);
         case 801: return run_bwd_tma<T, 8, 1>(ta, st);
-        case 802: return run_bwd_tma<T, 8, 2>(ta, st);
+        case 802: return run_bwd2_tma<T>(ta, st);
         case 804: return run_bwd_tma<T, 8, 4>(ta, st);
         case 808: return run_bwd_tma<T, 8, 8>(ta, st);
         default: return SSM_ERR_UNSUPPORTED;

@@ -287,7 +287,12 @@ def test_sequence_segments(shape, dtype):
 def test_tma_and_plain_staging_identical(shape, dtype, opts):
     """Rows that are 16-byte aligned run the TMA-staged kernels; the
     plain-staging kernels run the same arithmetic, so y and every gradient
-    are equal bit for bit between the two."""
+    are equal bit for bit between the two.  One exception: at dstate 16 with
+    8 states x 2 lanes per channel (from 8192 rows) the TMA backward holds two
+    channels of 4 states per lane, so its sums over channels (dB, dC) and over
+    states (du, ddelta, hence d delta_bias) associate differently -- those
+    agree to fp32 rounding, carried into the activation dtype; y, dA, dD and
+    dz stay bit-identical."""
     mk = _mk()
     from metal_kernelops_b200 import scan as scan_mod
     b, d, l, n, g = shape
@@ -304,8 +309,13 @@ def test_tma_and_plain_staging_identical(shape, dtype, opts):
             runs.append([y.detach()] + list(gr))
         finally:
             scan_mod.set_tma_staging(prev)
+    two_channel = n == 16 and b * d >= 8192
+    regrouped = ("u", "delta", "B", "C", "delta_bias")
     for name, a, b_ in zip(("y",) + tuple(use), *runs):
-        assert torch.equal(a, b_), name
+        if two_channel and name in regrouped:
+            assert orc.norm_rel(a.float().cpu(), b_.float().cpu()) <= (1e-6 if a.dtype == torch.float32 else 1e-4), name
+        else:
+            assert torch.equal(a, b_), name
 
 
 def test_backward_first_cuda_call_on_a_fresh_thread():
