@@ -244,6 +244,78 @@ __device__ __forceinline__ float block_sum(float v, float* sh) {
     return s;
 }
 
+// The same reductions over the first NB threads with two alternating scratch
+// rows (`pp` is [2][16] floats, `k` a per-thread call counter that every
+// thread advances alike): one barrier each.  A call writes the row its
+// predecessor did not, and the call before that one has been read by every
+// thread before any thread passed the barrier of the call in between.
+template <int NB>
+__device__ __forceinline__ float pp_sum(float v, float* pp, int& k) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    float* row = pp + 16 * k;
+    k ^= 1;
+    if ((threadIdx.x & 31) == 0) row[threadIdx.x >> 5] = v;
+    gsync<NB>();
+    float s = 0.0f;
+    for (int i = 0; i < group_warps<NB>(); ++i) s += row[i];
+    return s;
+}
+// two sums at once (NB <= 256)
+template <int NB>
+__device__ __forceinline__ float2 pp_sum2(float2 v, float* pp, int& k) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        v.x += __shfl_xor_sync(0xffffffffu, v.x, o);
+        v.y += __shfl_xor_sync(0xffffffffu, v.y, o);
+    }
+    float* row = pp + 16 * k;
+    k ^= 1;
+    if ((threadIdx.x & 31) == 0) {
+        row[threadIdx.x >> 5] = v.x;
+        row[8 + (threadIdx.x >> 5)] = v.y;
+    }
+    gsync<NB>();
+    float2 s = make_float2(0.0f, 0.0f);
+    for (int i = 0; i < group_warps<NB>(); ++i) {
+        s.x += row[i];
+        s.y += row[8 + i];
+    }
+    return s;
+}
+template <int NB>
+__device__ __forceinline__ float pp_incl_scan(float v, float* pp, int& k) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+    }
+    float* row = pp + 16 * k;
+    k ^= 1;
+    if (lane == 31) row[w] = v;
+    gsync<NB>();
+    float off = 0.0f;
+    for (int i = 0; i < w; ++i) off += row[i];
+    return v + off;
+}
+template <int NB>
+__device__ __forceinline__ float pp_suffix_scan(float v, float* pp, int& k) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float u = __shfl_down_sync(0xffffffffu, v, o);
+        if (lane + o < 32) v += u;
+    }
+    float* row = pp + 16 * k;
+    k ^= 1;
+    if (lane == 0) row[w] = v;
+    gsync<NB>();
+    float off = 0.0f;
+    for (int i = group_warps<NB>() - 1; i > w; --i) off += row[i];
+    return v + off;
+}
+
 // Dynamic shared memory, rounded up to 128 bytes: TMA tile destinations need
 // that alignment whatever the size of the kernel's static shared variables
 // (the launches reserve kSmemPad extra bytes).
@@ -324,6 +396,19 @@ __device__ __forceinline__ void stage_heads(const Args& a, HeadSh& hs, int64_t b
 template <int NB = 0>
 __device__ __forceinline__ Steps staged_steps(const Args& a, const HeadSh& hs, int k, int64_t c, float* scan_sh) {
     return steps_of<NB>(a, threadIdx.x < Q ? hs.raw[k][threadIdx.x] : 0.0f, c, hs.A[k], scan_sh);
+}
+// staged_steps with the one-barrier scan (ping-pong scratch, see pp_sum)
+template <int NB>
+__device__ __forceinline__ Steps staged_steps_pp(const Args& a, const HeadSh& hs, int k, int64_t c, float* pp,
+                                                 int& kk) {
+    Steps s;
+    const float raw = threadIdx.x < Q ? hs.raw[k][threadIdx.x] : 0.0f;
+    const bool valid = threadIdx.x < Q && c * Q + threadIdx.x < a.length;
+    s.raw = raw;
+    s.d = valid ? ((a.flags & SSM_SOFTPLUS) ? softplus_f(raw) : raw) : 0.0f;
+    s.cd = pp_incl_scan<NB>(s.d, pp, kk);
+    s.cs = hs.A[k] * s.cd;
+    return s;
 }
 
 // ===================================================================== F1b ==
@@ -980,7 +1065,7 @@ struct GradSh {
     float col[4][Q];          // column sums of E per TMEM quadrant
     float rowp[2][Q];         // row sums of E d, per column half
     float vp[2][Q];           // <x_s, Z_s> per column half
-    float scan[8];
+    float scan[32];           // [2][16] ping-pong rows of the block reductions
     float T[2];
 };
 
@@ -1124,7 +1209,8 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
         const bool pos_thread = tid < Q;           // owns chunk position s = tid
         stage_heads<kGC>(a, sh.hs, b, g, c, 0, (int)min64(kHeadsSh, a.hpg));
         gsync<kGC>();
-        Steps st = staged_steps<kGC>(a, sh.hs, 0, c, sh.scan);
+        int kpp = 0;                               // ping-pong row of the next block reduction
+        Steps st = staged_steps_pp<kGC>(a, sh.hs, 0, c, sh.scan, kpp);
         if (tid == Q - 1) sh.T[0] = st.cs;
         mask_factors<kGC>(sh.m, st);
         const int j0 = hf * (WX / 2);              // this thread's half of an X-like row (chunks)
@@ -1273,7 +1359,7 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
                 for (int w = 0; w < 4; ++w) colsum += sh.col[w][tid];
                 rowsum = sh.rowp[0][tid] + sh.rowp[1][tid];
             }
-            const float dD_sum = block_sum<kGC>(dD_head, sh.scan);
+            const float dD_sum = pp_sum<kGC>(dD_head, sh.scan, kpp);
             Steps st_next = st;
             if (hh + 1 < a.hpg) {
                 const int hk1 = (int)((hh + 1) % kHeadsSh);
@@ -1281,7 +1367,7 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
                     stage_heads<kGC>(a, sh.hs, b, g, c, hh + 1, (int)min64(kHeadsSh, a.hpg - hh - 1));
                     gsync<kGC>();
                 }
-                st_next = staged_steps<kGC>(a, sh.hs, hk1, c, sh.scan);
+                st_next = staged_steps_pp<kGC>(a, sh.hs, hk1, c, sh.scan, kpp);
                 if (tid == Q - 1) sh.T[(hh + 1) & 1] = st_next.cs;
             }
             if (!tc::mbar_wait(bar(kM2), par)) { report(a, 43); ok = false; }
@@ -1334,9 +1420,9 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
                 dd_direct = colsum + v_s;
             }
             // d/dT_c = exp(T) <dH_{c+1}, H_c> + sum_s d_s v_s, added at the chunk's last position
-            const float dv_sum = block_sum<kGC>(dv, sh.scan);
+            const float dv_sum = pp_sum<kGC>(dv, sh.scan, kpp);
             if (tid == Q - 1) dcs += dTc + dv_sum;
-            const float suffix = block_suffix_scan<kGC>(dcs, sh.scan);
+            const float suffix = pp_suffix_scan<kGC>(dcs, sh.scan, kpp);
             const float dd = fmaf(Ah, suffix, dd_direct);
             const float ddt = (a.flags & SSM_SOFTPLUS) ? dd * softplus_grad_f(st.raw) : dd;
             if constexpr (PAD) {
@@ -1348,8 +1434,9 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
             } else if (pos_thread && tid < valid) {
                 a.ddt[(b * L + t0 + tid) * a.nheads + h] = ddt;
             }
-            const float dA_sum = block_sum<kGC>(pos_thread ? dcs * st.cd : 0.0f, sh.scan);
-            const float db_sum = block_sum<kGC>(pos_thread && tid < valid ? ddt : 0.0f, sh.scan);
+            const float2 ab = pp_sum2<kGC>(make_float2(pos_thread ? dcs * st.cd : 0.0f,
+                                                       pos_thread && tid < valid ? ddt : 0.0f), sh.scan, kpp);
+            const float dA_sum = ab.x, db_sum = ab.y;
             if (tid == 0) {
                 a.dA_part[bhc] = dA_sum;
                 a.db_part[bhc] = db_sum;
