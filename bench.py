@@ -353,7 +353,7 @@ def run_scan(args, world, rank, device):
         "saved_for_backward": {"mode": "lean (states every 16 steps)" if args.lean else
                                "states every 4 steps + scan output",
                                "bytes": saved_bytes},
-        "roofline": {"bound": "hbm", "kernel": "selective_scan bwd (bwd_kernel + reduce)",
+        "roofline": {"bound": "hbm", "kernel": "selective_scan bwd (bwd2_tma_kernel + reduce)",
                      "achieved": bwd_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": bwd_gbs / peaks["hbm_gbs"], "peak_source": peak_kind,
                      "traffic": _traffic("selective_scan_bwd"),
