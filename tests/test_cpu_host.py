@@ -200,3 +200,35 @@ def test_chunk_scan_contract_on_cpu():
         mamba2_chunk_scan(x, dt, A, B, B, 0)
     with pytest.raises(ValueError):
         mamba2_chunk_scan(x, dt, A, torch.zeros(2, 13, 3, 5), torch.zeros(2, 13, 3, 5))
+
+
+@pytest.mark.parametrize("headdim,dstate", [(64, 128), (64, 64), (32, 128), (128, 128), (256, 64), (16, 16),
+                                            (40, 72), (96, 128), (64, 136), (64, 256), (12, 64)])
+def test_chunk_scan_tensor_core_shapes_match_library(headdim, dstate):
+    """`tc_shape` (which the Python wrapper uses to keep token-strided views)
+    says exactly which head shapes the library runs on the tensor cores: for
+    those, the saved-state buffer the library asks for is the tensor-core
+    layout (one 16 KB state image per (batch, 64-column virtual head, 128-step
+    chunk)); for the others it is the CUDA-core layout, the same as with
+    SSM_CUDA_CORES forced.  Host-only query."""
+    from metal_kernelops_b200 import _native as nat
+    from metal_kernelops_b200.cv import tc_shape
+    lib = nat.lib()
+
+    def saved(flags):
+        p = nat.ChunkScanParams()
+        p.batch, p.length, p.nheads, p.headdim, p.ngroups, p.dstate = 2, 300, 4, headdim, 2, dstate
+        p.chunk_size = 64
+        p.dtype, p.dt_dtype = nat.dtype_code(torch.bfloat16), nat.dtype_code(torch.float32)
+        p.flags = flags
+        s, w = nat._SZ(), nat._SZ()
+        assert lib.ssm_chunk_scan_sizes(p, s, w) == nat.SSM_OK
+        return s.value
+
+    virtual = headdim // 64 if headdim > 64 else 1
+    tc_bytes = (2 * 4 * virtual * 3 * 16384 + 255) // 256 * 256
+    if tc_shape(headdim, dstate):
+        assert saved(0) == tc_bytes
+        assert saved(nat.CUDA_CORES) != tc_bytes
+    else:
+        assert saved(0) == saved(nat.CUDA_CORES)
