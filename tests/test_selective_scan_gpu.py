@@ -283,6 +283,10 @@ def test_sequence_segments(shape, dtype):
     ((2, 32, 512, 32, 1), torch.float32, ("D", "z", "delta_bias")),
     ((2, 16, 256, 64, 1), torch.bfloat16, ("D", "z", "delta_bias")),
     ((2, 128, 272, 4, 4), torch.float32, ("D", "z", "delta_bias")),
+    # the two-channel dstate-16 backward: a last channel tile of 8 channels (one
+    # lane's pair may be half valid), segments, a ragged last chunk
+    ((1, 8200, 1992, 16, 1), torch.bfloat16, ("D", "z", "delta_bias")),
+    ((2, 8200, 776, 16, 2), torch.float32, ("D", "delta_bias")),
 ])
 def test_tma_and_plain_staging_identical(shape, dtype, opts):
     """Rows that are 16-byte aligned run the TMA-staged kernels; the
@@ -369,6 +373,7 @@ def test_backward_first_cuda_call_on_a_fresh_thread():
     ((2, 24, 1000, 16, 3), torch.float32, False),      # ragged last chunk
     ((2, 64, 250, 16, 1), torch.bfloat16, True),       # plain path (unaligned rows)
     ((2, 32, 512, 32, 1), torch.float32, True),        # plain path, 32 states
+    ((1, 8200, 1992, 16, 1), torch.bfloat16, False),   # two-channel backward, segments, partial tile
 ])
 def test_lean_backward_matches_saved_states(shape, dtype, plain):
     """The lean mode saves the state entering every 16-step chunk only and
