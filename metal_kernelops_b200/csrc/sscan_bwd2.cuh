@@ -18,8 +18,10 @@
 //    c0 + 1), so the first level of that reduction sends one channel's sums
 //    and keeps the other's with no select.
 // Every per-element formula and the order of every per-channel recurrence are
-// those of bwd_tma_kernel; the cross-channel and cross-state sums associate
-// differently, so dB, dC, du and ddelta differ from it in the last bits.
+// those of bwd_tma_kernel, except that dh a x_prev is formed as (dh a) x_prev
+// from the carried adjoint dh a (one multiply fewer); that and the
+// cross-channel and cross-state sums, which associate differently, make dA,
+// dB, dC, du and ddelta differ from it in the last bits.
 #pragma once
 
 template <typename T, bool LEAN>
@@ -353,12 +355,13 @@ bwd2_tma_kernel(const __grid_constant__ TmaArgs ta) {
                                 const float2 ar = __fmul2_rn(dlr2, An2[e][j]);
                                 const float2 aj = make_float2(exp2_mufu(ar.x), exp2_mufu(ar.y));
                                 const float2 dh = __ffma2_rn(g2, cc[j], q2[e][j]);
-                                const float2 tmp = __fmul2_rn(dh, __fmul2_rn(aj, xh[jj][e][j]));
+                                q2[e][j] = __fmul2_rn(dh, aj);
+                                // dh a x_prev, as (dh a) x_prev: the carried adjoint times the state
+                                const float2 tmp = __fmul2_rn(q2[e][j], xh[jj][e][j]);
                                 dda2 = __ffma2_rn(tmp, An2[e][j], dda2);
                                 dA2[e][j] = __ffma2_rn(tmp, dv2, dA2[e][j]);
                                 dua2 = __ffma2_rn(dh, bb[j], dua2);
                                 wb[j] = e == 0 ? __fmul2_rn(dh, du2) : __ffma2_rn(dh, du2, wb[j]);
-                                q2[e][j] = __fmul2_rn(dh, aj);
                                 // the state after step t: the next step's entering state
                                 const float2 xt = (jj + 1 < TS && !last) ? xh[jj + 1 < TS ? jj + 1 : jj][e][j] : x2[e][j];
                                 wc[j] = e == 0 ? __fmul2_rn(g2, xt) : __ffma2_rn(g2, xt, wc[j]);

@@ -294,9 +294,9 @@ def test_tma_and_plain_staging_identical(shape, dtype, opts):
     are equal bit for bit between the two.  One exception: at dstate 16 with
     8 states x 2 lanes per channel (from 8192 rows) the TMA backward holds two
     channels of 4 states per lane, so its sums over channels (dB, dC) and over
-    states (du, ddelta, hence d delta_bias) associate differently -- those
-    agree to fp32 rounding, carried into the activation dtype; y, dA, dD and
-    dz stay bit-identical."""
+    states (du, ddelta, hence d delta_bias) associate differently, and it
+    forms dh a x as (dh a) x (dA) -- those agree to fp32 rounding, carried into
+    the activation dtype; y, dD and dz stay bit-identical."""
     mk = _mk()
     from metal_kernelops_b200 import scan as scan_mod
     b, d, l, n, g = shape
@@ -314,7 +314,7 @@ def test_tma_and_plain_staging_identical(shape, dtype, opts):
         finally:
             scan_mod.set_tma_staging(prev)
     two_channel = n == 16 and b * d >= 8192
-    regrouped = ("u", "delta", "B", "C", "delta_bias")
+    regrouped = ("u", "delta", "A", "B", "C", "delta_bias")
     for name, a, b_ in zip(("y",) + tuple(use), *runs):
         if two_channel and name in regrouped:
             assert orc.norm_rel(a.float().cpu(), b_.float().cpu()) <= (1e-6 if a.dtype == torch.float32 else 1e-4), name
