@@ -72,6 +72,7 @@ __device__ int g_kernel_error;
 
 struct Args {
     int64_t batch, length, nheads, ngroups, nc;
+    int64_t b0;            // first batch row of this launch (grids cover a range of rows)
     // The tiles are P = 64 columns by N = 128 states.  A head whose headdim is a
     // multiple of 64 above 64 runs as pr "virtual heads" of 64 columns each
     // (columns of x, y and of the state are independent, and every gradient
@@ -446,7 +447,7 @@ __global__ void __launch_bounds__(kStThreads, 2) states2_kernel(const __grid_con
 
     const int tid = threadIdx.x, warp = tid >> 5;
     const bool producer = warp == kThreads / 32;
-    const int64_t h = blockIdx.x, b = blockIdx.y, g = h / a.hpg;   // h: virtual head
+    const int64_t h = blockIdx.x, b = blockIdx.y + a.b0, g = h / a.hpg;   // h: virtual head
     const int64_t H = a.hv, nc = a.nc;
     auto bar = [](uint64_t* m, int i) { return tc::smem_u32(&m[i]); };
 
@@ -639,7 +640,7 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
     __shared__ uint32_t tbase;
 
     const int tid = threadIdx.x, warp = tid >> 5;
-    const int64_t c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int64_t c = blockIdx.x, g = blockIdx.y, b = blockIdx.z + a.b0;
     const int64_t H = a.hv;
     const int64_t t0 = c * Q;
     const int valid = (int)min64(Q, a.length - t0);
@@ -837,7 +838,7 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const __grid_constant
     __shared__ uint32_t tbase;
 
     const int tid = threadIdx.x, warp = tid >> 5;
-    const int64_t h = blockIdx.x, b = blockIdx.y, g = h / a.hpg;   // h: virtual head
+    const int64_t h = blockIdx.x, b = blockIdx.y + a.b0, g = h / a.hpg;   // h: virtual head
     const int64_t L = a.length, H = a.hv, hh = head_of<PAD>(a, h);   // hh: the caller's head
     const int pw = pw_of<PAD>(a);
     const bool nrow = tid < na_of<PAD>(a);    // state n = tid exists
@@ -1091,7 +1092,7 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
     const bool mma_warp = warp == kGC / 32;
     const int q = warp & 3, hf = (warp >> 2) & 1;      // TMEM quadrant, column half
     const int r = q * 32 + lane;                       // TMEM row / tile row of this thread
-    const int64_t c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int64_t c = blockIdx.x, g = blockIdx.y, b = blockIdx.z + a.b0;
     const int64_t L = a.length, H = a.hv, G = a.ngroups;
     const int pw = pw_of<PAD>(a);
     const int64_t na = na_of<PAD>(a);
@@ -1554,7 +1555,7 @@ void sizes(const ssm_chunk_scan_params* p, size_t* saved_bytes, size_t* workspac
 
 static void make_args(const ssm_chunk_scan_params* p, Args& a) {
     a.batch = p->batch; a.length = p->length; a.nheads = p->nheads; a.ngroups = p->ngroups;
-    a.nc = n_chunks(p);
+    a.nc = n_chunks(p); a.b0 = 0;
     a.pr = virt_per_head(p); a.prs = a.pr == 4 ? 2 : a.pr == 2 ? 1 : 0;
     a.hv = p->nheads * a.pr; a.hpg = p->nheads / p->ngroups * a.pr;
     a.pa = p->headdim; a.pw = min64(p->headdim, P); a.na = p->dstate;
@@ -1621,14 +1622,99 @@ static int set_smem(const void* fn, size_t bytes) {
     return SSM_OK;
 }
 
+// One batch-row range [a.b0, a.b0 + rows) of the forward: the state pass, then
+// the outputs of the same rows.
+template <typename T, bool PAD>
+static int run_fwd_rows(const Args& a, int64_t rows, cudaStream_t s) {
+    states2_kernel<T, PAD><<<dim3((unsigned)a.hv, (unsigned)rows), kStThreads, kSmemStates2 + kSmemPad, s>>>(a);
+    if (int e = check_launch("chunk_scan fwd (tensor cores): states")) return e;
+    outputs_kernel<T, PAD><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)rows), kThreads, kSmemOutputs + kSmemPad, s>>>(a);
+    return check_launch("chunk_scan fwd (tensor cores): outputs");
+}
+// ... and of the backward (the parameter reduce runs once, over every row).
+template <typename T, bool PAD>
+static int run_bwd_rows(const Args& a, int64_t rows, cudaStream_t s) {
+    if (a.flags & SSM_HAS_Z)
+        dstates_kernel<T, true, PAD><<<dim3((unsigned)a.hv, (unsigned)rows), kThreads, kSmemDstates + kSmemPad, s>>>(a);
+    else
+        dstates_kernel<T, false, PAD><<<dim3((unsigned)a.hv, (unsigned)rows), kThreads, kSmemDstates + kSmemPad, s>>>(a);
+    if (int e = check_launch("chunk_scan bwd (tensor cores): dstates")) return e;
+    grads_kernel<T, PAD><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)rows), kGradThreads, kSmemGrads + kSmemPad, s>>>(a);
+    return check_launch("chunk_scan bwd (tensor cores): grads");
+}
+
+static int64_t sm_count_tc() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = 148;
+    }
+    return n;
+}
+
+// A second, non-blocking stream per device (created on first use, kept for the
+// process), on which the second half of the batch runs.
+static cudaStream_t side_stream() {
+    static std::mutex mu;
+    static cudaStream_t streams[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (!streams[dev] && cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking) != cudaSuccess) {
+        cudaGetLastError();
+        streams[dev] = nullptr;
+    }
+    return streams[dev];
+}
+
+// Runs `rows_fn(args, rows, stream)` over the whole batch.  The state kernels
+// run one CTA per (batch row, head) through every chunk; when that grid needs
+// more than one wave, the batch goes as two halves -- the first on the
+// caller's stream, the second on the side stream, forked from and joined back
+// into the caller's stream by events -- so that the last, partly filled wave
+// of one half's state kernel overlaps the other half's kernels instead of
+// leaving SMs idle.  Not while the caller's stream is being captured.
+template <class F>
+static int in_halves(const Args& a, cudaStream_t s, F&& rows_fn) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (a.batch < 2 || a.hv * a.batch <= 2 * sm_count_tc() ||
+        cudaStreamIsCapturing(s, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+        cudaGetLastError();
+        return rows_fn(a, a.batch, s);
+    }
+    cudaStream_t side = side_stream();
+    cudaEvent_t fork = nullptr, join = nullptr;
+    if (!side || cudaEventCreateWithFlags(&fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&join, cudaEventDisableTiming) != cudaSuccess) {
+        if (fork) cudaEventDestroy(fork);
+        cudaGetLastError();
+        return rows_fn(a, a.batch, s);
+    }
+    Args lo = a, hi = a;
+    const int64_t n0 = a.batch / 2;
+    hi.b0 = a.b0 + n0;
+    int e = SSM_OK;
+    if (cudaEventRecord(fork, s) != cudaSuccess || cudaStreamWaitEvent(side, fork, 0) != cudaSuccess)
+        e = check_launch("chunk_scan (tensor cores): stream fork");
+    if (!e) e = rows_fn(lo, n0, s);
+    if (!e) e = rows_fn(hi, a.batch - n0, side);
+    // joined in every case, so that nothing later on the caller's stream runs ahead
+    if (cudaEventRecord(join, side) != cudaSuccess || cudaStreamWaitEvent(s, join, 0) != cudaSuccess)
+        if (!e) e = check_launch("chunk_scan (tensor cores): stream join");
+    cudaEventDestroy(fork);
+    cudaEventDestroy(join);
+    return e;
+}
+
 template <typename T, bool PAD>
 static int run_fwd(const Args& a, cudaStream_t s) {
     if (int e = set_smem((const void*)states2_kernel<T, PAD>, kSmemStates2 + kSmemPad)) return e;
     if (int e = set_smem((const void*)outputs_kernel<T, PAD>, kSmemOutputs + kSmemPad)) return e;
-    states2_kernel<T, PAD><<<dim3((unsigned)a.hv, (unsigned)a.batch), kStThreads, kSmemStates2 + kSmemPad, s>>>(a);
-    if (int e = check_launch("chunk_scan fwd (tensor cores): states")) return e;
-    outputs_kernel<T, PAD><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)a.batch), kThreads, kSmemOutputs + kSmemPad, s>>>(a);
-    return check_launch("chunk_scan fwd (tensor cores): outputs");
+    return in_halves(a, s, [](const Args& r, int64_t rows, cudaStream_t st) { return run_fwd_rows<T, PAD>(r, rows, st); });
 }
 
 template <typename T, bool PAD>
@@ -1636,13 +1722,8 @@ static int run_bwd(const Args& a, const ssm_chunk_scan_params* p, cudaStream_t s
     if (int e = set_smem((const void*)dstates_kernel<T, false, PAD>, kSmemDstates + kSmemPad)) return e;
     if (int e = set_smem((const void*)dstates_kernel<T, true, PAD>, kSmemDstates + kSmemPad)) return e;
     if (int e = set_smem((const void*)grads_kernel<T, PAD>, kSmemGrads + kSmemPad)) return e;
-    if (a.flags & SSM_HAS_Z)
-        dstates_kernel<T, true, PAD><<<dim3((unsigned)a.hv, (unsigned)a.batch), kThreads, kSmemDstates + kSmemPad, s>>>(a);
-    else
-        dstates_kernel<T, false, PAD><<<dim3((unsigned)a.hv, (unsigned)a.batch), kThreads, kSmemDstates + kSmemPad, s>>>(a);
-    if (int e = check_launch("chunk_scan bwd (tensor cores): dstates")) return e;
-    grads_kernel<T, PAD><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)a.batch), kGradThreads, kSmemGrads + kSmemPad, s>>>(a);
-    if (int e = check_launch("chunk_scan bwd (tensor cores): grads")) return e;
+    if (int e = in_halves(a, s, [](const Args& r, int64_t rows, cudaStream_t st) { return run_bwd_rows<T, PAD>(r, rows, st); }))
+        return e;
     const bool has_d = p->flags & SSM_HAS_D, d_per_head = p->flags & SSM_D_PER_HEAD;
     const int64_t total = 2 * p->nheads + (has_d ? (d_per_head ? p->nheads * p->headdim : p->nheads) : 0);
     reduce_kernel<<<(unsigned)ceil_div(total, (int64_t)128), 128, 0, s>>>(
