@@ -303,3 +303,90 @@ def test_tc_other_head_shapes_take_the_tensor_cores():
     assert torch.equal(y1, y2)
     assert not torch.equal(y1, yc)
     assert orc.max_rel(y1.float().cpu(), yc.float().cpu()) <= 2e-2
+
+
+def _split_problem(seed):
+    """A problem whose state kernels need more than one wave (4 rows x 80 heads
+    > 2 per SM x 148 SMs), so the library splits the batch over two streams."""
+    return _inputs(4, 384, 80, 8, seed=seed, dtype=torch.bfloat16)
+
+
+def _fwd_bwd(m, vals):
+    t, y, s = _run(vals, "cuda", torch.float32, m.mamba2_chunk_scan, ("D", "dt_bias"), grad=True)
+    gr = torch.autograd.grad(y.float().square().sum() + s.float().sum(), [t[k] for k in ("x", "dt", "A", "B", "C")])
+    return [y.detach(), s.detach()] + list(gr)
+
+
+def test_split_batch_follows_the_callers_stream():
+    """The batch halves fork from and join back into the stream the call is
+    made on: run on a side torch stream, results equal the default stream's
+    bit for bit and are complete when that stream is synchronised."""
+    m = _mod()
+    vals = _split_problem(501)
+    ref = _fwd_bwd(m, vals)
+    torch.cuda.synchronize()
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        got = _fwd_bwd(m, vals)
+    st.synchronize()
+    for a, b in zip(ref, got):
+        assert torch.equal(a, b)
+
+
+def test_split_batch_from_two_host_threads():
+    """Two host threads, each on its own stream, run the split SSD at the same
+    time (they share the library's side stream): each result equals the one
+    computed alone."""
+    import threading
+    m = _mod()
+    probs = [_split_problem(502), _split_problem(503)]
+    alone = [_fwd_bwd(m, v) for v in probs]
+    torch.cuda.synchronize()
+    out, errs = [None, None], []
+
+    def work(i):
+        try:
+            st = torch.cuda.Stream()
+            with torch.cuda.stream(st):
+                out[i] = _fwd_bwd(m, probs[i])
+            st.synchronize()
+        except Exception as exc:  # noqa: BLE001
+            errs.append(exc)
+
+    ths = [threading.Thread(target=work, args=(i,)) for i in range(2)]
+    for th in ths:
+        th.start()
+    for th in ths:
+        th.join()
+    assert not errs, errs
+    for i in range(2):
+        for a, b in zip(alone[i], out[i]):
+            assert torch.equal(a, b)
+
+
+def test_forward_captures_into_a_cuda_graph():
+    """The tensor-core forward can be captured into a CUDA graph (the batch is
+    then not split: the capture stays on one stream) and the replay equals an
+    eager call on new inputs copied into the captured buffers."""
+    m = _mod()
+    vals = _split_problem(504)
+    dev = {k: (v.cuda() if k in ("x", "dt", "B", "C", "z") else v.cuda().float()) for k, v in vals.items()}
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):      # warm-up outside the capture
+        m.mamba2_chunk_scan(dev["x"], dev["dt"], dev["A"], dev["B"], dev["C"], 256, D=dev["D"],
+                            dt_bias=dev["dt_bias"], dt_softplus=True)
+    torch.cuda.current_stream().wait_stream(st)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        y, s = m.mamba2_chunk_scan(dev["x"], dev["dt"], dev["A"], dev["B"], dev["C"], 256, D=dev["D"],
+                                   dt_bias=dev["dt_bias"], dt_softplus=True)
+    new = _split_problem(505)
+    for k in ("x", "dt", "B", "C"):
+        dev[k].copy_(new[k].cuda())
+    g.replay()
+    torch.cuda.synchronize()
+    ye, se = m.mamba2_chunk_scan(dev["x"], dev["dt"], dev["A"], dev["B"], dev["C"], 256, D=dev["D"],
+                                 dt_bias=dev["dt_bias"], dt_softplus=True)
+    assert torch.equal(y, ye) and torch.equal(s, se)
+    del g
