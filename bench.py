@@ -773,11 +773,17 @@ def run_block(args, world, rank, device):
 
 def cpu_baseline_scan(cfg, threads, budget_s=15.0):
     """The oracle (reference CPU code restated) on a bounded sample: one batch
-    row, a slice of channels, the full sequence; fwd + bwd with autograd."""
+    row, a slice of channels, the full sequence; fwd + bwd with autograd.
+
+    The reference steps the sequence in Python, one autograd op per step, so
+    its rate grows with the channels per step until memory traffic takes over
+    (on 8 host cores: 13 k elem/s at 64 channels, 131 k at 1024, 57 k at a
+    full 5120-channel row, which takes 6 minutes).  512 channels keeps one
+    pass within the budget while sitting near the best rate."""
     from metal_kernelops_b200.workloads import selective_scan_inputs
     from oracle.ssm_oracle import selective_scan_ref
     torch.set_num_threads(threads)
-    channels = 64
+    channels = 512
     inp = selective_scan_inputs(1, channels, cfg["length"], cfg["dstate"], cfg["groups"],
                                 seed=cfg["seed"], act_dtype=torch.float32)
     names = ("u", "delta", "A", "B", "C", "D", "z", "delta_bias")
