@@ -1142,16 +1142,26 @@ static SegPlan plan_segments(int64_t base_ctas, int64_t nchunks, int per_sm) {
     return {ceil_div(nchunks, sc), sc};
 }
 
+// From 8192 rows the forward aims at kFwdTargetPerSm CTAs per SM when it cuts
+// (batch 2 x 5120 channels x 4096 steps: 6 segments 0.578 ms, 8 segments
+// 0.556 ms, 12 segments 0.576 ms).
+constexpr int kFwdTargetPerSm = 8;
 static SegPlan fwd_plan(const ssm_selective_scan_params* p, const Cfg& c) {
     const int64_t nct = ceil_div(p->dim / p->groups, 32 / c.lpc * kWarps);
-    return plan_segments(nct * p->groups * p->batch, ceil_div(p->length, kChunk), kFwdPerSm);
+    const int64_t base = nct * p->groups * p->batch, nchunks = ceil_div(p->length, kChunk);
+    const SegPlan sp = plan_segments(base, nchunks, kFwdPerSm);
+    if (sp.nseg == 1 || p->batch * p->dim < 8192) return sp;
+    const int64_t sc = max64(ceil_div(nchunks, ceil_div(sm_count() * kFwdTargetPerSm, base)), kMinSegChunks);
+    return {ceil_div(nchunks, sc), sc};
 }
 // The backward cuts the sequence whenever the grid would not fill every
 // resident slot once, and then aims at about kBwdTargetPerSm CTAs per SM: at
 // batch 2 and 4 x 5120 channels x 4096 steps (the per-GPU share of BASELINE
-// config 2 at 8 and 4 GPUs) that measured 1.47 -> 1.11 ms and 2.24 -> 2.10 ms;
-// the adjoint summary pass it adds costs less than the idle slots it fills.
-constexpr int kBwdTargetPerSm = 8;
+// config 2 at 8 and 4 GPUs) the two-channel backward measured, batch 2: 1.45 ms
+// in 2 segments, 1.07 ms in 8 (8 per SM), 1.03 ms in 12 (12 per SM); batch 4:
+// 2.17 ms uncut, 2.02 ms in 4, 1.98 ms in 6 (12 per SM).  The adjoint summary
+// pass it adds costs less than the idle slots it fills.
+constexpr int kBwdTargetPerSm = 12;
 static SegPlan bwd_plan(const ssm_selective_scan_params* p, const Cfg& c) {
     const int64_t nct = ceil_div(p->dim / p->groups, 32 / c.lpc * kWarps);
     const int64_t base = nct * p->groups * p->batch, nchunks = ceil_div(p->length, kChunk);
