@@ -286,6 +286,11 @@ typedef struct ssm_chunk_scan_params {
 
 int ssm_chunk_scan_sizes(const ssm_chunk_scan_params* p, size_t* saved_bytes,
                          size_t* workspace_bytes);
+/* On the tensor-core path, when batch x heads needs more than one wave of the
+ * per-(row, head) state kernels, the second half of the batch runs on an
+ * internal non-blocking stream of the current device, forked from `stream` and
+ * joined back into it by events before these return (not while `stream` is
+ * being captured): work enqueued later on `stream` runs after the whole call. */
 int ssm_chunk_scan_fwd(const ssm_chunk_scan_params* p, void* stream);
 int ssm_chunk_scan_bwd(const ssm_chunk_scan_params* p, void* stream);
 
