@@ -61,6 +61,7 @@ __device__ __forceinline__ float exp2_mufu(float x) {
 }
 
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;     // 1 / log2(e)
 
 // torch.nn.functional.softplus with its default threshold: x > 20 -> x.
 __device__ __forceinline__ float softplus_f(float x) {

@@ -19,7 +19,10 @@
 //    and keeps the other's with no select.
 // Every per-element formula and the order of every per-channel recurrence are
 // those of bwd_tma_kernel, except that dh a x_prev is formed as (dh a) x_prev
-// from the carried adjoint dh a (one multiply fewer); that and the
+// from the carried adjoint dh a (one multiply fewer), and that the per-step
+// scalar kept is delta' log2 e (the value the forward rounded its decays
+// from) instead of delta': dA accumulates in log2 e units and is scaled back
+// once, and du takes delta' as (delta' log2 e) ln 2.  These and the
 // cross-channel and cross-state sums, which associate differently, make dA,
 // dB, dC, du and ddelta differ from it in the last bits.
 #pragma once
@@ -43,7 +46,7 @@ bwd2_tma_kernel(const __grid_constant__ TmaArgs ta) {
 
     extern __shared__ __align__(128) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((128u - (tc::smem_u32(smem_raw) & 127u)) & 127u);
-    float2* dvu = reinterpret_cast<float2*>(smem + Lay::o_dvu);   // (delta', delta'*u)
+    float2* dvu = reinterpret_cast<float2*>(smem + Lay::o_dvu);   // (delta' log2 e, delta'*u)
     float* gs = reinterpret_cast<float*>(smem + Lay::o_f);        // gradient seen by the scan
     float* dua = gs + CPC * FS;                                   // sum_n dh*B
     float* dda = dua + CPC * FS;                                  // sum_n dh*a*x_prev*A
@@ -204,8 +207,9 @@ bwd2_tma_kernel(const __grid_constant__ TmaArgs ta) {
             float2 dv = add2(dr, f2(bch[cc]));
             if (softplus) dv = softplus2_fast(dv);
             const float2 du = mul2(dv, ur);
-            dvu[cc * FS + t] = make_float2(dv.x, du.x);
-            dvu[cc * FS + t + 1] = make_float2(dv.y, du.y);
+            const float2 dl = mul2(dv, f2(kLog2e));   // the forward's rounding of delta' log2 e
+            dvu[cc * FS + t] = make_float2(dl.x, du.x);
+            dvu[cc * FS + t + 1] = make_float2(dl.y, du.y);
             if (has_z) {
                 const float2 zr = Io2<T>::ld(&rz[cc * K + t]);
                 go = mul2(go, mul2(zr, sigmoid2_t<T>(zr)));
@@ -250,7 +254,7 @@ bwd2_tma_kernel(const __grid_constant__ TmaArgs ta) {
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
                     const float2 v = vr[e][t];
-                    const float dl = v.x * kLog2e;
+                    const float dl = v.x;
                     const float2 dl2 = make_float2(dl, dl), du2 = make_float2(v.y, v.y);
 #pragma unroll
                     for (int j = 0; j < 2; ++j) {
@@ -345,10 +349,9 @@ bwd2_tma_kernel(const __grid_constant__ TmaArgs ta) {
                         for (int e = 0; e < 2; ++e) {
                             const float2 v = vr[e][t];
                             const float gv = gr[e][t];
-                            const float2 g2 = make_float2(gv, gv), dv2 = make_float2(v.x, v.x);
+                            const float2 g2 = make_float2(gv, gv);
                             const float2 du2 = make_float2(v.y, v.y);
-                            const float dlr = v.x * kLog2e;
-                            const float2 dlr2 = make_float2(dlr, dlr);
+                            const float2 dlr2 = make_float2(v.x, v.x);   // delta' log2 e
                             float2 dua2 = make_float2(0.0f, 0.0f), dda2 = make_float2(0.0f, 0.0f);
 #pragma unroll
                             for (int j = 0; j < 2; ++j) {
@@ -359,7 +362,7 @@ bwd2_tma_kernel(const __grid_constant__ TmaArgs ta) {
                                 // dh a x_prev, as (dh a) x_prev: the carried adjoint times the state
                                 const float2 tmp = __fmul2_rn(q2[e][j], xh[jj][e][j]);
                                 dda2 = __ffma2_rn(tmp, An2[e][j], dda2);
-                                dA2[e][j] = __ffma2_rn(tmp, dv2, dA2[e][j]);
+                                dA2[e][j] = __ffma2_rn(tmp, dlr2, dA2[e][j]);   // in log2 e units
                                 dua2 = __ffma2_rn(dh, bb[j], dua2);
                                 wb[j] = e == 0 ? __fmul2_rn(dh, du2) : __ffma2_rn(dh, du2, wb[j]);
                                 // the state after step t: the next step's entering state
@@ -399,7 +402,7 @@ bwd2_tma_kernel(const __grid_constant__ TmaArgs ta) {
             const int i = tid + kThreads * k;
             const float2 ur = Io2<T>::ld(&ru[cc * K + t]);
             const float Dv = Dch[cc];
-            const float2 dv = make_float2(dvu[cc * FS + t].x, dvu[cc * FS + t + 1].x);
+            const float2 dv = mul2(make_float2(dvu[cc * FS + t].x, dvu[cc * FS + t + 1].x), f2(kLn2));
             const float2 gv = make_float2(gs[cc * FS + t], gs[cc * FS + t + 1]);
             const float2 dsum = make_float2(dua[cc * FS + t], dua[cc * FS + t + 1]);
             const float2 o_du = fma2(dv, dsum, mul2(gv, f2(Dv)));
@@ -465,8 +468,9 @@ bwd2_tma_kernel(const __grid_constant__ TmaArgs ta) {
         float* dap = a.dA_part + (bs * a.dim + d0 + cc2[e]) * N;
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-            dap[sub * NPT + ((2 * j) ^ pm)] = dA2[e][j].x;
-            dap[sub * NPT + ((2 * j + 1) ^ pm)] = dA2[e][j].y;
+            const float2 v = mul2(dA2[e][j], f2(kLn2));   // back from log2 e units
+            dap[sub * NPT + ((2 * j) ^ pm)] = v.x;
+            dap[sub * NPT + ((2 * j + 1) ^ pm)] = v.y;
         }
     }
     for (int i = tid; i < rows; i += kThreads) {
