@@ -622,10 +622,16 @@ __device__ __forceinline__ void mask_factors(MaskSh& m, const Steps& st) {
 }
 
 // ====================================================================== F2 ==
-// One CTA per (b, group, chunk).  TMEM: G [0,128), Y intra [128,192),
-// C H^T [192,256).
+// One CTA per (b, group, chunk), eight warps: warps w and w + 4 share TMEM lane
+// quadrant w % 4 (rows l = 32 (w % 4) + lane) and split its work -- the mask
+// pass by 16-column block parity (the lower-triangular mask gives quadrant q
+// q + 1 blocks per warp instead of 2 q + 2 for a lone warp), the epilogue by
+// column halves.  Threads 0..127 also own one chunk position each for the
+// per-position scalars.  TMEM: G [0,128), Y intra [128,192), C H^T [192,256).
+constexpr int kOutThreads = 256;
+
 template <typename T, bool PAD>
-__global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant__ Args a) {
+__global__ void __launch_bounds__(kOutThreads, 2) outputs_kernel(const __grid_constant__ Args a) {
     extern __shared__ __align__(128) unsigned char sm_raw[];
     unsigned char* const sm = aligned_smem(sm_raw);
     unsigned char* sC = sm;
@@ -634,12 +640,14 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
     unsigned char* sH = sX + kTileX;
     __shared__ MaskSh msh;
     __shared__ HeadSh hsh;
-    __shared__ float s_scan[4];
+    __shared__ float s_scan[8];
     __shared__ __align__(8) uint64_t mbar;
     __shared__ __align__(8) uint64_t lbar;    // tile loads, one phase per load
     __shared__ uint32_t tbase;
 
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int q = warp & 3, hf = warp >> 2;   // TMEM lane quadrant, block parity / column half
+    const int l = q * 32 + lane;              // TMEM row / chunk position of this thread
     const int64_t c = blockIdx.x, g = blockIdx.y, b = blockIdx.z + a.b0;
     const int64_t H = a.hv;
     const int64_t t0 = c * Q;
@@ -671,7 +679,7 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
     lok = __syncthreads_and(lok);
     tc::fence_after();
     const uint32_t tm = tbase;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     const uint32_t aC = tc::smem_u32(sC), aM = tc::smem_u32(sM), aX = tc::smem_u32(sX), aH = tc::smem_u32(sH);
     if (tid == 0 && lok) {
         const uint32_t idg = tc::idesc_f16(Pk<T>::kFmt, 128, 128, false, false);
@@ -699,49 +707,41 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
         }
         const int hk = (int)(hh % kHeadsSh);
         if (hk == 0) {
-            stage_heads(a, hsh, b, g, c, hh, (int)min64(kHeadsSh, a.hpg - hh));
+            stage_heads<kOutThreads>(a, hsh, b, g, c, hh, (int)min64(kHeadsSh, a.hpg - hh));
             __syncthreads();
         }
-        const Steps st = staged_steps(a, hsh, hk, c, s_scan);
-        mask_factors(msh, st);
-        // Mh row l = tid into sM (B is no longer needed once G is in TMEM)
+        const Steps st = staged_steps<kOutThreads>(a, hsh, hk, c, s_scan);
+        mask_factors<kOutThreads>(msh, st);
+        // Mh row l into sM (B is no longer needed once G is in TMEM): blocks
+        // j = hf, hf + 2, ...; the quadrant's last live block is 2 q + 1, so
+        // liveness is warp-uniform (tcgen05.ld is .sync.aligned)
         {
-            const int l = tid;
             const float csl = msh.cs2[l];
-            // blocks j, j + 1 per TMEM wait; a warp's last live block 2 warp + 1
-            // is odd, so a pair is live or dead as a whole (warp-uniform:
-            // tcgen05.ld is .sync.aligned)
-            for (int j0 = 0; j0 < Q / 16; j0 += 2) {
-                float v[2][16];
-                const bool live = 16 * j0 <= 32 * warp + 31;
-                if (live) {
-                    tc::tmem_ld16(tm + lane_off + 16 * j0, v[0]);
-                    tc::tmem_ld16(tm + lane_off + 16 * j0 + 16, v[1]);
-                    tc::tmem_wait_ld(v[0]);
-                    tc::tmem_pin(v[1]);
-                }
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int j = j0 + u;
-                    uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
-                    if (live && 16 * j <= l) {
+#pragma unroll 1
+            for (int j = hf; j < Q / 16; j += 2) {
+                uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+                if (j <= 2 * q + 1) {
+                    float v[16];
+                    tc::tmem_ld16(tm + lane_off + 16 * j, v);
+                    tc::tmem_wait_ld(v);
+                    if (16 * j <= l) {
                         if (16 * j + 15 < l) {
                             const float rf = exp2_mufu(csl - msh.cs2[16 * j + 15]);
 #pragma unroll
-                            for (int k = 0; k < 16; ++k) v[u][k] *= rf * msh.cf[16 * j + k] * msh.d[16 * j + k];
+                            for (int k = 0; k < 16; ++k) v[k] *= rf * msh.cf[16 * j + k] * msh.d[16 * j + k];
                         } else {
 #pragma unroll
                             for (int k = 0; k < 16; ++k) {
                                 const int s = 16 * j + k;
-                                v[u][k] = s <= l ? v[u][k] * exp2_mufu(csl - msh.cs2[s]) * msh.d[s] : 0.0f;
+                                v[k] = s <= l ? v[k] * exp2_mufu(csl - msh.cs2[s]) * msh.d[s] : 0.0f;
                             }
                         }
-                        lo = pack8<T>(v[u]);
-                        hi = pack8<T>(v[u] + 8);
+                        lo = pack8<T>(v);
+                        hi = pack8<T>(v + 8);
                     }
-                    *reinterpret_cast<uint4*>(sM + tc::tile_off(l, 2 * j, WB)) = lo;
-                    *reinterpret_cast<uint4*>(sM + tc::tile_off(l, 2 * j + 1, WB)) = hi;
                 }
+                *reinterpret_cast<uint4*>(sM + tc::tile_off(l, 2 * j, WB)) = lo;
+                *reinterpret_cast<uint4*>(sM + tc::tile_off(l, 2 * j + 1, WB)) = hi;
             }
         }
         const bool lw = tc::mbar_wait(lb, lpar);      // this head's x and H_c
@@ -760,55 +760,57 @@ __global__ void __launch_bounds__(kThreads) outputs_kernel(const __grid_constant
                 tc::mma_f16(tm + 192, tc::desc_k(aC, WB, 2 * ks), tc::desc_mn(aH, WH, 16 * ks), idy, ks > 0);
             tc::commit(tc::smem_u32(&mbar));
         }
-        // this row's gate inputs, loaded while the GEMMs run (the waits below
-        // order every later memory access after them)
-        const int64_t row = row_off<PAD>(a, b, t0 + tid, h), prow = prow_off(a, b, t0 + tid, h);
-        uint4 zr[P / 8];
-        if (has_z && tid < valid) {
+        // this row's gate inputs (its column half), loaded while the GEMMs run
+        // (the waits below order every later memory access after them)
+        const int64_t row = row_off<PAD>(a, b, t0 + l, h), prow = prow_off(a, b, t0 + l, h);
+        constexpr int HALFC = P / 2;              // columns per thread
+        const int col0 = hf * HALFC;
+        uint4 zr[HALFC / 8];
+        if (has_z && l < valid) {
 #pragma unroll
-            for (int q = 0; q < P / 8; ++q)
-                zr[q] = 8 * q < pw ? *reinterpret_cast<const uint4*>(zg + row + 8 * q) : make_uint4(0, 0, 0, 0);
+            for (int u = 0; u < HALFC / 8; ++u)
+                zr[u] = col0 + 8 * u < pw ? *reinterpret_cast<const uint4*>(zg + row + col0 + 8 * u) : make_uint4(0, 0, 0, 0);
         }
         if (!tc::mbar_wait(tc::smem_u32(&mbar), phase)) { report(a, 22); ok = false; }
         phase ^= 1;
         tc::fence_after();
         ok = __syncthreads_and(ok);
         if (ok) {
-            const int l = tid;
             const bool live = l < valid;
             const float el = exp2_mufu(msh.cs2[l]);
             const float Dh = hsh.D[hk];
 #pragma unroll
-            for (int j = 0; j < P / 16; ++j) {
+            for (int jj = 0; jj < HALFC / 16; ++jj) {
+                const int col = col0 + 16 * jj;
                 float yi[16], ye[16];
-                tc::tmem_ld16(tm + lane_off + 128 + 16 * j, yi);
-                tc::tmem_ld16(tm + lane_off + 192 + 16 * j, ye);
+                tc::tmem_ld16(tm + lane_off + 128 + col, yi);
+                tc::tmem_ld16(tm + lane_off + 192 + col, ye);
                 tc::tmem_wait_ld(yi);
                 tc::tmem_pin(ye);
                 if (!live) continue;
                 float xv[16];
-                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sX + tc::tile_off(l, 2 * j, WX)), xv);
-                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sX + tc::tile_off(l, 2 * j + 1, WX)), xv + 8);
+                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sX + tc::tile_off(l, col / 8, WX)), xv);
+                Pk<T>::unpack(*reinterpret_cast<const uint4*>(sX + tc::tile_off(l, col / 8 + 1, WX)), xv + 8);
                 float yv[16];
 #pragma unroll
                 for (int k = 0; k < 16; ++k) {
-                    const float Dk = has_d ? (d_per_head ? (16 * j + k < pw ? a.D[h * pw + 16 * j + k] : 0.0f) : Dh)
+                    const float Dk = has_d ? (d_per_head ? (col + k < pw ? a.D[h * pw + col + k] : 0.0f) : Dh)
                                            : 0.0f;
                     yv[k] = fmaf(el, ye[k], yi[k]) + Dk * xv[k];
                 }
                 if (has_z) {
                     if (ypg) {
-                        *reinterpret_cast<uint4*>(ypg + prow + 16 * j) = pack8<T>(yv);
-                        *reinterpret_cast<uint4*>(ypg + prow + 16 * j + 8) = pack8<T>(yv + 8);
+                        *reinterpret_cast<uint4*>(ypg + prow + col) = pack8<T>(yv);
+                        *reinterpret_cast<uint4*>(ypg + prow + col + 8) = pack8<T>(yv + 8);
                     }
                     float zv[16];
-                    Pk<T>::unpack(zr[2 * j], zv);
-                    Pk<T>::unpack(zr[2 * j + 1], zv + 8);
+                    Pk<T>::unpack(zr[2 * jj], zv);
+                    Pk<T>::unpack(zr[2 * jj + 1], zv + 8);
 #pragma unroll
                     for (int k = 0; k < 16; ++k) yv[k] *= zv[k] * sigmoid_f(zv[k]);
                 }
-                if (16 * j < pw) *reinterpret_cast<uint4*>(yg + row + 16 * j) = pack8<T>(yv);
-                if (16 * j + 8 < pw) *reinterpret_cast<uint4*>(yg + row + 16 * j + 8) = pack8<T>(yv + 8);
+                if (col < pw) *reinterpret_cast<uint4*>(yg + row + col) = pack8<T>(yv);
+                if (col + 8 < pw) *reinterpret_cast<uint4*>(yg + row + col + 8) = pack8<T>(yv + 8);
             }
         }
         tc::fence_before();
@@ -1628,7 +1630,7 @@ template <typename T, bool PAD>
 static int run_fwd_rows(const Args& a, int64_t rows, cudaStream_t s) {
     states2_kernel<T, PAD><<<dim3((unsigned)a.hv, (unsigned)rows), kStThreads, kSmemStates2 + kSmemPad, s>>>(a);
     if (int e = check_launch("chunk_scan fwd (tensor cores): states")) return e;
-    outputs_kernel<T, PAD><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)rows), kThreads, kSmemOutputs + kSmemPad, s>>>(a);
+    outputs_kernel<T, PAD><<<dim3((unsigned)a.nc, (unsigned)a.ngroups, (unsigned)rows), kOutThreads, kSmemOutputs + kSmemPad, s>>>(a);
     return check_launch("chunk_scan fwd (tensor cores): outputs");
 }
 // ... and of the backward (the parameter reduce runs once, over every row).
