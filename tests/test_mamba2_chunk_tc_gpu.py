@@ -390,3 +390,26 @@ def test_forward_captures_into_a_cuda_graph():
                                  dt_bias=dev["dt_bias"], dt_softplus=True)
     assert torch.equal(y, ye) and torch.equal(s, se)
     del g
+
+
+def test_split_batch_with_virtual_heads_and_padded_states():
+    """The batch split together with 64-column virtual heads (d_head 128) and a
+    zero-filled state tile (d_state 64): forward and every gradient agree with
+    the CUDA-core kernels (which share no code with the tensor-core path)."""
+    m = _mod()
+    vals = _inputs(4, 256, 40, 8, seed=506, dtype=torch.bfloat16, d_per_head=True, p=128, n=64)
+    opts = ("D", "z", "dt_bias", "initial_states")
+
+    def run():
+        t, y, s = _run(vals, "cuda", torch.float32, m.mamba2_chunk_scan, opts, grad=True)
+        gr = torch.autograd.grad(y.float().square().sum() + s.float().sum(), [t[k] for k in NAMES])
+        return [y.detach(), s.detach()] + list(gr)
+
+    tc = run()
+    prev = m.set_tensor_cores(False)
+    try:
+        cc = run()
+    finally:
+        m.set_tensor_cores(prev)
+    for name, a, b in zip(("y", "final") + NAMES, tc, cc):
+        assert orc.norm_rel(a.float().cpu(), b.float().cpu()) <= 2e-2, name

@@ -287,6 +287,7 @@ def test_sequence_segments(shape, dtype):
     # lane's pair may be half valid), segments, a ragged last chunk
     ((1, 8200, 1992, 16, 1), torch.bfloat16, ("D", "z", "delta_bias")),
     ((2, 8200, 776, 16, 2), torch.float32, ("D", "delta_bias")),
+    ((2, 4096, 256, 16, 1), torch.float16, ("D", "z", "delta_bias")),
 ])
 def test_tma_and_plain_staging_identical(shape, dtype, opts):
     """Rows that are 16-byte aligned run the TMA-staged kernels; the
