@@ -84,6 +84,7 @@ struct Args {
     int64_t hpg;           // virtual heads per group
     int64_t pa, pw, na;    // the caller's headdim, data columns per virtual head (min(pa, 64)), dstate
     int64_t xts;           // elements between tokens of x
+    int fold;              // the tensor maps copy a whole tile per box (see encode_rows)
     uint32_t flags;
     int dt_dtype;
     const void* x; const void* dt; const float* A; const void* B; const void* C;
@@ -327,17 +328,24 @@ __device__ __forceinline__ unsigned char* aligned_smem(unsigned char* raw) {
 }
 
 // The Q rows of chunk c of head / group hg of batch b, from a tensor map made by
-// encode_rows(): Q/8 boxes of 8 rows, each landing as the 8-row group of core
-// matrices of the tile.  Rows past the sequence come back as zeros.  One thread
-// issues; the bytes (Q * W * 16) complete on `mbar`.
+// encode_rows(): with `fold`, one box that is the whole tile; otherwise Q/8
+// boxes of 8 rows, each landing as the 8-row group of core matrices of the
+// tile.  Rows past the sequence come back as zeros.  One thread issues; the
+// bytes (Q * W * 16) complete on `mbar`.  (Each box costs the issuing thread
+// tens of cycles: sixteen per tile kept the other warps of the CTA waiting at
+// their next barrier.)
 template <int W>
 __device__ __forceinline__ void tma_rows(unsigned char* tile, const CUtensorMap& map, int64_t c, int64_t b,
-                                         int64_t hg, uint32_t mbar, int* status) {
+                                         int64_t hg, uint32_t mbar, int* status, int fold) {
     if (reinterpret_cast<uintptr_t>(&map) & 63u) {   // descriptors must be 64-byte aligned: never issue
         report(status, 98);
         return;
     }
     const uint32_t st = tc::smem_u32(tile);
+    if (fold) {
+        tc::tma_load5(st, &map, 0, 0, (int)(hg * W), (int)(c * (Q / 8)), (int)b, mbar);
+        return;
+    }
 #pragma unroll 4
     for (int k = 0; k < Q / 8; ++k)
         tc::tma_load5(st + k * W * 128, &map, 0, (int)(c * Q + 8 * k), 0, (int)b, (int)hg, mbar);
@@ -477,9 +485,9 @@ __global__ void __launch_bounds__(kStThreads, 2) states2_kernel(const __grid_con
                 const int buf = (int)(c & 1);
                 const uint32_t par = (uint32_t)((c >> 1) & 1);
                 tc::mbar_expect_tx(bar(lbx, buf), kRowsX);
-                tma_rows<WX>(sX0 + buf * kTileX, a.tm_x, c, b, h, bar(lbx, buf), a.status);
+                tma_rows<WX>(sX0 + buf * kTileX, a.tm_x, c, b, h, bar(lbx, buf), a.status, a.fold);
                 tc::mbar_expect_tx(bar(lbb, buf), kRowsB);
-                tma_rows<WB>(sB0 + buf * kTileB, a.tm_B, c, b, g, bar(lbb, buf), a.status);
+                tma_rows<WB>(sB0 + buf * kTileB, a.tm_B, c, b, g, bar(lbb, buf), a.status, a.fold);
                 xpend[buf] = bpend[buf] = par;
             };
             load(0);
@@ -667,8 +675,8 @@ __global__ void __launch_bounds__(kOutThreads, 2) outputs_kernel(const __grid_co
         tc::mbar_init(lb, 1);
         tc::fence_mbar_init();
         tc::mbar_expect_tx(lb, 2 * kRowsB);
-        tma_rows<WB>(sC, a.tm_C, c, b, g, lb, a.status);
-        tma_rows<WB>(sM, a.tm_B, c, b, g, lb, a.status);
+        tma_rows<WB>(sC, a.tm_C, c, b, g, lb, a.status, a.fold);
+        tma_rows<WB>(sM, a.tm_B, c, b, g, lb, a.status, a.fold);
         lpend = 0;
     }
     __syncthreads();                          // the barriers are initialised before anyone waits
@@ -702,7 +710,7 @@ __global__ void __launch_bounds__(kOutThreads, 2) outputs_kernel(const __grid_co
         if (tid == 0) {   // the previous head's GEMMs and epilogue are done with sX and sH
             lpend = lpar;
             tc::mbar_expect_tx(lb, kRowsX + kTileH);
-            tma_rows<WX>(sX, a.tm_x, c, b, h, lb, a.status);
+            tma_rows<WX>(sX, a.tm_x, c, b, h, lb, a.status, a.fold);
             tc::bulk_load(tc::smem_u32(sH), a.Ht + ((size_t)(b * H + h) * a.nc + c) * kTileH, kTileH, lb);
         }
         const int hk = (int)(hh % kHeadsSh);
@@ -891,9 +899,9 @@ __global__ void __launch_bounds__(kThreads) dstates_kernel(const __grid_constant
         const uint32_t lpar = (uint32_t)((a.nc - 1 - c) & 1);
         if (tid == 0) {   // the previous chunk's GEMMs and passes are done with these tiles
             tc::mbar_expect_tx(lb, kRowsB + kTileH + kRowsX);
-            tma_rows<WB>(sC, a.tm_C, c, b, g, lb, a.status);
+            tma_rows<WB>(sC, a.tm_C, c, b, g, lb, a.status, a.fold);
             tc::bulk_load(tc::smem_u32(sH), Hin + (size_t)c * kTileH, kTileH, lb);
-            tma_rows<WX>(sY, a.tm_dy, c, b, h, lb, a.status);
+            tma_rows<WX>(sY, a.tm_dy, c, b, h, lb, a.status, a.fold);
             lpend = lpar;
         }
         const Steps st = steps_of(a, raw, c, Ah, s_scan);
@@ -1113,8 +1121,8 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
         const int64_t h = g * a.hpg + hh;
         const int64_t bhc = (b * H + h) * a.nc + c;
         tc::mbar_expect_tx(bar(kLh), 2 * kRowsX + 2 * kTileH);
-        tma_rows<WX>(sX, a.tm_x, c, b, h, bar(kLh), a.status);
-        tma_rows<WX>(sY, a.tm_dy, c, b, h, bar(kLh), a.status);
+        tma_rows<WX>(sX, a.tm_x, c, b, h, bar(kLh), a.status, a.fold);
+        tma_rows<WX>(sY, a.tm_dy, c, b, h, bar(kLh), a.status, a.fold);
         tc::bulk_load(tc::smem_u32(sH), a.Ht + ((size_t)(b * H + h) * a.nc + c) * kTileH, kTileH, bar(kLh));
         tc::bulk_load(tc::smem_u32(sD), a.dHt + (size_t)bhc * kTileH, kTileH, bar(kLh));
         lpend = (uint32_t)(hh & 1);
@@ -1130,8 +1138,8 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
         tc::mbar_init(bar(kLh), 1);
         tc::fence_mbar_init();
         tc::mbar_expect_tx(bar(kBc), 2 * kRowsB);      // the MMA warp waits for these directly
-        tma_rows<WB>(sC, a.tm_C, c, b, g, bar(kBc), a.status);
-        tma_rows<WB>(sB, a.tm_B, c, b, g, bar(kBc), a.status);
+        tma_rows<WB>(sC, a.tm_C, c, b, g, bar(kBc), a.status, a.fold);
+        tma_rows<WB>(sB, a.tm_B, c, b, g, bar(kBc), a.status, a.fold);
         load_head(0);
     }
     tc::fence_before();
@@ -1563,6 +1571,7 @@ static void make_args(const ssm_chunk_scan_params* p, Args& a) {
     a.pa = p->headdim; a.pw = min64(p->headdim, P); a.na = p->dstate;
     a.flags = p->flags; a.dt_dtype = p->dt_dtype;
     a.xts = p->x_token_stride ? p->x_token_stride : p->nheads * p->headdim;
+    a.fold = (p->headdim == P && p->dstate == N && p->length % 8 == 0) ? 1 : 0;
     a.x = p->x; a.dt = p->dt; a.A = p->A; a.B = p->B; a.C = p->C; a.D = p->D; a.z = p->z;
     a.dt_bias = p->dt_bias; a.init = p->initial_states;
     a.y = p->y; a.final_state = p->final_state;
@@ -1598,16 +1607,31 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // 16-byte chunk, batch, head): a box of (8, 8, tile_width / 8, 1, 1) is one
 // 8-row group of core matrices of a tile (tile_off layout); rows past
 // `length` and chunks past `width` read as zeros.
+//
+// `fold` (width == tile_width and length a multiple of 8) splits the row into
+// (row mod 8, row group) and merges the heads into the chunk axis instead:
+// (8 elements, row mod 8, 16-byte chunk of the whole row, row group, batch),
+// so one box of (8, 8, tile_width / 8, Q / 8, 1) lands a whole tile in the
+// same layout.  Row groups past length / 8 read as zeros.
 static int encode_rows(CUtensorMap* m, const void* base, int dtype, int64_t batch, int64_t length, int64_t heads,
-                       int64_t width, int64_t tile_width, int64_t token_stride = 0) {
+                       int64_t width, int64_t tile_width, int64_t token_stride, bool fold) {
     auto enc = tensor_map_encoder();
     if (!enc) return fail(SSM_ERR_CUDA, "chunk_scan (tensor cores): cuTensorMapEncodeTiled unavailable");
     if (int s = ensure_context("chunk_scan (tensor cores)")) return s;
     const cuuint64_t es = 2;
-    cuuint64_t dim[5] = {8, (cuuint64_t)length, (cuuint64_t)(width / 8), (cuuint64_t)batch, (cuuint64_t)heads};
     const int64_t ts = token_stride ? token_stride : heads * width;   // elements between tokens
+    cuuint64_t dim[5] = {8, (cuuint64_t)length, (cuuint64_t)(width / 8), (cuuint64_t)batch, (cuuint64_t)heads};
     cuuint64_t str[4] = {(cuuint64_t)ts * es, 16, (cuuint64_t)(length * ts) * es, (cuuint64_t)width * es};
     cuuint32_t box[5] = {8, 8, (cuuint32_t)(tile_width / 8), 1, 1};
+    if (fold) {
+        if (width != tile_width || length % 8)
+            return fail(SSM_ERR_INVALID, "chunk_scan (tensor cores): whole-tile map for a ragged shape");
+        const cuuint64_t fdim[5] = {8, 8, (cuuint64_t)(heads * width / 8), (cuuint64_t)(length / 8), (cuuint64_t)batch};
+        const cuuint64_t fstr[4] = {(cuuint64_t)ts * es, 16, (cuuint64_t)(8 * ts) * es, (cuuint64_t)(length * ts) * es};
+        const cuuint32_t fbox[5] = {8, 8, (cuuint32_t)(tile_width / 8), (cuuint32_t)(Q / 8), 1};
+        for (int i = 0; i < 5; ++i) { dim[i] = fdim[i]; box[i] = fbox[i]; }
+        for (int i = 0; i < 4; ++i) str[i] = fstr[i];
+    }
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     const CUresult r = enc(m, dtype == SSM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
                            const_cast<void*>(base), dim, str, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -1767,9 +1791,9 @@ int fwd(const ssm_chunk_scan_params* p, cudaStream_t s) {
         return fail(SSM_ERR_INVALID, "chunk_scan fwd (tensor cores): x, B, C, z, y and saved must be 16-byte aligned");
     Args a;
     make_args(p, a);
-    if (int e = encode_rows(&a.tm_x, p->x, p->dtype, p->batch, p->length, a.hv, a.pw, P, a.xts)) return e;
-    if (int e = encode_rows(&a.tm_B, p->B, p->dtype, p->batch, p->length, p->ngroups, a.na, N, p->bc_token_stride)) return e;
-    if (int e = encode_rows(&a.tm_C, p->C, p->dtype, p->batch, p->length, p->ngroups, a.na, N, p->bc_token_stride)) return e;
+    if (int e = encode_rows(&a.tm_x, p->x, p->dtype, p->batch, p->length, a.hv, a.pw, P, a.xts, a.fold)) return e;
+    if (int e = encode_rows(&a.tm_B, p->B, p->dtype, p->batch, p->length, p->ngroups, a.na, N, p->bc_token_stride, a.fold)) return e;
+    if (int e = encode_rows(&a.tm_C, p->C, p->dtype, p->batch, p->length, p->ngroups, a.na, N, p->bc_token_stride, a.fold)) return e;
     return p->dtype == SSM_BF16 ? run_fwd_any<__nv_bfloat16>(a, s) : run_fwd_any<__half>(a, s);
 }
 
@@ -1791,10 +1815,10 @@ int bwd(const ssm_chunk_scan_params* p, cudaStream_t s) {
     a.dA_part = reinterpret_cast<float*>(ws + w.dh + w.dci + w.dt);
     a.db_part = reinterpret_cast<float*>(ws + w.dh + w.dci + w.dt + w.part);
     a.dD_part = reinterpret_cast<float*>(ws + w.dh + w.dci + w.dt + 2 * w.part);
-    if (int e = encode_rows(&a.tm_x, p->x, p->dtype, p->batch, p->length, a.hv, a.pw, P, a.xts)) return e;
-    if (int e = encode_rows(&a.tm_dy, p->dy, p->dtype, p->batch, p->length, a.hv, a.pw, P, p->nheads * p->headdim)) return e;
-    if (int e = encode_rows(&a.tm_B, p->B, p->dtype, p->batch, p->length, p->ngroups, a.na, N, p->bc_token_stride)) return e;
-    if (int e = encode_rows(&a.tm_C, p->C, p->dtype, p->batch, p->length, p->ngroups, a.na, N, p->bc_token_stride)) return e;
+    if (int e = encode_rows(&a.tm_x, p->x, p->dtype, p->batch, p->length, a.hv, a.pw, P, a.xts, a.fold)) return e;
+    if (int e = encode_rows(&a.tm_dy, p->dy, p->dtype, p->batch, p->length, a.hv, a.pw, P, p->nheads * p->headdim, a.fold)) return e;
+    if (int e = encode_rows(&a.tm_B, p->B, p->dtype, p->batch, p->length, p->ngroups, a.na, N, p->bc_token_stride, a.fold)) return e;
+    if (int e = encode_rows(&a.tm_C, p->C, p->dtype, p->batch, p->length, p->ngroups, a.na, N, p->bc_token_stride, a.fold)) return e;
     return p->dtype == SSM_BF16 ? run_bwd_any<__nv_bfloat16>(a, p, s) : run_bwd_any<__half>(a, p, s);
 }
 

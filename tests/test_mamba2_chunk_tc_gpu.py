@@ -217,14 +217,17 @@ def test_config3_gradient_slice_vs_oracle():
     assert nat.lib().ssm_take_kernel_error() == 0
 
 
+@pytest.mark.parametrize("length", [300, 296])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_tc_token_strided_inputs(dtype):
+def test_tc_token_strided_inputs(dtype, length):
     """x, B and C as column slices of one wider (batch, length, columns)
     buffer -- the Mamba-2 layer's convolution output -- are read through their
     token strides by the tensor maps and the x-row loads, not copied: y, the
-    final state and every gradient equal the call on dense copies bit for bit."""
+    final state and every gradient equal the call on dense copies bit for bit.
+    Length 296 (a multiple of 8) takes the whole-tile tensor maps, 300 the
+    8-row-group ones."""
     mod = _mod()
-    b, length, h, g = 2, 300, 8, 2
+    b, h, g = 2, 8, 2
     inner, gn, pad = h * P, g * N, 24
     gen = torch.Generator().manual_seed(77)
     wide = (torch.randn(b, length, inner + 2 * gn + pad, generator=gen)).to("cuda", dtype)
@@ -248,6 +251,36 @@ def test_tc_token_strided_inputs(dtype):
     assert mod.last_path() == "cuda"
     for a_, b_ in zip(*runs):
         assert torch.equal(a_, b_)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_tc_whole_tile_maps_match_row_group_maps(dtype):
+    """The two ways of copying a tile agree.  A length that is a multiple of 8
+    (296) copies each 128-row tile with one whole-tile box, zero-filling the
+    rows past the end; a ragged length (300) copies it in 8-row groups.  With
+    the same first 296 rows and dy zero on rows 296-299, the two runs give the
+    same y, dx, dB, dC and d dt on rows 0-295 (the rows past 296 of the longer
+    run only meet zeros there), and the same parameter gradients."""
+    mod = _mod()
+    b, h, g = 2, 8, 2
+    vals = _inputs(b, 300, h, g, seed=41, dtype=dtype)
+    x, dt, A, B, C, D, bias = (vals[k].cuda() for k in ("x", "dt", "A", "B", "C", "D", "dt_bias"))
+    gen = torch.Generator().manual_seed(42)
+    dy = torch.randn(b, 300, h, P, generator=gen).to("cuda", dtype)
+    dy[:, 296:] = 0
+    runs = []
+    for L in (300, 296):
+        leaves = [t[:, :L].contiguous().requires_grad_(True) for t in (x, dt, B, C)]
+        params = [t.clone().requires_grad_(True) for t in (A, D, bias)]
+        y, _ = mod.mamba2_chunk_scan(leaves[0], leaves[1], params[0], leaves[2], leaves[3], chunk_size=128,
+                                     D=params[1], dt_bias=params[2], dt_softplus=True)
+        assert mod.last_path() == "cuda"
+        grads = torch.autograd.grad((y.float() * dy[:, :L].float()).sum(), leaves + params)
+        runs.append(([y.detach()[:, :296]] + [t[:, :296] for t in grads[:4]], grads[4:]))
+    for name, a_, b_ in zip(("y", "dx", "ddt", "dB", "dC"), runs[0][0], runs[1][0]):
+        assert torch.equal(a_, b_), name
+    for name, a_, b_ in zip(("dA", "dD", "ddt_bias"), runs[0][1], runs[1][1]):
+        torch.testing.assert_close(a_, b_, rtol=1e-5, atol=1e-5, msg=name)
 
 
 # head shapes other than 64 x 128: zero-filled tiles (d_head < 64, d_state < 128)
