@@ -612,7 +612,7 @@ __global__ void __launch_bounds__(kStThreads, 2) states2_kernel(const __grid_con
 // position of s's 16-block.  For l past that block exp(cs_l - cs_s) =
 // exp(cs_l - cs_{e(s)}) cf_s, and both factors are <= 1 when cs is
 // non-increasing; the diagonal 16 x 16 blocks use direct exponentials.
-struct MaskSh {
+struct __align__(16) MaskSh {   // 16-byte aligned: read as float2 pairs
     float cs2[Q];
     float d[Q];
     float cf[Q];
@@ -734,9 +734,15 @@ __global__ void __launch_bounds__(kOutThreads, 2) outputs_kernel(const __grid_co
                     tc::tmem_wait_ld(v);
                     if (16 * j <= l) {
                         if (16 * j + 15 < l) {
-                            const float rf = exp2_mufu(csl - msh.cs2[16 * j + 15]);
+                            const float2 rf = f2(exp2_mufu(csl - msh.cs2[16 * j + 15]));
 #pragma unroll
-                            for (int k = 0; k < 16; ++k) v[k] *= rf * msh.cf[16 * j + k] * msh.d[16 * j + k];
+                            for (int k = 0; k < 16; k += 2) {   // v (rf cf d), in pairs
+                                const float2 w = mul2(mul2(rf, *reinterpret_cast<const float2*>(&msh.cf[16 * j + k])),
+                                                      *reinterpret_cast<const float2*>(&msh.d[16 * j + k]));
+                                const float2 r = mul2(make_float2(v[k], v[k + 1]), w);
+                                v[k] = r.x;
+                                v[k + 1] = r.y;
+                            }
                         } else {
 #pragma unroll
                             for (int k = 0; k < 16; ++k) {
@@ -1064,9 +1070,14 @@ __device__ __forceinline__ float warp_colsum16(float* v) {
 //   m1   MMA -> compute   dY X^T (and, for the first head, G) is in TMEM
 //   mask compute -> MMA   Mh, dG, exp(cs) dy, w o x written; S read
 //   m2   MMA -> compute   the eight GEMMs of the head are done
+//   ep   compute -> MMA   the epilogue has read the dy tile
+//   lh   copies -> compute  the head's x, dy, H and dH tiles landed
 // While the eight GEMMs run, the compute warps fetch the epilogue's global
-// inputs and compute the next head's step quantities; right after reading S
-// they start the next head's tile loads, which then overlap the epilogue.
+// inputs and compute the next head's step quantities.  The MMA warp copies
+// the next head's x, H and dH tiles in as soon as the GEMMs are done with
+// this head's (during the epilogue) and its dy tile once the epilogue has
+// read this one, so the copies' latency hides behind the epilogue and the
+// per-head scalar tail.
 constexpr int kGC = 256;                       // compute threads
 constexpr int kGradThreads = kGC + 32;
 
@@ -1094,9 +1105,9 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
     unsigned char* sH = sXW + kTileX;           // H_c^T
     unsigned char* sD = sH + kTileH;            // dH_{c+1}^T
     __shared__ GradSh sh;
-    __shared__ __align__(8) uint64_t bars[6];
+    __shared__ __align__(8) uint64_t bars[7];
     __shared__ uint32_t tbase;
-    enum { kBc = 0, kIn = 1, kM1 = 2, kMask = 3, kM2 = 4, kLh = 5 };   // kLh: a head's tiles landed
+    enum { kBc = 0, kIn = 1, kM1 = 2, kMask = 3, kM2 = 4, kLh = 5, kEp = 6 };
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool mma_warp = warp == kGC / 32;
@@ -1116,16 +1127,22 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
     const uint32_t bar0 = tc::smem_u32(&bars[0]);
     auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
 
-    uint32_t lpend = ~0u;                     // parity of a head load still in flight (thread 0)
-    auto load_head = [&](int64_t hh) {            // thread 0 only
+    // parity of a head load still in flight: head 0's (issued by thread 0), the
+    // later heads' (issued by lane 0 of the MMA warp)
+    uint32_t lpend = ~0u;
+    // one thread: the x, H and dH tiles of head hh, with the transaction count
+    // of all four tiles, so that the phase also waits for load_y(hh)
+    auto load_xhd = [&](int64_t hh) {
         const int64_t h = g * a.hpg + hh;
         const int64_t bhc = (b * H + h) * a.nc + c;
         tc::mbar_expect_tx(bar(kLh), 2 * kRowsX + 2 * kTileH);
         tma_rows<WX>(sX, a.tm_x, c, b, h, bar(kLh), a.status, a.fold);
-        tma_rows<WX>(sY, a.tm_dy, c, b, h, bar(kLh), a.status, a.fold);
-        tc::bulk_load(tc::smem_u32(sH), a.Ht + ((size_t)(b * H + h) * a.nc + c) * kTileH, kTileH, bar(kLh));
+        tc::bulk_load(tc::smem_u32(sH), a.Ht + (size_t)bhc * kTileH, kTileH, bar(kLh));
         tc::bulk_load(tc::smem_u32(sD), a.dHt + (size_t)bhc * kTileH, kTileH, bar(kLh));
         lpend = (uint32_t)(hh & 1);
+    };
+    auto load_y = [&](int64_t hh) {
+        tma_rows<WX>(sY, a.tm_dy, c, b, g * a.hpg + hh, bar(kLh), a.status, a.fold);
     };
 
     if (mma_warp) tc::tmem_alloc(tc::smem_u32(&tbase), 512);
@@ -1136,11 +1153,13 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
         tc::mbar_init(bar(kMask), kGC);
         tc::mbar_init(bar(kM2), 1);
         tc::mbar_init(bar(kLh), 1);
+        tc::mbar_init(bar(kEp), kGC);
         tc::fence_mbar_init();
         tc::mbar_expect_tx(bar(kBc), 2 * kRowsB);      // the MMA warp waits for these directly
         tma_rows<WB>(sC, a.tm_C, c, b, g, bar(kBc), a.status, a.fold);
         tma_rows<WB>(sB, a.tm_B, c, b, g, bar(kBc), a.status, a.fold);
-        load_head(0);
+        load_xhd(0);
+        load_y(0);
     }
     tc::fence_before();
     __syncthreads();
@@ -1213,8 +1232,20 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
                 tc::commit(bar(kM2));
             }
             __syncwarp();
+            if (hh + 1 < a.hpg) {
+                // the next head's tiles: x, H and dH once the GEMMs are done with
+                // this head's, dy once the epilogue has read this one
+                if (!wait_warp(kM2, par)) { ok = false; break; }
+                if (lane == 0) load_xhd(hh + 1);
+                __syncwarp();
+                const bool ep = wait_warp(kEp, par);
+                if (lane == 0) load_y(hh + 1);   // also when the wait gave up: the phase must complete
+                __syncwarp();
+                if (!ep) { ok = false; break; }
+            }
         }
         if (!ok && lane == 0) report(a, 44);
+        if (lane == 0 && lpend != ~0u) tc::mbar_wait(bar(kLh), lpend);   // no copy may land after exit
     } else {
         // --------------------------------------------------- compute warps --
         const bool pos_thread = tid < Q;           // owns chunk position s = tid
@@ -1302,9 +1333,13 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
                         tc::tmem_pin(dm);
                         float e[16];
                         if (16 * j + 15 < l) {
-                            const float rf = exp2_mufu(csl - sh.m.cs2[16 * j + 15]);
+                            const float2 rf = f2(exp2_mufu(csl - sh.m.cs2[16 * j + 15]));
 #pragma unroll
-                            for (int k = 0; k < 16; ++k) e[k] = rf * sh.m.cf[16 * j + k];
+                            for (int k = 0; k < 16; k += 2) {
+                                const float2 v = mul2(rf, *reinterpret_cast<const float2*>(&sh.m.cf[16 * j + k]));
+                                e[k] = v.x;
+                                e[k + 1] = v.y;
+                            }
                         } else {
 #pragma unroll
                             for (int k = 0; k < 16; ++k) {
@@ -1312,15 +1347,21 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
                                 e[k] = s <= l ? exp2_mufu(csl - sh.m.cs2[s]) : 0.0f;
                             }
                         }
+                        // the products in pairs (packed fp32, each rounded as alone)
                         float mh[16], dg[16];
 #pragma unroll
-                        for (int k = 0; k < 16; ++k) {
-                            const float ed = e[k] * sh.m.d[16 * j + k];
-                            const float gd = gv[k] * dm[k];
-                            mh[k] = gv[k] * ed;
-                            dg[k] = dm[k] * ed;
-                            E[k] = gd * e[k];
-                            rowsum = fmaf(gd, ed, rowsum);
+                        for (int k = 0; k < 16; k += 2) {
+                            const float2 e2 = make_float2(e[k], e[k + 1]);
+                            const float2 g2 = make_float2(gv[k], gv[k + 1]);
+                            const float2 m2 = make_float2(dm[k], dm[k + 1]);
+                            const float2 ed = mul2(e2, *reinterpret_cast<const float2*>(&sh.m.d[16 * j + k]));
+                            const float2 gd = mul2(g2, m2);
+                            const float2 mv = mul2(g2, ed), dv = mul2(m2, ed), ev = mul2(gd, e2);
+                            mh[k] = mv.x; mh[k + 1] = mv.y;
+                            dg[k] = dv.x; dg[k + 1] = dv.y;
+                            E[k] = ev.x; E[k + 1] = ev.y;
+                            rowsum = fmaf(gd.x, ed.x, rowsum);
+                            rowsum = fmaf(gd.y, ed.y, rowsum);
                         }
                         m0 = pack8<T>(mh); m1 = pack8<T>(mh + 8);
                         g0 = pack8<T>(dg); g1 = pack8<T>(dg + 8);
@@ -1417,12 +1458,10 @@ __global__ void __launch_bounds__(kGradThreads, 1) grads_kernel(const __grid_con
                 }
                 sh.vp[hf][s] = vpart * eTs;
             }
+            tc::mbar_arrive(bar(kEp));               // this thread is done with the dy tile
             tc::fence_before();                      // S read: the next head's dY X^T may overwrite it
-            gsync<kGC>();                            // every thread is done with the tiles; sh.vp complete
-            if (hh + 1 < a.hpg) {
-                if (tid == 0) load_head(hh + 1);
-                mask_factors<kGC>(sh.m, st_next);    // the scalars below use st, not sh.m
-            }
+            gsync<kGC>();                            // sh.vp complete
+            if (hh + 1 < a.hpg) mask_factors<kGC>(sh.m, st_next);   // the scalars below use st, not sh.m
             float dcs = 0.0f, dd_direct = 0.0f, dv = 0.0f;
             if (pos_thread) {
                 const float v_s = sh.vp[0][tid] + sh.vp[1][tid];

@@ -136,11 +136,17 @@ __device__ __forceinline__ void mbar_init(uint32_t mbar, uint32_t count) {
 __device__ __forceinline__ void fence_mbar_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
+// One try_wait, with a suspend-time hint of 64 ns: the thread sleeps at most
+// that long before it polls again.  Without a hint (the system's own limit)
+// warps were seen resuming 300 to 1,500 cycles after the phase completed; with
+// it the SSD backward at BASELINE config 3 ran 3.28 -> 3.17 ms (hints of 20 and
+// 200 ns: 3.19, 3.18; polling with test_wait: no gain).  A call still returns
+// false after the hint, so the callers' iteration limits keep every wait bounded.
 __device__ __forceinline__ bool mbar_try_wait(uint32_t mbar, uint32_t parity) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred P1;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2, 64;\n\t"
         "selp.b32 %0, 1, 0, P1;\n\t}\n"
         : "=r"(done) : "r"(mbar), "r"(parity) : "memory");
     return done != 0;
