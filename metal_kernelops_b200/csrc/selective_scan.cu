@@ -1341,8 +1341,16 @@ extern "C" int ssm_selective_scan_fwd(const ssm_selective_scan_params* p, void* 
         a.seg_p = reinterpret_cast<float*>(reinterpret_cast<char*>(p->workspace) + sg);
     }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (a.nseg > 1)
-        if (int s = by_dtype_fwd(p->act_dtype, c, a, st, 0)) return s;
+    if (a.nseg > 1) {                         // segment summaries (TMA-staged where it applies), combine
+        int s = fwd_sum_tma(p, c, a, st);
+        if (s == SSM_ERR_UNSUPPORTED) {
+            s = by_dtype_fwd(p->act_dtype, c, a, st, 0);
+        } else if (s == SSM_OK) {
+            combine_fwd_kernel<<<combine_blocks(a), 256, 0, st>>>(a);
+            s = check_launch("selective_scan fwd combine");
+        }
+        if (s) return s;
+    }
     const int s = fwd_tma(p, c, a, st);       // the TMA-staged main pass where it applies
     if (s != SSM_ERR_UNSUPPORTED) return s;
     return by_dtype_fwd(p->act_dtype, c, a, st, 1);
@@ -1381,8 +1389,16 @@ extern "C" int ssm_selective_scan_bwd(const ssm_selective_scan_params* p, void* 
         a.seg_x = reinterpret_cast<float*>(ws + 2 * w.bc + w.da + 2 * w.dd);
         a.seg_p = reinterpret_cast<float*>(ws + 2 * w.bc + w.da + 2 * w.dd + w.sg);
     }
-    if (a.nseg > 1)
-        if (int s = by_dtype_bwd(p->act_dtype, c, a, st, 0)) return s;
+    if (a.nseg > 1) {                         // adjoint summaries (TMA-staged where it applies), combine
+        int s = bwd_sum_tma(p, c, a, st);
+        if (s == SSM_ERR_UNSUPPORTED) {
+            s = by_dtype_bwd(p->act_dtype, c, a, st, 0);
+        } else if (s == SSM_OK) {
+            combine_bwd_kernel<<<combine_blocks(a), 256, 0, st>>>(a);
+            s = check_launch("selective_scan bwd combine");
+        }
+        if (s) return s;
+    }
     int s = bwd_tma(p, c, a, st);             // the TMA-staged main pass where it applies
     if (s == SSM_ERR_UNSUPPORTED) s = by_dtype_bwd(p->act_dtype, c, a, st, 1);
     if (s) return s;

@@ -326,6 +326,299 @@ fwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
     if (tid == 0) bulk_wait_all();
 }
 
+// The forward's segment summary (nseg > 1, every segment but the last): the
+// recurrence over this CTA's segment from a zero state, leaving the end state
+// and the product of the decays, with the same arithmetic as the summary mode
+// of the plain fwd_kernel.  Only u, delta and B are read.  Once phase 0 has
+// turned a chunk's tiles into the fp32 step scalars and B, the tiles are dead,
+// so the next chunk's copies are issued right then and land while this
+// chunk's recurrence runs.
+template <typename T, int NPT, int LPC>
+__global__ void __launch_bounds__(kThreads, NPT <= 8 ? 9 : 1)
+fwd_sum_tma_kernel(const __grid_constant__ TmaArgs ta) {
+    const Args& a = ta.a;
+    constexpr int CPW = 32 / LPC;
+    constexpr int CPC = CPW * kWarps;
+    constexpr int NP = NPT * LPC;
+    constexpr int NH = NPT / 2;
+    constexpr int K = kChunk;
+    constexpr int FS = K + 1;
+    using Lay = FwdTmaLayout<T, CPC, NP>;
+    static_assert(NPT % 4 == 0 && K == 16 && CPC % 16 == 0, "launch shape");
+
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((128u - (tc::smem_u32(smem_raw) & 127u)) & 127u);
+    const T* ru = reinterpret_cast<const T*>(smem + Lay::o_u);
+    const T* rd = reinterpret_cast<const T*>(smem + Lay::o_d);
+    const T* rB = reinterpret_cast<const T*>(smem + Lay::o_B);
+    float* Bs = reinterpret_cast<float*>(smem + Lay::o_bc);
+    float2* dvu = reinterpret_cast<float2*>(smem + Lay::o_dvu);   // (delta' log2e, delta' u)
+    float* bch = reinterpret_cast<float*>(smem + Lay::o_ch);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + Lay::o_bar);
+    int* okp = reinterpret_cast<int*>(smem + Lay::o_bar + 8);
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int cw = lane / LPC, sub = lane % LPC;
+    const int c = warp * CPW + cw;
+    const int64_t ct = blockIdx.x % a.nct, seg = blockIdx.x / a.nct, g = blockIdx.y, b = blockIdx.z;
+    const int64_t dl0 = ct * CPC;
+    const int rows = (int)min64(CPC, a.per_group - dl0);
+    const int64_t d0 = g * a.per_group + dl0;
+    const bool cvalid = c < rows;
+    const int64_t d = d0 + c;
+    const int64_t N = a.dstate, L = a.length;
+    const bool has_bias = a.flags & SSM_HAS_BIAS, softplus = a.flags & SSM_SOFTPLUS;
+    const int64_t bg = b * a.groups + g;
+    const int64_t sx = ((b * a.nseg + seg) * a.dim + d) * N;
+    const uint32_t mb = tc::smem_u32(bar);
+    const uint32_t tx = (uint32_t)(2 * CPC * K * sizeof(T) + NP * K * sizeof(T));
+
+    auto issue = [&](int64_t tile) {   // thread 0: this chunk's u, delta and B tiles
+        const int t0 = (int)(tile * K);
+        tc::mbar_expect_tx(mb, tx);
+        tma_load4(tc::smem_u32(ru), &ta.m_u, t0, (int)dl0, (int)g, (int)b, mb);
+        tma_load4(tc::smem_u32(rd), &ta.m_d, t0, (int)dl0, (int)g, (int)b, mb);
+        tma_load3(tc::smem_u32(rB), &ta.m_B, t0, 0, (int)bg, mb);
+    };
+
+    const int64_t tile_lo = seg * a.seg_chunks;
+    const int64_t tile_hi = min64(tile_lo + a.seg_chunks, a.nchunks);
+    if (tid == 0) {
+        tc::mbar_init(mb, 1);
+        tc::fence_mbar_init();
+        issue(tile_lo);
+    }
+    for (int i = tid; i < CPC; i += kThreads) bch[i] = (has_bias && i < rows) ? a.delta_bias[d0 + i] : 0.0f;
+    float2 An2[NH], x2[NH], p2[NH];
+#pragma unroll
+    for (int j = 0; j < NH; ++j) {
+        const int n = sub * NPT + 2 * j;
+        An2[j] = cvalid ? make_float2(a.A[d * N + n], a.A[d * N + n + 1]) : make_float2(0.0f, 0.0f);
+        x2[j] = make_float2(0.0f, 0.0f);
+        p2[j] = make_float2(1.0f, 1.0f);
+    }
+
+    for (int64_t tile = tile_lo; tile < tile_hi; ++tile) {
+        const int len = (int)min64(K, L - tile * K);
+        if (tid == 0) okp[0] = tc::mbar_wait(mb, (uint32_t)((tile - tile_lo) & 1), kPolls) ? 1 : 0;
+        __syncthreads();                       // also: the previous chunk's recurrence is done
+        if (!okp[0]) {
+            if (tid == 0) report(a, 72);
+            return;                            // no copy is in flight: the wait covered the only one
+        }
+        // phase 0: per-step scalars (two steps per item) and B to fp32 [t][n]
+#pragma unroll
+        for (int k = 0; k < CPC / 16; ++k) {
+            const int cc = (tid >> 3) + 16 * k, t = 2 * (tid & 7);
+            const float2 dr = Io2<T>::ld(&rd[cc * K + t]);
+            const float2 ur = Io2<T>::ld(&ru[cc * K + t]);
+            float2 dv = add2(dr, f2(bch[cc]));
+            if (softplus) dv = softplus2_fast(dv);
+            const float2 dl = mul2(dv, f2(kLog2e)), du = mul2(dv, ur);
+            dvu[cc * FS + t] = make_float2(dl.x, du.x);
+            dvu[cc * FS + t + 1] = make_float2(dl.y, du.y);
+        }
+        for (int i = tid; i < NP * K; i += kThreads) {
+            const int t = i / NP, n = i % NP;
+            Bs[t * NP + n] = ldf(&rB[n * K + t]);
+        }
+        __syncthreads();                       // the tiles are read: the next chunk's may land
+        if (tid == 0 && tile + 1 < tile_hi) issue(tile + 1);
+
+        // phase 1: the recurrence from a zero state, and the product of the decays
+        const float2* vr = dvu + c * FS;
+        auto step = [&](int t) {
+            const float2 v = vr[t];
+            const float2 dl2 = make_float2(v.x, v.x), du2 = make_float2(v.y, v.y);
+            const float4* B4 = reinterpret_cast<const float4*>(Bs + t * NP + sub * NPT);
+#pragma unroll
+            for (int q = 0; q < NPT / 4; ++q) {
+                const float4 bq = B4[q];
+                const float2 a0 = __fmul2_rn(dl2, An2[2 * q]);
+                const float2 a1 = __fmul2_rn(dl2, An2[2 * q + 1]);
+                const float2 e0 = make_float2(exp2_mufu(a0.x), exp2_mufu(a0.y));
+                const float2 e1 = make_float2(exp2_mufu(a1.x), exp2_mufu(a1.y));
+                x2[2 * q] = __ffma2_rn(e0, x2[2 * q], __fmul2_rn(du2, make_float2(bq.x, bq.y)));
+                x2[2 * q + 1] = __ffma2_rn(e1, x2[2 * q + 1], __fmul2_rn(du2, make_float2(bq.z, bq.w)));
+                p2[2 * q] = __fmul2_rn(p2[2 * q], e0);
+                p2[2 * q + 1] = __fmul2_rn(p2[2 * q + 1], e1);
+            }
+        };
+        if (len == K) {
+#pragma unroll
+            for (int t = 0; t < K; ++t) step(t);
+        } else {
+#pragma unroll 1
+            for (int t = 0; t < len; ++t) step(t);
+        }
+    }
+    if (cvalid) {
+#pragma unroll
+        for (int j = 0; j < NH; ++j) {
+            const int n = sub * NPT + 2 * j;
+            a.seg_x[sx + n] = x2[j].x; a.seg_p[sx + n] = p2[j].x;
+            a.seg_x[sx + n + 1] = x2[j].y; a.seg_p[sx + n + 1] = p2[j].y;
+        }
+    }
+}
+
+// The backward's segment summary (nseg > 1, every segment but the first): the
+// adjoint recurrence q <- a_t (g_t C_t + q) over this CTA's segment, walked
+// backwards from a zero adjoint at its end (g_t = dout_t, times the silu(z)
+// gate), leaving the adjoint at the segment's start and the product of the
+// decays, with the same arithmetic as the plain adj_kernel.  Reads delta,
+// dout, z and C; like the forward summary, the copies of the chunk before this
+// one are issued as soon as phase 0 has read this chunk's tiles.
+template <typename T, int CPC, int NP>
+struct AdjTmaLayout {
+    static constexpr int K = kChunk;
+    static constexpr int FS = K + 1;
+    static constexpr size_t tile = al128((size_t)CPC * K * sizeof(T));
+    static constexpr size_t bct = al128((size_t)NP * K * sizeof(T));
+    static constexpr size_t o_d = 0, o_g = tile, o_z = 2 * tile, o_C = 3 * tile;
+    static constexpr size_t o_c = o_C + bct;                              // fp32 [K][NP]
+    static constexpr size_t o_dv = o_c + (size_t)K * NP * 4;              // [CPC][FS] float2
+    static constexpr size_t o_ch = o_dv + (size_t)CPC * FS * 8;           // [CPC] float
+    static constexpr size_t o_bar = (o_ch + CPC * 4 + 7) / 8 * 8;
+    static constexpr size_t bytes = o_bar + 16;
+};
+
+template <typename T, int NPT, int LPC>
+__global__ void __launch_bounds__(kThreads, NPT <= 8 ? 8 : 1)
+adj_tma_kernel(const __grid_constant__ TmaArgs ta) {
+    const Args& a = ta.a;
+    constexpr int CPW = 32 / LPC;
+    constexpr int CPC = CPW * kWarps;
+    constexpr int NP = NPT * LPC;
+    constexpr int NH = NPT / 2;
+    constexpr int K = kChunk;
+    constexpr int FS = K + 1;
+    using Lay = AdjTmaLayout<T, CPC, NP>;
+    static_assert(NPT % 4 == 0 && K == 16 && CPC % 16 == 0, "launch shape");
+
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    unsigned char* smem = smem_raw + ((128u - (tc::smem_u32(smem_raw) & 127u)) & 127u);
+    const T* rd = reinterpret_cast<const T*>(smem + Lay::o_d);
+    const T* rg = reinterpret_cast<const T*>(smem + Lay::o_g);
+    const T* rz = reinterpret_cast<const T*>(smem + Lay::o_z);
+    const T* rC = reinterpret_cast<const T*>(smem + Lay::o_C);
+    float* Cs = reinterpret_cast<float*>(smem + Lay::o_c);
+    float2* dv = reinterpret_cast<float2*>(smem + Lay::o_dv);     // (delta' log2e, g)
+    float* bch = reinterpret_cast<float*>(smem + Lay::o_ch);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + Lay::o_bar);
+    int* okp = reinterpret_cast<int*>(smem + Lay::o_bar + 8);
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int cw = lane / LPC, sub = lane % LPC;
+    const int c = warp * CPW + cw;
+    const int64_t ct = blockIdx.x % a.nct, seg = blockIdx.x / a.nct + 1, g = blockIdx.y, b = blockIdx.z;
+    const int64_t dl0 = ct * CPC;
+    const int rows = (int)min64(CPC, a.per_group - dl0);
+    const int64_t d0 = g * a.per_group + dl0;
+    const bool cvalid = c < rows;
+    const int64_t d = d0 + c;
+    const int64_t N = a.dstate, L = a.length;
+    const bool has_z = a.flags & SSM_HAS_Z;
+    const bool has_bias = a.flags & SSM_HAS_BIAS, softplus = a.flags & SSM_SOFTPLUS;
+    const int64_t bg = b * a.groups + g;
+    const int64_t sx = ((b * a.nseg + seg) * a.dim + d) * N;
+    const uint32_t mb = tc::smem_u32(bar);
+    const uint32_t tx = (uint32_t)((has_z ? 3 : 2) * CPC * K * sizeof(T) + NP * K * sizeof(T));
+
+    auto issue = [&](int64_t tile) {   // thread 0: this chunk's delta, dout, z and C tiles
+        const int t0 = (int)(tile * K);
+        tc::mbar_expect_tx(mb, tx);
+        tma_load4(tc::smem_u32(rd), &ta.m_d, t0, (int)dl0, (int)g, (int)b, mb);
+        tma_load4(tc::smem_u32(rg), &ta.m_g, t0, (int)dl0, (int)g, (int)b, mb);
+        if (has_z) tma_load4(tc::smem_u32(rz), &ta.m_z, t0, (int)dl0, (int)g, (int)b, mb);
+        tma_load3(tc::smem_u32(rC), &ta.m_C, t0, 0, (int)bg, mb);
+    };
+
+    const int64_t tile_lo = seg * a.seg_chunks;
+    const int64_t tile_hi = min64(tile_lo + a.seg_chunks, a.nchunks);
+    if (tid == 0) {
+        tc::mbar_init(mb, 1);
+        tc::fence_mbar_init();
+        issue(tile_hi - 1);
+    }
+    for (int i = tid; i < CPC; i += kThreads) bch[i] = (has_bias && i < rows) ? a.delta_bias[d0 + i] : 0.0f;
+    float2 An2[NH], q2[NH], p2[NH];
+#pragma unroll
+    for (int j = 0; j < NH; ++j) {
+        const int n = sub * NPT + 2 * j;
+        An2[j] = cvalid ? make_float2(a.A[d * N + n], a.A[d * N + n + 1]) : make_float2(0.0f, 0.0f);
+        q2[j] = make_float2(0.0f, 0.0f);
+        p2[j] = make_float2(1.0f, 1.0f);
+    }
+    for (int64_t tile = tile_hi - 1; tile >= tile_lo; --tile) {
+        const int len = (int)min64(K, L - tile * K);
+        if (tid == 0) okp[0] = tc::mbar_wait(mb, (uint32_t)((tile_hi - 1 - tile) & 1), kPolls) ? 1 : 0;
+        __syncthreads();                       // also: the later chunk's recurrence is done
+        if (!okp[0]) {
+            if (tid == 0) report(a, 73);
+            return;                            // no copy is in flight: the wait covered the only one
+        }
+        // phase 0: per-step scalars (two steps per item) and C to fp32 [t][n]
+#pragma unroll
+        for (int k = 0; k < CPC / 16; ++k) {
+            const int cc = (tid >> 3) + 16 * k, t = 2 * (tid & 7);
+            const float2 dr = Io2<T>::ld(&rd[cc * K + t]);
+            float2 go = Io2<T>::ld(&rg[cc * K + t]);
+            float2 dl = add2(dr, f2(bch[cc]));
+            if (softplus) dl = softplus2_fast(dl);
+            if (has_z) {
+                const float2 zr = Io2<T>::ld(&rz[cc * K + t]);
+                go = mul2(go, mul2(zr, sigmoid2_t<T>(zr)));
+            }
+            dl = mul2(dl, f2(kLog2e));
+            dv[cc * FS + t] = make_float2(dl.x, go.x);
+            dv[cc * FS + t + 1] = make_float2(dl.y, go.y);
+        }
+        for (int i = tid; i < NP * K; i += kThreads) {
+            const int t = i / NP, n = i % NP;
+            Cs[t * NP + n] = ldf(&rC[n * K + t]);
+        }
+        __syncthreads();                       // the tiles are read: the earlier chunk's may land
+        if (tid == 0 && tile > tile_lo) issue(tile - 1);
+
+        const float2* vr = dv + c * FS;
+        auto step = [&](int t) {
+            const float2 v = vr[t];
+            const float2 dl2 = make_float2(v.x, v.x), g2 = make_float2(v.y, v.y);
+            const float4* C4 = reinterpret_cast<const float4*>(Cs + t * NP + sub * NPT);
+#pragma unroll
+            for (int q = 0; q < NPT / 4; ++q) {
+                const float4 cq = C4[q];
+                const float2 a0 = __fmul2_rn(dl2, An2[2 * q]);
+                const float2 a1 = __fmul2_rn(dl2, An2[2 * q + 1]);
+                const float2 e0 = make_float2(exp2_mufu(a0.x), exp2_mufu(a0.y));
+                const float2 e1 = make_float2(exp2_mufu(a1.x), exp2_mufu(a1.y));
+                q2[2 * q] = __fmul2_rn(__ffma2_rn(g2, make_float2(cq.x, cq.y), q2[2 * q]), e0);
+                q2[2 * q + 1] = __fmul2_rn(__ffma2_rn(g2, make_float2(cq.z, cq.w), q2[2 * q + 1]), e1);
+                p2[2 * q] = __fmul2_rn(p2[2 * q], e0);
+                p2[2 * q + 1] = __fmul2_rn(p2[2 * q + 1], e1);
+            }
+        };
+        if (len == K) {
+#pragma unroll
+            for (int t = K - 1; t >= 0; --t) step(t);
+        } else {
+#pragma unroll 1
+            for (int t = len - 1; t >= 0; --t) step(t);
+        }
+    }
+    if (cvalid) {
+#pragma unroll
+        for (int j = 0; j < NH; ++j) {
+            const int n = sub * NPT + 2 * j;
+            a.seg_x[sx + n] = q2[j].x; a.seg_p[sx + n] = p2[j].x;
+            a.seg_x[sx + n + 1] = q2[j].y; a.seg_p[sx + n + 1] = p2[j].y;
+        }
+    }
+}
+
 // ----------------------------------------------------------------- backward --
 template <typename T, int CPC, int NP, int NPT>
 struct BwdTmaLayout {
@@ -937,6 +1230,30 @@ static int run_fwd_tma(const TmaArgs& ta, cudaStream_t st) {
 }
 
 template <typename T, int NPT, int LPC>
+static int run_fwd_sum_tma(const TmaArgs& ta, cudaStream_t st) {
+    constexpr int CPC = 32 / LPC * kWarps;
+    const size_t sm = FwdTmaLayout<T, CPC, NPT * LPC>::bytes + 128;
+    auto k = fwd_sum_tma_kernel<T, NPT, LPC>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
+        return check_launch("selective_scan fwd summary (TMA): smem attribute");
+    const Args& a = ta.a;
+    k<<<dim3((unsigned)(a.nct * (a.nseg - 1)), (unsigned)a.groups, (unsigned)a.batch), kThreads, sm, st>>>(ta);
+    return check_launch("selective_scan fwd summary (TMA)");
+}
+
+template <typename T, int NPT, int LPC>
+static int run_adj_tma(const TmaArgs& ta, cudaStream_t st) {
+    constexpr int CPC = 32 / LPC * kWarps;
+    const size_t sm = AdjTmaLayout<T, CPC, NPT * LPC>::bytes + 128;
+    auto k = adj_tma_kernel<T, NPT, LPC>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
+        return check_launch("selective_scan bwd summary (TMA): smem attribute");
+    const Args& a = ta.a;
+    k<<<dim3((unsigned)(a.nct * (a.nseg - 1)), (unsigned)a.groups, (unsigned)a.batch), kThreads, sm, st>>>(ta);
+    return check_launch("selective_scan bwd summary (TMA)");
+}
+
+template <typename T, int NPT, int LPC>
 static int run_bwd_tma(const TmaArgs& ta, cudaStream_t st) {
     constexpr int CPC = 32 / LPC * kWarps;
     const size_t sm = BwdTmaLayout<T, CPC, NPT * LPC, NPT>::bytes + 128;
@@ -976,6 +1293,21 @@ static int dispatch_fwd_tma(const Cfg& c, const TmaArgs& ta, cudaStream_t st) {
 }
 
 template <typename T>
+static int dispatch_fwd_sum_tma(const Cfg& c, const TmaArgs& ta, cudaStream_t st) {
+    switch (c.npt * 100 + c.lpc) {
+        case 401: return run_fwd_sum_tma<T, 4, 1>(ta, st);
+        case 402: return run_fwd_sum_tma<T, 4, 2>(ta, st);
+        case 404: return run_fwd_sum_tma<T, 4, 4>(ta, st);
+        case 801: return run_fwd_sum_tma<T, 8, 1>(ta, st);
+        case 802: return run_fwd_sum_tma<T, 8, 2>(ta, st);
+        case 804: return run_fwd_sum_tma<T, 8, 4>(ta, st);
+        case 1602: return run_fwd_sum_tma<T, 16, 2>(ta, st);
+        case 1604: return run_fwd_sum_tma<T, 16, 4>(ta, st);
+        default: return SSM_ERR_UNSUPPORTED;
+    }
+}
+
+template <typename T>
 static int dispatch_bwd_tma(const Cfg& c, const TmaArgs& ta, cudaStream_t st) {
     switch (c.npt * 100 + c.lpc) {
         case 401: return run_bwd_tma<T, 4, 1>(ta, st);
@@ -1006,6 +1338,57 @@ int fwd_tma(const ssm_selective_scan_params* p, const Cfg& c, const Args& a, cud
         case SSM_F32: return dispatch_fwd_tma<float>(c, ta, st);
         case SSM_BF16: return dispatch_fwd_tma<__nv_bfloat16>(c, ta, st);
         default: return dispatch_fwd_tma<__half>(c, ta, st);
+    }
+}
+
+// The forward's segment summaries through TMA (SSM_ERR_UNSUPPORTED where the
+// TMA conditions do not hold: the caller then runs the plain summary pass).
+int fwd_sum_tma(const ssm_selective_scan_params* p, const Cfg& c, const Args& a, cudaStream_t st) {
+    if (a.nseg < 2 || !tma_ok(p, c, false)) return SSM_ERR_UNSUPPORTED;
+    if (int s = ensure_context("selective_scan fwd summary (TMA)")) return s;
+    const int cpc = 32 / c.lpc * kWarps, np = c.npt * c.lpc;
+    TmaArgs ta;
+    ta.a = a;
+    if (int s = encode_act(&ta.m_u, p->u, p, cpc)) return s;
+    if (int s = encode_act(&ta.m_d, p->delta, p, cpc)) return s;
+    if (int s = encode_bc(&ta.m_B, p->B, p, np)) return s;
+    switch (p->act_dtype) {
+        case SSM_F32: return dispatch_fwd_sum_tma<float>(c, ta, st);
+        case SSM_BF16: return dispatch_fwd_sum_tma<__nv_bfloat16>(c, ta, st);
+        default: return dispatch_fwd_sum_tma<__half>(c, ta, st);
+    }
+}
+
+// The backward's segment summaries through TMA, for the launch shapes the TMA
+// backward itself runs (SSM_ERR_UNSUPPORTED otherwise: the caller then runs
+// the plain summary pass).
+int bwd_sum_tma(const ssm_selective_scan_params* p, const Cfg& c, const Args& a, cudaStream_t st) {
+    if (a.nseg < 2 || !tma_ok(p, c, true)) return SSM_ERR_UNSUPPORTED;
+    if (int s = ensure_context("selective_scan bwd summary (TMA)")) return s;
+    const int cpc = 32 / c.lpc * kWarps, np = c.npt * c.lpc;
+    TmaArgs ta;
+    ta.a = a;
+    if (int s = encode_act(&ta.m_d, p->delta, p, cpc)) return s;
+    if (int s = encode_act(&ta.m_g, p->dout, p, cpc)) return s;
+    if (int s = encode_act(&ta.m_z, (p->flags & SSM_HAS_Z) ? p->z : p->delta, p, cpc)) return s;
+    if (int s = encode_bc(&ta.m_C, p->C, p, np)) return s;
+    const int key = c.npt * 100 + c.lpc;
+    auto by = [&](auto tag) -> int {
+        using T = decltype(tag);
+        switch (key) {
+            case 401: return run_adj_tma<T, 4, 1>(ta, st);
+            case 404: return run_adj_tma<T, 4, 4>(ta, st);
+            case 801: return run_adj_tma<T, 8, 1>(ta, st);
+            case 802: return run_adj_tma<T, 8, 2>(ta, st);
+            case 804: return run_adj_tma<T, 8, 4>(ta, st);
+            case 808: return run_adj_tma<T, 8, 8>(ta, st);
+            default: return SSM_ERR_UNSUPPORTED;
+        }
+    };
+    switch (p->act_dtype) {
+        case SSM_F32: return by(float{});
+        case SSM_BF16: return by(__nv_bfloat16{});
+        default: return by(__half{});
     }
 }
 

@@ -121,7 +121,9 @@ struct Cfg { int npt = 4, lpc = 4; };   // dstate > 64 is refused before use
 // on a CUDA failure.  The forward launches only the main pass (the segment
 // summary and combine passes, when nseg > 1, are the caller's).
 int fwd_tma(const ssm_selective_scan_params* p, const Cfg& c, const Args& a, cudaStream_t st);
+int fwd_sum_tma(const ssm_selective_scan_params* p, const Cfg& c, const Args& a, cudaStream_t st);
 int bwd_tma(const ssm_selective_scan_params* p, const Cfg& c, const Args& a, cudaStream_t st);
+int bwd_sum_tma(const ssm_selective_scan_params* p, const Cfg& c, const Args& a, cudaStream_t st);
 
 }  // namespace sscan
 }  // namespace ssm
