@@ -1006,16 +1006,18 @@ __global__ void reduce_kernel(const Args a, float* dB, float* dC, float* dA, flo
 // States per thread and lanes per channel.  Fewer lanes per channel mean fewer
 // shuffles per step; more lanes mean more threads, which small batch*dim
 // problems need to fill 148 SMs.  The N <= 16 thresholds come from timing every
-// shape at batch 2/4/8/16 x dim 5120 x length 4096 on a B200: the forward is
-// fastest with 8 states x 2 lanes from 24576 rows up (16 x 1 was 7 % slower at
-// 81920 rows), the backward switches to 8 x 2 from 16384 rows.
+// shape at batch 2/4/8/16 x dim 5120 x length 4096 on a B200: both passes are
+// fastest with 8 states x 2 lanes from 8192 rows up (16 x 1 was 7 % slower at
+// 81920 rows), with the sequence cut into segments where that tile alone
+// would not fill the GPU.
 static bool fwd_cfg(int64_t N, int64_t rows, Cfg& c) {
     if (N <= 4) c = {4, 1};
     else if (N <= 8) c = rows >= 49152 ? Cfg{8, 1} : Cfg{4, 2};
-    // from 8192 to 16384 rows the sequence is cut into segments (fwd_plan),
+    // from 8192 to 24576 rows the sequence is cut into segments (fwd_plan),
     // and the wider lane tile with more segments measured faster than 4 x 4
-    // with fewer (batch 2 x 5120 channels: 0.72 -> 0.58 ms)
-    else if (N <= 16) c = (rows >= 24576 || (rows >= 8192 && rows < 16384)) ? Cfg{8, 2} : Cfg{4, 4};
+    // with fewer (batch 2 x 5120 channels: 0.72 -> 0.58 ms; batch 4, once the
+    // segment summaries were TMA-staged: 0.942 -> 0.906 ms)
+    else if (N <= 16) c = rows >= 8192 ? Cfg{8, 2} : Cfg{4, 4};
     else if (N <= 32) c = rows >= 24576 ? Cfg{16, 2} : Cfg{8, 4};
     else if (N <= 64) c = {16, 4};
     else return false;
