@@ -235,6 +235,7 @@ bwd2_tma_kernel(const __grid_constant__ TmaArgs ta) {
         auto chunk_body = [&](auto full_tag) {
             constexpr bool FULL = decltype(full_tag)::value;
             float2 x2[2][2];
+            float2 x8[2][2];                  // LEAN, full chunk: the state entering step 2 TS
             const float2* vr[2] = {dvu + cf * FS, dvu + cs * FS};
             const float* gr[2] = {gs + cf * FS, gs + cs * FS};
             // the lane's saved states of channel slot e, in its permuted order
@@ -285,11 +286,29 @@ bwd2_tma_kernel(const __grid_constant__ TmaArgs ta) {
                 const int tb = sb * TS;
                 const int nb = FULL ? TS : min(TS, len - tb);
                 if constexpr (LEAN) {
-                    // the chunk's entering state, replayed over the sub-blocks before sb
-                    load_states(cslot);
-                    for (int pb = 0; pb < sb; ++pb) {
+                    // the chunk's entering state, replayed over the sub-blocks before
+                    // sb; in a full chunk the state at step 2 TS, passed on the way to
+                    // the last sub-block, is kept for the one before it (4 TS replayed
+                    // steps per chunk instead of 6 TS)
+                    if (FULL && sb == 2) {
 #pragma unroll
-                        for (int jj = 0; jj < TS; ++jj) replay(pb * TS + jj);
+                        for (int e = 0; e < 2; ++e) {
+                            x2[e][0] = x8[e][0];
+                            x2[e][1] = x8[e][1];
+                        }
+                    } else {
+                        load_states(cslot);
+                        for (int pb = 0; pb < sb; ++pb) {
+#pragma unroll
+                            for (int jj = 0; jj < TS; ++jj) replay(pb * TS + jj);
+                            if (FULL && pb == 1) {
+#pragma unroll
+                                for (int e = 0; e < 2; ++e) {
+                                    x8[e][0] = x2[e][0];
+                                    x8[e][1] = x2[e][1];
+                                }
+                            }
+                        }
                     }
                 } else {
                     // this sub-block's entering states (its copies are done: the
