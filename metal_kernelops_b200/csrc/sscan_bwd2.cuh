@@ -235,7 +235,7 @@ bwd2_tma_kernel(const __grid_constant__ TmaArgs ta) {
         auto chunk_body = [&](auto full_tag) {
             constexpr bool FULL = decltype(full_tag)::value;
             float2 x2[2][2];
-            float2 x8[2][2];                  // LEAN, full chunk: the state entering step 2 TS
+            float2 x8[2][2], x4[2][2];        // LEAN, full chunk: the states entering steps 2 TS and TS
             const float2* vr[2] = {dvu + cf * FS, dvu + cs * FS};
             const float* gr[2] = {gs + cf * FS, gs + cs * FS};
             // the lane's saved states of channel slot e, in its permuted order
@@ -290,22 +290,22 @@ bwd2_tma_kernel(const __grid_constant__ TmaArgs ta) {
                     // sb; in a full chunk the state at step 2 TS, passed on the way to
                     // the last sub-block, is kept for the one before it (4 TS replayed
                     // steps per chunk instead of 6 TS)
-                    if (FULL && sb == 2) {
+                    if (FULL && (sb == 2 || sb == 1)) {
 #pragma unroll
                         for (int e = 0; e < 2; ++e) {
-                            x2[e][0] = x8[e][0];
-                            x2[e][1] = x8[e][1];
+                            x2[e][0] = sb == 2 ? x8[e][0] : x4[e][0];
+                            x2[e][1] = sb == 2 ? x8[e][1] : x4[e][1];
                         }
                     } else {
                         load_states(cslot);
                         for (int pb = 0; pb < sb; ++pb) {
 #pragma unroll
                             for (int jj = 0; jj < TS; ++jj) replay(pb * TS + jj);
-                            if (FULL && pb == 1) {
+                            if (FULL && pb <= 1) {
 #pragma unroll
                                 for (int e = 0; e < 2; ++e) {
-                                    x8[e][0] = x2[e][0];
-                                    x8[e][1] = x2[e][1];
+                                    if (pb == 0) { x4[e][0] = x2[e][0]; x4[e][1] = x2[e][1]; }
+                                    else { x8[e][0] = x2[e][0]; x8[e][1] = x2[e][1]; }
                                 }
                             }
                         }
