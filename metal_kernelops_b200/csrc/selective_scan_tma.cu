@@ -854,6 +854,7 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
         auto chunk_body = [&](auto full_tag) {
             constexpr bool FULL = decltype(full_tag)::value;
             float2 x2[NH];
+            float2 x4[NH], x8[NH];            // LEAN, full chunk: the states entering steps TS and 2 TS
             const float2* vr = dvu + c * FS;
             const float* gr = gs + c * FS;
             int cslot = 0;
@@ -877,7 +878,13 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
                 const int tb = sb * TS;
                 const int nb = FULL ? TS : min(TS, len - tb);
                 if constexpr (LEAN) {
-                    // the chunk's entering state, replayed over the sub-blocks before sb
+                    // the chunk's entering state, replayed over the sub-blocks before
+                    // sb; in a full chunk the states at steps TS and 2 TS, passed on
+                    // the way to the last sub-block, are kept for the two before it
+                    if (FULL && (sb == 2 || sb == 1)) {
+#pragma unroll
+                        for (int j = 0; j < NH; ++j) x2[j] = sb == 2 ? x8[j] : x4[j];
+                    } else {
                     const float* src = sck + ((size_t)cslot * NQ * kThreads + tid) * 4;
 #pragma unroll
                     for (int j = 0; j < NH; ++j) {
@@ -903,6 +910,14 @@ bwd_tma_kernel(const __grid_constant__ TmaArgs ta) {
                                 x2[2 * qq + 1] = __ffma2_rn(e1, x2[2 * qq + 1], __fmul2_rn(du2, make_float2(bq.z, bq.w)));
                             }
                         }
+                        if (FULL && pb <= 1) {
+#pragma unroll
+                            for (int j = 0; j < NH; ++j) {
+                                if (pb == 0) x4[j] = x2[j];
+                                else x8[j] = x2[j];
+                            }
+                        }
+                    }
                     }
                 } else {
                 // this sub-block's entering states (its copies are done: the
