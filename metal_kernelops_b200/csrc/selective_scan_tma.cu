@@ -405,7 +405,7 @@ fwd_sum_tma_kernel(const __grid_constant__ TmaArgs ta) {
         __syncthreads();                       // also: the previous chunk's recurrence is done
         if (!okp[0]) {
             if (tid == 0) report(a, 72);
-            return;                            // no copy is in flight: the wait covered the only one
+            return;                            // the one copy in flight is the one this bounded wait gave up on
         }
         // phase 0: per-step scalars (two steps per item) and B to fp32 [t][n]
 #pragma unroll
@@ -558,7 +558,7 @@ adj_tma_kernel(const __grid_constant__ TmaArgs ta) {
         __syncthreads();                       // also: the later chunk's recurrence is done
         if (!okp[0]) {
             if (tid == 0) report(a, 73);
-            return;                            // no copy is in flight: the wait covered the only one
+            return;                            // the one copy in flight is the one this bounded wait gave up on
         }
         // phase 0: per-step scalars (two steps per item) and C to fp32 [t][n]
 #pragma unroll
